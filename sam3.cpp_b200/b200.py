@@ -1,0 +1,177 @@
+"""Python front end of libsam3_b200.so (the C ABI in include/sam3_b200.h).
+
+Thin ctypes bindings plus numpy conveniences used by the tests and by
+bench.py.  Every compute call goes to the CUDA library; there is no CPU
+path here, and loading fails loudly when the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libsam3_b200.so")
+HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "sam3_b200.h")
+
+STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS, STATUS_ABORTED = -2, -1, 0, 1
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
+MMQ_AUTO, MMQ_TC, MMQ_TC128, MMQ_SIMT = 0, 1, 2, 3
+
+_lib = None
+
+
+class B200Error(RuntimeError):
+    pass
+
+
+def build() -> None:
+    """Compile libsam3_b200.so in-tree (nvcc, sm_100a)."""
+    subprocess.run(["make", "-s", "-j8", "-C", PKG_DIR], check=True)
+
+
+def exported_symbols() -> list[str]:
+    """Function names declared in include/sam3_b200.h."""
+    import re
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(sam3b200_[a-z0-9_]+)\s*\(", txt)))
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise B200Error(f"{LIB_PATH} is missing: build it with `make -C {PKG_DIR}` (nvcc, sm_100a)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i64, i32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+    sig = {
+        "sam3b200_backend_init": (vp, [i32]),
+        "sam3b200_backend_free": (None, [vp]),
+        "sam3b200_backend_name": (ctypes.c_char_p, [vp]),
+        "sam3b200_backend_synchronize": (i32, [vp]),
+        "sam3b200_backend_stream": (vp, [vp]),
+        "sam3b200_last_error": (ctypes.c_char_p, []),
+        "sam3b200_buffer_alloc": (vp, [vp, sz]),
+        "sam3b200_buffer_free": (None, [vp, vp]),
+        "sam3b200_tensor_set": (i32, [vp, vp, vp, sz, sz]),
+        "sam3b200_tensor_get": (i32, [vp, vp, vp, sz, sz]),
+        "sam3b200_weight_upload": (vp, [vp, i32, vp, i64, i64]),
+        "sam3b200_weight_free": (None, [vp, vp]),
+        "sam3b200_mul_mat": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
+        "sam3b200_mul_mat_block_dots": (i32, [vp, vp, vp, i64, vp]),
+        "sam3b200_set_mmq_impl": (i32, [vp, i32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error() -> str:
+    return lib().sam3b200_last_error().decode()
+
+
+def _check(status: int, what: str) -> None:
+    if status != STATUS_SUCCESS:
+        raise B200Error(f"{what} failed (status {status}): {last_error()}")
+
+
+class DeviceBuffer:
+    """Device allocation owned by a Backend."""
+
+    def __init__(self, be: "Backend", nbytes: int):
+        self.be, self.nbytes = be, int(nbytes)
+        self.ptr = lib().sam3b200_buffer_alloc(be.h, self.nbytes)
+        if not self.ptr:
+            raise B200Error(f"buffer_alloc({nbytes}) failed: {last_error()}")
+
+    def set(self, arr: np.ndarray, offset: int = 0) -> None:
+        arr = np.ascontiguousarray(arr)
+        assert offset + arr.nbytes <= self.nbytes
+        _check(lib().sam3b200_tensor_set(self.be.h, self.ptr, arr.ctypes.data, offset, arr.nbytes), "tensor_set")
+
+    def get(self, shape, dtype, offset: int = 0) -> np.ndarray:
+        out = np.empty(shape, dtype=dtype)
+        assert offset + out.nbytes <= self.nbytes
+        _check(lib().sam3b200_tensor_get(self.be.h, self.ptr, out.ctypes.data, offset, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.ptr:
+            lib().sam3b200_buffer_free(self.be.h, self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Weight:
+    def __init__(self, be: "Backend", qtype: int, blocks: np.ndarray, K: int, N: int):
+        blocks = np.ascontiguousarray(blocks)
+        self.be, self.qtype, self.K, self.N = be, qtype, K, N
+        self.h = lib().sam3b200_weight_upload(be.h, qtype, blocks.ctypes.data, K, N)
+        if not self.h:
+            raise B200Error(f"weight_upload failed: {last_error()}")
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_weight_free(self.be.h, self.h)
+            self.h = None
+
+
+class Backend:
+    def __init__(self, device: int = 0):
+        self.h = lib().sam3b200_backend_init(device)
+        if not self.h:
+            raise B200Error(f"backend_init({device}) failed: {last_error()}")
+
+    @property
+    def name(self) -> str:
+        return lib().sam3b200_backend_name(self.h).decode()
+
+    @property
+    def stream(self) -> int:
+        return lib().sam3b200_backend_stream(self.h)
+
+    def synchronize(self) -> None:
+        _check(lib().sam3b200_backend_synchronize(self.h), "synchronize")
+
+    def alloc(self, nbytes: int) -> DeviceBuffer:
+        return DeviceBuffer(self, nbytes)
+
+    def upload(self, arr: np.ndarray) -> DeviceBuffer:
+        arr = np.ascontiguousarray(arr)
+        buf = DeviceBuffer(self, arr.nbytes)
+        buf.set(arr)
+        return buf
+
+    def weight(self, qtype: int, blocks: np.ndarray, K: int, N: int) -> Weight:
+        return Weight(self, qtype, blocks, K, N)
+
+    def set_mmq_impl(self, impl: int) -> int:
+        return lib().sam3b200_set_mmq_impl(self.h, impl)
+
+    def mul_mat(self, w: Weight, x: DeviceBuffer, M: int, y: DeviceBuffer, bias: DeviceBuffer | None = None,
+                ldx: int | None = None, ldy: int | None = None) -> None:
+        st = lib().sam3b200_mul_mat(self.h, w.h, x.ptr, ldx or w.K, M, bias.ptr if bias else None, y.ptr,
+                                    ldy or w.N)
+        _check(st, "mul_mat")
+
+    def mul_mat_block_dots(self, w: Weight, x: DeviceBuffer, M: int) -> np.ndarray:
+        nb = w.K // 32
+        out = self.alloc(M * w.N * nb * 4)
+        _check(lib().sam3b200_mul_mat_block_dots(self.h, w.h, x.ptr, M, out.ptr), "mul_mat_block_dots")
+        return out.get((M, w.N, nb), np.int32)
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_backend_free(self.h)
+            self.h = None

@@ -1,0 +1,284 @@
+// backend.cu -- the C ABI declared in include/sam3_b200.h: backend lifetime,
+// device buffers, synchronous tensor copies, weight upload into the
+// tensor-core layout, and the MUL_MAT node.
+#include "../../include/sam3_b200.h"
+#include "backend_impl.h"
+#include "mmq.cuh"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+using namespace b200;
+
+static thread_local std::string g_last_error;
+
+void b200::set_error(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+}
+
+bool b200::cuda_ok(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return true;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+bool b200::Backend::ensure_scratch(size_t need_codes, size_t need_scales) {
+    if (need_codes > act_codes_bytes) {
+        if (act_codes) cudaFree(act_codes);
+        act_codes = nullptr;
+        act_codes_bytes = 0;
+        if (!cuda_ok(cudaMalloc(&act_codes, need_codes), "cudaMalloc(activation codes)")) return false;
+        act_codes_bytes = need_codes;
+    }
+    if (need_scales > act_scales_bytes) {
+        if (act_scales) cudaFree(act_scales);
+        act_scales = nullptr;
+        act_scales_bytes = 0;
+        if (!cuda_ok(cudaMalloc(&act_scales, need_scales), "cudaMalloc(activation scales)")) return false;
+        if (!cuda_ok(cudaMemsetAsync(act_scales, 0, need_scales, stream), "cudaMemset(activation scales)"))
+            return false;
+        act_scales_bytes = need_scales;
+    }
+    return true;
+}
+
+extern "C" {
+
+const char *sam3b200_last_error(void) { return g_last_error.c_str(); }
+
+sam3b200_backend *sam3b200_backend_init(int device) {
+    int n = 0;
+    if (!cuda_ok(cudaGetDeviceCount(&n), "cudaGetDeviceCount")) return nullptr;
+    if (device < 0 || device >= n) {
+        set_error("device %d out of range (%d devices)", device, n);
+        return nullptr;
+    }
+    cudaDeviceProp prop;
+    if (!cuda_ok(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties")) return nullptr;
+    if (prop.major != 10) {
+        set_error("device %d is sm_%d%d; this backend is built for sm_100a only", device, prop.major, prop.minor);
+        return nullptr;
+    }
+    if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice")) return nullptr;
+    auto *be = new Backend();
+    be->device = device;
+    be->num_sms = prop.multiProcessorCount;
+    snprintf(be->name, sizeof(be->name), "B200[%d] %s", device, prop.name);
+    if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
+        !cuda_ok(cudaMalloc(&be->err, sizeof(int)), "cudaMalloc(err)") ||
+        !cuda_ok(cudaMemset(be->err, 0, sizeof(int)), "cudaMemset(err)")) {
+        delete be;
+        return nullptr;
+    }
+    return reinterpret_cast<sam3b200_backend *>(be);
+}
+
+void sam3b200_backend_free(sam3b200_backend *h) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return;
+    cudaSetDevice(be->device);
+    cudaStreamSynchronize(be->stream);
+    if (be->act_codes) cudaFree(be->act_codes);
+    if (be->act_scales) cudaFree(be->act_scales);
+    if (be->err) cudaFree(be->err);
+    cudaStreamDestroy(be->stream);
+    delete be;
+}
+
+const char *sam3b200_backend_name(const sam3b200_backend *h) {
+    auto *be = reinterpret_cast<const Backend *>(h);
+    return be ? be->name : "";
+}
+
+void *sam3b200_backend_stream(sam3b200_backend *h) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    return be ? static_cast<void *>(be->stream) : nullptr;
+}
+
+int sam3b200_backend_synchronize(sam3b200_backend *h) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(be->device);
+    if (!cuda_ok(cudaStreamSynchronize(be->stream), "cudaStreamSynchronize")) return SAM3B200_STATUS_FAILED;
+    int e = 0;
+    if (!cuda_ok(cudaMemcpy(&e, be->err, sizeof(int), cudaMemcpyDeviceToHost), "read error word"))
+        return SAM3B200_STATUS_FAILED;
+    if (e != 0) {
+        set_error("kernel pipeline wait timed out (error word 0x%x)", e);
+        cudaMemset(be->err, 0, sizeof(int));
+        return SAM3B200_STATUS_FAILED;
+    }
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+void *sam3b200_buffer_alloc(sam3b200_backend *h, size_t size) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return nullptr;
+    cudaSetDevice(be->device);
+    void *p = nullptr;
+    if (!cuda_ok(cudaMalloc(&p, size ? size : 1), "cudaMalloc")) return nullptr;
+    return p;
+}
+
+void sam3b200_buffer_free(sam3b200_backend *h, void *p) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || !p) return;
+    cudaSetDevice(be->device);
+    cudaStreamSynchronize(be->stream);
+    cudaFree(p);
+}
+
+int sam3b200_tensor_set(sam3b200_backend *h, void *dev, const void *host, size_t offset, size_t size) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || (!dev && size)) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(be->device);
+    if (!cuda_ok(cudaMemcpyAsync(static_cast<char *>(dev) + offset, host, size, cudaMemcpyHostToDevice, be->stream),
+                 "tensor_set") ||
+        !cuda_ok(cudaStreamSynchronize(be->stream), "tensor_set sync"))
+        return SAM3B200_STATUS_FAILED;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+int sam3b200_tensor_get(sam3b200_backend *h, const void *dev, void *host, size_t offset, size_t size) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || (!dev && size)) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(be->device);
+    if (!cuda_ok(cudaMemcpyAsync(host, static_cast<const char *>(dev) + offset, size, cudaMemcpyDeviceToHost,
+                                 be->stream),
+                 "tensor_get") ||
+        !cuda_ok(cudaStreamSynchronize(be->stream), "tensor_get sync"))
+        return SAM3B200_STATUS_FAILED;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const void *host_blocks, int64_t ne0,
+                                        int64_t ne1) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || !host_blocks) {
+        set_error("weight_upload: null argument");
+        return nullptr;
+    }
+    if (type != SAM3B200_TYPE_Q8_0 && type != SAM3B200_TYPE_Q4_0) {
+        set_error("weight_upload: unsupported weight type %d (Q8_0=8, Q4_0=2 supported)", type);
+        return nullptr;
+    }
+    if (ne0 <= 0 || ne1 <= 0 || ne0 % 32 != 0 || ne0 > (1 << 20) || ne1 > (1 << 24)) {
+        set_error("weight_upload: bad shape ne0=%lld ne1=%lld (ne0 must be a positive multiple of 32)",
+                  (long long)ne0, (long long)ne1);
+        return nullptr;
+    }
+    cudaSetDevice(be->device);
+    const int K = static_cast<int>(ne0), N = static_cast<int>(ne1);
+    const size_t block_bytes = type == SAM3B200_TYPE_Q8_0 ? 34 : 18;
+    const size_t raw_bytes = static_cast<size_t>(N) * (K / 32) * block_bytes;
+    auto *w = new Weight();
+    w->type = type;
+    w->K = K;
+    w->N = N;
+    w->ld = (N + 3) & ~3;
+    void *raw = nullptr;
+    bool ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
+              cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K * 2), "cudaMalloc(weight codes)") &&
+              cuda_ok(cudaMalloc(&w->scales, static_cast<size_t>(K / 32) * w->ld * 4), "cudaMalloc(weight scales)") &&
+              cuda_ok(cudaMemsetAsync(w->scales, 0, static_cast<size_t>(K / 32) * w->ld * 4, be->stream),
+                      "memset scales") &&
+              cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyHostToDevice, be->stream),
+                      "weight upload") &&
+              cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->scales, w->ld, be->stream), "weight repack") &&
+              cuda_ok(cudaStreamSynchronize(be->stream), "weight upload sync");
+    if (raw) cudaFree(raw);
+    if (!ok) {
+        if (w->codes) cudaFree(w->codes);
+        if (w->scales) cudaFree(w->scales);
+        delete w;
+        return nullptr;
+    }
+    return reinterpret_cast<sam3b200_weight *>(w);
+}
+
+void sam3b200_weight_free(sam3b200_backend *h, sam3b200_weight *wh) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    auto *w = reinterpret_cast<Weight *>(wh);
+    if (!w) return;
+    if (be) {
+        cudaSetDevice(be->device);
+        cudaStreamSynchronize(be->stream);
+    }
+    cudaFree(w->codes);
+    cudaFree(w->scales);
+    delete w;
+}
+
+int sam3b200_set_mmq_impl(sam3b200_backend *h, int impl) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return -1;
+    const int prev = be->mmq_impl;
+    if (impl >= SAM3B200_MMQ_AUTO && impl <= SAM3B200_MMQ_SIMT) be->mmq_impl = impl;
+    return prev;
+}
+
+}  // extern "C"
+
+// Quantise x into the backend's activation scratch and run the MUL_MAT.
+int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx, int64_t M, const float *bias,
+                      float *dst, int64_t ldd, int32_t *dump) {
+    if (!be || !w || !x || (!dst && !dump)) {
+        set_error("mul_mat: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (M <= 0 || M > (1 << 24) || ldx < w->K || (dst && ldd < w->N)) {
+        set_error("mul_mat: bad shape M=%lld ldx=%lld ldd=%lld for K=%d N=%d", (long long)M, (long long)ldx,
+                  (long long)ldd, w->K, w->N);
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(be->device);
+    const int Mi = static_cast<int>(M);
+    const int lda = (Mi + 3) & ~3;
+    if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K * 2, static_cast<size_t>(w->K / 32) * lda * 4))
+        return SAM3B200_STATUS_ALLOC_FAILED;
+    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_scales, lda, be->stream),
+                 "quantize activations"))
+        return SAM3B200_STATUS_FAILED;
+    MmqArgs a;
+    a.a = QMatrix{be->act_codes, be->act_scales, Mi, w->K, lda};
+    a.b = QMatrix{w->codes, w->scales, w->N, w->K, w->ld};
+    a.bias = bias;
+    a.y = dst;
+    a.ldy = ldd;
+    a.dump = dump;
+    a.err = be->err;
+    const int mode = dump ? MMQ_OUT_BLOCKDOTS : MMQ_OUT_F32;
+    int impl = be->mmq_impl;
+    if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
+    cudaError_t e;
+    if (impl == SAM3B200_MMQ_SIMT) e = mmq_simt(a, mode, be->stream);
+    else e = mmq_tc(a, mode, impl == SAM3B200_MMQ_TC128 ? 128 : 256, be->num_sms, be->stream);
+    if (!cuda_ok(e, "mul_mat launch")) return SAM3B200_STATUS_FAILED;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+extern "C" int sam3b200_mul_mat(sam3b200_backend *h, const sam3b200_weight *w, const float *x, int64_t ldx,
+                                int64_t M, const float *bias, float *dst, int64_t ldd) {
+    return run_mul_mat(reinterpret_cast<Backend *>(h), reinterpret_cast<const Weight *>(w), x, ldx, M, bias, dst,
+                       ldd, nullptr);
+}
+
+extern "C" int sam3b200_mul_mat_block_dots(sam3b200_backend *h, const sam3b200_weight *wh, const float *x, int64_t M,
+                                           int32_t *dst_dev) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    auto *w = reinterpret_cast<const Weight *>(wh);
+    if (!w) {
+        set_error("mul_mat_block_dots: null weight");
+        return SAM3B200_STATUS_FAILED;
+    }
+    const int st = run_mul_mat(be, w, x, w->K, M, nullptr, nullptr, 0, dst_dev);
+    if (st != SAM3B200_STATUS_SUCCESS) return st;
+    return sam3b200_backend_synchronize(h);
+}

@@ -1,0 +1,41 @@
+// backend_impl.h -- the objects behind the opaque handles of sam3_b200.h.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace b200 {
+
+struct Backend {
+    int device = 0;
+    int num_sms = 0;
+    cudaStream_t stream = nullptr;
+    int *err = nullptr;  // device error word written by bounded pipeline waits
+    int mmq_impl = 0;    // SAM3B200_MMQ_*
+    char name[320] = {0};
+    // scratch for the quantised activations of the current MUL_MAT
+    void *act_codes = nullptr;
+    size_t act_codes_bytes = 0;
+    float *act_scales = nullptr;
+    size_t act_scales_bytes = 0;
+
+    bool ensure_scratch(size_t need_codes, size_t need_scales);
+};
+
+// A 2-D weight in the tensor-core layout (see mmq.cuh).
+struct Weight {
+    int type = 0;  // ggml_type of the uploaded blocks
+    int K = 0;     // ne0
+    int N = 0;     // ne1
+    int ld = 0;    // scale row stride (N rounded up to 4)
+    void *codes = nullptr;
+    float *scales = nullptr;
+};
+
+void set_error(const char *fmt, ...);
+bool cuda_ok(cudaError_t e, const char *what);
+
+int run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx, int64_t M, const float *bias, float *dst,
+                int64_t ldd, int32_t *dump);
+
+}  // namespace b200

@@ -1,0 +1,42 @@
+import importlib.util
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+
+def _load_pkg_module(name: str):
+    """Load a module from the sam3.cpp_b200/ package directory (its name is
+    not a Python identifier, so it is loaded by path)."""
+    path = os.path.join(ROOT, "sam3.cpp_b200", f"{name}.py")
+    spec = importlib.util.spec_from_file_location(f"sam3_b200_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    import oracle as o
+    o.lib()
+    return o
+
+
+@pytest.fixture(scope="session")
+def b200():
+    return _load_pkg_module("b200")
+
+
+@pytest.fixture(scope="session")
+def backend(b200):
+    be = b200.Backend(0)
+    yield be
+    be.free()
