@@ -48,9 +48,8 @@ extern "C" {
 
 /* MUL_MAT implementation selector (sam3b200_set_mmq_impl). */
 #define SAM3B200_MMQ_AUTO 0 /* tensor-core kernel; SIMT for tiny M */
-#define SAM3B200_MMQ_TC   1 /* tcgen05 kernel, tile 128 x 256 */
-#define SAM3B200_MMQ_TC128 2 /* tcgen05 kernel, tile 128 x 128 */
-#define SAM3B200_MMQ_SIMT 3 /* one thread per output */
+#define SAM3B200_MMQ_TC   1 /* tcgen05 kernel, tile 128 x 128 */
+#define SAM3B200_MMQ_SIMT 2 /* one thread per output */
 
 typedef struct sam3b200_backend sam3b200_backend;
 typedef struct sam3b200_weight  sam3b200_weight;

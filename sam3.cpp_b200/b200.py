@@ -18,7 +18,7 @@ HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "sam3_b200.h")
 
 STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS, STATUS_ABORTED = -2, -1, 0, 1
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
-MMQ_AUTO, MMQ_TC, MMQ_TC128, MMQ_SIMT = 0, 1, 2, 3
+MMQ_AUTO, MMQ_TC, MMQ_SIMT = 0, 1, 2
 
 _lib = None
 

@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -29,7 +30,7 @@ bool b200::cuda_ok(cudaError_t e, const char *what) {
     return false;
 }
 
-bool b200::Backend::ensure_scratch(size_t need_codes, size_t need_scales) {
+bool b200::Backend::ensure_scratch(size_t need_codes, size_t need_quads) {
     if (need_codes > act_codes_bytes) {
         if (act_codes) cudaFree(act_codes);
         act_codes = nullptr;
@@ -37,14 +38,14 @@ bool b200::Backend::ensure_scratch(size_t need_codes, size_t need_scales) {
         if (!cuda_ok(cudaMalloc(&act_codes, need_codes), "cudaMalloc(activation codes)")) return false;
         act_codes_bytes = need_codes;
     }
-    if (need_scales > act_scales_bytes) {
-        if (act_scales) cudaFree(act_scales);
-        act_scales = nullptr;
-        act_scales_bytes = 0;
-        if (!cuda_ok(cudaMalloc(&act_scales, need_scales), "cudaMalloc(activation scales)")) return false;
-        if (!cuda_ok(cudaMemsetAsync(act_scales, 0, need_scales, stream), "cudaMemset(activation scales)"))
+    if (need_quads > act_quads_bytes) {
+        if (act_quads) cudaFree(act_quads);
+        act_quads = nullptr;
+        act_quads_bytes = 0;
+        if (!cuda_ok(cudaMalloc(&act_quads, need_quads), "cudaMalloc(activation scale quads)")) return false;
+        if (!cuda_ok(cudaMemsetAsync(act_quads, 0, need_quads, stream), "cudaMemset(activation scale quads)"))
             return false;
-        act_scales_bytes = need_scales;
+        act_quads_bytes = need_quads;
     }
     return true;
 }
@@ -70,6 +71,7 @@ sam3b200_backend *sam3b200_backend_init(int device) {
     auto *be = new Backend();
     be->device = device;
     be->num_sms = prop.multiProcessorCount;
+    if (const char *ev = getenv("SAM3B200_MMQ_CVT")) be->mmq_cvt = atoi(ev) == 0 ? 0 : 1;
     snprintf(be->name, sizeof(be->name), "B200[%d] %s", device, prop.name);
     if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
         !cuda_ok(cudaMalloc(&be->err, sizeof(int)), "cudaMalloc(err)") ||
@@ -86,7 +88,7 @@ void sam3b200_backend_free(sam3b200_backend *h) {
     cudaSetDevice(be->device);
     cudaStreamSynchronize(be->stream);
     if (be->act_codes) cudaFree(be->act_codes);
-    if (be->act_scales) cudaFree(be->act_scales);
+    if (be->act_quads) cudaFree(be->act_quads);
     if (be->err) cudaFree(be->err);
     cudaStreamDestroy(be->stream);
     delete be;
@@ -182,21 +184,21 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
     w->type = type;
     w->K = K;
     w->N = N;
-    w->ld = (N + 3) & ~3;
+    w->ld = (N + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
+    const size_t quad_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
     void *raw = nullptr;
     bool ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
-              cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K * 2), "cudaMalloc(weight codes)") &&
-              cuda_ok(cudaMalloc(&w->scales, static_cast<size_t>(K / 32) * w->ld * 4), "cudaMalloc(weight scales)") &&
-              cuda_ok(cudaMemsetAsync(w->scales, 0, static_cast<size_t>(K / 32) * w->ld * 4, be->stream),
-                      "memset scales") &&
+              cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K), "cudaMalloc(weight codes)") &&
+              cuda_ok(cudaMalloc(&w->quads, quad_bytes), "cudaMalloc(weight scale quads)") &&
+              cuda_ok(cudaMemsetAsync(w->quads, 0, quad_bytes, be->stream), "memset scale quads") &&
               cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyHostToDevice, be->stream),
                       "weight upload") &&
-              cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->scales, w->ld, be->stream), "weight repack") &&
+              cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->quads, w->ld, be->stream), "weight repack") &&
               cuda_ok(cudaStreamSynchronize(be->stream), "weight upload sync");
     if (raw) cudaFree(raw);
     if (!ok) {
         if (w->codes) cudaFree(w->codes);
-        if (w->scales) cudaFree(w->scales);
+        if (w->quads) cudaFree(w->quads);
         delete w;
         return nullptr;
     }
@@ -212,7 +214,7 @@ void sam3b200_weight_free(sam3b200_backend *h, sam3b200_weight *wh) {
         cudaStreamSynchronize(be->stream);
     }
     cudaFree(w->codes);
-    cudaFree(w->scales);
+    cudaFree(w->quads);
     delete w;
 }
 
@@ -240,15 +242,15 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     }
     cudaSetDevice(be->device);
     const int Mi = static_cast<int>(M);
-    const int lda = (Mi + 3) & ~3;
-    if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K * 2, static_cast<size_t>(w->K / 32) * lda * 4))
+    const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
+    if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K, static_cast<size_t>(w->K / 32) * lda * 16))
         return SAM3B200_STATUS_ALLOC_FAILED;
-    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_scales, lda, be->stream),
+    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_quads, lda, be->stream),
                  "quantize activations"))
         return SAM3B200_STATUS_FAILED;
     MmqArgs a;
-    a.a = QMatrix{be->act_codes, be->act_scales, Mi, w->K, lda};
-    a.b = QMatrix{w->codes, w->scales, w->N, w->K, w->ld};
+    a.a = QMatrix{be->act_codes, be->act_quads, Mi, w->K, lda};
+    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld};
     a.bias = bias;
     a.y = dst;
     a.ldy = ldd;
@@ -259,7 +261,7 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
     cudaError_t e;
     if (impl == SAM3B200_MMQ_SIMT) e = mmq_simt(a, mode, be->stream);
-    else e = mmq_tc(a, mode, impl == SAM3B200_MMQ_TC128 ? 128 : 256, be->num_sms, be->stream);
+    else e = mmq_tc(a, mode, be->num_sms, be->stream, be->mmq_cvt);
     if (!cuda_ok(e, "mul_mat launch")) return SAM3B200_STATUS_FAILED;
     return SAM3B200_STATUS_SUCCESS;
 }

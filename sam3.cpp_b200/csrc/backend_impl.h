@@ -12,14 +12,15 @@ struct Backend {
     cudaStream_t stream = nullptr;
     int *err = nullptr;  // device error word written by bounded pipeline waits
     int mmq_impl = 0;    // SAM3B200_MMQ_*
+    int mmq_cvt = 1;     // MMQ epilogue int->float conversion (tuning: env SAM3B200_MMQ_CVT=0|1)
     char name[320] = {0};
     // scratch for the quantised activations of the current MUL_MAT
     void *act_codes = nullptr;
     size_t act_codes_bytes = 0;
-    float *act_scales = nullptr;
-    size_t act_scales_bytes = 0;
+    void *act_quads = nullptr;
+    size_t act_quads_bytes = 0;
 
-    bool ensure_scratch(size_t need_codes, size_t need_scales);
+    bool ensure_scratch(size_t need_codes, size_t need_quads);
 };
 
 // A 2-D weight in the tensor-core layout (see mmq.cuh).
@@ -27,9 +28,9 @@ struct Weight {
     int type = 0;  // ggml_type of the uploaded blocks
     int K = 0;     // ne0
     int N = 0;     // ne1
-    int ld = 0;    // scale row stride (N rounded up to 4)
+    int ld = 0;    // scale-quad rows per block (N rounded up to 128)
     void *codes = nullptr;
-    float *scales = nullptr;
+    void *quads = nullptr;
 };
 
 void set_error(const char *fmt, ...);

@@ -5,12 +5,17 @@
 // sam3.cpp:3742,3783,3796,3799):
 //     y[m][n] = sum_b  (float) I_b[m][n] * (d_w[n][b] * d_x[m][b])
 //     I_b     = sum_{k in block b} q_w[n][k] * q_x[m][k]   (int32)
-// summed block by block in order in fp32.  This file computes exactly that:
-// the tensor core forms every I_b (kind::f16 on integer-valued fp16 codes,
-// exact in the fp32 accumulator), tensor memory holds it, and the epilogue
-// warps fold it into per-thread fp32 accumulators with the two fp16 scales
-// in block order -- the same fma sequence as the CPU oracle, so the result
-// is bit-identical to it.
+// summed block by block in order in fp32.
+//
+// How the tensor core does it, per 32-wide K block b of a 128 x 128 tile:
+//   * one kind::i8 MMA (K = 32) over the int8 codes puts I_b, the exact
+//     int32 block dot, into tensor memory;
+//   * one kind::f16 MMA (K = 16, only column 0 populated) puts the outer
+//     product S_b[m][n] = d_x[m][b] * d_w[n][b] next to it -- exact, since
+//     a product of two fp16 values fits an fp32 significand;
+//   * the epilogue warps convert I_b to fp32 (exact: |I_b| < 2^22) and fold
+//     acc = fma(I_b, S_b, acc) in block order.
+// That is the oracle's fma sequence, so results are bit-identical to it.
 #include "mmq.cuh"
 #include "ptx.cuh"
 
@@ -22,124 +27,149 @@
 namespace b200 {
 
 // ---------------------------------------------------------------------------
-// Activation quantiser: one warp per 32-element block.  Rule of ggml-cpu's
-// x86 quantize_row_q8_0: d = amax/127 stored as fp16, id = 127/amax,
-// q = round-half-even(x * id).  (Division is IEEE-exact here: the library is
-// built without fast-math.)
+// Activation quantiser.  Rule of ggml-cpu's x86 quantize_row_q8_0:
+// d = amax/127 stored as fp16, id = 127/amax, q = round-half-even(x * id).
+// All operations are IEEE round-to-nearest (the library is built without
+// fast-math; the intrinsics make it explicit).  Four threads per 32-element
+// block, eight consecutive floats each (two 16-byte loads).
 // ---------------------------------------------------------------------------
-__global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
-                                        __half *__restrict__ codes, float *__restrict__ scales, int ld) {
-    const int nblk = K >> 5;
-    const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (w >= static_cast<int64_t>(M) * nblk) return;
-    const int m = static_cast<int>(w / nblk);
-    const int b = static_cast<int>(w % nblk);
-    const float v = x[static_cast<int64_t>(m) * ldx + b * 32 + lane];
-    float amax = fabsf(v);
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float d = __fdiv_rn(amax, 127.f);
-    const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-    const int q = __float2int_rn(__fmul_rn(v, id));
-    codes[static_cast<int64_t>(m) * K + b * 32 + lane] = __int2half_rn(q);
-    if (lane == 0) scales[static_cast<int64_t>(b) * ld + m] = __half2float(__float2half_rn(d));
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
-cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, float *scales, int ld,
+template <bool VEC>
+__global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
+                                        int8_t *__restrict__ codes, uint4 *__restrict__ quads, int ld) {
+    const int per_row = K >> 3;  // threads per row
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool active = t < static_cast<int64_t>(M) * per_row;
+    const int m = active ? static_cast<int>(t / per_row) : 0;
+    const int e = active ? static_cast<int>(t % per_row) * 8 : 0;
+    float v[8];
+    if (active) {
+        const float *src = x + static_cast<int64_t>(m) * ldx + e;
+        if constexpr (VEC) {
+            const float4 a = *reinterpret_cast<const float4 *>(src);
+            const float4 b = *reinterpret_cast<const float4 *>(src + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = src[i];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    // the 4 threads of a block are consecutive lanes (K % 32 == 0)
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    if (!active) return;
+    const float d = __fdiv_rn(amax, 127.f);
+    const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = __float2int_rn(__fmul_rn(v[i], id));
+    *reinterpret_cast<uint2 *>(codes + static_cast<int64_t>(m) * K + e) =
+        make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
+    if ((e & 31) == 0)
+        quads[static_cast<int64_t>(e >> 5) * ld + m] = make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
+}
+
+cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
                              cudaStream_t s) {
-    if (K % 32 != 0 || M < 0) return cudaErrorInvalidValue;
+    if (K % 32 != 0 || M < 0 || ld < M) return cudaErrorInvalidValue;
     if (M == 0) return cudaSuccess;
-    const int64_t warps = static_cast<int64_t>(M) * (K / 32);
+    const int64_t threads_total = static_cast<int64_t>(M) * (K / 8);
     const int threads = 256;
-    const int64_t blocks = (warps * 32 + threads - 1) / threads;
-    quantize_rows_q8_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(x, ldx, M, K,
-                                                                              static_cast<__half *>(codes), scales, ld);
+    const unsigned blocks = static_cast<unsigned>((threads_total + threads - 1) / threads);
+    const bool vec = (ldx % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    if (vec)
+        quantize_rows_q8_kernel<true><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
+                                                                 static_cast<uint4 *>(quads), ld);
+    else
+        quantize_rows_q8_kernel<false><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
+                                                                  static_cast<uint4 *>(quads), ld);
     return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
-// Weight repack: ggml blocks -> integer fp16 codes + fp32 block scales.
+// Weight repack: ggml blocks -> int8 codes + scale quads.
 // ---------------------------------------------------------------------------
-__global__ void repack_q8_0_kernel(const uint8_t *__restrict__ blocks, int N, int K, __half *__restrict__ codes,
-                                   float *__restrict__ scales, int ld) {
+__global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ blocks, int N, int K,
+                                     int8_t *__restrict__ codes, uint4 *__restrict__ quads, int ld) {
     const int nblk = K >> 5;
     const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= static_cast<int64_t>(N) * nblk) return;
     const int n = static_cast<int>(w / nblk);
     const int b = static_cast<int>(w % nblk);
-    const uint8_t *blk = blocks + w * 34;
-    const int8_t q = static_cast<int8_t>(blk[2 + lane]);
-    codes[static_cast<int64_t>(n) * K + b * 32 + lane] = __int2half_rn(q);
+    int code;
+    const uint8_t *blk;
+    if (type == 8) {  // Q8_0 {fp16 d; int8 qs[32]}
+        blk = blocks + w * 34;
+        code = static_cast<int8_t>(blk[2 + lane]);
+    } else {          // Q4_0 {fp16 d; uint8 qs[16]}: low nibbles 0..15, high 16..31
+        blk = blocks + w * 18;
+        const uint8_t byte = blk[2 + (lane & 15)];
+        code = (lane < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
+    }
+    codes[static_cast<int64_t>(n) * K + b * 32 + lane] = static_cast<int8_t>(code);
     if (lane == 0) {
-        const uint16_t dbits = *reinterpret_cast<const uint16_t *>(blk);
-        scales[static_cast<int64_t>(b) * ld + n] = __half2float(__ushort_as_half(dbits));
+        const uint16_t dbits = static_cast<uint16_t>(blk[0] | (blk[1] << 8));
+        quads[static_cast<int64_t>(b) * ld + n] = make_uint4(dbits, 0u, 0u, 0u);
     }
 }
 
-__global__ void repack_q4_0_kernel(const uint8_t *__restrict__ blocks, int N, int K, __half *__restrict__ codes,
-                                   float *__restrict__ scales, int ld) {
-    const int nblk = K >> 5;
-    const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (w >= static_cast<int64_t>(N) * nblk) return;
-    const int n = static_cast<int>(w / nblk);
-    const int b = static_cast<int>(w % nblk);
-    const uint8_t *blk = blocks + w * 18;
-    const uint8_t byte = blk[2 + (lane & 15)];
-    const int nib = lane < 16 ? (byte & 0x0F) : (byte >> 4);
-    codes[static_cast<int64_t>(n) * K + b * 32 + lane] = __int2half_rn(nib - 8);
-    if (lane == 0) {
-        const uint16_t dbits = *reinterpret_cast<const uint16_t *>(blk);
-        scales[static_cast<int64_t>(b) * ld + n] = __half2float(__ushort_as_half(dbits));
-    }
-}
-
-cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, float *scales, int ld,
+cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
                                  cudaStream_t s) {
-    if (K % 32 != 0 || N <= 0) return cudaErrorInvalidValue;
+    if (K % 32 != 0 || N <= 0 || ld < N || (type != 8 && type != 2)) return cudaErrorInvalidValue;
     const int64_t warps = static_cast<int64_t>(N) * (K / 32);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((warps * 32 + threads - 1) / threads);
-    auto *b = static_cast<const uint8_t *>(blocks);
-    auto *c = static_cast<__half *>(codes);
-    if (type == 8) repack_q8_0_kernel<<<grid, threads, 0, s>>>(b, N, K, c, scales, ld);
-    else if (type == 2) repack_q4_0_kernel<<<grid, threads, 0, s>>>(b, N, K, c, scales, ld);
-    else return cudaErrorInvalidValue;
+    repack_weight_kernel<<<grid, threads, 0, s>>>(type, static_cast<const uint8_t *>(blocks), N, K,
+                                                  static_cast<int8_t *>(codes), static_cast<uint4 *>(quads), ld);
     return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
-// tcgen05 MMQ kernel.
+// tcgen05 MMQ kernel, CTA tile 128 (tokens) x 128 (features), persistent.
 //
-// CTA tile 128 (tokens) x BN (output features); persistent over tiles.
-// Warp roles (320 threads):
-//   warp 0     : TMA producer (one lane) -- per stage two K-blocks of A and
-//                B codes (128-byte swizzled) and their block scales.
-//   warp 1     : TMEM allocator + MMA issuer (one lane) -- per K-block two
-//                kind::f16 MMAs (K=16 each) into one of two TMEM buffers,
-//                then tcgen05.commit to that buffer's "full" barrier.
-//   warps 2..9 : epilogue -- per K-block read the int block dots from TMEM
-//                and fold them in with d_x*d_w; at the end of the tile add
-//                the bias and store.  Warp w reads TMEM lanes 32*(w%4)..+31
-//                (the lane quarter it may access) and column half (w-2)/4.
+// Warp roles (64 + 32 * 8 threads):
+//   warp 0     : TMA producer (one lane).  A stage holds four K-blocks: the
+//                A and B codes (128 int8 per row = one 128-byte swizzle
+//                atom) and the scale quads of the four blocks for A and B
+//                (4 x 2 KB each, one 3-D TMA box per operand).
+//   warp 1     : TMEM allocator + MMA issuer (one lane).  Per K-block into
+//                TMEM buffer `buf` (256 columns): I_b -> columns [0, 128)
+//                (int32), S_b -> [128, 256) (fp32); commit to tfull[buf].
+//   warps 2..9 : epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31 (the lane
+//                quarter it may access) and column half (w-2)/4 (64 cols).
+// Shared memory: STAGES x 48 KB stages, a 2 KB zero region (the unused
+// second K-chunk of every scale operand), barriers.
 // ---------------------------------------------------------------------------
-template <int BN>
 struct TcCfg {
     static constexpr int BM = 128;
-    static constexpr int BK = 64;  // fp16 per stage row: 128 bytes = one swizzle atom
-    static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int SA_BYTES = 2 * BM * 4;
-    static constexpr int SB_BYTES = 2 * BN * 4;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SA_BYTES + SB_BYTES;
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int BN = 128;
+    static constexpr int BLK = 4;                   // K-blocks per stage
+    static constexpr int BK = 32 * BLK;             // int8 per stage row: 128 bytes = one swizzle atom
+    static constexpr int A_BYTES = BM * BK;         // 16 KB
+    static constexpr int B_BYTES = BN * BK;         // 16 KB
+    static constexpr int Q_BYTES = 128 * 16;        // one block's scale operand: 2 KB
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * BLK * Q_BYTES;
+    static constexpr int STAGES = 4;
+    static constexpr int ZERO_OFF = STAGES * STAGE_BYTES;
+    static constexpr int BAR_OFF = ZERO_OFF + Q_BYTES;
     static constexpr int EPI_WARPS = 8;
     static constexpr int THREADS = 64 + EPI_WARPS * 32;
-    static constexpr int COLS = BN / 2;
-    static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
+    static constexpr int COLS = BN / 2;             // per epilogue thread
+    static constexpr int CHUNK = 32;
+    static constexpr int TMEM_COLS = 512;           // 2 buffers x (I 128 + S 128)
+    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
     static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -148,20 +178,36 @@ enum : int {
     ERR_WAIT_EMPTY = 1,
     ERR_WAIT_FULL_MMA = 2,
     ERR_WAIT_TEMPTY = 4,
-    ERR_WAIT_FULL_EPI = 8,
     ERR_WAIT_TFULL = 16,
 };
 
-template <int BN, int MODE>
-__global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
+// No-swizzle K-major operand descriptor for the K=16 scale MMA: core
+// matrices of 8 rows x 16 bytes, 8-row groups 128 bytes apart (SBO), the
+// second K-chunk `lbo` bytes after the first (it points at the zero region).
+__device__ __forceinline__ uint64_t noswz_kmajor_desc(uint32_t smem_addr, uint32_t lbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>(128u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    return d;  // layout type 0 = no swizzle
+}
+
+// Exact int32 -> fp32 for |v| < 2^22: place v in the significand of
+// 1.5 * 2^23 and subtract that constant (one integer add, one fp add).
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;
+constexpr float MAGIC_F = 12582912.0f;
+
+template <int MODE, int CVT>
+__global__ void __launch_bounds__(TcCfg::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                  const __grid_constant__ CUtensorMap tm_sa, const __grid_constant__ CUtensorMap tm_sb, int M, int N,
+                  const __grid_constant__ CUtensorMap tm_qa, const __grid_constant__ CUtensorMap tm_qb, int M, int N,
                   int nblk, const float *__restrict__ bias, float *__restrict__ y, int64_t ldy,
                   int32_t *__restrict__ dump, int *__restrict__ err) {
-    using C = TcCfg<BN>;
+    using C = TcCfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *empty = full + C::STAGES;
     uint64_t *tfull = empty + C::STAGES;
     uint64_t *tempty = tfull + 2;
@@ -170,14 +216,18 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_m = (M + C::BM - 1) / C::BM;
-    const int num_n = (N + BN - 1) / BN;
+    const int num_n = (N + C::BN - 1) / C::BN;
     const int num_tiles = num_m * num_n;
-    const int kstages = (nblk + 1) >> 1;
+    const int kstages = (nblk + C::BLK - 1) / C::BLK;
 
+    // zero region read by every scale MMA as its second K-chunk
+    for (int i = threadIdx.x; i < C::Q_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4 *>(smem + C::ZERO_OFF)[i] = make_uint4(0u, 0u, 0u, 0u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1 + C::EPI_WARPS);
+            mbar_init(&empty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
@@ -186,8 +236,8 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
         fence_mbar_init();
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
-        prefetch_tmap(&tm_sa);
-        prefetch_tmap(&tm_sb);
+        prefetch_tmap(&tm_qa);
+        prefetch_tmap(&tm_qb);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -205,18 +255,19 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 const int m0 = (t % num_m) * C::BM;
-                const int n0 = (t / num_m) * BN;
+                const int n0 = (t / num_m) * C::BN;
                 for (int ks = 0; ks < kstages; ++ks) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, err, ERR_WAIT_EMPTY)) {
                         ok = false;
                         break;
                     }
                     uint8_t *sb = smem + stage * C::STAGE_BYTES;
+                    uint8_t *q = sb + C::A_BYTES + C::B_BYTES;
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                     tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);
                     tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
-                    tma_load_2d(sb + C::A_BYTES + C::B_BYTES, &tm_sa, &full[stage], m0, ks * 2);
-                    tma_load_2d(sb + C::A_BYTES + C::B_BYTES + C::SA_BYTES, &tm_sb, &full[stage], n0, ks * 2);
+                    tma_load_3d(q, &tm_qa, &full[stage], 0, m0, ks * C::BLK);
+                    tma_load_3d(q + C::BLK * C::Q_BYTES, &tm_qb, &full[stage], 0, n0, ks * C::BLK);
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -226,7 +277,9 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(C::BM, BN);
+            constexpr uint32_t idesc_i = idesc_s8_s32(C::BM, C::BN);
+            constexpr uint32_t idesc_s = idesc_f16_f32(C::BM, C::BN);
+            const uint32_t zero_addr = smem_u32(smem + C::ZERO_OFF);
             int stage = 0;
             uint32_t phase = 0;
             uint32_t blk = 0;
@@ -240,20 +293,23 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint32_t b_addr = a_addr + C::A_BYTES;
-                    for (int j = 0; j < 2; ++j) {
-                        if (ks * 2 + j >= nblk) break;
+                    const uint32_t q_addr = b_addr + C::B_BYTES;
+                    for (int j = 0; j < C::BLK; ++j) {
+                        if (ks * C::BLK + j >= nblk) break;
                         const uint32_t buf = blk & 1u;
                         if (!mbar_wait(&tempty[buf], ((blk >> 1) & 1u) ^ 1u, err, ERR_WAIT_TEMPTY)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        const uint32_t d_tmem = tmem_base + buf * BN;
-#pragma unroll
-                        for (int kk = 0; kk < 2; ++kk) {
-                            const uint32_t koff = static_cast<uint32_t>((j * 2 + kk) * 32);  // 16 fp16 = 32 bytes
-                            mma_f16(d_tmem, sw128_kmajor_desc(a_addr + koff), sw128_kmajor_desc(b_addr + koff), idesc,
-                                    kk);
+                        const uint32_t d_tmem = tmem_base + buf * 256;
+                        const uint32_t koff = static_cast<uint32_t>(j * 32);  // 32 int8 = 32 bytes
+                        mma_i8(d_tmem, sw128_kmajor_desc(a_addr + koff), sw128_kmajor_desc(b_addr + koff), idesc_i, 0);
+                        if constexpr (MODE == MMQ_OUT_F32) {
+                            const uint32_t qa = q_addr + j * C::Q_BYTES;
+                            const uint32_t qb = q_addr + (C::BLK + j) * C::Q_BYTES;
+                            mma_f16(d_tmem + 128, noswz_kmajor_desc(qa, zero_addr - qa),
+                                    noswz_kmajor_desc(qb, zero_addr - qb), idesc_s, 0);
                         }
                         mma_commit(&tfull[buf]);
                         ++blk;
@@ -269,88 +325,65 @@ __global__ void __launch_bounds__(TcCfg<BN>::THREADS, 1)
         }
     } else {
         // ---- epilogue warps ----
-        constexpr int CHUNK = C::COLS >= 128 ? 32 : 64;  // TMEM columns per batch (register budget)
+        constexpr int CHUNK = C::CHUNK;
         const int q = warp & 3;
         const int h = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-        int stage = 0;
-        uint32_t phase = 0;
         uint32_t blk = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
             const int m0 = (t % num_m) * C::BM;
-            const int n0 = (t / num_m) * BN;
+            const int n0 = (t / num_m) * C::BN;
             const int m = m0 + row;
             float acc[C::COLS];
 #pragma unroll
             for (int i = 0; i < C::COLS; ++i) acc[i] = 0.f;
-            for (int ks = 0; ks < kstages; ++ks) {
-                // the stage's block scales have landed in shared memory
-                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, ERR_WAIT_FULL_EPI))) {
+            for (int b = 0; b < nblk; ++b) {
+                const uint32_t buf = blk & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (blk >> 1) & 1u, err, ERR_WAIT_TFULL))) {
                     ok = false;
                     break;
                 }
-                const float *sa_s =
-                    reinterpret_cast<const float *>(smem + stage * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES);
-                const float *sb_s = sa_s + 2 * C::BM;
-                for (int j = 0; j < 2; ++j) {
-                    const int b = ks * 2 + j;
-                    if (b >= nblk) break;
-                    const uint32_t buf = blk & 1u;
-                    if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (blk >> 1) & 1u, err, ERR_WAIT_TFULL))) {
-                        ok = false;
-                        break;
+                tc_fence_after();
+                const uint32_t ta = tmem_base + lane_addr + buf * 256 + h * C::COLS;
+#pragma unroll
+                for (int c0 = 0; c0 < C::COLS; c0 += CHUNK) {
+                    uint32_t vi[CHUNK], vs[CHUNK];
+                    tmem_ld_32x32b_x32(ta + c0, vi);
+                    if constexpr (MODE == MMQ_OUT_F32) tmem_ld_32x32b_x32(ta + 128 + c0, vs);
+                    tmem_wait_ld();
+                    if (c0 + CHUNK == C::COLS) {
+                        // the whole buffer is in registers: hand it back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
                     }
-                    tc_fence_after();
-                    const float dx = sa_s[j * C::BM + row];
-                    const float4 *dw4 = reinterpret_cast<const float4 *>(sb_s + j * BN + h * C::COLS);
+                    if constexpr (MODE == MMQ_OUT_F32) {
 #pragma unroll
-                    for (int c0 = 0; c0 < C::COLS; c0 += CHUNK) {
-                        uint32_t v[CHUNK];
-                        const uint32_t ta = tmem_base + lane_addr + buf * BN + h * C::COLS + c0;
-#pragma unroll
-                        for (int c = 0; c < CHUNK; c += 32)
-                            tmem_ld_32x32b_x32(ta + c, *reinterpret_cast<uint32_t(*)[32]>(&v[c]));
-                        tmem_wait_ld();
-                        if (c0 + CHUNK == C::COLS) {
-                            // every column of this buffer is in registers: hand it back to the MMA warp
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&tempty[buf]);
-                        }
-                        if constexpr (MODE == MMQ_OUT_F32) {
-#pragma unroll
-                            for (int i = 0; i < CHUNK; i += 4) {
-                                const float4 w4 = dw4[(c0 + i) >> 2];
-                                float s0, s1, s2, s3;
-                                fmul2(s0, s1, dx, dx, w4.x, w4.y);
-                                fmul2(s2, s3, dx, dx, w4.z, w4.w);
-                                ffma2(acc[c0 + i], acc[c0 + i + 1], __uint_as_float(v[i]), __uint_as_float(v[i + 1]),
-                                      s0, s1);
-                                ffma2(acc[c0 + i + 2], acc[c0 + i + 3], __uint_as_float(v[i + 2]),
-                                      __uint_as_float(v[i + 3]), s2, s3);
+                        for (int i = 0; i < CHUNK; i += 2) {
+                            float f0, f1;
+                            if constexpr (CVT == 0) {
+                                f0 = __int2float_rn(static_cast<int>(vi[i]));
+                                f1 = __int2float_rn(static_cast<int>(vi[i + 1]));
+                            } else {
+                                fadd2(f0, f1, __uint_as_float(vi[i] + MAGIC_BITS), __uint_as_float(vi[i + 1] + MAGIC_BITS),
+                                      -MAGIC_F, -MAGIC_F);
                             }
-                        } else {
-                            if (m < M) {
-                                for (int i = 0; i < CHUNK; ++i) {
-                                    const int n = n0 + h * C::COLS + c0 + i;
-                                    if (n < N)
-                                        dump[(static_cast<int64_t>(m) * N + n) * nblk + b] =
-                                            static_cast<int32_t>(__uint_as_float(v[i]));
-                                }
+                            ffma2(acc[c0 + i], acc[c0 + i + 1], f0, f1, __uint_as_float(vs[i]),
+                                  __uint_as_float(vs[i + 1]));
+                        }
+                    } else {
+                        if (m < M) {
+                            for (int i = 0; i < CHUNK; ++i) {
+                                const int n = n0 + h * C::COLS + c0 + i;
+                                if (n < N)
+                                    dump[(static_cast<int64_t>(m) * N + n) * nblk + b] = static_cast<int32_t>(vi[i]);
                             }
                         }
                     }
-                    ++blk;
                 }
-                if (!ok) break;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[stage]);
-                if (++stage == C::STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
+                ++blk;
             }
             if (!ok) break;
             if constexpr (MODE == MMQ_OUT_F32) {
@@ -402,90 +435,98 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-static bool make_tmap_2d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
-                         uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+// rank-2 or rank-3 tiled tensor map; dims/box innermost first, strides in
+// bytes for dims 1..rank-1.
+static bool make_tmap(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,
+                      const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle sw) {
     auto fn = encode_fn();
     if (!fn) return false;
-    cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {box_inner, box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+    cuuint64_t d[3], st[2];
+    cuuint32_t bx[3], es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+    }
+    for (int i = 0; i < rank - 1; ++i) st[i] = strides[i];
+    return fn(map, dt, rank, const_cast<void *>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int MODE>
+template <int MODE, int CVT>
 static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
-    using C = TcCfg<BN>;
-    const int M = a.a.rows, N = a.b.rows, K = a.a.K;
-    CUtensorMap tma, tmb, tmsa, tmsb;
-    if (!make_tmap_2d(&tma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.a.codes, K, M, uint64_t(K) * 2, C::BK, C::BM,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_2d(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.b.codes, K, N, uint64_t(K) * 2, C::BK, BN,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_2d(&tmsa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.a.scales, a.a.ld, K / 32, uint64_t(a.a.ld) * 4, C::BM,
-                      2, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tmap_2d(&tmsb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.b.scales, a.b.ld, K / 32, uint64_t(a.b.ld) * 4, BN, 2,
-                      CU_TENSOR_MAP_SWIZZLE_NONE))
+    using C = TcCfg;
+    const int M = a.a.rows, N = a.b.rows, K = a.a.K, nblk = K / 32;
+    CUtensorMap tma, tmb, tmqa, tmqb;
+    const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, db[2] = {uint64_t(K), uint64_t(N)}, sk[1] = {uint64_t(K)};
+    const uint32_t bxa[2] = {C::BK, C::BM}, bxb[2] = {C::BK, C::BN};
+    const uint64_t dqa[3] = {8, uint64_t(a.a.ld), uint64_t(nblk)}, sqa[2] = {16, uint64_t(a.a.ld) * 16};
+    const uint64_t dqb[3] = {8, uint64_t(a.b.ld), uint64_t(nblk)}, sqb[2] = {16, uint64_t(a.b.ld) * 16};
+    const uint32_t bxq[3] = {8, 128, C::BLK};
+    if (!make_tmap(&tma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a.codes, 2, da, sk, bxa, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, sk, bxb, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tmqa, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.a.quads, 3, dqa, sqa, bxq, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_tmap(&tmqb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.b.quads, 3, dqb, sqb, bxq, CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
-    auto kern = mmq_tc_kernel<BN, MODE>;
+    auto kern = mmq_tc_kernel<MODE, CVT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    const int tiles = ((M + C::BM - 1) / C::BM) * ((N + BN - 1) / BN);
+    const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, tmsa, tmsb, M, N, K / 32, a.bias, a.y, a.ldy, a.dump,
-                                                  a.err);
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, tmqa, tmqb, M, N, nblk, a.bias, a.y, a.ldy, a.dump, a.err);
     return cudaGetLastError();
 }
 
-cudaError_t mmq_tc(const MmqArgs &a, int mode, int bn, int num_sms, cudaStream_t s) {
+static bool valid_args(const MmqArgs &a) {
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
-    if (K != a.b.K || K % 32 != 0 || K % 8 != 0 || M <= 0 || N <= 0) return cudaErrorInvalidValue;
-    if (a.a.ld % 4 != 0 || a.b.ld % 4 != 0 || a.a.ld < M || a.b.ld < N) return cudaErrorInvalidValue;
-    if (num_sms <= 0) return cudaErrorInvalidValue;
-    if (mode == MMQ_OUT_F32) {
-        if (bn == 256) return launch_tc<256, MMQ_OUT_F32>(a, num_sms, s);
-        if (bn == 128) return launch_tc<128, MMQ_OUT_F32>(a, num_sms, s);
-    } else if (mode == MMQ_OUT_BLOCKDOTS) {
-        if (bn == 256) return launch_tc<256, MMQ_OUT_BLOCKDOTS>(a, num_sms, s);
-        if (bn == 128) return launch_tc<128, MMQ_OUT_BLOCKDOTS>(a, num_sms, s);
-    }
+    return K == a.b.K && K > 0 && K % 32 == 0 && M > 0 && N > 0 && a.a.ld >= M && a.b.ld >= N &&
+           a.a.ld % MMQ_ROW_ALIGN == 0 && a.b.ld % MMQ_ROW_ALIGN == 0;
+}
+
+cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt) {
+    if (!valid_args(a) || num_sms <= 0) return cudaErrorInvalidValue;
+    if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1>(a, num_sms, s);
+    if (mode == MMQ_OUT_F32)
+        return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0>(a, num_sms, s) : launch_tc<MMQ_OUT_F32, 1>(a, num_sms, s);
     return cudaErrorInvalidValue;
 }
 
 // ---------------------------------------------------------------------------
 // SIMT MMQ: one thread per output, same block-ordered fma sequence.
 // ---------------------------------------------------------------------------
-__global__ void mmq_simt_kernel(const __half *__restrict__ ca, const float *__restrict__ sa, int lda_s,
-                                const __half *__restrict__ cb, const float *__restrict__ sb, int ldb_s, int M, int N,
+__global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__restrict__ qa, int lda_q,
+                                const int8_t *__restrict__ cb, const uint4 *__restrict__ qb, int ldb_q, int M, int N,
                                 int K, const float *__restrict__ bias, float *__restrict__ y, int64_t ldy,
                                 int32_t *__restrict__ dump, int mode) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int m = blockIdx.y;
     if (n >= N || m >= M) return;
     const int nblk = K >> 5;
-    const __half *ar = ca + static_cast<int64_t>(m) * K;
-    const __half *br = cb + static_cast<int64_t>(n) * K;
+    const int8_t *ar = ca + static_cast<int64_t>(m) * K;
+    const int8_t *br = cb + static_cast<int64_t>(n) * K;
     float acc = 0.f;
     for (int b = 0; b < nblk; ++b) {
-        float isum = 0.f;
-        for (int j = 0; j < 32; ++j) isum = fmaf(__half2float(ar[b * 32 + j]), __half2float(br[b * 32 + j]), isum);
+        int isum = 0;
+        for (int j = 0; j < 32; ++j) isum += static_cast<int>(ar[b * 32 + j]) * static_cast<int>(br[b * 32 + j]);
         if (mode == MMQ_OUT_BLOCKDOTS) {
-            dump[(static_cast<int64_t>(m) * N + n) * nblk + b] = static_cast<int32_t>(isum);
+            dump[(static_cast<int64_t>(m) * N + n) * nblk + b] = isum;
         } else {
-            acc = fmaf(isum, sa[static_cast<int64_t>(b) * lda_s + m] * sb[static_cast<int64_t>(b) * ldb_s + n], acc);
+            const uint16_t xb = static_cast<uint16_t>(qa[static_cast<int64_t>(b) * lda_q + m].x);
+            const uint16_t wb = static_cast<uint16_t>(qb[static_cast<int64_t>(b) * ldb_q + n].x);
+            acc = fmaf(static_cast<float>(isum), __half2float(__ushort_as_half(xb)) * __half2float(__ushort_as_half(wb)),
+                       acc);
         }
     }
     if (mode == MMQ_OUT_F32) y[static_cast<int64_t>(m) * ldy + n] = bias ? acc + bias[n] : acc;
 }
 
 cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
+    if (!valid_args(a) || a.a.rows > 65535) return cudaErrorInvalidValue;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
-    if (K != a.b.K || K % 32 != 0 || M <= 0 || N <= 0 || M > 65535) return cudaErrorInvalidValue;
     dim3 grid((N + 127) / 128, M);
-    mmq_simt_kernel<<<grid, 128, 0, s>>>(static_cast<const __half *>(a.a.codes), a.a.scales, a.a.ld,
-                                         static_cast<const __half *>(a.b.codes), a.b.scales, a.b.ld, M, N, K, a.bias,
-                                         a.y, a.ldy, a.dump, mode);
+    mmq_simt_kernel<<<grid, 128, 0, s>>>(static_cast<const int8_t *>(a.a.codes), static_cast<const uint4 *>(a.a.quads),
+                                         a.a.ld, static_cast<const int8_t *>(a.b.codes),
+                                         static_cast<const uint4 *>(a.b.quads), a.b.ld, M, N, K, a.bias, a.y, a.ldy,
+                                         a.dump, mode);
     return cudaGetLastError();
 }
 

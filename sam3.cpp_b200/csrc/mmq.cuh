@@ -2,15 +2,16 @@
 // matrix multiply (ggml GGML_OP_MUL_MAT with Q8_0 / Q4_0 weights against
 // activations quantised on the fly to Q8_0, sam3.cpp:3742,3783,3796,3799).
 //
-// Device layouts ("repacked" operands):
-//   codes  : fp16 [rows, K] row-major, each value an exact small integer
-//            (the block's int8 / nibble-8 code).  fp16 holds every int8
-//            exactly, and a 32-term dot of such values accumulated by the
-//            tensor core in fp32 is exact (|sum| <= 32*127*127 < 2^24), so
-//            the MMA produces ggml's int32 block dot bit for bit.
-//   scales : fp32 [K/32, ld] block-major: scales[b*ld + row] = fp16->fp32
-//            of the block's d.  ld is rows rounded up to a multiple of 4 so
-//            a TMA row is 16-byte aligned.
+// Device layouts of a quantised operand ("QMatrix", rows x K):
+//   codes : int8 [rows, K] row-major -- the block's int8 code (Q8_0), or
+//           nibble - 8 (Q4_0).  A kind::i8 MMA of K = 32 over two such rows
+//           is exactly ggml's int32 block dot.
+//   quads : fp16 [K/32][ld][8] -- per (block, row) one 16-byte record whose
+//           first half is the block's fp16 scale d and the rest zero.  This
+//           is the K-major, no-swizzle core-matrix layout of a K=16 MMA
+//           operand with only column 0 populated, so a TMA copy of 128 rows
+//           of it is directly the operand of the scale MMA (S = d_x (x) d_w).
+//           ld = rows rounded up to a multiple of 128; padding rows are 0.
 #pragma once
 
 #include <cstdint>
@@ -23,33 +24,37 @@ enum MmqOut : int {
     MMQ_OUT_BLOCKDOTS = 1, // dump[(m*N + n)*nblk + b] = int32 block dot (debug/parity)
 };
 
+constexpr int MMQ_ROW_ALIGN = 128;
+
 struct QMatrix {
-    const void *codes;   // fp16 [rows, K]
-    const float *scales; // fp32 [K/32, ld]
+    const void *codes;  // int8 [rows, K]
+    const void *quads;  // fp16 [K/32][ld][8]
     int rows, K, ld;
 };
 
 struct MmqArgs {
-    QMatrix a;           // activations, rows = M
-    QMatrix b;           // weights, rows = N
-    const float *bias;   // [N] or null
-    float *y;            // [M, ldy]
+    QMatrix a;          // activations, rows = M
+    QMatrix b;          // weights, rows = N
+    const float *bias;  // [N] or null
+    float *y;           // [M, ldy]
     int64_t ldy;
-    int32_t *dump;       // MMQ_OUT_BLOCKDOTS only
-    int *err;            // device error word (0 = ok)
+    int32_t *dump;      // MMQ_OUT_BLOCKDOTS only
+    int *err;           // device error word (0 = ok)
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.
-cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, float *scales, int ld,
+// quads must hold K/32 * ld records; rows >= M are left untouched.
+cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
                              cudaStream_t s);
 
 // Repack ggml weight blocks (N rows of K) into the device layout.
 // type: 8 = Q8_0, 2 = Q4_0.  Returns cudaErrorInvalidValue otherwise.
-cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, float *scales, int ld,
+cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
                                  cudaStream_t s);
 
-// tcgen05 tensor-core MMQ.
-cudaError_t mmq_tc(const MmqArgs &args, int mode, int bn, int num_sms, cudaStream_t s);
+// tcgen05 tensor-core MMQ (tile 128 x 128).  cvt selects the epilogue's
+// exact int32 -> fp32 conversion: 0 = cvt instruction, 1 = magic-number add.
+cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, int cvt = 1);
 
 // Straight SIMT version of the same arithmetic (small M, cross-checks).
 cudaError_t mmq_simt(const MmqArgs &args, int mode, cudaStream_t s);

@@ -11,7 +11,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-IMPLS = ["TC", "TC128", "SIMT"]
+IMPLS = ["TC", "SIMT"]
 
 
 def _case(oracle, qt, M, K, N, seed, x_scale=1.0):
@@ -23,7 +23,7 @@ def _case(oracle, qt, M, K, N, seed, x_scale=1.0):
 
 
 def _impl(b200, name):
-    return {"TC": b200.MMQ_TC, "TC128": b200.MMQ_TC128, "SIMT": b200.MMQ_SIMT}[name]
+    return {"TC": b200.MMQ_TC, "SIMT": b200.MMQ_SIMT}[name]
 
 
 @pytest.mark.parametrize("impl", IMPLS)
