@@ -105,8 +105,84 @@ int sam3b200_mul_mat(sam3b200_backend *be, const sam3b200_weight *w, const float
 int sam3b200_mul_mat_block_dots(sam3b200_backend *be, const sam3b200_weight *w, const float *x, int64_t M,
                                 int32_t *dst_dev);
 
+/* Kernel launches the backend has issued so far (encoder and MUL_MAT). */
+long long sam3b200_backend_launch_count(const sam3b200_backend *be);
+
+/* Per-kernel-class timing, the analogue of the reference's timed sub-graph
+ * profiling helper (sam3.cpp:5041-5094): while enabled, CUDA events are
+ * recorded on the backend stream around every launch of class 0 (the
+ * quantised MUL_MAT); profile_read syncs and returns their summed time and
+ * count.  Enabling resets the record. */
+int sam3b200_backend_profile(sam3b200_backend *be, int enable);
+int sam3b200_backend_profile_read(sam3b200_backend *be, int cls, double *total_ms, int *n);
+
 /* Select the MUL_MAT kernel (SAM3B200_MMQ_*); returns the previous one. */
 int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
+
+/* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
+ *
+ * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds
+ * for the encoder (sam3.cpp:74-98): img_size 1008, patch 14, embed 1024,
+ * depth 32, heads 16 (head_dim must be 64), mlp 4736, window 24, global
+ * blocks {7, 15, 23, 31}, pos_embed grid 24 (img/patch/3, sam3.cpp:2533),
+ * neck_dim 256; wtype is the ggml type of the four linear weights of every
+ * block (Q8_0 or Q4_0; sam3.cpp:2476-2499 picks it per tensor). */
+typedef struct {
+    int img, patch, embed, depth, heads, mlp, window;
+    int n_global;
+    int global_idx[4];
+    int pos_grid, neck_dim, wtype;
+} sam3b200_vit_hparams;
+
+typedef struct sam3b200_vit sam3b200_vit;
+
+/* Allocate an encoder and its activation buffers on the backend's device
+ * (the model + state pair of sam3_load_model / sam3_create_state,
+ * sam3.cpp:3204-3348, 3380-3415, restricted to the visual encoder). */
+sam3b200_vit *sam3b200_vit_create(sam3b200_backend *be, const sam3b200_vit_hparams *hp);
+void sam3b200_vit_free(sam3b200_vit *vit);
+
+/* One weight tensor by its weight-file name and ggml shape (ne[0..3]),
+ * the per-tensor step of sam3_load_tensors (sam3.cpp:3095-3198): names
+ * "vit.patch_embed.proj.weight", "vit.pos_embed", "vit.ln_pre.{weight,bias}",
+ * "vit.blocks.<i>.{norm1,norm2}.{weight,bias}", "...attn.qkv.{weight,bias}",
+ * "...attn.proj.{weight,bias}", "...mlp.lin1.{weight,bias}",
+ * "...mlp.lin2.{weight,bias}", "...attn.freqs_cis", "neck.trk.<s>.*"
+ * (sam3.cpp:2529-2600).  Linear weights are Q8_0/Q4_0, the rest F32/F16. */
+int sam3b200_vit_set_tensor(sam3b200_vit *vit, const char *name, int type, const void *data, const int64_t ne[4]);
+
+/* Number of encoder tensors not yet set; their names, newline-separated,
+ * into buf (may be NULL). */
+int sam3b200_vit_missing(sam3b200_vit *vit, char *buf, int cap);
+
+/* sam3_encode_image (sam3.cpp:6028-6149): uint8 RGB HWC host image of any
+ * size (resized like sam3_resize_bilinear when it is not img x img), then
+ * preprocessing, ViT and tracker neck; the four neck maps are copied to
+ * out_host[i] (f32 [neck_dim, W, H], W = H = 4G, 2G, G, G/2 for G =
+ * img/patch; NULL entries are skipped).  Synchronous. */
+int sam3b200_encode_image(sam3b200_vit *vit, const uint8_t *rgb, int w, int h, float *const out_host[4]);
+
+/* Same with the image already in device memory; asynchronous on the
+ * backend stream; results stay in the encoder's buffers
+ * (sam3b200_vit_output). */
+int sam3b200_encode_image_device(sam3b200_vit *vit, const uint8_t *rgb_dev, int w, int h);
+
+/* Device pointer and ggml shape of output i (0..3 = neck_trk_i, -1 = the
+ * ViT output [embed, G, G]) of the last encode. */
+int sam3b200_vit_output(sam3b200_vit *vit, int i, const float **dev, int64_t ne[4]);
+
+/* sam3_preprocess_image (sam3.cpp:3490-3518, with sam3_resize_bilinear
+ * :3445-3485 when w x h != img x img): device uint8 RGB HWC -> device f32
+ * CHW [img, img, 3] normalised (p/255 - 0.5)/0.5.  Asynchronous. */
+int sam3b200_preprocess(sam3b200_backend *be, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev);
+
+/* Stage runners on caller-provided device tensors, the analogue of the
+ * reference's stage test hooks (sam3.h sam3_vit_prefix_stage /
+ * sam3_vit_block_stage): prefix image f32 CHW -> x [embed, G, G]; one
+ * block in place on x; neck from x into the encoder's outputs. */
+int sam3b200_vit_run_prefix(sam3b200_vit *vit, const float *img_chw_dev, float *x_dev);
+int sam3b200_vit_run_block(sam3b200_vit *vit, int idx, float *x_dev);
+int sam3b200_vit_run_neck(sam3b200_vit *vit, const float *x_dev);
 
 #ifdef __cplusplus
 }

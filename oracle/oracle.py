@@ -118,3 +118,129 @@ def block_dots(qtype: int, wq: np.ndarray, K: int, N: int, x: np.ndarray, n_thre
     n_threads = n_threads or (os.cpu_count() or 1)
     lib().orc_mul_mat_block_dots(qtype, _ptr(np.ascontiguousarray(wq)), K, N, _ptr(x), M, _ptr(out), n_threads)
     return out
+
+
+# ---- SAM3 visual encoder restatement (vit_oracle.h) ------------------------
+
+class _Hp(ctypes.Structure):
+    _fields_ = [("img", ctypes.c_int), ("patch", ctypes.c_int), ("E", ctypes.c_int), ("depth", ctypes.c_int),
+                ("heads", ctypes.c_int), ("mlp", ctypes.c_int), ("window", ctypes.c_int),
+                ("n_global", ctypes.c_int), ("global_idx", ctypes.c_int * 4), ("pos_grid", ctypes.c_int),
+                ("neck_dim", ctypes.c_int), ("wtype", ctypes.c_int)]
+
+
+class _BlockW(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("norm1_w", "norm1_b", "norm2_w", "norm2_b", "qkv_w", "qkv_b",
+                                               "proj_w", "proj_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b", "freqs")]
+
+
+class _NeckW(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("dc1_w", "dc1_b", "dc2_w", "dc2_b", "c1_w", "c1_b", "c3_w", "c3_b")]
+
+
+class _VitW(ctypes.Structure):
+    _fields_ = [("patch_w", ctypes.c_void_p), ("pos_embed", ctypes.c_void_p), ("ln_pre_w", ctypes.c_void_p),
+                ("ln_pre_b", ctypes.c_void_p), ("blocks", _BlockW * 64), ("neck", _NeckW * 4)]
+
+
+def _vit_lib():
+    L = lib()
+    if not getattr(L, "_vit_sigs", False):
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        L.orc_preprocess_sam3.argtypes = [vp, i32, i32, i32, vp]
+        L.orc_vit_prefix.argtypes = [vp, vp, vp, vp, i32]
+        L.orc_vit_block.argtypes = [vp, vp, i32, vp, i32]
+        L.orc_neck.argtypes = [vp, vp, vp, vp, i32]
+        L.orc_layer_norm.argtypes = [vp, vp, ctypes.c_int64, i32, ctypes.c_float, vp, vp, i32]
+        L.orc_attention.argtypes = [vp, vp, vp, i32, i32, i32, ctypes.c_float, vp, i32]
+        for f in ("orc_preprocess_sam3", "orc_vit_prefix", "orc_vit_block", "orc_neck", "orc_layer_norm",
+                  "orc_attention"):
+            getattr(L, f).restype = None
+        L._vit_sigs = True
+    return L
+
+
+class OracleVit:
+    """CPU restatement of the SAM3 visual encoder over a tensor dict
+    (name -> (ggml type, array, ne), as produced by model.random_vit_weights)."""
+
+    def __init__(self, hp: dict, tensors: dict, n_threads: int = 0):
+        self.hp, self.t = dict(hp), tensors
+        self.nt = n_threads or (os.cpu_count() or 1)
+        self.G = hp["img"] // hp["patch"]
+        self._keep = []
+        h = _Hp()
+        h.img, h.patch, h.E, h.depth, h.heads = hp["img"], hp["patch"], hp["embed"], hp["depth"], hp["heads"]
+        h.mlp, h.window, h.pos_grid, h.neck_dim, h.wtype = hp["mlp"], hp["window"], hp["pos_grid"], \
+            hp["neck_dim"], hp["wtype"]
+        h.n_global = len(hp["global_idx"])
+        for i, g in enumerate(hp["global_idx"]):
+            h.global_idx[i] = g
+        self.h = h
+        w = _VitW()
+        w.patch_w = self._p("vit.patch_embed.proj.weight")
+        w.pos_embed = self._p("vit.pos_embed")
+        w.ln_pre_w, w.ln_pre_b = self._p("vit.ln_pre.weight"), self._p("vit.ln_pre.bias")
+        for i in range(hp["depth"]):
+            b, pre = w.blocks[i], f"vit.blocks.{i}."
+            b.norm1_w, b.norm1_b = self._p(pre + "norm1.weight"), self._p(pre + "norm1.bias")
+            b.norm2_w, b.norm2_b = self._p(pre + "norm2.weight"), self._p(pre + "norm2.bias")
+            b.qkv_w, b.qkv_b = self._p(pre + "attn.qkv.weight"), self._p(pre + "attn.qkv.bias")
+            b.proj_w, b.proj_b = self._p(pre + "attn.proj.weight"), self._p(pre + "attn.proj.bias")
+            b.fc1_w, b.fc1_b = self._p(pre + "mlp.lin1.weight"), self._p(pre + "mlp.lin1.bias")
+            b.fc2_w, b.fc2_b = self._p(pre + "mlp.lin2.weight"), self._p(pre + "mlp.lin2.bias")
+            b.freqs = self._p(pre + "attn.freqs_cis")
+        pre = "neck.trk."
+        names = {0: ("0.dconv_2x2_0", "0.dconv_2x2_1"), 1: ("1.dconv_2x2", None), 2: (None, None), 3: (None, None)}
+        for s in range(4):
+            nw = w.neck[s]
+            d1, d2 = names[s]
+            if d1:
+                nw.dc1_w, nw.dc1_b = self._p(pre + d1 + ".weight"), self._p(pre + d1 + ".bias")
+            if d2:
+                nw.dc2_w, nw.dc2_b = self._p(pre + d2 + ".weight"), self._p(pre + d2 + ".bias")
+            nw.c1_w, nw.c1_b = self._p(pre + f"{s}.conv_1x1.weight"), self._p(pre + f"{s}.conv_1x1.bias")
+            nw.c3_w, nw.c3_b = self._p(pre + f"{s}.conv_3x3.weight"), self._p(pre + f"{s}.conv_3x3.bias")
+        self.w = w
+
+    def _p(self, name):
+        arr = self.t[name][1]
+        if self.t[name][0] == F32:
+            arr = np.ascontiguousarray(arr, dtype=np.float32)
+        else:
+            arr = np.ascontiguousarray(arr)
+        self._keep.append(arr)
+        return arr.ctypes.data
+
+    def preprocess(self, rgb: np.ndarray) -> np.ndarray:
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        S = self.hp["img"]
+        out = np.empty((3, S, S), np.float32)
+        _vit_lib().orc_preprocess_sam3(rgb.ctypes.data, rgb.shape[1], rgb.shape[0], S, out.ctypes.data)
+        return out
+
+    def prefix(self, img_chw: np.ndarray) -> np.ndarray:
+        img_chw = np.ascontiguousarray(img_chw, dtype=np.float32)
+        x = np.empty((self.G * self.G, self.hp["embed"]), np.float32)
+        _vit_lib().orc_vit_prefix(ctypes.byref(self.h), ctypes.byref(self.w), img_chw.ctypes.data, x.ctypes.data,
+                                  self.nt)
+        return x
+
+    def block(self, i: int, x: np.ndarray) -> np.ndarray:
+        x = np.array(x, dtype=np.float32, copy=True, order="C")
+        _vit_lib().orc_vit_block(ctypes.byref(self.h), ctypes.byref(self.w.blocks[i]), i, x.ctypes.data, self.nt)
+        return x
+
+    def neck(self, x: np.ndarray) -> list:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        D, G = self.hp["neck_dim"], self.G
+        outs = [np.empty((s, s, D), np.float32) for s in (4 * G, 2 * G, G, G // 2)]
+        ptrs = (ctypes.c_void_p * 4)(*[o.ctypes.data for o in outs])
+        _vit_lib().orc_neck(ctypes.byref(self.h), ctypes.byref(self.w.neck), x.ctypes.data, ptrs, self.nt)
+        return outs
+
+    def encode(self, rgb: np.ndarray, depth: int | None = None) -> tuple:
+        x = self.prefix(self.preprocess(rgb))
+        for i in range(self.hp["depth"] if depth is None else depth):
+            x = self.block(i, x)
+        return x, self.neck(x)

@@ -63,6 +63,21 @@ def lib() -> ctypes.CDLL:
         "sam3b200_mul_mat": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
         "sam3b200_mul_mat_block_dots": (i32, [vp, vp, vp, i64, vp]),
         "sam3b200_set_mmq_impl": (i32, [vp, i32]),
+        "sam3b200_vit_create": (vp, [vp, vp]),
+        "sam3b200_vit_free": (None, [vp]),
+        "sam3b200_vit_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_vit_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_encode_image": (i32, [vp, vp, i32, i32, vp]),
+        "sam3b200_encode_image_device": (i32, [vp, vp, i32, i32]),
+        "sam3b200_vit_output": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p), vp]),
+        "sam3b200_vit_run_prefix": (i32, [vp, vp, vp]),
+        "sam3b200_vit_run_block": (i32, [vp, i32, vp]),
+        "sam3b200_vit_run_neck": (i32, [vp, vp]),
+        "sam3b200_preprocess": (i32, [vp, vp, i32, i32, i32, vp]),
+        "sam3b200_backend_launch_count": (ctypes.c_longlong, [vp]),
+        "sam3b200_backend_profile": (i32, [vp, i32]),
+        "sam3b200_backend_profile_read": (i32, [vp, i32, ctypes.POINTER(ctypes.c_double),
+                                                ctypes.POINTER(ctypes.c_int)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -127,6 +142,91 @@ class Weight:
             self.h = None
 
 
+class VitHparams(ctypes.Structure):
+    """sam3b200_vit_hparams (include/sam3_b200.h)."""
+    _fields_ = [("img", ctypes.c_int), ("patch", ctypes.c_int), ("embed", ctypes.c_int), ("depth", ctypes.c_int),
+                ("heads", ctypes.c_int), ("mlp", ctypes.c_int), ("window", ctypes.c_int),
+                ("n_global", ctypes.c_int), ("global_idx", ctypes.c_int * 4), ("pos_grid", ctypes.c_int),
+                ("neck_dim", ctypes.c_int), ("wtype", ctypes.c_int)]
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "VitHparams":
+        h = cls()
+        for k in ("img", "patch", "embed", "depth", "heads", "mlp", "window", "pos_grid", "neck_dim", "wtype"):
+            setattr(h, k, int(d[k]))
+        g = list(d["global_idx"])
+        h.n_global = len(g)
+        for i, v in enumerate(g):
+            h.global_idx[i] = int(v)
+        return h
+
+
+class Vit:
+    """The visual encoder (sam3b200_vit) on a backend."""
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = VitHparams.from_dict(hp)
+        self.h = lib().sam3b200_vit_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"vit_create failed: {last_error()}")
+        self.G = hp["img"] // hp["patch"]
+
+    def set_tensor(self, name: str, ttype: int, data: np.ndarray, ne) -> None:
+        data = np.ascontiguousarray(data)
+        ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+        _check(lib().sam3b200_vit_set_tensor(self.h, name.encode(), ttype, data.ctypes.data, ne4), f"set {name}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            self.set_tensor(name, t, arr, ne)
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_vit_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} encoder tensors missing: {buf.value.decode()[:200]}")
+
+    def encode(self, rgb: np.ndarray) -> list:
+        """sam3b200_encode_image: host uint8 HxWx3 -> four f32 [side, side, neck_dim] maps."""
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        h, w = rgb.shape[:2]
+        D = self.hp["neck_dim"]
+        outs = [np.empty((s, s, D), np.float32) for s in (4 * self.G, 2 * self.G, self.G, self.G // 2)]
+        ptrs = (ctypes.c_void_p * 4)(*[o.ctypes.data for o in outs])
+        _check(lib().sam3b200_encode_image(self.h, rgb.ctypes.data, w, h, ptrs), "encode_image")
+        return outs
+
+    def encode_device(self, rgb_dev: "DeviceBuffer", w: int, h: int) -> None:
+        _check(lib().sam3b200_encode_image_device(self.h, rgb_dev.ptr, w, h), "encode_image_device")
+
+    def output(self, i: int):
+        p = ctypes.c_void_p()
+        ne = (ctypes.c_int64 * 4)()
+        _check(lib().sam3b200_vit_output(self.h, i, ctypes.byref(p), ne), "vit_output")
+        return p.value, tuple(ne)
+
+    def output_host(self, i: int) -> np.ndarray:
+        ptr, ne = self.output(i)
+        self.be.synchronize()
+        out = np.empty((ne[2], ne[1], ne[0]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, ptr, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def run_prefix(self, img_chw: "DeviceBuffer", x: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_vit_run_prefix(self.h, img_chw.ptr, x.ptr), "run_prefix")
+
+    def run_block(self, idx: int, x: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_vit_run_block(self.h, idx, x.ptr), "run_block")
+
+    def run_neck(self, x: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_vit_run_neck(self.h, x.ptr), "run_neck")
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_vit_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -170,6 +270,25 @@ class Backend:
         out = self.alloc(M * w.N * nb * 4)
         _check(lib().sam3b200_mul_mat_block_dots(self.h, w.h, x.ptr, M, out.ptr), "mul_mat_block_dots")
         return out.get((M, w.N, nb), np.int32)
+
+    def preprocess(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
+        _check(lib().sam3b200_preprocess(self.h, rgb_dev.ptr, w, h, img, out.ptr), "preprocess")
+
+    @property
+    def launches(self) -> int:
+        return int(lib().sam3b200_backend_launch_count(self.h))
+
+    def profile(self, enable: bool) -> None:
+        _check(lib().sam3b200_backend_profile(self.h, 1 if enable else 0), "profile")
+
+    def profile_read(self, cls: int = 0):
+        """(total ms, launch count) of the timed kernel class since profiling was enabled."""
+        t, n = ctypes.c_double(), ctypes.c_int()
+        _check(lib().sam3b200_backend_profile_read(self.h, cls, ctypes.byref(t), ctypes.byref(n)), "profile_read")
+        return t.value, n.value
+
+    def vit(self, hp: dict) -> Vit:
+        return Vit(self, hp)
 
     def free(self) -> None:
         if self.h:

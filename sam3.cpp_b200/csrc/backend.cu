@@ -50,9 +50,52 @@ bool b200::Backend::ensure_scratch(size_t need_codes, size_t need_quads) {
     return true;
 }
 
+void b200::Backend::prof_mark(int cls) {
+    if (!profiling || cls < 0 || cls > 3) return;
+    auto &v = prof_events[cls];
+    if (prof_used[cls] == v.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return;
+        v.push_back(e);
+    }
+    cudaEventRecord(v[prof_used[cls]++], stream);
+}
+
 extern "C" {
 
 const char *sam3b200_last_error(void) { return g_last_error.c_str(); }
+
+long long sam3b200_backend_launch_count(const sam3b200_backend *h) {
+    auto *be = reinterpret_cast<const Backend *>(h);
+    return be ? be->launches : -1;
+}
+
+int sam3b200_backend_profile(sam3b200_backend *h, int enable) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return SAM3B200_STATUS_FAILED;
+    be->profiling = enable;
+    for (auto &u : be->prof_used) u = 0;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+int sam3b200_backend_profile_read(sam3b200_backend *h, int cls, double *total_ms, int *n) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || cls < 0 || cls > 3) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(be->device);
+    if (!cuda_ok(cudaStreamSynchronize(be->stream), "profile sync")) return SAM3B200_STATUS_FAILED;
+    double t = 0;
+    const size_t pairs = be->prof_used[cls] / 2;
+    for (size_t i = 0; i < pairs; ++i) {
+        float ms = 0.f;
+        if (!cuda_ok(cudaEventElapsedTime(&ms, be->prof_events[cls][2 * i], be->prof_events[cls][2 * i + 1]),
+                     "event elapsed"))
+            return SAM3B200_STATUS_FAILED;
+        t += ms;
+    }
+    if (total_ms) *total_ms = t;
+    if (n) *n = static_cast<int>(pairs);
+    return SAM3B200_STATUS_SUCCESS;
+}
 
 sam3b200_backend *sam3b200_backend_init(int device) {
     int n = 0;
@@ -90,6 +133,8 @@ void sam3b200_backend_free(sam3b200_backend *h) {
     if (be->act_codes) cudaFree(be->act_codes);
     if (be->act_quads) cudaFree(be->act_quads);
     if (be->err) cudaFree(be->err);
+    for (auto &v : be->prof_events)
+        for (auto e : v) cudaEventDestroy(e);
     cudaStreamDestroy(be->stream);
     delete be;
 }
@@ -260,8 +305,11 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     int impl = be->mmq_impl;
     if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
     cudaError_t e;
+    be->count(2);
+    be->prof_mark(0);
     if (impl == SAM3B200_MMQ_SIMT) e = mmq_simt(a, mode, be->stream);
     else e = mmq_tc(a, mode, be->num_sms, be->stream, be->mmq_cvt);
+    be->prof_mark(0);
     if (!cuda_ok(e, "mul_mat launch")) return SAM3B200_STATUS_FAILED;
     return SAM3B200_STATUS_SUCCESS;
 }

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <vector>
+
 namespace b200 {
 
 struct Backend {
@@ -21,6 +23,15 @@ struct Backend {
     size_t act_quads_bytes = 0;
 
     bool ensure_scratch(size_t need_codes, size_t need_quads);
+
+    // launch accounting and optional per-kernel-class event timing
+    // (sam3b200_backend_profile_*): class 0 = quantised MUL_MAT
+    long long launches = 0;
+    int profiling = 0;
+    std::vector<cudaEvent_t> prof_events[4];  // begin/end pairs per class
+    size_t prof_used[4] = {0, 0, 0, 0};
+    void count(int n = 1) { launches += n; }
+    void prof_mark(int cls);
 };
 
 // A 2-D weight in the tensor-core layout (see mmq.cuh).

@@ -18,11 +18,9 @@
 // That is the oracle's fma sequence, so results are bit-identical to it.
 #include "mmq.cuh"
 #include "ptx.cuh"
+#include "tmap.h"
 
 #include <cuda_fp16.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
 
 namespace b200 {
 
@@ -198,12 +196,35 @@ __device__ __forceinline__ uint64_t noswz_kmajor_desc(uint32_t smem_addr, uint32
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;
 constexpr float MAGIC_F = 12582912.0f;
 
+struct MmqEpi {
+    const float *bias;
+    float *y;
+    int64_t ldy;
+    int32_t *dump;
+    int add;
+    const int *rowmap;
+    int gelu;
+    int8_t *qcodes;
+    uint4 *qquads;
+    int qld;
+};
+
+__device__ __forceinline__ float gelu_erf_f(float x) {
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
+}
+
+__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
+    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+}
+
 template <int MODE, int CVT>
 __global__ void __launch_bounds__(TcCfg::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const __grid_constant__ CUtensorMap tm_qa, const __grid_constant__ CUtensorMap tm_qb, int M, int N,
-                  int nblk, const float *__restrict__ bias, float *__restrict__ y, int64_t ldy,
-                  int32_t *__restrict__ dump, int *__restrict__ err) {
+                  int nblk, const MmqEpi ep, int *__restrict__ err) {
+    const float *__restrict__ bias = ep.bias;
+    int32_t *__restrict__ dump = ep.dump;
     using C = TcCfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -305,7 +326,7 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
                         const uint32_t d_tmem = tmem_base + buf * 256;
                         const uint32_t koff = static_cast<uint32_t>(j * 32);  // 32 int8 = 32 bytes
                         mma_i8(d_tmem, sw128_kmajor_desc(a_addr + koff), sw128_kmajor_desc(b_addr + koff), idesc_i, 0);
-                        if constexpr (MODE == MMQ_OUT_F32) {
+                        if constexpr (MODE != MMQ_OUT_BLOCKDOTS) {
                             const uint32_t qa = q_addr + j * C::Q_BYTES;
                             const uint32_t qb = q_addr + (C::BLK + j) * C::Q_BYTES;
                             mma_f16(d_tmem + 128, noswz_kmajor_desc(qa, zero_addr - qa),
@@ -351,7 +372,7 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
                 for (int c0 = 0; c0 < C::COLS; c0 += CHUNK) {
                     uint32_t vi[CHUNK], vs[CHUNK];
                     tmem_ld_32x32b_x32(ta + c0, vi);
-                    if constexpr (MODE == MMQ_OUT_F32) tmem_ld_32x32b_x32(ta + 128 + c0, vs);
+                    if constexpr (MODE != MMQ_OUT_BLOCKDOTS) tmem_ld_32x32b_x32(ta + 128 + c0, vs);
                     tmem_wait_ld();
                     if (c0 + CHUNK == C::COLS) {
                         // the whole buffer is in registers: hand it back to the MMA warp
@@ -359,7 +380,7 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[buf]);
                     }
-                    if constexpr (MODE == MMQ_OUT_F32) {
+                    if constexpr (MODE != MMQ_OUT_BLOCKDOTS) {
 #pragma unroll
                         for (int i = 0; i < CHUNK; i += 2) {
                             float f0, f1;
@@ -389,25 +410,67 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
             if constexpr (MODE == MMQ_OUT_F32) {
                 if (m < M) {
                     const int nb = n0 + h * C::COLS;
-                    float *yr = y + static_cast<int64_t>(m) * ldy + nb;
-                    const bool vec = ((ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+                    const int r = ep.rowmap ? ep.rowmap[m] : m;
+                    float *yr = ep.y + static_cast<int64_t>(r) * ep.ldy + nb;
+                    const bool vec = ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0);
 #pragma unroll
                     for (int j = 0; j < C::COLS; j += 4) {
-                        float4 o = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                        float o[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
                         if (vec && nb + j + 3 < N) {
                             if (bias) {
                                 const float4 bb = *reinterpret_cast<const float4 *>(bias + nb + j);
-                                o.x += bb.x;
-                                o.y += bb.y;
-                                o.z += bb.z;
-                                o.w += bb.w;
+                                o[0] = __fadd_rn(o[0], bb.x);
+                                o[1] = __fadd_rn(o[1], bb.y);
+                                o[2] = __fadd_rn(o[2], bb.z);
+                                o[3] = __fadd_rn(o[3], bb.w);
                             }
-                            *reinterpret_cast<float4 *>(yr + j) = o;
+                            if (ep.add) {
+                                const float4 prev = *reinterpret_cast<const float4 *>(yr + j);
+                                o[0] = __fadd_rn(prev.x, o[0]);
+                                o[1] = __fadd_rn(prev.y, o[1]);
+                                o[2] = __fadd_rn(prev.z, o[2]);
+                                o[3] = __fadd_rn(prev.w, o[3]);
+                            }
+                            *reinterpret_cast<float4 *>(yr + j) = make_float4(o[0], o[1], o[2], o[3]);
                         } else {
-                            const float ov[4] = {o.x, o.y, o.z, o.w};
-                            for (int e = 0; e < 4; ++e)
-                                if (nb + j + e < N) yr[j + e] = bias ? ov[e] + bias[nb + j + e] : ov[e];
+                            for (int e = 0; e < 4; ++e) {
+                                if (nb + j + e >= N) break;
+                                float val = bias ? __fadd_rn(o[e], bias[nb + j + e]) : o[e];
+                                if (ep.add) val = __fadd_rn(yr[j + e], val);
+                                yr[j + e] = val;
+                            }
                         }
+                    }
+                }
+            } else if constexpr (MODE == MMQ_OUT_Q8) {
+                // this thread's 64 columns are two whole 32-wide Q8_0 blocks of the output row
+                if (m < M) {
+                    const int nb = n0 + h * C::COLS;
+#pragma unroll
+                    for (int hb = 0; hb < C::COLS; hb += 32) {
+                        if (nb + hb >= N) break;
+                        float amax = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            float val = bias ? __fadd_rn(acc[hb + i], bias[nb + hb + i]) : acc[hb + i];
+                            if (ep.gelu) val = gelu_erf_f(val);
+                            acc[hb + i] = val;
+                            amax = fmaxf(amax, fabsf(val));
+                        }
+                        const float d = __fdiv_rn(amax, 127.f);
+                        const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            pk[i] = pack4_i8(__float2int_rn(__fmul_rn(acc[hb + 4 * i], id)),
+                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 1], id)),
+                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 2], id)),
+                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 3], id)));
+                        uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
+                        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        ep.qquads[static_cast<int64_t>((nb + hb) >> 5) * ep.qld + m] =
+                            make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
                     }
                 }
             }
@@ -422,36 +485,6 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void *p = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// rank-2 or rank-3 tiled tensor map; dims/box innermost first, strides in
-// bytes for dims 1..rank-1.
-static bool make_tmap(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int rank, const uint64_t *dims,
-                      const uint64_t *strides, const uint32_t *box, CUtensorMapSwizzle sw) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t d[3], st[2];
-    cuuint32_t bx[3], es[3] = {1, 1, 1};
-    for (int i = 0; i < rank; ++i) {
-        d[i] = dims[i];
-        bx[i] = box[i];
-    }
-    for (int i = 0; i < rank - 1; ++i) st[i] = strides[i];
-    return fn(map, dt, rank, const_cast<void *>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int MODE, int CVT>
 static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
     using C = TcCfg;
@@ -472,7 +505,18 @@ static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, tmqa, tmqb, M, N, nblk, a.bias, a.y, a.ldy, a.dump, a.err);
+    MmqEpi ep;
+    ep.bias = a.bias;
+    ep.y = a.y;
+    ep.ldy = a.ldy;
+    ep.dump = a.dump;
+    ep.add = a.add;
+    ep.rowmap = a.rowmap;
+    ep.gelu = a.gelu;
+    ep.qcodes = static_cast<int8_t *>(a.out_codes);
+    ep.qquads = static_cast<uint4 *>(a.out_quads);
+    ep.qld = a.out_ld;
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, tmqa, tmqb, M, N, nblk, ep, a.err);
     return cudaGetLastError();
 }
 
@@ -485,6 +529,10 @@ static bool valid_args(const MmqArgs &a) {
 cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt) {
     if (!valid_args(a) || num_sms <= 0) return cudaErrorInvalidValue;
     if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1>(a, num_sms, s);
+    if (mode == MMQ_OUT_Q8) {
+        if (a.b.rows % 32 != 0 || !a.out_codes || !a.out_quads || a.out_ld < a.a.rows) return cudaErrorInvalidValue;
+        return launch_tc<MMQ_OUT_Q8, 1>(a, num_sms, s);
+    }
     if (mode == MMQ_OUT_F32)
         return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0>(a, num_sms, s) : launch_tc<MMQ_OUT_F32, 1>(a, num_sms, s);
     return cudaErrorInvalidValue;

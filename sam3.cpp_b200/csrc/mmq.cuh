@@ -20,8 +20,10 @@
 namespace b200 {
 
 enum MmqOut : int {
-    MMQ_OUT_F32 = 0,       // y[m*ldy + n] = acc (+ bias[n])
+    MMQ_OUT_F32 = 0,       // y[r*ldy + n] (+)= acc + bias[n], r = rowmap ? rowmap[m] : m
     MMQ_OUT_BLOCKDOTS = 1, // dump[(m*N + n)*nblk + b] = int32 block dot (debug/parity)
+    MMQ_OUT_Q8 = 2,        // v = acc + bias (GELU-erf if gelu), re-quantised to Q8_0 (ggml-cpu
+                           // activation rule) into the QMatrix (out_codes, out_quads, out_ld)
 };
 
 constexpr int MMQ_ROW_ALIGN = 128;
@@ -40,6 +42,12 @@ struct MmqArgs {
     int64_t ldy;
     int32_t *dump;      // MMQ_OUT_BLOCKDOTS only
     int *err;           // device error word (0 = ok)
+    int add = 0;                    // MMQ_OUT_F32: y = y + (acc + bias)
+    const int *rowmap = nullptr;    // MMQ_OUT_F32: output row of tile row m
+    int gelu = 0;                   // MMQ_OUT_Q8
+    void *out_codes = nullptr;      // MMQ_OUT_Q8: int8 [M, N]
+    void *out_quads = nullptr;      // MMQ_OUT_Q8: [N/32][out_ld][16 B]
+    int out_ld = 0;
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.

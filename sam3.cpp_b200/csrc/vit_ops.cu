@@ -1,0 +1,307 @@
+// vit_ops.cu -- see vit_ops.cuh.  All float arithmetic that the CPU oracle
+// performs in a fixed order is written with explicit round-to-nearest
+// intrinsics so nvcc cannot contract it into FMAs; LayerNorm sums in double
+// like ggml_norm does.
+#include "vit_ops.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace b200 {
+
+static inline unsigned grid_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
+
+// ---- preprocessing -----------------------------------------------------------
+__global__ void preprocess_kernel(const uint8_t *__restrict__ rgb, int img, float *__restrict__ out) {
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t plane = static_cast<int64_t>(img) * img;
+    if (p >= plane) return;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const float v = __fdiv_rn(static_cast<float>(rgb[p * 3 + c]), 255.0f);
+        out[c * plane + p] = __fdiv_rn(__fsub_rn(v, 0.5f), 0.5f);
+    }
+}
+
+cudaError_t preprocess_sam3(const uint8_t *rgb, int img, float *out, cudaStream_t s) {
+    if (img <= 0) return cudaErrorInvalidValue;
+    preprocess_kernel<<<grid_for(static_cast<int64_t>(img) * img, 256), 256, 0, s>>>(rgb, img, out);
+    return cudaGetLastError();
+}
+
+__global__ void resize_kernel(const uint8_t *__restrict__ src, int sw, int sh, uint8_t *__restrict__ dst, int dw,
+                              int dh) {
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (p >= static_cast<int64_t>(dw) * dh) return;
+    const int x = static_cast<int>(p % dw), y = static_cast<int>(p / dw);
+    const double sx = __ddiv_rn(sw, dw), sy = __ddiv_rn(sh, dh);
+    double fy = __dsub_rn(__dmul_rn(__dadd_rn(y, 0.5), sy), 0.5);
+    if (fy < 0.0) fy = 0.0;
+    const int y0 = static_cast<int>(fy), y1 = (y0 < sh - 1) ? y0 + 1 : y0;
+    const double wy = __dsub_rn(fy, y0), wy0 = __dsub_rn(1.0, wy);
+    double fx = __dsub_rn(__dmul_rn(__dadd_rn(x, 0.5), sx), 0.5);
+    if (fx < 0.0) fx = 0.0;
+    const int x0 = static_cast<int>(fx), x1 = (x0 < sw - 1) ? x0 + 1 : x0;
+    const double wx = __dsub_rn(fx, x0), wx0 = __dsub_rn(1.0, wx);
+    for (int c = 0; c < 3; ++c) {
+        const double p00 = src[(y0 * sw + x0) * 3 + c], p01 = src[(y0 * sw + x1) * 3 + c];
+        const double p10 = src[(y1 * sw + x0) * 3 + c], p11 = src[(y1 * sw + x1) * 3 + c];
+        const double top = __dadd_rn(__dmul_rn(wx0, p00), __dmul_rn(wx, p01));
+        const double bot = __dadd_rn(__dmul_rn(wx0, p10), __dmul_rn(wx, p11));
+        const double v = __dadd_rn(__dmul_rn(wy0, top), __dmul_rn(wy, bot));
+        int iv = static_cast<int>(__dadd_rn(v, 0.5));
+        iv = iv < 0 ? 0 : (iv > 255 ? 255 : iv);
+        dst[(static_cast<int64_t>(y) * dw + x) * 3 + c] = static_cast<uint8_t>(iv);
+    }
+}
+
+cudaError_t resize_bilinear_u8(const uint8_t *src, int sw, int sh, uint8_t *dst, int dw, int dh, cudaStream_t s) {
+    if (sw <= 0 || sh <= 0 || dw <= 0 || dh <= 0) return cudaErrorInvalidValue;
+    resize_kernel<<<grid_for(static_cast<int64_t>(dw) * dh, 256), 256, 0, s>>>(src, sw, sh, dst, dw, dh);
+    return cudaGetLastError();
+}
+
+// ---- patch embedding im2col --------------------------------------------------
+__global__ void im2col_patch_kernel(const float *__restrict__ img, int S, int p, int G, int kp, __half *__restrict__ a) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(G) * G * kp) return;
+    const int t = static_cast<int>(i / kp), k = static_cast<int>(i % kp);
+    float v = 0.f;
+    if (k < 3 * p * p) {
+        const int c = k / (p * p), ky = (k / p) % p, kx = k % p;
+        const int px = t % G, py = t / G;
+        v = img[static_cast<int64_t>(c) * S * S + static_cast<int64_t>(py * p + ky) * S + px * p + kx];
+    }
+    a[i] = __float2half_rn(v);
+}
+
+cudaError_t im2col_patch(const float *img, int S, int p, int kp, void *a, cudaStream_t s) {
+    const int G = S / p;
+    if (G <= 0 || kp < 3 * p * p) return cudaErrorInvalidValue;
+    im2col_patch_kernel<<<grid_for(static_cast<int64_t>(G) * G * kp, 256), 256, 0, s>>>(img, S, p, G, kp,
+                                                                                       static_cast<__half *>(a));
+    return cudaGetLastError();
+}
+
+// ---- LayerNorm helpers (ggml_norm semantics, warp per row) -------------------
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// mean and 1/sqrt(var + eps) of a row, as ggml_norm computes them
+__device__ __forceinline__ void row_stats(const float *__restrict__ r, int n, float eps, int lane, float &mean,
+                                          float &scale) {
+    double sum = 0.0;
+    for (int i = lane; i < n; i += 32) sum += r[i];
+    sum = warp_sum_d(sum);
+    mean = static_cast<float>(sum / n);
+    double sum2 = 0.0;
+    for (int i = lane; i < n; i += 32) {
+        const float v = __fsub_rn(r[i], mean);
+        sum2 += static_cast<double>(__fmul_rn(v, v));
+    }
+    sum2 = warp_sum_d(sum2);
+    const float variance = static_cast<float>(sum2 / n);
+    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+}
+
+__device__ __forceinline__ float ln_apply(float x, float mean, float scale, float w, float b) {
+    return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(x, mean), scale), w), b);
+}
+
+__global__ void add_pos_ln_kernel(const float *__restrict__ conv, const float *__restrict__ pos, int g, int G, int E,
+                                  const float *__restrict__ w, const float *__restrict__ b, float eps,
+                                  float *__restrict__ x) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= G * G) return;
+    const int gw = (row % G) % g, gh = (row / G) % g;
+    const float *cr = conv + static_cast<int64_t>(row) * E;
+    const float *pr = pos + static_cast<int64_t>(gw + g * gh) * E;
+    float *xr = x + static_cast<int64_t>(row) * E;
+    for (int i = lane; i < E; i += 32) xr[i] = __fadd_rn(cr[i], pr[i]);
+    __syncwarp();
+    float mean, scale;
+    row_stats(xr, E, eps, lane, mean, scale);
+    for (int i = lane; i < E; i += 32) xr[i] = ln_apply(xr[i], mean, scale, w[i], b[i]);
+}
+
+cudaError_t add_pos_layernorm(const float *conv, const float *pos, int g, int G, int E, const float *w,
+                              const float *b, float eps, float *x, cudaStream_t s) {
+    if (E % 32 != 0 || G <= 0 || g <= 0) return cudaErrorInvalidValue;
+    add_pos_ln_kernel<<<grid_for(static_cast<int64_t>(G) * G, 8), 256, 0, s>>>(conv, pos, g, G, E, w, b, eps, x);
+    return cudaGetLastError();
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+           ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+}
+
+// one warp per token row; lane l owns the 32-wide blocks l, l+32, ...
+__global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const float *__restrict__ w,
+                             const float *__restrict__ b, float eps, int G, int win, int8_t *__restrict__ codes,
+                             uint4 *__restrict__ quads, int ld) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= rows) return;
+    const float *xr = x + static_cast<int64_t>(t) * E;
+    float mean, scale;
+    row_stats(xr, E, eps, lane, mean, scale);
+    int r = t;
+    if (win > 0) {  // ggml_win_part position
+        const int tx = t % G, ty = t / G, nw = G / win;
+        r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
+    }
+    const int nblk = E >> 5;
+    for (int blk = lane; blk < nblk; blk += 32) {
+        float y[32];
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(xr + blk * 32 + i);
+            const float4 ww = *reinterpret_cast<const float4 *>(w + blk * 32 + i);
+            const float4 bb = *reinterpret_cast<const float4 *>(b + blk * 32 + i);
+            y[i] = ln_apply(v.x, mean, scale, ww.x, bb.x);
+            y[i + 1] = ln_apply(v.y, mean, scale, ww.y, bb.y);
+            y[i + 2] = ln_apply(v.z, mean, scale, ww.z, bb.z);
+            y[i + 3] = ln_apply(v.w, mean, scale, ww.w, bb.w);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(y[i]));
+        const float d = __fdiv_rn(amax, 127.f);
+        const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            pk[i] = pack4(__float2int_rn(__fmul_rn(y[4 * i], id)), __float2int_rn(__fmul_rn(y[4 * i + 1], id)),
+                          __float2int_rn(__fmul_rn(y[4 * i + 2], id)), __float2int_rn(__fmul_rn(y[4 * i + 3], id)));
+        uint4 *dst = reinterpret_cast<uint4 *>(codes + static_cast<int64_t>(r) * E + blk * 32);
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        quads[static_cast<int64_t>(blk) * ld + r] = make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
+    }
+}
+
+cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
+                         void *codes, void *quads, int ld, cudaStream_t s) {
+    if (E % 32 != 0 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows != G * G)))
+        return cudaErrorInvalidValue;
+    ln_q8_kernel<<<grid_for(rows, 8), 256, 0, s>>>(x, rows, E, w, b, eps, G, win, static_cast<int8_t *>(codes),
+                                                   static_cast<uint4 *>(quads), ld);
+    return cudaGetLastError();
+}
+
+// ---- qkv split + RoPE ---------------------------------------------------------
+__global__ void qkv_rope_kernel(const float *__restrict__ qkv, const float *__restrict__ freqs, int B, int N, int E,
+                                int heads, __nv_bfloat16 *__restrict__ q, __nv_bfloat16 *__restrict__ k,
+                                __nv_bfloat16 *__restrict__ v) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (row, head, pair)
+    if (i >= static_cast<int64_t>(B) * N * heads * 32) return;
+    const int pr = static_cast<int>(i & 31);
+    const int h = static_cast<int>((i >> 5) % heads);
+    const int64_t row = (i >> 5) / heads;
+    const int n = static_cast<int>(row % N), bb = static_cast<int>(row / N);
+    const float *src = qkv + row * 3 * E + h * 64 + 2 * pr;
+    const float2 qq = *reinterpret_cast<const float2 *>(src);
+    const float2 kk = *reinterpret_cast<const float2 *>(src + E);
+    const float2 vv = *reinterpret_cast<const float2 *>(src + 2 * E);
+    float2 qo = qq, ko = kk;
+    if (freqs) {
+        const float2 cs = *reinterpret_cast<const float2 *>(freqs + (static_cast<int64_t>(n) * 32 + pr) * 2);
+        qo.x = __fsub_rn(__fmul_rn(qq.x, cs.x), __fmul_rn(qq.y, cs.y));
+        qo.y = __fadd_rn(__fmul_rn(qq.x, cs.y), __fmul_rn(qq.y, cs.x));
+        ko.x = __fsub_rn(__fmul_rn(kk.x, cs.x), __fmul_rn(kk.y, cs.y));
+        ko.y = __fadd_rn(__fmul_rn(kk.x, cs.y), __fmul_rn(kk.y, cs.x));
+    }
+    const int64_t o = ((static_cast<int64_t>(bb) * heads + h) * N + n) * 64 + 2 * pr;
+    *reinterpret_cast<__nv_bfloat162 *>(q + o) = __floats2bfloat162_rn(qo.x, qo.y);
+    *reinterpret_cast<__nv_bfloat162 *>(k + o) = __floats2bfloat162_rn(ko.x, ko.y);
+    *reinterpret_cast<__nv_bfloat162 *>(v + o) = __floats2bfloat162_rn(vv.x, vv.y);
+}
+
+cudaError_t qkv_rope_split(const float *qkv, const float *freqs, int B, int N, int E, int heads, void *q, void *k,
+                           void *v, cudaStream_t s) {
+    if (E != heads * 64 || B <= 0 || N <= 0) return cudaErrorInvalidValue;
+    qkv_rope_kernel<<<grid_for(static_cast<int64_t>(B) * N * heads * 32, 256), 256, 0, s>>>(
+        qkv, freqs, B, N, E, heads, static_cast<__nv_bfloat16 *>(q), static_cast<__nv_bfloat16 *>(k),
+        static_cast<__nv_bfloat16 *>(v));
+    return cudaGetLastError();
+}
+
+__global__ void rowmap_kernel(int G, int win, int *__restrict__ rowmap) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= G * G) return;
+    const int tx = t % G, ty = t / G, nw = G / win;
+    const int r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
+    rowmap[r] = t;
+}
+
+cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s) {
+    if (win <= 0 || G % win != 0) return cudaErrorInvalidValue;
+    rowmap_kernel<<<grid_for(static_cast<int64_t>(G) * G, 256), 256, 0, s>>>(G, win, rowmap);
+    return cudaGetLastError();
+}
+
+// ---- neck helpers ----------------------------------------------------------------
+__global__ void f32_to_f16_kernel(const float4 *__restrict__ x, int64_t n4, uint2 *__restrict__ y) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const float4 v = x[i];
+    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    y[i] = make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&b));
+}
+
+cudaError_t f32_to_f16(const float *x, int64_t n, void *y, cudaStream_t s) {
+    if (n % 4 != 0) return cudaErrorInvalidValue;
+    f32_to_f16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(reinterpret_cast<const float4 *>(x), n / 4,
+                                                           static_cast<uint2 *>(y));
+    return cudaGetLastError();
+}
+
+__global__ void maxpool_kernel(const float *__restrict__ x, int G, int C, __half *__restrict__ y) {
+    const int g = G / 2;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(g) * g * C) return;
+    const int c = static_cast<int>(i % C);
+    const int p = static_cast<int>(i / C), ox = p % g, oy = p / g;
+    const float *b0 = x + (static_cast<int64_t>(2 * oy) * G + 2 * ox) * C + c;
+    float m = b0[0];
+    const float v1 = b0[C], v2 = b0[static_cast<int64_t>(G) * C], v3 = b0[static_cast<int64_t>(G) * C + C];
+    if (v1 > m) m = v1;
+    if (v2 > m) m = v2;
+    if (v3 > m) m = v3;
+    y[i] = __float2half_rn(m);
+}
+
+cudaError_t maxpool2x2_f16(const float *x, int G, int C, void *y, cudaStream_t s) {
+    if (G % 2 != 0) return cudaErrorInvalidValue;
+    maxpool_kernel<<<grid_for(static_cast<int64_t>(G / 2) * (G / 2) * C, 256), 256, 0, s>>>(x, G, C,
+                                                                                            static_cast<__half *>(y));
+    return cudaGetLastError();
+}
+
+// one thread per (pixel, tap, 8 channels)
+__global__ void im2col3x3_kernel(const uint4 *__restrict__ x, int W, int H, int C8, uint4 *__restrict__ a) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(W) * H * 9 * C8) return;
+    const int c8 = static_cast<int>(i % C8);
+    const int tap = static_cast<int>((i / C8) % 9);
+    const int64_t p = i / (9 * C8);
+    const int px = static_cast<int>(p % W), py = static_cast<int>(p / W);
+    const int sx = px + tap % 3 - 1, sy = py + tap / 3 - 1;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (sx >= 0 && sy >= 0 && sx < W && sy < H) v = x[(static_cast<int64_t>(sy) * W + sx) * C8 + c8];
+    a[i] = v;
+}
+
+cudaError_t im2col3x3_f16(const void *x, int W, int H, int C, void *a, cudaStream_t s) {
+    if (C % 8 != 0) return cudaErrorInvalidValue;
+    im2col3x3_kernel<<<grid_for(static_cast<int64_t>(W) * H * 9 * (C / 8), 256), 256, 0, s>>>(
+        static_cast<const uint4 *>(x), W, H, C / 8, static_cast<uint4 *>(a));
+    return cudaGetLastError();
+}
+
+}  // namespace b200

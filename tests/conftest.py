@@ -40,3 +40,17 @@ def backend(b200):
     be = b200.Backend(0)
     yield be
     be.free()
+
+
+@pytest.fixture(scope="session")
+def model():
+    return _load_pkg_module("model")
+
+
+def rel_err(got, ref):
+    """max |got - ref| / max |ref| -- the normwise form of the north-star
+    bound 'fp32 tensor outputs within max relative error 1e-2'."""
+    import numpy as np
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))

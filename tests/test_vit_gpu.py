@@ -1,0 +1,122 @@
+"""GPU parity of the SAM3 visual encoder (sam3_encode_image, sam3.cpp:6028)
+against the CPU oracle, through the C ABI, stage by stage and end to end.
+
+Tolerance (north-star bound for fp32 tensors): max|got - ref| / max|ref|
+<= 1e-2.  Preprocessing is integer-exact and checked bit for bit.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def small(model, oracle, backend):
+    hp = model.SAM3_VIT_TEST
+    tensors = model.random_vit_weights(hp, seed=1)
+    vit = backend.vit(hp)
+    vit.load(tensors)
+    ov = oracle.OracleVit(hp, tensors)
+    yield hp, tensors, vit, ov
+    vit.free()
+
+
+@pytest.mark.parametrize("w,h", [(672, 672), (500, 380), (1200, 1198)])
+def test_preprocess_bit_exact(model, oracle, backend, small, w, h):
+    hp, _, _, ov = small
+    rgb = np.random.default_rng(w + h).integers(0, 256, size=(h, w, 3), dtype=np.uint8)
+    src = backend.upload(rgb)
+    out = backend.alloc(3 * hp["img"] ** 2 * 4)
+    backend.preprocess(src, w, h, hp["img"], out)
+    backend.synchronize()
+    got = out.get((3, hp["img"], hp["img"]), np.float32)
+    assert np.array_equal(got, ov.preprocess(rgb))
+
+
+def test_prefix(backend, small):
+    hp, _, vit, ov = small
+    img = ov.preprocess(np.random.default_rng(3).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8))
+    ref = ov.prefix(img)
+    dimg, dx = backend.upload(img), backend.alloc(ref.nbytes)
+    vit.run_prefix(dimg, dx)
+    backend.synchronize()
+    assert rel_err(dx.get(ref.shape, np.float32), ref) <= TOL
+
+
+@pytest.mark.parametrize("idx", [0, 1])  # block 0 windowed, block 1 global
+def test_block(backend, small, idx):
+    hp, _, vit, ov = small
+    x = np.random.default_rng(idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
+    ref = ov.block(idx, x)
+    dx = backend.upload(x)
+    vit.run_block(idx, dx)
+    backend.synchronize()
+    err = rel_err(dx.get(ref.shape, np.float32), ref)
+    assert err <= TOL, err
+
+
+def test_neck(backend, small):
+    hp, _, vit, ov = small
+    x = np.random.default_rng(9).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
+    refs = ov.neck(x)
+    vit.run_neck(backend.upload(x))
+    for i, ref in enumerate(refs):
+        err = rel_err(vit.output_host(i), ref)
+        assert err <= TOL, (i, err)
+
+
+def test_encode_end_to_end(small):
+    hp, _, vit, ov = small
+    rgb = np.random.default_rng(5).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8)
+    x_ref, outs_ref = ov.encode(rgb)
+    outs = vit.encode(rgb)
+    assert rel_err(vit.output_host(-1).reshape(x_ref.shape), x_ref) <= TOL
+    for i in range(4):
+        err = rel_err(outs[i], outs_ref[i])
+        assert err <= TOL, (i, err)
+
+
+def test_encode_twice_is_deterministic(small):
+    hp, _, vit, _ = small
+    rgb = np.random.default_rng(6).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8)
+    a = vit.encode(rgb)
+    b = vit.encode(rgb)
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)
+
+
+@pytest.fixture(scope="module")
+def full8(model, oracle, backend):
+    """SAM3 ViT-32 geometry (1008^2, embed 1024, 16 heads, mlp 4736) with 8
+    blocks, block 7 global -- the two block kinds at full size."""
+    hp = dict(model.SAM3_VIT, depth=8, global_idx=(7,))
+    tensors = model.random_vit_weights(hp, seed=2)
+    vit = backend.vit(hp)
+    vit.load(tensors)
+    yield hp, vit, oracle.OracleVit(hp, tensors)
+    vit.free()
+
+
+@pytest.mark.parametrize("idx", [0, 7])
+def test_full_size_block(backend, full8, idx):
+    hp, vit, ov = full8
+    x = np.random.default_rng(idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
+    ref = ov.block(idx, x)
+    dx = backend.upload(x)
+    vit.run_block(idx, dx)
+    backend.synchronize()
+    err = rel_err(dx.get(ref.shape, np.float32), ref)
+    assert err <= TOL, err
+
+
+def test_missing_weights_fail_loudly(b200, backend, model):
+    hp = model.SAM3_VIT_TEST
+    vit = backend.vit(hp)
+    with pytest.raises(b200.B200Error):
+        vit.encode(np.zeros((hp["img"], hp["img"], 3), np.uint8))
+    with pytest.raises(b200.B200Error):
+        vit.set_tensor("vit.blocks.0.attn.qkv.weight", 1, np.zeros(4, np.float32), (2, 2))
+    vit.free()
