@@ -116,6 +116,23 @@ long long sam3b200_backend_launch_count(const sam3b200_backend *be);
 int sam3b200_backend_profile(sam3b200_backend *be, int enable);
 int sam3b200_backend_profile_read(sam3b200_backend *be, int cls, double *total_ms, int *n);
 
+/* MUL_MAT that allocates nothing.  No counterpart in the reference: it is
+ * for callers that cannot let the library call cudaMalloc while they
+ * compute -- a framework that plans all device memory up front (as ggml's
+ * graph allocator does for a backend's graph_compute) or a latency-bound
+ * loop that cannot take cudaMalloc's implicit synchronisation.  Same
+ * arguments and result as sam3b200_mul_mat; the quantised activations go to
+ * a fixed 48 MiB array compiled into the library (resident on every GPU
+ * that loads it, until the process exits) instead of backend scratch.
+ * Shapes whose scratch (M*K bytes of codes + K/32 * roundup(M,128) * 16
+ * bytes of scales) exceeds 48 MiB are rejected with an error message.  The
+ * first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls on a device share the
+ * array: calls that overlap on the GPU race and must be serialised by the
+ * caller.  Asynchronous on the backend stream. */
+int sam3b200_mul_mat_noalloc(sam3b200_backend *be, const sam3b200_weight *w, const float *x, int64_t ldx, int64_t M,
+                             const float *bias, float *dst, int64_t ldd);
+
 /* Select the MUL_MAT kernel (SAM3B200_MMQ_*); returns the previous one. */
 int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
 

@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_weight_free": (None, [vp, vp]),
         "sam3b200_mul_mat": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
         "sam3b200_mul_mat_block_dots": (i32, [vp, vp, vp, i64, vp]),
+        "sam3b200_mul_mat_noalloc": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
         "sam3b200_set_mmq_impl": (i32, [vp, i32]),
         "sam3b200_vit_create": (vp, [vp, vp]),
         "sam3b200_vit_free": (None, [vp]),
@@ -264,6 +265,13 @@ class Backend:
         st = lib().sam3b200_mul_mat(self.h, w.h, x.ptr, ldx or w.K, M, bias.ptr if bias else None, y.ptr,
                                     ldy or w.N)
         _check(st, "mul_mat")
+
+    def mul_mat_noalloc(self, w: Weight, x: DeviceBuffer, M: int, y: DeviceBuffer,
+                        bias: DeviceBuffer | None = None) -> None:
+        """sam3b200_mul_mat_noalloc: the MUL_MAT with its activation scratch in
+        the library's fixed device array (for callers that cannot allocate)."""
+        st = lib().sam3b200_mul_mat_noalloc(self.h, w.h, x.ptr, w.K, M, bias.ptr if bias else None, y.ptr, w.N)
+        _check(st, "mul_mat_noalloc")
 
     def mul_mat_block_dots(self, w: Weight, x: DeviceBuffer, M: int) -> np.ndarray:
         nb = w.K // 32

@@ -1,0 +1,103 @@
+// mmq_static.cu -- sam3b200_mul_mat_noalloc: the quantised MUL_MAT for
+// callers that cannot allocate device memory.
+//
+// sam3b200_mul_mat quantises the activations into scratch buffers that the
+// backend allocates (and grows) with cudaMalloc on demand.  Some callers
+// cannot let that happen while they compute: a host framework that plans
+// every device byte up front (ggml's graph allocator hands a backend its
+// buffers and expects graph_compute to allocate nothing), or a latency-bound
+// loop that cannot absorb cudaMalloc's implicit device synchronisation and
+// its failure path.  This entry point computes the same result with its
+// scratch in a fixed array compiled into the library instead.
+//
+// The array lives in device memory of every GPU that loads the library, for
+// the life of the process, and is shared by all calls on that device: two
+// calls that overlap on the GPU (different streams or backends on the same
+// device) race on it and must be serialised by the caller.
+#include "../../include/sam3_b200.h"
+#include "backend_impl.h"
+#include "mmq.cuh"
+
+#include <mutex>
+
+namespace b200 {
+
+// 48 MiB: enough for every MUL_MAT of the SAM3 ViT-32 at 5184 tokens
+// (largest: mlp.lin2, K = 4736: 24.6 MB of codes + 12.4 MB of scale quads).
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(48) << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int MAX_DEVICES = 64;
+std::mutex g_addr_mutex;
+void *g_addr[MAX_DEVICES] = {nullptr};
+
+// Device address of the scratch array on `device`, resolved once per device
+// with that device current (the array's host-side name is only a stand-in).
+void *scratch_address(int device) {
+    if (device < 0 || device >= MAX_DEVICES) return nullptr;
+    std::lock_guard<std::mutex> lock(g_addr_mutex);
+    if (!g_addr[device]) {
+        void *p = nullptr;
+        if (!cuda_ok(cudaSetDevice(device), "cudaSetDevice") ||
+            !cuda_ok(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)"))
+            return nullptr;
+        g_addr[device] = p;
+    }
+    return g_addr[device];
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weight *wh, const float *x, int64_t ldx,
+                                        int64_t M, const float *bias, float *dst, int64_t ldd) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    auto *w = reinterpret_cast<const Weight *>(wh);
+    if (!be || !w || !x || !dst) {
+        set_error("mul_mat_noalloc: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (M <= 0 || M > (1 << 24) || ldx < w->K || ldd < w->N) {
+        set_error("mul_mat_noalloc: bad shape M=%lld ldx=%lld ldd=%lld for K=%d N=%d", (long long)M, (long long)ldx,
+                  (long long)ldd, w->K, w->N);
+        return SAM3B200_STATUS_FAILED;
+    }
+    const int Mi = static_cast<int>(M);
+    const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
+    const size_t codes_bytes = (static_cast<size_t>(Mi) * w->K + 255) / 256 * 256;
+    const size_t quad_bytes = static_cast<size_t>(w->K / 32) * lda * 16;
+    if (codes_bytes + quad_bytes > NOALLOC_SCRATCH_BYTES) {
+        set_error("mul_mat_noalloc: M=%d x K=%d needs %zu bytes of scratch, more than the fixed %zu-byte array "
+                  "(use sam3b200_mul_mat, or split M)",
+                  Mi, w->K, codes_bytes + quad_bytes, NOALLOC_SCRATCH_BYTES);
+        return SAM3B200_STATUS_FAILED;
+    }
+    unsigned char *base = static_cast<unsigned char *>(scratch_address(be->device));
+    if (!base) return SAM3B200_STATUS_FAILED;
+    if (!cuda_ok(cudaSetDevice(be->device), "cudaSetDevice")) return SAM3B200_STATUS_FAILED;
+    void *codes = base;
+    void *quads = base + codes_bytes;
+    // Nothing in the scratch has to start at zero: every code and scale of
+    // rows [0, M) is rewritten below, and padding rows [M, lda) only feed
+    // output rows that are never stored.
+    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, codes, quads, lda, be->stream), "quantize activations"))
+        return SAM3B200_STATUS_FAILED;
+    MmqArgs a;
+    a.a = QMatrix{codes, quads, Mi, w->K, lda};
+    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld};
+    a.bias = bias;
+    a.y = dst;
+    a.ldy = ldd;
+    a.dump = nullptr;
+    a.err = be->err;
+    be->count(2);
+    const cudaError_t e = Mi < 64 ? mmq_simt(a, MMQ_OUT_F32, be->stream)
+                                  : mmq_tc(a, MMQ_OUT_F32, be->num_sms, be->stream, be->mmq_cvt);
+    if (!cuda_ok(e, "mul_mat_noalloc launch")) return SAM3B200_STATUS_FAILED;
+    return SAM3B200_STATUS_SUCCESS;
+}
