@@ -172,6 +172,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--images", type=int, default=BATCH,
+                    help="images per step (default 64, the config's batch; smaller only for profiling runs)")
     args = ap.parse_args()
 
     model_mod = _load("model")
@@ -195,8 +197,9 @@ def main():
     del tensors
 
     S = hp["img"]
-    mine = list(range(rank, BATCH, world))
-    imgs = model_mod.random_images(BATCH, S, seed=1234)[mine]
+    batch = args.images
+    mine = list(range(rank, batch, world))
+    imgs = model_mod.random_images(batch, S, seed=1234)[mine]
     dev_imgs = [be.upload(im) for im in imgs]
     pinned = torch.from_numpy(imgs).pin_memory()
     stream = torch.cuda.ExternalStream(be.stream)
@@ -254,7 +257,7 @@ def main():
         step_e2e()
     e2e_ms = timed(step_e2e, args.steps)
 
-    images = BATCH * args.steps
+    images = batch * args.steps
     value = images / (ms / 1000.0)
     e2e = images / (e2e_ms / 1000.0)
     ops = vit_ops_per_image(hp)
@@ -270,12 +273,12 @@ def main():
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "cfg3: SAM3 visual-only ViT-32 (Q8_0) + trk SimpleFPN neck, 1008x1008, "
                                    "64 seeded uint8 images per step split across ranks",
-                       "global_batch": BATCH, "seq_len": (S // hp["patch"]) ** 2, "parallelism": f"dp{world}",
+                       "global_batch": batch, "seq_len": (S // hp["patch"]) ** 2, "parallelism": f"dp{world}",
                        "weights": "random-init N(0,0.02), Q8_0 reference quantiser rule",
                        "l2": "no flush: per-image working set (~0.5 GB of weights) exceeds the 126 MB L2"},
             "e2e": {"value": e2e, "unit": "images/s",
-                    "h2d_bytes_per_step": int(BATCH * S * S * 3 // world),
-                    "d2h_bytes_per_step": int(small.nbytes * BATCH // world)},
+                    "h2d_bytes_per_step": int(batch * S * S * 3),
+                    "d2h_bytes_per_step": int(small.nbytes * batch)},
             "roofline": {"kernel": "mmq_tc_kernel (quantised MUL_MAT, 4 per ViT block)", "bound": "tensor",
                          "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
                          "frac": achieved / peak_int8 if peak_int8 else None, "traffic": None,
