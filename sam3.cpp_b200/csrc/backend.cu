@@ -115,6 +115,7 @@ sam3b200_backend *sam3b200_backend_init(int device) {
     be->device = device;
     be->num_sms = prop.multiProcessorCount;
     if (const char *ev = getenv("SAM3B200_MMQ_CVT")) be->mmq_cvt = atoi(ev) == 0 ? 0 : 1;
+    if (const char *ev = getenv("SAM3B200_MMQ_BN")) be->mmq_bn = atoi(ev) == 128 ? 128 : 64;
     snprintf(be->name, sizeof(be->name), "B200[%d] %s", device, prop.name);
     if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
         !cuda_ok(cudaMalloc(&be->err, sizeof(int)), "cudaMalloc(err)") ||
@@ -308,7 +309,7 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     be->count(2);
     be->prof_mark(0);
     if (impl == SAM3B200_MMQ_SIMT) e = mmq_simt(a, mode, be->stream);
-    else e = mmq_tc(a, mode, be->num_sms, be->stream, be->mmq_cvt);
+    else e = mmq_tc(a, mode, be->num_sms, be->stream, be->mmq_cvt, be->mmq_bn);
     be->prof_mark(0);
     if (!cuda_ok(e, "mul_mat launch")) return SAM3B200_STATUS_FAILED;
     return SAM3B200_STATUS_SUCCESS;

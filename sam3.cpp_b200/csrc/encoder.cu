@@ -203,7 +203,7 @@ static bool mmq(Vit *v, const void *codes, const void *quads, const QWeight &w, 
     a.out_quads = out_quads;
     a.out_ld = v->Tpad;
     v->be->prof_mark(0);
-    const bool ok = launched(v, mmq_tc(a, mode, v->be->num_sms, v->be->stream, v->be->mmq_cvt), "mmq");
+    const bool ok = launched(v, mmq_tc(a, mode, v->be->num_sms, v->be->stream, v->be->mmq_cvt, v->be->mmq_bn), "mmq");
     v->be->prof_mark(0);
     return ok;
 }

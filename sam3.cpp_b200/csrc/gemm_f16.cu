@@ -70,60 +70,65 @@ __global__ void __launch_bounds__(GCfg::THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
-                for (int ks = 0; ks < kstages; ++ks) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, 1)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sb = smem + stage * C::STAGE_BYTES;
+        // TMA producer: warp-uniform loop, one elected lane issues
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, err, 1))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *sb = smem + stage * C::STAGE_BYTES;
+                if (elect_one()) {
                     mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
                     tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);
                     tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                }
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16_f32(C::BM, C::BN);
-            int stage = 0;
-            uint32_t phase = 0, it = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-                const uint32_t buf = it & 1u;
-                if (!mbar_wait(&tempty[buf], ((it >> 1) & 1u) ^ 1u, err, 4)) break;
+        // MMA issuer: warp-uniform loop, one elected lane issues
+        constexpr uint32_t idesc = idesc_f16_f32(C::BM, C::BN);
+        int stage = 0;
+        uint32_t phase = 0, it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+            const uint32_t buf = it & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tempty[buf], ((it >> 1) & 1u) ^ 1u, err, 4))) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + buf * C::BN;
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, 2))) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + buf * C::BN;
-                for (int ks = 0; ks < kstages; ++ks) {
-                    if (!mbar_wait(&full[stage], phase, err, 2)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-                    const uint32_t b_addr = a_addr + C::A_BYTES;
+                const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+                const uint32_t b_addr = a_addr + C::A_BYTES;
+                if (elect_one()) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_f16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
                                 (ks | kk) != 0);
                     mma_commit(&empty[stage]);
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
                 }
-                if (!ok) break;
-                mma_commit(&tfull[buf]);
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
             }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&tfull[buf]);
+            __syncwarp();
         }
     } else {
         const int q = warp & 3;

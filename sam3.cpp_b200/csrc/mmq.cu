@@ -38,7 +38,7 @@ __device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
 
 template <bool VEC>
 __global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
-                                        int8_t *__restrict__ codes, uint4 *__restrict__ quads, int ld) {
+                                        int8_t *__restrict__ codes, __half *__restrict__ quads, int ld) {
     const int per_row = K >> 3;  // threads per row
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const bool active = t < static_cast<int64_t>(M) * per_row;
@@ -75,7 +75,7 @@ __global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx
     *reinterpret_cast<uint2 *>(codes + static_cast<int64_t>(m) * K + e) =
         make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
     if ((e & 31) == 0)
-        quads[static_cast<int64_t>(e >> 5) * ld + m] = make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
+        quads[act_quad_index(e >> 5, m, ld)] = __float2half_rn(d);
 }
 
 cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
@@ -88,10 +88,10 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
     const bool vec = (ldx % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     if (vec)
         quantize_rows_q8_kernel<true><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
-                                                                 static_cast<uint4 *>(quads), ld);
+                                                                 static_cast<__half *>(quads), ld);
     else
         quantize_rows_q8_kernel<false><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
-                                                                  static_cast<uint4 *>(quads), ld);
+                                                                  static_cast<__half *>(quads), ld);
     return cudaGetLastError();
 }
 
@@ -118,8 +118,10 @@ __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ block
     }
     codes[static_cast<int64_t>(n) * K + b * 32 + lane] = static_cast<int8_t>(code);
     if (lane == 0) {
-        const uint16_t dbits = static_cast<uint16_t>(blk[0] | (blk[1] << 8));
-        quads[static_cast<int64_t>(b) * ld + n] = make_uint4(dbits, 0u, 0u, 0u);
+        const uint32_t dbits = static_cast<uint32_t>(blk[0] | (blk[1] << 8));
+        uint32_t rec[4] = {0u, 0u, 0u, 0u};  // d in fp16 slot b % 8
+        rec[(b & 7) >> 1] = (b & 1) ? (dbits << 16) : dbits;
+        quads[static_cast<int64_t>(b) * ld + n] = make_uint4(rec[0], rec[1], rec[2], rec[3]);
     }
 }
 
@@ -150,23 +152,27 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
 // Shared memory: STAGES x 48 KB stages, a 2 KB zero region (the unused
 // second K-chunk of every scale operand), barriers.
 // ---------------------------------------------------------------------------
+template <int BN_, int EPI_ = 8>
 struct TcCfg {
     static constexpr int BM = 128;
-    static constexpr int BN = 128;
+    static constexpr int BN = BN_;
     static constexpr int BLK = 4;                   // K-blocks per stage
     static constexpr int BK = 32 * BLK;             // int8 per stage row: 128 bytes = one swizzle atom
     static constexpr int A_BYTES = BM * BK;         // 16 KB
-    static constexpr int B_BYTES = BN * BK;         // 16 KB
-    static constexpr int Q_BYTES = 128 * 16;        // one block's scale operand: 2 KB
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + 2 * BLK * Q_BYTES;
-    static constexpr int STAGES = 4;
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int Q_BYTES = BM * 16;         // one block's A scale operand: 2 KB
+    static constexpr int QB_BYTES = BN * 16;        // one block's B scale operand
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES + BLK * QB_BYTES;  // A scales: one group record
+    static constexpr int STAGES = BN == 128 ? 4 : 6;
     static constexpr int ZERO_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = ZERO_OFF + Q_BYTES;
-    static constexpr int EPI_WARPS = 8;
+    static constexpr int EPI_WARPS = EPI_;           // 8 or 16 epilogue warps
     static constexpr int THREADS = 64 + EPI_WARPS * 32;
-    static constexpr int COLS = BN / 2;             // per epilogue thread
+    static constexpr int COLS = BN / (EPI_WARPS / 4);  // per epilogue thread
     static constexpr int CHUNK = 32;
-    static constexpr int TMEM_COLS = 512;           // 2 buffers x (I 128 + S 128)
+    static constexpr int SLOT_COLS = 2 * BN;        // one K-block: I (BN columns) then S (BN columns)
+    static constexpr int SLOTS = 512 / SLOT_COLS;   // K-blocks in flight between MMA and epilogue
+    static constexpr int TMEM_COLS = 512;
     static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
     static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -205,7 +211,7 @@ struct MmqEpi {
     const int *rowmap;
     int gelu;
     int8_t *qcodes;
-    uint4 *qquads;
+    __half *qquads;
     int qld;
 };
 
@@ -218,21 +224,21 @@ __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
            ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
-template <int MODE, int CVT>
-__global__ void __launch_bounds__(TcCfg::THREADS, 1)
+template <int MODE, int CVT, int BN, int EPI>
+__global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                  const __grid_constant__ CUtensorMap tm_qa, const __grid_constant__ CUtensorMap tm_qb, int M, int N,
-                  int nblk, const MmqEpi ep, int *__restrict__ err) {
+                  const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
+                  int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err) {
     const float *__restrict__ bias = ep.bias;
     int32_t *__restrict__ dump = ep.dump;
-    using C = TcCfg;
+    using C = TcCfg<BN, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *empty = full + C::STAGES;
     uint64_t *tfull = empty + C::STAGES;
-    uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *tempty = tfull + C::SLOTS;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + C::SLOTS);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -250,15 +256,14 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < C::SLOTS; ++i) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], C::EPI_WARPS);
         }
         fence_mbar_init();
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
-        prefetch_tmap(&tm_qa);
-        prefetch_tmap(&tm_qb);
+
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -270,77 +275,88 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int m0 = (t % num_m) * C::BM;
-                const int n0 = (t / num_m) * C::BN;
-                for (int ks = 0; ks < kstages; ++ks) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1u, err, ERR_WAIT_EMPTY)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sb = smem + stage * C::STAGE_BYTES;
-                    uint8_t *q = sb + C::A_BYTES + C::B_BYTES;
-                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+        // ---- TMA producer: warp-uniform loop, one elected lane issues ----
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            const int m0 = (t % num_m) * C::BM;
+            const int n0 = (t / num_m) * C::BN;
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, err, ERR_WAIT_EMPTY))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *sb = smem + stage * C::STAGE_BYTES;
+                uint8_t *q = sb + C::A_BYTES + C::B_BYTES;
+                if (elect_one()) {
+                    // scale records are contiguous per (group or block, tile): one bulk copy each
+                    const int b0 = ks * C::BLK;
+                    const int nb = nblk - b0 < C::BLK ? nblk - b0 : C::BLK;
+                    mbar_arrive_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES + C::Q_BYTES + nb * C::QB_BYTES);
                     tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);
                     tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
-                    tma_load_3d(q, &tm_qa, &full[stage], 0, m0, ks * C::BLK);
-                    tma_load_3d(q + C::BLK * C::Q_BYTES, &tm_qb, &full[stage], 0, n0, ks * C::BLK);
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                    bulk_load(q, quads_a + (static_cast<int64_t>(b0 >> 3) * lda_q + m0) * 16, C::Q_BYTES, &full[stage]);
+                    for (int j = 0; j < nb; ++j)
+                        bulk_load(q + C::Q_BYTES + j * C::QB_BYTES,
+                                  quads_b + (static_cast<int64_t>(b0 + j) * ldb_q + n0) * 16, C::QB_BYTES, &full[stage]);
+                }
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc_i = idesc_s8_s32(C::BM, C::BN);
-            constexpr uint32_t idesc_s = idesc_f16_f32(C::BM, C::BN);
-            const uint32_t zero_addr = smem_u32(smem + C::ZERO_OFF);
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t blk = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                for (int ks = 0; ks < kstages; ++ks) {
-                    if (!mbar_wait(&full[stage], phase, err, ERR_WAIT_FULL_MMA)) {
+        // ---- MMA issuer: warp-uniform loop, one elected lane issues ----
+        constexpr uint32_t idesc_i = idesc_s8_s32(C::BM, C::BN);
+        constexpr uint32_t idesc_s = idesc_f16_f32(C::BM, C::BN);
+        const uint32_t zero_addr = smem_u32(smem + C::ZERO_OFF);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t blk = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, ERR_WAIT_FULL_MMA))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+                const uint32_t b_addr = a_addr + C::A_BYTES;
+                const uint32_t q_addr = b_addr + C::B_BYTES;
+                const uint64_t qa_desc = noswz_kmajor_desc(q_addr, zero_addr - q_addr);
+                for (int j = 0; j < C::BLK; ++j) {
+                    if (ks * C::BLK + j >= nblk) break;
+                    const uint32_t buf = blk % C::SLOTS;
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&tempty[buf], ((blk / C::SLOTS) & 1u) ^ 1u, err, ERR_WAIT_TEMPTY))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
-                    const uint32_t b_addr = a_addr + C::A_BYTES;
-                    const uint32_t q_addr = b_addr + C::B_BYTES;
-                    for (int j = 0; j < C::BLK; ++j) {
-                        if (ks * C::BLK + j >= nblk) break;
-                        const uint32_t buf = blk & 1u;
-                        if (!mbar_wait(&tempty[buf], ((blk >> 1) & 1u) ^ 1u, err, ERR_WAIT_TEMPTY)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t d_tmem = tmem_base + buf * 256;
-                        const uint32_t koff = static_cast<uint32_t>(j * 32);  // 32 int8 = 32 bytes
-                        mma_i8(d_tmem, sw128_kmajor_desc(a_addr + koff), sw128_kmajor_desc(b_addr + koff), idesc_i, 0);
-                        if constexpr (MODE != MMQ_OUT_BLOCKDOTS) {
-                            const uint32_t qa = q_addr + j * C::Q_BYTES;
-                            const uint32_t qb = q_addr + (C::BLK + j) * C::Q_BYTES;
-                            mma_f16(d_tmem + 128, noswz_kmajor_desc(qa, zero_addr - qa),
-                                    noswz_kmajor_desc(qb, zero_addr - qb), idesc_s, 0);
-                        }
+                    const uint32_t d_tmem = tmem_base + buf * C::SLOT_COLS;
+                    const uint32_t koff = static_cast<uint32_t>(j * 32);  // 32 int8 = 32 bytes
+                    const uint64_t a_desc = sw128_kmajor_desc(a_addr + koff);
+                    const uint64_t b_desc = sw128_kmajor_desc(b_addr + koff);
+                    const uint32_t qb = q_addr + C::Q_BYTES + j * C::QB_BYTES;
+                    const uint64_t qb_desc = noswz_kmajor_desc(qb, zero_addr - qb);
+                    if (elect_one()) {
+                        mma_i8(d_tmem, a_desc, b_desc, idesc_i, 0);
+                        if constexpr (MODE != MMQ_OUT_BLOCKDOTS) mma_f16(d_tmem + C::BN, qa_desc, qb_desc, idesc_s, 0);
                         mma_commit(&tfull[buf]);
-                        ++blk;
                     }
-                    if (!ok) break;
-                    mma_commit(&empty[stage]);
-                    if (++stage == C::STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
+                    __syncwarp();
+                    ++blk;
+                }
+                if (!ok) break;
+                if (elect_one()) mma_commit(&empty[stage]);
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
                 }
             }
         }
@@ -361,18 +377,18 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < C::COLS; ++i) acc[i] = 0.f;
             for (int b = 0; b < nblk; ++b) {
-                const uint32_t buf = blk & 1u;
-                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (blk >> 1) & 1u, err, ERR_WAIT_TFULL))) {
+                const uint32_t buf = blk % C::SLOTS;
+                if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (blk / C::SLOTS) & 1u, err, ERR_WAIT_TFULL))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tmem_base + lane_addr + buf * 256 + h * C::COLS;
+                const uint32_t ta = tmem_base + lane_addr + buf * C::SLOT_COLS + h * C::COLS;
 #pragma unroll
                 for (int c0 = 0; c0 < C::COLS; c0 += CHUNK) {
                     uint32_t vi[CHUNK], vs[CHUNK];
                     tmem_ld_32x32b_x32(ta + c0, vi);
-                    if constexpr (MODE != MMQ_OUT_BLOCKDOTS) tmem_ld_32x32b_x32(ta + 128 + c0, vs);
+                    if constexpr (MODE != MMQ_OUT_BLOCKDOTS) tmem_ld_32x32b_x32(ta + C::BN + c0, vs);
                     tmem_wait_ld();
                     if (c0 + CHUNK == C::COLS) {
                         // the whole buffer is in registers: hand it back to the MMA warp
@@ -469,8 +485,7 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
                         uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
                         dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                         dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                        ep.qquads[static_cast<int64_t>((nb + hb) >> 5) * ep.qld + m] =
-                            make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
+                        ep.qquads[act_quad_index((nb + hb) >> 5, m, ep.qld)] = __float2half_rn(d);
                     }
                 }
             }
@@ -485,22 +500,17 @@ __global__ void __launch_bounds__(TcCfg::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-template <int MODE, int CVT>
+template <int MODE, int CVT, int BN, int EPI>
 static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
-    using C = TcCfg;
+    using C = TcCfg<BN, EPI>;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K, nblk = K / 32;
-    CUtensorMap tma, tmb, tmqa, tmqb;
+    CUtensorMap tma, tmb;
     const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, db[2] = {uint64_t(K), uint64_t(N)}, sk[1] = {uint64_t(K)};
     const uint32_t bxa[2] = {C::BK, C::BM}, bxb[2] = {C::BK, C::BN};
-    const uint64_t dqa[3] = {8, uint64_t(a.a.ld), uint64_t(nblk)}, sqa[2] = {16, uint64_t(a.a.ld) * 16};
-    const uint64_t dqb[3] = {8, uint64_t(a.b.ld), uint64_t(nblk)}, sqb[2] = {16, uint64_t(a.b.ld) * 16};
-    const uint32_t bxq[3] = {8, 128, C::BLK};
     if (!make_tmap(&tma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a.codes, 2, da, sk, bxa, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, sk, bxb, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap(&tmqa, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.a.quads, 3, dqa, sqa, bxq, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_tmap(&tmqb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.b.quads, 3, dqb, sqb, bxq, CU_TENSOR_MAP_SWIZZLE_NONE))
+        !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, sk, bxb, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    auto kern = mmq_tc_kernel<MODE, CVT>;
+    auto kern = mmq_tc_kernel<MODE, CVT, BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
@@ -514,9 +524,11 @@ static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
     ep.rowmap = a.rowmap;
     ep.gelu = a.gelu;
     ep.qcodes = static_cast<int8_t *>(a.out_codes);
-    ep.qquads = static_cast<uint4 *>(a.out_quads);
+    ep.qquads = static_cast<__half *>(a.out_quads);
     ep.qld = a.out_ld;
-    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, tmqa, tmqb, M, N, nblk, ep, a.err);
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, static_cast<const uint8_t *>(a.a.quads),
+                                                  static_cast<const uint8_t *>(a.b.quads), M, N, nblk, a.a.ld, a.b.ld,
+                                                  ep, a.err);
     return cudaGetLastError();
 }
 
@@ -526,15 +538,27 @@ static bool valid_args(const MmqArgs &a) {
            a.a.ld % MMQ_ROW_ALIGN == 0 && a.b.ld % MMQ_ROW_ALIGN == 0;
 }
 
-cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt) {
-    if (!valid_args(a) || num_sms <= 0) return cudaErrorInvalidValue;
-    if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1>(a, num_sms, s);
+// 8 epilogue warps: each thread drains 32 (BN = 64) or 64 (BN = 128) columns,
+// so a 32-wide Q8_0 output block stays inside one thread.  (16 warps with a
+// software-pipelined drain measured slower on B200.)
+template <int BN>
+static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt) {
+    constexpr int EPI_F32 = 8;
+    if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1, BN, 8>(a, num_sms, s);
     if (mode == MMQ_OUT_Q8) {
         if (a.b.rows % 32 != 0 || !a.out_codes || !a.out_quads || a.out_ld < a.a.rows) return cudaErrorInvalidValue;
-        return launch_tc<MMQ_OUT_Q8, 1>(a, num_sms, s);
+        return launch_tc<MMQ_OUT_Q8, 1, BN, 8>(a, num_sms, s);
     }
     if (mode == MMQ_OUT_F32)
-        return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0>(a, num_sms, s) : launch_tc<MMQ_OUT_F32, 1>(a, num_sms, s);
+        return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0, BN, EPI_F32>(a, num_sms, s)
+                        : launch_tc<MMQ_OUT_F32, 1, BN, EPI_F32>(a, num_sms, s);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt, int bn) {
+    if (!valid_args(a) || num_sms <= 0) return cudaErrorInvalidValue;
+    if (bn == 64) return dispatch_tc<64>(a, mode, num_sms, s, cvt);
+    if (bn == 128) return dispatch_tc<128>(a, mode, num_sms, s, cvt);
     return cudaErrorInvalidValue;
 }
 
@@ -558,10 +582,9 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
         if (mode == MMQ_OUT_BLOCKDOTS) {
             dump[(static_cast<int64_t>(m) * N + n) * nblk + b] = isum;
         } else {
-            const uint16_t xb = static_cast<uint16_t>(qa[static_cast<int64_t>(b) * lda_q + m].x);
-            const uint16_t wb = static_cast<uint16_t>(qb[static_cast<int64_t>(b) * ldb_q + n].x);
-            acc = fmaf(static_cast<float>(isum), __half2float(__ushort_as_half(xb)) * __half2float(__ushort_as_half(wb)),
-                       acc);
+            const float dx = __half2float(reinterpret_cast<const __half *>(qa)[act_quad_index(b, m, lda_q)]);
+            const float dw = __half2float(reinterpret_cast<const __half *>(qb)[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]);
+            acc = fmaf(static_cast<float>(isum), dx * dw, acc);
         }
     }
     if (mode == MMQ_OUT_F32) y[static_cast<int64_t>(m) * ldy + n] = bias ? acc + bias[n] : acc;

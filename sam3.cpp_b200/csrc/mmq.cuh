@@ -6,11 +6,14 @@
 //   codes : int8 [rows, K] row-major -- the block's int8 code (Q8_0), or
 //           nibble - 8 (Q4_0).  A kind::i8 MMA of K = 32 over two such rows
 //           is exactly ggml's int32 block dot.
-//   quads : fp16 [K/32][ld][8] -- per (block, row) one 16-byte record whose
-//           first half is the block's fp16 scale d and the rest zero.  This
-//           is the K-major, no-swizzle core-matrix layout of a K=16 MMA
-//           operand with only column 0 populated, so a TMA copy of 128 rows
-//           of it is directly the operand of the scale MMA (S = d_x (x) d_w).
+//   quads : 16-byte scale records, the K-major no-swizzle core-matrix rows of
+//           a K=16 MMA operand, from which one K=16 kind::f16 MMA forms the
+//           exact outer product S_b = d_x[:, b] (x) d_w[:, b]:
+//             activations (A side) -- fp16 [ceil(K/256)][ld][8], record
+//               (g, m) holds the scales of blocks 8g .. 8g+7 of row m;
+//             weights (B side)     -- fp16 [K/32][ld][8], record (b, n)
+//               holds d_w[n][b] in slot b % 8 and zeros elsewhere,
+//           so A-record . B-record = d_x[m][b] * d_w[n][b] exactly.
 //           ld = rows rounded up to a multiple of 128; padding rows are 0.
 #pragma once
 
@@ -28,9 +31,15 @@ enum MmqOut : int {
 
 constexpr int MMQ_ROW_ALIGN = 128;
 
+// element offset (in fp16 units) of block b's scale of row m in an A-side
+// (activation) quad array with `ld` rows per group
+__host__ __device__ constexpr int64_t act_quad_index(int b, int m, int ld) {
+    return (static_cast<int64_t>(b >> 3) * ld + m) * 8 + (b & 7);
+}
+
 struct QMatrix {
     const void *codes;  // int8 [rows, K]
-    const void *quads;  // fp16 [K/32][ld][8]
+    const void *quads;  // A side: fp16 [ceil(K/256)][ld][8]; B side: fp16 [K/32][ld][8]
     int rows, K, ld;
 };
 
@@ -46,12 +55,12 @@ struct MmqArgs {
     const int *rowmap = nullptr;    // MMQ_OUT_F32: output row of tile row m
     int gelu = 0;                   // MMQ_OUT_Q8
     void *out_codes = nullptr;      // MMQ_OUT_Q8: int8 [M, N]
-    void *out_quads = nullptr;      // MMQ_OUT_Q8: [N/32][out_ld][16 B]
+    void *out_quads = nullptr;      // MMQ_OUT_Q8: A-side records [ceil(N/256)][out_ld][16 B]
     int out_ld = 0;
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.
-// quads must hold K/32 * ld records; rows >= M are left untouched.
+// quads must hold ceil(K/256) * ld records; rows >= M are left untouched.
 cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
                              cudaStream_t s);
 
@@ -60,9 +69,10 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
                                  cudaStream_t s);
 
-// tcgen05 tensor-core MMQ (tile 128 x 128).  cvt selects the epilogue's
-// exact int32 -> fp32 conversion: 0 = cvt instruction, 1 = magic-number add.
-cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, int cvt = 1);
+// tcgen05 tensor-core MMQ, tile 128 x bn (bn = 64 or 128).  cvt selects the
+// epilogue's exact int32 -> fp32 conversion: 0 = cvt instruction, 1 =
+// magic-number add.
+cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, int cvt = 1, int bn = 128);
 
 // Straight SIMT version of the same arithmetic (small M, cross-checks).
 cudaError_t mmq_simt(const MmqArgs &args, int mode, cudaStream_t s);

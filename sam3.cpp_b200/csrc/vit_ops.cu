@@ -140,34 +140,71 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
            ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
-// one warp per token row; lane l owns the 32-wide blocks l, l+32, ...
+// One warp per token row, one pass over HBM: lane l keeps the 32-wide
+// blocks l and l + 32 (E <= 2048) in registers, the row statistics are
+// formed from registers (double sums, as ggml_norm), then each lane
+// normalises and quantises its own blocks.
 __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const float *__restrict__ w,
                              const float *__restrict__ b, float eps, int G, int win, int8_t *__restrict__ codes,
-                             uint4 *__restrict__ quads, int ld) {
+                             __half *__restrict__ quads, int ld) {
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (t >= rows) return;
     const float *xr = x + static_cast<int64_t>(t) * E;
-    float mean, scale;
-    row_stats(xr, E, eps, lane, mean, scale);
+    const int nblk = E >> 5;
+    float v[2][32];
+    double sum = 0.0;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const int blk = lane + 32 * s;
+        if (blk < nblk) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                const float4 q = *reinterpret_cast<const float4 *>(xr + blk * 32 + i);
+                v[s][i] = q.x;
+                v[s][i + 1] = q.y;
+                v[s][i + 2] = q.z;
+                v[s][i + 3] = q.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sum += v[s][i];
+        }
+    }
+    sum = warp_sum_d(sum);
+    const float mean = static_cast<float>(sum / E);
+    double sum2 = 0.0;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        if (lane + 32 * s < nblk) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float d = __fsub_rn(v[s][i], mean);
+                sum2 += static_cast<double>(__fmul_rn(d, d));
+            }
+        }
+    }
+    sum2 = warp_sum_d(sum2);
+    const float variance = static_cast<float>(sum2 / E);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
     int r = t;
     if (win > 0) {  // ggml_win_part position
         const int tx = t % G, ty = t / G, nw = G / win;
         r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
     }
-    const int nblk = E >> 5;
-    for (int blk = lane; blk < nblk; blk += 32) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const int blk = lane + 32 * s;
+        if (blk >= nblk) continue;
         float y[32];
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-            const float4 v = *reinterpret_cast<const float4 *>(xr + blk * 32 + i);
             const float4 ww = *reinterpret_cast<const float4 *>(w + blk * 32 + i);
             const float4 bb = *reinterpret_cast<const float4 *>(b + blk * 32 + i);
-            y[i] = ln_apply(v.x, mean, scale, ww.x, bb.x);
-            y[i + 1] = ln_apply(v.y, mean, scale, ww.y, bb.y);
-            y[i + 2] = ln_apply(v.z, mean, scale, ww.z, bb.z);
-            y[i + 3] = ln_apply(v.w, mean, scale, ww.w, bb.w);
+            y[i] = ln_apply(v[s][i], mean, scale, ww.x, bb.x);
+            y[i + 1] = ln_apply(v[s][i + 1], mean, scale, ww.y, bb.y);
+            y[i + 2] = ln_apply(v[s][i + 2], mean, scale, ww.z, bb.z);
+            y[i + 3] = ln_apply(v[s][i + 3], mean, scale, ww.w, bb.w);
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(y[i]));
@@ -181,16 +218,16 @@ __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const
         uint4 *dst = reinterpret_cast<uint4 *>(codes + static_cast<int64_t>(r) * E + blk * 32);
         dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        quads[static_cast<int64_t>(blk) * ld + r] = make_uint4(__half_as_ushort(__float2half_rn(d)), 0u, 0u, 0u);
+        quads[static_cast<int64_t>((blk >> 3) * ld + r) * 8 + (blk & 7)] = __float2half_rn(d);
     }
 }
 
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s) {
-    if (E % 32 != 0 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows != G * G)))
+    if (E % 32 != 0 || E > 2048 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows != G * G)))
         return cudaErrorInvalidValue;
     ln_q8_kernel<<<grid_for(rows, 8), 256, 0, s>>>(x, rows, E, w, b, eps, G, win, static_cast<int8_t *>(codes),
-                                                   static_cast<uint4 *>(quads), ld);
+                                                   static_cast<__half *>(quads), ld);
     return cudaGetLastError();
 }
 
