@@ -547,7 +547,7 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
     if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1, BN, 8>(a, num_sms, s);
     if (mode == MMQ_OUT_Q8) {
         if (a.b.rows % 32 != 0 || !a.out_codes || !a.out_quads || a.out_ld < a.a.rows) return cudaErrorInvalidValue;
-        return launch_tc<MMQ_OUT_Q8, 1, BN, 8>(a, num_sms, s);
+        return cvt == 0 ? launch_tc<MMQ_OUT_Q8, 0, BN, 8>(a, num_sms, s) : launch_tc<MMQ_OUT_Q8, 1, BN, 8>(a, num_sms, s);
     }
     if (mode == MMQ_OUT_F32)
         return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0, BN, EPI_F32>(a, num_sms, s)
