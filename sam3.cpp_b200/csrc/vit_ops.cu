@@ -222,12 +222,96 @@ __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const
     }
 }
 
+// Coalesced variant for E a multiple of 128 (NJ = E / 128): lane l holds
+// x[128 j + 4 l .. + 3], so every load is one 512-byte warp transaction.  The
+// 32-element quantisation block 4 j + l / 8 then spans lanes 8 (l / 8) ..
+// + 7 and its amax is a three-step shuffle.  The double-precision sums are
+// those of ggml_norm (exact for these magnitudes, so the lane order does not
+// change them).
+template <int NJ>
+__global__ void ln_q8_coal_kernel(const float *__restrict__ x, int rows, const float *__restrict__ w,
+                                  const float *__restrict__ b, float eps, int G, int win, int8_t *__restrict__ codes,
+                                  __half *__restrict__ quads, int ld) {
+    constexpr int E = NJ * 128;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= rows) return;
+    const float *xr = x + static_cast<int64_t>(t) * E + 4 * lane;
+    float4 v[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) v[j] = *reinterpret_cast<const float4 *>(xr + 128 * j);
+    double s0 = 0.0, s1 = 0.0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        s0 += static_cast<double>(v[j].x) + static_cast<double>(v[j].y);
+        s1 += static_cast<double>(v[j].z) + static_cast<double>(v[j].w);
+    }
+    const double sum = warp_sum_d(s0 + s1);
+    const float mean = static_cast<float>(sum / E);
+    double q0 = 0.0, q1 = 0.0;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const float d0 = __fsub_rn(v[j].x, mean), d1 = __fsub_rn(v[j].y, mean);
+        const float d2 = __fsub_rn(v[j].z, mean), d3 = __fsub_rn(v[j].w, mean);
+        q0 += static_cast<double>(__fmul_rn(d0, d0)) + static_cast<double>(__fmul_rn(d1, d1));
+        q1 += static_cast<double>(__fmul_rn(d2, d2)) + static_cast<double>(__fmul_rn(d3, d3));
+    }
+    const double sum2 = warp_sum_d(q0 + q1);
+    const float variance = static_cast<float>(sum2 / E);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+    int r = t;
+    if (win > 0) {  // ggml_win_part position
+        const int tx = t % G, ty = t / G, nw = G / win;
+        r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
+    }
+    int8_t *cr = codes + static_cast<int64_t>(r) * E + 4 * lane;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const int e = 128 * j + 4 * lane;
+        const float4 ww = *reinterpret_cast<const float4 *>(w + e);
+        const float4 bb = *reinterpret_cast<const float4 *>(b + e);
+        const float y0 = ln_apply(v[j].x, mean, scale, ww.x, bb.x), y1 = ln_apply(v[j].y, mean, scale, ww.y, bb.y);
+        const float y2 = ln_apply(v[j].z, mean, scale, ww.z, bb.z), y3 = ln_apply(v[j].w, mean, scale, ww.w, bb.w);
+        float amax = fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3)));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        const float d = __fdiv_rn(amax, 127.f);
+        const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+        *reinterpret_cast<uint32_t *>(cr + 128 * j) =
+            pack4(__float2int_rn(__fmul_rn(y0, id)), __float2int_rn(__fmul_rn(y1, id)),
+                  __float2int_rn(__fmul_rn(y2, id)), __float2int_rn(__fmul_rn(y3, id)));
+        if ((lane & 7) == 0) {
+            const int blk = 4 * j + (lane >> 3);
+            quads[static_cast<int64_t>((blk >> 3) * ld + r) * 8 + (blk & 7)] = __float2half_rn(d);
+        }
+    }
+}
+
+template <int NJ>
+static void launch_ln_coal(const float *x, int rows, const float *w, const float *b, float eps, int G, int win,
+                           void *codes, void *quads, int ld, cudaStream_t s) {
+    ln_q8_coal_kernel<NJ><<<grid_for(rows, 8), 256, 0, s>>>(x, rows, w, b, eps, G, win, static_cast<int8_t *>(codes),
+                                                             static_cast<__half *>(quads), ld);
+}
+
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s) {
     if (E % 32 != 0 || E > 2048 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows != G * G)))
         return cudaErrorInvalidValue;
-    ln_q8_kernel<<<grid_for(rows, 8), 256, 0, s>>>(x, rows, E, w, b, eps, G, win, static_cast<int8_t *>(codes),
-                                                   static_cast<__half *>(quads), ld);
+    switch (E) {
+    case 128: launch_ln_coal<1>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 256: launch_ln_coal<2>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 512: launch_ln_coal<4>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 768: launch_ln_coal<6>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 1024: launch_ln_coal<8>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 1280: launch_ln_coal<10>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 1536: launch_ln_coal<12>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    case 2048: launch_ln_coal<16>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
+    default:
+        ln_q8_kernel<<<grid_for(rows, 8), 256, 0, s>>>(x, rows, E, w, b, eps, G, win, static_cast<int8_t *>(codes),
+                                                       static_cast<__half *>(quads), ld);
+    }
     return cudaGetLastError();
 }
 
