@@ -1,13 +1,30 @@
 // attn.cu -- ggml_flash_attn_ext without mask (sam3.cpp:3778): per (window,
-// head) out = softmax(Q K^T * scale) V, head_dim 64.  Q, K, V are bf16
-// [B*heads][N][64]; the output is f32 [B*N][heads*64] (ggml's
+// head) out = softmax(Q K^T * scale) V, head_dim 64, on the 5th-generation
+// tensor cores.  Q and K are bf16 [B*heads][N][64], V is stored transposed,
+// bf16 [B*heads][64][N]; the output is f32 [B*N][heads*64] (ggml's
 // [HD, NH, N, B] result reshaped to [E, W, H, B], sam3.cpp:3780-3781).
 //
-// Flash-attention tiling: a CTA owns 64 query rows of one (window, head),
-// four warps x 16 rows; keys stream through shared memory in 64-row tiles
-// (double-buffered cp.async), scores and the running output stay in
-// registers, the softmax is online (running max and sum per row).
+// A CTA owns two 128-row query tiles (t = 0, 1) of one (window, head) and
+// streams the keys in tiles of 128:
+//   warp 0     : TMA producer -- both Q tiles once, then K and V^T tiles
+//                through a STAGES-deep ring (128-byte swizzle, zero fill
+//                past N);
+//   warp 1     : TMEM allocator + MMA issuer -- S_t(j) = Q_t K_j^T (M = 128,
+//                N = 128 keys, K = 64) and, once softmax t has written
+//                P_t(j), PV_t(j) = P_t(j) V_j (A = P read from tensor memory,
+//                N = 64, K = 128 keys).  The tiles alternate, so the tensor
+//                core works on one tile while the other tile's softmax runs;
+//   warps 2..9 : softmax, warps 2 + 4t .. 5 + 4t for tile t, one query row per
+//                thread (the TMEM lane quarter of warp w is w % 4).  Per key
+//                tile: pass 1 takes the row max of S, pass 2 writes
+//                P = 2^(s c - m) as bf16 into tensor memory and sums it; the
+//                output row stays in registers and PV_t(j-1) is folded in as
+//                O = O 2^(m(j-2) - m(j-1)) + PV_t(j-1), one step behind.
+// Tensor memory (512 columns): tile t at 256 t: S (128 columns), P (64: 128
+// bf16 packed in pairs), PV (64).
 #include "attn.cuh"
+#include "ptx.cuh"
+#include "tmap.h"
 
 #include <cstdint>
 
@@ -17,211 +34,305 @@ namespace b200 {
 
 namespace {
 
-constexpr int BQ = 64, BKV = 64, HD = 64;
+struct AttnCfg {
+    static constexpr int BQ = 128, BKV = 128, HD = 64, QT = 2;
+    static constexpr int STAGES = 3;
+    static constexpr int Q_BYTES = BQ * HD * 2;         // 16 KB per query tile
+    static constexpr int K_BYTES = BKV * HD * 2;        // 16 KB
+    static constexpr int V_BYTES = HD * BKV * 2;        // 16 KB: two 64-key halves of 64 rows x 128 B
+    static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+    static constexpr int KV_OFF = QT * Q_BYTES;
+    static constexpr int BAR_OFF = KV_OFF + STAGES * STAGE_BYTES;  // 128 KB: one CTA per SM
+    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+    static constexpr int THREADS = 64 + QT * 128;
+    static constexpr uint32_t S_COL = 0, P_COL = 128, PV_COL = 192, TILE_COLS = 256;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+enum : int {
+    AERR_Q = 1 << 8,
+    AERR_KV_EMPTY = 1 << 9,
+    AERR_KV_FULL = 1 << 10,
+    AERR_S_EMPTY = 1 << 11,
+    AERR_P_FULL = 1 << 12,
+    AERR_PV_EMPTY = 1 << 13,
+    AERR_S_FULL = 1 << 14,
+    AERR_PV_FULL = 1 << 15,
+};
 
-// rows of 64 bf16 (128 bytes); 16-byte chunks XOR-swizzled by row % 8
-__device__ __forceinline__ uint32_t swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
-    const int n = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-
-__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&v);
-}
-
-// 64 rows x 128 bytes from global rows [row0, row0 + 64) (rows >= n are zero)
-__device__ __forceinline__ void load_tile(uint8_t *sm, const __nv_bfloat16 *g, int row0, int n) {
-    const uint32_t base = smem_addr(sm);
+// Row max over 32 scores (the keys past N are skipped when MASKED).
+template <bool MASKED>
+__device__ __forceinline__ float chunk_max(const uint32_t (&s)[32], float mx, int nvalid_here) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = threadIdx.x + i * 128;
-        const int row = c >> 3, ch = c & 7;
-        const bool valid = row0 + row < n;
-        const __nv_bfloat16 *src = g + static_cast<int64_t>(valid ? row0 + row : 0) * HD + ch * 8;
-        cp_async16(base + swz(row, ch), src, valid);
+    for (int i = 0; i < 32; ++i)
+        if (!MASKED || i < nvalid_here) mx = fmaxf(mx, __uint_as_float(s[i]));
+    return mx;
+}
+
+// p = 2^(s c - m) for 32 scores, packed as bf16 pairs; returns the sum of p.
+template <bool MASKED>
+__device__ __forceinline__ float chunk_exp(const uint32_t (&s)[32], float c, float neg_m, uint32_t (&pk)[16],
+                                           int nvalid_here) {
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        float p0 = ex2_approx(fmaf(__uint_as_float(s[i]), c, neg_m));
+        float p1 = ex2_approx(fmaf(__uint_as_float(s[i + 1]), c, neg_m));
+        if (MASKED) {
+            if (i >= nvalid_here) p0 = 0.f;
+            if (i + 1 >= nvalid_here) p1 = 0.f;
+        }
+        sum += p0 + p1;
+        const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+        pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&h);
     }
+    return sum;
 }
 
 }  // namespace
 
-__global__ void __launch_bounds__(128) flash_attn_kernel(const __nv_bfloat16 *__restrict__ q,
-                                                         const __nv_bfloat16 *__restrict__ k,
-                                                         const __nv_bfloat16 *__restrict__ v, int N, int heads,
-                                                         float scale_log2, float *__restrict__ out) {
-    __shared__ __align__(128) uint8_t sq[BQ * 128];
-    __shared__ __align__(128) uint8_t sk[2][BKV * 128];
-    __shared__ __align__(128) uint8_t sv[2][BKV * 128];
+__global__ void __launch_bounds__(AttnCfg::THREADS, 1)
+    flash_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, int N, int heads, float c_log2,
+                         float *__restrict__ out, int *__restrict__ err) {
+    using C = AttnCfg;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *q_full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *kv_full = q_full + 1;
+    uint64_t *kv_empty = kv_full + C::STAGES;
+    uint64_t *s_full = kv_empty + C::STAGES;  // [QT]
+    uint64_t *s_empty = s_full + C::QT;       // [QT]
+    uint64_t *p_full = s_empty + C::QT;       // [QT]
+    uint64_t *pv_full = p_full + C::QT;       // [QT]
+    uint64_t *pv_empty = pv_full + C::QT;     // [QT]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pv_empty + C::QT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
-    const int q0 = blockIdx.x * BQ;
-    const __nv_bfloat16 *qg = q + static_cast<int64_t>(bh) * N * HD;
-    const __nv_bfloat16 *kg = k + static_cast<int64_t>(bh) * N * HD;
-    const __nv_bfloat16 *vg = v + static_cast<int64_t>(bh) * N * HD;
-    const int ntiles = (N + BKV - 1) / BKV;
+    const int q0 = blockIdx.x * C::QT * C::BQ;
+    const int ntiles = (N + C::BKV - 1) / C::BKV;
+    const int nq = N - q0 > C::BQ ? C::QT : 1;  // query tiles of this CTA that hold rows < N
 
-    load_tile(sq, qg, q0, N);
-    load_tile(sk[0], kg, 0, N);
-    load_tile(sv[0], vg, 0, N);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-
-    uint32_t qa[4][4];
-    float o[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-    const int g = lane >> 2, tq = lane & 3;
-
-    for (int it = 0; it < ntiles; ++it) {
-        const int buf = it & 1;
-        if (it + 1 < ntiles) {
-            load_tile(sk[buf ^ 1], kg, (it + 1) * BKV, N);
-            load_tile(sv[buf ^ 1], vg, (it + 1) * BKV, N);
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        if (it == 0) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const int row = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-                const int ch = 2 * kk + (lane >> 4);
-                ldsm_x4(smem_addr(sq) + swz(row, ch), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
-            }
+        for (int t = 0; t < C::QT; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&s_empty[t], 4);
+            mbar_init(&p_full[t], 4);
+            mbar_init(&pv_full[t], 1);
+            mbar_init(&pv_empty[t], 4);
         }
-        // S = Q K^T for this warp's 16 rows x 64 keys
-        float s[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-        const uint32_t kb = smem_addr(sk[buf]);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-                const int row = 8 * j + (lane & 7) + 8 * (lane >> 4);
-                const int ch = 2 * kk + ((lane >> 3) & 1);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4(kb + swz(row, ch), b0, b1, b2, b3);
-                mma_bf16(s[j], qa[kk], b0, b1);
-                mma_bf16(s[j + 1], qa[kk], b2, b3);
-            }
-        }
-        // online softmax (rows g and g + 8 of the warp's 16)
-        const int key0 = it * BKV;
-        float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = key0 + 8 * j + 2 * tq + (e & 1);
-                float val = key < N ? s[j][e] * scale_log2 : -INFINITY;
-                s[j][e] = val;
-                mx[e >> 1] = fmaxf(mx[e >> 1], val);
-            }
-        }
-        float alpha[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-            const float m_new = fmaxf(m_run[r], mx[r]);
-            alpha[r] = exp2f(m_run[r] - m_new);
-            m_run[r] = m_new;
-        }
-        float rs[2] = {0.f, 0.f};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float p = exp2f(s[j][e] - m_run[e >> 1]);
-                s[j][e] = p;
-                rs[e >> 1] += p;
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-            rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-            l_run[r] = l_run[r] * alpha[r] + rs[r];
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            o[j][0] *= alpha[0];
-            o[j][1] *= alpha[0];
-            o[j][2] *= alpha[1];
-            o[j][3] *= alpha[1];
-        }
-        // O += P V
-        const uint32_t vb = smem_addr(sv[buf]);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t pa[4];
-            pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-            pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-            pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-                const int row = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1);
-                const int ch = j + (lane >> 4);
-                uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vb + swz(row, ch), b0, b1, b2, b3);
-                mma_bf16(o[j], pa, b0, b1);
-                mma_bf16(o[j + 1], pa, b2, b3);
-            }
-        }
-        __syncthreads();
+        fence_mbar_init();
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+        prefetch_tmap(&tm_v);
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-
-    const int b = bh / heads, h = bh % heads;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        const int n = q0 + warp * 16 + g + 8 * r;
-        if (n >= N) continue;
-        const float inv = 1.0f / l_run[r];
-        float *dst = out + (static_cast<int64_t>(b) * N + n) * heads * HD + h * HD;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float2 *>(dst + 8 * j + 2 * tq) = make_float2(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
     }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---- TMA producer ----
+        if (elect_one()) {
+            mbar_arrive_expect_tx(q_full, nq * C::Q_BYTES);
+            for (int t = 0; t < nq; ++t) tma_load_3d(smem + t * C::Q_BYTES, &tm_q, q_full, 0, q0 + t * C::BQ, bh);
+        }
+        __syncwarp();
+        for (int j = 0; j < ntiles; ++j) {
+            const int st = j % C::STAGES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / C::STAGES) & 1) ^ 1, err, AERR_KV_EMPTY)))
+                break;
+            uint8_t *kb = smem + C::KV_OFF + st * C::STAGE_BYTES;
+            if (elect_one()) {
+                mbar_arrive_expect_tx(&kv_full[st], C::STAGE_BYTES);
+                tma_load_3d(kb, &tm_k, &kv_full[st], 0, j * C::BKV, bh);
+                tma_load_3d(kb + C::K_BYTES, &tm_v, &kv_full[st], j * C::BKV, 0, bh);
+                tma_load_3d(kb + C::K_BYTES + C::V_BYTES / 2, &tm_v, &kv_full[st], j * C::BKV + 64, 0, bh);
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer ----
+        constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BKV);
+        constexpr uint32_t idesc_pv = idesc_bf16_f32(128, C::HD);
+        auto issue_s = [&](int t, int j) -> bool {
+            const int st = j % C::STAGES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (j / C::STAGES) & 1, err, AERR_KV_FULL)) ||
+                !__all_sync(0xffffffffu, mbar_wait(&s_empty[t], (j & 1) ^ 1, err, AERR_S_EMPTY)))
+                return false;
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(smem + t * C::Q_BYTES);
+            const uint32_t k_addr = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES);
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < C::HD / 16; ++kk)
+                    mma_f16(tmem + t * C::TILE_COLS + C::S_COL, sw128_kmajor_desc(q_addr + kk * 32),
+                            sw128_kmajor_desc(k_addr + kk * 32), idesc_s, kk > 0);
+                mma_commit(&s_full[t]);
+            }
+            __syncwarp();
+            return true;
+        };
+        auto issue_pv = [&](int t, int j) -> bool {
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], j & 1, err, AERR_P_FULL)) ||
+                !__all_sync(0xffffffffu, mbar_wait(&pv_empty[t], (j & 1) ^ 1, err, AERR_PV_EMPTY)))
+                return false;
+            tc_fence_after();
+            const int st = j % C::STAGES;
+            const uint32_t v_addr = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES + C::K_BYTES);
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < C::BKV / 16; ++kk) {
+                    // keys 16 kk .. +15: 64-key half kk / 4, 32-byte slice kk % 4 of its 128-byte rows
+                    const uint32_t va = v_addr + (kk >> 2) * (C::V_BYTES / 2) + (kk & 3) * 32;
+                    mma_f16_ts(tmem + t * C::TILE_COLS + C::PV_COL, tmem + t * C::TILE_COLS + C::P_COL + kk * 8,
+                               sw128_kmajor_desc(va), idesc_pv, kk > 0);
+                }
+                mma_commit(&pv_full[t]);
+                if (t == nq - 1) mma_commit(&kv_empty[st]);  // the stage's last reader
+            }
+            __syncwarp();
+            return true;
+        };
+        bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, AERR_Q));
+        for (int t = 0; t < nq && ok; ++t) ok = issue_s(t, 0);
+        for (int j = 0; j < ntiles && ok; ++j) {
+            for (int t = 0; t < nq && ok; ++t) {
+                ok = issue_pv(t, j);
+                if (ok && j + 1 < ntiles) ok = issue_s(t, j + 1);
+            }
+        }
+    } else {
+        // ---- softmax: one query row per thread ----
+        const int t = (warp - 2) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t base = tmem + t * C::TILE_COLS + (static_cast<uint32_t>(quarter * 32) << 16);
+        if (t < nq) {
+            float o[C::HD];
+#pragma unroll
+            for (int i = 0; i < C::HD; ++i) o[i] = 0.f;
+            float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+            bool ok = true;
+            // O = O alpha + PV_t(i) (PV_t(i) was formed against the running max of step i)
+            auto fold_pv = [&](int i, float alpha) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait(&pv_full[t], i & 1, err, AERR_PV_FULL))) return false;
+                tc_fence_after();
+                uint32_t pv[C::HD];
+                tmem_ld_32x32b_x32(base + C::PV_COL, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
+                tmem_ld_32x32b_x32(base + C::PV_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&pv_empty[t]);
+#pragma unroll
+                for (int d = 0; d < C::HD; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(pv[d]));
+                return true;
+            };
+            for (int j = 0; j < ntiles; ++j) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, err, AERR_S_FULL))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int nvalid = N - j * C::BKV;  // keys of this tile below N
+                // pass 1: row max of the raw scores (c > 0, so the max commutes with the scaling)
+                float mx = -INFINITY;
+#pragma unroll
+                for (int cc = 0; cc < C::BKV; cc += 64) {
+                    uint32_t s0[32], s1[32];
+                    tmem_ld_32x32b_x32(base + C::S_COL + cc, s0);
+                    tmem_ld_32x32b_x32(base + C::S_COL + cc + 32, s1);
+                    tmem_wait_ld();
+                    if (nvalid >= C::BKV) {
+                        mx = chunk_max<false>(s0, mx, 32);
+                        mx = chunk_max<false>(s1, mx, 32);
+                    } else {
+                        mx = chunk_max<true>(s0, mx, nvalid - cc);
+                        mx = chunk_max<true>(s1, mx, nvalid - cc - 32);
+                    }
+                }
+                const float m_new = fmaxf(m_run, mx * c_log2);
+                const float alpha = ex2_approx(m_run - m_new);
+                // P_t's previous contents were read by PV_t(j-1): fold it first
+                if (j > 0 && !fold_pv(j - 1, alpha_prev)) {
+                    ok = false;
+                    break;
+                }
+                // pass 2: P = 2^(s c - m) into tensor memory, row sum
+                float rsum = 0.f;
+#pragma unroll
+                for (int cc = 0; cc < C::BKV; cc += 32) {
+                    uint32_t s0[32], pk[16];
+                    tmem_ld_32x32b_x32(base + C::S_COL + cc, s0);
+                    tmem_wait_ld();
+                    rsum += nvalid >= C::BKV ? chunk_exp<false>(s0, c_log2, -m_new, pk, 32)
+                                             : chunk_exp<true>(s0, c_log2, -m_new, pk, nvalid - cc);
+                    tmem_st_32x32b_x16(base + C::P_COL + cc / 2, pk);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&s_empty[t]);
+                    mbar_arrive(&p_full[t]);
+                }
+                l_run = fmaf(l_run, alpha, rsum);
+                m_run = m_new;
+                alpha_prev = alpha;
+            }
+            if (ok && fold_pv(ntiles - 1, alpha_prev)) {
+                const int n = q0 + t * C::BQ + row;
+                if (n < N) {
+                    const int bb = bh / heads, h = bh % heads;
+                    const float inv = 1.0f / l_run;
+                    float *dst = out + (static_cast<int64_t>(bb) * N + n) * heads * C::HD + h * C::HD;
+#pragma unroll
+                    for (int d = 0; d < C::HD; d += 4)
+                        *reinterpret_cast<float4 *>(dst + d) =
+                            make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-cudaError_t flash_attention(const void *q, const void *k, const void *v, int B, int N, int heads, float scale,
-                            float *out, cudaStream_t s) {
-    if (B <= 0 || N <= 0 || heads <= 0) return cudaErrorInvalidValue;
-    dim3 grid((N + BQ - 1) / BQ, B * heads);
-    flash_attn_kernel<<<grid, 128, 0, s>>>(static_cast<const __nv_bfloat16 *>(q),
-                                           static_cast<const __nv_bfloat16 *>(k),
-                                           static_cast<const __nv_bfloat16 *>(v), N, heads,
-                                           scale * 1.4426950408889634f, out);
+cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B, int N, int heads, float scale,
+                            float *out, int *err, cudaStream_t s) {
+    using C = AttnCfg;
+    if (B <= 0 || N <= 0 || heads <= 0 || N % 8 != 0 || !err) return cudaErrorInvalidValue;
+    const uint64_t bhn = static_cast<uint64_t>(B) * heads;
+    CUtensorMap tq, tk, tv;
+    const uint64_t dqk[3] = {64, static_cast<uint64_t>(N), bhn};
+    const uint64_t sqk[2] = {64 * 2, static_cast<uint64_t>(N) * 64 * 2};
+    const uint32_t bqk[3] = {64, 128, 1};
+    const uint64_t dv[3] = {static_cast<uint64_t>(N), 64, bhn};
+    const uint64_t sv[2] = {static_cast<uint64_t>(N) * 2, static_cast<uint64_t>(N) * 64 * 2};
+    const uint32_t bv[3] = {64, 64, 1};
+    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 3, dqk, sqk, bqk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 3, dqk, sqk, bqk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vt, 3, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    dim3 grid((N + C::QT * C::BQ - 1) / (C::QT * C::BQ), static_cast<unsigned>(bhn));
+    flash_attn_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tq, tk, tv, N, heads, scale * 1.4426950408889634f,
+                                                                  out, err);
     return cudaGetLastError();
 }
 

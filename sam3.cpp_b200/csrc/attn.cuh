@@ -5,8 +5,10 @@
 
 namespace b200 {
 
-// q, k, v: bf16 [B*heads][N][64]; out: f32 [B*N][heads*64].
-cudaError_t flash_attention(const void *q, const void *k, const void *v, int B, int N, int heads, float scale,
-                            float *out, cudaStream_t s);
+// q, k: bf16 [B*heads][N][64]; vt: bf16 [B*heads][64][N] (V transposed);
+// out: f32 [B*N][heads*64].  N must be a multiple of 8 (TMA row pitch).
+// Bounded waits report through *err (device word).
+cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B, int N, int heads, float scale,
+                            float *out, int *err, cudaStream_t s);
 
 }  // namespace b200

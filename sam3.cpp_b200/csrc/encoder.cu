@@ -256,7 +256,7 @@ static bool run_block(Vit *v, int i, float *x) {
                                   v->q.p, v->k.p, v->v.p, s),
                    "qkv_rope") &&
            launched(v, flash_attention(v->q.p, v->k.p, v->v.p, B, N, hp.heads, 1.0f / sqrtf(static_cast<float>(E / hp.heads)),
-                                   v->attn.as<float>(), s),
+                                   v->attn.as<float>(), v->be->err, s),
                    "attention") &&
            launched(v, quantize_rows_q8(v->attn.as<float>(), E, T, E, v->codes_a.p, v->quads_a.p, v->Tpad, s), "quant") &&
            mmq(v, v->codes_a.p, v->quads_a.p, w.proj, MMQ_OUT_F32, w.proj_b.as<float>(), x, 1,
