@@ -12,8 +12,10 @@
 //   warp 1     : TMEM allocator + MMA issuer -- S_t(j) = Q_t K_j^T (M = 128,
 //                N = 128 keys, K = 64) and, once softmax t has written
 //                P_t(j), PV_t(j) = P_t(j) V_j (A = P read from tensor memory,
-//                N = 64, K = 128 keys).  The tiles alternate, so the tensor
-//                core works on one tile while the other tile's softmax runs;
+//                N = 64, K = 128 keys) followed by S_t(j+1), with one commit
+//                (ready[t]) for the pair: commits hold the issuing thread far
+//                longer than MMAs.  The tiles alternate, so the tensor core
+//                works on one tile while the other tile's softmax runs;
 //   warps 2..9 : softmax, warps 2 + 4t .. 5 + 4t for tile t, one query row per
 //                thread (the TMEM lane quarter of warp w is w % 4).  Per key
 //                tile: pass 1 takes the row max of S, pass 2 writes
@@ -101,12 +103,11 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     uint64_t *q_full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *kv_full = q_full + 1;
     uint64_t *kv_empty = kv_full + C::STAGES;
-    uint64_t *s_full = kv_empty + C::STAGES;  // [QT]
-    uint64_t *s_empty = s_full + C::QT;       // [QT]
-    uint64_t *p_full = s_empty + C::QT;       // [QT]
-    uint64_t *pv_full = p_full + C::QT;       // [QT]
-    uint64_t *pv_empty = pv_full + C::QT;     // [QT]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pv_empty + C::QT);
+    // ready[t] phase j: S_t(j) (and PV_t(j-1)) are in tensor memory.
+    // pdone[t] phase j: softmax t has read S_t(j), folded PV_t(j-1) and written P_t(j).
+    uint64_t *ready = kv_empty + C::STAGES;  // [QT]
+    uint64_t *pdone = ready + C::QT;         // [QT]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pdone + C::QT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
@@ -121,11 +122,8 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
             mbar_init(&kv_empty[s], 1);
         }
         for (int t = 0; t < C::QT; ++t) {
-            mbar_init(&s_full[t], 1);
-            mbar_init(&s_empty[t], 4);
-            mbar_init(&p_full[t], 4);
-            mbar_init(&pv_full[t], 1);
-            mbar_init(&pv_empty[t], 4);
+            mbar_init(&ready[t], 1);
+            mbar_init(&pdone[t], 4);
         }
         fence_mbar_init();
         prefetch_tmap(&tm_q);
@@ -165,52 +163,62 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
         // ---- MMA issuer ----
         constexpr uint32_t idesc_s = idesc_bf16_f32(128, C::BKV);
         constexpr uint32_t idesc_pv = idesc_bf16_f32(128, C::HD);
-        auto issue_s = [&](int t, int j) -> bool {
-            const int st = j % C::STAGES;
-            if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (j / C::STAGES) & 1, err, AERR_KV_FULL)) ||
-                !__all_sync(0xffffffffu, mbar_wait(&s_empty[t], (j & 1) ^ 1, err, AERR_S_EMPTY)))
-                return false;
-            tc_fence_after();
+        // S_t(j) = Q_t K_j^T (caller has waited for stage j and for S_t to be free)
+        auto mma_s = [&](int t, int j) {
             const uint32_t q_addr = smem_u32(smem + t * C::Q_BYTES);
-            const uint32_t k_addr = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES);
-            if (elect_one()) {
+            const uint32_t k_addr = smem_u32(smem + C::KV_OFF + (j % C::STAGES) * C::STAGE_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < C::HD / 16; ++kk)
-                    mma_f16(tmem + t * C::TILE_COLS + C::S_COL, sw128_kmajor_desc(q_addr + kk * 32),
-                            sw128_kmajor_desc(k_addr + kk * 32), idesc_s, kk > 0);
-                mma_commit(&s_full[t]);
-            }
-            __syncwarp();
-            return true;
+            for (int kk = 0; kk < C::HD / 16; ++kk)
+                mma_f16(tmem + t * C::TILE_COLS + C::S_COL, sw128_kmajor_desc(q_addr + kk * 32),
+                        sw128_kmajor_desc(k_addr + kk * 32), idesc_s, kk > 0);
         };
-        auto issue_pv = [&](int t, int j) -> bool {
-            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], j & 1, err, AERR_P_FULL)) ||
-                !__all_sync(0xffffffffu, mbar_wait(&pv_empty[t], (j & 1) ^ 1, err, AERR_PV_EMPTY)))
-                return false;
+        // PV_t(j) = P_t(j) V_j
+        auto mma_pv = [&](int t, int j) {
+            const uint32_t v_addr = smem_u32(smem + C::KV_OFF + (j % C::STAGES) * C::STAGE_BYTES + C::K_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < C::BKV / 16; ++kk) {
+                // keys 16 kk .. +15: 64-key half kk / 4, 32-byte slice kk % 4 of its 128-byte rows
+                const uint32_t va = v_addr + (kk >> 2) * (C::V_BYTES / 2) + (kk & 3) * 32;
+                mma_f16_ts(tmem + t * C::TILE_COLS + C::PV_COL, tmem + t * C::TILE_COLS + C::P_COL + kk * 8,
+                           sw128_kmajor_desc(va), idesc_pv, kk > 0);
+            }
+        };
+        bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, AERR_Q)) &&
+                  __all_sync(0xffffffffu, mbar_wait(&kv_full[0], 0, err, AERR_KV_FULL));
+        if (ok) {
             tc_fence_after();
-            const int st = j % C::STAGES;
-            const uint32_t v_addr = smem_u32(smem + C::KV_OFF + st * C::STAGE_BYTES + C::K_BYTES);
             if (elect_one()) {
-#pragma unroll
-                for (int kk = 0; kk < C::BKV / 16; ++kk) {
-                    // keys 16 kk .. +15: 64-key half kk / 4, 32-byte slice kk % 4 of its 128-byte rows
-                    const uint32_t va = v_addr + (kk >> 2) * (C::V_BYTES / 2) + (kk & 3) * 32;
-                    mma_f16_ts(tmem + t * C::TILE_COLS + C::PV_COL, tmem + t * C::TILE_COLS + C::P_COL + kk * 8,
-                               sw128_kmajor_desc(va), idesc_pv, kk > 0);
+                for (int t = 0; t < nq; ++t) {
+                    mma_s(t, 0);
+                    mma_commit(&ready[t]);
                 }
-                mma_commit(&pv_full[t]);
-                if (t == nq - 1) mma_commit(&kv_empty[st]);  // the stage's last reader
             }
             __syncwarp();
-            return true;
-        };
-        bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, AERR_Q));
-        for (int t = 0; t < nq && ok; ++t) ok = issue_s(t, 0);
+        }
         for (int j = 0; j < ntiles && ok; ++j) {
-            for (int t = 0; t < nq && ok; ++t) {
-                ok = issue_pv(t, j);
-                if (ok && j + 1 < ntiles) ok = issue_s(t, j + 1);
+            const bool more = j + 1 < ntiles;
+            if (more && !__all_sync(0xffffffffu,
+                                    mbar_wait(&kv_full[(j + 1) % C::STAGES], ((j + 1) / C::STAGES) & 1, err, AERR_KV_FULL))) {
+                ok = false;
+                break;
             }
+            for (int t = 0; t < nq && ok; ++t) {
+                // softmax t is done with S_t(j), PV_t(j-1) and has written P_t(j)
+                if (!__all_sync(0xffffffffu, mbar_wait(&pdone[t], j & 1, err, AERR_P_FULL))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (elect_one()) {
+                    mma_pv(t, j);
+                    if (more) mma_s(t, j + 1);
+                    mma_commit(&ready[t]);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&kv_empty[j % C::STAGES]);  // every reader of stage j has been issued
+            __syncwarp();
         }
     } else {
         // ---- softmax: one query row per thread ----
@@ -224,23 +232,18 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
             for (int i = 0; i < C::HD; ++i) o[i] = 0.f;
             float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
             bool ok = true;
-            // O = O alpha + PV_t(i) (PV_t(i) was formed against the running max of step i)
-            auto fold_pv = [&](int i, float alpha) -> bool {
-                if (!__all_sync(0xffffffffu, mbar_wait(&pv_full[t], i & 1, err, AERR_PV_FULL))) return false;
-                tc_fence_after();
+            // O = O alpha + PV (PV_t(j-1) was formed against the running max of step j-1);
+            // the caller has waited for ready[t] phase j
+            auto fold_pv = [&](float alpha) {
                 uint32_t pv[C::HD];
                 tmem_ld_32x32b_x32(base + C::PV_COL, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
                 tmem_ld_32x32b_x32(base + C::PV_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
                 tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&pv_empty[t]);
 #pragma unroll
                 for (int d = 0; d < C::HD; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(pv[d]));
-                return true;
             };
             for (int j = 0; j < ntiles; ++j) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, err, AERR_S_FULL))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&ready[t], j & 1, err, AERR_S_FULL))) {
                     ok = false;
                     break;
                 }
@@ -264,11 +267,8 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                 }
                 const float m_new = fmaxf(m_run, mx * c_log2);
                 const float alpha = ex2_approx(m_run - m_new);
-                // P_t's previous contents were read by PV_t(j-1): fold it first
-                if (j > 0 && !fold_pv(j - 1, alpha_prev)) {
-                    ok = false;
-                    break;
-                }
+                // PV_t(j-1) (complete with S_t(j)) has read P_t(j-1): fold it, then overwrite P_t
+                if (j > 0) fold_pv(alpha_prev);
                 // pass 2: P = 2^(s c - m) into tensor memory, row sum
                 float rsum = 0.f;
 #pragma unroll
@@ -283,15 +283,14 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&s_empty[t]);
-                    mbar_arrive(&p_full[t]);
-                }
+                if (lane == 0) mbar_arrive(&pdone[t]);
                 l_run = fmaf(l_run, alpha, rsum);
                 m_run = m_new;
                 alpha_prev = alpha;
             }
-            if (ok && fold_pv(ntiles - 1, alpha_prev)) {
+            if (ok && __all_sync(0xffffffffu, mbar_wait(&ready[t], ntiles & 1, err, AERR_PV_FULL))) {
+                tc_fence_after();
+                fold_pv(alpha_prev);
                 const int n = q0 + t * C::BQ + row;
                 if (n < N) {
                     const int bb = bh / heads, h = bh % heads;
