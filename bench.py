@@ -43,6 +43,11 @@ def _load(name):
     return mod
 
 
+# DRAM traffic of one MUL_MAT launch at the cfg3 shapes (mean of qkv, proj, fc1,
+# fc2), from an ncu capture of ViT block 0's four launches.
+MMQ_DRAM_BYTES_PER_LAUNCH = 30.07e6
+
+
 def vit_ops_per_image(hp):
     """2*M*K*N summed over the 4 linear layers of every block."""
     T = (hp["img"] // hp["patch"]) ** 2
@@ -184,6 +189,7 @@ def main():
     import torch
     import torch.distributed as dist
     b200 = _load("b200")
+    shard = _load("shard")
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
@@ -198,7 +204,7 @@ def main():
 
     S = hp["img"]
     batch = args.images
-    mine = list(range(rank, batch, world))
+    mine = shard.image_shard(batch, rank, world)
     imgs = model_mod.random_images(batch, S, seed=1234)[mine]
     dev_imgs = [be.upload(im) for im in imgs]
     pinned = torch.from_numpy(imgs).pin_memory()
@@ -232,11 +238,7 @@ def main():
         e1.record(stream)
         be.synchronize()
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+        ms = shard.max_over_ranks(e0.elapsed_time(e1), device=torch.device("cuda", local))
         barrier()
         return ms
 
@@ -281,7 +283,11 @@ def main():
                     "d2h_bytes_per_step": int(small.nbytes * batch)},
             "roofline": {"kernel": "mmq_tc_kernel (quantised MUL_MAT, 4 per ViT block)", "bound": "tensor",
                          "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
-                         "frac": achieved / peak_int8 if peak_int8 else None, "traffic": None,
+                         "frac": achieved / peak_int8 if peak_int8 else None,
+                         "traffic": MMQ_DRAM_BYTES_PER_LAUNCH, "traffic_unit": "bytes per launch",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
+                                           "MUL_MAT launches of one ViT block (qkv 21.7, proj 28.8, fc1 13.0, "
+                                           "fc2 56.7 MB); operands stream L2 -> SM, not from DRAM",
                          "peak_source": "dense int8 measured in this run (cuBLASLt torch._int_mm 8192^3); "
                                         "MEASURED_PEAKS.json holds no int8 figure",
                          "ops_per_image": ops, "launches_timed": mmq_n,
