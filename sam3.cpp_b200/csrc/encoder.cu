@@ -76,7 +76,7 @@ struct Vit {
     NeckScaleW neck[4];
     std::vector<std::string> missing;
     // activations
-    DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, qkv, q, k, v, attn, rowmap;
+    DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, q, k, v, attn, rowmap;
     DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4];
     int out_side[4] = {0, 0, 0, 0};
     int img_cap = 0;  // pixels of img_u8
@@ -157,7 +157,7 @@ static bool alloc_activations(Vit *v) {
               v->x.alloc(static_cast<size_t>(T) * E * 4) && v->codes_a.alloc(static_cast<size_t>(T) * E) &&
               v->quads_a.alloc(static_cast<size_t>(E / 32) * v->Tpad * 16) &&
               v->codes_b.alloc(static_cast<size_t>(T) * maxk) &&
-              v->quads_b.alloc(maxk / 32 * v->Tpad * 16) && v->qkv.alloc(static_cast<size_t>(T) * 3 * E * 4) &&
+              v->quads_b.alloc(maxk / 32 * v->Tpad * 16) &&
               v->q.alloc(static_cast<size_t>(T) * E * 2) && v->k.alloc(static_cast<size_t>(T) * E * 2) &&
               v->v.alloc(static_cast<size_t>(T) * E * 2) && v->attn.alloc(static_cast<size_t>(T) * E * 4) &&
               v->rowmap.alloc(static_cast<size_t>(T) * 4) && v->x16.alloc(static_cast<size_t>(T) * E * 2) &&
@@ -208,6 +208,29 @@ static bool mmq(Vit *v, const void *codes, const void *quads, const QWeight &w, 
     return ok;
 }
 
+// qkv projection with the attention-input epilogue: bias, RoPE, bf16 Q, K and V^T
+static bool mmq_qkv(Vit *v, const BlockW &w, int win_tokens) {
+    MmqArgs a;
+    a.a = QMatrix{v->codes_a.p, v->quads_a.p, v->T, w.qkv.K, v->Tpad};
+    a.b = QMatrix{w.qkv.codes.p, w.qkv.quads.p, w.qkv.N, w.qkv.K, w.qkv.ld};
+    a.bias = w.qkv_b.as<float>();
+    a.y = nullptr;
+    a.ldy = 0;
+    a.dump = nullptr;
+    a.err = v->be->err;
+    a.q_out = v->q.p;
+    a.k_out = v->k.p;
+    a.vt_out = v->v.p;
+    a.freqs = w.freqs.p ? w.freqs.as<float>() : nullptr;
+    a.win_tokens = win_tokens;
+    a.heads = v->hp.heads;
+    v->be->prof_mark(0);
+    const bool ok =
+        launched(v, mmq_tc(a, MMQ_OUT_QKV, v->be->num_sms, v->be->stream, v->be->mmq_cvt, v->be->mmq_bn), "mmq qkv");
+    v->be->prof_mark(0);
+    return ok;
+}
+
 static bool gemm(Vit *v, const void *a, const DevBuf &b, int M, int N, int K, const DevBuf *bias, int gelu,
                  int out_f16, void *out, int store, int win, int cout) {
     GemmF16Args g;
@@ -250,11 +273,7 @@ static bool run_block(Vit *v, int i, float *x) {
     return launched(v, layernorm_q8(x, T, E, w.n1w.as<float>(), w.n1b.as<float>(), 1e-5f, G, glob ? 0 : ws,
                                 v->codes_a.p, v->quads_a.p, v->Tpad, s),
                    "ln1") &&
-           mmq(v, v->codes_a.p, v->quads_a.p, w.qkv, MMQ_OUT_F32, w.qkv_b.as<float>(), v->qkv.as<float>(), 0, nullptr,
-               nullptr, nullptr, 0) &&
-           launched(v, qkv_rope_split(v->qkv.as<float>(), w.freqs.p ? w.freqs.as<float>() : nullptr, B, N, E, hp.heads,
-                                  v->q.p, v->k.p, v->v.p, s),
-                   "qkv_rope") &&
+           mmq_qkv(v, w, N) &&
            launched(v, flash_attention(v->q.p, v->k.p, v->v.p, B, N, hp.heads, 1.0f / sqrtf(static_cast<float>(E / hp.heads)),
                                    v->attn.as<float>(), v->be->err, s),
                    "attention") &&

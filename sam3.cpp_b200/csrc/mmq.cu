@@ -20,6 +20,7 @@
 #include "ptx.cuh"
 #include "tmap.h"
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace b200 {
@@ -213,6 +214,9 @@ struct MmqEpi {
     int8_t *qcodes;
     __half *qquads;
     int qld;
+    __nv_bfloat16 *q, *k, *vt;
+    const float *freqs;
+    int win_tokens, heads;
 };
 
 __device__ __forceinline__ float gelu_erf_f(float x) {
@@ -458,6 +462,47 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
                         }
                     }
                 }
+            } else if constexpr (MODE == MMQ_OUT_QKV) {
+                // this thread's COLS columns lie inside one 64-wide head of the q, k or v third
+                if (m < M) {
+                    const int nb = n0 + h * C::COLS;
+                    const int E = N / 3;
+                    const int part = nb / E, c0 = nb - part * E, hd = c0 >> 6, d0 = c0 & 63;
+                    const int win = m / ep.win_tokens, pos = m - win * ep.win_tokens;
+                    const int64_t bh = static_cast<int64_t>(win) * ep.heads + hd;
+#pragma unroll
+                    for (int i = 0; i < C::COLS; ++i)
+                        if (bias) acc[i] = __fadd_rn(acc[i], bias[nb + i]);
+                    if (part < 2) {
+                        if (ep.freqs) {
+                            const float *fr = ep.freqs + (static_cast<int64_t>(pos) * 32 + (d0 >> 1)) * 2;
+#pragma unroll
+                            for (int i = 0; i < C::COLS; i += 2) {
+                                const float2 cs = *reinterpret_cast<const float2 *>(fr + i);
+                                const float x0 = acc[i], x1 = acc[i + 1];
+                                acc[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+                                acc[i + 1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+                            }
+                        }
+                        __nv_bfloat16 *dst = (part == 0 ? ep.q : ep.k) + (bh * ep.win_tokens + pos) * 64 + d0;
+#pragma unroll
+                        for (int i = 0; i < C::COLS; i += 8) {
+                            uint4 u;
+                            uint32_t *uw = reinterpret_cast<uint32_t *>(&u);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[i + 2 * e], acc[i + 2 * e + 1]);
+                                uw[e] = *reinterpret_cast<const uint32_t *>(&p2);
+                            }
+                            *reinterpret_cast<uint4 *>(dst + i) = u;
+                        }
+                    } else {
+                        // V^T: consecutive lanes hold consecutive tokens, so each store is 64 contiguous bytes
+                        __nv_bfloat16 *dst = ep.vt + (bh * 64 + d0) * ep.win_tokens + pos;
+#pragma unroll
+                        for (int i = 0; i < C::COLS; ++i) dst[static_cast<int64_t>(i) * ep.win_tokens] = __float2bfloat16_rn(acc[i]);
+                    }
+                }
             } else if constexpr (MODE == MMQ_OUT_Q8) {
                 // this thread's 64 columns are two whole 32-wide Q8_0 blocks of the output row
                 if (m < M) {
@@ -526,6 +571,12 @@ static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
     ep.qcodes = static_cast<int8_t *>(a.out_codes);
     ep.qquads = static_cast<__half *>(a.out_quads);
     ep.qld = a.out_ld;
+    ep.q = static_cast<__nv_bfloat16 *>(a.q_out);
+    ep.k = static_cast<__nv_bfloat16 *>(a.k_out);
+    ep.vt = static_cast<__nv_bfloat16 *>(a.vt_out);
+    ep.freqs = a.freqs;
+    ep.win_tokens = a.win_tokens;
+    ep.heads = a.heads;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, static_cast<const uint8_t *>(a.a.quads),
                                                   static_cast<const uint8_t *>(a.b.quads), M, N, nblk, a.a.ld, a.b.ld,
                                                   ep, a.err);
@@ -552,6 +603,12 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
     if (mode == MMQ_OUT_F32)
         return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0, BN, EPI_F32>(a, num_sms, s)
                         : launch_tc<MMQ_OUT_F32, 1, BN, EPI_F32>(a, num_sms, s);
+    if (mode == MMQ_OUT_QKV) {
+        if (!a.q_out || !a.k_out || !a.vt_out || a.heads <= 0 || a.b.rows != 3 * 64 * a.heads ||
+            a.win_tokens <= 0 || a.a.rows % a.win_tokens != 0)
+            return cudaErrorInvalidValue;
+        return cvt == 0 ? launch_tc<MMQ_OUT_QKV, 0, BN, 8>(a, num_sms, s) : launch_tc<MMQ_OUT_QKV, 1, BN, 8>(a, num_sms, s);
+    }
     return cudaErrorInvalidValue;
 }
 

@@ -27,6 +27,10 @@ enum MmqOut : int {
     MMQ_OUT_BLOCKDOTS = 1, // dump[(m*N + n)*nblk + b] = int32 block dot (debug/parity)
     MMQ_OUT_Q8 = 2,        // v = acc + bias (GELU-erf if gelu), re-quantised to Q8_0 (ggml-cpu
                            // activation rule) into the QMatrix (out_codes, out_quads, out_ld)
+    MMQ_OUT_QKV = 3,       // attention inputs of a ViT block (sam3.cpp:3742-3776): v = acc + bias over
+                           // N = 3E columns (q | k | v thirds, 64-wide heads), RoPE on the q and k
+                           // thirds (sam3.cpp:3671-3710), written as bf16 Q, K [win*heads][tokens][64]
+                           // and V^T [win*heads][64][tokens]; row m = window * win_tokens + token
 };
 
 constexpr int MMQ_ROW_ALIGN = 128;
@@ -57,6 +61,12 @@ struct MmqArgs {
     void *out_codes = nullptr;      // MMQ_OUT_Q8: int8 [M, N]
     void *out_quads = nullptr;      // MMQ_OUT_Q8: A-side records [ceil(N/256)][out_ld][16 B]
     int out_ld = 0;
+    void *q_out = nullptr;          // MMQ_OUT_QKV: bf16 outputs
+    void *k_out = nullptr;
+    void *vt_out = nullptr;
+    const float *freqs = nullptr;   // MMQ_OUT_QKV: RoPE table [win_tokens][32][2] (cos, sin), or null
+    int win_tokens = 0;             // MMQ_OUT_QKV: tokens per window
+    int heads = 0;                  // MMQ_OUT_QKV: heads (N = 3 * 64 * heads)
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.

@@ -315,71 +315,6 @@ cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const 
     return cudaGetLastError();
 }
 
-// ---- qkv split + RoPE ---------------------------------------------------------
-// One CTA per (64-token tile, window * head): q and k rows [bh][n][64] are
-// written directly; V goes through a shared-memory transpose so that V^T
-// [bh][64][N] is written in 128-byte rows (the layout the attention's
-// K-major V operand wants).
-__global__ void __launch_bounds__(256) qkv_rope_kernel(const float *__restrict__ qkv, const float *__restrict__ freqs,
-                                                       int N, int E, int heads, __nv_bfloat16 *__restrict__ q,
-                                                       __nv_bfloat16 *__restrict__ k, __nv_bfloat16 *__restrict__ vt) {
-    __shared__ __nv_bfloat16 vs[64][64 + 8];  // [dim][token]
-    const int bh = blockIdx.y, bb = bh / heads, h = bh % heads;
-    const int t0 = blockIdx.x * 64;
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int item = it * 256 + threadIdx.x;  // (token, pair)
-        const int tl = item >> 5, pr = item & 31, n = t0 + tl;
-        if (n < N) {
-            const float *src = qkv + (static_cast<int64_t>(bb) * N + n) * 3 * E + h * 64 + 2 * pr;
-            const float2 qq = *reinterpret_cast<const float2 *>(src);
-            const float2 kk = *reinterpret_cast<const float2 *>(src + E);
-            const float2 vv = *reinterpret_cast<const float2 *>(src + 2 * E);
-            float2 qo = qq, ko = kk;
-            if (freqs) {
-                const float2 cs = *reinterpret_cast<const float2 *>(freqs + (static_cast<int64_t>(n) * 32 + pr) * 2);
-                qo.x = __fsub_rn(__fmul_rn(qq.x, cs.x), __fmul_rn(qq.y, cs.y));
-                qo.y = __fadd_rn(__fmul_rn(qq.x, cs.y), __fmul_rn(qq.y, cs.x));
-                ko.x = __fsub_rn(__fmul_rn(kk.x, cs.x), __fmul_rn(kk.y, cs.y));
-                ko.y = __fadd_rn(__fmul_rn(kk.x, cs.y), __fmul_rn(kk.y, cs.x));
-            }
-            const int64_t o = (static_cast<int64_t>(bh) * N + n) * 64 + 2 * pr;
-            *reinterpret_cast<__nv_bfloat162 *>(q + o) = __floats2bfloat162_rn(qo.x, qo.y);
-            *reinterpret_cast<__nv_bfloat162 *>(k + o) = __floats2bfloat162_rn(ko.x, ko.y);
-            vs[2 * pr][tl] = __float2bfloat16_rn(vv.x);
-            vs[2 * pr + 1][tl] = __float2bfloat16_rn(vv.y);
-        }
-    }
-    __syncthreads();
-    // V^T rows: thread -> (dim, 8-token chunk); N % 8 == 0 keeps every 16-byte store aligned
-#pragma unroll
-    for (int it = 0; it < 2; ++it) {
-        const int item = it * 256 + threadIdx.x;
-        const int d = item >> 3, ch = item & 7, n = t0 + ch * 8;
-        if (n < N) {
-            uint4 w;
-            uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                __nv_bfloat162 pair;
-                pair.x = vs[d][ch * 8 + 2 * e];
-                pair.y = vs[d][ch * 8 + 2 * e + 1];
-                wp[e] = *reinterpret_cast<uint32_t *>(&pair);
-            }
-            *reinterpret_cast<uint4 *>(vt + (static_cast<int64_t>(bh) * 64 + d) * N + n) = w;
-        }
-    }
-}
-
-cudaError_t qkv_rope_split(const float *qkv, const float *freqs, int B, int N, int E, int heads, void *q, void *k,
-                           void *vt, cudaStream_t s) {
-    if (E != heads * 64 || B <= 0 || N <= 0 || N % 8 != 0) return cudaErrorInvalidValue;
-    dim3 grid((N + 63) / 64, B * heads);
-    qkv_rope_kernel<<<grid, 256, 0, s>>>(qkv, freqs, N, E, heads, static_cast<__nv_bfloat16 *>(q),
-                                         static_cast<__nv_bfloat16 *>(k), static_cast<__nv_bfloat16 *>(vt));
-    return cudaGetLastError();
-}
-
 __global__ void rowmap_kernel(int G, int win, int *__restrict__ rowmap) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= G * G) return;

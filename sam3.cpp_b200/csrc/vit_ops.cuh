@@ -29,12 +29,6 @@ cudaError_t add_pos_layernorm(const float *conv, const float *pos, int g, int G,
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s);
 
-// qkv rows (B windows x N tokens, 3E wide) -> RoPE'd Q and K as bf16
-// [B][heads][N][64] and V transposed, bf16 [B][heads][64][N]
-// (sam3.cpp:3747-3776, 3671-3710).  freqs: [N][32][2].  N % 8 == 0.
-cudaError_t qkv_rope_split(const float *qkv, const float *freqs, int B, int N, int E, int heads, void *q, void *k,
-                           void *vt, cudaStream_t s);
-
 // Row map of ggml_win_unpart: windowed row -> token row (G x G grid).
 cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s);
 
