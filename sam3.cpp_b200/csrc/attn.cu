@@ -1,8 +1,11 @@
 // attn.cu -- ggml_flash_attn_ext without mask (sam3.cpp:3778): per (window,
 // head) out = softmax(Q K^T * scale) V, head_dim 64, on the 5th-generation
 // tensor cores.  Q and K are bf16 [B*heads][N][64], V is stored transposed,
-// bf16 [B*heads][64][N]; the output is f32 [B*N][heads*64] (ggml's
-// [HD, NH, N, B] result reshaped to [E, W, H, B], sam3.cpp:3780-3781).
+// bf16 [B*heads][64][N]; the output is [B*N][heads*64] (ggml's
+// [HD, NH, N, B] result reshaped to [E, W, H, B], sam3.cpp:3780-3781), either
+// f32 or -- for the proj MUL_MAT that follows -- quantised to Q8_0 with the
+// ggml-cpu activation rule (each softmax thread holds two whole 32-wide
+// blocks of its row), bit-identical to quantising the f32 output.
 //
 // A CTA owns two 128-row query tiles (t = 0, 1) of one (window, head) and
 // streams the keys in tiles of 128:
@@ -31,6 +34,7 @@
 #include <cstdint>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 namespace b200 {
 
@@ -96,7 +100,8 @@ __device__ __forceinline__ float chunk_exp(const uint32_t (&s)[32], float c, flo
 __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     flash_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, int N, int heads, float c_log2,
-                         float *__restrict__ out, int *__restrict__ err) {
+                         float *__restrict__ out, int8_t *__restrict__ qcodes, __half *__restrict__ qquads, int qld,
+                         int *__restrict__ err) {
     using C = AttnCfg;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -295,11 +300,40 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                 if (n < N) {
                     const int bb = bh / heads, h = bh % heads;
                     const float inv = 1.0f / l_run;
-                    float *dst = out + (static_cast<int64_t>(bb) * N + n) * heads * C::HD + h * C::HD;
+                    const int64_t r = static_cast<int64_t>(bb) * N + n;  // output row
 #pragma unroll
-                    for (int d = 0; d < C::HD; d += 4)
-                        *reinterpret_cast<float4 *>(dst + d) =
-                            make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                    for (int d = 0; d < C::HD; ++d) o[d] = o[d] * inv;
+                    if (qcodes) {
+                        const int E = heads * C::HD;
+#pragma unroll
+                        for (int hb = 0; hb < C::HD; hb += 32) {
+                            float amax = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[hb + i]));
+                            const float dq = __fdiv_rn(amax, 127.f);
+                            const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int a0 = __float2int_rn(__fmul_rn(o[hb + 4 * i], id));
+                                const int a1 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 1], id));
+                                const int a2 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 2], id));
+                                const int a3 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 3], id));
+                                pk[i] = (static_cast<uint32_t>(a0) & 0xFFu) | ((static_cast<uint32_t>(a1) & 0xFFu) << 8) |
+                                        ((static_cast<uint32_t>(a2) & 0xFFu) << 16) | ((static_cast<uint32_t>(a3) & 0xFFu) << 24);
+                            }
+                            uint4 *dst = reinterpret_cast<uint4 *>(qcodes + r * E + h * C::HD + hb);
+                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            const int blk = (h * C::HD + hb) >> 5;
+                            qquads[(static_cast<int64_t>(blk >> 3) * qld + r) * 8 + (blk & 7)] = __float2half_rn(dq);
+                        }
+                    } else {
+                        float *dst = out + r * heads * C::HD + h * C::HD;
+#pragma unroll
+                        for (int d = 0; d < C::HD; d += 4)
+                            *reinterpret_cast<float4 *>(dst + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+                    }
                 }
             }
         }
@@ -311,9 +345,11 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
 }
 
 cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B, int N, int heads, float scale,
-                            float *out, int *err, cudaStream_t s) {
+                            const AttnOut &o, int *err, cudaStream_t s) {
     using C = AttnCfg;
-    if (B <= 0 || N <= 0 || heads <= 0 || N % 8 != 0 || !err) return cudaErrorInvalidValue;
+    if (B <= 0 || N <= 0 || heads <= 0 || N % 8 != 0 || !err || (!o.f32 && !o.codes) ||
+        (o.codes && (!o.quads || o.ld < B * N)))
+        return cudaErrorInvalidValue;
     const uint64_t bhn = static_cast<uint64_t>(B) * heads;
     CUtensorMap tq, tk, tv;
     const uint64_t dqk[3] = {64, static_cast<uint64_t>(N), bhn};
@@ -330,8 +366,9 @@ cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     dim3 grid((N + C::QT * C::BQ - 1) / (C::QT * C::BQ), static_cast<unsigned>(bhn));
-    flash_attn_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tq, tk, tv, N, heads, scale * 1.4426950408889634f,
-                                                                  out, err);
+    flash_attn_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(
+        tq, tk, tv, N, heads, scale * 1.4426950408889634f, o.f32, static_cast<int8_t *>(o.codes),
+        static_cast<__half *>(o.quads), o.ld, err);
     return cudaGetLastError();
 }
 

@@ -5,10 +5,20 @@
 
 namespace b200 {
 
-// q, k: bf16 [B*heads][N][64]; vt: bf16 [B*heads][64][N] (V transposed);
-// out: f32 [B*N][heads*64].  N must be a multiple of 8 (TMA row pitch).
-// Bounded waits report through *err (device word).
+// Output of the attention, [B*N][heads*64] in row order: f32 rows, or (codes
+// set) Q8_0 codes int8 [B*N][heads*64] + activation scale records
+// [ceil(heads*64/256)][ld][8] fp16, the quantised layout the MUL_MAT reads.
+struct AttnOut {
+    float *f32 = nullptr;
+    void *codes = nullptr;
+    void *quads = nullptr;
+    int ld = 0;
+};
+
+// q, k: bf16 [B*heads][N][64]; vt: bf16 [B*heads][64][N] (V transposed).
+// N must be a multiple of 8 (TMA row pitch).  Bounded waits report through
+// *err (device word).
 cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B, int N, int heads, float scale,
-                            float *out, int *err, cudaStream_t s);
+                            const AttnOut &out, int *err, cudaStream_t s);
 
 }  // namespace b200

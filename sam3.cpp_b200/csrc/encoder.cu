@@ -76,7 +76,7 @@ struct Vit {
     NeckScaleW neck[4];
     std::vector<std::string> missing;
     // activations
-    DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, q, k, v, attn, rowmap;
+    DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, q, k, v, rowmap;
     DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4];
     int out_side[4] = {0, 0, 0, 0};
     int img_cap = 0;  // pixels of img_u8
@@ -159,7 +159,7 @@ static bool alloc_activations(Vit *v) {
               v->codes_b.alloc(static_cast<size_t>(T) * maxk) &&
               v->quads_b.alloc(maxk / 32 * v->Tpad * 16) &&
               v->q.alloc(static_cast<size_t>(T) * E * 2) && v->k.alloc(static_cast<size_t>(T) * E * 2) &&
-              v->v.alloc(static_cast<size_t>(T) * E * 2) && v->attn.alloc(static_cast<size_t>(T) * E * 4) &&
+              v->v.alloc(static_cast<size_t>(T) * E * 2) &&
               v->rowmap.alloc(static_cast<size_t>(T) * 4) && v->x16.alloc(static_cast<size_t>(T) * E * 2) &&
               v->mp16.alloc(static_cast<size_t>(T / 4) * E * 2) &&
               v->n_a.alloc(static_cast<size_t>(4) * T * v->MID * 2) &&
@@ -270,14 +270,17 @@ static bool run_block(Vit *v, int i, float *x) {
     const bool glob = is_global(hp, i);
     const int B = glob ? 1 : (G / ws) * (G / ws);
     const int N = glob ? T : ws * ws;
+    AttnOut attn_q8;  // the proj MUL_MAT's quantised input (window order), written by the attention
+    attn_q8.codes = v->codes_a.p;
+    attn_q8.quads = v->quads_a.p;
+    attn_q8.ld = v->Tpad;
     return launched(v, layernorm_q8(x, T, E, w.n1w.as<float>(), w.n1b.as<float>(), 1e-5f, G, glob ? 0 : ws,
                                 v->codes_a.p, v->quads_a.p, v->Tpad, s),
                    "ln1") &&
            mmq_qkv(v, w, N) &&
            launched(v, flash_attention(v->q.p, v->k.p, v->v.p, B, N, hp.heads, 1.0f / sqrtf(static_cast<float>(E / hp.heads)),
-                                   v->attn.as<float>(), v->be->err, s),
+                                   attn_q8, v->be->err, s),
                    "attention") &&
-           launched(v, quantize_rows_q8(v->attn.as<float>(), E, T, E, v->codes_a.p, v->quads_a.p, v->Tpad, s), "quant") &&
            mmq(v, v->codes_a.p, v->quads_a.p, w.proj, MMQ_OUT_F32, w.proj_b.as<float>(), x, 1,
                glob ? nullptr : v->rowmap.as<int>(), nullptr, nullptr, 0) &&
            launched(v, layernorm_q8(x, T, E, w.n2w.as<float>(), w.n2b.as<float>(), 1e-5f, G, 0, v->codes_a.p, v->quads_a.p,
