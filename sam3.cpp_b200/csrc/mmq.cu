@@ -20,6 +20,8 @@
 #include "ptx.cuh"
 #include "tmap.h"
 
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -138,39 +140,55 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
 }
 
 // ---------------------------------------------------------------------------
-// tcgen05 MMQ kernel, CTA tile 128 (tokens) x 128 (features), persistent.
+// tcgen05 MMQ kernel.  CTA tile: 96 tokens x BN features (BN = 64 or 128),
+// persistent over tiles.
 //
-// Warp roles (64 + 32 * 8 threads):
-//   warp 0     : TMA producer (one lane).  A stage holds four K-blocks: the
-//                A and B codes (128 int8 per row = one 128-byte swizzle
-//                atom) and the scale quads of the four blocks for A and B
-//                (4 x 2 KB each, one 3-D TMA box per operand).
-//   warp 1     : TMEM allocator + MMA issuer (one lane).  Per K-block into
-//                TMEM buffer `buf` (256 columns): I_b -> columns [0, 128)
-//                (int32), S_b -> [128, 256) (fp32); commit to tfull[buf].
-//   warps 2..9 : epilogue.  Warp w reads TMEM lanes 32*(w%4)..+31 (the lane
-//                quarter it may access) and column half (w-2)/4 (64 cols).
-// Shared memory: STAGES x 48 KB stages, a 2 KB zero region (the unused
-// second K-chunk of every scale operand), barriers.
+// The MMAs are M = 128 and the TMEM lane quarter of sub-partition q is
+// readable only by that sub-partition's warps.  Sub-partition 1 runs the MMA
+// issuer and the TMA producer (measured: epilogue warps sharing a
+// sub-partition with the MMA issuer hand TMEM slots back 350-1100 cycles
+// late, and every slot waits for them), so its lane quarter (MMA rows
+// 32..63) carries zero rows and the tile's 96 tokens sit in MMA rows 0..31
+// and 64..127.  The tensor core has the headroom for the idle quarter.
+//
+// Warp roles (8 warps):
+//   warp 1     : TMEM allocator + MMA issuer (one elected lane).  Per K-block
+//                into TMEM slot `buf` (2 BN columns): I_b -> [0, BN) (int32),
+//                S_b -> [BN, 2 BN) (fp32); commit to tfull[buf].
+//   warp 5     : TMA producer (one elected lane).  A stage holds four
+//                K-blocks: the A codes (three 32-row boxes into MMA rows 0..31
+//                and 64..127), the B codes (128 int8 per row = one 128-byte
+//                swizzle atom), the A scale records of the stage's 8-block
+//                group and the four blocks' B scale records (bulk copies).
+//   warps w with w % 4 != 1 : epilogue (EPQ = 2 or 4 per lane quarter).  Warp
+//                w reads TMEM lane quarter w % 4 (0, 2 or 3: tile rows 0..31,
+//                32..63, 64..95) and column slice w / 4 (BN / EPQ columns of
+//                one output row per thread).
+// Shared memory: STAGES stages (MMA rows 32..63 of the A codes and A records
+// zero), a 2 KB zero region (the unused second K-chunk of every scale
+// operand), barriers.
 // ---------------------------------------------------------------------------
-template <int BN_, int EPI_ = 8>
+template <int BN_, int EPQ_ = 2>
 struct TcCfg {
-    static constexpr int BM = 128;
+    static constexpr int BM = 128;                  // MMA rows
+    static constexpr int ROWS = 96;                 // tokens per tile
     static constexpr int BN = BN_;
     static constexpr int BLK = 4;                   // K-blocks per stage
     static constexpr int BK = 32 * BLK;             // int8 per stage row: 128 bytes = one swizzle atom
     static constexpr int A_BYTES = BM * BK;         // 16 KB
     static constexpr int B_BYTES = BN * BK;
-    static constexpr int Q_BYTES = BM * 16;         // one block's A scale operand: 2 KB
+    static constexpr int Q_BYTES = BM * 16;         // the stage's A scale operand (one record group): 2 KB
     static constexpr int QB_BYTES = BN * 16;        // one block's B scale operand
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES + BLK * QB_BYTES;  // A scales: one group record
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES + BLK * QB_BYTES;
     static constexpr int STAGES = BN == 128 ? 4 : 6;
     static constexpr int ZERO_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = ZERO_OFF + Q_BYTES;
-    static constexpr int EPI_WARPS = EPI_;           // 8 or 16 epilogue warps
-    static constexpr int THREADS = 64 + EPI_WARPS * 32;
-    static constexpr int COLS = BN / (EPI_WARPS / 4);  // per epilogue thread
+    static constexpr int EPQ = EPQ_;                // epilogue warps per used lane quarter (2 or 4)
+    static constexpr int THREADS = 128 * EPQ;       // warps w % 4 == 1 beyond warps 1 and 5 stay idle
+    static constexpr int EPI_WARPS = 3 * EPQ;
+    static constexpr int COLS = BN / EPQ;           // output columns per epilogue thread
     static constexpr int CHUNK = 32;
+    static_assert(COLS % CHUNK == 0, "whole 32-column TMEM loads (and whole Q8_0 blocks) per thread");
     static constexpr int SLOT_COLS = 2 * BN;        // one K-block: I (BN columns) then S (BN columns)
     static constexpr int SLOTS = 512 / SLOT_COLS;   // K-blocks in flight between MMA and epilogue
     static constexpr int TMEM_COLS = 512;
@@ -228,14 +246,14 @@ __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
            ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
-template <int MODE, int CVT, int BN, int EPI>
-__global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
+template <int MODE, int CVT, int BN, int EPQ>
+__global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
                   int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err) {
     const float *__restrict__ bias = ep.bias;
     int32_t *__restrict__ dump = ep.dump;
-    using C = TcCfg<BN, EPI>;
+    using C = TcCfg<BN, EPQ>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
@@ -246,14 +264,22 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int num_m = (M + C::BM - 1) / C::BM;
+    const int num_m = (M + C::ROWS - 1) / C::ROWS;
     const int num_n = (N + C::BN - 1) / C::BN;
     const int num_tiles = num_m * num_n;
     const int kstages = (nblk + C::BLK - 1) / C::BLK;
 
-    // zero region read by every scale MMA as its second K-chunk
+    // zero region read by every scale MMA as its second K-chunk, and the
+    // idle lane quarter's MMA rows 32..63 of every stage's A codes and records
     for (int i = threadIdx.x; i < C::Q_BYTES / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(smem + C::ZERO_OFF)[i] = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < C::STAGES * (32 * C::BK + 32 * 16) / 16; i += blockDim.x) {
+        const int st = i / ((32 * C::BK + 32 * 16) / 16), j = i % ((32 * C::BK + 32 * 16) / 16);
+        uint8_t *sb = smem + st * C::STAGE_BYTES;
+        uint8_t *dst = j < 32 * C::BK / 16 ? sb + 32 * C::BK + j * 16
+                                           : sb + C::A_BYTES + C::B_BYTES + 32 * 16 + (j - 32 * C::BK / 16) * 16;
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -278,14 +304,17 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp == 5) {
         // ---- TMA producer: warp-uniform loop, one elected lane issues ----
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-            const int m0 = (t % num_m) * C::BM;
+            const int m0 = (t % num_m) * C::ROWS;
             const int n0 = (t / num_m) * C::BN;
+            // A scale records of rows [m0, m0 + 96) that exist (lda_q >= M; rows past it are never stored)
+            const int r1 = lda_q - m0 < 32 ? (lda_q - m0 > 0 ? lda_q - m0 : 0) : 32;
+            const int r2 = lda_q - m0 - 32 < 64 ? (lda_q - m0 - 32 > 0 ? lda_q - m0 - 32 : 0) : 64;
             for (int ks = 0; ks < kstages; ++ks) {
                 if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, err, ERR_WAIT_EMPTY))) {
                     ok = false;
@@ -297,10 +326,15 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
                     // scale records are contiguous per (group or block, tile): one bulk copy each
                     const int b0 = ks * C::BLK;
                     const int nb = nblk - b0 < C::BLK ? nblk - b0 : C::BLK;
-                    mbar_arrive_expect_tx(&full[stage], C::A_BYTES + C::B_BYTES + C::Q_BYTES + nb * C::QB_BYTES);
-                    tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);
+                    mbar_arrive_expect_tx(&full[stage],
+                                          3 * 32 * C::BK + C::B_BYTES + (r1 + r2) * 16 + nb * C::QB_BYTES);
+                    tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);                         // MMA rows 0..31
+                    tma_load_2d(sb + 64 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 32);       // 64..95
+                    tma_load_2d(sb + 96 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 64);       // 96..127
                     tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
-                    bulk_load(q, quads_a + (static_cast<int64_t>(b0 >> 3) * lda_q + m0) * 16, C::Q_BYTES, &full[stage]);
+                    const uint8_t *qa = quads_a + (static_cast<int64_t>(b0 >> 3) * lda_q + m0) * 16;
+                    if (r1 > 0) bulk_load(q, qa, r1 * 16, &full[stage]);
+                    if (r2 > 0) bulk_load(q + 64 * 16, qa + 32 * 16, r2 * 16, &full[stage]);
                     for (int j = 0; j < nb; ++j)
                         bulk_load(q + C::Q_BYTES + j * C::QB_BYTES,
                                   quads_b + (static_cast<int64_t>(b0 + j) * ldb_q + n0) * 16, C::QB_BYTES, &full[stage]);
@@ -364,17 +398,17 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
                 }
             }
         }
-    } else {
+    } else if ((warp & 3) != 1) {
         // ---- epilogue warps ----
         constexpr int CHUNK = C::CHUNK;
-        const int q = warp & 3;
-        const int h = (warp - 2) >> 2;
-        const int row = q * 32 + lane;
+        const int q = warp & 3;                              // TMEM lane quarter: 0, 2 or 3
+        const int h = warp >> 2;                             // column slice
+        const int row = (q == 0 ? 0 : (q - 1) * 32) + lane;  // tile row (token m0 + row)
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         uint32_t blk = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-            const int m0 = (t % num_m) * C::BM;
+            const int m0 = (t % num_m) * C::ROWS;
             const int n0 = (t / num_m) * C::BN;
             const int m = m0 + row;
             float acc[C::COLS];
@@ -545,20 +579,20 @@ __global__ void __launch_bounds__(TcCfg<BN, EPI>::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-template <int MODE, int CVT, int BN, int EPI>
-static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
-    using C = TcCfg<BN, EPI>;
+template <int MODE, int CVT, int BN, int EPQ = 2>
+static cudaError_t launch_tc_epq(const MmqArgs &a, int num_sms, cudaStream_t s) {
+    using C = TcCfg<BN, EPQ>;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K, nblk = K / 32;
     CUtensorMap tma, tmb;
     const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, db[2] = {uint64_t(K), uint64_t(N)}, sk[1] = {uint64_t(K)};
-    const uint32_t bxa[2] = {C::BK, C::BM}, bxb[2] = {C::BK, C::BN};
+    const uint32_t bxa[2] = {C::BK, 32}, bxb[2] = {C::BK, C::BN};
     if (!make_tmap(&tma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a.codes, 2, da, sk, bxa, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, sk, bxb, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    auto kern = mmq_tc_kernel<MODE, CVT, BN, EPI>;
+    auto kern = mmq_tc_kernel<MODE, CVT, BN, EPQ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
+    const int tiles = ((M + C::ROWS - 1) / C::ROWS) * ((N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     MmqEpi ep;
     ep.bias = a.bias;
@@ -583,6 +617,23 @@ static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// Epilogue warps per used lane quarter: 4 (default; measured 48.1 against
+// 42.1 images/s with 2) or 2 (tuning: env SAM3B200_MMQ_EPQ=2).
+static int mmq_epq() {
+    static const int v = [] {
+        const char *ev = getenv("SAM3B200_MMQ_EPQ");
+        return ev && atoi(ev) == 2 ? 2 : 4;
+    }();
+    return v;
+}
+
+template <int MODE, int CVT, int BN>
+static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
+    if constexpr (BN == 128)  // 4 warps per quarter need BN / 4 >= 32 columns each
+        if (mmq_epq() == 4) return launch_tc_epq<MODE, CVT, BN, 4>(a, num_sms, s);
+    return launch_tc_epq<MODE, CVT, BN, 2>(a, num_sms, s);
+}
+
 static bool valid_args(const MmqArgs &a) {
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
     return K == a.b.K && K > 0 && K % 32 == 0 && M > 0 && N > 0 && a.a.ld >= M && a.b.ld >= N &&
@@ -594,20 +645,19 @@ static bool valid_args(const MmqArgs &a) {
 // software-pipelined drain measured slower on B200.)
 template <int BN>
 static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt) {
-    constexpr int EPI_F32 = 8;
-    if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 1, BN, 8>(a, num_sms, s);
+    if (mode == MMQ_OUT_BLOCKDOTS) return launch_tc<MMQ_OUT_BLOCKDOTS, 0, BN>(a, num_sms, s);
     if (mode == MMQ_OUT_Q8) {
         if (a.b.rows % 32 != 0 || !a.out_codes || !a.out_quads || a.out_ld < a.a.rows) return cudaErrorInvalidValue;
-        return cvt == 0 ? launch_tc<MMQ_OUT_Q8, 0, BN, 8>(a, num_sms, s) : launch_tc<MMQ_OUT_Q8, 1, BN, 8>(a, num_sms, s);
+        return cvt == 0 ? launch_tc<MMQ_OUT_Q8, 0, BN>(a, num_sms, s) : launch_tc<MMQ_OUT_Q8, 1, BN>(a, num_sms, s);
     }
     if (mode == MMQ_OUT_F32)
-        return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0, BN, EPI_F32>(a, num_sms, s)
-                        : launch_tc<MMQ_OUT_F32, 1, BN, EPI_F32>(a, num_sms, s);
+        return cvt == 0 ? launch_tc<MMQ_OUT_F32, 0, BN>(a, num_sms, s)
+                        : launch_tc<MMQ_OUT_F32, 1, BN>(a, num_sms, s);
     if (mode == MMQ_OUT_QKV) {
         if (!a.q_out || !a.k_out || !a.vt_out || a.heads <= 0 || a.b.rows != 3 * 64 * a.heads ||
             a.win_tokens <= 0 || a.a.rows % a.win_tokens != 0)
             return cudaErrorInvalidValue;
-        return cvt == 0 ? launch_tc<MMQ_OUT_QKV, 0, BN, 8>(a, num_sms, s) : launch_tc<MMQ_OUT_QKV, 1, BN, 8>(a, num_sms, s);
+        return cvt == 0 ? launch_tc<MMQ_OUT_QKV, 0, BN>(a, num_sms, s) : launch_tc<MMQ_OUT_QKV, 1, BN>(a, num_sms, s);
     }
     return cudaErrorInvalidValue;
 }
