@@ -45,7 +45,7 @@ def _load(name):
 
 # DRAM traffic of one MUL_MAT launch at the cfg3 shapes (mean of qkv, proj, fc1,
 # fc2), from an ncu capture of ViT block 0's four launches.
-MMQ_DRAM_BYTES_PER_LAUNCH = 30.07e6
+MMQ_DRAM_BYTES_PER_LAUNCH = 27.44e6
 
 
 def vit_ops_per_image(hp):
@@ -286,8 +286,8 @@ def main():
                          "frac": achieved / peak_int8 if peak_int8 else None,
                          "traffic": MMQ_DRAM_BYTES_PER_LAUNCH, "traffic_unit": "bytes per launch",
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
-                                           "MUL_MAT launches of one ViT block (qkv 21.7, proj 28.8, fc1 13.0, "
-                                           "fc2 56.7 MB); operands stream L2 -> SM, not from DRAM",
+                                           "MUL_MAT launches of one ViT block (qkv 10.6, proj 28.9, fc1 13.1, "
+                                           "fc2 57.1 MB); operands stream L2 -> SM, not from DRAM",
                          "peak_source": "dense int8 measured in this run (cuBLASLt torch._int_mm 8192^3); "
                                         "MEASURED_PEAKS.json holds no int8 figure",
                          "ops_per_image": ops, "launches_timed": mmq_n,
