@@ -7,11 +7,15 @@
 // ggml-cpu activation rule (each softmax thread holds two whole 32-wide
 // blocks of its row), bit-identical to quantising the f32 output.
 //
-// A CTA owns two 128-row query tiles (t = 0, 1) of one (window, head) and
-// streams the keys in tiles of 128:
-//   warp 0     : TMA producer -- both Q tiles once, then K and V^T tiles
-//                through a STAGES-deep ring (128-byte swizzle, zero fill
-//                past N);
+// A CTA owns two query tiles (t = 0, 1) of 96 queries of one (window, head)
+// and streams the keys in tiles of 128.  The MMAs are M = 128; the TMEM lane
+// quarter of sub-partition 1 (MMA rows 32..63), where the MMA issuer and the
+// producer run, carries zero query rows, so no softmax warp shares their
+// sub-partition (such warps fall behind and hold every hand-off back).  576
+// and 5184 tokens are whole numbers of 192-query CTAs.
+//   warp 5     : TMA producer -- both Q tiles once (three 32-row boxes into
+//                MMA rows 0..31 and 64..127), then K and V^T tiles through a
+//                STAGES-deep ring (128-byte swizzle, zero fill past N);
 //   warp 1     : TMEM allocator + MMA issuer -- S_t(j) = Q_t K_j^T (M = 128,
 //                N = 128 keys, K = 64) and, once softmax t has written
 //                P_t(j), PV_t(j) = P_t(j) V_j (A = P read from tensor memory,
@@ -19,7 +23,7 @@
 //                (ready[t]) for the pair: commits hold the issuing thread far
 //                longer than MMAs.  The tiles alternate, so the tensor core
 //                works on one tile while the other tile's softmax runs;
-//   warps 2..9 : softmax, warps 2 + 4t .. 5 + 4t for tile t, one query row per
+//   warps 0, 2, 3 (tile 0) and 4, 6, 7 (tile 1): softmax, one query row per
 //                thread (the TMEM lane quarter of warp w is w % 4).  Per key
 //                tile: pass 1 takes the row max of S, pass 2 writes
 //                P = 2^(s c - m) as bf16 into tensor memory and sums it; the
@@ -41,7 +45,7 @@ namespace b200 {
 namespace {
 
 struct AttnCfg {
-    static constexpr int BQ = 128, BKV = 128, HD = 64, QT = 2;
+    static constexpr int BQ = 128, ROWS = 96, BKV = 128, HD = 64, QT = 2;
     static constexpr int STAGES = 3;
     static constexpr int Q_BYTES = BQ * HD * 2;         // 16 KB per query tile
     static constexpr int K_BYTES = BKV * HD * 2;        // 16 KB
@@ -50,7 +54,7 @@ struct AttnCfg {
     static constexpr int KV_OFF = QT * Q_BYTES;
     static constexpr int BAR_OFF = KV_OFF + STAGES * STAGE_BYTES;  // 128 KB: one CTA per SM
     static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-    static constexpr int THREADS = 64 + QT * 128;
+    static constexpr int THREADS = 256;
     static constexpr uint32_t S_COL = 0, P_COL = 128, PV_COL = 192, TILE_COLS = 256;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -116,9 +120,16 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
-    const int q0 = blockIdx.x * C::QT * C::BQ;
+    const int q0 = blockIdx.x * C::QT * C::ROWS;
     const int ntiles = (N + C::BKV - 1) / C::BKV;
-    const int nq = N - q0 > C::BQ ? C::QT : 1;  // query tiles of this CTA that hold rows < N
+    const int nq = N - q0 > C::ROWS ? C::QT : 1;  // query tiles of this CTA that hold rows < N
+
+    // MMA rows 32..63 of both Q tiles stay zero (TMA writes rows 0..31 and 64..127)
+    for (int i = threadIdx.x; i < C::QT * 32 * 128 / 16; i += blockDim.x) {
+        const int t = i / (32 * 128 / 16), j = i % (32 * 128 / 16);
+        *reinterpret_cast<uint4 *>(smem + t * C::Q_BYTES + 32 * 128 + j * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -128,7 +139,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
         }
         for (int t = 0; t < C::QT; ++t) {
             mbar_init(&ready[t], 1);
-            mbar_init(&pdone[t], 4);
+            mbar_init(&pdone[t], 3);
         }
         fence_mbar_init();
         prefetch_tmap(&tm_q);
@@ -144,11 +155,17 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp == 5) {
         // ---- TMA producer ----
         if (elect_one()) {
-            mbar_arrive_expect_tx(q_full, nq * C::Q_BYTES);
-            for (int t = 0; t < nq; ++t) tma_load_3d(smem + t * C::Q_BYTES, &tm_q, q_full, 0, q0 + t * C::BQ, bh);
+            mbar_arrive_expect_tx(q_full, nq * 3 * 32 * 128);
+            for (int t = 0; t < nq; ++t) {
+                uint8_t *qb = smem + t * C::Q_BYTES;
+                const int r0 = q0 + t * C::ROWS;
+                tma_load_3d(qb, &tm_q, q_full, 0, r0, bh);                 // MMA rows 0..31
+                tma_load_3d(qb + 64 * 128, &tm_q, q_full, 0, r0 + 32, bh);  // 64..95
+                tma_load_3d(qb + 96 * 128, &tm_q, q_full, 0, r0 + 64, bh);  // 96..127
+            }
         }
         __syncwarp();
         for (int j = 0; j < ntiles; ++j) {
@@ -225,11 +242,11 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
             if (elect_one()) mma_commit(&kv_empty[j % C::STAGES]);  // every reader of stage j has been issued
             __syncwarp();
         }
-    } else {
+    } else if ((warp & 3) != 1) {
         // ---- softmax: one query row per thread ----
-        const int t = (warp - 2) >> 2;
-        const int quarter = warp & 3;
-        const int row = quarter * 32 + lane;
+        const int t = warp >> 2;
+        const int quarter = warp & 3;                             // 0, 2 or 3
+        const int row = (quarter == 0 ? 0 : (quarter - 1) * 32) + lane;  // query q0 + 96 t + row
         const uint32_t base = tmem + t * C::TILE_COLS + (static_cast<uint32_t>(quarter * 32) << 16);
         if (t < nq) {
             float o[C::HD];
@@ -296,7 +313,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
             if (ok && __all_sync(0xffffffffu, mbar_wait(&ready[t], ntiles & 1, err, AERR_PV_FULL))) {
                 tc_fence_after();
                 fold_pv(alpha_prev);
-                const int n = q0 + t * C::BQ + row;
+                const int n = q0 + t * C::ROWS + row;
                 if (n < N) {
                     const int bb = bh / heads, h = bh % heads;
                     const float inv = 1.0f / l_run;
@@ -354,18 +371,19 @@ cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B,
     CUtensorMap tq, tk, tv;
     const uint64_t dqk[3] = {64, static_cast<uint64_t>(N), bhn};
     const uint64_t sqk[2] = {64 * 2, static_cast<uint64_t>(N) * 64 * 2};
+    const uint32_t bq[3] = {64, 32, 1};
     const uint32_t bqk[3] = {64, 128, 1};
     const uint64_t dv[3] = {static_cast<uint64_t>(N), 64, bhn};
     const uint64_t sv[2] = {static_cast<uint64_t>(N) * 2, static_cast<uint64_t>(N) * 64 * 2};
     const uint32_t bv[3] = {64, 64, 1};
-    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 3, dqk, sqk, bqk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 3, dqk, sqk, bq, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 3, dqk, sqk, bqk, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, vt, 3, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(flash_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    dim3 grid((N + C::QT * C::BQ - 1) / (C::QT * C::BQ), static_cast<unsigned>(bhn));
+    dim3 grid((N + C::QT * C::ROWS - 1) / (C::QT * C::ROWS), static_cast<unsigned>(bhn));
     flash_attn_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(
         tq, tk, tv, N, heads, scale * 1.4426950408889634f, o.f32, static_cast<int8_t *>(o.codes),
         static_cast<__half *>(o.quads), o.ld, err);

@@ -4,8 +4,12 @@
 //                (128-byte swizzle);
 //   warp 1     : TMEM allocator + MMA issuer (one lane), four K=16 MMAs
 //                per stage accumulating into TMEM buffer (tile & 1);
-//   warps 2..5 : epilogue, one accumulator row per thread, while the MMA
-//                warp already works on the next tile in the other buffer.
+//   warps 2..17: epilogue, four warps per TMEM lane quarter (warp w reads
+//                lane quarter w % 4 and the 32-column slice (w - 2) / 4 of a
+//                row), while the MMA warp already works on the next tile in
+//                the other buffer.  With a single epilogue warp per
+//                sub-partition the drain of a 128 x 128 tile outlasted the
+//                MMAs of the next one for K <= 1024.
 #include "gemm_f16.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -20,8 +24,9 @@ struct GCfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGES = 6;
     static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-    static constexpr int THREADS = 192;
-    static constexpr int EPI_WARPS = 4;
+    static constexpr int EPI_WARPS = 16;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int COLS = BN / (EPI_WARPS / 4);  // columns per epilogue thread
     static constexpr int TMEM_COLS = 256;
     static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
     static_assert(SMEM_BYTES <= 232448, "smem");
@@ -132,6 +137,7 @@ __global__ void __launch_bounds__(GCfg::THREADS, 1)
         }
     } else {
         const int q = warp & 3;
+        const int cs = ((warp - 2) >> 2) * C::COLS;  // this warp's column slice
         const int row = q * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         uint32_t it = 0;
@@ -141,11 +147,11 @@ __global__ void __launch_bounds__(GCfg::THREADS, 1)
             tc_fence_after();
             const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
             const int m = m0 + row;
-            for (int c = 0; c < C::BN; c += 32) {
+            for (int c = cs; c < cs + C::COLS; c += 32) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * C::BN + c, v);
                 tmem_wait_ld();
-                if (c + 32 == C::BN) {
+                if (c + 32 == cs + C::COLS) {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tempty[buf]);
