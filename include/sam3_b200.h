@@ -193,6 +193,11 @@ int sam3b200_vit_output(sam3b200_vit *vit, int i, const float **dev, int64_t ne[
  * CHW [img, img, 3] normalised (p/255 - 0.5)/0.5.  Asynchronous. */
 int sam3b200_preprocess(sam3b200_backend *be, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev);
 
+/* sam2_preprocess_image (sam3.cpp:3522-3548, same resize): the SAM2 / Hiera
+ * input, normalised (p/255 - mean[c]) / std[c] with the ImageNet mean
+ * (0.485, 0.456, 0.406) and std (0.229, 0.224, 0.225).  Asynchronous. */
+int sam3b200_preprocess_sam2(sam3b200_backend *be, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev);
+
 /* Stage runners on caller-provided device tensors, the analogue of the
  * reference's stage test hooks (sam3.h sam3_vit_prefix_stage /
  * sam3_vit_block_stage): prefix image f32 CHW -> x [embed, G, G]; one

@@ -148,12 +148,13 @@ def _vit_lib():
     if not getattr(L, "_vit_sigs", False):
         vp, i32 = ctypes.c_void_p, ctypes.c_int
         L.orc_preprocess_sam3.argtypes = [vp, i32, i32, i32, vp]
+        L.orc_preprocess_sam2.argtypes = [vp, i32, i32, i32, vp]
         L.orc_vit_prefix.argtypes = [vp, vp, vp, vp, i32]
         L.orc_vit_block.argtypes = [vp, vp, i32, vp, i32]
         L.orc_neck.argtypes = [vp, vp, vp, vp, i32]
         L.orc_layer_norm.argtypes = [vp, vp, ctypes.c_int64, i32, ctypes.c_float, vp, vp, i32]
         L.orc_attention.argtypes = [vp, vp, vp, i32, i32, i32, ctypes.c_float, vp, i32]
-        for f in ("orc_preprocess_sam3", "orc_vit_prefix", "orc_vit_block", "orc_neck", "orc_layer_norm",
+        for f in ("orc_preprocess_sam3", "orc_preprocess_sam2", "orc_vit_prefix", "orc_vit_block", "orc_neck", "orc_layer_norm",
                   "orc_attention"):
             getattr(L, f).restype = None
         L._vit_sigs = True
@@ -217,6 +218,13 @@ class OracleVit:
         S = self.hp["img"]
         out = np.empty((3, S, S), np.float32)
         _vit_lib().orc_preprocess_sam3(rgb.ctypes.data, rgb.shape[1], rgb.shape[0], S, out.ctypes.data)
+        return out
+
+    def preprocess_sam2(self, rgb: np.ndarray, img: int) -> np.ndarray:
+        """sam2_preprocess_image (sam3.cpp:3522-3548) to img x img."""
+        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+        out = np.empty((3, img, img), np.float32)
+        _vit_lib().orc_preprocess_sam2(rgb.ctypes.data, rgb.shape[1], rgb.shape[0], img, out.ctypes.data)
         return out
 
     def prefix(self, img_chw: np.ndarray) -> np.ndarray:

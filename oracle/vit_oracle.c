@@ -55,6 +55,27 @@ void orc_preprocess_sam3(const uint8_t *rgb, int w, int h, int img, float *out) 
     free(tmp);
 }
 
+/* sam2_preprocess_image, sam3.cpp:3522-3548: the same resize, ImageNet
+ * normalisation (v - mean[c]) / std[c] with v = p / 255.0f. */
+void orc_preprocess_sam2(const uint8_t *rgb, int w, int h, int img, float *out) {
+    static const float mean[3] = {0.485f, 0.456f, 0.406f};
+    static const float std_d[3] = {0.229f, 0.224f, 0.225f};
+    uint8_t *tmp = NULL;
+    const uint8_t *px = rgb;
+    if (w != img || h != img) {
+        tmp = (uint8_t *)malloc((size_t)img * img * 3);
+        resize_bilinear(rgb, w, h, tmp, img, img);
+        px = tmp;
+    }
+    for (int c = 0; c < 3; ++c)
+        for (int y = 0; y < img; ++y)
+            for (int x = 0; x < img; ++x) {
+                const float v = px[(y * img + x) * 3 + c] / 255.0f;
+                out[(size_t)c * img * img + (size_t)y * img + x] = (v - mean[c]) / std_d[c];
+            }
+    free(tmp);
+}
+
 /* ---- ggml_norm + affine: sam3.cpp:1041-1051 ---------------------------- */
 void orc_layer_norm(const float *x, float *y, int64_t rows, int n, float eps, const float *w, const float *b,
                     int n_threads) {

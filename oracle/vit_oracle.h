@@ -59,6 +59,9 @@ typedef struct {
  * uint8 HWC (w x h) -> f32 CHW img x img, (p/255 - 0.5)/0.5 */
 void orc_preprocess_sam3(const uint8_t *rgb, int w, int h, int img, float *out_chw);
 
+/* sam2_preprocess_image (sam3.cpp:3522-3548): ImageNet mean/std. */
+void orc_preprocess_sam2(const uint8_t *rgb, int w, int h, int img, float *out_chw);
+
 /* ggml_norm over rows of n (sam3_layer_norm, sam3.cpp:1041-1051) then * w + b */
 void orc_layer_norm(const float *x, float *y, int64_t rows, int n, float eps, const float *w, const float *b,
                     int n_threads);

@@ -75,6 +75,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_vit_run_block": (i32, [vp, i32, vp]),
         "sam3b200_vit_run_neck": (i32, [vp, vp]),
         "sam3b200_preprocess": (i32, [vp, vp, i32, i32, i32, vp]),
+        "sam3b200_preprocess_sam2": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_backend_launch_count": (ctypes.c_longlong, [vp]),
         "sam3b200_backend_profile": (i32, [vp, i32]),
         "sam3b200_backend_profile_read": (i32, [vp, i32, ctypes.POINTER(ctypes.c_double),
@@ -281,6 +282,10 @@ class Backend:
 
     def preprocess(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
         _check(lib().sam3b200_preprocess(self.h, rgb_dev.ptr, w, h, img, out.ptr), "preprocess")
+
+    def preprocess_sam2(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
+        """sam2_preprocess_image: ImageNet-normalised CHW (sam3.cpp:3522-3548)."""
+        _check(lib().sam3b200_preprocess_sam2(self.h, rgb_dev.ptr, w, h, img, out.ptr), "preprocess_sam2")
 
     @property
     def launches(self) -> int:

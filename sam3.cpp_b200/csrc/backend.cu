@@ -3,7 +3,9 @@
 // tensor-core layout, and the MUL_MAT node.
 #include "../../include/sam3_b200.h"
 #include "backend_impl.h"
+#include "gemm_f16.cuh"
 #include "mmq.cuh"
+#include "vit_ops.cuh"
 
 #include <cstdarg>
 #include <cstdio>
@@ -213,38 +215,64 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
         set_error("weight_upload: null argument");
         return nullptr;
     }
-    if (type != SAM3B200_TYPE_Q8_0 && type != SAM3B200_TYPE_Q4_0) {
-        set_error("weight_upload: unsupported weight type %d (Q8_0=8, Q4_0=2 supported)", type);
+    const bool quant = type == SAM3B200_TYPE_Q8_0 || type == SAM3B200_TYPE_Q4_0 || type == SAM3B200_TYPE_Q4_1;
+    const bool dense = type == SAM3B200_TYPE_F16 || type == SAM3B200_TYPE_F32;
+    if (!quant && !dense) {
+        set_error("weight_upload: unsupported weight type %d (F32=0, F16=1, Q4_0=2, Q4_1=3, Q8_0=8)", type);
         return nullptr;
     }
-    if (ne0 <= 0 || ne1 <= 0 || ne0 % 32 != 0 || ne0 > (1 << 20) || ne1 > (1 << 24)) {
-        set_error("weight_upload: bad shape ne0=%lld ne1=%lld (ne0 must be a positive multiple of 32)",
-                  (long long)ne0, (long long)ne1);
+    if (ne0 <= 0 || ne1 <= 0 || ne0 > (1 << 20) || ne1 > (1 << 24) || (quant && ne0 % 32 != 0) ||
+        (dense && ne0 % 8 != 0)) {
+        set_error("weight_upload: bad shape ne0=%lld ne1=%lld (ne0 must be a positive multiple of %d)",
+                  (long long)ne0, (long long)ne1, quant ? 32 : 8);
         return nullptr;
     }
     cudaSetDevice(be->device);
     const int K = static_cast<int>(ne0), N = static_cast<int>(ne1);
-    const size_t block_bytes = type == SAM3B200_TYPE_Q8_0 ? 34 : 18;
-    const size_t raw_bytes = static_cast<size_t>(N) * (K / 32) * block_bytes;
     auto *w = new Weight();
     w->type = type;
     w->K = K;
     w->N = N;
     w->ld = (N + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
-    const size_t quad_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
     void *raw = nullptr;
-    bool ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
-              cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K), "cudaMalloc(weight codes)") &&
-              cuda_ok(cudaMalloc(&w->quads, quad_bytes), "cudaMalloc(weight scale quads)") &&
-              cuda_ok(cudaMemsetAsync(w->quads, 0, quad_bytes, be->stream), "memset scale quads") &&
-              cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyHostToDevice, be->stream),
-                      "weight upload") &&
-              cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->quads, w->ld, be->stream), "weight repack") &&
-              cuda_ok(cudaStreamSynchronize(be->stream), "weight upload sync");
+    bool ok;
+    if (dense) {
+        // F16 as is; F32 rounded to fp16 (the fp16 tensor-core GEMM computes both)
+        const size_t elems = static_cast<size_t>(N) * K;
+        ok = cuda_ok(cudaMalloc(&w->dense, elems * 2), "cudaMalloc(dense weight)");
+        if (ok && type == SAM3B200_TYPE_F16) {
+            ok = cuda_ok(cudaMemcpyAsync(w->dense, host_blocks, elems * 2, cudaMemcpyHostToDevice, be->stream),
+                         "weight upload");
+        } else if (ok) {
+            ok = cuda_ok(cudaMalloc(&raw, elems * 4), "cudaMalloc(weight staging)") &&
+                 cuda_ok(cudaMemcpyAsync(raw, host_blocks, elems * 4, cudaMemcpyHostToDevice, be->stream),
+                         "weight upload") &&
+                 cuda_ok(f32_rows_to_f16(static_cast<const float *>(raw), K, N, K, w->dense, be->stream), "to f16");
+        }
+        ok = ok && cuda_ok(cudaStreamSynchronize(be->stream), "weight upload sync");
+    } else {
+        const size_t block_bytes = type == SAM3B200_TYPE_Q8_0 ? 34 : type == SAM3B200_TYPE_Q4_0 ? 18 : 20;
+        const size_t raw_bytes = static_cast<size_t>(N) * (K / 32) * block_bytes;
+        const size_t quad_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
+        const size_t min_bytes = static_cast<size_t>(K / 32) * w->ld * 2;
+        ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
+             cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K), "cudaMalloc(weight codes)") &&
+             cuda_ok(cudaMalloc(&w->quads, quad_bytes), "cudaMalloc(weight scale quads)") &&
+             cuda_ok(cudaMemsetAsync(w->quads, 0, quad_bytes, be->stream), "memset scale quads") &&
+             (type != SAM3B200_TYPE_Q4_1 || (cuda_ok(cudaMalloc(&w->mins, min_bytes), "cudaMalloc(weight minima)") &&
+                                             cuda_ok(cudaMemsetAsync(w->mins, 0, min_bytes, be->stream), "memset"))) &&
+             cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyHostToDevice, be->stream),
+                     "weight upload") &&
+             cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->quads, w->ld, be->stream, w->mins),
+                     "weight repack") &&
+             cuda_ok(cudaStreamSynchronize(be->stream), "weight upload sync");
+    }
     if (raw) cudaFree(raw);
     if (!ok) {
         if (w->codes) cudaFree(w->codes);
         if (w->quads) cudaFree(w->quads);
+        if (w->mins) cudaFree(w->mins);
+        if (w->dense) cudaFree(w->dense);
         delete w;
         return nullptr;
     }
@@ -261,6 +289,8 @@ void sam3b200_weight_free(sam3b200_backend *h, sam3b200_weight *wh) {
     }
     cudaFree(w->codes);
     cudaFree(w->quads);
+    cudaFree(w->mins);
+    cudaFree(w->dense);
     delete w;
 }
 
@@ -288,10 +318,42 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     }
     cudaSetDevice(be->device);
     const int Mi = static_cast<int>(M);
+    if (w->dense) {
+        // F16 / F32 weights: x -> fp16 (ggml's vec_dot_type for F16), fp16 tensor-core GEMM, f32 out
+        if (dump) {
+            set_error("mul_mat_block_dots: weight type %d has no integer block dots", w->type);
+            return SAM3B200_STATUS_FAILED;
+        }
+        if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K * 2, 16)) return SAM3B200_STATUS_ALLOC_FAILED;
+        GemmF16Args g;
+        g.a = be->act_codes;
+        g.b = w->dense;
+        g.M = Mi;
+        g.N = w->N;
+        g.K = w->K;
+        g.bias = bias;
+        g.gelu = 0;
+        g.out_f16 = 0;
+        g.out = dst;
+        g.ldo = ldd;
+        g.store = GEMM_STORE_ROWMAJOR;
+        g.win = 0;
+        g.cout = 0;
+        g.err = be->err;
+        be->count(2);
+        be->prof_mark(0);
+        const bool ok = cuda_ok(f32_rows_to_f16(x, ldx, Mi, w->K, be->act_codes, be->stream), "x to f16") &&
+                        cuda_ok(gemm_f16(g, be->num_sms, be->stream), "mul_mat f16 gemm");
+        be->prof_mark(0);
+        return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+    }
     const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
-    if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K, static_cast<size_t>(w->K / 32) * lda * 16))
+    const size_t quad_bytes = static_cast<size_t>(w->K / 32) * lda * 16;
+    const bool q41 = w->type == SAM3B200_TYPE_Q4_1;  // Q8_1 activations: the sum fields follow the scales
+    if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K, q41 ? 2 * quad_bytes : quad_bytes))
         return SAM3B200_STATUS_ALLOC_FAILED;
-    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_quads, lda, be->stream),
+    void *sums = q41 ? static_cast<char *>(be->act_quads) + quad_bytes : nullptr;
+    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_quads, lda, be->stream, sums),
                  "quantize activations"))
         return SAM3B200_STATUS_FAILED;
     MmqArgs a;
@@ -302,9 +364,12 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     a.ldy = ldd;
     a.dump = dump;
     a.err = be->err;
+    a.b_mins = w->mins;
+    a.a_sums = sums;
     const int mode = dump ? MMQ_OUT_BLOCKDOTS : MMQ_OUT_F32;
     int impl = be->mmq_impl;
     if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
+    if (q41) impl = SAM3B200_MMQ_SIMT;  // the m_w * s_x term exists only in the SIMT kernel
     cudaError_t e;
     be->count(2);
     be->prof_mark(0);

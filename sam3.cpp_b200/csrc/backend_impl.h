@@ -43,6 +43,8 @@ struct Weight {
     int ld = 0;    // scale-quad rows per block (N rounded up to 128)
     void *codes = nullptr;
     void *quads = nullptr;
+    void *mins = nullptr;   // Q4_1: fp16 block minima [K/32][ld]
+    void *dense = nullptr;  // F16 / F32 weights: fp16 [N][K] for the fp16 tensor-core GEMM
 };
 
 void set_error(const char *fmt, ...);

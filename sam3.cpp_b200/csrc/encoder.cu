@@ -630,7 +630,8 @@ int sam3b200_vit_output(sam3b200_vit *hv, int i, const float **dev, int64_t *ne)
     return SAM3B200_STATUS_SUCCESS;
 }
 
-int sam3b200_preprocess(sam3b200_backend *hb, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev) {
+static int preprocess_common(sam3b200_backend *hb, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev,
+                             bool sam2) {
     auto *be = reinterpret_cast<Backend *>(hb);
     if (!be || !rgb_dev || !out_dev || w <= 0 || h <= 0 || img <= 0) {
         set_error("preprocess: bad argument");
@@ -646,9 +647,19 @@ int sam3b200_preprocess(sam3b200_backend *hb, const uint8_t *rgb_dev, int w, int
             return SAM3B200_STATUS_FAILED;
         src = tmp;
     }
-    const bool ok = cuda_ok(preprocess_sam3(src, img, out_dev, be->stream), "preprocess");
+    const bool ok = cuda_ok(sam2 ? preprocess_sam2(src, img, out_dev, be->stream)
+                                 : preprocess_sam3(src, img, out_dev, be->stream),
+                            "preprocess");
     if (tmp) cudaFreeAsync(tmp, be->stream);
     return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_preprocess(sam3b200_backend *hb, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev) {
+    return preprocess_common(hb, rgb_dev, w, h, img, out_dev, false);
+}
+
+int sam3b200_preprocess_sam2(sam3b200_backend *hb, const uint8_t *rgb_dev, int w, int h, int img, float *out_dev) {
+    return preprocess_common(hb, rgb_dev, w, h, img, out_dev, true);
 }
 
 int sam3b200_vit_run_prefix(sam3b200_vit *hv, const float *img_chw_dev, float *x_dev) {

@@ -41,7 +41,8 @@ __device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
 
 template <bool VEC>
 __global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
-                                        int8_t *__restrict__ codes, __half *__restrict__ quads, int ld) {
+                                        int8_t *__restrict__ codes, __half *__restrict__ quads,
+                                        __half *__restrict__ sums, int ld) {
     const int per_row = K >> 3;  // threads per row
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const bool active = t < static_cast<int64_t>(M) * per_row;
@@ -69,20 +70,28 @@ __global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx
     // the 4 threads of a block are consecutive lanes (K % 32 == 0)
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    if (!active) return;
     const float d = __fdiv_rn(amax, 127.f);
     const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-    int q[8];
+    int q[8], qsum = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = __float2int_rn(__fmul_rn(v[i], id));
+    for (int i = 0; i < 8; ++i) {
+        q[i] = __float2int_rn(__fmul_rn(v[i], id));
+        qsum += q[i];
+    }
+    // Q8_1 sum field: s = d * sum(q) in fp32 (d unrounded), stored as fp16
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+    if (!active) return;
     *reinterpret_cast<uint2 *>(codes + static_cast<int64_t>(m) * K + e) =
         make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
-    if ((e & 31) == 0)
+    if ((e & 31) == 0) {
         quads[act_quad_index(e >> 5, m, ld)] = __float2half_rn(d);
+        if (sums) sums[act_quad_index(e >> 5, m, ld)] = __float2half_rn(__fmul_rn(d, static_cast<float>(qsum)));
+    }
 }
 
 cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
-                             cudaStream_t s) {
+                             cudaStream_t s, void *sums) {
     if (K % 32 != 0 || M < 0 || ld < M) return cudaErrorInvalidValue;
     if (M == 0) return cudaSuccess;
     const int64_t threads_total = static_cast<int64_t>(M) * (K / 8);
@@ -91,10 +100,12 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
     const bool vec = (ldx % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     if (vec)
         quantize_rows_q8_kernel<true><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
-                                                                 static_cast<__half *>(quads), ld);
+                                                                 static_cast<__half *>(quads),
+                                                                 static_cast<__half *>(sums), ld);
     else
         quantize_rows_q8_kernel<false><<<blocks, threads, 0, s>>>(x, ldx, M, K, static_cast<int8_t *>(codes),
-                                                                  static_cast<__half *>(quads), ld);
+                                                                  static_cast<__half *>(quads),
+                                                                  static_cast<__half *>(sums), ld);
     return cudaGetLastError();
 }
 
@@ -102,7 +113,8 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 // Weight repack: ggml blocks -> int8 codes + scale quads.
 // ---------------------------------------------------------------------------
 __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ blocks, int N, int K,
-                                     int8_t *__restrict__ codes, uint4 *__restrict__ quads, int ld) {
+                                     int8_t *__restrict__ codes, uint4 *__restrict__ quads, __half *__restrict__ mins,
+                                     int ld) {
     const int nblk = K >> 5;
     const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -114,10 +126,15 @@ __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ block
     if (type == 8) {  // Q8_0 {fp16 d; int8 qs[32]}
         blk = blocks + w * 34;
         code = static_cast<int8_t>(blk[2 + lane]);
-    } else {          // Q4_0 {fp16 d; uint8 qs[16]}: low nibbles 0..15, high 16..31
+    } else if (type == 2) {  // Q4_0 {fp16 d; uint8 qs[16]}: low nibbles 0..15, high 16..31
         blk = blocks + w * 18;
         const uint8_t byte = blk[2 + (lane & 15)];
         code = (lane < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
+    } else {                 // Q4_1 {fp16 d; fp16 m; uint8 qs[16]}: code = nibble, value = d * code + m
+        blk = blocks + w * 20;
+        const uint8_t byte = blk[4 + (lane & 15)];
+        code = lane < 16 ? (byte & 0x0F) : (byte >> 4);
+        if (lane == 0) mins[static_cast<int64_t>(b) * ld + n] = __half(__half_raw{static_cast<unsigned short>(blk[2] | (blk[3] << 8))});
     }
     codes[static_cast<int64_t>(n) * K + b * 32 + lane] = static_cast<int8_t>(code);
     if (lane == 0) {
@@ -129,13 +146,15 @@ __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ block
 }
 
 cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
-                                 cudaStream_t s) {
-    if (K % 32 != 0 || N <= 0 || ld < N || (type != 8 && type != 2)) return cudaErrorInvalidValue;
+                                 cudaStream_t s, void *mins) {
+    if (K % 32 != 0 || N <= 0 || ld < N || (type != 8 && type != 2 && type != 3) || (type == 3 && !mins))
+        return cudaErrorInvalidValue;
     const int64_t warps = static_cast<int64_t>(N) * (K / 32);
     const int threads = 256;
     const unsigned grid = static_cast<unsigned>((warps * 32 + threads - 1) / threads);
     repack_weight_kernel<<<grid, threads, 0, s>>>(type, static_cast<const uint8_t *>(blocks), N, K,
-                                                  static_cast<int8_t *>(codes), static_cast<uint4 *>(quads), ld);
+                                                  static_cast<int8_t *>(codes), static_cast<uint4 *>(quads),
+                                                  static_cast<__half *>(mins), ld);
     return cudaGetLastError();
 }
 
@@ -663,7 +682,7 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
 }
 
 cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt, int bn) {
-    if (!valid_args(a) || num_sms <= 0) return cudaErrorInvalidValue;
+    if (!valid_args(a) || num_sms <= 0 || a.b_mins) return cudaErrorInvalidValue;  // Q4_1: SIMT path only
     if (bn == 64) return dispatch_tc<64>(a, mode, num_sms, s, cvt);
     if (bn == 128) return dispatch_tc<128>(a, mode, num_sms, s, cvt);
     return cudaErrorInvalidValue;
@@ -675,7 +694,8 @@ cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int 
 __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__restrict__ qa, int lda_q,
                                 const int8_t *__restrict__ cb, const uint4 *__restrict__ qb, int ldb_q, int M, int N,
                                 int K, const float *__restrict__ bias, float *__restrict__ y, int64_t ldy,
-                                int32_t *__restrict__ dump, int mode) {
+                                int32_t *__restrict__ dump, int mode, const __half *__restrict__ mins_b,
+                                const __half *__restrict__ sums_a) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int m = blockIdx.y;
     if (n >= N || m >= M) return;
@@ -692,19 +712,23 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
             const float dx = __half2float(reinterpret_cast<const __half *>(qa)[act_quad_index(b, m, lda_q)]);
             const float dw = __half2float(reinterpret_cast<const __half *>(qb)[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]);
             acc = fmaf(static_cast<float>(isum), dx * dw, acc);
+            if (mins_b)  // Q4_1 x Q8_1: + m_w * s_x per block (ggml vec_dot_q4_1_q8_1)
+                acc = fmaf(__half2float(mins_b[static_cast<int64_t>(b) * ldb_q + n]),
+                           __half2float(sums_a[act_quad_index(b, m, lda_q)]), acc);
         }
     }
     if (mode == MMQ_OUT_F32) y[static_cast<int64_t>(m) * ldy + n] = bias ? acc + bias[n] : acc;
 }
 
 cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
-    if (!valid_args(a) || a.a.rows > 65535) return cudaErrorInvalidValue;
+    if (!valid_args(a) || a.a.rows > 65535 || (a.b_mins && !a.a_sums)) return cudaErrorInvalidValue;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
     dim3 grid((N + 127) / 128, M);
     mmq_simt_kernel<<<grid, 128, 0, s>>>(static_cast<const int8_t *>(a.a.codes), static_cast<const uint4 *>(a.a.quads),
                                          a.a.ld, static_cast<const int8_t *>(a.b.codes),
                                          static_cast<const uint4 *>(a.b.quads), a.b.ld, M, N, K, a.bias, a.y, a.ldy,
-                                         a.dump, mode);
+                                         a.dump, mode, static_cast<const __half *>(a.b_mins),
+                                         static_cast<const __half *>(a.a_sums));
     return cudaGetLastError();
 }
 

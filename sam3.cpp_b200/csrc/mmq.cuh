@@ -67,17 +67,22 @@ struct MmqArgs {
     const float *freqs = nullptr;   // MMQ_OUT_QKV: RoPE table [win_tokens][32][2] (cos, sin), or null
     int win_tokens = 0;             // MMQ_OUT_QKV: tokens per window
     int heads = 0;                  // MMQ_OUT_QKV: heads (N = 3 * 64 * heads)
+    const void *b_mins = nullptr;   // Q4_1 weights: fp16 m_w [K/32][ld] (SIMT path)
+    const void *a_sums = nullptr;   // Q4_1 weights: Q8_1 sum fields of the activations (act_quad_index layout)
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.
 // quads must hold ceil(K/256) * ld records; rows >= M are left untouched.
+// sums (optional): the Q8_1 sum fields s = fp16(d * sum(q)) in the quads'
+// element layout (act_quad_index), for Q4_1 weights.
 cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *codes, void *quads, int ld,
-                             cudaStream_t s);
+                             cudaStream_t s, void *sums = nullptr);
 
 // Repack ggml weight blocks (N rows of K) into the device layout.
-// type: 8 = Q8_0, 2 = Q4_0.  Returns cudaErrorInvalidValue otherwise.
+// type: 8 = Q8_0, 2 = Q4_0, 3 = Q4_1 (codes = nibbles 0..15, block minima to
+// `mins`, fp16 [K/32][ld]).  Returns cudaErrorInvalidValue otherwise.
 cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
-                                 cudaStream_t s);
+                                 cudaStream_t s, void *mins = nullptr);
 
 // tcgen05 tensor-core MMQ, tile 128 x bn (bn = 64 or 128).  cvt selects the
 // epilogue's exact int32 -> fp32 conversion: 0 = cvt instruction, 1 =

@@ -62,6 +62,10 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
         set_error("mul_mat_noalloc: null argument");
         return SAM3B200_STATUS_FAILED;
     }
+    if (w->dense || w->mins) {
+        set_error("mul_mat_noalloc: weight type %d is not supported (Q8_0 and Q4_0 only)", w->type);
+        return SAM3B200_STATUS_FAILED;
+    }
     if (M <= 0 || M > (1 << 24) || ldx < w->K || ldd < w->N) {
         set_error("mul_mat_noalloc: bad shape M=%lld ldx=%lld ldd=%lld for K=%d N=%d", (long long)M, (long long)ldx,
                   (long long)ldd, w->K, w->N);

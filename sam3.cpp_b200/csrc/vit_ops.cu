@@ -12,21 +12,36 @@ namespace b200 {
 static inline unsigned grid_for(int64_t n, int threads) { return static_cast<unsigned>((n + threads - 1) / threads); }
 
 // ---- preprocessing -----------------------------------------------------------
-__global__ void preprocess_kernel(const uint8_t *__restrict__ rgb, int img, float *__restrict__ out) {
+// (p / 255 - mean[c]) / std[c] per channel, every step rounded as the
+// reference's float expression is
+struct ChannelNorm {
+    float mean[3], std[3];
+};
+
+__global__ void preprocess_kernel(const uint8_t *__restrict__ rgb, int img, const ChannelNorm nrm,
+                                  float *__restrict__ out) {
     const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t plane = static_cast<int64_t>(img) * img;
     if (p >= plane) return;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
         const float v = __fdiv_rn(static_cast<float>(rgb[p * 3 + c]), 255.0f);
-        out[c * plane + p] = __fdiv_rn(__fsub_rn(v, 0.5f), 0.5f);
+        out[c * plane + p] = __fdiv_rn(__fsub_rn(v, nrm.mean[c]), nrm.std[c]);
     }
 }
 
-cudaError_t preprocess_sam3(const uint8_t *rgb, int img, float *out, cudaStream_t s) {
+static cudaError_t preprocess_norm(const uint8_t *rgb, int img, const ChannelNorm &nrm, float *out, cudaStream_t s) {
     if (img <= 0) return cudaErrorInvalidValue;
-    preprocess_kernel<<<grid_for(static_cast<int64_t>(img) * img, 256), 256, 0, s>>>(rgb, img, out);
+    preprocess_kernel<<<grid_for(static_cast<int64_t>(img) * img, 256), 256, 0, s>>>(rgb, img, nrm, out);
     return cudaGetLastError();
+}
+
+cudaError_t preprocess_sam3(const uint8_t *rgb, int img, float *out, cudaStream_t s) {
+    return preprocess_norm(rgb, img, ChannelNorm{{0.5f, 0.5f, 0.5f}, {0.5f, 0.5f, 0.5f}}, out, s);
+}
+
+cudaError_t preprocess_sam2(const uint8_t *rgb, int img, float *out, cudaStream_t s) {
+    return preprocess_norm(rgb, img, ChannelNorm{{0.485f, 0.456f, 0.406f}, {0.229f, 0.224f, 0.225f}}, out, s);
 }
 
 __global__ void resize_kernel(const uint8_t *__restrict__ src, int sw, int sh, uint8_t *__restrict__ dst, int dw,
@@ -336,6 +351,21 @@ __global__ void f32_to_f16_kernel(const float4 *__restrict__ x, int64_t n4, uint
     const float4 v = x[i];
     __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
     y[i] = make_uint2(*reinterpret_cast<uint32_t *>(&a), *reinterpret_cast<uint32_t *>(&b));
+}
+
+__global__ void f32_rows_to_f16_kernel(const float *__restrict__ x, int64_t ldx, int M, int K,
+                                       __half *__restrict__ y) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(M) * K) return;
+    const int64_t m = i / K, k = i % K;
+    y[i] = __float2half_rn(x[m * ldx + k]);
+}
+
+cudaError_t f32_rows_to_f16(const float *x, int64_t ldx, int M, int K, void *y, cudaStream_t s) {
+    if (M <= 0 || K <= 0 || ldx < K) return cudaErrorInvalidValue;
+    f32_rows_to_f16_kernel<<<grid_for(static_cast<int64_t>(M) * K, 256), 256, 0, s>>>(x, ldx, M, K,
+                                                                                      static_cast<__half *>(y));
+    return cudaGetLastError();
 }
 
 cudaError_t f32_to_f16(const float *x, int64_t n, void *y, cudaStream_t s) {

@@ -12,6 +12,10 @@ namespace b200 {
 // f32 CHW (p/255 - 0.5)/0.5.  Inputs of another size go through
 // resize_bilinear_u8 first (sam3.cpp:3445-3485, double precision).
 cudaError_t preprocess_sam3(const uint8_t *rgb, int img, float *out_chw, cudaStream_t s);
+
+// sam2_preprocess_image (sam3.cpp:3522-3548): the same layout with the
+// ImageNet normalisation, mean (0.485, 0.456, 0.406), std (0.229, 0.224, 0.225).
+cudaError_t preprocess_sam2(const uint8_t *rgb, int img, float *out_chw, cudaStream_t s);
 cudaError_t resize_bilinear_u8(const uint8_t *src, int sw, int sh, uint8_t *dst, int dw, int dh, cudaStream_t s);
 
 // im2col of the 14x14 stride-14 patch embedding (ggml_conv_2d_sk_p0,
@@ -33,6 +37,10 @@ cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const 
 cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s);
 
 cudaError_t f32_to_f16(const float *x, int64_t n, void *y, cudaStream_t s);
+
+// Rows [0, M) of an f32 matrix with row stride ldx -> dense fp16 [M][K]
+// (round to nearest even, as ggml_fp32_to_fp16).
+cudaError_t f32_rows_to_f16(const float *x, int64_t ldx, int M, int K, void *y, cudaStream_t s);
 
 // 2x2 stride-2 max pool of an HWC f32 map (G x G x C) -> fp16 (G/2)^2 x C.
 cudaError_t maxpool2x2_f16(const float *x, int G, int C, void *y, cudaStream_t s);

@@ -1,5 +1,6 @@
-"""GPU parity of the MUL_MAT path (ggml_mul_mat with Q8_0 / Q4_0 weights,
-sam3.cpp:3742,3783,3796,3799) against the CPU oracle, through the C ABI.
+"""GPU parity of the MUL_MAT path (ggml_mul_mat with Q8_0 / Q4_0 / Q4_1 / F16 /
+F32 weights, sam3.cpp:3742,3783,3796,3799) against the CPU oracle, through the
+C ABI.
 
 Bar (stated per test):
   * int32 block dots: bit-exact (the MMA path's own dots, dumped);
@@ -104,8 +105,48 @@ def test_vit_shapes_sampled_rows(oracle, b200, backend, K, N):
 
 
 def test_bad_weight_type_is_rejected(b200, backend):
-    blocks = np.zeros(20, np.uint8)
+    blocks = np.zeros(64, np.uint8)
     with pytest.raises(b200.B200Error):
-        backend.weight(3, blocks, 32, 1)   # Q4_1 is not wired into the MMQ yet
+        backend.weight(6, blocks, 32, 1)   # ggml Q5_0: not a sam3.cpp weight type
     with pytest.raises(b200.B200Error):
         backend.weight(8, blocks, 48, 1)   # K not a multiple of 32
+    with pytest.raises(b200.B200Error):
+        backend.weight(1, blocks, 12, 1)   # F16 rows must be a multiple of 8 (16-byte TMA pitch)
+
+
+@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (37, 96, 136), (1, 32, 8)])
+def test_q4_1_bit_exact(oracle, b200, backend, M, K, N):
+    """Q4_1 weights x Q8_1 activations (ggml vec_dot_q4_1_q8_1): block dots of the nibble codes and the
+    f32 output, whose per-block sum is fma(I, d_w d_x, acc) then fma(m_w, s_x, acc), bit-exact."""
+    wq, x, bias = _case(oracle, 3, M, K, N, seed=M + 11 * K + N)
+    w = backend.weight(3, wq, K, N)
+    dx, db = backend.upload(x), backend.upload(bias)
+    dots = backend.mul_mat_block_dots(w, dx, M)
+    y = backend.alloc(M * N * 4)
+    backend.mul_mat(w, dx, M, y, bias=db)
+    backend.synchronize()
+    assert np.array_equal(dots, oracle.block_dots(3, wq, K, N, x))
+    assert np.array_equal(y.get((M, N), np.float32), oracle.mul_mat(3, wq, K, N, x) + bias[None, :])
+    w.free()
+
+
+@pytest.mark.parametrize("qt", [1, 0])
+@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (37, 96, 136), (5184, 1024, 1024)])
+def test_dense_weights_within_bound(oracle, b200, backend, qt, M, K, N):
+    """F16 weights (x rounded to fp16 as ggml's vec_dot_type) and F32 weights (stored as fp16 here) on the
+    fp16 tensor-core GEMM: max|d| / max|ref| <= 1e-2 against the oracle's fp32 dots."""
+    rng = np.random.default_rng(M + K + N + qt)
+    w = rng.normal(0, 0.02, size=(N, K)).astype(np.float32)
+    x = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+    bias = rng.normal(0, 0.02, size=(N,)).astype(np.float32)
+    blocks = w.astype(np.float16) if qt == 1 else w
+    wt = backend.weight(qt, blocks, K, N)
+    dx, db, y = backend.upload(x), backend.upload(bias), backend.alloc(M * N * 4)
+    backend.mul_mat(wt, dx, M, y, bias=db)
+    backend.synchronize()
+    got = y.get((M, N), np.float32)
+    rows = np.arange(0, M, max(1, M // 200))
+    ref = oracle.mul_mat(qt, np.ascontiguousarray(blocks).view(np.uint8), K, N, x[rows]) + bias[None, :]
+    err = np.abs(got[rows] - ref).max() / np.abs(ref).max()
+    assert err <= 1e-2, err
+    wt.free()

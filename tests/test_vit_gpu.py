@@ -36,6 +36,19 @@ def test_preprocess_bit_exact(model, oracle, backend, small, w, h):
     assert np.array_equal(got, ov.preprocess(rgb))
 
 
+@pytest.mark.parametrize("w,h,img", [(1024, 1024, 1024), (640, 480, 1024), (300, 900, 512)])
+def test_preprocess_sam2_bit_exact(oracle, backend, small, w, h, img):
+    """sam2_preprocess_image (sam3.cpp:3522-3548): ImageNet normalisation, same resize."""
+    _, _, _, ov = small
+    rgb = np.random.default_rng(7 * w + h).integers(0, 256, size=(h, w, 3), dtype=np.uint8)
+    src = backend.upload(rgb)
+    out = backend.alloc(3 * img * img * 4)
+    backend.preprocess_sam2(src, w, h, img, out)
+    backend.synchronize()
+    got = out.get((3, img, img), np.float32)
+    assert np.array_equal(got, ov.preprocess_sam2(rgb, img))
+
+
 def test_prefix(backend, small):
     hp, _, vit, ov = small
     img = ov.preprocess(np.random.default_rng(3).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8))
