@@ -136,6 +136,18 @@ int sam3b200_mul_mat_noalloc(sam3b200_backend *be, const sam3b200_weight *w, con
 /* Select the MUL_MAT kernel (SAM3B200_MMQ_*); returns the previous one. */
 int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
 
+/* GGML_OP_FLASH_ATTN_EXT as the ViT blocks use it (sam3.cpp:3778: no mask,
+ * max_bias 0, logit softcap 0): dst = softmax(q k^T * scale) v per (head,
+ * batch).  q, k, v: device f32 ggml tensors [D, N, heads, batch], contiguous
+ * (memory [batch][heads][N][D]); dst: device f32 [D, heads, N, batch]
+ * (memory [batch][N][heads][D]), the layout ggml_flash_attn_ext returns.
+ * Supported: D == 64, N a multiple of 8, self-attention (same N for q and
+ * k/v); other shapes fail with an error message.  Computed on the tensor
+ * cores with bf16 q, k, v and fp32 softmax/accumulation (within 1e-2 of the
+ * f32 reference).  Asynchronous on the backend stream. */
+int sam3b200_flash_attn_ext(sam3b200_backend *be, const float *q, const float *k, const float *v, int64_t D,
+                            int64_t N, int64_t heads, int64_t batch, float scale, float *dst);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

@@ -120,6 +120,17 @@ def block_dots(qtype: int, wq: np.ndarray, K: int, N: int, x: np.ndarray, n_thre
     return out
 
 
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, batch: int, N: int, heads: int, scale: float,
+              n_threads: int = 0) -> np.ndarray:
+    """ggml_flash_attn_ext in f32 (vit_oracle.c orc_attention): q, k, v [batch*heads][N][64] (ggml
+    [64, N, heads, batch]) -> [batch*N][heads*64] (ggml [64, heads, N, batch])."""
+    q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+    out = np.empty((batch * N, heads * 64), np.float32)
+    _vit_lib().orc_attention(q.ctypes.data, k.ctypes.data, v.ctypes.data, batch, N, heads, scale, out.ctypes.data,
+                             n_threads or (os.cpu_count() or 1))
+    return out
+
+
 # ---- SAM3 visual encoder restatement (vit_oracle.h) ------------------------
 
 class _Hp(ctypes.Structure):

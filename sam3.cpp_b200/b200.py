@@ -76,6 +76,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_vit_run_neck": (i32, [vp, vp]),
         "sam3b200_preprocess": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_preprocess_sam2": (i32, [vp, vp, i32, i32, i32, vp]),
+        "sam3b200_flash_attn_ext": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, ctypes.c_float, vp]),
         "sam3b200_backend_launch_count": (ctypes.c_longlong, [vp]),
         "sam3b200_backend_profile": (i32, [vp, i32]),
         "sam3b200_backend_profile_read": (i32, [vp, i32, ctypes.POINTER(ctypes.c_double),
@@ -282,6 +283,12 @@ class Backend:
 
     def preprocess(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
         _check(lib().sam3b200_preprocess(self.h, rgb_dev.ptr, w, h, img, out.ptr), "preprocess")
+
+    def flash_attn_ext(self, q: DeviceBuffer, k: DeviceBuffer, v: DeviceBuffer, D: int, N: int, heads: int,
+                       batch: int, scale: float, dst: DeviceBuffer) -> None:
+        """GGML_OP_FLASH_ATTN_EXT (sam3.cpp:3778): f32 [D, N, heads, batch] in, [D, heads, N, batch] out."""
+        _check(lib().sam3b200_flash_attn_ext(self.h, q.ptr, k.ptr, v.ptr, D, N, heads, batch, scale, dst.ptr),
+               "flash_attn_ext")
 
     def preprocess_sam2(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
         """sam2_preprocess_image: ImageNet-normalised CHW (sam3.cpp:3522-3548)."""

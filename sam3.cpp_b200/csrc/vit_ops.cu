@@ -330,6 +330,61 @@ cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const 
     return cudaGetLastError();
 }
 
+// ---- attention inputs from ggml f32 tensors ----------------------------------
+// Q, K, V f32 [BH][N][64] (ggml [64, N, H, B]) -> bf16 Q, K in the same layout
+// and bf16 V^T [BH][64][N]; one CTA per (64-token tile, bh), V through a
+// shared-memory transpose.
+__global__ void __launch_bounds__(256) attn_inputs_kernel(const float *__restrict__ q, const float *__restrict__ k,
+                                                          const float *__restrict__ v, int N,
+                                                          __nv_bfloat16 *__restrict__ qb, __nv_bfloat16 *__restrict__ kb,
+                                                          __nv_bfloat16 *__restrict__ vt) {
+    __shared__ __nv_bfloat16 vs[64][64 + 8];  // [dim][token]
+    const int64_t bh = blockIdx.y;
+    const int t0 = blockIdx.x * 64;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int item = it * 256 + threadIdx.x;  // (token, dim pair)
+        const int tl = item >> 5, pr = item & 31, n = t0 + tl;
+        if (n < N) {
+            const int64_t o = (bh * N + n) * 64 + 2 * pr;
+            const float2 qq = *reinterpret_cast<const float2 *>(q + o);
+            const float2 kk = *reinterpret_cast<const float2 *>(k + o);
+            const float2 vv = *reinterpret_cast<const float2 *>(v + o);
+            *reinterpret_cast<__nv_bfloat162 *>(qb + o) = __floats2bfloat162_rn(qq.x, qq.y);
+            *reinterpret_cast<__nv_bfloat162 *>(kb + o) = __floats2bfloat162_rn(kk.x, kk.y);
+            vs[2 * pr][tl] = __float2bfloat16_rn(vv.x);
+            vs[2 * pr + 1][tl] = __float2bfloat16_rn(vv.y);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int item = it * 256 + threadIdx.x;  // (dim, 8-token chunk); N % 8 == 0 keeps 16-byte stores aligned
+        const int d = item >> 3, ch = item & 7, n = t0 + ch * 8;
+        if (n < N) {
+            uint4 w;
+            uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 pair;
+                pair.x = vs[d][ch * 8 + 2 * e];
+                pair.y = vs[d][ch * 8 + 2 * e + 1];
+                wp[e] = *reinterpret_cast<uint32_t *>(&pair);
+            }
+            *reinterpret_cast<uint4 *>(vt + (bh * 64 + d) * N + n) = w;
+        }
+    }
+}
+
+cudaError_t attn_inputs_from_f32(const float *q, const float *k, const float *v, int BH, int N, void *qb, void *kb,
+                                 void *vt, cudaStream_t s) {
+    if (BH <= 0 || N <= 0 || N % 8 != 0) return cudaErrorInvalidValue;
+    dim3 grid((N + 63) / 64, BH);
+    attn_inputs_kernel<<<grid, 256, 0, s>>>(q, k, v, N, static_cast<__nv_bfloat16 *>(qb),
+                                            static_cast<__nv_bfloat16 *>(kb), static_cast<__nv_bfloat16 *>(vt));
+    return cudaGetLastError();
+}
+
 __global__ void rowmap_kernel(int G, int win, int *__restrict__ rowmap) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= G * G) return;

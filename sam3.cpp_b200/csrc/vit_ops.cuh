@@ -33,6 +33,11 @@ cudaError_t add_pos_layernorm(const float *conv, const float *pos, int g, int G,
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s);
 
+// Attention inputs from ggml f32 tensors Q, K, V [64, N, H, B] (contiguous:
+// [BH][N][64]) -> bf16 Q, K (same layout) and V^T [BH][64][N].  N % 8 == 0.
+cudaError_t attn_inputs_from_f32(const float *q, const float *k, const float *v, int BH, int N, void *qb, void *kb,
+                                 void *vt, cudaStream_t s);
+
 // Row map of ggml_win_unpart: windowed row -> token row (G x G grid).
 cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s);
 
