@@ -148,6 +148,36 @@ int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
 int sam3b200_flash_attn_ext(sam3b200_backend *be, const float *q, const float *k, const float *v, int64_t D,
                             int64_t N, int64_t heads, int64_t batch, float scale, float *dst);
 
+/* GGML_OP_CONV_TRANSPOSE_2D as ggml_conv_transpose_2d_p0 builds it
+ * (sam3.cpp:3884,3887,3898 neck; :10654,10673 mask decoder): no padding, any
+ * stride.  w: device ggml F16 kernel [KW, KH, OC, IC] (memory
+ * [ic][oc][ky][kx]); x: device f32 [IW, IH, IC, 1] (memory [ic][iy][ix]);
+ * dst: device f32 [OW, OH, OC, 1], OW = (IW-1)*stride + KW, OH likewise.
+ * x is rounded to fp16 as ggml's CPU path does; products are summed in fp32
+ * on the tensor cores.  Asynchronous on the backend stream (allocates its
+ * scratch from the stream-ordered pool). */
+int sam3b200_conv_transpose_2d(sam3b200_backend *be, const void *w_f16, const float *x, int64_t iw, int64_t ih,
+                               int64_t ic, int64_t oc, int64_t kw, int64_t kh, int stride, float *dst);
+
+/* GGML_OP_CONV_2D: ggml_conv_2d(kernel, input, s0, s1, p0, p1, d0, d1) and its
+ * _sk_p0 / _s1_ph forms (sam3.cpp:3819 patch embedding, :3889-3921 neck,
+ * :4474 Hiera patch embedding, :11541 memory-encoder downsampling).
+ * w: device ggml F16 kernel [KW, KH, IC, OC] (memory [oc][ic][ky][kx]);
+ * x: device f32 [IW, IH, IC, 1]; dst: device f32 [OW, OH, OC, 1] with
+ * OW = (IW + 2*p0 - d0*(KW-1) - 1)/s0 + 1 (OH likewise).  im2col in fp16 as
+ * ggml's CPU path, fp32 accumulation on the tensor cores.  Asynchronous. */
+int sam3b200_conv_2d(sam3b200_backend *be, const void *w_f16, const float *x, int64_t iw, int64_t ih, int64_t ic,
+                     int64_t oc, int64_t kw, int64_t kh, int s0, int s1, int p0, int p1, int d0, int d1, float *dst);
+
+/* GGML_OP_GET_ROWS (ggml_get_rows: the text encoder's token-embedding
+ * lookup, sam3.cpp:3927-4068): dst[i][:] = row idx[i] of src, dequantised to
+ * f32 by ggml's rules (F32, F16, Q4_0, Q4_1, Q8_0).  src: device rows of
+ * ncols elements in the ggml block format of `type`; idx: device int32 [n];
+ * dst: device f32 [n][ncols].  An index outside [0, nrows) yields a zero row
+ * and makes the next sam3b200_backend_synchronize fail.  Asynchronous. */
+int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t ncols, int64_t nrows,
+                      const int32_t *idx, int64_t n, float *dst);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

@@ -131,6 +131,56 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, batch: int, N: int, h
     return out
 
 
+def conv_transpose_2d(w: np.ndarray, x: np.ndarray, stride: int) -> np.ndarray:
+    """ggml_conv_transpose_2d_p0 (sam3.cpp:3884; ggml op GGML_OP_CONV_TRANSPOSE_2D) in float64.
+
+    w: fp16 [ic][oc][kh][kw] (ggml [KW, KH, OC, IC]); x: f32 [ic][ih][iw].  As ggml's CPU path, the
+    input is rounded to fp16 before the products; out[oc][oy][ox] sums x[ic][iy][ix] * w[ic][oc][ky][kx]
+    over oy = stride*iy + ky, ox = stride*ix + kx (no padding).  Returns f32 [oc][oh][ow]."""
+    ic, oc, kh, kw = w.shape
+    _, ih, iw = x.shape
+    xs = x.astype(np.float16).astype(np.float64).reshape(ic, ih * iw)
+    wd = w.astype(np.float64)
+    oh, ow = (ih - 1) * stride + kh, (iw - 1) * stride + kw
+    out = np.zeros((oc, oh, ow), np.float64)
+    for ky in range(kh):
+        for kx in range(kw):
+            t = (wd[:, :, ky, kx].T @ xs).reshape(oc, ih, iw)
+            out[:, ky:ky + stride * (ih - 1) + 1:stride, kx:kx + stride * (iw - 1) + 1:stride] += t
+    return out.astype(np.float32)
+
+
+def conv_2d(w: np.ndarray, x: np.ndarray, s0: int, s1: int, p0: int, p1: int, d0: int = 1, d1: int = 1) -> np.ndarray:
+    """ggml_conv_2d (sam3.cpp:3819, 3891, 4474; ggml im2col + mul_mat) in float64.
+
+    w: fp16 [oc][ic][kh][kw] (ggml [KW, KH, IC, OC]); x: f32 [ic][ih][iw], rounded to fp16 as ggml's
+    im2col does for an F16 kernel; zero padding p0/p1, strides s0/s1, dilations d0/d1 (x then y).
+    Returns f32 [oc][oh][ow]."""
+    oc, ic, kh, kw = w.shape
+    _, ih, iw = x.shape
+    ow = (iw + 2 * p0 - d0 * (kw - 1) - 1) // s0 + 1
+    oh = (ih + 2 * p1 - d1 * (kh - 1) - 1) // s1 + 1
+    xp = np.zeros((ic, ih + 2 * p1 + s1 * oh, iw + 2 * p0 + s0 * ow), np.float64)
+    xp[:, p1:p1 + ih, p0:p0 + iw] = x.astype(np.float16).astype(np.float64)
+    wd = w.astype(np.float64)
+    out = np.zeros((oc, oh * ow), np.float64)
+    for ky in range(kh):
+        for kx in range(kw):
+            y0, x0 = ky * d1, kx * d0
+            patch = xp[:, y0:y0 + s1 * oh:s1, x0:x0 + s0 * ow:s0].reshape(ic, oh * ow)
+            out += wd[:, :, ky, kx] @ patch
+    return out.reshape(oc, oh, ow).astype(np.float32)
+
+
+def get_rows(qtype: int, rows: np.ndarray, ncols: int, idx: np.ndarray) -> np.ndarray:
+    """ggml_get_rows: dequantise the selected rows (ggml dequantize_row_* rules) -> f32 [n][ncols]."""
+    if qtype == F32:
+        return np.ascontiguousarray(rows.view(np.float32).reshape(-1, ncols)[idx])
+    if qtype == F16:
+        return rows.view(np.float16).reshape(-1, ncols)[idx].astype(np.float32)
+    return dequantize(qtype, np.ascontiguousarray(rows.reshape(rows.shape[0], -1)[idx]), ncols)
+
+
 # ---- SAM3 visual encoder restatement (vit_oracle.h) ------------------------
 
 class _Hp(ctypes.Structure):

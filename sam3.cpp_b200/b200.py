@@ -77,6 +77,9 @@ def lib() -> ctypes.CDLL:
         "sam3b200_preprocess": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_preprocess_sam2": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_flash_attn_ext": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, ctypes.c_float, vp]),
+        "sam3b200_conv_transpose_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, vp]),
+        "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
+        "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
         "sam3b200_backend_launch_count": (ctypes.c_longlong, [vp]),
         "sam3b200_backend_profile": (i32, [vp, i32]),
         "sam3b200_backend_profile_read": (i32, [vp, i32, ctypes.POINTER(ctypes.c_double),
@@ -289,6 +292,24 @@ class Backend:
         """GGML_OP_FLASH_ATTN_EXT (sam3.cpp:3778): f32 [D, N, heads, batch] in, [D, heads, N, batch] out."""
         _check(lib().sam3b200_flash_attn_ext(self.h, q.ptr, k.ptr, v.ptr, D, N, heads, batch, scale, dst.ptr),
                "flash_attn_ext")
+
+    def conv_transpose_2d(self, w: DeviceBuffer, x: DeviceBuffer, iw: int, ih: int, ic: int, oc: int, kw: int,
+                          kh: int, stride: int, dst: DeviceBuffer) -> None:
+        """GGML_OP_CONV_TRANSPOSE_2D (ggml_conv_transpose_2d_p0): F16 kernel [kw, kh, oc, ic], f32 input
+        [iw, ih, ic] -> f32 [(iw-1)*stride+kw, (ih-1)*stride+kh, oc]."""
+        _check(lib().sam3b200_conv_transpose_2d(self.h, w.ptr, x.ptr, iw, ih, ic, oc, kw, kh, stride, dst.ptr),
+               "conv_transpose_2d")
+
+    def conv_2d(self, w: DeviceBuffer, x: DeviceBuffer, iw: int, ih: int, ic: int, oc: int, kw: int, kh: int,
+                s0: int, s1: int, p0: int, p1: int, d0: int, d1: int, dst: DeviceBuffer) -> None:
+        """GGML_OP_CONV_2D (ggml_conv_2d): F16 kernel [kw, kh, ic, oc], f32 input [iw, ih, ic] -> f32 [ow, oh, oc]."""
+        _check(lib().sam3b200_conv_2d(self.h, w.ptr, x.ptr, iw, ih, ic, oc, kw, kh, s0, s1, p0, p1, d0, d1, dst.ptr),
+               "conv_2d")
+
+    def get_rows(self, qtype: int, src: DeviceBuffer, ncols: int, nrows: int, idx: DeviceBuffer, n: int,
+                 dst: DeviceBuffer) -> None:
+        """GGML_OP_GET_ROWS: dst[i] = dequantised row idx[i] of src (F32, F16, Q4_0, Q4_1, Q8_0)."""
+        _check(lib().sam3b200_get_rows(self.h, qtype, src.ptr, ncols, nrows, idx.ptr, n, dst.ptr), "get_rows")
 
     def preprocess_sam2(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
         """sam2_preprocess_image: ImageNet-normalised CHW (sam3.cpp:3522-3548)."""

@@ -161,7 +161,10 @@ int sam3b200_backend_synchronize(sam3b200_backend *h) {
     if (!cuda_ok(cudaMemcpy(&e, be->err, sizeof(int), cudaMemcpyDeviceToHost), "read error word"))
         return SAM3B200_STATUS_FAILED;
     if (e != 0) {
-        set_error("kernel pipeline wait timed out (error word 0x%x)", e);
+        if (e == (1 << 20))  // ops.cu: a get_rows index outside the source rows
+            set_error("get_rows: row index out of range (error word 0x%x)", e);
+        else
+            set_error("kernel pipeline wait timed out (error word 0x%x)", e);
         cudaMemset(be->err, 0, sizeof(int));
         return SAM3B200_STATUS_FAILED;
     }
