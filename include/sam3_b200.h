@@ -178,6 +178,53 @@ int sam3b200_conv_2d(sam3b200_backend *be, const void *w_f16, const float *x, in
 int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t ncols, int64_t nrows,
                       const int32_t *idx, int64_t n, float *dst);
 
+/* ---- SAM2 Hiera image encoder (config 1: Hiera trunk + FPN neck) ----------
+ * The graph sam2_build_hiera_graph + sam2_build_fpn_neck_graph build
+ * (sam3.cpp:4467-4583), per-block metadata as sam2_precompute_hiera_metadata
+ * (sam3.cpp:1680-1740).  Weights by their weight-file names
+ * (sam3.cpp:1800-1851): "hiera.patch_embed.{weight,bias}", "hiera.pos_embed",
+ * "hiera.pos_embed_window", "hiera.blocks.<i>.{norm1,norm2}.{weight,bias}",
+ * "...attn.qkv.{weight,bias}", "...attn.proj.{weight,bias}",
+ * "...mlp.fc1/fc2.{weight,bias}", "...proj.{weight,bias}" (stage
+ * transitions), "fpn.convs.<j>.{weight,bias}".  Linear weights Q8_0/Q4_0,
+ * convolution and norm tensors F32/F16. */
+typedef struct {
+    int32_t img;                     /* input side, 1024 */
+    int32_t embed;                   /* hiera_embed_dim */
+    int32_t heads;                   /* hiera_num_heads */
+    int32_t stages[4];
+    int32_t q_pool;
+    int32_t window_spec[4];
+    int32_t n_global;
+    int32_t global_idx[8];
+    int32_t bkg_h, bkg_w;            /* hiera.pos_embed grid */
+    int32_t neck_dim;                /* 256 */
+    int32_t fpn_top_down_n;
+    int32_t fpn_top_down_levels[4];
+    int32_t scalp;
+} sam3b200_hiera_hparams;
+
+typedef struct sam3b200_hiera sam3b200_hiera;
+
+sam3b200_hiera *sam3b200_hiera_create(sam3b200_backend *be, const sam3b200_hiera_hparams *hp);
+void sam3b200_hiera_free(sam3b200_hiera *h);
+int sam3b200_hiera_set_tensor(sam3b200_hiera *h, const char *name, int type, const void *data, const int64_t ne[4]);
+/* Number of tensors still missing; their names, newline-separated, into buf. */
+int sam3b200_hiera_missing(sam3b200_hiera *h, char *buf, int cap);
+/* Block i's metadata: dim_in, dim_out, heads, window size (0 = global), Q stride. */
+int sam3b200_hiera_block_info(sam3b200_hiera *h, int i, int32_t info[5]);
+/* Stage runners (device pointers, asynchronous): patch embedding + positional
+ * embedding, image f32 CHW [3][img][img] -> x [S*S][embed] (S = img/4); one
+ * block, x [H*W][dim_in] -> out [H'*W'][dim_out] (H' = H/2 at a Q-stride
+ * block; out may equal x otherwise). */
+int sam3b200_hiera_run_prefix(sam3b200_hiera *h, const float *img_chw_dev, float *x_dev);
+int sam3b200_hiera_run_block(sam3b200_hiera *h, int i, const float *x_dev, int H, int W, float *out_dev);
+/* Whole encoder from a preprocessed image (sam3b200_preprocess_sam2 output). */
+int sam3b200_hiera_encode_device(sam3b200_hiera *h, const float *img_chw_dev);
+/* Outputs: i = 0..3 FPN levels [neck_dim, W, H, 1] (levels >= 4 - scalp fail),
+ * i = 4..7 stage outputs [dim, W, H, 1]; token-major device f32. */
+int sam3b200_hiera_output(sam3b200_hiera *h, int i, const float **dev, int64_t ne[4]);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

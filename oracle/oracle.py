@@ -150,18 +150,19 @@ def conv_transpose_2d(w: np.ndarray, x: np.ndarray, stride: int) -> np.ndarray:
     return out.astype(np.float32)
 
 
-def conv_2d(w: np.ndarray, x: np.ndarray, s0: int, s1: int, p0: int, p1: int, d0: int = 1, d1: int = 1) -> np.ndarray:
+def conv_2d(w: np.ndarray, x: np.ndarray, s0: int, s1: int, p0: int, p1: int, d0: int = 1, d1: int = 1,
+            f16: bool = True) -> np.ndarray:
     """ggml_conv_2d (sam3.cpp:3819, 3891, 4474; ggml im2col + mul_mat) in float64.
 
     w: fp16 [oc][ic][kh][kw] (ggml [KW, KH, IC, OC]); x: f32 [ic][ih][iw], rounded to fp16 as ggml's
     im2col does for an F16 kernel; zero padding p0/p1, strides s0/s1, dilations d0/d1 (x then y).
-    Returns f32 [oc][oh][ow]."""
+    Returns f32 [oc][oh][ow].  f16=False: an F32 kernel (ggml's f32 im2col path, no rounding)."""
     oc, ic, kh, kw = w.shape
     _, ih, iw = x.shape
     ow = (iw + 2 * p0 - d0 * (kw - 1) - 1) // s0 + 1
     oh = (ih + 2 * p1 - d1 * (kh - 1) - 1) // s1 + 1
     xp = np.zeros((ic, ih + 2 * p1 + s1 * oh, iw + 2 * p0 + s0 * ow), np.float64)
-    xp[:, p1:p1 + ih, p0:p0 + iw] = x.astype(np.float16).astype(np.float64)
+    xp[:, p1:p1 + ih, p0:p0 + iw] = (x.astype(np.float16) if f16 else x).astype(np.float64)
     wd = w.astype(np.float64)
     out = np.zeros((oc, oh * ow), np.float64)
     for ky in range(kh):

@@ -80,6 +80,15 @@ def lib() -> ctypes.CDLL:
         "sam3b200_conv_transpose_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, vp]),
         "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
+        "sam3b200_hiera_create": (vp, [vp, vp]),
+        "sam3b200_hiera_free": (None, [vp]),
+        "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_hiera_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_hiera_block_info": (i32, [vp, i32, vp]),
+        "sam3b200_hiera_run_prefix": (i32, [vp, vp, vp]),
+        "sam3b200_hiera_run_block": (i32, [vp, i32, vp, i32, i32, vp]),
+        "sam3b200_hiera_encode_device": (i32, [vp, vp]),
+        "sam3b200_hiera_output": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p), vp]),
         "sam3b200_backend_launch_count": (ctypes.c_longlong, [vp]),
         "sam3b200_backend_profile": (i32, [vp, i32]),
         "sam3b200_backend_profile_read": (i32, [vp, i32, ctypes.POINTER(ctypes.c_double),
@@ -233,6 +242,85 @@ class Vit:
             self.h = None
 
 
+class HieraHparams(ctypes.Structure):
+    """sam3b200_hiera_hparams (include/sam3_b200.h)."""
+    _fields_ = [("img", ctypes.c_int32), ("embed", ctypes.c_int32), ("heads", ctypes.c_int32),
+                ("stages", ctypes.c_int32 * 4), ("q_pool", ctypes.c_int32), ("window_spec", ctypes.c_int32 * 4),
+                ("n_global", ctypes.c_int32), ("global_idx", ctypes.c_int32 * 8), ("bkg_h", ctypes.c_int32),
+                ("bkg_w", ctypes.c_int32), ("neck_dim", ctypes.c_int32), ("fpn_top_down_n", ctypes.c_int32),
+                ("fpn_top_down_levels", ctypes.c_int32 * 4), ("scalp", ctypes.c_int32)]
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "HieraHparams":
+        h = cls()
+        for k in ("img", "embed", "heads", "q_pool", "bkg_h", "bkg_w", "neck_dim", "scalp"):
+            setattr(h, k, int(d[k]))
+        for k in ("stages", "window_spec"):
+            for i, v in enumerate(d[k]):
+                getattr(h, k)[i] = int(v)
+        h.n_global = len(d["global_idx"])
+        for i, v in enumerate(d["global_idx"]):
+            h.global_idx[i] = int(v)
+        h.fpn_top_down_n = len(d["fpn_top_down_levels"])
+        for i, v in enumerate(d["fpn_top_down_levels"]):
+            h.fpn_top_down_levels[i] = int(v)
+        return h
+
+
+class Hiera:
+    """The SAM2 Hiera image encoder (sam3b200_hiera) on a backend."""
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = HieraHparams.from_dict(hp)
+        self.h = lib().sam3b200_hiera_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"hiera_create failed: {last_error()}")
+
+    def set_tensor(self, name: str, ttype: int, data: np.ndarray, ne) -> None:
+        data = np.ascontiguousarray(data)
+        ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+        _check(lib().sam3b200_hiera_set_tensor(self.h, name.encode(), ttype, data.ctypes.data, ne4), f"set {name}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            self.set_tensor(name, t, arr, ne)
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_hiera_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} hiera tensors missing: {buf.value.decode()[:200]}")
+
+    def block_info(self, i: int) -> tuple:
+        info = (ctypes.c_int32 * 5)()
+        _check(lib().sam3b200_hiera_block_info(self.h, i, info), "hiera_block_info")
+        return tuple(info)
+
+    def run_prefix(self, img_chw: "DeviceBuffer", x: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_hiera_run_prefix(self.h, img_chw.ptr, x.ptr), "hiera_run_prefix")
+
+    def run_block(self, i: int, x: "DeviceBuffer", H: int, W: int, out: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_hiera_run_block(self.h, i, x.ptr, H, W, out.ptr), "hiera_run_block")
+
+    def encode_device(self, img_chw: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_hiera_encode_device(self.h, img_chw.ptr), "hiera_encode_device")
+
+    def output_host(self, i: int) -> np.ndarray:
+        """i = 0..3 FPN levels, 4..7 stage outputs: f32 [H, W, C]."""
+        p = ctypes.c_void_p()
+        ne = (ctypes.c_int64 * 4)()
+        _check(lib().sam3b200_hiera_output(self.h, i, ctypes.byref(p), ne), "hiera_output")
+        self.be.synchronize()
+        out = np.empty((ne[2], ne[1], ne[0]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_hiera_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -330,6 +418,9 @@ class Backend:
 
     def vit(self, hp: dict) -> Vit:
         return Vit(self, hp)
+
+    def hiera(self, hp: dict) -> Hiera:
+        return Hiera(self, hp)
 
     def free(self) -> None:
         if self.h:

@@ -1,0 +1,926 @@
+// hiera.cu -- the SAM2 Hiera image encoder on the B200 backend: the graph
+// sam2_build_hiera_graph + sam2_build_fpn_neck_graph build (sam3.cpp:4467-4583)
+// executed as a fixed sequence of kernels on the backend stream.
+//
+// Per block (sam2_hiera_block_forward, sam3.cpp:4299-4461), x [H*W][C_in]
+// token-major f32 (ggml [C, W, H, 1]):
+//   normed  = LN(x) (eps 1e-6)                                   ln_rows_kernel
+//   shortcut= dim_proj(normed) (+ 2x2 max pool at a Q-stride block), or x
+//   qkv     = MUL_MAT(window-partitioned normed) + bias            win_gather_q8_kernel, mmq_tc
+//             (sam2_window_partition: zero padding to a multiple of the window, window index
+//              wy + nWh * wx, token lx + ws * ly; global blocks keep the token order)
+//   q       = 2x2 max pool of q inside each window at a Q-stride block  qpool_kernel
+//   o       = softmax(q k^T / sqrt(hd)) v per (window, head)      hiera_attn_kernel
+//   x'      = shortcut + crop(unpartition(MUL_MAT(o) + bias))      unpart_add_kernel
+//   x'     += fc2(ggml_gelu(fc1(LN(x')))) (tanh GELU through ggml's fp16 table)
+// The four MUL_MATs of a block and the dimension projection run on the
+// tcgen05 MMQ kernel (exact int32 block dots, mmq.cu); the attention here is
+// a SIMT flash loop in fp32 for any head dimension multiple of 4 up to 128,
+// query/key counts of Q-pooled blocks and padded windows.
+#include "../../include/sam3_b200.h"
+#include "gemm_f16.cuh"
+#include "model_util.h"
+#include "vit_ops.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+namespace b200 {
+namespace {
+
+__device__ __forceinline__ double hwarp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ggml_norm + ggml_mul + ggml_add over each row, f32 out (one warp per row)
+__global__ void ln_rows_kernel(const float *__restrict__ x, int rows, int E, const float *__restrict__ w,
+                               const float *__restrict__ b, float eps, float *__restrict__ y) {
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= rows) return;
+    const float *xr = x + static_cast<int64_t>(t) * E;
+    double s = 0.0;
+    for (int c = lane; c < E; c += 32) s += static_cast<double>(xr[c]);
+    s = hwarp_sum_d(s);
+    const float mean = static_cast<float>(s / E);
+    double s2 = 0.0;
+    for (int c = lane; c < E; c += 32) {
+        const float d = __fsub_rn(xr[c], mean);
+        s2 += static_cast<double>(__fmul_rn(d, d));
+    }
+    s2 = hwarp_sum_d(s2);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(s2 / E), eps)));
+    float *yr = y + static_cast<int64_t>(t) * E;
+    for (int c = lane; c < E; c += 32)
+        yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), scale), w[c]), b[c]);
+}
+
+// Quantise one 32-wide block (ggml-cpu activation rule) and store codes + scale record.
+__device__ __forceinline__ void q8_block_store(const float (&v)[32], int8_t *codes, __half *quads, int blk, int64_t r,
+                                               int ld) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = __fdiv_rn(amax, 127.f);
+    const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+    uint32_t pk[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            w |= (static_cast<uint32_t>(__float2int_rn(__fmul_rn(v[4 * i + e], id))) & 0xFFu) << (8 * e);
+        pk[i] = w;
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(codes + blk * 32);
+    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    quads[act_quad_index(blk, static_cast<int>(r), ld)] = __float2half_rn(d);
+}
+
+// Window partition (with zero padding) of normed [H][W][C] fused with the Q8
+// quantisation of the qkv MUL_MAT input: row r = w * ws^2 + lx + ws * ly of
+// window w = wy + nWh * wx.  One warp per row, one lane per 32-wide block.
+__global__ void win_gather_q8_kernel(const float *__restrict__ x, int H, int W, int C, int ws, int nWh, int rows,
+                                     int8_t *__restrict__ codes, __half *__restrict__ quads, int ld) {
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const int N = ws * ws, w = r / N, n = r % N;
+    const int gx = n % ws + ws * (w / nWh), gy = n / ws + ws * (w % nWh);
+    const float *src = (gx < W && gy < H) ? x + (static_cast<int64_t>(gy) * W + gx) * C : nullptr;
+    int8_t *cr = codes + static_cast<int64_t>(r) * C;
+    for (int blk = lane; blk < C / 32; blk += 32) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const float4 q = src ? *reinterpret_cast<const float4 *>(src + blk * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = q.x;
+            v[i + 1] = q.y;
+            v[i + 2] = q.z;
+            v[i + 3] = q.w;
+        }
+        q8_block_store(v, cr, quads, blk, r, ld);
+    }
+}
+
+// 2x2 max pool of the q part (columns [0, C)) of qkv rows [Bw][wh][ww] (row stride
+// ld) -> qp [Bw][wh/2][ww/2][C] (sam2_maxpool_2d on q, sam3.cpp:4371-4381).
+__global__ void qpool_kernel(const float *__restrict__ qkv, int64_t ld, int Bw, int ww, int wh, int C,
+                             float *__restrict__ qp) {
+    const int pw = ww / 2, ph = wh / 2;
+    const int64_t total = static_cast<int64_t>(Bw) * pw * ph * C;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int c = static_cast<int>(i % C);
+    const int64_t t = i / C;
+    const int px = static_cast<int>(t % pw), py = static_cast<int>((t / pw) % ph), w = static_cast<int>(t / (pw * ph));
+    const int64_t n0 = static_cast<int64_t>(w) * ww * wh + static_cast<int64_t>(2 * py) * ww + 2 * px;
+    const float a = qkv[n0 * ld + c], b = qkv[(n0 + 1) * ld + c];
+    const float d = qkv[(n0 + ww) * ld + c], e = qkv[(n0 + ww + 1) * ld + c];
+    qp[i] = fmaxf(fmaxf(a, b), fmaxf(d, e));
+}
+
+// 2x2 max pool of a token-major map [H][W][C] -> [H/2][W/2][C] (sam2_maxpool_2d)
+__global__ void maxpool2_f32_kernel(const float *__restrict__ x, int H, int W, int C, float *__restrict__ y) {
+    const int W2 = W / 2, H2 = H / 2;
+    const int64_t total = static_cast<int64_t>(H2) * W2 * C;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int c = static_cast<int>(i % C);
+    const int64_t t = i / C;
+    const int xx = static_cast<int>(t % W2), yy = static_cast<int>(t / W2);
+    const int64_t r0 = (static_cast<int64_t>(2 * yy) * W + 2 * xx) * C + c;
+    y[i] = fmaxf(fmaxf(x[r0], x[r0 + C]), fmaxf(x[r0 + static_cast<int64_t>(W) * C], x[r0 + static_cast<int64_t>(W) * C + C]));
+}
+
+// softmax(q k^T * scale) v for every (window, head): 4 threads per query row,
+// DQ = hd / 4 dimensions each; 64-key tiles of k and v in shared memory;
+// online softmax in base 2.  q rows (window bw, token n): q + (bw*NQ + n) * q_ld
+// + h*hd; k, v likewise with NKV and kv_ld; o rows of o_ld (heads concatenated).
+template <int DQ>
+__global__ void __launch_bounds__(256) hiera_attn_kernel(const float *__restrict__ q, int64_t q_ld, int NQ,
+                                                         const float *__restrict__ k, const float *__restrict__ v,
+                                                         int64_t kv_ld, int NKV, int heads, float scale_log2,
+                                                         float *__restrict__ o, int64_t o_ld) {
+    constexpr int HD = 4 * DQ, KT = 64;
+    extern __shared__ float sm[];
+    float *ks = sm, *vs = sm + KT * HD;
+    const int bw = blockIdx.y / heads, h = blockIdx.y % heads;
+    const int row = blockIdx.x * 64 + (threadIdx.x >> 2), part = threadIdx.x & 3;
+    const bool valid = row < NQ;
+    float qv[DQ], acc[DQ];
+    const float *qr = q + (static_cast<int64_t>(bw) * NQ + (valid ? row : 0)) * q_ld + h * HD + part * DQ;
+#pragma unroll
+    for (int i = 0; i < DQ; ++i) {
+        qv[i] = valid ? qr[i] * scale_log2 : 0.f;
+        acc[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (int j0 = 0; j0 < NKV; j0 += KT) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < KT * HD; e += blockDim.x) {
+            const int kk = e / HD, d = e % HD, key = j0 + kk;
+            float kv = 0.f, vv = 0.f;
+            if (key < NKV) {
+                const int64_t off = (static_cast<int64_t>(bw) * NKV + key) * kv_ld + h * HD + d;
+                kv = k[off];
+                vv = v[off];
+            }
+            ks[e] = kv;
+            vs[e] = vv;
+        }
+        __syncthreads();
+        const int nk = NKV - j0 < KT ? NKV - j0 : KT;
+        for (int kk = 0; kk < nk; ++kk) {
+            const float *kr = ks + kk * HD + part * DQ;
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < DQ; ++i) s = fmaf(qv[i], kr[i], s);
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            if (s > m) {
+                const float alpha = exp2f(m - s);
+                l *= alpha;
+#pragma unroll
+                for (int i = 0; i < DQ; ++i) acc[i] *= alpha;
+                m = s;
+            }
+            const float p = exp2f(s - m);
+            l += p;
+            const float *vr = vs + kk * HD + part * DQ;
+#pragma unroll
+            for (int i = 0; i < DQ; ++i) acc[i] = fmaf(p, vr[i], acc[i]);
+        }
+    }
+    if (valid) {
+        const float inv = 1.0f / l;
+        float *orow = o + (static_cast<int64_t>(bw) * NQ + row) * o_ld + h * HD + part * DQ;
+#pragma unroll
+        for (int i = 0; i < DQ; ++i) orow[i] = acc[i] * inv;
+    }
+}
+
+template <int DQ>
+cudaError_t launch_attn(const float *q, int64_t q_ld, int NQ, const float *k, const float *v, int64_t kv_ld, int NKV,
+                        int Bw, int heads, float scale, float *o, int64_t o_ld, cudaStream_t s) {
+    const int smem = 2 * 64 * 4 * DQ * 4;
+    cudaError_t e = cudaFuncSetAttribute(hiera_attn_kernel<DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((NQ + 63) / 64, static_cast<unsigned>(Bw * heads));
+    hiera_attn_kernel<DQ><<<grid, 256, smem, s>>>(q, q_ld, NQ, k, v, kv_ld, NKV, heads, scale * 1.4426950408889634f, o,
+                                                  o_ld);
+    return cudaGetLastError();
+}
+
+cudaError_t hiera_attention(int hd, const float *q, int64_t q_ld, int NQ, const float *k, const float *v,
+                            int64_t kv_ld, int NKV, int Bw, int heads, float scale, float *o, int64_t o_ld,
+                            cudaStream_t s) {
+    if (NQ <= 0 || NKV <= 0 || Bw <= 0 || heads <= 0 || static_cast<int64_t>(Bw) * heads > 65535)
+        return cudaErrorInvalidValue;
+    switch (hd) {
+    case 32: return launch_attn<8>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 48: return launch_attn<12>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 56: return launch_attn<14>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 64: return launch_attn<16>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 72: return launch_attn<18>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 96: return launch_attn<24>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 112: return launch_attn<28>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    case 128: return launch_attn<32>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// x_out[t] = shortcut[t] + proj[row(t)] over the H x W output map: the window
+// unpartition (with crop) of sam3.cpp:4243-4281 fused with the residual add
+// (:4426).  ws == 0: proj is already in token order.
+__global__ void unpart_add_kernel(const float *__restrict__ sc, const float *__restrict__ proj, int H, int W, int C,
+                                  int ws, int nWh, float *__restrict__ out) {
+    const int64_t total = static_cast<int64_t>(H) * W * C;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int c = static_cast<int>(i % C);
+    const int64_t t = i / C;
+    int64_t r = t;
+    if (ws > 0) {
+        const int x = static_cast<int>(t % W), y = static_cast<int>(t / W);
+        r = static_cast<int64_t>(y / ws + nWh * (x / ws)) * ws * ws + x % ws + ws * (y % ws);
+    }
+    out[i] = __fadd_rn(sc[i], proj[r * C + c]);
+}
+
+// Patch embedding in f32, as the reference's F32 kernel computes it
+// (ggml_conv_2d with an F32 kernel: f32 im2col + f32 MUL_MAT, sam3.cpp:4474):
+// Conv2d(3 -> E, k 7, s 4, p 3) + bias, then + pe; x [P][E] token-major.  One
+// thread per (pixel, channel); the kernel [E][147] sits in shared memory.
+__global__ void patch_conv_f32_kernel(const float *__restrict__ img, int img_side, int S, int E,
+                                      const float *__restrict__ w, const float *__restrict__ bias,
+                                      const float *__restrict__ pe, float *__restrict__ x) {
+    extern __shared__ float wsm[];
+    for (int i = threadIdx.x; i < E * 147; i += blockDim.x) wsm[i] = w[i];
+    __syncthreads();
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= static_cast<int64_t>(S) * S * E) return;
+    const int e = static_cast<int>(idx % E);
+    const int p = static_cast<int>(idx / E);
+    const int ox = p % S, oy = p / S;
+    const float *wr = wsm + e * 147;
+    float acc = 0.f;
+    for (int ic = 0; ic < 3; ++ic)
+        for (int ky = 0; ky < 7; ++ky) {
+            const int iy = oy * 4 + ky - 3;
+            if (iy < 0 || iy >= img_side) continue;
+            const float *row = img + (static_cast<int64_t>(ic) * img_side + iy) * img_side;
+            for (int kx = 0; kx < 7; ++kx) {
+                const int ix = ox * 4 + kx - 3;
+                if (ix >= 0 && ix < img_side) acc = fmaf(row[ix], wr[(ic * 7 + ky) * 7 + kx], acc);
+            }
+        }
+    x[idx] = __fadd_rn(__fadd_rn(acc, bias[e]), pe[idx]);
+}
+
+// FPN top-down fusion: y[t] = lat[t] + prev[nearest 2x source of t] (sam3.cpp:4568-4573)
+__global__ void upsample2_add_kernel(const float *__restrict__ lat, const float *__restrict__ prev, int H, int W, int D,
+                                     float *__restrict__ y) {
+    const int64_t total = static_cast<int64_t>(H) * W * D;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int d = static_cast<int>(i % D);
+    const int64_t t = i / D;
+    const int x = static_cast<int>(t % W), yy = static_cast<int>(t / W);
+    y[i] = __fadd_rn(lat[i], prev[(static_cast<int64_t>(yy / 2) * (W / 2) + x / 2) * D + d]);
+}
+
+inline unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+inline int round128(int64_t n) { return static_cast<int>((n + 127) / 128 * 128); }
+
+// Bicubic resize of a CHW map (Keys kernel, a = -0.75, half-pixel centres,
+// clamped taps): the host-side positional-embedding precompute of
+// sam3.cpp:4076-4108, restated.
+void bicubic_chw(const std::vector<float> &src, int C, int hi, int wi, std::vector<float> &dst, int ho, int wo) {
+    auto cubic = [](float x) -> float {
+        x = fabsf(x);
+        if (x < 1.0f) return (1.25f * x - 2.25f) * x * x + 1.0f;
+        if (x < 2.0f) return ((-0.75f * x + 3.75f) * x - 6.0f) * x + 3.0f;
+        return 0.0f;
+    };
+    dst.assign(static_cast<size_t>(C) * ho * wo, 0.f);
+    for (int c = 0; c < C; ++c)
+        for (int y = 0; y < ho; ++y) {
+            const float fy = (static_cast<float>(y) + 0.5f) * static_cast<float>(hi) / static_cast<float>(ho) - 0.5f;
+            const int iy = static_cast<int>(floorf(fy));
+            const float dy = fy - static_cast<float>(iy);
+            for (int x = 0; x < wo; ++x) {
+                const float fx = (static_cast<float>(x) + 0.5f) * static_cast<float>(wi) / static_cast<float>(wo) - 0.5f;
+                const int ix = static_cast<int>(floorf(fx));
+                const float dx = fx - static_cast<float>(ix);
+                float val = 0.0f;
+                for (int jj = -1; jj <= 2; ++jj) {
+                    const float wy = cubic(dy - static_cast<float>(jj));
+                    const int sy = std::min(std::max(iy + jj, 0), hi - 1);
+                    for (int ii = -1; ii <= 2; ++ii) {
+                        const float wx = cubic(dx - static_cast<float>(ii));
+                        const int sx = std::min(std::max(ix + ii, 0), wi - 1);
+                        val += wy * wx * src[(static_cast<size_t>(c) * hi + sy) * wi + sx];
+                    }
+                }
+                dst[(static_cast<size_t>(c) * ho + y) * wo + x] = val;
+            }
+        }
+}
+
+struct HBlock {
+    int dim_in = 0, dim_out = 0, heads = 0, ws = 0, stage = 0;
+    bool q_stride = false;
+    DevBuf n1w, n1b, n2w, n2b, qkv_b, proj_b, fc1_b, fc2_b, dproj_b;
+    QWeight qkv, proj, fc1, fc2, dproj;
+};
+
+struct FpnLevel {
+    DevBuf w16, b;  // fp16 [D][C], f32 [D]
+    int C = 0;
+};
+
+}  // namespace
+
+struct Hiera {
+    Backend *be = nullptr;
+    sam3b200_hiera_hparams hp{};
+    int S = 0;  // patch grid side
+    int stage_ends[4] = {0, 0, 0, 0};
+    std::vector<HBlock> blk;
+    DevBuf patch_w32, patch_b, pe;  // f32 kernel [E][3*7*7]
+    std::vector<float> pos_bkg, pos_win;  // host copies until both are set
+    FpnLevel fpn[4];
+    std::vector<std::string> missing;
+    // activations
+    DevBuf xa, xb, normed, shortf, shortp, qkv, qp, attn, proj, codes_a, quads_a, codes_b, quads_b;
+    DevBuf stage_out[4], fpn_out[4], x16;
+    int stage_side[4] = {0, 0, 0, 0}, stage_dim[4] = {0, 0, 0, 0};
+    int n_fpn = 0;
+    bool ready = false;
+};
+
+namespace {
+
+bool hlaunched(Hiera *h, cudaError_t e, const char *what, int n = 1) {
+    h->be->count(n);
+    return cuda_ok(e, what);
+}
+
+bool h_mmq(Hiera *h, const void *codes, const void *quads, int M, const QWeight &w, int mode, const float *bias,
+           float *y, int add, void *oc, void *oq, int gelu) {
+    MmqArgs a;
+    const int ld = round128(M);
+    a.a = QMatrix{codes, quads, M, w.K, ld};
+    a.b = QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld};
+    a.bias = bias;
+    a.y = y;
+    a.ldy = w.N;
+    a.dump = nullptr;
+    a.err = h->be->err;
+    a.add = add;
+    a.gelu = gelu;
+    a.out_codes = oc;
+    a.out_quads = oq;
+    a.out_ld = ld;
+    h->be->prof_mark(0);
+    const bool ok = hlaunched(h, mmq_tc(a, mode, h->be->num_sms, h->be->stream, h->be->mmq_cvt, h->be->mmq_bn), "hiera mmq");
+    h->be->prof_mark(0);
+    return ok;
+}
+
+// Derive the per-block metadata exactly as sam2_precompute_hiera_metadata (sam3.cpp:1680-1740).
+bool hiera_metadata(Hiera *h) {
+    const auto &hp = h->hp;
+    int total = 0;
+    for (int s = 0; s < 4; ++s) {
+        if (hp.stages[s] <= 0) return false;
+        total += hp.stages[s];
+        h->stage_ends[s] = total - 1;
+    }
+    std::vector<int> qpool;
+    for (int s = 0; s < 3 && static_cast<int>(qpool.size()) < hp.q_pool; ++s) qpool.push_back(h->stage_ends[s] + 1);
+    h->blk.resize(total);
+    int cur = 0, embed = hp.embed, nh = hp.heads;
+    for (int i = 0; i < total; ++i) {
+        HBlock &b = h->blk[i];
+        int ws = hp.window_spec[cur];
+        for (int g = 0; g < hp.n_global && g < 8; ++g)
+            if (hp.global_idx[g] == i) ws = 0;
+        b.ws = ws;
+        int dout = embed;
+        if (i > 0 && i - 1 == h->stage_ends[cur]) {
+            dout = embed * 2;
+            nh *= 2;
+            ++cur;
+        }
+        b.stage = cur;
+        b.dim_in = embed;
+        b.dim_out = dout;
+        b.heads = nh;
+        b.q_stride = false;
+        for (int qb : qpool)
+            if (qb == i) b.q_stride = true;
+        embed = dout;
+        if (b.dim_in % 32 != 0 || b.dim_out % 32 != 0 || b.dim_out % b.heads != 0) return false;
+    }
+    return true;
+}
+
+struct BlockGeo {
+    int H, W, Ho, Wo, ws, nWh, Bw, N, wq_w, wq_h, NQ, ws_o, nWh_o;
+};
+
+BlockGeo block_geo(const HBlock &b, int H, int W) {
+    BlockGeo g{};
+    g.H = H;
+    g.W = W;
+    g.Ho = b.q_stride ? H / 2 : H;
+    g.Wo = b.q_stride ? W / 2 : W;
+    g.ws = b.ws;
+    if (b.ws > 0) {
+        const int Hp = (H + b.ws - 1) / b.ws * b.ws, Wp = (W + b.ws - 1) / b.ws * b.ws;
+        g.nWh = Hp / b.ws;
+        g.Bw = g.nWh * (Wp / b.ws);
+        g.N = b.ws * b.ws;
+        g.wq_w = g.wq_h = b.ws;
+    } else {
+        g.nWh = 1;
+        g.Bw = 1;
+        g.N = H * W;
+        g.wq_w = W;
+        g.wq_h = H;
+    }
+    g.NQ = b.q_stride ? (g.wq_w / 2) * (g.wq_h / 2) : g.N;
+    if (b.ws > 0) {
+        g.ws_o = b.q_stride ? b.ws / 2 : b.ws;
+        const int pad = (g.ws_o - g.Ho % g.ws_o) % g.ws_o;  // sam3.cpp:4409-4414
+        g.nWh_o = (g.Ho + pad) / g.ws_o;
+    } else {
+        g.ws_o = 0;
+        g.nWh_o = 1;
+    }
+    return g;
+}
+
+bool alloc_hiera(Hiera *h) {
+    const auto &hp = h->hp;
+    const int S = h->S;
+    size_t mx_x = 0, mx_norm = 0, mx_sf = 0, mx_sp = 0, mx_qkv = 0, mx_qp = 0, mx_codes_a = 0, mx_quads_a = 0,
+           mx_codes_b = 0, mx_quads_b = 0;
+    int H = S, W = S;
+    for (size_t i = 0; i < h->blk.size(); ++i) {
+        const HBlock &b = h->blk[i];
+        const BlockGeo g = block_geo(b, H, W);
+        const size_t T = static_cast<size_t>(H) * W, To = static_cast<size_t>(g.Ho) * g.Wo;
+        const size_t rw = static_cast<size_t>(g.Bw) * g.N, rq = static_cast<size_t>(g.Bw) * g.NQ;
+        mx_x = std::max({mx_x, T * b.dim_in, To * b.dim_out});
+        mx_norm = std::max(mx_norm, T * b.dim_in);
+        mx_sf = std::max(mx_sf, T * b.dim_out);
+        mx_sp = std::max(mx_sp, To * b.dim_out);
+        mx_qkv = std::max(mx_qkv, rw * 3 * b.dim_out);
+        mx_qp = std::max(mx_qp, rq * b.dim_out);
+        mx_codes_a = std::max({mx_codes_a, rw * b.dim_in, T * b.dim_in, rq * b.dim_out, To * b.dim_out});
+        const size_t ga = static_cast<size_t>((std::max(b.dim_in, b.dim_out) + 255) / 256);
+        mx_quads_a = std::max({mx_quads_a, ga * round128(static_cast<int64_t>(std::max({rw, T, rq, To}))) * 16});
+        mx_codes_b = std::max(mx_codes_b, To * 4 * b.dim_out);
+        mx_quads_b = std::max(mx_quads_b, static_cast<size_t>((4 * b.dim_out + 255) / 256) * round128(To) * 16);
+        H = g.Ho;
+        W = g.Wo;
+        if (static_cast<int>(i) == h->stage_ends[b.stage]) {
+            h->stage_side[b.stage] = H;
+            h->stage_dim[b.stage] = b.dim_out;
+        }
+    }
+    bool ok = h->xa.alloc(mx_x * 4) &&
+              h->xb.alloc(mx_x * 4) && h->normed.alloc(mx_norm * 4) && h->shortf.alloc(mx_sf * 4) &&
+              h->shortp.alloc(mx_sp * 4) && h->qkv.alloc(mx_qkv * 4) && h->qp.alloc(mx_qp * 4) &&
+              h->attn.alloc(mx_qp * 4) && h->proj.alloc(mx_qp * 4) && h->codes_a.alloc(mx_codes_a) &&
+              h->quads_a.alloc(mx_quads_a) && h->codes_b.alloc(mx_codes_b) && h->quads_b.alloc(mx_quads_b);
+    size_t mx16 = 0;
+    for (int s = 0; s < 4 && ok; ++s) {
+        const size_t T = static_cast<size_t>(h->stage_side[s]) * h->stage_side[s];
+        ok = h->stage_out[s].alloc(T * h->stage_dim[s] * 4) && h->fpn_out[s].alloc(T * hp.neck_dim * 4);
+        mx16 = std::max(mx16, T * h->stage_dim[s] * 2);
+    }
+    ok = ok && h->x16.alloc(mx16);
+    if (!ok) return false;
+    return cuda_ok(cudaMemsetAsync(h->quads_a.p, 0, h->quads_a.n, h->be->stream), "memset") &&
+           cuda_ok(cudaMemsetAsync(h->quads_b.p, 0, h->quads_b.n, h->be->stream), "memset") &&
+           cuda_ok(cudaStreamSynchronize(h->be->stream), "alloc sync");
+}
+
+bool make_pe(Hiera *h) {
+    const auto &hp = h->hp;
+    const int E = hp.embed, S = h->S, ws = hp.window_spec[0];
+    std::vector<float> bk;
+    bicubic_chw(h->pos_bkg, E, hp.bkg_h, hp.bkg_w, bk, S, S);
+    std::vector<float> pe(static_cast<size_t>(E) * S * S);
+    for (int e = 0; e < E; ++e)
+        for (int y = 0; y < S; ++y)
+            for (int x = 0; x < S; ++x)
+                pe[static_cast<size_t>(e) + static_cast<size_t>(x) * E + static_cast<size_t>(y) * E * S] =
+                    bk[(static_cast<size_t>(e) * S + y) * S + x] +
+                    h->pos_win[(static_cast<size_t>(e) * ws + (y % ws)) * ws + (x % ws)];
+    return upload(h->pe, pe.data(), pe.size() * 4, h->be->stream);
+}
+
+bool run_prefix(Hiera *h, const float *img_chw, float *x) {
+    const auto &hp = h->hp;
+    const int S = h->S, E = hp.embed;
+    const int smem = E * 147 * 4;
+    if (!hlaunched(h, cudaFuncSetAttribute(patch_conv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                   "hiera patch smem", 0))
+        return false;
+    patch_conv_f32_kernel<<<blocks_for(static_cast<int64_t>(S) * S * E, 256), 256, smem, h->be->stream>>>(
+        img_chw, hp.img, S, E, h->patch_w32.as<float>(), h->patch_b.as<float>(), h->pe.as<float>(), x);
+    return hlaunched(h, cudaGetLastError(), "hiera patch embedding");
+}
+
+bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
+    const HBlock &b = h->blk[i];
+    const BlockGeo g = block_geo(b, H, W);
+    cudaStream_t s = h->be->stream;
+    const int Ci = b.dim_in, Co = b.dim_out, T = H * W, To = g.Ho * g.Wo;
+    const int rw = g.Bw * g.N, rq = g.Bw * g.NQ;
+    if (g.ws_o > 0 && static_cast<int64_t>((g.Wo + g.ws_o - 1) / g.ws_o) * g.nWh_o * g.ws_o * g.ws_o > rq) {
+        set_error("hiera block %d: the output windows do not match the partition (%dx%d, window %d)", i, H, W, b.ws);
+        return false;
+    }
+    // 1. LN1
+    ln_rows_kernel<<<blocks_for(T, 8), 256, 0, s>>>(x, T, Ci, b.n1w.as<float>(), b.n1b.as<float>(), 1e-6f,
+                                                    h->normed.as<float>());
+    if (!hlaunched(h, cudaGetLastError(), "hiera ln1")) return false;
+    // 2. shortcut
+    const float *sc = x;
+    if (Ci != Co) {
+        if (!hlaunched(h, quantize_rows_q8(h->normed.as<float>(), Ci, T, Ci, h->codes_a.p, h->quads_a.p, round128(T), s),
+                       "hiera quantize") ||
+            !h_mmq(h, h->codes_a.p, h->quads_a.p, T, b.dproj, MMQ_OUT_F32, b.dproj_b.as<float>(),
+                   h->shortf.as<float>(), 0, nullptr, nullptr, 0))
+            return false;
+        sc = h->shortf.as<float>();
+    }
+    if (b.q_stride) {
+        maxpool2_f32_kernel<<<blocks_for(static_cast<int64_t>(To) * Co, 256), 256, 0, s>>>(sc, H, W, Co,
+                                                                                            h->shortp.as<float>());
+        if (!hlaunched(h, cudaGetLastError(), "hiera pool shortcut")) return false;
+        sc = h->shortp.as<float>();
+    }
+    // 3. qkv over the window-partitioned normed input
+    cudaError_t e;
+    if (b.ws > 0) {
+        win_gather_q8_kernel<<<blocks_for(rw, 8), 256, 0, s>>>(h->normed.as<float>(), H, W, Ci, b.ws, g.nWh, rw,
+                                                               h->codes_a.as<int8_t>(), h->quads_a.as<__half>(),
+                                                               round128(rw));
+        e = cudaGetLastError();
+    } else {
+        e = quantize_rows_q8(h->normed.as<float>(), Ci, T, Ci, h->codes_a.p, h->quads_a.p, round128(T), s);
+    }
+    if (!hlaunched(h, e, "hiera qkv input") ||
+        !h_mmq(h, h->codes_a.p, h->quads_a.p, rw, b.qkv, MMQ_OUT_F32, b.qkv_b.as<float>(), h->qkv.as<float>(), 0,
+               nullptr, nullptr, 0))
+        return false;
+    // 4. Q pooling inside the windows
+    const float *qptr = h->qkv.as<float>();
+    int64_t q_ld = 3 * Co;
+    if (b.q_stride) {
+        qpool_kernel<<<blocks_for(static_cast<int64_t>(rq) * Co, 256), 256, 0, s>>>(h->qkv.as<float>(), 3 * Co, g.Bw,
+                                                                                    g.wq_w, g.wq_h, Co,
+                                                                                    h->qp.as<float>());
+        if (!hlaunched(h, cudaGetLastError(), "hiera qpool")) return false;
+        qptr = h->qp.as<float>();
+        q_ld = Co;
+    }
+    // 5. attention per (window, head)
+    const int hd = Co / b.heads;
+    if (!hlaunched(h,
+                   hiera_attention(hd, qptr, q_ld, g.NQ, h->qkv.as<float>() + Co, h->qkv.as<float>() + 2 * Co, 3 * Co,
+                                   g.N, g.Bw, b.heads, 1.0f / sqrtf(static_cast<float>(hd)), h->attn.as<float>(), Co,
+                                   s),
+                   "hiera attention"))
+        return false;
+    // 6. output projection
+    if (!hlaunched(h, quantize_rows_q8(h->attn.as<float>(), Co, rq, Co, h->codes_a.p, h->quads_a.p, round128(rq), s),
+                   "hiera quantize attn") ||
+        !h_mmq(h, h->codes_a.p, h->quads_a.p, rq, b.proj, MMQ_OUT_F32, b.proj_b.as<float>(), h->proj.as<float>(), 0,
+               nullptr, nullptr, 0))
+        return false;
+    // 7. unpartition + crop + residual
+    unpart_add_kernel<<<blocks_for(static_cast<int64_t>(To) * Co, 256), 256, 0, s>>>(sc, h->proj.as<float>(), g.Ho, g.Wo,
+                                                                                     Co, g.ws_o, g.nWh_o, out);
+    if (!hlaunched(h, cudaGetLastError(), "hiera unpartition")) return false;
+    // 8. MLP: LN2 -> fc1 + GELU (tanh, fp16 table) -> Q8 -> fc2 + bias, residual
+    return hlaunched(h,
+                     layernorm_q8(out, To, Co, b.n2w.as<float>(), b.n2b.as<float>(), 1e-6f, g.Wo, 0, h->codes_a.p,
+                                  h->quads_a.p, round128(To), s),
+                     "hiera ln2") &&
+           h_mmq(h, h->codes_a.p, h->quads_a.p, To, b.fc1, MMQ_OUT_Q8, b.fc1_b.as<float>(), nullptr, 0, h->codes_b.p,
+                 h->quads_b.p, 2) &&
+           h_mmq(h, h->codes_b.p, h->quads_b.p, To, b.fc2, MMQ_OUT_F32, b.fc2_b.as<float>(), out, 1, nullptr, nullptr,
+                 0);
+}
+
+bool run_fpn(Hiera *h) {
+    const auto &hp = h->hp;
+    cudaStream_t s = h->be->stream;
+    const int D = hp.neck_dim;
+    // laterals: convs[3 - i] on stage i (1x1 conv = fp16 GEMM + bias), token-major [T][D]
+    for (int i = 0; i < 4; ++i) {
+        const FpnLevel &L = h->fpn[3 - i];
+        const int T = h->stage_side[i] * h->stage_side[i];
+        if (!hlaunched(h, f32_to_f16(h->stage_out[i].as<float>(), static_cast<int64_t>(T) * L.C, h->x16.p, s),
+                       "fpn f16"))
+            return false;
+        GemmF16Args g{};
+        g.a = h->x16.p;
+        g.b = L.w16.p;
+        g.M = T;
+        g.N = D;
+        g.K = L.C;
+        g.bias = L.b.as<float>();
+        g.out = h->fpn_out[i].p;
+        g.ldo = D;
+        g.store = GEMM_STORE_ROWMAJOR;
+        g.err = h->be->err;
+        if (!hlaunched(h, gemm_f16(g, h->be->num_sms, s), "fpn lateral")) return false;
+    }
+    // top-down: from the coarsest level down; levels listed in fpn_top_down_levels add the
+    // 2x nearest upsample of the previous fused level (sam3.cpp:4556-4578)
+    int prev = -1;
+    for (int ri = 0; ri < 4; ++ri) {
+        const int i = 3 - ri;
+        bool td = false;
+        for (int j = 0; j < hp.fpn_top_down_n && j < 4; ++j)
+            if (hp.fpn_top_down_levels[j] == i) td = true;
+        if (td && prev >= 0) {
+            const int side = h->stage_side[i];
+            if (h->stage_side[prev] * 2 != side) {
+                set_error("hiera fpn: level %d is not twice level %d", i, prev);
+                return false;
+            }
+            const int64_t n = static_cast<int64_t>(side) * side * D;
+            upsample2_add_kernel<<<blocks_for(n, 256), 256, 0, s>>>(h->fpn_out[i].as<float>(),
+                                                                     h->fpn_out[prev].as<float>(), side, side, D,
+                                                                     h->fpn_out[i].as<float>());
+            if (!hlaunched(h, cudaGetLastError(), "fpn top-down")) return false;
+            prev = i;
+        } else if (td || prev < 0) {
+            prev = i;
+        }
+    }
+    return true;
+}
+
+bool encode(Hiera *h, const float *img_chw) {
+    float *x = h->xa.as<float>(), *y = h->xb.as<float>();
+    if (!run_prefix(h, img_chw, x)) return false;
+    int H = h->S, W = h->S;
+    for (size_t i = 0; i < h->blk.size(); ++i) {
+        const HBlock &b = h->blk[i];
+        float *dst = b.q_stride ? y : x;  // shape changes need a second buffer
+        if (!run_block(h, static_cast<int>(i), x, H, W, dst)) return false;
+        if (b.q_stride) std::swap(x, y);
+        if (b.q_stride) {
+            H /= 2;
+            W /= 2;
+        }
+        if (static_cast<int>(i) == h->stage_ends[b.stage]) {
+            const size_t bytes = static_cast<size_t>(H) * W * b.dim_out * 4;
+            if (!cuda_ok(cudaMemcpyAsync(h->stage_out[b.stage].p, x, bytes, cudaMemcpyDeviceToDevice, h->be->stream),
+                         "stage copy"))
+                return false;
+        }
+    }
+    return run_fpn(h);
+}
+
+bool check_ready(Hiera *h) {
+    if (h->ready) return true;
+    h->missing.clear();
+    if (!h->patch_w32.p) h->missing.push_back("hiera.patch_embed.weight");
+    if (!h->patch_b.p) h->missing.push_back("hiera.patch_embed.bias");
+    if (!h->pe.p) h->missing.push_back("hiera.pos_embed / hiera.pos_embed_window");
+    for (size_t i = 0; i < h->blk.size(); ++i) {
+        const HBlock &b = h->blk[i];
+        const std::string p = "hiera.blocks." + std::to_string(i);
+        if (!b.n1w.p || !b.n1b.p || !b.n2w.p || !b.n2b.p) h->missing.push_back(p + ".norm1/norm2");
+        if (!b.qkv.set || !b.qkv_b.p) h->missing.push_back(p + ".attn.qkv");
+        if (!b.proj.set || !b.proj_b.p) h->missing.push_back(p + ".attn.proj");
+        if (!b.fc1.set || !b.fc1_b.p || !b.fc2.set || !b.fc2_b.p) h->missing.push_back(p + ".mlp");
+        if (b.dim_in != b.dim_out && (!b.dproj.set || !b.dproj_b.p)) h->missing.push_back(p + ".proj");
+    }
+    for (int j = 0; j < 4; ++j)
+        if (!h->fpn[j].w16.p || !h->fpn[j].b.p) h->missing.push_back("fpn.convs." + std::to_string(j));
+    if (!h->missing.empty()) {
+        set_error("hiera: %zu tensors missing (first: %s)", h->missing.size(), h->missing[0].c_str());
+        return false;
+    }
+    h->ready = true;
+    return true;
+}
+
+}  // namespace
+}  // namespace b200
+
+using namespace b200;
+
+sam3b200_hiera *sam3b200_hiera_create(sam3b200_backend *hb, const sam3b200_hiera_hparams *hp) {
+    auto *be = reinterpret_cast<Backend *>(hb);
+    if (!be || !hp) return nullptr;
+    if (hp->img <= 0 || hp->img % 32 != 0 || hp->embed <= 0 || hp->embed % 32 != 0 || hp->heads <= 0 ||
+        hp->neck_dim <= 0 || hp->neck_dim % 8 != 0 || hp->window_spec[0] <= 0 || hp->bkg_h <= 0 || hp->bkg_w <= 0 ||
+        hp->scalp < 0 || hp->scalp > 3) {
+        set_error("hiera_create: unsupported hyperparameters");
+        return nullptr;
+    }
+    cudaSetDevice(be->device);
+    auto *h = new Hiera();
+    h->be = be;
+    h->hp = *hp;
+    h->S = (hp->img + 2 * 3 - 7) / 4 + 1;
+    if (!hiera_metadata(h)) {
+        set_error("hiera_create: block dimensions must be multiples of 32 and divisible by the head count");
+        delete h;
+        return nullptr;
+    }
+    h->n_fpn = 4 - hp->scalp;
+    if (!alloc_hiera(h)) {
+        delete h;
+        return nullptr;
+    }
+    return reinterpret_cast<sam3b200_hiera *>(h);
+}
+
+void sam3b200_hiera_free(sam3b200_hiera *hh) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h) return;
+    cudaSetDevice(h->be->device);
+    cudaStreamSynchronize(h->be->stream);
+    delete h;
+}
+
+int sam3b200_hiera_block_info(sam3b200_hiera *hh, int i, int32_t info[5]) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !info || i < 0 || i >= static_cast<int>(h->blk.size())) return SAM3B200_STATUS_FAILED;
+    const HBlock &b = h->blk[i];
+    info[0] = b.dim_in;
+    info[1] = b.dim_out;
+    info[2] = b.heads;
+    info[3] = b.ws;
+    info[4] = b.q_stride ? 1 : 0;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+int sam3b200_hiera_set_tensor(sam3b200_hiera *hh, const char *name_c, int type, const void *data, const int64_t *ne) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !name_c || !data || !ne) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(h->be->device);
+    const std::string name(name_c);
+    const auto &hp = h->hp;
+    cudaStream_t s = h->be->stream;
+    const int64_t n = ne[0] * (ne[1] > 0 ? ne[1] : 1) * (ne[2] > 0 ? ne[2] : 1) * (ne[3] > 0 ? ne[3] : 1);
+    std::vector<float> f;
+    auto vec = [&](DevBuf &d, int64_t want) -> int {
+        if (n != want) {
+            set_error("%s: %lld elements, expected %lld", name_c, (long long)n, (long long)want);
+            return SAM3B200_STATUS_FAILED;
+        }
+        if (!to_f32(type, data, n, f) || !upload(d, f.data(), f.size() * 4, s)) return SAM3B200_STATUS_FAILED;
+        return SAM3B200_STATUS_SUCCESS;
+    };
+    h->ready = false;
+    if (name == "hiera.patch_embed.weight") {  // [7, 7, 3, E]: memory [e][(ic, ky, kx)]
+        if (ne[0] != 7 || ne[1] != 7 || ne[2] != 3 || ne[3] != hp.embed || !to_f32(type, data, n, f)) {
+            set_error("%s: expected [7, 7, 3, %d] F32/F16", name_c, hp.embed);
+            return SAM3B200_STATUS_FAILED;
+        }
+        return upload(h->patch_w32, f.data(), f.size() * 4, s) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+    }
+    if (name == "hiera.patch_embed.bias") return vec(h->patch_b, hp.embed);
+    if (name == "hiera.pos_embed" || name == "hiera.pos_embed_window") {
+        const bool bkg = name == "hiera.pos_embed";
+        const int64_t want = bkg ? static_cast<int64_t>(hp.bkg_h) * hp.bkg_w * hp.embed
+                                 : static_cast<int64_t>(hp.window_spec[0]) * hp.window_spec[0] * hp.embed;
+        if (n != want || !to_f32(type, data, n, f)) {
+            set_error("%s: %lld elements, expected %lld", name_c, (long long)n, (long long)want);
+            return SAM3B200_STATUS_FAILED;
+        }
+        (bkg ? h->pos_bkg : h->pos_win) = f;
+        if (!h->pos_bkg.empty() && !h->pos_win.empty() && !make_pe(h)) return SAM3B200_STATUS_FAILED;
+        return SAM3B200_STATUS_SUCCESS;
+    }
+    if (name.rfind("fpn.convs.", 0) == 0) {
+        const int j = atoi(name.c_str() + 10);
+        if (j < 0 || j > 3) return SAM3B200_STATUS_FAILED;
+        FpnLevel &L = h->fpn[j];
+        const int C = h->stage_dim[3 - j];
+        if (name.size() > 7 && name.compare(name.size() - 7, 7, ".weight") == 0) {
+            if (n != static_cast<int64_t>(C) * hp.neck_dim || !to_f32(type, data, n, f)) {
+                set_error("%s: expected [1, 1, %d, %d]", name_c, C, hp.neck_dim);
+                return SAM3B200_STATUS_FAILED;
+            }
+            L.C = C;
+            return upload_f16(L.w16, f, s) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+        }
+        return vec(L.b, hp.neck_dim);
+    }
+    if (name.rfind("hiera.blocks.", 0) == 0) {
+        const int i = atoi(name.c_str() + 13);
+        if (i < 0 || i >= static_cast<int>(h->blk.size())) return SAM3B200_STATUS_FAILED;
+        HBlock &b = h->blk[i];
+        const std::string p = "hiera.blocks." + std::to_string(i) + ".";
+        const std::string r = name.substr(p.size());
+        if (r == "norm1.weight") return vec(b.n1w, b.dim_in);
+        if (r == "norm1.bias") return vec(b.n1b, b.dim_in);
+        if (r == "norm2.weight") return vec(b.n2w, b.dim_out);
+        if (r == "norm2.bias") return vec(b.n2b, b.dim_out);
+        if (r == "attn.qkv.bias") return vec(b.qkv_b, 3 * b.dim_out);
+        if (r == "attn.proj.bias") return vec(b.proj_b, b.dim_out);
+        if (r == "mlp.fc1.bias") return vec(b.fc1_b, 4 * b.dim_out);
+        if (r == "mlp.fc2.bias") return vec(b.fc2_b, b.dim_out);
+        if (r == "proj.bias") return vec(b.dproj_b, b.dim_out);
+        QWeight *w = nullptr;
+        int64_t K = 0, N = 0;
+        if (r == "attn.qkv.weight") w = &b.qkv, K = b.dim_in, N = 3 * b.dim_out;
+        else if (r == "attn.proj.weight") w = &b.proj, K = b.dim_out, N = b.dim_out;
+        else if (r == "mlp.fc1.weight") w = &b.fc1, K = b.dim_out, N = 4 * b.dim_out;
+        else if (r == "mlp.fc2.weight") w = &b.fc2, K = 4 * b.dim_out, N = b.dim_out;
+        else if (r == "proj.weight") w = &b.dproj, K = b.dim_in, N = b.dim_out;
+        if (w) {
+            if (ne[0] != K || ne[1] != N) {
+                set_error("%s: shape [%lld, %lld], expected [%lld, %lld]", name_c, (long long)ne[0], (long long)ne[1],
+                          (long long)K, (long long)N);
+                return SAM3B200_STATUS_FAILED;
+            }
+            return upload_qweight(h->be, *w, type, data, K, N) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+        }
+    }
+    set_error("hiera: unknown tensor %s", name_c);
+    return SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_hiera_missing(sam3b200_hiera *hh, char *buf, int cap) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h) return -1;
+    check_ready(h);
+    std::string all;
+    for (const auto &m : h->missing) all += m + "\n";
+    if (buf && cap > 0) snprintf(buf, static_cast<size_t>(cap), "%s", all.c_str());
+    return static_cast<int>(h->missing.size());
+}
+
+int sam3b200_hiera_run_prefix(sam3b200_hiera *hh, const float *img_chw_dev, float *x_dev) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !img_chw_dev || !x_dev || !h->patch_w32.p || !h->patch_b.p || !h->pe.p) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(h->be->device);
+    return run_prefix(h, img_chw_dev, x_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_hiera_run_block(sam3b200_hiera *hh, int i, const float *x_dev, int H, int W, float *out_dev) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !x_dev || !out_dev || i < 0 || i >= static_cast<int>(h->blk.size()) || H <= 0 || W <= 0 ||
+        (h->blk[i].q_stride && (H % 2 || W % 2)))
+        return SAM3B200_STATUS_FAILED;
+    // the activation buffers are sized for the model's own geometry
+    int Hs = h->S;
+    for (int j = 0; j < i; ++j)
+        if (h->blk[j].q_stride) Hs /= 2;
+    if (H * W > Hs * Hs) {
+        set_error("hiera_run_block: %dx%d exceeds the %dx%d map of block %d", H, W, Hs, Hs, i);
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(h->be->device);
+    return run_block(h, i, x_dev, H, W, out_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_hiera_encode_device(sam3b200_hiera *hh, const float *img_chw_dev) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !img_chw_dev) return SAM3B200_STATUS_FAILED;
+    cudaSetDevice(h->be->device);
+    if (!check_ready(h)) return SAM3B200_STATUS_FAILED;
+    return encode(h, img_chw_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_hiera_output(sam3b200_hiera *hh, int i, const float **dev, int64_t *ne) {
+    auto *h = reinterpret_cast<Hiera *>(hh);
+    if (!h || !dev || !ne || i < 0 || i > 7) return SAM3B200_STATUS_FAILED;
+    const int s = i & 3;
+    if (i < 4 && s >= h->n_fpn) {
+        *dev = nullptr;
+        return SAM3B200_STATUS_FAILED;
+    }
+    *dev = i < 4 ? h->fpn_out[s].as<float>() : h->stage_out[s].as<float>();
+    ne[0] = i < 4 ? h->hp.neck_dim : h->stage_dim[s];
+    ne[1] = h->stage_side[s];
+    ne[2] = h->stage_side[s];
+    ne[3] = 1;
+    return SAM3B200_STATUS_SUCCESS;
+}

@@ -260,6 +260,18 @@ __device__ __forceinline__ float gelu_erf_f(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
 }
 
+// ggml_gelu on the CPU backend (GGML_GELU_FP16, the Hiera MLP, sam3.cpp:4453):
+// 0 at x <= -10, x at x >= 10, else the fp16 table entry of the tanh form at
+// fp16(x): fp16(0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x^2)))).
+__device__ __forceinline__ float gelu_tanh_f16(float x) {
+    if (x <= -10.0f) return 0.0f;
+    if (x >= 10.0f) return x;
+    const float h = __half2float(__float2half_rn(x));
+    const float inner = __fmul_rn(__fmul_rn(0.79788456080286535587989211986876f, h),
+                                  __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, h), h)));
+    return __half2float(__float2half_rn(__fmul_rn(__fmul_rn(0.5f, h), __fadd_rn(1.0f, tanhf(inner)))));
+}
+
 __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
     return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
            ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
@@ -567,7 +579,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             float val = bias ? __fadd_rn(acc[hb + i], bias[nb + hb + i]) : acc[hb + i];
-                            if (ep.gelu) val = gelu_erf_f(val);
+                            if (ep.gelu == 1) val = gelu_erf_f(val);
+                            else if (ep.gelu == 2) val = gelu_tanh_f16(val);
                             acc[hb + i] = val;
                             amax = fmaxf(amax, fabsf(val));
                         }

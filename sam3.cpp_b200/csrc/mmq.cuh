@@ -57,7 +57,7 @@ struct MmqArgs {
     int *err;           // device error word (0 = ok)
     int add = 0;                    // MMQ_OUT_F32: y = y + (acc + bias)
     const int *rowmap = nullptr;    // MMQ_OUT_F32: output row of tile row m
-    int gelu = 0;                   // MMQ_OUT_Q8
+    int gelu = 0;                   // MMQ_OUT_Q8: 0 none, 1 GELU-erf, 2 ggml_gelu (tanh form, fp16 table)
     void *out_codes = nullptr;      // MMQ_OUT_Q8: int8 [M, N]
     void *out_quads = nullptr;      // MMQ_OUT_Q8: A-side records [ceil(N/256)][out_ld][16 B]
     int out_ld = 0;

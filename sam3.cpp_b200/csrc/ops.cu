@@ -168,6 +168,7 @@ int fail(const char *msg) {
 }
 
 }  // namespace
+
 }  // namespace b200
 
 using namespace b200;
