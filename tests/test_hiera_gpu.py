@@ -106,3 +106,28 @@ def test_hiera_rejects_unknown_tensor_and_missing(b200, backend):
             model.load({})  # nothing set: missing tensors reported
     finally:
         model.free()
+
+
+@pytest.mark.parametrize("i", [4, 5, 10])
+def test_block_matches_oracle_1024(oracle, hiera_oracle, backend, i):
+    """Stage-2 geometry of a 1024x1024 input: block 4 (14-token windows padded 64 -> 70), block 5
+    (global, 4096 tokens: the fp16 tensor-core score/softmax/PV path) and block 10 (Q-stride, padded
+    windows, cropped output)."""
+    hp = hiera_tiny(1024)
+    gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=21)
+    model = backend.hiera(hp)
+    try:
+        model.load(gpu)
+        blocks, _ = hiera_oracle.metadata(hp)
+        m = blocks[i]
+        S, So = 64, (32 if m["q_stride"] else 64)
+        x = np.random.default_rng(200 + i).normal(0, 1, size=(S, S, m["dim_in"])).astype(np.float32)
+        out = backend.alloc(So * So * m["dim_out"] * 4)
+        model.run_block(i, backend.upload(x), S, S, out)
+        backend.synchronize()
+        p = f"hiera.blocks.{i}."
+        want = hiera_oracle.block(m, {k[len(p):]: v for k, v in ref.items() if k.startswith(p)}, x)
+        err = rel_err(out.get((So, So, m["dim_out"]), np.float32), want)
+        assert err <= 1e-2, (i, err)
+    finally:
+        model.free()
