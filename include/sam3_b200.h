@@ -141,12 +141,29 @@ int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
  * batch).  q, k, v: device f32 ggml tensors [D, N, heads, batch], contiguous
  * (memory [batch][heads][N][D]); dst: device f32 [D, heads, N, batch]
  * (memory [batch][N][heads][D]), the layout ggml_flash_attn_ext returns.
- * Supported: D == 64, N a multiple of 8, self-attention (same N for q and
- * k/v); other shapes fail with an error message.  Computed on the tensor
- * cores with bf16 q, k, v and fp32 softmax/accumulation (within 1e-2 of the
- * f32 reference).  Asynchronous on the backend stream. */
+ * D == 64 with N a multiple of 8 runs on the tensor cores (bf16 q, k, v,
+ * fp32 softmax and accumulation: within 1e-2 of the f32 reference); the other
+ * head dimensions of sam3b200_flash_attn_ext_view run in fp32.  Asynchronous
+ * on the backend stream. */
 int sam3b200_flash_attn_ext(sam3b200_backend *be, const float *q, const float *k, const float *v, int64_t D,
                             int64_t N, int64_t heads, int64_t batch, float scale, float *dst);
+
+/* GGML_OP_FLASH_ATTN_EXT in the general form sam3.cpp builds (max_bias 0,
+ * softcap 0): q [D, NQ, heads, batch], k and v [D, NKV, heads, batch] given by
+ * their ggml strides in ELEMENTS, nb[0..2] = (nb1, nb2, nb3) / sizeof(float)
+ * (token, head, batch; the D elements of one token are contiguous) -- so the
+ * permuted V view of sam3.cpp:3767 is passed as it is; mask_f16: NULL or the
+ * F16 mask [NKV, >= NQ] with row stride mask_nb1 elements, added to every
+ * head's scores (the text encoder's causal mask, sam3.cpp:3934-3951); a -inf
+ * entry removes the key, a row with every key removed yields zeros.  dst: f32
+ * [D, heads, NQ, batch] contiguous.  D in {16, 32, 48, 56, 64, 72, 96, 112,
+ * 128, 256}.  Contiguous unmasked self-attention with D == 64 and NQ a
+ * multiple of 8 takes the tensor-core path; every other form runs in fp32 on
+ * the CUDA cores.  Asynchronous on the backend stream. */
+int sam3b200_flash_attn_ext_view(sam3b200_backend *be, const float *q, const float *k, const float *v,
+                                 const void *mask_f16, int64_t mask_nb1, int64_t D, int64_t NQ, int64_t NKV,
+                                 int64_t heads, int64_t batch, const int64_t q_nb[3], const int64_t k_nb[3],
+                                 const int64_t v_nb[3], float scale, float *dst);
 
 /* GGML_OP_CONV_TRANSPOSE_2D as ggml_conv_transpose_2d_p0 builds it
  * (sam3.cpp:3884,3887,3898 neck; :10654,10673 mask decoder): no padding, any

@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
         "sam3b200_preprocess": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_preprocess_sam2": (i32, [vp, vp, i32, i32, i32, vp]),
         "sam3b200_flash_attn_ext": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, ctypes.c_float, vp]),
+        "sam3b200_flash_attn_ext_view": (i32, [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp,
+                                                ctypes.c_float, vp]),
         "sam3b200_conv_transpose_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, vp]),
         "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
@@ -380,6 +382,15 @@ class Backend:
         """GGML_OP_FLASH_ATTN_EXT (sam3.cpp:3778): f32 [D, N, heads, batch] in, [D, heads, N, batch] out."""
         _check(lib().sam3b200_flash_attn_ext(self.h, q.ptr, k.ptr, v.ptr, D, N, heads, batch, scale, dst.ptr),
                "flash_attn_ext")
+
+    def flash_attn_ext_view(self, q: int, k: int, v: int, mask: int | None, mask_nb1: int, D: int, NQ: int,
+                            NKV: int, heads: int, batch: int, q_nb, k_nb, v_nb, scale: float, dst: DeviceBuffer) -> None:
+        """General GGML_OP_FLASH_ATTN_EXT: q, k, v, mask are device addresses (views allowed); *_nb are the
+        element strides (token, head, batch); dst f32 [D, heads, NQ, batch]."""
+        arr = lambda nb: (ctypes.c_int64 * 3)(*[int(x) for x in nb])
+        _check(lib().sam3b200_flash_attn_ext_view(self.h, q, k, v, mask, mask_nb1, D, NQ, NKV, heads, batch,
+                                                  arr(q_nb), arr(k_nb), arr(v_nb), scale, dst.ptr),
+               "flash_attn_ext_view")
 
     def conv_transpose_2d(self, w: DeviceBuffer, x: DeviceBuffer, iw: int, ih: int, ic: int, oc: int, kw: int,
                           kh: int, stride: int, dst: DeviceBuffer) -> None:

@@ -570,37 +570,6 @@ int sam3b200_preprocess_sam2(sam3b200_backend *hb, const uint8_t *rgb_dev, int w
     return preprocess_common(hb, rgb_dev, w, h, img, out_dev, true);
 }
 
-int sam3b200_flash_attn_ext(sam3b200_backend *hb, const float *q, const float *k, const float *v, int64_t D,
-                            int64_t N, int64_t heads, int64_t batch, float scale, float *dst) {
-    auto *be = reinterpret_cast<Backend *>(hb);
-    if (!be || !q || !k || !v || !dst) {
-        set_error("flash_attn_ext: null argument");
-        return SAM3B200_STATUS_FAILED;
-    }
-    if (D != 64 || N <= 0 || N % 8 != 0 || heads <= 0 || batch <= 0 || N > (1 << 20) || heads * batch > 65535) {
-        set_error("flash_attn_ext: unsupported shape D=%lld N=%lld heads=%lld batch=%lld (D = 64, N %% 8 == 0)",
-                  (long long)D, (long long)N, (long long)heads, (long long)batch);
-        return SAM3B200_STATUS_FAILED;
-    }
-    cudaSetDevice(be->device);
-    const int BH = static_cast<int>(heads * batch), Ni = static_cast<int>(N);
-    const size_t bytes = static_cast<size_t>(BH) * Ni * 64 * 2;
-    void *buf = nullptr;
-    if (!cuda_ok(cudaMallocAsync(&buf, 3 * bytes, be->stream), "cudaMallocAsync(attention inputs)"))
-        return SAM3B200_STATUS_ALLOC_FAILED;
-    char *qb = static_cast<char *>(buf);
-    AttnOut o;
-    o.f32 = dst;
-    be->count(2);
-    const bool ok = cuda_ok(attn_inputs_from_f32(q, k, v, BH, Ni, qb, qb + bytes, qb + 2 * bytes, be->stream),
-                            "attention inputs") &&
-                    cuda_ok(flash_attention(qb, qb + bytes, qb + 2 * bytes, static_cast<int>(batch), Ni,
-                                            static_cast<int>(heads), scale, o, be->err, be->stream),
-                            "flash_attn_ext");
-    cudaFreeAsync(buf, be->stream);
-    return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
-}
-
 int sam3b200_vit_run_prefix(sam3b200_vit *hv, const float *img_chw_dev, float *x_dev) {
     auto *v = reinterpret_cast<Vit *>(hv);
     if (!v || !img_chw_dev || !x_dev) return SAM3B200_STATUS_FAILED;

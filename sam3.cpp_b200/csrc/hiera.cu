@@ -10,14 +10,16 @@
 //             (sam2_window_partition: zero padding to a multiple of the window, window index
 //              wy + nWh * wx, token lx + ws * ly; global blocks keep the token order)
 //   q       = 2x2 max pool of q inside each window at a Q-stride block  qpool_kernel
-//   o       = softmax(q k^T / sqrt(hd)) v per (window, head)      hiera_attn_kernel
+//   o       = softmax(q k^T / sqrt(hd)) v per (window, head)      attention_simt / fp16 GEMMs
 //   x'      = shortcut + crop(unpartition(MUL_MAT(o) + bias))      unpart_add_kernel
 //   x'     += fc2(ggml_gelu(fc1(LN(x')))) (tanh GELU through ggml's fp16 table)
 // The four MUL_MATs of a block and the dimension projection run on the
-// tcgen05 MMQ kernel (exact int32 block dots, mmq.cu); the attention here is
-// a SIMT flash loop in fp32 for any head dimension multiple of 4 up to 128,
-// query/key counts of Q-pooled blocks and padded windows.
+// tcgen05 MMQ kernel (exact int32 block dots, mmq.cu); the windowed attention
+// is the general SIMT flash loop (attn_simt.cu: any head dimension, query/key
+// counts of Q-pooled blocks, padded windows), global attention two fp16
+// tensor-core GEMMs around a row softmax.
 #include "../../include/sam3_b200.h"
+#include "attn_simt.cuh"
 #include "gemm_f16.cuh"
 #include "model_util.h"
 #include "vit_ops.cuh"
@@ -138,103 +140,6 @@ __global__ void maxpool2_f32_kernel(const float *__restrict__ x, int H, int W, i
     const int xx = static_cast<int>(t % W2), yy = static_cast<int>(t / W2);
     const int64_t r0 = (static_cast<int64_t>(2 * yy) * W + 2 * xx) * C + c;
     y[i] = fmaxf(fmaxf(x[r0], x[r0 + C]), fmaxf(x[r0 + static_cast<int64_t>(W) * C], x[r0 + static_cast<int64_t>(W) * C + C]));
-}
-
-// softmax(q k^T * scale) v for every (window, head): 4 threads per query row,
-// DQ = hd / 4 dimensions each; 64-key tiles of k and v in shared memory;
-// online softmax in base 2.  q rows (window bw, token n): q + (bw*NQ + n) * q_ld
-// + h*hd; k, v likewise with NKV and kv_ld; o rows of o_ld (heads concatenated).
-template <int DQ>
-__global__ void __launch_bounds__(256) hiera_attn_kernel(const float *__restrict__ q, int64_t q_ld, int NQ,
-                                                         const float *__restrict__ k, const float *__restrict__ v,
-                                                         int64_t kv_ld, int NKV, int heads, float scale_log2,
-                                                         float *__restrict__ o, int64_t o_ld) {
-    constexpr int HD = 4 * DQ, KT = 64;
-    extern __shared__ float sm[];
-    float *ks = sm, *vs = sm + KT * HD;
-    const int bw = blockIdx.y / heads, h = blockIdx.y % heads;
-    const int row = blockIdx.x * 64 + (threadIdx.x >> 2), part = threadIdx.x & 3;
-    const bool valid = row < NQ;
-    float qv[DQ], acc[DQ];
-    const float *qr = q + (static_cast<int64_t>(bw) * NQ + (valid ? row : 0)) * q_ld + h * HD + part * DQ;
-#pragma unroll
-    for (int i = 0; i < DQ; ++i) {
-        qv[i] = valid ? qr[i] * scale_log2 : 0.f;
-        acc[i] = 0.f;
-    }
-    float m = -INFINITY, l = 0.f;
-    for (int j0 = 0; j0 < NKV; j0 += KT) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < KT * HD; e += blockDim.x) {
-            const int kk = e / HD, d = e % HD, key = j0 + kk;
-            float kv = 0.f, vv = 0.f;
-            if (key < NKV) {
-                const int64_t off = (static_cast<int64_t>(bw) * NKV + key) * kv_ld + h * HD + d;
-                kv = k[off];
-                vv = v[off];
-            }
-            ks[e] = kv;
-            vs[e] = vv;
-        }
-        __syncthreads();
-        const int nk = NKV - j0 < KT ? NKV - j0 : KT;
-        for (int kk = 0; kk < nk; ++kk) {
-            const float *kr = ks + kk * HD + part * DQ;
-            float s = 0.f;
-#pragma unroll
-            for (int i = 0; i < DQ; ++i) s = fmaf(qv[i], kr[i], s);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            if (s > m) {
-                const float alpha = exp2f(m - s);
-                l *= alpha;
-#pragma unroll
-                for (int i = 0; i < DQ; ++i) acc[i] *= alpha;
-                m = s;
-            }
-            const float p = exp2f(s - m);
-            l += p;
-            const float *vr = vs + kk * HD + part * DQ;
-#pragma unroll
-            for (int i = 0; i < DQ; ++i) acc[i] = fmaf(p, vr[i], acc[i]);
-        }
-    }
-    if (valid) {
-        const float inv = 1.0f / l;
-        float *orow = o + (static_cast<int64_t>(bw) * NQ + row) * o_ld + h * HD + part * DQ;
-#pragma unroll
-        for (int i = 0; i < DQ; ++i) orow[i] = acc[i] * inv;
-    }
-}
-
-template <int DQ>
-cudaError_t launch_attn(const float *q, int64_t q_ld, int NQ, const float *k, const float *v, int64_t kv_ld, int NKV,
-                        int Bw, int heads, float scale, float *o, int64_t o_ld, cudaStream_t s) {
-    const int smem = 2 * 64 * 4 * DQ * 4;
-    cudaError_t e = cudaFuncSetAttribute(hiera_attn_kernel<DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((NQ + 63) / 64, static_cast<unsigned>(Bw * heads));
-    hiera_attn_kernel<DQ><<<grid, 256, smem, s>>>(q, q_ld, NQ, k, v, kv_ld, NKV, heads, scale * 1.4426950408889634f, o,
-                                                  o_ld);
-    return cudaGetLastError();
-}
-
-cudaError_t hiera_attention(int hd, const float *q, int64_t q_ld, int NQ, const float *k, const float *v,
-                            int64_t kv_ld, int NKV, int Bw, int heads, float scale, float *o, int64_t o_ld,
-                            cudaStream_t s) {
-    if (NQ <= 0 || NKV <= 0 || Bw <= 0 || heads <= 0 || static_cast<int64_t>(Bw) * heads > 65535)
-        return cudaErrorInvalidValue;
-    switch (hd) {
-    case 32: return launch_attn<8>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 48: return launch_attn<12>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 56: return launch_attn<14>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 64: return launch_attn<16>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 72: return launch_attn<18>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 96: return launch_attn<24>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 112: return launch_attn<28>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    case 128: return launch_attn<32>(q, q_ld, NQ, k, v, kv_ld, NKV, Bw, heads, scale, o, o_ld, s);
-    default: return cudaErrorInvalidValue;
-    }
 }
 
 // x_out[t] = shortcut[t] + proj[row(t)] over the H x W output map: the window
@@ -525,7 +430,7 @@ BlockGeo block_geo(const HBlock &b, int H, int W) {
 }
 
 // Global blocks with long sequences run their attention as two fp16
-// tensor-core GEMMs around a row softmax (the windows stay on hiera_attn_kernel).
+// tensor-core GEMMs around a row softmax (the windows stay on attention_simt).
 bool global_on_tensor_cores(const HBlock &b, const BlockGeo &g) {
     const int hd = b.dim_out / b.heads;
     return b.ws == 0 && g.N >= 512 && g.N % 8 == 0 && hd % 8 == 0;
@@ -707,11 +612,15 @@ bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
             go.err = h->be->err;
             if (!hlaunched(h, gemm_f16(go, h->be->num_sms, s), "hiera global pv")) return false;
         }
-    } else if (!hlaunched(h,
-                          hiera_attention(hd, qptr, q_ld, g.NQ, h->qkv.as<float>() + Co, h->qkv.as<float>() + 2 * Co,
-                                          3 * Co, g.N, g.Bw, b.heads, scale, h->attn.as<float>(), Co, s),
-                          "hiera attention")) {
-        return false;
+    } else {
+        const AttnStrides qs{static_cast<int64_t>(g.NQ) * q_ld, hd, q_ld};
+        const AttnStrides kvs{static_cast<int64_t>(g.N) * 3 * Co, hd, 3 * Co};
+        const AttnStrides os{static_cast<int64_t>(g.NQ) * Co, hd, Co};
+        if (!hlaunched(h,
+                       attention_simt(hd, qptr, qs, g.NQ, h->qkv.as<float>() + Co, kvs, h->qkv.as<float>() + 2 * Co, kvs,
+                                      g.N, g.Bw, b.heads, nullptr, 0, scale, h->attn.as<float>(), os, s),
+                       "hiera attention"))
+            return false;
     }
     // 6. output projection
     if (!hlaunched(h, quantize_rows_q8(h->attn.as<float>(), Co, rq, Co, h->codes_a.p, h->quads_a.p, round128(rq), s),

@@ -1,7 +1,12 @@
-// ops.cu -- op-level entry points of the drop-in boundary besides MUL_MAT and
-// FLASH_ATTN_EXT: the convolutions and the row gather that sam3.cpp's graphs
+// ops.cu -- op-level entry points of the drop-in boundary besides MUL_MAT:
+// the attention, the convolutions and the row gather that sam3.cpp's graphs
 // dispatch to the backend.
 //
+//   GGML_OP_FLASH_ATTN_EXT     contiguous self-attention with head dim 64 and N
+//                              a multiple of 8 on the tcgen05 kernel (attn.cu,
+//                              bf16 operands); every other form -- head dims 16
+//                              to 256, different query/key counts, strided views,
+//                              an F16 mask -- on the fp32 loop of attn_simt.cu.
 //   GGML_OP_CONV_TRANSPOSE_2D  ggml_conv_transpose_2d_p0 (sam3.cpp:3884,3887,
 //                              3898, 10654, 10673): F16 kernel [KW,KH,OC,IC],
 //                              F32 input [W,H,IC,1], no padding, any stride.
@@ -25,8 +30,11 @@
 //   conv_2d:           im2col[p][(ic, ky, kx)] (fp16, K padded to 8), then
 //                      out[oc][p] = sum_k W[oc][k] * im2col[p][k] (GEMM M = OC,
 //                      N = OH*OW) -- the output is ggml's [OW, OH, OC] layout.
+#include "attn.cuh"
+#include "attn_simt.cuh"
 #include "backend_impl.h"
 #include "gemm_f16.cuh"
+#include "vit_ops.cuh"
 #include "../../include/sam3_b200.h"
 #include <cuda_fp16.h>
 
@@ -300,4 +308,58 @@ int sam3b200_get_rows(sam3b200_backend *hb, int type, const void *src, int64_t n
                                                                        nrows, row_bytes, idx, dst, be->err);
     be->count(1);
     return cuda_ok(cudaGetLastError(), "get_rows") ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_flash_attn_ext(sam3b200_backend *hb, const float *q, const float *k, const float *v, int64_t D,
+                            int64_t N, int64_t heads, int64_t batch, float scale, float *dst) {
+    const int64_t nb[3] = {D, N * D, heads * N * D};
+    return sam3b200_flash_attn_ext_view(hb, q, k, v, nullptr, 0, D, N, N, heads, batch, nb, nb, nb, scale, dst);
+}
+
+int sam3b200_flash_attn_ext_view(sam3b200_backend *hb, const float *q, const float *k, const float *v,
+                                 const void *mask_f16, int64_t mask_nb1, int64_t D, int64_t NQ, int64_t NKV,
+                                 int64_t heads, int64_t batch, const int64_t q_nb[3], const int64_t k_nb[3],
+                                 const int64_t v_nb[3], float scale, float *dst) {
+    auto *be = reinterpret_cast<Backend *>(hb);
+    if (!be || !q || !k || !v || !dst || !q_nb || !k_nb || !v_nb) return fail("flash_attn_ext: null argument");
+    const bool dims_ok = (D == 16 || D == 32 || D == 48 || D == 56 || D == 64 || D == 72 || D == 96 || D == 112 ||
+                          D == 128 || D == 256);
+    if (!dims_ok || NQ <= 0 || NKV <= 0 || heads <= 0 || batch <= 0 || NQ > (1 << 24) || NKV > (1 << 24) ||
+        heads * batch > 65535 || (mask_f16 && mask_nb1 < NKV)) {
+        set_error("flash_attn_ext: unsupported shape D=%lld NQ=%lld NKV=%lld heads=%lld batch=%lld (D in {16, 32, 48, "
+                  "56, 64, 72, 96, 112, 128, 256})",
+                  (long long)D, (long long)NQ, (long long)NKV, (long long)heads, (long long)batch);
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(be->device);
+    auto contiguous = [&](const int64_t *nb, int64_t n) { return nb[0] == D && nb[1] == n * D && nb[2] == heads * n * D; };
+    const AttnStrides os{NQ * heads * D, D, heads * D};  // dst [D, heads, NQ, batch]
+    if (D == 64 && !mask_f16 && NQ == NKV && NQ % 8 == 0 && contiguous(q_nb, NQ) && contiguous(k_nb, NKV) &&
+        contiguous(v_nb, NKV)) {
+        // tensor cores: bf16 q, k and v^T staged from the f32 tensors
+        const int BH = static_cast<int>(heads * batch), Ni = static_cast<int>(NQ);
+        const size_t bytes = static_cast<size_t>(BH) * Ni * 64 * 2;
+        void *buf = nullptr;
+        if (!cuda_ok(cudaMallocAsync(&buf, 3 * bytes, be->stream), "cudaMallocAsync(attention inputs)"))
+            return SAM3B200_STATUS_ALLOC_FAILED;
+        char *qb = static_cast<char *>(buf);
+        AttnOut o;
+        o.f32 = dst;
+        be->count(2);
+        const bool ok = cuda_ok(attn_inputs_from_f32(q, k, v, BH, Ni, qb, qb + bytes, qb + 2 * bytes, be->stream),
+                                "attention inputs") &&
+                        cuda_ok(flash_attention(qb, qb + bytes, qb + 2 * bytes, static_cast<int>(batch), Ni,
+                                                static_cast<int>(heads), scale, o, be->err, be->stream),
+                                "flash_attn_ext");
+        cudaFreeAsync(buf, be->stream);
+        return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+    }
+    be->count(1);
+    const AttnStrides qs{q_nb[2], q_nb[1], q_nb[0]}, ks{k_nb[2], k_nb[1], k_nb[0]}, vs{v_nb[2], v_nb[1], v_nb[0]};
+    return cuda_ok(attention_simt(static_cast<int>(D), q, qs, static_cast<int>(NQ), k, ks, v, vs,
+                                  static_cast<int>(NKV), static_cast<int>(batch), static_cast<int>(heads),
+                                  static_cast<const __half *>(mask_f16), mask_nb1, scale, dst, os, be->stream),
+                   "flash_attn_ext")
+               ? SAM3B200_STATUS_SUCCESS
+               : SAM3B200_STATUS_FAILED;
 }

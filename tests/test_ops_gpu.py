@@ -3,6 +3,8 @@ graphs dispatch besides MUL_MAT), through the C ABI, against the oracle."""
 import numpy as np
 import pytest
 
+from conftest import rel_err
+
 pytestmark = pytest.mark.gpu
 
 
@@ -25,9 +27,7 @@ def test_flash_attn_ext_matches_oracle(oracle, backend, batch, heads, N):
 def test_flash_attn_ext_rejects_unsupported(b200, backend):
     buf = backend.alloc(4096)
     with pytest.raises(b200.B200Error):
-        backend.flash_attn_ext(buf, buf, buf, 128, 8, 1, 1, 0.1, buf)  # head dim 128
-    with pytest.raises(b200.B200Error):
-        backend.flash_attn_ext(buf, buf, buf, 64, 12, 1, 1, 0.1, buf)  # N not a multiple of 8
+        backend.flash_attn_ext(buf, buf, buf, 80, 8, 1, 1, 0.1, buf)  # head dim 80
 
 
 # GGML_OP_CONV_TRANSPOSE_2D: the case table of the reference's own CPU-vs-Metal test
@@ -134,3 +134,72 @@ def test_conv_rejects_bad_shapes(b200, backend):
         backend.conv_transpose_2d(buf, buf, 0, 4, 1, 1, 2, 2, 2, buf)
     with pytest.raises(b200.B200Error):
         backend.get_rows(8, buf, 48, 4, buf, 1, buf)  # Q8_0 rows need a multiple of 32 columns
+
+
+def _contig_nb(D, N, H):
+    return (D, N * D, H * N * D)
+
+
+@pytest.mark.parametrize("D,NQ,NKV,H,B", [(16, 40, 56, 8, 2), (32, 64, 64, 4, 1), (96, 49, 196, 2, 3),
+                                          (256, 33, 70, 1, 2), (64, 24, 100, 2, 1)])
+def test_flash_attn_ext_general_shapes(oracle, backend, D, NQ, NKV, H, B):
+    """Head dims of the SAM decoder (16), Hiera (96) and memory attention (256); cross-attention shapes."""
+    rng = np.random.default_rng(D + NQ + NKV)
+    q = rng.normal(0, 1, size=(B, H, NQ, D)).astype(np.float32)
+    k = rng.normal(0, 1, size=(B, H, NKV, D)).astype(np.float32)
+    v = rng.normal(0, 1, size=(B, H, NKV, D)).astype(np.float32)
+    scale = 1.0 / np.sqrt(D)
+    dq, dk, dv = backend.upload(q), backend.upload(k), backend.upload(v)
+    out = backend.alloc(B * NQ * H * D * 4)
+    backend.flash_attn_ext_view(dq.ptr, dk.ptr, dv.ptr, None, 0, D, NQ, NKV, H, B, _contig_nb(D, NQ, H),
+                                _contig_nb(D, NKV, H), _contig_nb(D, NKV, H), scale, out)
+    backend.synchronize()
+    ref = oracle.attention_general(q, k, v, scale)
+    assert rel_err(out.get(ref.shape, np.float32), ref) <= 1e-4  # fp32 path
+
+
+def test_flash_attn_ext_causal_mask_and_dead_row(oracle, backend):
+    """The text encoder's causal F16 mask (sam3.cpp:3934-3951), padded rows, and a row whose keys are all
+    masked (zeros)."""
+    D, N, H, B, ld = 64, 32, 4, 2, 40
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.normal(0, 1, size=(B, H, N, D)).astype(np.float32) for _ in range(3))
+    mask = np.zeros((N, ld), np.float16)
+    mask[np.triu_indices(N, 1)] = -np.inf
+    mask[5, :] = -np.inf  # every key of query row 5 removed
+    out = backend.alloc(B * N * H * D * 4)
+    dq, dk, dv, dm = backend.upload(q), backend.upload(k), backend.upload(v), backend.upload(mask)  # kept alive
+    backend.flash_attn_ext_view(dq.ptr, dk.ptr, dv.ptr, dm.ptr, ld, D, N, N, H, B, _contig_nb(D, N, H),
+                                _contig_nb(D, N, H), _contig_nb(D, N, H), 0.125, out)
+    backend.synchronize()
+    got = out.get((B, N, H, D), np.float32)
+    ref = oracle.attention_general(q, k, v, 0.125, mask[:, :N].astype(np.float32))
+    assert np.all(got[:, 5] == 0)
+    assert rel_err(got, ref) <= 1e-4
+
+
+def test_flash_attn_ext_permuted_views(oracle, backend):
+    """q, k, v as strided views into one qkv tensor ([3*H*D, N, B] memory, as the ViT's qkv projection
+    output is split at sam3.cpp:3747-3767), passed with their ggml strides."""
+    D, N, H, B = 64, 50, 3, 2
+    rng = np.random.default_rng(4)
+    qkv = rng.normal(0, 1, size=(B, N, 3, H, D)).astype(np.float32)
+    d = backend.upload(qkv)
+    nb = (3 * H * D, D, N * 3 * H * D)  # token, head, batch
+    base = d.ptr
+    out = backend.alloc(B * N * H * D * 4)
+    backend.flash_attn_ext_view(base, base + H * D * 4, base + 2 * H * D * 4, None, 0, D, N, N, H, B, nb, nb, nb,
+                                0.125, out)
+    backend.synchronize()
+    q, k, v = (qkv[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    ref = oracle.attention_general(q, k, v, 0.125)
+    assert rel_err(out.get(ref.shape, np.float32), ref) <= 1e-4
+
+
+def test_flash_attn_ext_view_rejects(b200, backend):
+    buf = backend.alloc(4096)
+    nb = (24, 24, 24)
+    with pytest.raises(b200.B200Error):
+        backend.flash_attn_ext_view(buf.ptr, buf.ptr, buf.ptr, None, 0, 24, 1, 1, 1, 1, nb, nb, nb, 0.1, buf)
+    with pytest.raises(b200.B200Error):  # mask rows shorter than the key count
+        backend.flash_attn_ext_view(buf.ptr, buf.ptr, buf.ptr, buf.ptr, 4, 16, 2, 8, 1, 1, nb, nb, nb, 0.1, buf)
