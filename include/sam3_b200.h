@@ -242,6 +242,47 @@ int sam3b200_hiera_encode_device(sam3b200_hiera *h, const float *img_chw_dev);
  * i = 4..7 stage outputs [dim, W, H, 1]; token-major device f32. */
 int sam3b200_hiera_output(sam3b200_hiera *h, int i, const float **dev, int64_t ne[4]);
 
+/* ---- SAM prompt encoder + mask decoder (PVS, sam3_segment_pvs) -----------
+ * The graph of sam3.cpp:10765-11115 (decoder sam3_build_sam_dec_graph
+ * :10548-10763) on the B200.  Inputs are the encoder's three finest maps in
+ * token-major device f32: image features [H*H][256] (neck / FPN level 2),
+ * feat_s0 [(4H)^2][256] and feat_s1 [(2H)^2][256] (levels 0 and 1).  Weights
+ * by their weight-file names (sam3.cpp:1854-1968): "sam_pe.*", "sam_dec.*",
+ * "no_mem_embed". */
+typedef struct {
+    int32_t feat_size;        /* H: 64 for SAM2 at 1024, 72 for SAM3 at 1008 */
+    int32_t embed;            /* 256 */
+    int32_t depth;            /* two-way blocks, 2 */
+    int32_t heads;            /* 8 */
+    int32_t mlp_dim;          /* 2048 */
+    int32_t n_multimask;      /* 3: four mask tokens */
+    int32_t pred_obj_scores;  /* 1: object-score token and head */
+    int32_t max_points;       /* prompt token capacity including the padding token (<= 64) */
+} sam3b200_sam_dec_hparams;
+
+typedef struct sam3b200_sam_dec sam3b200_sam_dec;
+
+sam3b200_sam_dec *sam3b200_sam_dec_create(sam3b200_backend *be, const sam3b200_sam_dec_hparams *hp);
+void sam3b200_sam_dec_free(sam3b200_sam_dec *d);
+int sam3b200_sam_dec_set_tensor(sam3b200_sam_dec *d, const char *name, int type, const void *data,
+                                const int64_t ne[4]);
+int sam3b200_sam_dec_missing(sam3b200_sam_dec *d, char *buf, int cap);
+/* One PVS decode: prompts in original-image pixels (coords x, y pairs; labels
+ * 1 positive, 0 negative, 2 / 3 box corners, in the reference's order: box
+ * corners, positive, negative; the padding token is appended here),
+ * orig_w x orig_h the original image, img_size the encoder input side.
+ * Synchronous (reads back the IoU and object scores). */
+int sam3b200_sam_dec_run(sam3b200_sam_dec *d, const float *img_feats_dev, const float *feat_s0_dev,
+                         const float *feat_s1_dev, const float *coords, const int32_t *labels, int n_prompts,
+                         int orig_w, int orig_h, int img_size);
+/* Results of the last run: mask logits [n_multimask + 1][(4H)^2] (device),
+ * IoU predictions, object-score logit, SAM output token [256] (device). */
+int sam3b200_sam_dec_outputs(sam3b200_sam_dec *d, const float **masks_dev, float iou[4], float *obj_logit,
+                             const float **sam_token_dev);
+/* Mask m resized to out_w x out_h (bilinear, sam3.cpp:9617-9643) and
+ * binarised at logit 0 (:11071-11075): dst_dev uint8 [out_h][out_w], 255 / 0. */
+int sam3b200_sam_dec_mask(sam3b200_sam_dec *d, int m, int out_w, int out_h, uint8_t *dst_dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

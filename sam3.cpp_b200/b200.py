@@ -82,6 +82,14 @@ def lib() -> ctypes.CDLL:
         "sam3b200_conv_transpose_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, vp]),
         "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
+        "sam3b200_sam_dec_create": (vp, [vp, vp]),
+        "sam3b200_sam_dec_free": (None, [vp]),
+        "sam3b200_sam_dec_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_sam_dec_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_sam_dec_run": (i32, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32]),
+        "sam3b200_sam_dec_outputs": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), vp, vp,
+                                           ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_sam_dec_mask": (i32, [vp, i32, i32, i32, vp]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -323,6 +331,69 @@ class Hiera:
             self.h = None
 
 
+class SamDecHparams(ctypes.Structure):
+    """sam3b200_sam_dec_hparams (include/sam3_b200.h)."""
+    _fields_ = [(k, ctypes.c_int32) for k in ("feat_size", "embed", "depth", "heads", "mlp_dim", "n_multimask",
+                                              "pred_obj_scores", "max_points")]
+
+
+class SamDecoder:
+    """SAM prompt encoder + mask decoder (sam3b200_sam_dec) on a backend."""
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = SamDecHparams(*[int(hp[k]) for k, _ in SamDecHparams._fields_])
+        self.h = lib().sam3b200_sam_dec_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"sam_dec_create failed: {last_error()}")
+
+    def set_tensor(self, name: str, ttype: int, data: np.ndarray, ne) -> None:
+        data = np.ascontiguousarray(data)
+        ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+        _check(lib().sam3b200_sam_dec_set_tensor(self.h, name.encode(), ttype, data.ctypes.data, ne4), f"set {name}")
+
+    def load(self, tensors: dict) -> None:
+        for name, (t, arr, ne) in tensors.items():
+            self.set_tensor(name, t, arr, ne)
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_sam_dec_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} decoder tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, img_feats: int, feat_s0: int, feat_s1: int, coords, labels, orig_w: int, orig_h: int,
+            img_size: int) -> None:
+        """Device addresses of the three feature maps; prompts in original-image pixels."""
+        c = np.ascontiguousarray(coords, np.float32).reshape(-1)
+        lab = np.ascontiguousarray(labels, np.int32)
+        _check(lib().sam3b200_sam_dec_run(self.h, img_feats, feat_s0, feat_s1, c.ctypes.data, lab.ctypes.data,
+                                          lab.size, orig_w, orig_h, img_size), "sam_dec_run")
+
+    def outputs(self) -> tuple:
+        """(mask logits [n][4H][4H], iou [4], obj logit, sam token [256]) on the host."""
+        mp, tp = ctypes.c_void_p(), ctypes.c_void_p()
+        iou = (ctypes.c_float * 4)()
+        obj = ctypes.c_float()
+        _check(lib().sam3b200_sam_dec_outputs(self.h, ctypes.byref(mp), iou, ctypes.byref(obj), ctypes.byref(tp)),
+               "sam_dec_outputs")
+        S, n = 4 * self.hp["feat_size"], self.hp["n_multimask"] + 1
+        masks = np.empty((n, S, S), np.float32)
+        tok = np.empty(self.hp["embed"], np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, mp.value, masks.ctypes.data, 0, masks.nbytes), "tensor_get")
+        _check(lib().sam3b200_tensor_get(self.be.h, tp.value, tok.ctypes.data, 0, tok.nbytes), "tensor_get")
+        return masks, np.array(iou[:n], np.float32), obj.value, tok
+
+    def mask(self, m: int, out_w: int, out_h: int) -> np.ndarray:
+        buf = DeviceBuffer(self.be, out_w * out_h)
+        _check(lib().sam3b200_sam_dec_mask(self.h, m, out_w, out_h, buf.ptr), "sam_dec_mask")
+        self.be.synchronize()
+        return buf.get((out_h, out_w), np.uint8)
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_sam_dec_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -432,6 +503,9 @@ class Backend:
 
     def hiera(self, hp: dict) -> Hiera:
         return Hiera(self, hp)
+
+    def sam_decoder(self, hp: dict) -> SamDecoder:
+        return SamDecoder(self, hp)
 
     def free(self) -> None:
         if self.h:

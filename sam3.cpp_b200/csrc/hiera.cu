@@ -22,6 +22,7 @@
 #include "attn_simt.cuh"
 #include "gemm_f16.cuh"
 #include "model_util.h"
+#include "row_norm.cuh"
 #include "vit_ops.cuh"
 
 #include <algorithm>
@@ -33,35 +34,6 @@
 
 namespace b200 {
 namespace {
-
-__device__ __forceinline__ double hwarp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// ggml_norm + ggml_mul + ggml_add over each row, f32 out (one warp per row)
-__global__ void ln_rows_kernel(const float *__restrict__ x, int rows, int E, const float *__restrict__ w,
-                               const float *__restrict__ b, float eps, float *__restrict__ y) {
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (t >= rows) return;
-    const float *xr = x + static_cast<int64_t>(t) * E;
-    double s = 0.0;
-    for (int c = lane; c < E; c += 32) s += static_cast<double>(xr[c]);
-    s = hwarp_sum_d(s);
-    const float mean = static_cast<float>(s / E);
-    double s2 = 0.0;
-    for (int c = lane; c < E; c += 32) {
-        const float d = __fsub_rn(xr[c], mean);
-        s2 += static_cast<double>(__fmul_rn(d, d));
-    }
-    s2 = hwarp_sum_d(s2);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(s2 / E), eps)));
-    float *yr = y + static_cast<int64_t>(t) * E;
-    for (int c = lane; c < E; c += 32)
-        yr[c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[c], mean), scale), w[c]), b[c]);
-}
 
 // Quantise one 32-wide block (ggml-cpu activation rule) and store codes + scale record.
 __device__ __forceinline__ void q8_block_store(const float (&v)[32], int8_t *codes, __half *quads, int blk, int64_t r,
