@@ -200,6 +200,14 @@ def get_rows(qtype: int, rows: np.ndarray, ncols: int, idx: np.ndarray) -> np.nd
     return dequantize(qtype, np.ascontiguousarray(rows.reshape(rows.shape[0], -1)[idx]), ncols)
 
 
+def preprocess_sam2(rgb: np.ndarray, img: int) -> np.ndarray:
+    """sam2_preprocess_image (sam3.cpp:3522-3548): uint8 HxWx3 -> ImageNet-normalised f32 [3][img][img]."""
+    rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
+    out = np.empty((3, img, img), np.float32)
+    _vit_lib().orc_preprocess_sam2(rgb.ctypes.data, rgb.shape[1], rgb.shape[0], img, out.ctypes.data)
+    return out
+
+
 # ---- SAM3 visual encoder restatement (vit_oracle.h) ------------------------
 
 class _Hp(ctypes.Structure):
@@ -301,11 +309,7 @@ class OracleVit:
         return out
 
     def preprocess_sam2(self, rgb: np.ndarray, img: int) -> np.ndarray:
-        """sam2_preprocess_image (sam3.cpp:3522-3548) to img x img."""
-        rgb = np.ascontiguousarray(rgb, dtype=np.uint8)
-        out = np.empty((3, img, img), np.float32)
-        _vit_lib().orc_preprocess_sam2(rgb.ctypes.data, rgb.shape[1], rgb.shape[0], img, out.ctypes.data)
-        return out
+        return preprocess_sam2(rgb, img)
 
     def prefix(self, img_chw: np.ndarray) -> np.ndarray:
         img_chw = np.ascontiguousarray(img_chw, dtype=np.float32)

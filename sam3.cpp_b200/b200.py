@@ -315,6 +315,13 @@ class Hiera:
     def encode_device(self, img_chw: "DeviceBuffer") -> None:
         _check(lib().sam3b200_hiera_encode_device(self.h, img_chw.ptr), "hiera_encode_device")
 
+    def output_ptr(self, i: int) -> int:
+        """Device address of output i (0..3 FPN levels, 4..7 stage outputs)."""
+        p = ctypes.c_void_p()
+        ne = (ctypes.c_int64 * 4)()
+        _check(lib().sam3b200_hiera_output(self.h, i, ctypes.byref(p), ne), "hiera_output")
+        return p.value
+
     def output_host(self, i: int) -> np.ndarray:
         """i = 0..3 FPN levels, 4..7 stage outputs: f32 [H, W, C]."""
         p = ctypes.c_void_p()
