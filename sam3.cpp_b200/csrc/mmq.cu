@@ -277,12 +277,124 @@ __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
            ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
+// Tile output of one epilogue thread: the COLS accumulators of tile row m for
+// output columns [nb, nb + COLS) -- bias, then the mode's epilogue (residual
+// add through the row map / GELU + Q8_0 re-quantisation / RoPE + head split).
+template <int MODE, int COLS>
+__device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS], int m, int M, int N, int nb) {
+    const float *__restrict__ bias = ep.bias;
+    if constexpr (MODE == MMQ_OUT_F32) {
+        if (m < M) {
+            const int r = ep.rowmap ? ep.rowmap[m] : m;
+            float *yr = ep.y + static_cast<int64_t>(r) * ep.ldy + nb;
+            const bool vec = ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0);
+#pragma unroll
+            for (int j = 0; j < COLS; j += 4) {
+                float o[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
+                if (vec && nb + j + 3 < N) {
+                    if (bias) {
+                        const float4 bb = *reinterpret_cast<const float4 *>(bias + nb + j);
+                        o[0] = __fadd_rn(o[0], bb.x);
+                        o[1] = __fadd_rn(o[1], bb.y);
+                        o[2] = __fadd_rn(o[2], bb.z);
+                        o[3] = __fadd_rn(o[3], bb.w);
+                    }
+                    if (ep.add) {
+                        const float4 prev = *reinterpret_cast<const float4 *>(yr + j);
+                        o[0] = __fadd_rn(prev.x, o[0]);
+                        o[1] = __fadd_rn(prev.y, o[1]);
+                        o[2] = __fadd_rn(prev.z, o[2]);
+                        o[3] = __fadd_rn(prev.w, o[3]);
+                    }
+                    *reinterpret_cast<float4 *>(yr + j) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    for (int e = 0; e < 4; ++e) {
+                        if (nb + j + e >= N) break;
+                        float val = bias ? __fadd_rn(o[e], bias[nb + j + e]) : o[e];
+                        if (ep.add) val = __fadd_rn(yr[j + e], val);
+                        yr[j + e] = val;
+                    }
+                }
+            }
+        }
+    } else if constexpr (MODE == MMQ_OUT_QKV) {
+        // this thread's COLS columns lie inside one 64-wide head of the q, k or v third
+        if (m < M) {
+            const int E = N / 3;
+            const int part = nb / E, c0 = nb - part * E, hd = c0 >> 6, d0 = c0 & 63;
+            const int win = m / ep.win_tokens, pos = m - win * ep.win_tokens;
+            const int64_t bh = static_cast<int64_t>(win) * ep.heads + hd;
+#pragma unroll
+            for (int i = 0; i < COLS; ++i)
+                if (bias) acc[i] = __fadd_rn(acc[i], bias[nb + i]);
+            if (part < 2) {
+                if (ep.freqs) {
+                    const float *fr = ep.freqs + (static_cast<int64_t>(pos) * 32 + (d0 >> 1)) * 2;
+#pragma unroll
+                    for (int i = 0; i < COLS; i += 2) {
+                        const float2 cs = *reinterpret_cast<const float2 *>(fr + i);
+                        const float x0 = acc[i], x1 = acc[i + 1];
+                        acc[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+                        acc[i + 1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+                    }
+                }
+                __nv_bfloat16 *dst = (part == 0 ? ep.q : ep.k) + (bh * ep.win_tokens + pos) * 64 + d0;
+#pragma unroll
+                for (int i = 0; i < COLS; i += 8) {
+                    uint4 u;
+                    uint32_t *uw = reinterpret_cast<uint32_t *>(&u);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[i + 2 * e], acc[i + 2 * e + 1]);
+                        uw[e] = *reinterpret_cast<const uint32_t *>(&p2);
+                    }
+                    *reinterpret_cast<uint4 *>(dst + i) = u;
+                }
+            } else {
+                // V^T: consecutive lanes hold consecutive tokens, so each store is 64 contiguous bytes
+                __nv_bfloat16 *dst = ep.vt + (bh * 64 + d0) * ep.win_tokens + pos;
+#pragma unroll
+                for (int i = 0; i < COLS; ++i) dst[static_cast<int64_t>(i) * ep.win_tokens] = __float2bfloat16_rn(acc[i]);
+            }
+        }
+    } else if constexpr (MODE == MMQ_OUT_Q8) {
+        // this thread's 64 columns are two whole 32-wide Q8_0 blocks of the output row
+        if (m < M) {
+#pragma unroll
+            for (int hb = 0; hb < COLS; hb += 32) {
+                if (nb + hb >= N) break;
+                float amax = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    float val = bias ? __fadd_rn(acc[hb + i], bias[nb + hb + i]) : acc[hb + i];
+                    if (ep.gelu == 1) val = gelu_erf_f(val);
+                    else if (ep.gelu == 2) val = gelu_tanh_f16(val);
+                    acc[hb + i] = val;
+                    amax = fmaxf(amax, fabsf(val));
+                }
+                const float d = __fdiv_rn(amax, 127.f);
+                const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    pk[i] = pack4_i8(__float2int_rn(__fmul_rn(acc[hb + 4 * i], id)),
+                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 1], id)),
+                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 2], id)),
+                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 3], id)));
+                uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
+                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                ep.qquads[act_quad_index((nb + hb) >> 5, m, ep.qld)] = __float2half_rn(d);
+            }
+        }
+    }
+}
+
 template <int MODE, int CVT, int BN, int EPQ>
 __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
                   int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err) {
-    const float *__restrict__ bias = ep.bias;
     int32_t *__restrict__ dump = ep.dump;
     using C = TcCfg<BN, EPQ>;
     extern __shared__ uint8_t smem_raw[];
@@ -492,114 +604,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                 ++blk;
             }
             if (!ok) break;
-            if constexpr (MODE == MMQ_OUT_F32) {
-                if (m < M) {
-                    const int nb = n0 + h * C::COLS;
-                    const int r = ep.rowmap ? ep.rowmap[m] : m;
-                    float *yr = ep.y + static_cast<int64_t>(r) * ep.ldy + nb;
-                    const bool vec = ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0);
-#pragma unroll
-                    for (int j = 0; j < C::COLS; j += 4) {
-                        float o[4] = {acc[j], acc[j + 1], acc[j + 2], acc[j + 3]};
-                        if (vec && nb + j + 3 < N) {
-                            if (bias) {
-                                const float4 bb = *reinterpret_cast<const float4 *>(bias + nb + j);
-                                o[0] = __fadd_rn(o[0], bb.x);
-                                o[1] = __fadd_rn(o[1], bb.y);
-                                o[2] = __fadd_rn(o[2], bb.z);
-                                o[3] = __fadd_rn(o[3], bb.w);
-                            }
-                            if (ep.add) {
-                                const float4 prev = *reinterpret_cast<const float4 *>(yr + j);
-                                o[0] = __fadd_rn(prev.x, o[0]);
-                                o[1] = __fadd_rn(prev.y, o[1]);
-                                o[2] = __fadd_rn(prev.z, o[2]);
-                                o[3] = __fadd_rn(prev.w, o[3]);
-                            }
-                            *reinterpret_cast<float4 *>(yr + j) = make_float4(o[0], o[1], o[2], o[3]);
-                        } else {
-                            for (int e = 0; e < 4; ++e) {
-                                if (nb + j + e >= N) break;
-                                float val = bias ? __fadd_rn(o[e], bias[nb + j + e]) : o[e];
-                                if (ep.add) val = __fadd_rn(yr[j + e], val);
-                                yr[j + e] = val;
-                            }
-                        }
-                    }
-                }
-            } else if constexpr (MODE == MMQ_OUT_QKV) {
-                // this thread's COLS columns lie inside one 64-wide head of the q, k or v third
-                if (m < M) {
-                    const int nb = n0 + h * C::COLS;
-                    const int E = N / 3;
-                    const int part = nb / E, c0 = nb - part * E, hd = c0 >> 6, d0 = c0 & 63;
-                    const int win = m / ep.win_tokens, pos = m - win * ep.win_tokens;
-                    const int64_t bh = static_cast<int64_t>(win) * ep.heads + hd;
-#pragma unroll
-                    for (int i = 0; i < C::COLS; ++i)
-                        if (bias) acc[i] = __fadd_rn(acc[i], bias[nb + i]);
-                    if (part < 2) {
-                        if (ep.freqs) {
-                            const float *fr = ep.freqs + (static_cast<int64_t>(pos) * 32 + (d0 >> 1)) * 2;
-#pragma unroll
-                            for (int i = 0; i < C::COLS; i += 2) {
-                                const float2 cs = *reinterpret_cast<const float2 *>(fr + i);
-                                const float x0 = acc[i], x1 = acc[i + 1];
-                                acc[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-                                acc[i + 1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-                            }
-                        }
-                        __nv_bfloat16 *dst = (part == 0 ? ep.q : ep.k) + (bh * ep.win_tokens + pos) * 64 + d0;
-#pragma unroll
-                        for (int i = 0; i < C::COLS; i += 8) {
-                            uint4 u;
-                            uint32_t *uw = reinterpret_cast<uint32_t *>(&u);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const __nv_bfloat162 p2 = __floats2bfloat162_rn(acc[i + 2 * e], acc[i + 2 * e + 1]);
-                                uw[e] = *reinterpret_cast<const uint32_t *>(&p2);
-                            }
-                            *reinterpret_cast<uint4 *>(dst + i) = u;
-                        }
-                    } else {
-                        // V^T: consecutive lanes hold consecutive tokens, so each store is 64 contiguous bytes
-                        __nv_bfloat16 *dst = ep.vt + (bh * 64 + d0) * ep.win_tokens + pos;
-#pragma unroll
-                        for (int i = 0; i < C::COLS; ++i) dst[static_cast<int64_t>(i) * ep.win_tokens] = __float2bfloat16_rn(acc[i]);
-                    }
-                }
-            } else if constexpr (MODE == MMQ_OUT_Q8) {
-                // this thread's 64 columns are two whole 32-wide Q8_0 blocks of the output row
-                if (m < M) {
-                    const int nb = n0 + h * C::COLS;
-#pragma unroll
-                    for (int hb = 0; hb < C::COLS; hb += 32) {
-                        if (nb + hb >= N) break;
-                        float amax = 0.f;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            float val = bias ? __fadd_rn(acc[hb + i], bias[nb + hb + i]) : acc[hb + i];
-                            if (ep.gelu == 1) val = gelu_erf_f(val);
-                            else if (ep.gelu == 2) val = gelu_tanh_f16(val);
-                            acc[hb + i] = val;
-                            amax = fmaxf(amax, fabsf(val));
-                        }
-                        const float d = __fdiv_rn(amax, 127.f);
-                        const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-                        uint32_t pk[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            pk[i] = pack4_i8(__float2int_rn(__fmul_rn(acc[hb + 4 * i], id)),
-                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 1], id)),
-                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 2], id)),
-                                             __float2int_rn(__fmul_rn(acc[hb + 4 * i + 3], id)));
-                        uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
-                        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                        ep.qquads[act_quad_index((nb + hb) >> 5, m, ep.qld)] = __float2half_rn(d);
-                    }
-                }
-            }
+            if constexpr (MODE != MMQ_OUT_BLOCKDOTS) tile_store<MODE, C::COLS>(ep, acc, m, M, N, n0 + h * C::COLS);
         }
     }
     tc_fence_before();
