@@ -243,8 +243,18 @@ __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const
 // + 7 and its amax is a three-step shuffle.  The double-precision sums are
 // those of ggml_norm (exact for these magnitudes, so the lane order does not
 // change them).
+// 128-thread CTAs; for E = 1024 at most 56 registers: 9 CTAs (36 warps) per
+// SM, so the 5184 rows of a 72 x 72 map run as one wave (64 registers gave 32
+// warps per SM: 1.09 waves, the last 4% of rows a second round of DRAM
+// latency).  Other widths keep a budget they fit without spilling.
 template <int NJ>
-__global__ void ln_q8_coal_kernel(const float *__restrict__ x, int rows, const float *__restrict__ w,
+struct LnMinBlocks {
+    static constexpr int value = NJ <= 4 || NJ == 8 ? 9 : NJ <= 6 ? 8 : 4;
+};
+
+template <int NJ>
+__global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
+    ln_q8_coal_kernel(const float *__restrict__ x, int rows, const float *__restrict__ w,
                                   const float *__restrict__ b, float eps, int G, int win, int8_t *__restrict__ codes,
                                   __half *__restrict__ quads, int ld) {
     constexpr int E = NJ * 128;
@@ -306,7 +316,7 @@ __global__ void ln_q8_coal_kernel(const float *__restrict__ x, int rows, const f
 template <int NJ>
 static void launch_ln_coal(const float *x, int rows, const float *w, const float *b, float eps, int G, int win,
                            void *codes, void *quads, int ld, cudaStream_t s) {
-    ln_q8_coal_kernel<NJ><<<grid_for(rows, 8), 256, 0, s>>>(x, rows, w, b, eps, G, win, static_cast<int8_t *>(codes),
+    ln_q8_coal_kernel<NJ><<<grid_for(rows, 4), 128, 0, s>>>(x, rows, w, b, eps, G, win, static_cast<int8_t *>(codes),
                                                              static_cast<__half *>(quads), ld);
 }
 
