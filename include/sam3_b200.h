@@ -283,6 +283,35 @@ int sam3b200_sam_dec_outputs(sam3b200_sam_dec *d, const float **masks_dev, float
  * binarised at logit 0 (:11071-11075): dst_dev uint8 [out_h][out_w], 255 / 0. */
 int sam3b200_sam_dec_mask(sam3b200_sam_dec *d, int m, int out_w, int out_h, uint8_t *dst_dev);
 
+/* ---- SAM3 text encoder (the PCS path's text side) ------------------------
+ * The graph sam3_build_text_encoder_graph builds (sam3.cpp:4039-4066; block
+ * :3958-4032; causal mask :3934-3951): token embedding rows + positional
+ * embedding, `layers` pre-LN blocks (16-head causal attention, GELU-erf MLP),
+ * final LayerNorm, resizer to out_dim.  Weights by name (sam3.cpp:2628-2654):
+ * "text.token_embed.weight", "text.pos_embed", "text.ln_final.*",
+ * "text.resizer.*", "text.blocks.<i>.{attn.in_proj,attn.out_proj,ln_1,ln_2,
+ * mlp.fc1,mlp.fc2}.{weight,bias}". */
+typedef struct {
+    int32_t width;    /* 1024 */
+    int32_t heads;    /* 16 (head dim 64) */
+    int32_t layers;   /* 24 */
+    int32_t ctx_len;  /* 32 */
+    int32_t vocab;    /* 49408 */
+    int32_t out_dim;  /* 256 */
+} sam3b200_text_hparams;
+
+typedef struct sam3b200_text sam3b200_text;
+
+sam3b200_text *sam3b200_text_create(sam3b200_backend *be, const sam3b200_text_hparams *hp);
+void sam3b200_text_free(sam3b200_text *t);
+int sam3b200_text_set_tensor(sam3b200_text *t, const char *name, int type, const void *data, const int64_t ne[4]);
+int sam3b200_text_missing(sam3b200_text *t, char *buf, int cap);
+/* Encode n_ids (<= ctx_len) host token ids, padded with id 0 to ctx_len as
+ * the reference does.  Asynchronous after the id upload. */
+int sam3b200_text_encode(sam3b200_text *t, const int32_t *ids, int n_ids);
+/* Text features: device f32 [out_dim, ctx_len] (memory [ctx_len][out_dim]). */
+int sam3b200_text_output(sam3b200_text *t, const float **dev, int64_t ne[2]);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

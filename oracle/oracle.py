@@ -132,20 +132,20 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, batch: int, N: int, h
 
 
 def attention_general(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float,
-                      mask: np.ndarray | None = None) -> np.ndarray:
+                      mask: np.ndarray | None = None, dtype=np.float64) -> np.ndarray:
     """ggml_flash_attn_ext with max_bias 0 and no softcap, in float64: q [B][H][NQ][D], k, v
     [B][H][NKV][D], mask f32 [NQ][NKV] (or None) added to the scaled scores; a key whose mask is -inf
     is skipped and a row with every key skipped gives zeros.  Returns f32 [B][NQ][H][D] (ggml dst
     [D, H, NQ, B])."""
-    s = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), k.astype(np.float64)) * scale
+    s = np.einsum("bhqd,bhkd->bhqk", q.astype(dtype), k.astype(dtype)) * dtype(scale)
     if mask is not None:
-        s = s + mask.astype(np.float64)[None, None]
+        s = s + mask.astype(dtype)[None, None]
     mx = np.max(s, axis=-1, keepdims=True)
     dead = ~np.isfinite(mx)
     p = np.exp(s - np.where(dead, 0.0, mx))
     p = np.where(np.isfinite(s), p, 0.0)
     den = p.sum(-1, keepdims=True)
-    o = np.einsum("bhqk,bhkd->bhqd", p, v.astype(np.float64)) / np.where(den > 0, den, 1.0)
+    o = np.einsum("bhqk,bhkd->bhqd", p, v.astype(dtype)) / np.where(den > 0, den, dtype(1.0))
     return o.transpose(0, 2, 1, 3).astype(np.float32)
 
 

@@ -90,6 +90,12 @@ def lib() -> ctypes.CDLL:
         "sam3b200_sam_dec_outputs": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), vp, vp,
                                            ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_sam_dec_mask": (i32, [vp, i32, i32, i32, vp]),
+        "sam3b200_text_create": (vp, [vp, vp]),
+        "sam3b200_text_free": (None, [vp]),
+        "sam3b200_text_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_text_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_text_encode": (i32, [vp, vp, i32]),
+        "sam3b200_text_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), vp]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -401,6 +407,46 @@ class SamDecoder:
             self.h = None
 
 
+class TextEncoder:
+    """The SAM3 text encoder (sam3b200_text) on a backend."""
+
+    FIELDS = ("width", "heads", "layers", "ctx_len", "vocab", "out_dim")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 6)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_text_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"text_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_text_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_text_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} text tensors missing: {buf.value.decode()[:300]}")
+
+    def encode(self, ids) -> np.ndarray:
+        """Token ids -> f32 [ctx_len][out_dim] text features (host)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        _check(lib().sam3b200_text_encode(self.h, ids.ctypes.data, ids.size), "text_encode")
+        p = ctypes.c_void_p()
+        ne = (ctypes.c_int64 * 2)()
+        _check(lib().sam3b200_text_output(self.h, ctypes.byref(p), ne), "text_output")
+        self.be.synchronize()
+        out = np.empty((ne[1], ne[0]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_text_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -513,6 +559,9 @@ class Backend:
 
     def sam_decoder(self, hp: dict) -> SamDecoder:
         return SamDecoder(self, hp)
+
+    def text_encoder(self, hp: dict) -> TextEncoder:
+        return TextEncoder(self, hp)
 
     def free(self) -> None:
         if self.h:

@@ -216,8 +216,8 @@ __global__ void patch_conv_f32_kernel(const float *__restrict__ img, int img_sid
 }
 
 // FPN top-down fusion: y[t] = lat[t] + prev[nearest 2x source of t] (sam3.cpp:4568-4573)
-__global__ void upsample2_add_kernel(const float *__restrict__ lat, const float *__restrict__ prev, int H, int W, int D,
-                                     float *__restrict__ y) {
+__global__ void upsample2_add_kernel(const float *lat, const float *__restrict__ prev, int H, int W, int D,
+                                     float *y) {  // y may alias lat
     const int64_t total = static_cast<int64_t>(H) * W * D;
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= total) return;

@@ -35,8 +35,9 @@ namespace {
 inline unsigned nblocks(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
 // c = a + b (+ per-column vectors v1, v2 when given): rows x D
-__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ v1,
-                           const float *__restrict__ v2, int64_t rows, int D, float *__restrict__ c) {
+// (c may alias a or b)
+__global__ void add_kernel(const float *a, const float *b, const float *__restrict__ v1, const float *__restrict__ v2,
+                           int64_t rows, int D, float *c) {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= rows * D) return;
     const int d = static_cast<int>(i % D);
