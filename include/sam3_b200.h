@@ -312,6 +312,46 @@ int sam3b200_text_encode(sam3b200_text *t, const int32_t *ids, int n_ids);
 /* Text features: device f32 [out_dim, ctx_len] (memory [ctx_len][out_dim]). */
 int sam3b200_text_output(sam3b200_text *t, const float **dev, int64_t ne[2]);
 
+/* ---- Memory attention of the video tracker -------------------------------
+ * The graph sam3_build_mem_attn_graph builds (sam3.cpp:9228-9341) with the
+ * inputs sam3_propagate_single prepares (:11175-11310): current-frame tokens
+ * conditioned on the memory bank through `layers` blocks of single-head
+ * self-attention (RoPE on q and k), cross-attention to the memories (keys
+ * from prompt + prompt_pos, values from prompt, both projected mem_dim ->
+ * d_model; RoPE on q and on the first M_total - n_obj_ptr_tokens keys only),
+ * ReLU feed-forward, then LayerNorm.  Weights by name (sam3.cpp:2008-2042):
+ * "mem_attn.norm.{weight,bias}", "mem_attn.layers.<i>.{sa,ca}.{q,k,v,out}_proj
+ * .{weight,bias}", ".linear1", ".linear2", ".norm1".."norm3". */
+typedef struct {
+    int32_t d_model;         /* 256 (neck_dim; the single head's width) */
+    int32_t mem_dim;         /* 64 (mem_out_dim) */
+    int32_t layers;          /* 4 */
+    int32_t ffn_dim;         /* 2048 */
+    int32_t max_tokens;      /* capacity: current-frame tokens N (H*H) */
+    int32_t max_mem_tokens;  /* capacity: memory tokens M_total (spatial + object-pointer) */
+} sam3b200_mem_attn_hparams;
+
+typedef struct sam3b200_mem_attn sam3b200_mem_attn;
+
+sam3b200_mem_attn *sam3b200_mem_attn_create(sam3b200_backend *be, const sam3b200_mem_attn_hparams *hp);
+void sam3b200_mem_attn_free(sam3b200_mem_attn *m);
+int sam3b200_mem_attn_set_tensor(sam3b200_mem_attn *m, const char *name, int type, const void *data,
+                                 const int64_t ne[4]);
+int sam3b200_mem_attn_missing(sam3b200_mem_attn *m, char *buf, int cap);
+/* Host inputs (the tensors sam3_propagate_single sets), ggml layouts:
+ * curr, src_pos [d_model, N]; prompt, prompt_pos [mem_dim, M_total];
+ * rope_q [2, d_model/2, N]; rope_k [2, d_model/2, M_total - n_obj_ptr_tokens]
+ * or NULL (no rotation of the keys).  Asynchronous after the uploads. */
+int sam3b200_mem_attn_run(sam3b200_mem_attn *m, const float *curr, const float *src_pos, const float *prompt,
+                          const float *prompt_pos, const float *rope_q, const float *rope_k, int n_tokens,
+                          int n_mem_tokens, int n_obj_ptr_tokens);
+/* The same with every input already in device memory. */
+int sam3b200_mem_attn_run_device(sam3b200_mem_attn *m, const float *curr, const float *src_pos,
+                                 const float *prompt, const float *prompt_pos, const float *rope_q,
+                                 const float *rope_k, int n_tokens, int n_mem_tokens, int n_obj_ptr_tokens);
+/* Conditioned tokens: device f32 [d_model, N] of the last run. */
+int sam3b200_mem_attn_output(sam3b200_mem_attn *m, const float **dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

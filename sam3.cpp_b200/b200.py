@@ -96,6 +96,13 @@ def lib() -> ctypes.CDLL:
         "sam3b200_text_missing": (i32, [vp, ctypes.c_char_p, i32]),
         "sam3b200_text_encode": (i32, [vp, vp, i32]),
         "sam3b200_text_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), vp]),
+        "sam3b200_mem_attn_create": (vp, [vp, vp]),
+        "sam3b200_mem_attn_free": (None, [vp]),
+        "sam3b200_mem_attn_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_mem_attn_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_mem_attn_run": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+        "sam3b200_mem_attn_run_device": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+        "sam3b200_mem_attn_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -447,6 +454,50 @@ class TextEncoder:
             self.h = None
 
 
+class MemAttention:
+    """The tracker's memory attention (sam3b200_mem_attn) on a backend."""
+
+    FIELDS = ("d_model", "mem_dim", "layers", "ffn_dim", "max_tokens", "max_mem_tokens")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 6)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_mem_attn_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"mem_attn_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_mem_attn_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_mem_attn_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} mem_attn tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, curr, src_pos, prompt, prompt_pos, rope_q, rope_k, n_obj_ptr_tokens: int) -> np.ndarray:
+        """Host f32 inputs (token-major: curr/src_pos [N][D], prompt/prompt_pos [M][MD], rope_q [N][D/2][2],
+        rope_k [M - n_obj_ptr_tokens][D/2][2] or None) -> conditioned tokens [N][D] (host)."""
+        a = [np.ascontiguousarray(x, np.float32) for x in (curr, src_pos, prompt, prompt_pos, rope_q)]
+        rk = None if rope_k is None else np.ascontiguousarray(rope_k, np.float32)
+        N, M = a[0].shape[0], a[2].shape[0]
+        _check(lib().sam3b200_mem_attn_run(self.h, *[x.ctypes.data for x in a], None if rk is None else rk.ctypes.data,
+                                           N, M, n_obj_ptr_tokens), "mem_attn_run")
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_mem_attn_output(self.h, ctypes.byref(p)), "mem_attn_output")
+        self.be.synchronize()
+        out = np.empty((N, self.hp["d_model"]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_mem_attn_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -562,6 +613,9 @@ class Backend:
 
     def text_encoder(self, hp: dict) -> TextEncoder:
         return TextEncoder(self, hp)
+
+    def mem_attention(self, hp: dict) -> MemAttention:
+        return MemAttention(self, hp)
 
     def free(self) -> None:
         if self.h:
