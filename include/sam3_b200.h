@@ -352,6 +352,48 @@ int sam3b200_mem_attn_run_device(sam3b200_mem_attn *m, const float *curr, const 
 /* Conditioned tokens: device f32 [d_model, N] of the last run. */
 int sam3b200_mem_attn_output(sam3b200_mem_attn *m, const float **dev);
 
+/* ---- Memory encoder of the video tracker ----------------------------------
+ * sam3_encode_memory (sam3.cpp:11510-11615) up to the stored [mem_dim, H, H]
+ * memory features: mask logits resized to img (bilinear), sigmoid * scale +
+ * bias, resized to 16H; mask downsampler (4 x conv 3x3 s2 + LayerNorm2d +
+ * GELU, conv 1x1); + conv 1x1 of the frame's pixel features; 2 CXBlock
+ * fusers (sam3_cxblock_forward, :9066-9108); conv 1x1 to mem_dim; plus
+ * no_obj_embed_spatial when the object score is <= 0.  Weights by name
+ * (sam3.cpp:1972-2005): "mem_enc.ds.{0,3,6,9,12}.*" (convolutions),
+ * "mem_enc.ds.{1,4,7,10}.*" (LayerNorm2d), "mem_enc.pix_feat_proj.*",
+ * "mem_enc.fuser.<i>.{dwconv,norm,pwconv1,pwconv2}.*", ".gamma",
+ * "mem_enc.out_proj.*", optional "no_obj_embed_spatial"; "mem_enc.tpos_enc"
+ * is accepted and left to the host prompt builder. */
+typedef struct {
+    int32_t feat;          /* H: 64 (SAM2 at 1024), 72 (SAM3 at 1008) */
+    int32_t img;           /* the effective image size (HIGH_RES): 1024 / 1008 */
+    int32_t d_model;       /* 256 */
+    int32_t mem_dim;       /* 64 */
+    int32_t fuser_layers;  /* 2 */
+    int32_t fuser_dim;     /* 1024 */
+    float sigmoid_scale;   /* sigmoid_scale_x100 / 100 (20.0) */
+    float sigmoid_bias;    /* sigmoid_bias_x100 / 100 (-10.0) */
+    int32_t max_mask;      /* capacity: mask_w * mask_h of the logits */
+} sam3b200_mem_enc_hparams;
+
+typedef struct sam3b200_mem_enc sam3b200_mem_enc;
+
+sam3b200_mem_enc *sam3b200_mem_enc_create(sam3b200_backend *be, const sam3b200_mem_enc_hparams *hp);
+void sam3b200_mem_enc_free(sam3b200_mem_enc *m);
+int sam3b200_mem_enc_set_tensor(sam3b200_mem_enc *m, const char *name, int type, const void *data,
+                                const int64_t ne[4]);
+int sam3b200_mem_enc_missing(sam3b200_mem_enc *m, char *buf, int cap);
+/* Host inputs: mask logits [mask_h][mask_w] (the decoder's low-resolution
+ * mask), pixel features [d_model, H, H] (memory [H*H][d_model], the tracker
+ * neck's level-2 map).  Asynchronous after the uploads. */
+int sam3b200_mem_enc_run(sam3b200_mem_enc *m, const float *mask_logits, int mask_w, int mask_h,
+                         const float *pix_feat, float obj_score);
+/* The same with both inputs in device memory. */
+int sam3b200_mem_enc_run_device(sam3b200_mem_enc *m, const float *mask_logits, int mask_w, int mask_h,
+                                const float *pix_feat, float obj_score);
+/* Memory features: device f32 [mem_dim, H, H] (memory [H*H][mem_dim]). */
+int sam3b200_mem_enc_output(sam3b200_mem_enc *m, const float **dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

@@ -103,6 +103,13 @@ def lib() -> ctypes.CDLL:
         "sam3b200_mem_attn_run": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32]),
         "sam3b200_mem_attn_run_device": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32]),
         "sam3b200_mem_attn_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_mem_enc_create": (vp, [vp, vp]),
+        "sam3b200_mem_enc_free": (None, [vp]),
+        "sam3b200_mem_enc_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_mem_enc_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_mem_enc_run": (i32, [vp, vp, i32, i32, vp, ctypes.c_float]),
+        "sam3b200_mem_enc_run_device": (i32, [vp, vp, i32, i32, vp, ctypes.c_float]),
+        "sam3b200_mem_enc_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -498,6 +505,53 @@ class MemAttention:
             self.h = None
 
 
+class MemEncHparams(ctypes.Structure):
+    _fields_ = [("feat", ctypes.c_int32), ("img", ctypes.c_int32), ("d_model", ctypes.c_int32),
+                ("mem_dim", ctypes.c_int32), ("fuser_layers", ctypes.c_int32), ("fuser_dim", ctypes.c_int32),
+                ("sigmoid_scale", ctypes.c_float), ("sigmoid_bias", ctypes.c_float), ("max_mask", ctypes.c_int32)]
+
+
+class MemEncoder:
+    """The tracker's memory encoder (sam3b200_mem_enc) on a backend."""
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = MemEncHparams(**{k: hp[k] for k, _ in MemEncHparams._fields_})
+        self.h = lib().sam3b200_mem_enc_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"mem_enc_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_mem_enc_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_mem_enc_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} mem_enc tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, mask_logits: np.ndarray, pix_feat: np.ndarray, obj_score: float = 1.0) -> np.ndarray:
+        """Host mask logits [mh][mw] and pixel features [H*H][d_model] -> memory features [H*H][mem_dim]."""
+        ml = np.ascontiguousarray(mask_logits, np.float32)
+        pf = np.ascontiguousarray(pix_feat, np.float32)
+        _check(lib().sam3b200_mem_enc_run(self.h, ml.ctypes.data, ml.shape[1], ml.shape[0], pf.ctypes.data,
+                                          float(obj_score)), "mem_enc_run")
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_mem_enc_output(self.h, ctypes.byref(p)), "mem_enc_output")
+        self.be.synchronize()
+        H = self.hp["feat"]
+        out = np.empty((H * H, self.hp["mem_dim"]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_mem_enc_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -616,6 +670,9 @@ class Backend:
 
     def mem_attention(self, hp: dict) -> MemAttention:
         return MemAttention(self, hp)
+
+    def mem_encoder(self, hp: dict) -> MemEncoder:
+        return MemEncoder(self, hp)
 
     def free(self) -> None:
         if self.h:

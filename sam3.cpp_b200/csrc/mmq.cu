@@ -16,6 +16,7 @@
 //   * the epilogue warps convert I_b to fp32 (exact: |I_b| < 2^22) and fold
 //     acc = fma(I_b, S_b, acc) in block order.
 // That is the oracle's fma sequence, so results are bit-identical to it.
+#include "act.cuh"
 #include "mmq.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
@@ -255,22 +256,6 @@ struct MmqEpi {
     const float *freqs;
     int win_tokens, heads;
 };
-
-__device__ __forceinline__ float gelu_erf_f(float x) {
-    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, erff(__fmul_rn(x, 0.70710678118654752440f))));
-}
-
-// ggml_gelu on the CPU backend (GGML_GELU_FP16, the Hiera MLP, sam3.cpp:4453):
-// 0 at x <= -10, x at x >= 10, else the fp16 table entry of the tanh form at
-// fp16(x): fp16(0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x^2)))).
-__device__ __forceinline__ float gelu_tanh_f16(float x) {
-    if (x <= -10.0f) return 0.0f;
-    if (x >= 10.0f) return x;
-    const float h = __half2float(__float2half_rn(x));
-    const float inner = __fmul_rn(__fmul_rn(0.79788456080286535587989211986876f, h),
-                                  __fadd_rn(1.0f, __fmul_rn(__fmul_rn(0.044715f, h), h)));
-    return __half2float(__float2half_rn(__fmul_rn(__fmul_rn(0.5f, h), __fadd_rn(1.0f, tanhf(inner)))));
-}
 
 __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
     return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
