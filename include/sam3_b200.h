@@ -394,6 +394,38 @@ int sam3b200_mem_enc_run_device(sam3b200_mem_enc *m, const float *mask_logits, i
 /* Memory features: device f32 [mem_dim, H, H] (memory [H*H][mem_dim]). */
 int sam3b200_mem_enc_output(sam3b200_mem_enc *m, const float **dev);
 
+/* ---- Fusion encoder of the SAM3 detector (the PCS path) --------------------
+ * The graph sam3_build_fenc_graph builds (sam3.cpp:8146-8165; layer
+ * :8033-8139): `layers` pre-LN blocks over the detector's image tokens --
+ * self-attention with the positional code on q and k, cross-attention to the
+ * prompt tokens under their padding bias, ReLU FFN.  Weights by name
+ * (sam3.cpp:2655-2682): "fenc.layers.<i>.{sa,ca}.in_proj_{weight,bias}",
+ * ".{sa,ca}.out_proj.*", ".linear1.*", ".linear2.*", ".norm1".."norm3". */
+typedef struct {
+    int32_t d_model;     /* 256 */
+    int32_t heads;       /* 8 (fenc_heads) */
+    int32_t layers;      /* 6 (fenc_layers) */
+    int32_t ffn_dim;     /* 2048 (fenc_ffn_dim) */
+    int32_t max_tokens;  /* capacity: image tokens (72 * 72) */
+    int32_t max_prompt;  /* capacity: prompt tokens (text ctx_len 32 + geometry tokens) */
+} sam3b200_fenc_hparams;
+
+typedef struct sam3b200_fenc sam3b200_fenc;
+
+sam3b200_fenc *sam3b200_fenc_create(sam3b200_backend *be, const sam3b200_fenc_hparams *hp);
+void sam3b200_fenc_free(sam3b200_fenc *f);
+int sam3b200_fenc_set_tensor(sam3b200_fenc *f, const char *name, int type, const void *data, const int64_t ne[4]);
+int sam3b200_fenc_missing(sam3b200_fenc *f, char *buf, int cap);
+/* Host inputs: image_feats, pos [d_model, n_tokens] (the detector neck's
+ * level-2 map and its sine code), prompt [d_model, n_prompt], prompt_bias
+ * [n_prompt] (0 valid, -1e9 padding; NULL = no mask). */
+int sam3b200_fenc_run(sam3b200_fenc *f, const float *image_feats, const float *prompt, const float *pos,
+                      const float *prompt_bias, int n_tokens, int n_prompt);
+int sam3b200_fenc_run_device(sam3b200_fenc *f, const float *image_feats, const float *prompt, const float *pos,
+                             const float *prompt_bias, int n_tokens, int n_prompt);
+/* Conditioned image tokens: device f32 [d_model, n_tokens]. */
+int sam3b200_fenc_output(sam3b200_fenc *f, const float **dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

@@ -110,6 +110,13 @@ def lib() -> ctypes.CDLL:
         "sam3b200_mem_enc_run": (i32, [vp, vp, i32, i32, vp, ctypes.c_float]),
         "sam3b200_mem_enc_run_device": (i32, [vp, vp, i32, i32, vp, ctypes.c_float]),
         "sam3b200_mem_enc_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_fenc_create": (vp, [vp, vp]),
+        "sam3b200_fenc_free": (None, [vp]),
+        "sam3b200_fenc_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_fenc_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_fenc_run": (i32, [vp, vp, vp, vp, vp, i32, i32]),
+        "sam3b200_fenc_run_device": (i32, [vp, vp, vp, vp, vp, i32, i32]),
+        "sam3b200_fenc_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -552,6 +559,49 @@ class MemEncoder:
             self.h = None
 
 
+class FusionEncoder:
+    """The detector's fusion encoder (sam3b200_fenc) on a backend."""
+
+    FIELDS = ("d_model", "heads", "layers", "ffn_dim", "max_tokens", "max_prompt")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 6)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_fenc_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"fenc_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_fenc_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_fenc_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} fenc tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, image_feats, prompt, pos, prompt_bias=None) -> np.ndarray:
+        """Host f32 token-major inputs (image_feats/pos [N][D], prompt [T][D], prompt_bias [T] or None)
+        -> conditioned tokens [N][D]."""
+        img, pr, ps = (np.ascontiguousarray(a, np.float32) for a in (image_feats, prompt, pos))
+        pb = None if prompt_bias is None else np.ascontiguousarray(prompt_bias, np.float32)
+        _check(lib().sam3b200_fenc_run(self.h, img.ctypes.data, pr.ctypes.data, ps.ctypes.data,
+                                       None if pb is None else pb.ctypes.data, img.shape[0], pr.shape[0]), "fenc_run")
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_fenc_output(self.h, ctypes.byref(p)), "fenc_output")
+        self.be.synchronize()
+        out = np.empty(img.shape, np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_fenc_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -673,6 +723,9 @@ class Backend:
 
     def mem_encoder(self, hp: dict) -> MemEncoder:
         return MemEncoder(self, hp)
+
+    def fusion_encoder(self, hp: dict) -> FusionEncoder:
+        return FusionEncoder(self, hp)
 
     def free(self) -> None:
         if self.h:

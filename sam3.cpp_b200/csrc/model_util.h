@@ -65,6 +65,7 @@ inline int64_t type_row_bytes(int type, int64_t k) {
     case SAM3B200_TYPE_F16: return 2 * k;
     case SAM3B200_TYPE_Q8_0: return k / 32 * 34;
     case SAM3B200_TYPE_Q4_0: return k / 32 * 18;
+    case SAM3B200_TYPE_Q4_1: return k / 32 * 20;
     default: return -1;
     }
 }
@@ -106,6 +107,20 @@ inline bool upload_qweight(Backend *be, QWeight &w, int type, const void *data, 
     raw.release();
     w.set = ok;
     return ok;
+}
+
+// Upload rows [r0, r0 + rows) of a ggml [K, N] weight as a weight of its own
+// (rows are independent in every type): the per-view MUL_MATs of a fused
+// in_proj become separate weights.
+inline sam3b200_weight *upload_weight_rows(Backend *be, int type, const void *data, int64_t K, int64_t r0,
+                                           int64_t rows) {
+    const int64_t rb = type_row_bytes(type, K);
+    if (rb <= 0) {
+        set_error("weight rows: type %d unsupported", type);
+        return nullptr;
+    }
+    return sam3b200_weight_upload(reinterpret_cast<sam3b200_backend *>(be), type,
+                                  static_cast<const char *>(data) + r0 * rb, K, rows);
 }
 
 }  // namespace b200
