@@ -426,6 +426,79 @@ int sam3b200_fenc_run_device(sam3b200_fenc *f, const float *image_feats, const f
 /* Conditioned image tokens: device f32 [d_model, n_tokens]. */
 int sam3b200_fenc_output(sam3b200_fenc *f, const float **dev);
 
+/* ---- DETR decoder of the SAM3 detector (the PCS path) ---------------------
+ * The graph sam3_build_ddec_graph builds (sam3.cpp:8749-8888): presence token
+ * + num_queries object queries refined through `layers` post-norm layers
+ * (self-attention, text cross-attention under the padding bias, image
+ * cross-attention under the box-relative bias of sam3_compute_box_rpb, ReLU
+ * FFN) with per-layer query positions from the boxes' sine code and box
+ * refinement; then the dot-product scores against the pooled text
+ * (sam3_dot_product_scoring, :8640-8739) and the presence logit.  Weights by
+ * name (sam3.cpp:2684-2789): "ddec.*" and "scoring.*". */
+typedef struct {
+    int32_t d_model;      /* 256 */
+    int32_t heads;        /* 8 (ddec_heads) */
+    int32_t layers;       /* 6 (ddec_layers) */
+    int32_t ffn_dim;      /* 2048 (ddec_ffn_dim; also the scoring prompt MLP) */
+    int32_t num_queries;  /* 200 (ddec_num_queries) */
+    int32_t feat;         /* 72: the side of the image-token grid */
+    int32_t max_prompt;   /* capacity: text (+ geometry) tokens */
+} sam3b200_ddec_hparams;
+
+typedef struct sam3b200_ddec sam3b200_ddec;
+
+sam3b200_ddec *sam3b200_ddec_create(sam3b200_backend *be, const sam3b200_ddec_hparams *hp);
+void sam3b200_ddec_free(sam3b200_ddec *d);
+int sam3b200_ddec_set_tensor(sam3b200_ddec *d, const char *name, int type, const void *data, const int64_t ne[4]);
+int sam3b200_ddec_missing(sam3b200_ddec *d, char *buf, int cap);
+/* Host inputs: enc_feats, enc_pos [d_model, feat*feat] (the fusion encoder's
+ * output and the image positional code), text [d_model, n_text], text_bias
+ * [n_text] (0 / -1e9; NULL = no mask), text_valid [n_text] (n_text/n_valid
+ * for valid tokens, 0 for padding; NULL = plain mean). */
+int sam3b200_ddec_run(sam3b200_ddec *d, const float *enc_feats, const float *enc_pos, const float *text,
+                      const float *text_bias, const float *text_valid, int n_text);
+int sam3b200_ddec_run_device(sam3b200_ddec *d, const float *enc_feats, const float *enc_pos, const float *text,
+                             const float *text_bias, const float *text_valid, int n_text);
+/* Device outputs of the last run: queries [d_model, 1 + num_queries]
+ * (presence, then the normed object queries: the segmentation head's input),
+ * boxes [4, num_queries] (cx, cy, w, h in [0, 1]), class scores
+ * [num_queries], presence logit [1].  Any pointer may be NULL. */
+int sam3b200_ddec_outputs(sam3b200_ddec *d, const float **queries, const float **boxes, const float **scores,
+                          const float **presence);
+
+/* ---- Segmentation head of the SAM3 detector (the PCS path) ----------------
+ * The graph sam3_build_seg_head_graph builds (sam3.cpp:8975-9058): the
+ * fusion-encoder tokens cross-attend to the prompt, replace the lowest FPN
+ * level, and the pixel decoder (sam3_pixel_decoder, :8899-8960: nearest 2x
+ * upsample + add, conv 3x3, GroupNorm(8), ReLU, twice) brings them to 4*feat;
+ * a 1x1 instance head and the 3-layer mask-embedding MLP of the queries give
+ * the mask logits.  Weights by name (sam3.cpp:2845-2880): "seg.*". */
+typedef struct {
+    int32_t d_model;      /* 256 */
+    int32_t heads;        /* 8 */
+    int32_t feat;         /* 72: the fusion-encoder grid; the masks are 4 * feat square */
+    int32_t max_queries;  /* capacity: queries per run (200) */
+    int32_t max_prompt;   /* capacity: prompt tokens */
+} sam3b200_seg_hparams;
+
+typedef struct sam3b200_seg sam3b200_seg;
+
+sam3b200_seg *sam3b200_seg_create(sam3b200_backend *be, const sam3b200_seg_hparams *hp);
+void sam3b200_seg_free(sam3b200_seg *h);
+int sam3b200_seg_set_tensor(sam3b200_seg *h, const char *name, int type, const void *data, const int64_t ne[4]);
+int sam3b200_seg_missing(sam3b200_seg *h, char *buf, int cap);
+/* Host inputs: enc [d_model, feat^2] (fusion encoder output), fpn0
+ * [d_model, (4 feat)^2] and fpn1 [d_model, (2 feat)^2] (the detector neck's
+ * finest levels), queries [d_model, n_queries] (the decoder's object
+ * queries), text [d_model, n_text], text_bias [n_text] or NULL. */
+int sam3b200_seg_run(sam3b200_seg *h, const float *enc, const float *fpn0, const float *fpn1, const float *queries,
+                     int n_queries, const float *text, const float *text_bias, int n_text);
+int sam3b200_seg_run_device(sam3b200_seg *h, const float *enc, const float *fpn0, const float *fpn1,
+                            const float *queries, int n_queries, const float *text, const float *text_bias,
+                            int n_text);
+/* Mask logits: device f32 [(4 feat)^2, n_queries] (memory [n_queries][pixels]). */
+int sam3b200_seg_output(sam3b200_seg *h, const float **dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds

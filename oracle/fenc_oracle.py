@@ -27,7 +27,8 @@ def rows(w: tuple, r0: int, n: int) -> tuple:
 
 def mha(q, k, v, heads: int, mask=None, dtype=np.float64, chunk=1024) -> np.ndarray:
     """Multi-head softmax(q k^T / sqrt(hd) + mask) v over token-major q [NQ][D], k, v [NK][D]; mask
-    [NQ][NK] additive (an -inf entry removes the key).  Query chunks bound the memory."""
+    [NQ][NK] additive, shared by the heads, or [heads][NQ][NK] (an -inf entry removes the key).  Query
+    chunks bound the memory."""
     NQ, D = q.shape
     hd = D // heads
     scale = 1.0 / math.sqrt(hd)
@@ -38,7 +39,7 @@ def mha(q, k, v, heads: int, mask=None, dtype=np.float64, chunk=1024) -> np.ndar
         for i in range(0, NQ, chunk):
             s = (q[i:i + chunk, sl].astype(dtype) @ kh.T) * dtype(scale)
             if mask is not None:
-                s = s + mask[i:i + chunk].astype(dtype)
+                s = s + (mask[h] if mask.ndim == 3 else mask)[i:i + chunk].astype(dtype)
             m = s.max(axis=1, keepdims=True)
             p = np.exp(s - np.where(np.isfinite(m), m, 0))
             den = p.sum(axis=1, keepdims=True)

@@ -117,6 +117,20 @@ def lib() -> ctypes.CDLL:
         "sam3b200_fenc_run": (i32, [vp, vp, vp, vp, vp, i32, i32]),
         "sam3b200_fenc_run_device": (i32, [vp, vp, vp, vp, vp, i32, i32]),
         "sam3b200_fenc_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_ddec_create": (vp, [vp, vp]),
+        "sam3b200_ddec_free": (None, [vp]),
+        "sam3b200_ddec_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_ddec_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_ddec_run": (i32, [vp, vp, vp, vp, vp, vp, i32]),
+        "sam3b200_ddec_run_device": (i32, [vp, vp, vp, vp, vp, vp, i32]),
+        "sam3b200_ddec_outputs": (i32, [vp] + [ctypes.POINTER(ctypes.c_void_p)] * 4),
+        "sam3b200_seg_create": (vp, [vp, vp]),
+        "sam3b200_seg_free": (None, [vp]),
+        "sam3b200_seg_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_seg_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_seg_run": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
+        "sam3b200_seg_run_device": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
+        "sam3b200_seg_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -602,6 +616,96 @@ class FusionEncoder:
             self.h = None
 
 
+class DetrDecoder:
+    """The detector's DETR decoder with scoring and presence head (sam3b200_ddec) on a backend."""
+
+    FIELDS = ("d_model", "heads", "layers", "ffn_dim", "num_queries", "feat", "max_prompt")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 7)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_ddec_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"ddec_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_ddec_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_ddec_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} ddec tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, enc, enc_pos, text, text_bias=None, text_valid=None) -> dict:
+        """Host f32 token-major inputs -> dict of host outputs: queries [1+NQ][D], boxes [NQ][4],
+        scores [NQ], presence (float)."""
+        e, ep, tx = (np.ascontiguousarray(a, np.float32) for a in (enc, enc_pos, text))
+        tb = None if text_bias is None else np.ascontiguousarray(text_bias, np.float32)
+        tv = None if text_valid is None else np.ascontiguousarray(text_valid, np.float32)
+        _check(lib().sam3b200_ddec_run(self.h, e.ctypes.data, ep.ctypes.data, tx.ctypes.data,
+                                       None if tb is None else tb.ctypes.data, None if tv is None else tv.ctypes.data,
+                                       tx.shape[0]), "ddec_run")
+        ptr = [ctypes.c_void_p() for _ in range(4)]
+        _check(lib().sam3b200_ddec_outputs(self.h, *[ctypes.byref(x) for x in ptr]), "ddec_outputs")
+        self.be.synchronize()
+        NQ, D = self.hp["num_queries"], self.hp["d_model"]
+        outs = [np.empty((NQ + 1, D), np.float32), np.empty((NQ, 4), np.float32), np.empty(NQ, np.float32),
+                np.empty(1, np.float32)]
+        for p, o in zip(ptr, outs):
+            _check(lib().sam3b200_tensor_get(self.be.h, p.value, o.ctypes.data, 0, o.nbytes), "tensor_get")
+        return dict(queries=outs[0], boxes=outs[1], scores=outs[2], presence=float(outs[3][0]))
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_ddec_free(self.h)
+            self.h = None
+
+
+class SegHead:
+    """The detector's segmentation head (sam3b200_seg) on a backend."""
+
+    FIELDS = ("d_model", "heads", "feat", "max_queries", "max_prompt")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 5)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_seg_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"seg_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        """tensors: name -> (ggml type, array, ne)"""
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_seg_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_seg_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} seg tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, enc, fpn0, fpn1, queries, text, text_bias=None) -> np.ndarray:
+        """Host f32 token-major inputs -> mask logits [n_queries][(4 feat)^2]."""
+        e, f0, f1, q, tx = (np.ascontiguousarray(a, np.float32) for a in (enc, fpn0, fpn1, queries, text))
+        tb = None if text_bias is None else np.ascontiguousarray(text_bias, np.float32)
+        _check(lib().sam3b200_seg_run(self.h, e.ctypes.data, f0.ctypes.data, f1.ctypes.data, q.ctypes.data, q.shape[0],
+                                      tx.ctypes.data, None if tb is None else tb.ctypes.data, tx.shape[0]), "seg_run")
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_seg_output(self.h, ctypes.byref(p)), "seg_output")
+        self.be.synchronize()
+        out = np.empty((q.shape[0], 16 * self.hp["feat"] ** 2), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_seg_free(self.h)
+            self.h = None
+
+
 class Backend:
     def __init__(self, device: int = 0):
         self.h = lib().sam3b200_backend_init(device)
@@ -726,6 +830,12 @@ class Backend:
 
     def fusion_encoder(self, hp: dict) -> FusionEncoder:
         return FusionEncoder(self, hp)
+
+    def detr_decoder(self, hp: dict) -> DetrDecoder:
+        return DetrDecoder(self, hp)
+
+    def seg_head(self, hp: dict) -> SegHead:
+        return SegHead(self, hp)
 
     def free(self) -> None:
         if self.h:

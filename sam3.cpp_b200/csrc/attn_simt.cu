@@ -11,11 +11,14 @@
 namespace b200 {
 namespace {
 
-template <int DQ>
+__device__ __forceinline__ float mask_value(__half m) { return __half2float(m); }
+__device__ __forceinline__ float mask_value(float m) { return m; }
+
+template <int DQ, typename MT>
 __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict__ q, AttnStrides qs, int NQ,
                                                         const float *__restrict__ k, AttnStrides ks,
                                                         const float *__restrict__ v, AttnStrides vs, int NKV, int heads,
-                                                        const __half *__restrict__ mask, int64_t mask_ld,
+                                                        const MT *__restrict__ mask, int64_t mask_ld, int64_t mask_hs,
                                                         float scale_log2, float *__restrict__ o, AttnStrides os) {
     constexpr int HD = 4 * DQ, KT = 64;
     constexpr float LOG2E = 1.4426950408889634f;
@@ -33,7 +36,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
         qv[i] = valid ? qr[i] * scale_log2 : 0.f;
         acc[i] = 0.f;
     }
-    const __half *mrow = mask ? mask + static_cast<int64_t>(valid ? row : 0) * mask_ld : nullptr;
+    const MT *mrow = mask ? mask + h * mask_hs + static_cast<int64_t>(valid ? row : 0) * mask_ld : nullptr;
     float m = -INFINITY, l = 0.f;
     for (int j0 = 0; j0 < NKV; j0 += KT) {
         __syncthreads();
@@ -57,7 +60,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
             s += __shfl_xor_sync(0xffffffffu, s, 1);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
             if (mrow) {
-                const float mv = __half2float(mrow[j0 + kk]);
+                const float mv = mask_value(mrow[j0 + kk]);
                 if (mv == -INFINITY) continue;  // the 4 threads of a row agree
                 s = fmaf(mv, LOG2E, s);
             }
@@ -83,17 +86,44 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
     }
 }
 
-template <int DQ>
+template <int DQ, typename MT>
 cudaError_t launch(const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks, const float *v,
-                   AttnStrides vs, int NKV, int batch, int heads, const __half *mask, int64_t mask_ld, float scale,
-                   float *o, AttnStrides os, cudaStream_t s) {
+                   AttnStrides vs, int NKV, int batch, int heads, const MT *mask, int64_t mask_ld, int64_t mask_hs,
+                   float scale, float *o, AttnStrides os, cudaStream_t s) {
     const int smem = 2 * 64 * 4 * DQ * 4;
-    cudaError_t e = cudaFuncSetAttribute(attn_simt_kernel<DQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_simt_kernel<DQ, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((NQ + 63) / 64, static_cast<unsigned>(batch * heads));
-    attn_simt_kernel<DQ><<<grid, 256, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld,
-                                                 scale * 1.4426950408889634f, o, os);
+    attn_simt_kernel<DQ, MT><<<grid, 256, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld, mask_hs,
+                                                     scale * 1.4426950408889634f, o, os);
     return cudaGetLastError();
+}
+
+template <typename MT>
+cudaError_t dispatch(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks, const float *v,
+                     AttnStrides vs, int NKV, int batch, int heads, const MT *mask, int64_t mask_ld, int64_t mask_hs,
+                     float scale, float *o, AttnStrides os, cudaStream_t s) {
+    if (NQ <= 0 || NKV <= 0 || batch <= 0 || heads <= 0 || static_cast<int64_t>(batch) * heads > 65535 ||
+        (mask && (mask_ld < NKV || mask_hs < 0)))
+        return cudaErrorInvalidValue;
+#define B200_ATTN_CASE(d)                                                                                            \
+    case 4 * d:                                                                                                      \
+        return launch<d, MT>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, mask_hs, scale, o, os, s)
+    switch (D) {
+        B200_ATTN_CASE(4);
+        B200_ATTN_CASE(8);
+        B200_ATTN_CASE(12);
+        B200_ATTN_CASE(14);
+        B200_ATTN_CASE(16);
+        B200_ATTN_CASE(18);
+        B200_ATTN_CASE(24);
+        B200_ATTN_CASE(28);
+        B200_ATTN_CASE(32);
+        B200_ATTN_CASE(64);
+    default: return cudaErrorInvalidValue;
+    }
+#undef B200_ATTN_CASE
 }
 
 }  // namespace
@@ -101,22 +131,14 @@ cudaError_t launch(const float *q, AttnStrides qs, int NQ, const float *k, AttnS
 cudaError_t attention_simt(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
                            const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                            int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s) {
-    if (NQ <= 0 || NKV <= 0 || batch <= 0 || heads <= 0 || static_cast<int64_t>(batch) * heads > 65535 ||
-        (mask && mask_ld < NKV))
-        return cudaErrorInvalidValue;
-    switch (D) {
-    case 16: return launch<4>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 32: return launch<8>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 48: return launch<12>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 56: return launch<14>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 64: return launch<16>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 72: return launch<18>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 96: return launch<24>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 112: return launch<28>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 128: return launch<32>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 256: return launch<64>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    default: return cudaErrorInvalidValue;
-    }
+    return dispatch<__half>(D, q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, 0, scale, o, os, s);
+}
+
+cudaError_t attention_simt_f32mask(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                   const float *v, AttnStrides vs, int NKV, int batch, int heads, const float *mask,
+                                   int64_t mask_ld, int64_t mask_hs, float scale, float *o, AttnStrides os,
+                                   cudaStream_t s) {
+    return dispatch<float>(D, q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, mask_hs, scale, o, os, s);
 }
 
 }  // namespace b200

@@ -25,4 +25,12 @@ cudaError_t attention_simt(int D, const float *q, AttnStrides qs, int NQ, const 
                            const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                            int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s);
 
+// The same with an f32 mask per head: head h of query row n reads
+// mask[h * mask_hs + n * mask_ld + k] (the SOFT_MAX_EXT mask the reference
+// keeps in f32 for the detector's box-relative bias, sam3.cpp:8580-8590).
+cudaError_t attention_simt_f32mask(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                   const float *v, AttnStrides vs, int NKV, int batch, int heads, const float *mask,
+                                   int64_t mask_ld, int64_t mask_hs, float scale, float *o, AttnStrides os,
+                                   cudaStream_t s);
+
 }  // namespace b200
