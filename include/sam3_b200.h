@@ -569,6 +569,54 @@ int sam3b200_vit_run_prefix(sam3b200_vit *vit, const float *img_chw_dev, float *
 int sam3b200_vit_run_block(sam3b200_vit *vit, int idx, float *x_dev);
 int sam3b200_vit_run_neck(sam3b200_vit *vit, const float *x_dev);
 
+/* ---- Weight files (sam3_load_model / sam3_load_tensors) -------------------
+ * The format sam3.cpp reads (sam3.cpp:3095-3198, 3204-3330): magic "sam3"
+ * (version 3) or "sam2" (version 1), ftype, tensor count, the int32
+ * hyper-parameter words of sam3_load_hparams / sam2_load_hparams
+ * (:1481-1525, :1568-1630), then per tensor n_dims, name length, ggml type,
+ * ne[0..n_dims), the name, zero padding to a 32-byte file offset and the data.
+ * Opening scans the records (no tensor data is read and no GPU is used). */
+typedef struct sam3b200_file sam3b200_file;
+
+sam3b200_file *sam3b200_file_open(const char *path);
+void sam3b200_file_close(sam3b200_file *f);
+int sam3b200_file_info(const sam3b200_file *f, uint32_t *magic, int32_t *version, int32_t *ftype,
+                       int32_t *n_tensors);
+/* Copies up to cap hyper-parameter words; returns how many the file holds. */
+int sam3b200_file_hparams(const sam3b200_file *f, int32_t *words, int cap);
+/* Record i: name, ggml type, ne[4] (1-padded), data offset and size in bytes. */
+int sam3b200_file_tensor(const sam3b200_file *f, int i, char *name, int name_cap, int32_t *type, int64_t ne[4],
+                         int64_t *offset, int64_t *bytes);
+/* Runner hyper-parameters derived from the file (SAM3: ViT + text; SAM2: Hiera). */
+int sam3b200_file_vit_hparams(const sam3b200_file *f, sam3b200_vit_hparams *out);
+int sam3b200_file_text_hparams(const sam3b200_file *f, sam3b200_text_hparams *out);
+int sam3b200_file_hiera_hparams(const sam3b200_file *f, sam3b200_hiera_hparams *out);
+
+/* The runners a file's tensors go to, by name prefix: "vit."/"neck.trk."
+ * -> vit, "hiera."/"fpn." -> hiera, "text." -> text, "sam_pe."/"sam_dec."/
+ * "no_mem_embed" -> sam_dec, "mem_attn." -> mem_attn, "mem_enc."/
+ * "no_obj_embed_spatial" -> mem_enc, "fenc." -> fenc, "ddec."/"scoring." ->
+ * ddec, "seg." -> seg.  A NULL runner leaves its tensors skipped. */
+typedef struct {
+    sam3b200_vit *vit;
+    sam3b200_hiera *hiera;
+    sam3b200_text *text;
+    sam3b200_sam_dec *sam_dec;
+    sam3b200_mem_attn *mem_attn;
+    sam3b200_mem_enc *mem_enc;
+    sam3b200_fenc *fenc;
+    sam3b200_ddec *ddec;
+    sam3b200_seg *seg;
+} sam3b200_model_parts;
+
+/* Stream every tensor to its runner through two pinned staging buffers (a
+ * reader thread overlaps the file reads with the device copies).  Fails on
+ * the first tensor a runner rejects; counts loaded and skipped tensors. */
+int sam3b200_file_load(sam3b200_file *f, sam3b200_backend *be, const sam3b200_model_parts *parts,
+                       int64_t *n_loaded, int64_t *n_skipped);
+/* Names of the tensors the last load skipped, newline-separated; returns the count. */
+int sam3b200_file_skipped(const sam3b200_file *f, char *buf, int cap);
+
 #ifdef __cplusplus
 }
 #endif

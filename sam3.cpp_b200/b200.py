@@ -131,6 +131,16 @@ def lib() -> ctypes.CDLL:
         "sam3b200_seg_run": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
         "sam3b200_seg_run_device": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
         "sam3b200_seg_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_file_open": (vp, [ctypes.c_char_p]),
+        "sam3b200_file_close": (None, [vp]),
+        "sam3b200_file_info": (i32, [vp, vp, vp, vp, vp]),
+        "sam3b200_file_hparams": (i32, [vp, vp, i32]),
+        "sam3b200_file_tensor": (i32, [vp, i32, ctypes.c_char_p, i32, vp, vp, vp, vp]),
+        "sam3b200_file_vit_hparams": (i32, [vp, vp]),
+        "sam3b200_file_text_hparams": (i32, [vp, vp]),
+        "sam3b200_file_hiera_hparams": (i32, [vp, vp]),
+        "sam3b200_file_load": (i32, [vp, vp, vp, vp, vp]),
+        "sam3b200_file_skipped": (i32, [vp, ctypes.c_char_p, i32]),
         "sam3b200_hiera_create": (vp, [vp, vp]),
         "sam3b200_hiera_free": (None, [vp]),
         "sam3b200_hiera_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -225,6 +235,12 @@ class VitHparams(ctypes.Structure):
         for i, v in enumerate(g):
             h.global_idx[i] = int(v)
         return h
+
+    def to_dict(self) -> dict:
+        d = {k: getattr(self, k) for k in ("img", "patch", "embed", "depth", "heads", "mlp", "window", "pos_grid",
+                                           "neck_dim", "wtype")}
+        d["global_idx"] = tuple(self.global_idx[:self.n_global])
+        return d
 
 
 class Vit:
@@ -703,6 +719,74 @@ class SegHead:
     def free(self) -> None:
         if self.h:
             lib().sam3b200_seg_free(self.h)
+            self.h = None
+
+
+class WeightFile:
+    """A sam3.cpp weight file opened by the native reader (sam3b200_file_*); opening reads the header,
+    hyper-parameters and tensor directory only."""
+
+    PART_NAMES = ("vit", "hiera", "text", "sam_dec", "mem_attn", "mem_enc", "fenc", "ddec", "seg")
+
+    def __init__(self, path: str):
+        self.h = lib().sam3b200_file_open(str(path).encode())
+        if not self.h:
+            raise B200Error(f"file_open failed: {last_error()}")
+
+    def info(self) -> dict:
+        m, v, f, n = ctypes.c_uint32(), ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        _check(lib().sam3b200_file_info(self.h, ctypes.byref(m), ctypes.byref(v), ctypes.byref(f), ctypes.byref(n)),
+               "file_info")
+        return dict(magic=m.value, version=v.value, ftype=f.value, n_tensors=n.value)
+
+    def hparams(self) -> list[int]:
+        n = lib().sam3b200_file_hparams(self.h, None, 0)
+        words = (ctypes.c_int32 * max(n, 1))()
+        lib().sam3b200_file_hparams(self.h, words, n)
+        return list(words)[:n]
+
+    def tensors(self) -> list[dict]:
+        out = []
+        for i in range(self.info()["n_tensors"]):
+            name = ctypes.create_string_buffer(4097)
+            t, ne, off, nb = ctypes.c_int32(), (ctypes.c_int64 * 4)(), ctypes.c_int64(), ctypes.c_int64()
+            _check(lib().sam3b200_file_tensor(self.h, i, name, 4097, ctypes.byref(t), ne, ctypes.byref(off),
+                                              ctypes.byref(nb)), "file_tensor")
+            out.append(dict(name=name.value.decode(), type=t.value, ne=tuple(ne), offset=off.value, bytes=nb.value))
+        return out
+
+    def vit_hparams(self) -> "VitHparams":
+        h = VitHparams()
+        _check(lib().sam3b200_file_vit_hparams(self.h, ctypes.byref(h)), "file_vit_hparams")
+        return h
+
+    def text_hparams(self) -> dict:
+        h = (ctypes.c_int32 * 6)()
+        _check(lib().sam3b200_file_text_hparams(self.h, h), "file_text_hparams")
+        return dict(zip(TextEncoder.FIELDS, list(h)))
+
+    def hiera_hparams(self) -> "HieraHparams":
+        h = HieraHparams()
+        _check(lib().sam3b200_file_hiera_hparams(self.h, ctypes.byref(h)), "file_hiera_hparams")
+        return h
+
+    def load(self, backend: "Backend", **parts) -> tuple[int, int]:
+        """Stream the tensors to the given runners (keyword per PART_NAMES, e.g. vit=Vit(...));
+        returns (loaded, skipped)."""
+        ptrs = (ctypes.c_void_p * len(self.PART_NAMES))(*[parts[k].h if k in parts else None for k in self.PART_NAMES])
+        loaded, skipped = ctypes.c_int64(), ctypes.c_int64()
+        _check(lib().sam3b200_file_load(self.h, backend.h, ptrs, ctypes.byref(loaded), ctypes.byref(skipped)),
+               "file_load")
+        return loaded.value, skipped.value
+
+    def skipped(self) -> list[str]:
+        buf = ctypes.create_string_buffer(1 << 20)
+        lib().sam3b200_file_skipped(self.h, buf, len(buf))
+        return [s for s in buf.value.decode().split("\n") if s]
+
+    def close(self) -> None:
+        if self.h:
+            lib().sam3b200_file_close(self.h)
             self.h = None
 
 
