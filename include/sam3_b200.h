@@ -499,6 +499,39 @@ int sam3b200_seg_run_device(sam3b200_seg *h, const float *enc, const float *fpn0
 /* Mask logits: device f32 [(4 feat)^2, n_queries] (memory [n_queries][pixels]). */
 int sam3b200_seg_output(sam3b200_seg *h, const float **dev);
 
+/* ---- Geometry (exemplar-prompt) encoder of the SAM3 detector --------------
+ * The transformer of sam3_build_geom_enc_graph (sam3.cpp:7677-7800) over the
+ * geometry tokens the host prepares (box embeddings + CLS after the final
+ * projection and norm, sam3_precompute_geom_input): `layers` pre-LN layers
+ * of self-attention (no position), cross-attention to the image (keys from
+ * features + positional code, values from features), ReLU FFN, then
+ * geom.encode_norm.  Weights by name (sam3.cpp:2821-2842):
+ * "geom.layers.<i>.*", "geom.encode_norm.*"; the other "geom.*" tensors feed
+ * the host-side token preparation. */
+typedef struct {
+    int32_t d_model;           /* 256 */
+    int32_t heads;             /* 8 */
+    int32_t layers;            /* 3 (geom_layers) */
+    int32_t ffn_dim;           /* 2048 */
+    int32_t max_tokens;        /* capacity: exemplar boxes + 1 */
+    int32_t max_image_tokens;  /* capacity: image tokens (72 * 72) */
+} sam3b200_geom_hparams;
+
+typedef struct sam3b200_geom sam3b200_geom;
+
+sam3b200_geom *sam3b200_geom_create(sam3b200_backend *be, const sam3b200_geom_hparams *hp);
+void sam3b200_geom_free(sam3b200_geom *g);
+int sam3b200_geom_set_tensor(sam3b200_geom *g, const char *name, int type, const void *data, const int64_t ne[4]);
+int sam3b200_geom_missing(sam3b200_geom *g, char *buf, int cap);
+/* Host inputs: tokens [d_model, n_tokens], img_feats and img_pe
+ * [d_model, n_image]. */
+int sam3b200_geom_run(sam3b200_geom *g, const float *tokens, int n_tokens, const float *img_feats,
+                      const float *img_pe, int n_image);
+int sam3b200_geom_run_device(sam3b200_geom *g, const float *tokens, int n_tokens, const float *img_feats,
+                             const float *img_pe, int n_image);
+/* Encoded geometry tokens: device f32 [d_model, n_tokens]. */
+int sam3b200_geom_output(sam3b200_geom *g, const float **dev);
+
 /* ---- SAM3 visual encoder (sam3_encode_image for a visual-only model) ----
  *
  * Hyper-parameters of the ViT + tracker neck, the fields sam3_hparams holds
@@ -596,7 +629,8 @@ int sam3b200_file_hiera_hparams(const sam3b200_file *f, sam3b200_hiera_hparams *
  * -> vit, "hiera."/"fpn." -> hiera, "text." -> text, "sam_pe."/"sam_dec."/
  * "no_mem_embed" -> sam_dec, "mem_attn." -> mem_attn, "mem_enc."/
  * "no_obj_embed_spatial" -> mem_enc, "fenc." -> fenc, "ddec."/"scoring." ->
- * ddec, "seg." -> seg.  A NULL runner leaves its tensors skipped. */
+ * ddec, "seg." -> seg, "geom.layers."/"geom.encode_norm." -> geom.  A NULL
+ * runner leaves its tensors skipped. */
 typedef struct {
     sam3b200_vit *vit;
     sam3b200_hiera *hiera;
@@ -607,6 +641,7 @@ typedef struct {
     sam3b200_fenc *fenc;
     sam3b200_ddec *ddec;
     sam3b200_seg *seg;
+    sam3b200_geom *geom;
 } sam3b200_model_parts;
 
 /* Stream every tensor to its runner through two pinned staging buffers (a

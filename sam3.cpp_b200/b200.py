@@ -131,6 +131,13 @@ def lib() -> ctypes.CDLL:
         "sam3b200_seg_run": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
         "sam3b200_seg_run_device": (i32, [vp, vp, vp, vp, vp, i32, vp, vp, i32]),
         "sam3b200_seg_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_geom_create": (vp, [vp, vp]),
+        "sam3b200_geom_free": (None, [vp]),
+        "sam3b200_geom_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_geom_missing": (i32, [vp, ctypes.c_char_p, i32]),
+        "sam3b200_geom_run": (i32, [vp, vp, i32, vp, vp, i32]),
+        "sam3b200_geom_run_device": (i32, [vp, vp, i32, vp, vp, i32]),
+        "sam3b200_geom_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_file_open": (vp, [ctypes.c_char_p]),
         "sam3b200_file_close": (None, [vp]),
         "sam3b200_file_info": (i32, [vp, vp, vp, vp, vp]),
@@ -722,11 +729,51 @@ class SegHead:
             self.h = None
 
 
+class GeometryEncoder:
+    """The detector's geometry (exemplar-prompt) encoder transformer (sam3b200_geom) on a backend."""
+
+    FIELDS = ("d_model", "heads", "layers", "ffn_dim", "max_tokens", "max_image_tokens")
+
+    def __init__(self, be: "Backend", hp: dict):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * 6)(*[int(hp[k]) for k in self.FIELDS])
+        self.h = lib().sam3b200_geom_create(be.h, ctypes.byref(self._chp))
+        if not self.h:
+            raise B200Error(f"geom_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_geom_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+        buf = ctypes.create_string_buffer(1 << 16)
+        n = lib().sam3b200_geom_missing(self.h, buf, len(buf))
+        if n:
+            raise B200Error(f"{n} geom tensors missing: {buf.value.decode()[:300]}")
+
+    def run(self, tokens, img_feats, img_pe) -> np.ndarray:
+        """Host f32 token-major tokens [S][D], img_feats / img_pe [N][D] -> encoded tokens [S][D]."""
+        x, im, pe = (np.ascontiguousarray(a, np.float32) for a in (tokens, img_feats, img_pe))
+        _check(lib().sam3b200_geom_run(self.h, x.ctypes.data, x.shape[0], im.ctypes.data, pe.ctypes.data, im.shape[0]),
+               "geom_run")
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_geom_output(self.h, ctypes.byref(p)), "geom_output")
+        self.be.synchronize()
+        out = np.empty(x.shape, np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_geom_free(self.h)
+            self.h = None
+
+
 class WeightFile:
     """A sam3.cpp weight file opened by the native reader (sam3b200_file_*); opening reads the header,
     hyper-parameters and tensor directory only."""
 
-    PART_NAMES = ("vit", "hiera", "text", "sam_dec", "mem_attn", "mem_enc", "fenc", "ddec", "seg")
+    PART_NAMES = ("vit", "hiera", "text", "sam_dec", "mem_attn", "mem_enc", "fenc", "ddec", "seg", "geom")
 
     def __init__(self, path: str):
         self.h = lib().sam3b200_file_open(str(path).encode())
@@ -920,6 +967,9 @@ class Backend:
 
     def seg_head(self, hp: dict) -> SegHead:
         return SegHead(self, hp)
+
+    def geometry_encoder(self, hp: dict) -> GeometryEncoder:
+        return GeometryEncoder(self, hp)
 
     def free(self) -> None:
         if self.h:

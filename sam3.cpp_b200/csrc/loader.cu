@@ -186,6 +186,8 @@ int route(const sam3b200_model_parts *m, const std::string &n, int type, const v
     if (m->ddec && (starts(n, "ddec.") || starts(n, "scoring.")))
         return sam3b200_ddec_set_tensor(m->ddec, n.c_str(), type, data, ne);
     if (m->seg && starts(n, "seg.")) return sam3b200_seg_set_tensor(m->seg, n.c_str(), type, data, ne);
+    if (m->geom && (starts(n, "geom.layers.") || starts(n, "geom.encode_norm.")))
+        return sam3b200_geom_set_tensor(m->geom, n.c_str(), type, data, ne);
     *taken = false;
     return SAM3B200_STATUS_SUCCESS;
 }
