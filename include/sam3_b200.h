@@ -583,6 +583,11 @@ int sam3b200_encode_image_device(sam3b200_vit *vit, const uint8_t *rgb_dev, int 
 /* Device pointer and ggml shape of output i (0..3 = neck_trk_i, -1 = the
  * ViT output [embed, G, G]) of the last encode. */
 int sam3b200_vit_output(sam3b200_vit *vit, int i, const float **dev, int64_t ne[4]);
+/* The detector neck's level i (0..3) of the last encode, same layout: a full
+ * (not visual-only) SAM3 model runs both necks of sam3_build_neck_graph
+ * (sam3.cpp:3867-3925) on the ViT output, "neck.det.<s>.*" weights beside
+ * "neck.trk.<s>.*"; fails when no neck.det tensor was set. */
+int sam3b200_vit_output_det(sam3b200_vit *vit, int i, const float **dev, int64_t ne[4]);
 
 /* sam3_preprocess_image (sam3.cpp:3490-3518, with sam3_resize_bilinear
  * :3445-3485 when w x h != img x img): device uint8 RGB HWC -> device f32
@@ -625,8 +630,8 @@ int sam3b200_file_vit_hparams(const sam3b200_file *f, sam3b200_vit_hparams *out)
 int sam3b200_file_text_hparams(const sam3b200_file *f, sam3b200_text_hparams *out);
 int sam3b200_file_hiera_hparams(const sam3b200_file *f, sam3b200_hiera_hparams *out);
 
-/* The runners a file's tensors go to, by name prefix: "vit."/"neck.trk."
- * -> vit, "hiera."/"fpn." -> hiera, "text." -> text, "sam_pe."/"sam_dec."/
+/* The runners a file's tensors go to, by name prefix: "vit."/"neck.trk."/
+ * "neck.det." -> vit, "hiera."/"fpn." -> hiera, "text." -> text, "sam_pe."/"sam_dec."/
  * "no_mem_embed" -> sam_dec, "mem_attn." -> mem_attn, "mem_enc."/
  * "no_obj_embed_spatial" -> mem_enc, "fenc." -> fenc, "ddec."/"scoring." ->
  * ddec, "seg." -> seg, "geom.layers."/"geom.encode_norm." -> geom.  A NULL

@@ -253,7 +253,7 @@ class OracleVit:
     """CPU restatement of the SAM3 visual encoder over a tensor dict
     (name -> (ggml type, array, ne), as produced by model.random_vit_weights)."""
 
-    def __init__(self, hp: dict, tensors: dict, n_threads: int = 0):
+    def __init__(self, hp: dict, tensors: dict, n_threads: int = 0, neck_prefix: str = "neck.trk."):
         self.hp, self.t = dict(hp), tensors
         self.nt = n_threads or (os.cpu_count() or 1)
         self.G = hp["img"] // hp["patch"]
@@ -279,7 +279,7 @@ class OracleVit:
             b.fc1_w, b.fc1_b = self._p(pre + "mlp.lin1.weight"), self._p(pre + "mlp.lin1.bias")
             b.fc2_w, b.fc2_b = self._p(pre + "mlp.lin2.weight"), self._p(pre + "mlp.lin2.bias")
             b.freqs = self._p(pre + "attn.freqs_cis")
-        pre = "neck.trk."
+        pre = neck_prefix  # the tracker's neck, or "neck.det." for the detector's (same graph)
         names = {0: ("0.dconv_2x2_0", "0.dconv_2x2_1"), 1: ("1.dconv_2x2", None), 2: (None, None), 3: (None, None)}
         for s in range(4):
             nw = w.neck[s]

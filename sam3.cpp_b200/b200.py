@@ -138,6 +138,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_geom_run": (i32, [vp, vp, i32, vp, vp, i32]),
         "sam3b200_geom_run_device": (i32, [vp, vp, i32, vp, vp, i32]),
         "sam3b200_geom_output": (i32, [vp, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_vit_output_det": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p), vp]),
         "sam3b200_file_open": (vp, [ctypes.c_char_p]),
         "sam3b200_file_close": (None, [vp]),
         "sam3b200_file_info": (i32, [vp, vp, vp, vp, vp]),
@@ -299,6 +300,16 @@ class Vit:
         self.be.synchronize()
         out = np.empty((ne[2], ne[1], ne[0]), np.float32)
         _check(lib().sam3b200_tensor_get(self.be.h, ptr, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
+    def output_det_host(self, i: int) -> np.ndarray:
+        """Detector-neck level i (full SAM3 models): f32 [side, side, neck_dim]."""
+        p = ctypes.c_void_p()
+        ne = (ctypes.c_int64 * 4)()
+        _check(lib().sam3b200_vit_output_det(self.h, i, ctypes.byref(p), ne), "vit_output_det")
+        self.be.synchronize()
+        out = np.empty((ne[2], ne[1], ne[0]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
         return out
 
     def run_prefix(self, img_chw: "DeviceBuffer", x: "DeviceBuffer") -> None:

@@ -42,10 +42,12 @@ struct Vit {
     DevBuf patch_w, pos, lnpre_w, lnpre_b;
     std::vector<BlockW> blk;
     NeckScaleW neck[4];
+    NeckScaleW neck_det[4];  // detector neck (full SAM3 models): same graph, its own weights
+    bool det_any = false;    // a neck.det tensor was set
     std::vector<std::string> missing;
     // activations
     DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, q, k, v, rowmap;
-    DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4];
+    DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4], out_det[4];
     int out_side[4] = {0, 0, 0, 0};
     int img_cap = 0;  // pixels of img_u8
 };
@@ -200,36 +202,41 @@ static bool run_block(Vit *v, int i, float *x) {
                0);
 }
 
-static bool run_neck(Vit *v, const float *x) {
+// sam3_build_neck_graph (sam3.cpp:3867-3925) with the scale weights n, writing outs[0..3]
+static bool run_neck(Vit *v, const float *x, const NeckScaleW *n, DevBuf *outs) {
     const auto &hp = v->hp;
     cudaStream_t s = v->be->stream;
     const int E = hp.embed, G = v->G, T = v->T, D = hp.neck_dim, MID = v->MID;
-    const NeckScaleW *n = v->neck;
     if (!launched(v, f32_to_f16(x, static_cast<int64_t>(T) * E, v->x16.p, s), "f32_to_f16")) return false;
     // scale 0: ConvT(E->512)+GELU, ConvT(512->D), conv1x1, conv3x3 at 4G
     if (!gemm(v, v->x16.p, n[0].dc1, T, 4 * MID, E, &n[0].dc1_b, 1, 1, v->n_a.p, GEMM_STORE_CONVT2X2, G, MID) ||
         !gemm(v, v->n_a.p, n[0].dc2, 4 * T, 4 * D, MID, &n[0].dc2_b, 0, 1, v->n_c.p, GEMM_STORE_CONVT2X2, 2 * G, D) ||
         !gemm(v, v->n_c.p, n[0].c1, 16 * T, D, D, &n[0].c1_b, 0, 1, v->n_d.p, GEMM_STORE_ROWMAJOR, 0, 0) ||
         !launched(v, im2col3x3_f16(v->n_d.p, 4 * G, 4 * G, D, v->n_col.p, s), "im2col") ||
-        !gemm(v, v->n_col.p, n[0].c3, 16 * T, D, 9 * D, &n[0].c3_b, 0, 0, v->out[0].p, GEMM_STORE_ROWMAJOR, 0, 0))
+        !gemm(v, v->n_col.p, n[0].c3, 16 * T, D, 9 * D, &n[0].c3_b, 0, 0, outs[0].p, GEMM_STORE_ROWMAJOR, 0, 0))
         return false;
     // scale 1: ConvT(E->512), conv1x1(512->D), conv3x3 at 2G
     if (!gemm(v, v->x16.p, n[1].dc1, T, 4 * MID, E, &n[1].dc1_b, 0, 1, v->n_a.p, GEMM_STORE_CONVT2X2, G, MID) ||
         !gemm(v, v->n_a.p, n[1].c1, 4 * T, D, MID, &n[1].c1_b, 0, 1, v->n_d.p, GEMM_STORE_ROWMAJOR, 0, 0) ||
         !launched(v, im2col3x3_f16(v->n_d.p, 2 * G, 2 * G, D, v->n_col.p, s), "im2col") ||
-        !gemm(v, v->n_col.p, n[1].c3, 4 * T, D, 9 * D, &n[1].c3_b, 0, 0, v->out[1].p, GEMM_STORE_ROWMAJOR, 0, 0))
+        !gemm(v, v->n_col.p, n[1].c3, 4 * T, D, 9 * D, &n[1].c3_b, 0, 0, outs[1].p, GEMM_STORE_ROWMAJOR, 0, 0))
         return false;
     // scale 2: conv1x1(E->D), conv3x3 at G
     if (!gemm(v, v->x16.p, n[2].c1, T, D, E, &n[2].c1_b, 0, 1, v->n_d.p, GEMM_STORE_ROWMAJOR, 0, 0) ||
         !launched(v, im2col3x3_f16(v->n_d.p, G, G, D, v->n_col.p, s), "im2col") ||
-        !gemm(v, v->n_col.p, n[2].c3, T, D, 9 * D, &n[2].c3_b, 0, 0, v->out[2].p, GEMM_STORE_ROWMAJOR, 0, 0))
+        !gemm(v, v->n_col.p, n[2].c3, T, D, 9 * D, &n[2].c3_b, 0, 0, outs[2].p, GEMM_STORE_ROWMAJOR, 0, 0))
         return false;
     // scale 3: maxpool 2x2, conv1x1(E->D), conv3x3 at G/2
     const int g = G / 2;
     return launched(v, maxpool2x2_f16(x, G, E, v->mp16.p, s), "maxpool") &&
            gemm(v, v->mp16.p, n[3].c1, g * g, D, E, &n[3].c1_b, 0, 1, v->n_d.p, GEMM_STORE_ROWMAJOR, 0, 0) &&
            launched(v, im2col3x3_f16(v->n_d.p, g, g, D, v->n_col.p, s), "im2col") &&
-           gemm(v, v->n_col.p, n[3].c3, g * g, D, 9 * D, &n[3].c3_b, 0, 0, v->out[3].p, GEMM_STORE_ROWMAJOR, 0, 0);
+           gemm(v, v->n_col.p, n[3].c3, g * g, D, 9 * D, &n[3].c3_b, 0, 0, outs[3].p, GEMM_STORE_ROWMAJOR, 0, 0);
+}
+
+// both necks: the tracker's, then the detector's when its weights are set
+static bool run_necks(Vit *v, const float *x) {
+    return run_neck(v, x, v->neck, v->out) && (!v->det_any || run_neck(v, x, v->neck_det, v->out_det));
 }
 
 static bool check_ready(Vit *v) {
@@ -266,11 +273,15 @@ static bool check_ready(Vit *v) {
          "2.conv_3x3.bias"},
         {nullptr, nullptr, nullptr, nullptr, "3.conv_1x1.weight", "3.conv_1x1.bias", "3.conv_3x3.weight",
          "3.conv_3x3.bias"}};
-    for (int sc = 0; sc < 4; ++sc) {
-        const DevBuf *bufs[8] = {&v->neck[sc].dc1, &v->neck[sc].dc1_b, &v->neck[sc].dc2, &v->neck[sc].dc2_b,
-                                 &v->neck[sc].c1,  &v->neck[sc].c1_b,  &v->neck[sc].c3,  &v->neck[sc].c3_b};
-        for (int j = 0; j < 8; ++j)
-            if (sn[sc][j]) need(*bufs[j], std::string("neck.trk.") + sn[sc][j]);
+    for (int which = 0; which < (v->det_any ? 2 : 1); ++which) {
+        const NeckScaleW *nk = which == 0 ? v->neck : v->neck_det;
+        const std::string pre = which == 0 ? "neck.trk." : "neck.det.";
+        for (int sc = 0; sc < 4; ++sc) {
+            const DevBuf *bufs[8] = {&nk[sc].dc1, &nk[sc].dc1_b, &nk[sc].dc2, &nk[sc].dc2_b,
+                                     &nk[sc].c1,  &nk[sc].c1_b,  &nk[sc].c3,  &nk[sc].c3_b};
+            for (int j = 0; j < 8; ++j)
+                if (sn[sc][j]) need(*bufs[j], pre + sn[sc][j]);
+        }
     }
     if (!v->missing.empty()) {
         set_error("encoder weights missing: %zu tensors, first %s", v->missing.size(), v->missing[0].c_str());
@@ -293,7 +304,7 @@ static bool encode(Vit *v, const uint8_t *rgb_dev, int w, int h) {
     if (!run_prefix(v, v->img_f32.as<float>(), v->x.as<float>())) return false;
     for (int i = 0; i < hp.depth; ++i)
         if (!run_block(v, i, v->x.as<float>())) return false;
-    return run_neck(v, v->x.as<float>());
+    return run_necks(v, v->x.as<float>());
 }
 
 }  // namespace b200
@@ -416,8 +427,20 @@ int sam3b200_vit_set_tensor(sam3b200_vit *hv, const char *name_c, int type, cons
         return SAM3B200_STATUS_FAILED;
     }
     int sc = -1;
+    NeckScaleW *nwp = nullptr;
     if (sscanf(name_c, "neck.trk.%d.%127s", &sc, tail) == 2 && sc >= 0 && sc < 4) {
-        NeckScaleW &nw = v->neck[sc];
+        nwp = &v->neck[sc];
+    } else if (sscanf(name_c, "neck.det.%d.%127s", &sc, tail) == 2 && sc >= 0 && sc < 4) {
+        if (!v->det_any) {  // first detector-neck tensor: its four outputs
+            for (int i = 0; i < 4; ++i)
+                if (!v->out_det[i].alloc(static_cast<size_t>(v->out_side[i]) * v->out_side[i] * D * 4))
+                    return SAM3B200_STATUS_ALLOC_FAILED;
+            v->det_any = true;
+        }
+        nwp = &v->neck_det[sc];
+    }
+    if (nwp) {
+        NeckScaleW &nw = *nwp;
         const std::string t(tail);
         if (!to_f32(type, data, n, f)) return SAM3B200_STATUS_FAILED;
         auto bias = [&](DevBuf &d, int64_t expect) -> int {
@@ -517,6 +540,22 @@ int sam3b200_encode_image(sam3b200_vit *hv, const uint8_t *rgb, int w, int h, fl
     return sam3b200_backend_synchronize(reinterpret_cast<sam3b200_backend *>(v->be));
 }
 
+int sam3b200_vit_output_det(sam3b200_vit *hv, int i, const float **dev, int64_t *ne) {
+    auto *v = reinterpret_cast<Vit *>(hv);
+    if (!v || i < 0 || i > 3 || !dev) return SAM3B200_STATUS_FAILED;
+    if (!v->det_any) {
+        set_error("vit_output_det: the encoder has no detector neck (neck.det tensors not set)");
+        return SAM3B200_STATUS_FAILED;
+    }
+    *dev = v->out_det[i].as<float>();
+    if (ne) {
+        ne[0] = v->hp.neck_dim;
+        ne[1] = ne[2] = v->out_side[i];
+        ne[3] = 1;
+    }
+    return SAM3B200_STATUS_SUCCESS;
+}
+
 int sam3b200_vit_output(sam3b200_vit *hv, int i, const float **dev, int64_t *ne) {
     auto *v = reinterpret_cast<Vit *>(hv);
     if (!v || i < -1 || i > 3 || !dev) return SAM3B200_STATUS_FAILED;
@@ -588,7 +627,7 @@ int sam3b200_vit_run_neck(sam3b200_vit *hv, const float *x_dev) {
     auto *v = reinterpret_cast<Vit *>(hv);
     if (!v || !x_dev) return SAM3B200_STATUS_FAILED;
     cudaSetDevice(v->be->device);
-    return run_neck(v, x_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+    return run_necks(v, x_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
 }
 
 }  // extern "C"

@@ -173,7 +173,8 @@ bool starts(const std::string &s, const char *p) { return s.compare(0, strlen(p)
 int route(const sam3b200_model_parts *m, const std::string &n, int type, const void *data, const int64_t *ne,
           bool *taken) {
     *taken = true;
-    if (m->vit && (starts(n, "vit.") || starts(n, "neck.trk."))) return sam3b200_vit_set_tensor(m->vit, n.c_str(), type, data, ne);
+    if (m->vit && (starts(n, "vit.") || starts(n, "neck.trk.") || starts(n, "neck.det.")))
+        return sam3b200_vit_set_tensor(m->vit, n.c_str(), type, data, ne);
     if (m->hiera && (starts(n, "hiera.") || starts(n, "fpn.")))
         return sam3b200_hiera_set_tensor(m->hiera, n.c_str(), type, data, ne);
     if (m->text && starts(n, "text.")) return sam3b200_text_set_tensor(m->text, n.c_str(), type, data, ne);

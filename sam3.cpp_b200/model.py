@@ -115,6 +115,12 @@ def random_vit_weights(hp: dict, seed: int = 0) -> dict:
     return t
 
 
+def random_det_neck_weights(hp: dict, seed: int = 0) -> dict:
+    """The detector neck of a full SAM3 model ("neck.det.*", the tracker neck's shapes, sam3.cpp:2556-2600)."""
+    t = random_vit_weights(dict(hp, depth=0), seed=seed)
+    return {k.replace("neck.trk.", "neck.det."): v for k, v in t.items() if k.startswith("neck.trk.")}
+
+
 def random_images(n: int, side: int, seed: int = 0) -> np.ndarray:
     """n seeded uniform uint8 RGB images, HWC."""
     rng = np.random.default_rng(seed)

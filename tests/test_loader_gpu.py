@@ -51,7 +51,7 @@ def test_file_load_matches_set_tensor(tmp_path, oracle, b200, backend, model):
     vit_t = model.random_vit_weights(hp, seed=1)
     txt_t = text_tensors(oracle)
     extra = {"geom.boxes_direct_project.weight": (0, np.zeros((256, 4), np.float32), (4, 256)),
-             "neck.det.0.conv_1x1.bias": (0, np.zeros(256, np.float32), (256,))}
+             "sam_dec.iou_token.weight": (0, np.zeros(256, np.float32), (256, 1))}  # no decoder passed: skipped
     path = tmp_path / "sam3_small.ggml"
     wf.write(str(path), wf.SAM3_MAGIC, wf.SAM3_VERSION, 8, wf.sam3_hparam_words(hp, **TEXT_SMALL),
              {**vit_t, **txt_t, **extra})

@@ -133,3 +133,25 @@ def test_missing_weights_fail_loudly(b200, backend, model):
     with pytest.raises(b200.B200Error):
         vit.set_tensor("vit.blocks.0.attn.qkv.weight", 1, np.zeros(4, np.float32), (2, 2))
     vit.free()
+
+
+def test_detector_neck(model, oracle, backend, small):
+    """A full SAM3 model's second neck ("neck.det.*") on the same ViT output: its four levels match the
+    oracle neck with those weights, and the tracker neck's levels are unchanged by its presence."""
+    hp, tensors, vit_trk, _ = small
+    det = model.random_det_neck_weights(hp, seed=9)
+    vit = backend.vit(hp)
+    try:
+        vit.load({**tensors, **det})
+        rgb = np.random.default_rng(8).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8)
+        trk = vit.encode(rgb)
+        for a, b in zip(trk, vit_trk.encode(rgb)):
+            assert np.array_equal(a, b)
+        x = vit.output_host(-1)
+        od = oracle.OracleVit(hp, {**tensors, **det}, neck_prefix="neck.det.")
+        want = od.neck(x.reshape(-1, hp["embed"]))
+        for i in range(4):
+            got = vit.output_det_host(i)
+            assert rel_err(got.reshape(want[i].shape), want[i]) <= TOL, i
+    finally:
+        vit.free()
