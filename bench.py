@@ -16,6 +16,7 @@ tracker SimpleFPN neck -- the whole of sam3_encode_image.
           device, as in sam3.cpp:6138-6149)
 
 python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+python bench.py --workload pcs|video   (secondary lines: config 4 detector / config 5 tracker stages, 1 GPU)
 """
 from __future__ import annotations
 
@@ -177,6 +178,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video"],
+                    help="encode (default: the headline, config 3); pcs / video: the config 4 detector or the "
+                         "config 5 tracker memory stages, timed per image / frame (sam3.cpp_b200/component_bench.py)")
     ap.add_argument("--images", type=int, default=BATCH,
                     help="images per step (default 64, the config's batch; smaller only for profiling runs)")
     args = ap.parse_args()
@@ -185,6 +189,14 @@ def main():
     hp = dict(model_mod.SAM3_VIT)
     if args.impl == "reference":
         return run_reference(args, hp, model_mod)
+    if args.workload != "encode":
+        b200 = _load("b200")
+        comp = _load("component_bench")
+        be = b200.Backend(0)
+        fn = comp.run_pcs if args.workload == "pcs" else comp.run_video
+        print(json.dumps(fn(b200, model_mod, be, args.steps, args.warmup)), flush=True)
+        be.free()
+        return 0
 
     import torch
     import torch.distributed as dist

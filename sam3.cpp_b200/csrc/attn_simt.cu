@@ -11,6 +11,12 @@
 namespace b200 {
 namespace {
 
+// head dimension owned by register i of row-thread `part` (see attn_simt_kernel)
+template <int DQ, bool VEC>
+__device__ __forceinline__ int dim_of(int i, int part) {
+    return VEC ? (i >> 2) * 16 + part * 4 + (i & 3) : part * DQ + i;
+}
+
 __device__ __forceinline__ float mask_value(__half m) { return __half2float(m); }
 __device__ __forceinline__ float mask_value(float m) { return m; }
 
@@ -22,18 +28,24 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
                                                         float scale_log2, float *__restrict__ o, AttnStrides os) {
     constexpr int HD = 4 * DQ, KT = 64;
     constexpr float LOG2E = 1.4426950408889634f;
+    // Dimension ownership: with DQ % 4 == 0 the 4 threads of a row own
+    // interleaved 4-float chunks (thread p: dims 16 j + 4 p + 0..3), so their
+    // 16-byte shared-memory reads of one key row fall in distinct banks (a
+    // contiguous DQ-float slice per thread would put all four in one bank
+    // group: 4-way conflicts on every read); otherwise contiguous slices.
+    constexpr bool VEC = DQ % 4 == 0;
     extern __shared__ float sm[];
     float *ksm = sm, *vsm = sm + KT * HD;
     const int b = blockIdx.y / heads, h = blockIdx.y % heads;
-    const int row = blockIdx.x * 64 + (threadIdx.x >> 2), part = threadIdx.x & 3;
+    const int row = blockIdx.x * (blockDim.x >> 2) + (threadIdx.x >> 2), part = threadIdx.x & 3;
     const bool valid = row < NQ;
     const float *kb = k + b * ks.b + h * ks.h;
     const float *vb = v + b * vs.b + h * vs.h;
     float qv[DQ], acc[DQ];
-    const float *qr = q + b * qs.b + h * qs.h + static_cast<int64_t>(valid ? row : 0) * qs.n + part * DQ;
+    const float *qr = q + b * qs.b + h * qs.h + static_cast<int64_t>(valid ? row : 0) * qs.n;
 #pragma unroll
     for (int i = 0; i < DQ; ++i) {
-        qv[i] = valid ? qr[i] * scale_log2 : 0.f;
+        qv[i] = valid ? qr[dim_of<DQ, VEC>(i, part)] * scale_log2 : 0.f;
         acc[i] = 0.f;
     }
     const MT *mrow = mask ? mask + h * mask_hs + static_cast<int64_t>(valid ? row : 0) * mask_ld : nullptr;
@@ -53,10 +65,22 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
         __syncthreads();
         const int nk = NKV - j0 < KT ? NKV - j0 : KT;
         for (int kk = 0; kk < nk; ++kk) {
-            const float *kr = ksm + kk * HD + part * DQ;
             float s = 0.f;
+            if constexpr (VEC) {
+                const float4 *kr = reinterpret_cast<const float4 *>(ksm + kk * HD) + part;
 #pragma unroll
-            for (int i = 0; i < DQ; ++i) s = fmaf(qv[i], kr[i], s);
+                for (int i = 0; i < DQ; i += 4) {
+                    const float4 kv4 = kr[i];  // dims 16 (i / 4) + 4 part + 0..3
+                    s = fmaf(qv[i], kv4.x, s);
+                    s = fmaf(qv[i + 1], kv4.y, s);
+                    s = fmaf(qv[i + 2], kv4.z, s);
+                    s = fmaf(qv[i + 3], kv4.w, s);
+                }
+            } else {
+                const float *kr = ksm + kk * HD + part * DQ;
+#pragma unroll
+                for (int i = 0; i < DQ; ++i) s = fmaf(qv[i], kr[i], s);
+            }
             s += __shfl_xor_sync(0xffffffffu, s, 1);
             s += __shfl_xor_sync(0xffffffffu, s, 2);
             if (mrow) {
@@ -73,16 +97,28 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
             }
             const float p = exp2f(s - m);
             l += p;
-            const float *vr = vsm + kk * HD + part * DQ;
+            if constexpr (VEC) {
+                const float4 *vr = reinterpret_cast<const float4 *>(vsm + kk * HD) + part;
 #pragma unroll
-            for (int i = 0; i < DQ; ++i) acc[i] = fmaf(p, vr[i], acc[i]);
+                for (int i = 0; i < DQ; i += 4) {
+                    const float4 vv4 = vr[i];
+                    acc[i] = fmaf(p, vv4.x, acc[i]);
+                    acc[i + 1] = fmaf(p, vv4.y, acc[i + 1]);
+                    acc[i + 2] = fmaf(p, vv4.z, acc[i + 2]);
+                    acc[i + 3] = fmaf(p, vv4.w, acc[i + 3]);
+                }
+            } else {
+                const float *vr = vsm + kk * HD + part * DQ;
+#pragma unroll
+                for (int i = 0; i < DQ; ++i) acc[i] = fmaf(p, vr[i], acc[i]);
+            }
         }
     }
     if (valid) {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        float *orow = o + b * os.b + h * os.h + static_cast<int64_t>(row) * os.n + part * DQ;
+        float *orow = o + b * os.b + h * os.h + static_cast<int64_t>(row) * os.n;
 #pragma unroll
-        for (int i = 0; i < DQ; ++i) orow[i] = acc[i] * inv;
+        for (int i = 0; i < DQ; ++i) orow[dim_of<DQ, VEC>(i, part)] = acc[i] * inv;
     }
 }
 

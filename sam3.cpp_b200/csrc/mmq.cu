@@ -723,9 +723,58 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
     if (mode == MMQ_OUT_F32) y[static_cast<int64_t>(m) * ldy + n] = bias ? acc + bias[n] : acc;
 }
 
+// Skinny MUL_MAT (at most 64 activation rows, f32 output, Q8_0 / Q4_0 codes):
+// the same per-block arithmetic as mmq_simt_kernel -- exact int32 block dot,
+// acc = fma(float(I), d_x * d_w, acc) in block order -- so its outputs are
+// bit-identical to it, with 16-byte loads of both code rows, the dots formed
+// by __dp4a and the block loop unrolled so several blocks' loads are in
+// flight.  CTA: 32 weight rows x 8 activation rows, one output per thread.
+constexpr int SKINNY_MAX_M = 64;
+
+__global__ void __launch_bounds__(256) mmq_skinny_kernel(const int8_t *__restrict__ ca, const __half *__restrict__ qa,
+                                                         int lda_q, const int8_t *__restrict__ cb,
+                                                         const __half *__restrict__ qb, int ldb_q, int M, int N, int K,
+                                                         const float *__restrict__ bias, float *__restrict__ y,
+                                                         int64_t ldy) {
+    const int n = blockIdx.x * 32 + (threadIdx.x & 31);
+    const int m = blockIdx.y * 8 + (threadIdx.x >> 5);
+    if (n >= N || m >= M) return;
+    const int nblk = K >> 5;
+    const int4 *br = reinterpret_cast<const int4 *>(cb + static_cast<int64_t>(n) * K);
+    const int4 *ar = reinterpret_cast<const int4 *>(ca + static_cast<int64_t>(m) * K);
+    float acc = 0.f;
+#pragma unroll 4
+    for (int b = 0; b < nblk; ++b) {
+        const int4 w0 = __ldg(br + 2 * b), w1 = __ldg(br + 2 * b + 1);
+        const int4 a0 = __ldg(ar + 2 * b), a1 = __ldg(ar + 2 * b + 1);
+        const float dw = __half2float(qb[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]);
+        const float dx = __half2float(qa[act_quad_index(b, m, lda_q)]);
+        int isum = 0;
+        isum = __dp4a(a0.x, w0.x, isum);
+        isum = __dp4a(a0.y, w0.y, isum);
+        isum = __dp4a(a0.z, w0.z, isum);
+        isum = __dp4a(a0.w, w0.w, isum);
+        isum = __dp4a(a1.x, w1.x, isum);
+        isum = __dp4a(a1.y, w1.y, isum);
+        isum = __dp4a(a1.z, w1.z, isum);
+        isum = __dp4a(a1.w, w1.w, isum);
+        acc = fmaf(static_cast<float>(isum), dx * dw, acc);
+    }
+    y[static_cast<int64_t>(m) * ldy + n] = bias ? acc + bias[n] : acc;
+}
+
 cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
     if (!valid_args(a) || a.a.rows > 65535 || (a.b_mins && !a.a_sums)) return cudaErrorInvalidValue;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
+    const bool aligned = (reinterpret_cast<uintptr_t>(a.a.codes) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.b.codes) & 15) == 0;
+    if (mode == MMQ_OUT_F32 && !a.b_mins && M <= SKINNY_MAX_M && aligned) {
+        mmq_skinny_kernel<<<dim3((N + 31) / 32, (M + 7) / 8), 256, 0, s>>>(
+            static_cast<const int8_t *>(a.a.codes), static_cast<const __half *>(a.a.quads), a.a.ld,
+            static_cast<const int8_t *>(a.b.codes), static_cast<const __half *>(a.b.quads), a.b.ld, M, N, K, a.bias,
+            a.y, a.ldy);
+        return cudaGetLastError();
+    }
     dim3 grid((N + 127) / 128, M);
     mmq_simt_kernel<<<grid, 128, 0, s>>>(static_cast<const int8_t *>(a.a.codes), static_cast<const uint4 *>(a.a.quads),
                                          a.a.ld, static_cast<const int8_t *>(a.b.codes),

@@ -2,6 +2,10 @@
 F32 weights, sam3.cpp:3742,3783,3796,3799) against the CPU oracle, through the
 C ABI.
 
+Rows up to 64 with f32 output take the skinny kernel (weights read once per
+CTA, dp4a dots), larger SIMT cases the one-output-per-thread kernel; both
+fold the blocks in the same order.
+
 Bar (stated per test):
   * int32 block dots: bit-exact (the MMA path's own dots, dumped);
   * f32 output: bit-exact with the oracle's block-ordered fma sequence,
@@ -46,7 +50,8 @@ def test_block_dots_bit_exact(oracle, b200, backend, impl, qt, M, K, N):
 
 @pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("qt", [8, 2])
-@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (300, 1024, 512), (5, 64, 40), (129, 4736 // 4, 264)])
+@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (300, 1024, 512), (5, 64, 40), (129, 4736 // 4, 264),
+                                   (32, 1024, 1000), (64, 96, 72), (65, 64, 40)])
 def test_mul_mat_f32_matches_oracle(oracle, b200, backend, impl, qt, M, K, N):
     wq, x, bias = _case(oracle, qt, M, K, N, seed=M + 3 * K + N)
     prev = backend.set_mmq_impl(_impl(b200, impl))
