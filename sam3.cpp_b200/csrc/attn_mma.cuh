@@ -1,0 +1,21 @@
+// attn_mma.cuh -- softmax(q k^T * scale + mask) v on the tensor cores
+// (mma.sync, fp16 operands, fp32 accumulation) for head dims 32, 64, 128 and
+// 256 with the strided operands and optional fp16 mask of attention_simt:
+// the runners' attention where an fp16 rounding of q, k, v and of the
+// probabilities is inside their tolerance (the tracker's memory attention,
+// the detector's fusion / geometry encoders and segmentation head).
+#pragma once
+
+#include "attn_simt.cuh"
+
+namespace b200 {
+
+bool attention_mma_supported(int D);
+
+// Same arguments and result layout as attention_simt (fp16 mask shared by the
+// heads; a -inf entry removes the key; a row with every key removed yields zeros).
+cudaError_t attention_mma(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                          const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
+                          int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s);
+
+}  // namespace b200

@@ -12,10 +12,10 @@
 // pos), its v rows another; the cross-attention's q rows one, its k and v
 // rows one [D, 2D] weight over the prompt.  Every output element is the same
 // row dot as in the reference's per-view MUL_MATs.  Attention is
-// attention_simt on the strided q/k/v (8 heads of 32 channels); the padding
+// attention_mma on the strided q/k/v (tensor cores, 8 heads of 32 channels); the padding
 // bias is cast to the fp16 mask of FLASH_ATTN_EXT.
 #include "../../include/sam3_b200.h"
-#include "attn_simt.cuh"
+#include "attn_mma.cuh"
 #include "eltwise.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
@@ -87,14 +87,14 @@ bool forward(Fenc *f, const float *img, const float *prompt, const float *pos, c
         // self-attention: q, k from LN1(x) + pos, v from LN1(x)
         if (!ln(L.n1w, L.n1b) || !add(xn, pos, nd, qin) || !flin(f, L.sqk, qin, D, N, L.sqk_b, qk, 2 * D) ||
             !flin(f, L.sv, xn, D, N, L.sv_b, v, D) ||
-            !fok(f, attention_simt(HD, qk, s2, N, qk + D, s2, v, s1, N, 1, H, nullptr, 0, scale, att, s1, s),
+            !fok(f, attention_mma(HD, qk, s2, N, qk + D, s2, v, s1, N, 1, H, nullptr, 0, scale, att, s1, s),
                  "fenc self attention") ||
             !flin(f, L.so, att, D, N, L.so_b, tmp, D) || !add(x, tmp, nd, x))
             return false;
         // cross-attention to the prompt tokens
         if (!ln(L.n2w, L.n2b) || !flin(f, L.cq, xn, D, N, L.cq_b, qin, D) ||
             !flin(f, L.ckv, prompt, D, T, L.ckv_b, kv, 2 * D) ||
-            !fok(f, attention_simt(HD, qin, s1, N, kv, s2, kv + D, s2, T, 1, H, mask, T, scale, att, s1, s),
+            !fok(f, attention_mma(HD, qin, s1, N, kv, s2, kv + D, s2, T, 1, H, mask, T, scale, att, s1, s),
                  "fenc cross attention") ||
             !flin(f, L.co, att, D, N, L.co_b, tmp, D) || !add(x, tmp, nd, x))
             return false;
@@ -150,9 +150,9 @@ sam3b200_fenc *sam3b200_fenc_create(sam3b200_backend *hb, const sam3b200_fenc_hp
     if (!be || !hp) return nullptr;
     const int D = hp->d_model;
     const int HD = hp->heads > 0 && D % hp->heads == 0 ? D / hp->heads : 0;
-    if (D <= 0 || D % 32 != 0 || (HD != 16 && HD != 32 && HD != 64 && HD != 128) || hp->layers <= 0 ||
+    if (D <= 0 || D % 32 != 0 || !attention_mma_supported(HD) || hp->layers <= 0 ||
         hp->ffn_dim <= 0 || hp->ffn_dim % 32 != 0 || hp->max_tokens <= 0 || hp->max_prompt <= 0) {
-        set_error("fenc_create: unsupported hyperparameters (head dim 16/32/64/128, widths multiples of 32)");
+        set_error("fenc_create: unsupported hyperparameters (head dim 32/64/128/256, widths multiples of 32)");
         return nullptr;
     }
     cudaSetDevice(be->device);

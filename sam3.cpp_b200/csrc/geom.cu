@@ -10,7 +10,8 @@
 //
 // Fused in_proj weights are split by rows at load (self-attention: one
 // [D, 3D] GEMM over LN1(x); cross-attention: q rows, then k and v rows as
-// separate GEMMs over img + pe and img).  Attention is attention_simt.
+// separate GEMMs over img + pe and img).  Attention is attention_simt (fp32;
+// at most a few geometry tokens per call).
 #include "../../include/sam3_b200.h"
 #include "attn_simt.cuh"
 #include "eltwise.cuh"

@@ -12,9 +12,9 @@
 // keys and values are projected up from mem_dim (64) channels, and only the
 // first M_total - n_obj_ptr_tokens keys (the spatial memories) are rotated.
 // Linear layers are run_mul_mat (the exact quantised MUL_MAT; fp16 GEMM for
-// F16/F32 weights); attention is attention_simt (head dim 256).
+// F16/F32 weights); attention is attention_mma (tensor cores, head dim 256).
 #include "../../include/sam3_b200.h"
-#include "attn_simt.cuh"
+#include "attn_mma.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
 
@@ -136,7 +136,7 @@ bool forward(MemAttn *m, const float *curr, const float *spos, const float *prom
         if (!mln(m, x, N, L.n1w, L.n1b, xn) || !mlin(m, L.sq, xn, D, N, L.sqb, q, D) ||
             !mlin(m, L.sk, xn, D, N, L.skb, k, D) || !mlin(m, L.sv, xn, D, N, L.svb, v, D) ||
             !mrope(m, q, rope_q, N) || !mrope(m, k, rope_q, N) ||
-            !mok(m, attention_simt(D, q, rs, N, k, rs, v, rs, N, 1, 1, nullptr, 0, scale, att, rs, s),
+            !mok(m, attention_mma(D, q, rs, N, k, rs, v, rs, N, 1, 1, nullptr, 0, scale, att, rs, s),
                  "mem_attn self attention") ||
             !mlin(m, L.so, att, D, N, L.sob, tmp, D) || !madd(m, x, tmp, nd))
             return false;
@@ -144,7 +144,7 @@ bool forward(MemAttn *m, const float *curr, const float *spos, const float *prom
         if (!mln(m, x, N, L.n2w, L.n2b, xn) || !mlin(m, L.cq, xn, D, N, L.cqb, q, D) ||
             !mlin(m, L.ck, kvpos, MD, M, L.ckb, k, D) || !mlin(m, L.cv, prompt, MD, M, L.cvb, v, D) ||
             !mrope(m, q, rope_q, N) || (rope_k && !mrope(m, k, rope_k, Ms)) ||
-            !mok(m, attention_simt(D, q, rs, N, k, rs, v, rs, M, 1, 1, nullptr, 0, scale, att, rs, s),
+            !mok(m, attention_mma(D, q, rs, N, k, rs, v, rs, M, 1, 1, nullptr, 0, scale, att, rs, s),
                  "mem_attn cross attention") ||
             !mlin(m, L.co, att, D, N, L.cob, tmp, D) || !madd(m, x, tmp, nd))
             return false;
@@ -200,10 +200,10 @@ sam3b200_mem_attn *sam3b200_mem_attn_create(sam3b200_backend *hb, const sam3b200
     auto *be = reinterpret_cast<Backend *>(hb);
     if (!be || !hp) return nullptr;
     const int D = hp->d_model;
-    if ((D != 16 && D != 32 && D != 64 && D != 128 && D != 256) || hp->mem_dim <= 0 || hp->mem_dim % 32 != 0 ||
+    if (!attention_mma_supported(D) || hp->mem_dim <= 0 || hp->mem_dim % 32 != 0 ||
         hp->layers <= 0 || hp->ffn_dim <= 0 || hp->ffn_dim % 32 != 0 || hp->max_tokens <= 0 ||
         hp->max_mem_tokens <= 0) {
-        set_error("mem_attn_create: unsupported hyperparameters (d_model in {16,32,64,128,256}, mem_dim and "
+        set_error("mem_attn_create: unsupported hyperparameters (d_model in {32,64,128,256}, mem_dim and "
                   "ffn_dim multiples of 32)");
         return nullptr;
     }

@@ -15,7 +15,7 @@
 // group_norm (double sums, then scale, weight, bias); the 1x1 convolution and
 // the mask product are f32 tiled GEMMs.
 #include "../../include/sam3_b200.h"
-#include "attn_simt.cuh"
+#include "attn_mma.cuh"
 #include "eltwise.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
@@ -294,7 +294,7 @@ bool forward(SegHead *h, const float *enc_in, const float *fpn0, const float *fp
     const AttnStrides s1{0, HD, D}, s2{0, HD, 2 * D};
     if (!sok(h, cudaGetLastError(), "seg norm") || !slin(h, h->ca_q, xn, D, N, q, D) ||
         !slin(h, h->ca_kv, text, D, T, kv, 2 * D) ||
-        !sok(h, attention_simt(HD, q, s1, static_cast<int>(N), kv, s2, kv + D, s2, T, 1, NH, mask, T,
+        !sok(h, attention_mma(HD, q, s1, static_cast<int>(N), kv, s2, kv + D, s2, T, 1, NH, mask, T,
                                1.0f / sqrtf(static_cast<float>(HD)), att, s1, s),
              "seg prompt attention") ||
         !slin(h, h->ca_o, att, D, N, tmp, D))
