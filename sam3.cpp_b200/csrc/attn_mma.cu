@@ -35,13 +35,21 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int D>
+__device__ __forceinline__ __half to_half(float x) { return __float2half_rn(x); }
+__device__ __forceinline__ __half to_half(__half x) { return x; }
+
+// KVT: f32 or fp16 keys / values.  Split-KV (gridDim.z > 1): split z takes
+// keys [z * chunk, (z + 1) * chunk) and writes its unnormalised accumulator
+// and (max, sum) per row to part_o / part_ml instead of o; attn_combine_kernel
+// merges the splits.
+template <int D, typename KVT>
 __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restrict__ q, AttnStrides qs, int NQ,
-                                                            const float *__restrict__ k, AttnStrides ks,
-                                                            const float *__restrict__ v, AttnStrides vs, int NKV,
+                                                            const KVT *__restrict__ k, AttnStrides ks,
+                                                            const KVT *__restrict__ v, AttnStrides vs, int NKV,
                                                             int heads, const __half *__restrict__ mask,
                                                             int64_t mask_ld, float scale_log2, float *__restrict__ o,
-                                                            AttnStrides os) {
+                                                            AttnStrides os, int chunk, float *__restrict__ part_o,
+                                                            float2 *__restrict__ part_ml) {
     constexpr int DP = D + 8;   // shared row pitch (halves) of Q and K: fragment loads hit distinct banks
     constexpr int KP = BK + 8;  // shared row pitch of V^T
     constexpr int DT = D / 8;   // 8-wide output column tiles per warp
@@ -55,8 +63,9 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const float *qb = q + b * qs.b + h * qs.h;
-    const float *kb = k + b * ks.b + h * ks.h;
-    const float *vb = v + b * vs.b + h * vs.h;
+    const KVT *kb = k + b * ks.b + h * ks.h;
+    const KVT *vb = v + b * vs.b + h * vs.h;
+    const int kv_lo = blockIdx.z * chunk, kv_hi = min(NKV, kv_lo + chunk);
 
     for (int e = threadIdx.x; e < BQ * D; e += NTHREADS) {
         const int r = e / D, d = e % D, row = q0 + r;
@@ -72,17 +81,17 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
     for (int i = 0; i < DT; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.f;
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
 
-    for (int j0 = 0; j0 < NKV; j0 += BK) {
+    for (int j0 = kv_lo; j0 < kv_hi; j0 += BK) {
         __syncthreads();
         for (int e = threadIdx.x; e < BK * D; e += NTHREADS) {
             const int kk = e / D, d = e % D, key = j0 + kk;
-            float kv = 0.f, vv = 0.f;
-            if (key < NKV) {
-                kv = kb[static_cast<int64_t>(key) * ks.n + d];
-                vv = vb[static_cast<int64_t>(key) * vs.n + d];
+            __half kv = __float2half_rn(0.f), vv = kv;
+            if (key < kv_hi) {
+                kv = to_half(kb[static_cast<int64_t>(key) * ks.n + d]);
+                vv = to_half(vb[static_cast<int64_t>(key) * vs.n + d]);
             }
-            ksm[kk * DP + d] = __float2half_rn(kv);
-            vts[d * KP + kk] = __float2half_rn(vv);
+            ksm[kk * DP + d] = kv;
+            vts[d * KP + kk] = vv;
         }
         __syncthreads();
         // S = Q K^T for this warp's 16 rows x 64 keys
@@ -108,7 +117,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
                 const int key = j0 + nt * 8 + t4 * 2 + (c & 1);
                 float s = sacc[nt][c] * scale_log2;
                 const __half *mr = c < 2 ? mrow_a : mrow_b;
-                if (key >= NKV) {
+                if (key >= kv_hi) {
                     s = -INFINITY;
                 } else if (mr) {
                     const float mv = __half2float(mr[key]);
@@ -165,6 +174,20 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
     l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+    if (part_o) {  // split-KV partial: unnormalised accumulator + (max, sum) per row
+        const int64_t base = (static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * NQ;
+        if (t4 == 0) {
+            if (row_a < NQ) part_ml[base + row_a] = make_float2(m_a, l_a);
+            if (row_b < NQ) part_ml[base + row_b] = make_float2(m_b, l_b);
+        }
+#pragma unroll
+        for (int dt = 0; dt < DT; ++dt) {
+            const int d = dt * 8 + t4 * 2;
+            if (row_a < NQ) *reinterpret_cast<float2 *>(part_o + (base + row_a) * D + d) = make_float2(oacc[dt][0], oacc[dt][1]);
+            if (row_b < NQ) *reinterpret_cast<float2 *>(part_o + (base + row_b) * D + d) = make_float2(oacc[dt][2], oacc[dt][3]);
+        }
+        return;
+    }
     const float inv_a = l_a > 0.f ? 1.f / l_a : 0.f, inv_b = l_b > 0.f ? 1.f / l_b : 0.f;
     float *ob = o + b * os.b + h * os.h;
 #pragma unroll
@@ -181,16 +204,45 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
     }
 }
 
+// out(row, :) = sum_z 2^(m_z - M) acc_z / sum_z 2^(m_z - M) l_z over the splits (M = max_z m_z)
 template <int D>
-cudaError_t launch_mma(const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks, const float *v,
+__global__ void attn_combine_kernel(const float *__restrict__ part_o, const float2 *__restrict__ part_ml, int splits,
+                                    int NQ, int heads, float *__restrict__ o, AttnStrides os) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t BH = static_cast<int64_t>(gridDim.y);
+    if (i >= static_cast<int64_t>(NQ) * D) return;
+    const int row = static_cast<int>(i / D), d = static_cast<int>(i % D), bh = blockIdx.y;
+    float M = -INFINITY;
+    for (int z = 0; z < splits; ++z) M = fmaxf(M, part_ml[(z * BH + bh) * NQ + row].x);
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY)
+        for (int z = 0; z < splits; ++z) {
+            const int64_t r = (z * BH + bh) * NQ + row;
+            const float2 ml = part_ml[r];
+            const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+            num = fmaf(w, part_o[r * D + d], num);
+            den = fmaf(w, ml.y, den);
+        }
+    const int b = bh / heads, h = bh % heads;
+    o[b * os.b + h * os.h + static_cast<int64_t>(row) * os.n + d] = den > 0.f ? num / den : 0.f;
+}
+
+template <int D, typename KVT>
+cudaError_t launch_mma(const float *q, AttnStrides qs, int NQ, const KVT *k, AttnStrides ks, const KVT *v,
                        AttnStrides vs, int NKV, int batch, int heads, const __half *mask, int64_t mask_ld, float scale,
-                       float *o, AttnStrides os, cudaStream_t s) {
+                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml, cudaStream_t s) {
     const int smem = ((BQ + BK) * (D + 8) + D * (BK + 8)) * 2;
-    cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((NQ + BQ - 1) / BQ, static_cast<unsigned>(batch * heads));
-    attn_mma_kernel<D><<<grid, NTHREADS, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld,
-                                                     scale * 1.4426950408889634f, o, os);
+    const int chunk = splits > 1 ? ((NKV + splits - 1) / splits + BK - 1) / BK * BK : NKV;
+    const int nz = (NKV + chunk - 1) / chunk;
+    dim3 grid((NQ + BQ - 1) / BQ, static_cast<unsigned>(batch * heads), static_cast<unsigned>(nz));
+    attn_mma_kernel<D, KVT><<<grid, NTHREADS, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld,
+                                                          scale * 1.4426950408889634f, o, os, chunk,
+                                                          nz > 1 ? part_o : nullptr, part_ml);
+    if ((e = cudaGetLastError()) != cudaSuccess || nz == 1) return e;
+    dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(NQ) * D + 255) / 256), static_cast<unsigned>(batch * heads));
+    attn_combine_kernel<D><<<cgrid, 256, 0, s>>>(part_o, part_ml, nz, NQ, heads, o, os);
     return cudaGetLastError();
 }
 
@@ -205,10 +257,25 @@ cudaError_t attention_mma(int D, const float *q, AttnStrides qs, int NQ, const f
         (mask && mask_ld < NKV))
         return cudaErrorInvalidValue;
     switch (D) {
-    case 32: return launch_mma<32>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 64: return launch_mma<64>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 128: return launch_mma<128>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
-    case 256: return launch_mma<256>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, s);
+    case 32: return launch_mma<32, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s);
+    case 64: return launch_mma<64, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s);
+    case 128: return launch_mma<128, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s);
+    case 256: return launch_mma<256, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int NQ, const __half *k, AttnStrides ks,
+                                      const __half *v, AttnStrides vs, int NKV, int batch, int heads, float scale,
+                                      float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml,
+                                      cudaStream_t s) {
+    if (NQ <= 0 || NKV <= 0 || batch <= 0 || heads <= 0 || static_cast<int64_t>(batch) * heads > 65535 ||
+        splits < 1 || splits > 64 || (splits > 1 && (!part_o || !part_ml)))
+        return cudaErrorInvalidValue;
+    switch (D) {
+    case 64: return launch_mma<64, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
+    case 128: return launch_mma<128, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
+    case 256: return launch_mma<256, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
     default: return cudaErrorInvalidValue;
     }
 }

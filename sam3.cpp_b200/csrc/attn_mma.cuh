@@ -18,4 +18,14 @@ cudaError_t attention_mma(int D, const float *q, AttnStrides qs, int NQ, const f
                           const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                           int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s);
 
+// fp16 keys and values (already rounded: half the bytes to stage), no mask,
+// keys split `splits` ways across CTAs (split-KV) so that few long query rows
+// still fill the GPU: part_o (splits * batch * heads * NQ * D floats) and
+// part_ml (splits * batch * heads * NQ float2) hold the partial results until
+// a combine pass writes o.  Head dims 64, 128, 256.
+cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int NQ, const __half *k, AttnStrides ks,
+                                      const __half *v, AttnStrides vs, int NKV, int batch, int heads, float scale,
+                                      float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml,
+                                      cudaStream_t s);
+
 }  // namespace b200

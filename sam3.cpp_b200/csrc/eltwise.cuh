@@ -32,4 +32,10 @@ static __global__ void ew_bias_mask_kernel(const float *__restrict__ bias, int64
     if (i < nq * nt) mask[i] = __float2half_rn(bias[i % nt]);
 }
 
+// y = fp16(x)
+static __global__ void ew_to_half_kernel(const float *__restrict__ x, int64_t n, __half *__restrict__ y) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __float2half_rn(x[i]);
+}
+
 }  // namespace b200

@@ -12,16 +12,19 @@
 // keys and values are projected up from mem_dim (64) channels, and only the
 // first M_total - n_obj_ptr_tokens keys (the spatial memories) are rotated.
 // Linear layers are run_mul_mat (the exact quantised MUL_MAT; fp16 GEMM for
-// F16/F32 weights); attention is attention_mma (tensor cores, head dim 256).
+// F16/F32 weights); attention runs on the tensor cores (attn_mma.cu: head dim
+// 256, fp16 k and v, the keys split across CTAs).
 #include "../../include/sam3_b200.h"
 #include "attn_mma.cuh"
 #include "model_util.h"
+#include "eltwise.cuh"
 #include "row_norm.cuh"
 
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 namespace b200 {
@@ -79,6 +82,9 @@ struct MemAttn {
     DevBuf normw, normb;
     // activations
     DevBuf x, xn, q, k, v, att, tmp, ffn, kvpos, out;
+    // attention operands in fp16 and the split-KV partial results
+    DevBuf k16, v16, part_o, part_ml;
+    int splits = 1;
     // host-run staging of the inputs
     DevBuf in_curr, in_spos, in_prompt, in_ppos, in_rq, in_rk;
     std::vector<std::string> missing;
@@ -115,6 +121,22 @@ bool mrope(MemAttn *m, float *x, const float *table, int64_t rows) {
     return mok(m, cudaGetLastError(), "mem_attn rope");
 }
 
+// single-head attention of N queries over NK keys on the tensor cores: k, v
+// rounded to fp16 once, the keys split across CTAs so 4096 queries fill the GPU
+bool attend(MemAttn *m, const float *q, const float *k, const float *v, int N, int NK, float scale, float *out) {
+    const int D = m->hp.d_model;
+    const int64_t n = static_cast<int64_t>(NK) * D;
+    cudaStream_t s = m->be->stream;
+    ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(k, n, m->k16.as<__half>());
+    ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(v, n, m->v16.as<__half>());
+    const AttnStrides rs{0, 0, D};
+    return mok(m, cudaGetLastError(), "mem_attn fp16 k, v") &&
+           mok(m, attention_mma_f16kv_split(D, q, rs, N, m->k16.as<__half>(), rs, m->v16.as<__half>(), rs, NK, 1, 1,
+                                            scale, out, rs, m->splits, m->part_o.as<float>(), m->part_ml.as<float2>(),
+                                            s),
+               "mem_attn attention");
+}
+
 bool forward(MemAttn *m, const float *curr, const float *spos, const float *prompt, const float *ppos,
              const float *rope_q, const float *rope_k, int N, int M, int n_ptr) {
     const int D = m->hp.d_model, MD = m->hp.mem_dim, F = m->hp.ffn_dim;
@@ -124,7 +146,6 @@ bool forward(MemAttn *m, const float *curr, const float *spos, const float *prom
     float *x = m->x.as<float>(), *xn = m->xn.as<float>(), *q = m->q.as<float>(), *k = m->k.as<float>();
     float *v = m->v.as<float>(), *att = m->att.as<float>(), *tmp = m->tmp.as<float>(), *kvpos = m->kvpos.as<float>();
     const float scale = 1.0f / sqrtf(static_cast<float>(D));
-    const AttnStrides rs{0, 0, D};  // one head, rows of D channels
     ma_add_scaled_kernel<<<mblocks(nd), 256, 0, s>>>(curr, spos, 0.1f, nd, x);
     if (!mok(m, cudaGetLastError(), "mem_attn input")) return false;
     // the keys' positional sum prompt + prompt_pos is the same for every layer
@@ -136,16 +157,14 @@ bool forward(MemAttn *m, const float *curr, const float *spos, const float *prom
         if (!mln(m, x, N, L.n1w, L.n1b, xn) || !mlin(m, L.sq, xn, D, N, L.sqb, q, D) ||
             !mlin(m, L.sk, xn, D, N, L.skb, k, D) || !mlin(m, L.sv, xn, D, N, L.svb, v, D) ||
             !mrope(m, q, rope_q, N) || !mrope(m, k, rope_q, N) ||
-            !mok(m, attention_mma(D, q, rs, N, k, rs, v, rs, N, 1, 1, nullptr, 0, scale, att, rs, s),
-                 "mem_attn self attention") ||
+            !attend(m, q, k, v, N, N, scale, att) ||
             !mlin(m, L.so, att, D, N, L.sob, tmp, D) || !madd(m, x, tmp, nd))
             return false;
         // cross-attention to the memories: k from prompt + pos, v from prompt
         if (!mln(m, x, N, L.n2w, L.n2b, xn) || !mlin(m, L.cq, xn, D, N, L.cqb, q, D) ||
             !mlin(m, L.ck, kvpos, MD, M, L.ckb, k, D) || !mlin(m, L.cv, prompt, MD, M, L.cvb, v, D) ||
             !mrope(m, q, rope_q, N) || (rope_k && !mrope(m, k, rope_k, Ms)) ||
-            !mok(m, attention_mma(D, q, rs, N, k, rs, v, rs, M, 1, 1, nullptr, 0, scale, att, rs, s),
-                 "mem_attn cross attention") ||
+            !attend(m, q, k, v, N, M, scale, att) ||
             !mlin(m, L.co, att, D, N, L.cob, tmp, D) || !madd(m, x, tmp, nd))
             return false;
         // feed-forward
@@ -200,10 +219,10 @@ sam3b200_mem_attn *sam3b200_mem_attn_create(sam3b200_backend *hb, const sam3b200
     auto *be = reinterpret_cast<Backend *>(hb);
     if (!be || !hp) return nullptr;
     const int D = hp->d_model;
-    if (!attention_mma_supported(D) || hp->mem_dim <= 0 || hp->mem_dim % 32 != 0 ||
+    if ((D != 64 && D != 128 && D != 256) || hp->mem_dim <= 0 || hp->mem_dim % 32 != 0 ||
         hp->layers <= 0 || hp->ffn_dim <= 0 || hp->ffn_dim % 32 != 0 || hp->max_tokens <= 0 ||
         hp->max_mem_tokens <= 0) {
-        set_error("mem_attn_create: unsupported hyperparameters (d_model in {32,64,128,256}, mem_dim and "
+        set_error("mem_attn_create: unsupported hyperparameters (d_model in {64,128,256}, mem_dim and "
                   "ffn_dim multiples of 32)");
         return nullptr;
     }
@@ -214,7 +233,13 @@ sam3b200_mem_attn *sam3b200_mem_attn_create(sam3b200_backend *hb, const sam3b200
     m->ly.resize(hp->layers);
     const size_t N = hp->max_tokens, M = hp->max_mem_tokens, NM = N > M ? N : M;
     const size_t d = D, md = hp->mem_dim;
-    const bool ok = m->x.alloc(N * d * 4) && m->xn.alloc(N * d * 4) && m->q.alloc(N * d * 4) &&
+    // split-KV: about two CTAs per SM for the 64-query tiles of max_tokens
+    const int qtiles = static_cast<int>((N + 63) / 64);
+    m->splits = std::min(8, std::max(1, (2 * be->num_sms + qtiles - 1) / qtiles));
+    const size_t sp = static_cast<size_t>(m->splits);
+    const bool ok = m->k16.alloc(NM * d * 2) && m->v16.alloc(NM * d * 2) && m->part_o.alloc(sp * N * d * 4) &&
+                    m->part_ml.alloc(sp * N * 8) && m->x.alloc(N * d * 4) && m->xn.alloc(N * d * 4) &&
+                    m->q.alloc(N * d * 4) &&
                     m->k.alloc(NM * d * 4) && m->v.alloc(NM * d * 4) && m->att.alloc(N * d * 4) &&
                     m->tmp.alloc(N * d * 4) && m->ffn.alloc(N * hp->ffn_dim * 4) && m->kvpos.alloc(M * md * 4) &&
                     m->out.alloc(N * d * 4);
