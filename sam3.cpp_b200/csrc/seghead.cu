@@ -8,17 +8,20 @@
 //   emb = conv1x1(p1)                                         instance_seg_head
 //   masks[q][pixel] = mask_embed(queries[q]) . emb[pixel]     mask_predictor
 //
-// Maps are token-major [H][W][C].  The 3x3 convolutions keep ggml's f32
-// arithmetic for F32 kernels (quantised weight files) and round the input to
-// fp16 for F16 kernels, as ggml's im2col of an F16 kernel does; they run as a
-// tiled direct convolution on the CUDA cores.  GroupNorm(8) follows ggml's
+// Maps are token-major [H][W][C].  The 3x3 convolutions run as im2col + the
+// fp16 tensor-core GEMM (fp16 input and kernel, fp32 accumulation): ggml's
+// own arithmetic for F16 kernels (its im2col of an F16 kernel is F16), within
+// the 1e-2 bound for the F32 kernels of quantised files, as the tracker neck's
+// convolutions.  GroupNorm(8) follows ggml's
 // group_norm (double sums, then scale, weight, bias); the 1x1 convolution and
 // the mask product are f32 tiled GEMMs.
 #include "../../include/sam3_b200.h"
 #include "attn_mma.cuh"
 #include "eltwise.cuh"
+#include "gemm_f16.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
+#include "vit_ops.cuh"
 
 #include <cmath>
 #include <cstdio>
@@ -42,75 +45,6 @@ __global__ void sh_up_add_kernel(const float *__restrict__ fpn, const float *__r
     const int y = static_cast<int>(p / S), x = static_cast<int>(p % S);
     const int64_t q = static_cast<int64_t>(y / 2) * (S / 2) + x / 2;
     out[i] = __fadd_rn(fpn[i], prev[q * C + c]);
-}
-
-// 3x3 stride-1 pad-1 convolution, token-major in [S][S][C] and out [S][S][O]:
-// out = bias[o] + sum over (c, ky, kx) of in(y + ky - 1, x + kx - 1, c) * w[o][c][ky][kx].
-// CTA tile: 64 pixels of one row x 64 output channels; 256 threads, each 2
-// pixels (x, x + 32) x 8 channels; input channels staged 8 at a time.
-constexpr int CV_PX = 64, CV_OC = 64, CV_CC = 8;
-
-__global__ void __launch_bounds__(256) sh_conv3_kernel(const float *__restrict__ in, int S, int C,
-                                                       const float *__restrict__ w, const float *__restrict__ bias,
-                                                       int O, int in_f16, float *__restrict__ out) {
-    __shared__ float xs[CV_CC][3][CV_PX + 2];
-    __shared__ __align__(16) float ws[CV_CC][9][CV_OC];
-    const int tiles_x = (S + CV_PX - 1) / CV_PX;
-    const int y = blockIdx.x / tiles_x, x0 = (blockIdx.x % tiles_x) * CV_PX;
-    const int o0 = blockIdx.y * CV_OC;
-    const int pp = threadIdx.x & 31, og = threadIdx.x >> 5;
-    float acc[2][8];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[a][j] = 0.0f;
-    for (int c0 = 0; c0 < C; c0 += CV_CC) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < CV_CC * 3 * (CV_PX + 2); e += blockDim.x) {
-            const int cc = e / (3 * (CV_PX + 2)), r = (e / (CV_PX + 2)) % 3, xx = e % (CV_PX + 2);
-            const int iy = y + r - 1, ix = x0 + xx - 1, c = c0 + cc;
-            float v = 0.0f;
-            if (iy >= 0 && iy < S && ix >= 0 && ix < S && c < C) {
-                v = in[(static_cast<int64_t>(iy) * S + ix) * C + c];
-                if (in_f16) v = __half2float(__float2half_rn(v));
-            }
-            xs[cc][r][xx] = v;
-        }
-        for (int e = threadIdx.x; e < CV_CC * 9 * CV_OC; e += blockDim.x) {
-            const int oc = e % CV_OC, t = (e / CV_OC) % 9, cc = e / (CV_OC * 9);
-            const int o = o0 + oc, c = c0 + cc;
-            ws[cc][t][oc] = (o < O && c < C) ? w[(static_cast<int64_t>(o) * C + c) * 9 + t] : 0.0f;
-        }
-        __syncthreads();
-        for (int cc = 0; cc < CV_CC; ++cc) {
-#pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-#pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                    const float a0 = xs[cc][ky][pp + kx], a1 = xs[cc][ky][pp + 32 + kx];
-                    const float4 w0 = *reinterpret_cast<const float4 *>(&ws[cc][ky * 3 + kx][og * 8]);
-                    const float4 w1 = *reinterpret_cast<const float4 *>(&ws[cc][ky * 3 + kx][og * 8 + 4]);
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        acc[0][j] = fmaf(a0, wv[j], acc[0][j]);
-                        acc[1][j] = fmaf(a1, wv[j], acc[1][j]);
-                    }
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 2; ++a) {
-        const int x = x0 + pp + 32 * a;
-        if (x >= S) continue;
-        float *orow = out + (static_cast<int64_t>(y) * S + x) * O;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int o = o0 + og * 8 + j;
-            if (o < O) orow[o] = __fadd_rn(acc[a][j], bias[o]);
-        }
-    }
 }
 
 // f32 C[m][n] = sum_k A[m][k] B[n][k] (+ bias[n]); A, B row-major with K
@@ -227,10 +161,11 @@ struct SegHead {
     Backend *be = nullptr;
     sam3b200_seg_hparams hp{};
     Lin ca_q, ca_kv, ca_o, me[3];
-    DevBuf canw, canb, convw[2], convb[2], gnw[2], gnb[2], instw, instb;
-    bool conv_f16[2] = {false, false}, inst_f16 = false;
+    DevBuf canw, canb, convw[2], convb[2], gnw[2], gnb[2], instw, instb;  // convw: fp16 [O][(ky*3+kx)*C + c]
+    bool inst_f16 = false;
     // activations
     DevBuf enc, xn, q, kv, att, tmp, mask, m0, m1, emb, h1, h2, mev, out, gn_part, gn_stat;
+    DevBuf x16, col;  // the 3x3 convolutions' fp16 input and im2col operand
     // host-run staging
     DevBuf in_enc, in_fpn0, in_fpn1, in_q, in_text, in_bias;
     std::vector<std::string> missing;
@@ -259,10 +194,22 @@ bool conv_gn(SegHead *h, int stage, const float *merged, int S, float *out) {
     const int D = h->hp.d_model;
     cudaStream_t s = h->be->stream;
     const int64_t P = static_cast<int64_t>(S) * S;
-    dim3 grid(static_cast<unsigned>(S * ((S + CV_PX - 1) / CV_PX)), static_cast<unsigned>((D + CV_OC - 1) / CV_OC));
-    sh_conv3_kernel<<<grid, 256, 0, s>>>(merged, S, D, h->convw[stage].as<float>(), h->convb[stage].as<float>(), D,
-                                         h->conv_f16[stage] ? 1 : 0, out);
-    if (!sok(h, cudaGetLastError(), "seg conv3x3")) return false;
+    GemmF16Args g{};
+    g.a = h->col.p;
+    g.b = h->convw[stage].p;
+    g.M = static_cast<int>(P);
+    g.N = D;
+    g.K = 9 * D;
+    g.bias = h->convb[stage].as<float>();
+    g.out = out;
+    g.ldo = D;
+    g.store = GEMM_STORE_ROWMAJOR;
+    g.err = h->be->err;
+    h->be->count(3);
+    if (!cuda_ok(f32_to_f16(merged, P * D, h->x16.p, s), "seg conv input") ||
+        !cuda_ok(im2col3x3_f16(h->x16.p, S, S, D, h->col.p, s), "seg im2col") ||
+        !cuda_ok(gemm_f16(g, h->be->num_sms, s), "seg conv3x3"))
+        return false;
     double *part = h->gn_part.as<double>();
     float *mean = h->gn_stat.as<float>(), *scale = mean + kGroups;
     const int64_t n = P * (D / kGroups);
@@ -385,6 +332,7 @@ sam3b200_seg *sam3b200_seg_create(sam3b200_backend *hb, const sam3b200_seg_hpara
                     h->emb.alloc(16 * N * D * 4) && h->h1.alloc(NQ * D * 4) && h->h2.alloc(NQ * D * 4) &&
                     h->mev.alloc(NQ * D * 4) && h->out.alloc(NQ * 16 * N * 4) &&
                     h->gn_part.alloc(kGroups * GN_BLOCKS * 8) && h->gn_stat.alloc(2 * kGroups * 4) &&
+                    h->x16.alloc(16 * N * D * 2) && h->col.alloc(16 * N * 9 * D * 2) &&
                     h->in_enc.alloc(N * D * 4) && h->in_fpn0.alloc(16 * N * D * 4) && h->in_fpn1.alloc(4 * N * D * 4) &&
                     h->in_q.alloc(NQ * D * 4) && h->in_text.alloc(T * D * 4) && h->in_bias.alloc(T * 4);
     if (!ok) {
@@ -454,8 +402,15 @@ int sam3b200_seg_set_tensor(sam3b200_seg *hh, const char *name_c, int type, cons
                 return BAD;
             }
             if (i == 2) return OK;  // registered but unused by the pixel decoder (sam3.cpp:8954-8955)
-            h->conv_f16[i] = type == SAM3B200_TYPE_F16;
-            return vec(h->convw[i], n);
+            if (!to_f32(type, data, n, v)) return BAD;
+            std::vector<float> w(static_cast<size_t>(n));  // ggml [kx][ky][c][o] -> [o][(ky*3+kx)*C + c]
+            for (int64_t o = 0; o < D; ++o)
+                for (int64_t c = 0; c < D; ++c)
+                    for (int ky = 0; ky < 3; ++ky)
+                        for (int kx = 0; kx < 3; ++kx)
+                            w[static_cast<size_t>(o * 9 * D + (ky * 3 + kx) * D + c)] =
+                                v[static_cast<size_t>(((o * D + c) * 3 + ky) * 3 + kx)];
+            return upload_f16(h->convw[i], w, h->be->stream) ? OK : BAD;
         }
         if (name == "seg.pixel_decoder.conv_layers." + si + ".bias") return i == 2 ? OK : vec(h->convb[i], D);
         if (name == "seg.pixel_decoder.norms." + si + ".weight") return i == 2 ? OK : vec(h->gnw[i], D);
