@@ -1,7 +1,8 @@
 // attn_mma.cu -- attention on the tensor cores for the runners whose shapes
 // the tcgen05 flash kernel (attn.cu: head dim 64, self-attention, no mask)
 // does not take: head dims 32 / 64 / 128 / 256, any query and key counts,
-// strided operands, an optional fp16 additive mask shared by the heads.
+// strided operands, an optional additive mask (fp16 shared by the heads, or
+// f32 per head).
 //
 // Flash-attention loop with warp-level mma.sync m16n8k16 (fp16 operands, fp32
 // accumulation): a CTA holds 64 query rows (4 warps x 16) and walks the keys
@@ -35,6 +36,9 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+__device__ __forceinline__ float mask_f(__half m) { return __half2float(m); }
+__device__ __forceinline__ float mask_f(float m) { return m; }
+
 __device__ __forceinline__ __half to_half(float x) { return __float2half_rn(x); }
 __device__ __forceinline__ __half to_half(__half x) { return x; }
 
@@ -42,12 +46,12 @@ __device__ __forceinline__ __half to_half(__half x) { return x; }
 // keys [z * chunk, (z + 1) * chunk) and writes its unnormalised accumulator
 // and (max, sum) per row to part_o / part_ml instead of o; attn_combine_kernel
 // merges the splits.
-template <int D, typename KVT>
+template <int D, typename KVT, typename MT>
 __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restrict__ q, AttnStrides qs, int NQ,
                                                             const KVT *__restrict__ k, AttnStrides ks,
                                                             const KVT *__restrict__ v, AttnStrides vs, int NKV,
-                                                            int heads, const __half *__restrict__ mask,
-                                                            int64_t mask_ld, float scale_log2, float *__restrict__ o,
+                                                            int heads, const MT *__restrict__ mask, int64_t mask_ld,
+                                                            int64_t mask_hs, float scale_log2, float *__restrict__ o,
                                                             AttnStrides os, int chunk, float *__restrict__ part_o,
                                                             float2 *__restrict__ part_ml) {
     constexpr int DP = D + 8;   // shared row pitch (halves) of Q and K: fragment loads hit distinct banks
@@ -73,8 +77,9 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
     }
     const int rw = warp * 16 + g;  // this thread's tile rows rw and rw + 8
     const int row_a = q0 + rw, row_b = row_a + 8;
-    const __half *mrow_a = mask && row_a < NQ ? mask + static_cast<int64_t>(row_a) * mask_ld : nullptr;
-    const __half *mrow_b = mask && row_b < NQ ? mask + static_cast<int64_t>(row_b) * mask_ld : nullptr;
+    const MT *mh = mask ? mask + h * mask_hs : nullptr;  // the head's mask (mask_hs 0: shared by the heads)
+    const MT *mrow_a = mh && row_a < NQ ? mh + static_cast<int64_t>(row_a) * mask_ld : nullptr;
+    const MT *mrow_b = mh && row_b < NQ ? mh + static_cast<int64_t>(row_b) * mask_ld : nullptr;
 
     float oacc[DT][4];
 #pragma unroll
@@ -116,11 +121,11 @@ __global__ void __launch_bounds__(NTHREADS) attn_mma_kernel(const float *__restr
             for (int c = 0; c < 4; ++c) {
                 const int key = j0 + nt * 8 + t4 * 2 + (c & 1);
                 float s = sacc[nt][c] * scale_log2;
-                const __half *mr = c < 2 ? mrow_a : mrow_b;
+                const MT *mr = c < 2 ? mrow_a : mrow_b;
                 if (key >= kv_hi) {
                     s = -INFINITY;
                 } else if (mr) {
-                    const float mv = __half2float(mr[key]);
+                    const float mv = mask_f(mr[key]);
                     s = mv == -INFINITY ? -INFINITY : fmaf(mv, LOG2E, s);
                 }
                 sacc[nt][c] = s;
@@ -227,18 +232,20 @@ __global__ void attn_combine_kernel(const float *__restrict__ part_o, const floa
     o[b * os.b + h * os.h + static_cast<int64_t>(row) * os.n + d] = den > 0.f ? num / den : 0.f;
 }
 
-template <int D, typename KVT>
+template <int D, typename KVT, typename MT = __half>
 cudaError_t launch_mma(const float *q, AttnStrides qs, int NQ, const KVT *k, AttnStrides ks, const KVT *v,
-                       AttnStrides vs, int NKV, int batch, int heads, const __half *mask, int64_t mask_ld, float scale,
-                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml, cudaStream_t s) {
+                       AttnStrides vs, int NKV, int batch, int heads, const MT *mask, int64_t mask_ld, float scale,
+                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml, cudaStream_t s,
+                       int64_t mask_hs = 0) {
     const int smem = ((BQ + BK) * (D + 8) + D * (BK + 8)) * 2;
-    cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_mma_kernel<D, KVT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     const int chunk = splits > 1 ? ((NKV + splits - 1) / splits + BK - 1) / BK * BK : NKV;
     const int nz = (NKV + chunk - 1) / chunk;
     dim3 grid((NQ + BQ - 1) / BQ, static_cast<unsigned>(batch * heads), static_cast<unsigned>(nz));
-    attn_mma_kernel<D, KVT><<<grid, NTHREADS, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld,
-                                                          scale * 1.4426950408889634f, o, os, chunk,
+    attn_mma_kernel<D, KVT, MT><<<grid, NTHREADS, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld,
+                                                              mask_hs, scale * 1.4426950408889634f, o, os, chunk,
                                                           nz > 1 ? part_o : nullptr, part_ml);
     if ((e = cudaGetLastError()) != cudaSuccess || nz == 1) return e;
     dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(NQ) * D + 255) / 256), static_cast<unsigned>(batch * heads));
@@ -265,6 +272,22 @@ cudaError_t attention_mma(int D, const float *q, AttnStrides qs, int NQ, const f
     }
 }
 
+cudaError_t attention_mma_f32mask(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                  const float *v, AttnStrides vs, int NKV, int batch, int heads, const float *mask,
+                                  int64_t mask_ld, int64_t mask_hs, float scale, float *o, AttnStrides os,
+                                  cudaStream_t s) {
+    if (NQ <= 0 || NKV <= 0 || batch <= 0 || heads <= 0 || static_cast<int64_t>(batch) * heads > 65535 ||
+        (mask && (mask_ld < NKV || mask_hs < 0)))
+        return cudaErrorInvalidValue;
+    switch (D) {
+    case 32: return launch_mma<32, float, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s, mask_hs);
+    case 64: return launch_mma<64, float, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s, mask_hs);
+    case 128: return launch_mma<128, float, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s, mask_hs);
+    case 256: return launch_mma<256, float, float>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, scale, o, os, 1, nullptr, nullptr, s, mask_hs);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int NQ, const __half *k, AttnStrides ks,
                                       const __half *v, AttnStrides vs, int NKV, int batch, int heads, float scale,
                                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml,
@@ -273,9 +296,9 @@ cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int
         splits < 1 || splits > 64 || (splits > 1 && (!part_o || !part_ml)))
         return cudaErrorInvalidValue;
     switch (D) {
-    case 64: return launch_mma<64, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
-    case 128: return launch_mma<128, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
-    case 256: return launch_mma<256, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
+    case 64: return launch_mma<64, __half, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
+    case 128: return launch_mma<128, __half, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
+    case 256: return launch_mma<256, __half, __half>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, splits, part_o, part_ml, s);
     default: return cudaErrorInvalidValue;
     }
 }

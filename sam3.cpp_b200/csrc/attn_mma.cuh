@@ -18,6 +18,13 @@ cudaError_t attention_mma(int D, const float *q, AttnStrides qs, int NQ, const f
                           const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                           int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s);
 
+// The same with an f32 mask per head (head h of query row n reads
+// mask[h * mask_hs + n * mask_ld + key]): the DETR decoder's box-relative bias.
+cudaError_t attention_mma_f32mask(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                  const float *v, AttnStrides vs, int NKV, int batch, int heads, const float *mask,
+                                  int64_t mask_ld, int64_t mask_hs, float scale, float *o, AttnStrides os,
+                                  cudaStream_t s);
+
 // fp16 keys and values (already rounded: half the bytes to stage), no mask,
 // keys split `splits` ways across CTAs (split-KV) so that few long query rows
 // still fill the GPU: part_o (splits * batch * heads * NQ * D floats) and

@@ -18,10 +18,11 @@
 //
 // Every linear layer is run_mul_mat (the exact quantised MUL_MAT; fp16 GEMM for
 // F16/F32), with the fused in_proj weights split by rows; attention is
-// attention_simt (8 heads of 32), the image cross-attention with the f32
-// per-head bias the reference keeps in f32 (SOFT_MAX_EXT).
+// attention_simt (8 heads of 32) for the small self and text attention, the
+// image cross-attention on the tensor cores (attn_mma.cu: fp16 q, k, v, fp32
+// scores) with the f32 per-head bias the reference keeps in f32 (SOFT_MAX_EXT).
 #include "../../include/sam3_b200.h"
-#include "attn_simt.cuh"
+#include "attn_mma.cuh"
 #include "eltwise.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
@@ -294,9 +295,9 @@ bool forward(Ddec *d, const float *enc, const float *enc_pos, const float *text,
         if (!dadd(d, q, qpos, qd, qin) || !dlin(d, L.ca_q, qin, D, NQ1, att, D) ||
             !dlin(d, L.ca_k, d->kin.as<float>(), D, N, d->kimg.as<float>(), D) ||
             !dlin(d, L.ca_v, enc, D, N, d->vimg.as<float>(), D) ||
-            !dok(d, attention_simt_f32mask(HD, att, s1, NQ1, d->kimg.as<float>(), s1, d->vimg.as<float>(), s1, N, 1,
-                                           NH, d->rmask.as<float>(), N, static_cast<int64_t>(NQ1) * N, scale, v, s1,
-                                           s),
+            !dok(d, attention_mma_f32mask(HD, att, s1, NQ1, d->kimg.as<float>(), s1, d->vimg.as<float>(), s1, N, 1,
+                                          NH, d->rmask.as<float>(), N, static_cast<int64_t>(NQ1) * N, scale, v, s1,
+                                          s),
                  "ddec image attention") ||
             !dlin(d, L.ca_o, v, D, NQ1, tmp, D) || !dadd(d, q, tmp, qd, qin) || !dln(d, qin, NQ1, L.n1w, L.n1b, q))
             return false;
