@@ -1,4 +1,4 @@
-"""DETR decoder of the SAM3 detector with scoring and presence head through the
+"""DETR decoder of the SAM3 detector with scoring and presence head (sam3.cpp:8171-8888) through the
 C ABI against the CPU oracle (oracle/ddec_oracle.py): d_model 256, 8 heads, 6 layers, FFN 2048, 200
 queries over the 72 x 72 image tokens (config 4), Q4_0 weights; the K = 2 boxRPB layer in F32 as the
 weight-type rule leaves it (sam3.cpp:2722-2734)."""

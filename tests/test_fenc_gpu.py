@@ -1,4 +1,4 @@
-"""Fusion encoder of the SAM3 detector through the C ABI against the CPU oracle
+"""Fusion encoder of the SAM3 detector (sam3.cpp:8033-8165) through the C ABI against the CPU oracle
 (oracle/fenc_oracle.py): d_model 256, 8 heads, 6 layers, FFN 2048 (sam3.cpp:2655-2682), Q4_0 weights
 as in config 4."""
 import numpy as np

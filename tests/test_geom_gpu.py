@@ -1,4 +1,4 @@
-"""Geometry (exemplar-prompt) encoder transformer of the SAM3 detector through the
+"""Geometry (exemplar-prompt) encoder transformer of the SAM3 detector (sam3.cpp:7677-7800) through the
 C ABI against the CPU oracle (oracle/geom_oracle.py): 3 layers over box + CLS tokens attending to the
 72 x 72 image tokens, Q4_0 weights."""
 import numpy as np

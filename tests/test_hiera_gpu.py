@@ -1,4 +1,4 @@
-"""SAM2 Hiera image encoder (config 1 = Hiera-tiny) through the
+"""SAM2 Hiera image encoder (sam3.cpp:4194-4583; config 1 = Hiera-tiny) through the
 C ABI against the CPU oracle (oracle/hiera_oracle.py)."""
 import numpy as np
 import pytest

@@ -1,4 +1,4 @@
-"""Tracker memory attention through the C ABI against the CPU oracle
+"""Tracker memory attention (sam3.cpp:9228-9341) through the C ABI against the CPU oracle
 (oracle/mem_attn_oracle.py): d_model 256, mem_dim 64, 4 layers, FFN 2048, as the SAM2/SAM3 trackers
 register them (sam3.cpp:2008-2042)."""
 import numpy as np

@@ -1,4 +1,4 @@
-"""Tracker memory encoder through the C ABI against the CPU oracle
+"""Tracker memory encoder (sam3.cpp:11510-11615) through the C ABI against the CPU oracle
 (oracle/mem_enc_oracle.py), for Q8_0 files (F32 convolution kernels, Q8_0 fuser MLP) and F16 files
 (F16 everywhere the weight-type rule allows it, sam3.cpp:1762-1786)."""
 import numpy as np

@@ -1,4 +1,4 @@
-"""SAM prompt encoder + mask decoder (PVS) through the C ABI against the CPU
+"""SAM prompt encoder + mask decoder (PVS, sam3.cpp:10164-11115) through the C ABI against the CPU
 oracle (oracle/sam_dec_oracle.py): decoder outputs within 1e-2, final binary masks at IoU >= 0.99."""
 import numpy as np
 import pytest

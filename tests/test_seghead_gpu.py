@@ -1,4 +1,4 @@
-"""Segmentation head of the SAM3 detector through the C ABI against the CPU oracle
+"""Segmentation head of the SAM3 detector (sam3.cpp:8899-9058) through the C ABI against the CPU oracle
 (oracle/seghead_oracle.py): the pixel decoder to 4 * feat, the instance head and the mask product;
 Q4_0 linear weights with F32 convolution kernels (quantised files) and an F16 variant."""
 import numpy as np

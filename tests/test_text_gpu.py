@@ -1,4 +1,4 @@
-"""SAM3 text encoder (the PCS path's text side) through the C ABI against the CPU
+"""SAM3 text encoder (the PCS path's text side, sam3.cpp:3943-4066) through the C ABI against the CPU
 oracle (oracle/text_oracle.py), at config 4's sizes: width 1024, 24 layers, 32-token context, vocabulary
 49408, Q4_0 linear weights."""
 import numpy as np
