@@ -195,6 +195,56 @@ int sam3b200_conv_2d(sam3b200_backend *be, const void *w_f16, const float *x, in
 int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t ncols, int64_t nrows,
                       const int32_t *idx, int64_t n, float *dst);
 
+/* ---- Graph level: the backend's supports_op and graph_compute -------------
+ * ggml_backend_graph_compute (sam3.cpp:1023-1028) hands a backend the nodes
+ * of one graph in execution order; ggml's scheduler first asks the backend's
+ * supports_op which nodes it may take.  sam3b200_tensor is a ggml graph node
+ * flattened to plain C: the fields of struct ggml_tensor a backend reads to
+ * execute a node (type, ne, nb in bytes, op, op_params, flags, src, data,
+ * extra).  A ggml shim copies each node into one of these; enum ggml_op
+ * differs between ggml versions, so ops have this ABI's own codes. */
+#define SAM3B200_TYPE_I32 26 /* enum ggml_type GGML_TYPE_I32: GET_ROWS indices */
+
+#define SAM3B200_OP_NONE              0 /* leaf: data already on the device */
+#define SAM3B200_OP_VIEW              1 /* VIEW / RESHAPE / PERMUTE / TRANSPOSE: data aliases src[0], nothing runs */
+#define SAM3B200_OP_MUL_MAT           2 /* ggml_mul_mat(src0 = weight, src1 = x) */
+#define SAM3B200_OP_ADD               3 /* only as the bias add right after a MUL_MAT (fused into it) */
+#define SAM3B200_OP_FLASH_ATTN_EXT    4 /* ggml_flash_attn_ext(q, k, v, mask), op_params[0..2] = scale, max_bias, softcap */
+#define SAM3B200_OP_CONV_TRANSPOSE_2D 5 /* ggml_conv_transpose_2d_p0(kernel, x), op_params[0] = stride */
+#define SAM3B200_OP_CONV_2D           6 /* ggml_conv_2d_direct(kernel, x), op_params = s0, s1, p0, p1, d0, d1 */
+#define SAM3B200_OP_GET_ROWS          7 /* ggml_get_rows(rows, I32 indices) */
+
+#define SAM3B200_TENSOR_FLAG_OUTPUT 2 /* GGML_TENSOR_FLAG_OUTPUT: the caller reads this node */
+
+typedef struct sam3b200_tensor {
+    int32_t type;          /* ggml_type value (SAM3B200_TYPE_*) */
+    int32_t op;            /* SAM3B200_OP_* */
+    int64_t ne[4];         /* elements per dimension, ne[0] innermost */
+    size_t nb[4];          /* strides in bytes, as ggml's nb */
+    int32_t op_params[16]; /* ggml op_params words (floats by their bits) */
+    int32_t flags;         /* SAM3B200_TENSOR_FLAG_* */
+    const struct sam3b200_tensor *src[4];
+    void *data;            /* device address */
+    void *extra;           /* MUL_MAT src0: the sam3b200_weight from sam3b200_weight_upload */
+} sam3b200_tensor;
+
+/* ggml_backend supports_op: 1 if this backend executes `node` as it stands
+ * (op, types, shapes and strides), 0 if not -- there is no CPU fallback, so a
+ * node reported 0 must go to another backend.  Pure host code: needs no
+ * device and launches nothing. */
+int sam3b200_supports_op(const sam3b200_tensor *node);
+
+/* ggml_backend graph_compute: run nodes[0..n_nodes) in order on the backend
+ * stream and wait for them, returning the ggml_status.  Every node is checked
+ * first (sam3b200_supports_op, then the graph rules: a MUL_MAT's weight is an
+ * uploaded handle of matching shape; an ADD is accepted only as the bias add
+ * of the MUL_MAT just before it, whose result nothing else reads and which is
+ * not flagged OUTPUT -- the pair runs as one MUL_MAT with the bias fused);
+ * if any node is rejected nothing is launched and the message names the
+ * node.  The checks come before the backend is touched, so a NULL backend
+ * reports a rejected graph's own error first. */
+int sam3b200_graph_compute(sam3b200_backend *be, sam3b200_tensor *const *nodes, int n_nodes);
+
 /* ---- SAM2 Hiera image encoder (config 1: Hiera trunk + FPN neck) ----------
  * The graph sam2_build_hiera_graph + sam2_build_fpn_neck_graph build
  * (sam3.cpp:4467-4583), per-block metadata as sam2_precompute_hiera_metadata

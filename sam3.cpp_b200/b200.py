@@ -19,8 +19,72 @@ HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "sam3_b200.h")
 STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS, STATUS_ABORTED = -2, -1, 0, 1
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
 MMQ_AUTO, MMQ_TC, MMQ_SIMT = 0, 1, 2
+TYPE_I32 = 26
+(OP_NONE, OP_VIEW, OP_MUL_MAT, OP_ADD, OP_FLASH_ATTN_EXT, OP_CONV_TRANSPOSE_2D, OP_CONV_2D,
+ OP_GET_ROWS) = range(8)
+TENSOR_FLAG_OUTPUT = 2
 
 _lib = None
+
+
+class GraphTensor(ctypes.Structure):
+    """sam3b200_tensor (include/sam3_b200.h): one ggml graph node flattened to plain C."""
+
+
+GraphTensor._fields_ = [
+    ("type", ctypes.c_int32),
+    ("op", ctypes.c_int32),
+    ("ne", ctypes.c_int64 * 4),
+    ("nb", ctypes.c_size_t * 4),
+    ("op_params", ctypes.c_int32 * 16),
+    ("flags", ctypes.c_int32),
+    ("src", ctypes.POINTER(GraphTensor) * 4),
+    ("data", ctypes.c_void_p),
+    ("extra", ctypes.c_void_p),
+]
+
+# bytes per block and elements per block (ggml type traits)
+_BLOCK = {TYPE_F32: (4, 1), TYPE_F16: (2, 1), TYPE_I32: (4, 1), TYPE_Q4_0: (18, 32), TYPE_Q4_1: (20, 32),
+          TYPE_Q8_0: (34, 32)}
+
+
+def graph_tensor(ttype: int, ne, op: int = OP_NONE, src=(), data: int | None = None, nb=None, op_params=(),
+                 flags: int = 0, extra: int | None = None) -> GraphTensor:
+    """A graph node with ggml's packed strides unless `nb` (bytes) is given.  The node keeps references to
+    its sources so their structures stay alive as long as it does."""
+    ne = list(ne) + [1] * (4 - len(ne))
+    t = GraphTensor()
+    t.type, t.op, t.flags = ttype, op, flags
+    if nb is None:
+        bb, be = _BLOCK[ttype]
+        nb = [bb, bb * (ne[0] // be)]
+        nb += [nb[1] * ne[1], nb[1] * ne[1] * ne[2]]
+    for d in range(4):
+        t.ne[d], t.nb[d] = ne[d], nb[d]
+    for i, v in enumerate(op_params):
+        t.op_params[i] = v
+    for i, s in enumerate(src):
+        if s is not None:
+            t.src[i] = ctypes.pointer(s)
+    t.data, t.extra = data, extra
+    t._keep = list(src)
+    return t
+
+
+def f32_bits(x: float) -> int:
+    """An f32 op parameter as the int32 word ggml stores it in op_params."""
+    return int(np.array([x], np.float32).view(np.int32)[0])
+
+
+def supports_op(node: GraphTensor) -> bool:
+    """sam3b200_supports_op: whether the backend executes this node (host-only check)."""
+    return bool(lib().sam3b200_supports_op(node))
+
+
+def graph_compute_status(be_handle, nodes) -> int:
+    """sam3b200_graph_compute on a list of GraphTensor nodes; returns the ggml_status."""
+    arr = (ctypes.POINTER(GraphTensor) * max(len(nodes), 1))(*[ctypes.pointer(n) for n in nodes])
+    return lib().sam3b200_graph_compute(be_handle, arr, len(nodes))
 
 
 class B200Error(RuntimeError):
@@ -82,6 +146,8 @@ def lib() -> ctypes.CDLL:
         "sam3b200_conv_transpose_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, vp]),
         "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
+        "sam3b200_supports_op": (i32, [ctypes.POINTER(GraphTensor)]),
+        "sam3b200_graph_compute": (i32, [vp, ctypes.POINTER(ctypes.POINTER(GraphTensor)), i32]),
         "sam3b200_sam_dec_create": (vp, [vp, vp]),
         "sam3b200_sam_dec_free": (None, [vp]),
         "sam3b200_sam_dec_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -934,6 +1000,10 @@ class Backend:
                  dst: DeviceBuffer) -> None:
         """GGML_OP_GET_ROWS: dst[i] = dequantised row idx[i] of src (F32, F16, Q4_0, Q4_1, Q8_0)."""
         _check(lib().sam3b200_get_rows(self.h, qtype, src.ptr, ncols, nrows, idx.ptr, n, dst.ptr), "get_rows")
+
+    def graph_compute(self, nodes) -> None:
+        """sam3b200_graph_compute: run GraphTensor nodes in order and wait for them (ggml graph_compute)."""
+        _check(graph_compute_status(self.h, nodes), "graph_compute")
 
     def preprocess_sam2(self, rgb_dev: DeviceBuffer, w: int, h: int, img: int, out: DeviceBuffer) -> None:
         """sam2_preprocess_image: ImageNet-normalised CHW (sam3.cpp:3522-3548)."""

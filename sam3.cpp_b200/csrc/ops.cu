@@ -236,8 +236,11 @@ int sam3b200_conv_2d(sam3b200_backend *hb, const void *w_f16, const float *x, in
     if (iw <= 0 || ih <= 0 || ic <= 0 || oc <= 0 || kw <= 0 || kh <= 0 || s0 <= 0 || s1 <= 0 || p0 < 0 || p1 < 0 ||
         d0 <= 0 || d1 <= 0 || iw > (1 << 20) || ih > (1 << 20) || ic * kh * kw > (1 << 24) || oc > (1 << 24))
         return fail("conv_2d: unsupported shape");
-    const int64_t ow = (iw + 2 * p0 - d0 * (kw - 1) - 1) / s0 + 1;
-    const int64_t oh = (ih + 2 * p1 - d1 * (kh - 1) - 1) / s1 + 1;
+    // a negative span (dilated kernel overhanging the padded input) must not truncate to one output column
+    const int64_t span_w = iw + 2 * p0 - d0 * (kw - 1) - 1, span_h = ih + 2 * p1 - d1 * (kh - 1) - 1;
+    if (span_w < 0 || span_h < 0) return fail("conv_2d: kernel larger than the padded input");
+    const int64_t ow = span_w / s0 + 1;
+    const int64_t oh = span_h / s1 + 1;
     if (ow <= 0 || oh <= 0 || ow * oh > (1ll << 30)) return fail("conv_2d: empty or oversized output");
     cudaSetDevice(be->device);
     const int64_t K = ic * kh * kw, Kp = pad8(K), P = ow * oh;

@@ -1,0 +1,210 @@
+"""CPU checks of the graph-level entries (sam3b200_supports_op, sam3b200_graph_compute): the node
+layout of the C ABI, which nodes the backend accepts, and the graph rules, all decided on the host
+before any device work -- the backend half of ggml_backend_graph_compute (sam3.cpp:1019-1030)."""
+import ctypes
+
+import pytest
+
+F32, F16, Q4_0, Q4_1, Q8_0, I32 = 0, 1, 2, 3, 8, 26
+A = 1 << 20  # a fake, 16-byte aligned device address: these checks never dereference data
+
+
+@pytest.fixture(scope="module")
+def g(b200):
+    b200.lib()
+    return b200
+
+
+def test_node_layout_matches_the_header(g):
+    """sam3b200_tensor: 192 bytes, src at 144 (static_assert on the C side)."""
+    assert ctypes.sizeof(g.GraphTensor) == 192
+    assert g.GraphTensor.src.offset == 144
+    assert g.GraphTensor.ne.offset == 8 and g.GraphTensor.nb.offset == 40 and g.GraphTensor.flags.offset == 136
+
+
+def _mm(g, wtype=Q8_0, K=256, N=96, rows=(40,), data=None):
+    w = g.graph_tensor(wtype, [K, N])
+    x = g.graph_tensor(F32, [K, *rows], data=A)
+    return g.graph_tensor(F32, [N, *rows], op=g.OP_MUL_MAT, src=(w, x), data=data)
+
+
+def _fa(g, D=64, NQ=48, NKV=48, H=2, B=2, mask=True, params=None):
+    nb = [4, 3 * H * D * 4, D * 4, NQ * 3 * H * D * 4]  # views into one [B, N, 3, H, D] qkv tensor
+    q = g.graph_tensor(F32, [D, NQ, H, B], nb=nb, data=A)
+    k = g.graph_tensor(F32, [D, NKV, H, B], nb=nb, data=A + H * D * 4)
+    v = g.graph_tensor(F32, [D, NKV, H, B], nb=nb, data=A + 2 * H * D * 4)
+    m = g.graph_tensor(F16, [NKV, NQ], data=A) if mask else None
+    params = params if params is not None else (g.f32_bits(0.125), 0, 0)
+    return g.graph_tensor(F32, [D, H, NQ, B], op=g.OP_FLASH_ATTN_EXT, src=(q, k, v, m), op_params=params,
+                          data=A)
+
+
+def _conv(g, iw=20, ih=18, ic=32, oc=40, k=3, params=(1, 1, 1, 1, 1, 1), out=None):
+    w = g.graph_tensor(F16, [k, k, ic, oc], data=A)
+    x = g.graph_tensor(F32, [iw, ih, ic, 1], data=A)
+    if out is None:
+        s0, s1, p0, p1, d0, d1 = params
+        out = [(iw + 2 * p0 - d0 * (k - 1) - 1) // s0 + 1, (ih + 2 * p1 - d1 * (k - 1) - 1) // s1 + 1, oc, 1]
+    return g.graph_tensor(F32, out, op=g.OP_CONV_2D, src=(w, x), op_params=params, data=A)
+
+
+def _convt(g, iw=10, ih=9, ic=40, oc=16, k=2, s=2, out=None):
+    w = g.graph_tensor(F16, [k, k, oc, ic], data=A)
+    x = g.graph_tensor(F32, [iw, ih, ic, 1], data=A)
+    return g.graph_tensor(F32, out or [(iw - 1) * s + k, (ih - 1) * s + k, oc, 1], op=g.OP_CONV_TRANSPOSE_2D,
+                          src=(w, x), op_params=(s,), data=A)
+
+
+def _rows(g, stype=Q4_0, ncols=256, nrows=500, n=32, itype=I32):
+    r = g.graph_tensor(stype, [ncols, nrows], data=A)
+    i = g.graph_tensor(itype, [n], data=A)
+    return g.graph_tensor(F32, [ncols, n], op=g.OP_GET_ROWS, src=(r, i), data=A)
+
+
+@pytest.mark.parametrize("wtype", [Q8_0, Q4_0, Q4_1, F16, F32])
+def test_supports_mul_mat_weight_types(g, wtype):
+    assert g.supports_op(_mm(g, wtype))
+
+
+def test_supports_the_forms_sam3_builds(g):
+    assert g.supports_op(_mm(g, rows=(24, 24, 9)))        # windowed activations [K, 24, 24, 9] (sam3.cpp:3742)
+    assert g.supports_op(_fa(g))                          # strided q/k/v views + F16 mask
+    assert g.supports_op(_fa(g, D=16, NQ=7, NKV=4096, mask=False))  # decoder cross-attention shape
+    assert g.supports_op(_conv(g))                        # ggml_conv_2d_s1_ph
+    assert g.supports_op(_conv(g, iw=56, ih=42, ic=3, oc=32, k=14, params=(14, 14, 0, 0, 1, 1)))  # patch embed
+    assert g.supports_op(_convt(g))
+    for t in (F32, F16, Q4_0, Q4_1, Q8_0):
+        assert g.supports_op(_rows(g, t))
+    mm = _mm(g)
+    bias = g.graph_tensor(F32, [96], data=A)
+    assert g.supports_op(g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [96, 40], op=g.OP_VIEW, src=(mm,), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [96, 40]))   # leaf
+
+
+def _not_packed_rows(g):
+    mm = _mm(g)
+    mm.src[1].contents.nb[0] = 8
+    return mm
+
+
+def _bias_of_wrong_length(g):
+    return g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(_mm(g), g.graph_tensor(F32, [95], data=A)), data=A)
+
+
+REJECTED = {
+    "unknown op": lambda g: g.graph_tensor(F32, [4], op=99, data=A),
+    "Q5_0 weight": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(6, [256, 96], nb=[22, 176, 176 * 96, 176 * 96]), g.graph_tensor(F32, [256, 40], data=A)),
+        data=A),
+    "K not a multiple of 32": lambda g: _mm(g, K=48),
+    "x ne0 != K": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(Q8_0, [256, 96]), g.graph_tensor(F32, [224, 40], data=A)), data=A),
+    "x f16": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(Q8_0, [256, 96]), g.graph_tensor(F16, [256, 40], data=A)), data=A),
+    "x rows not packed": _not_packed_rows,
+    "x dims not flattening": lambda g: g.graph_tensor(F32, [96, 4, 5], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(Q8_0, [256, 96]),
+        g.graph_tensor(F32, [256, 4, 5], nb=[4, 1024, 8192, 40960], data=A)), data=A),
+    "result shape": lambda g: g.graph_tensor(F32, [95, 40], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(Q8_0, [256, 96]), g.graph_tensor(F32, [256, 40], data=A)), data=A),
+    "3-D weight": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(Q8_0, [256, 96, 2]), g.graph_tensor(F32, [256, 40], data=A)), data=A),
+    "ADD of two activations": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(
+        g.graph_tensor(F32, [96, 40], data=A), g.graph_tensor(F32, [96], data=A)), data=A),
+    "ADD bias of the wrong length": _bias_of_wrong_length,
+    "attention head dim 80": lambda g: _fa(g, D=80),
+    "attention max_bias": lambda g: _fa(g, params=(g.f32_bits(0.125), g.f32_bits(8.0), 0)),
+    "attention softcap": lambda g: _fa(g, params=(g.f32_bits(0.125), 0, g.f32_bits(30.0))),
+    "attention mask shorter than NQ": lambda g: _fa_short_mask(g),
+    "conv channel mismatch": lambda g: _conv_channel_mismatch(g),
+    # span -1: C division would truncate it to one output column
+    "conv kernel over the padded input": lambda g: _conv(g, iw=6, ih=6, k=7, params=(2, 2, 0, 0, 1, 1),
+                                                         out=[1, 1, 40, 1]),
+    "conv result shape": lambda g: _conv(g, out=[20, 17, 40, 1]),
+    "conv zero stride": lambda g: _conv(g, params=(0, 1, 1, 1, 1, 1), out=[20, 18, 40, 1]),
+    "conv transpose result shape": lambda g: _convt(g, out=[20, 17, 16, 1]),
+    "get_rows f32 indices": lambda g: _rows(g, itype=F32),
+    "get_rows Q4_0 with 48 columns": lambda g: _rows(g, Q4_0, ncols=48),
+}
+
+
+def _fa_short_mask(g):
+    fa = _fa(g)
+    fa.src[3].contents.ne[1] = 40  # NQ = 48
+    return fa
+
+
+def _conv_channel_mismatch(g):
+    c = _conv(g)
+    c.src[1].contents.ne[2] = 31
+    return c
+
+
+@pytest.mark.parametrize("case", sorted(REJECTED))
+def test_rejects(g, case):
+    node = REJECTED[case](g)
+    assert not g.supports_op(node), case
+    assert g.graph_compute_status(None, [node]) == g.STATUS_FAILED
+    assert "node 0 rejected" in g.last_error(), g.last_error()
+
+
+def test_valid_graph_passes_every_check_before_the_backend(g):
+    """A graph of supported nodes with aligned data gets as far as the missing backend."""
+    nodes = [_conv(g), _convt(g), _rows(g), _fa(g)]
+    assert g.graph_compute_status(None, nodes) == g.STATUS_FAILED
+    assert "null backend" in g.last_error(), g.last_error()
+    assert g.graph_compute_status(None, []) == g.STATUS_FAILED
+    assert "null backend" in g.last_error()
+
+
+def test_add_must_directly_follow_its_mul_mat(g):
+    mm = _mm(g, data=A)
+    bias = g.graph_tensor(F32, [96], data=A)
+    add = g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A)
+    assert g.graph_compute_status(None, [mm, _conv(g), add]) == g.STATUS_FAILED
+    assert "node 2 rejected: ADD runs only fused" in g.last_error(), g.last_error()
+
+
+def test_add_is_not_fused_over_an_output_or_shared_mul_mat(g):
+    mm = _mm(g, data=A)
+    mm.flags = g.TENSOR_FLAG_OUTPUT
+    bias = g.graph_tensor(F32, [96], data=A)
+    add = g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A)
+    assert g.graph_compute_status(None, [mm, add]) == g.STATUS_FAILED
+    assert "node 1 rejected" in g.last_error()
+    mm.flags = 0
+    view = g.graph_tensor(F32, [96, 40], op=g.OP_VIEW, src=(mm,), data=A)  # a second reader of the MUL_MAT
+    assert g.graph_compute_status(None, [mm, add, view]) == g.STATUS_FAILED
+    assert "node 1 rejected" in g.last_error()
+
+
+def test_mul_mat_needs_an_uploaded_weight_handle(g):
+    mm = _mm(g, data=A)
+    assert g.graph_compute_status(None, [mm]) == g.STATUS_FAILED
+    assert "node 0 rejected: MUL_MAT weight has no handle" in g.last_error(), g.last_error()
+
+
+def test_unaligned_or_missing_data_is_rejected(g):
+    c = _conv(g)
+    c.data = A + 4
+    assert g.graph_compute_status(None, [c]) == g.STATUS_FAILED
+    assert "node 0 rejected: result data" in g.last_error()
+    c = _conv(g)
+    c.src[1].contents.data = None
+    assert g.graph_compute_status(None, [c]) == g.STATUS_FAILED
+    assert "node 0 rejected: src1 data" in g.last_error()
+
+
+def test_empty_nodes_are_skipped(g):
+    """ggml backends skip nodes with a zero dimension; so does this one (even an otherwise odd node)."""
+    e = g.graph_tensor(F32, [0, 4], op=99)
+    assert g.supports_op(e)
+    assert g.graph_compute_status(None, [e]) == g.STATUS_FAILED
+    assert "null backend" in g.last_error()
+
+
+def test_null_node_list_is_rejected(g):
+    L = g.lib()
+    assert L.sam3b200_graph_compute(None, None, 3) == g.STATUS_FAILED
+    assert "null node list" in g.last_error()
