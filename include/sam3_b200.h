@@ -94,8 +94,9 @@ void sam3b200_weight_free(sam3b200_backend *be, sam3b200_weight *w);
  * with x quantised to Q8_0 the way ggml-cpu does, and the per-32-block
  * int32 dots scaled by the two fp16 block scales (ggml vec_dot semantics).
  * x: device f32, M rows of K floats, row stride ldx; bias: device f32 [N]
- * or NULL; dst: device f32, M rows, row stride ldd.  Asynchronous on the
- * backend stream, like a node inside ggml_backend_graph_compute. */
+ * or NULL, 16-byte aligned (refused otherwise); dst: device f32, M rows,
+ * row stride ldd.  Asynchronous on the backend stream, like a node inside
+ * ggml_backend_graph_compute. */
 int sam3b200_mul_mat(sam3b200_backend *be, const sam3b200_weight *w, const float *x, int64_t ldx, int64_t M,
                      const float *bias, float *dst, int64_t ldd);
 

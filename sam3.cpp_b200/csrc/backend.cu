@@ -385,6 +385,10 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
 
 extern "C" int sam3b200_mul_mat(sam3b200_backend *h, const sam3b200_weight *w, const float *x, int64_t ldx,
                                 int64_t M, const float *bias, float *dst, int64_t ldd) {
+    if (reinterpret_cast<uintptr_t>(bias) & 15) {  // the tensor-core epilogue reads the bias as float4
+        set_error("mul_mat: bias must be 16-byte aligned");
+        return SAM3B200_STATUS_FAILED;
+    }
     return run_mul_mat(reinterpret_cast<Backend *>(h), reinterpret_cast<const Weight *>(w), x, ldx, M, bias, dst,
                        ldd, nullptr);
 }

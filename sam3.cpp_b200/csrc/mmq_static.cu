@@ -58,6 +58,10 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
                                         int64_t M, const float *bias, float *dst, int64_t ldd) {
     auto *be = reinterpret_cast<Backend *>(h);
     auto *w = reinterpret_cast<const Weight *>(wh);
+    if (reinterpret_cast<uintptr_t>(bias) & 15) {  // the tensor-core epilogue reads the bias as float4
+        set_error("mul_mat_noalloc: bias must be 16-byte aligned");
+        return SAM3B200_STATUS_FAILED;
+    }
     if (!be || !w || !x || !dst) {
         set_error("mul_mat_noalloc: null argument");
         return SAM3B200_STATUS_FAILED;
