@@ -159,8 +159,9 @@ int sam3b200_flash_attn_ext(sam3b200_backend *be, const float *q, const float *k
  * entry removes the key, a row with every key removed yields zeros.  dst: f32
  * [D, heads, NQ, batch] contiguous.  D in {16, 32, 48, 56, 64, 72, 96, 112,
  * 128, 256}.  Contiguous unmasked self-attention with D == 64 and NQ a
- * multiple of 8 takes the tensor-core path; every other form runs in fp32 on
- * the CUDA cores.  Asynchronous on the backend stream. */
+ * multiple of 8 (q, k, v 8-byte and dst 16-byte aligned) takes the
+ * tensor-core path; every other form runs in fp32 on the CUDA cores.
+ * Asynchronous on the backend stream. */
 int sam3b200_flash_attn_ext_view(sam3b200_backend *be, const float *q, const float *k, const float *v,
                                  const void *mask_f16, int64_t mask_nb1, int64_t D, int64_t NQ, int64_t NKV,
                                  int64_t heads, int64_t batch, const int64_t q_nb[3], const int64_t k_nb[3],

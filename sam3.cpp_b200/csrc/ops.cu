@@ -337,8 +337,11 @@ int sam3b200_flash_attn_ext_view(sam3b200_backend *hb, const float *q, const flo
     cudaSetDevice(be->device);
     auto contiguous = [&](const int64_t *nb, int64_t n) { return nb[0] == D && nb[1] == n * D && nb[2] == heads * n * D; };
     const AttnStrides os{NQ * heads * D, D, heads * D};  // dst [D, heads, NQ, batch]
+    // the tensor-core path stages q, k, v with 8-byte loads and stores dst 16 bytes at a time; views at
+    // other offsets take the fp32 path, which reads and writes single floats
+    auto aligned = [](const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; };
     if (D == 64 && !mask_f16 && NQ == NKV && NQ % 8 == 0 && contiguous(q_nb, NQ) && contiguous(k_nb, NKV) &&
-        contiguous(v_nb, NKV)) {
+        contiguous(v_nb, NKV) && aligned(q, 8) && aligned(k, 8) && aligned(v, 8) && aligned(dst, 16)) {
         // tensor cores: bf16 q, k and v^T staged from the f32 tensors
         const int BH = static_cast<int>(heads * batch), Ni = static_cast<int>(NQ);
         const size_t bytes = static_cast<size_t>(BH) * Ni * 64 * 2;
