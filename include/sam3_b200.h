@@ -404,6 +404,43 @@ int sam3b200_mem_attn_run_device(sam3b200_mem_attn *m, const float *curr, const 
 /* Conditioned tokens: device f32 [d_model, N] of the last run. */
 int sam3b200_mem_attn_output(sam3b200_mem_attn *m, const float **dev);
 
+/* Host-side preparation of the memory attention's inputs for one propagated
+ * frame, as sam3_propagate_single does it before it builds its graph
+ * (sam3.cpp:11175-11233).  No device work.
+ *
+ * sam3_select_memory_frames (sam3.cpp:9427-9451): the memory-bank slots that
+ * take part -- all of them when there are at most max_slots, else the first,
+ * the newest and evenly spaced ones between -- sorted, written to out[cap];
+ * returns the count or -1. */
+int sam3b200_select_memory_frames(int bank_size, int max_slots, int32_t *out, int cap);
+
+typedef struct {
+    int32_t d_model;      /* D: 256 (the object-pointer width) */
+    int32_t mem_dim;      /* MD: 64 (memory feature width, prompt row width) */
+    int32_t num_maskmem;  /* 7: rows of the temporal code table */
+    int32_t max_obj_ptrs; /* 16: pointers taken from the pointer bank */
+} sam3b200_mem_prompt_hparams;
+
+/* sam3_build_prompt_and_pos (sam3.cpp:9126-9217) with the temporal positions
+ * of sam3_propagate_single: prompt and prompt_pos rows of MD floats --
+ * n_slots * slot_tokens spatial memory tokens (features as given; positional
+ * code = the slot's spatial code + mem_enc.tpos_enc row num_maskmem - t - 1,
+ * t = 0 for a conditioning slot and n_slots - s otherwise, no temporal code
+ * for t >= num_maskmem), then D / MD tokens per object pointer for the first
+ * min(n_ptrs, max_obj_ptrs) pointers (positional code: the 1-D sine code of
+ * max(1, |cur_frame - ptr_frames[p]|) / 15 through obj_ptr_tpos_proj,
+ * weight [D, MD] in ggml layout + bias [MD]).  The slots are the selected
+ * ones, in the order of sam3b200_select_memory_frames.  NULL tpos_enc /
+ * tpos_proj_w / tpos_proj_b act as zeros (a model without them).  Returns the
+ * prompt token count M_total and the pointer-token count, or -1 (too many
+ * tokens for cap_tokens, null inputs). */
+int64_t sam3b200_build_mem_prompt(const sam3b200_mem_prompt_hparams *hp, int n_slots, int slot_tokens,
+                                  const float *const *slot_feats, const float *const *slot_pes,
+                                  const int32_t *slot_is_cond, int n_ptrs, const float *const *obj_ptrs,
+                                  const int32_t *ptr_frames, int cur_frame, const float *tpos_enc,
+                                  const float *tpos_proj_w, const float *tpos_proj_b, float *prompt,
+                                  float *prompt_pos, int64_t cap_tokens, int32_t *n_ptr_tokens);
+
 /* ---- Memory encoder of the video tracker ----------------------------------
  * sam3_encode_memory (sam3.cpp:11510-11615) up to the stored [mem_dim, H, H]
  * memory features: mask logits resized to img (bilinear), sigmoid * scale +

@@ -1,0 +1,77 @@
+"""CPU restatement of the tracker's memory prompt preparation (TEST INFRASTRUCTURE ONLY).
+
+Only tests/ import this module, as the checker of sam3b200_select_memory_frames and
+sam3b200_build_mem_prompt.  It restates, in plain Python / numpy:
+  - sam3_select_memory_frames (sam3.cpp:9427-9451): every slot when the bank holds at most
+    max_slots, else slot 0, the newest slot and max_slots - 2 evenly spaced ones between them
+    (float step (bank - 2) / (remaining + 1), truncated, clamped to bank - 2), sorted, unique;
+  - the temporal positions of sam3_propagate_single (sam3.cpp:11196-11233): t = 0 for a
+    conditioning slot, n_sel - s otherwise; pointer distance max(1, |frame - pointer frame|) for the
+    first min(n, max_obj_ptrs) pointers;
+  - sam3_build_prompt_and_pos (sam3.cpp:9126-9217): spatial tokens with pos + tpos_enc[num_maskmem
+    - t - 1] when 0 <= t < num_maskmem; each pointer split into D / MD tokens whose positional
+    code is obj_ptr_tpos_proj(sine_1d(distance / 15)) (sam3_get_1d_sine_pe, sam3.cpp:3641-3651).
+Token rows are [tokens][MD] float32.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+
+def select_memory_frames(bank_size: int, max_slots: int) -> list[int]:
+    if bank_size <= max_slots:
+        return list(range(bank_size))
+    sel = [0, bank_size - 1]
+    remaining = max_slots - 2
+    if remaining > 0:
+        step = F32(bank_size - 2) / F32(remaining + 1)
+        for i in range(remaining):
+            idx = 1 + int(F32(i + 1) * step)
+            sel.append(min(idx, bank_size - 2))
+    return sorted(set(sel))
+
+
+def sine_pe_1d(pos: float, dim: int, temperature: float = 10000.0) -> np.ndarray:
+    half = dim // 2
+    i = np.arange(half)
+    paired = (i & ~1).astype(F32)
+    dim_t = np.power(F32(temperature), paired / F32(half)).astype(F32)
+    val = (F32(pos) / dim_t).astype(F32)
+    return np.concatenate([np.sin(val), np.cos(val)]).astype(F32)
+
+
+def build_mem_prompt(d_model: int, mem_dim: int, num_maskmem: int, max_obj_ptrs: int, slot_feats, slot_pes,
+                     slot_is_cond, obj_ptrs, ptr_frames, cur_frame: int, tpos_enc=None, tpos_proj_w=None,
+                     tpos_proj_b=None):
+    """Returns (prompt [M_total][MD], prompt_pos [M_total][MD], n_ptr_tokens).  tpos_enc
+    [num_maskmem][MD]; tpos_proj_w [MD][D] (ggml [D, MD]); tpos_proj_b [MD]; None = zeros."""
+    MD, D = mem_dim, d_model
+    split = D // MD
+    n_sel = len(slot_feats)
+    if tpos_enc is None:
+        tpos_enc = np.zeros((num_maskmem, MD), F32)
+    prompt, pos = [], []
+    for s in range(n_sel):
+        t = 0 if slot_is_cond[s] else n_sel - s
+        f = np.asarray(slot_feats[s], F32).reshape(-1, MD)
+        p = np.asarray(slot_pes[s], F32).reshape(-1, MD).copy()
+        if 0 <= t < num_maskmem:
+            p = (p + tpos_enc[num_maskmem - t - 1][None, :]).astype(F32)
+        prompt.append(f)
+        pos.append(p)
+    n_ptr_tokens = 0
+    w = np.zeros((MD, D), F32) if tpos_proj_w is None else np.asarray(tpos_proj_w, F32).reshape(MD, D)
+    b = np.zeros(MD, F32) if tpos_proj_b is None else np.asarray(tpos_proj_b, F32)
+    for p in range(min(len(obj_ptrs), max_obj_ptrs)):
+        rel = max(1, abs(cur_frame - ptr_frames[p]))
+        sine = sine_pe_1d(F32(rel) / F32(15.0), D).astype(np.float64)
+        proj = (b.astype(np.float64) + w.astype(np.float64) @ sine).astype(F32)
+        ptr = np.asarray(obj_ptrs[p], F32).reshape(split, MD)
+        prompt.append(ptr)
+        pos.append(np.repeat(proj[None, :], split, axis=0))
+        n_ptr_tokens += split
+    if not prompt:
+        return np.zeros((0, MD), F32), np.zeros((0, MD), F32), 0
+    return np.concatenate(prompt).astype(F32), np.concatenate(pos).astype(F32), n_ptr_tokens

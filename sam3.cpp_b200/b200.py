@@ -81,6 +81,50 @@ def supports_op(node: GraphTensor) -> bool:
     return bool(lib().sam3b200_supports_op(node))
 
 
+class MemPromptHparams(ctypes.Structure):
+    """sam3b200_mem_prompt_hparams (include/sam3_b200.h)."""
+    _fields_ = [("d_model", ctypes.c_int32), ("mem_dim", ctypes.c_int32), ("num_maskmem", ctypes.c_int32),
+                ("max_obj_ptrs", ctypes.c_int32)]
+
+
+def select_memory_frames(bank_size: int, max_slots: int) -> list[int]:
+    """sam3b200_select_memory_frames: the memory-bank slots one propagated frame attends to."""
+    cap = max(bank_size, max_slots, 2)
+    out = (ctypes.c_int32 * cap)()
+    n = lib().sam3b200_select_memory_frames(bank_size, max_slots, out, cap)
+    if n < 0:
+        raise B200Error(f"select_memory_frames failed: {last_error()}")
+    return list(out[:n])
+
+
+def build_mem_prompt(hp: dict, slot_feats, slot_pes, slot_is_cond, obj_ptrs, ptr_frames, cur_frame: int,
+                     tpos_enc=None, tpos_proj_w=None, tpos_proj_b=None):
+    """sam3b200_build_mem_prompt on host arrays: returns (prompt [M][MD], prompt_pos [M][MD],
+    n_ptr_tokens), the inputs of MemAttention.run.  hp: d_model, mem_dim, num_maskmem, max_obj_ptrs."""
+    h = MemPromptHparams(hp["d_model"], hp["mem_dim"], hp["num_maskmem"], hp["max_obj_ptrs"])
+    f32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+    feats, pes, ptrs = [f32(a) for a in slot_feats], [f32(a) for a in slot_pes], [f32(a) for a in obj_ptrs]
+    n_slots, n_ptrs = len(feats), len(ptrs)
+    slot_tokens = feats[0].size // hp["mem_dim"] if n_slots else 0
+    ptr_arr = lambda arrs: (ctypes.c_void_p * max(len(arrs), 1))(*[a.ctypes.data for a in arrs])
+    cond = np.ascontiguousarray(slot_is_cond, dtype=np.int32).reshape(-1)
+    frames = np.ascontiguousarray(ptr_frames, dtype=np.int32).reshape(-1)
+    te, w, b = f32(tpos_enc), f32(tpos_proj_w), f32(tpos_proj_b)
+    split = hp["d_model"] // hp["mem_dim"]
+    cap = n_slots * slot_tokens + min(n_ptrs, hp["max_obj_ptrs"]) * split
+    prompt = np.empty((max(cap, 1), hp["mem_dim"]), np.float32)
+    pos = np.empty_like(prompt)
+    n_ptr_tokens = ctypes.c_int32()
+    data = lambda a: None if a is None else a.ctypes.data
+    m = lib().sam3b200_build_mem_prompt(ctypes.byref(h), n_slots, slot_tokens, ptr_arr(feats), ptr_arr(pes),
+                                        cond.ctypes.data, n_ptrs, ptr_arr(ptrs), frames.ctypes.data, cur_frame,
+                                        data(te), data(w), data(b), prompt.ctypes.data, pos.ctypes.data, cap,
+                                        ctypes.byref(n_ptr_tokens))
+    if m < 0:
+        raise B200Error(f"build_mem_prompt failed: {last_error()}")
+    return prompt[:m], pos[:m], n_ptr_tokens.value
+
+
 def graph_compute_status(be_handle, nodes) -> int:
     """sam3b200_graph_compute on a list of GraphTensor nodes; returns the ggml_status."""
     arr = (ctypes.POINTER(GraphTensor) * max(len(nodes), 1))(*[ctypes.pointer(n) for n in nodes])
@@ -147,6 +191,9 @@ def lib() -> ctypes.CDLL:
         "sam3b200_conv_2d": (i32, [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp]),
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
         "sam3b200_supports_op": (i32, [ctypes.POINTER(GraphTensor)]),
+        "sam3b200_select_memory_frames": (i32, [i32, i32, vp, i32]),
+        "sam3b200_build_mem_prompt": (i64, [vp, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, i64,
+                                            vp]),
         "sam3b200_graph_compute": (i32, [vp, ctypes.POINTER(ctypes.POINTER(GraphTensor)), i32]),
         "sam3b200_sam_dec_create": (vp, [vp, vp]),
         "sam3b200_sam_dec_free": (None, [vp]),

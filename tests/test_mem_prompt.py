@@ -1,0 +1,108 @@
+"""Host-side memory prompt preparation of the tracker (sam3b200_select_memory_frames,
+sam3b200_build_mem_prompt) against the CPU restatement of sam3_select_memory_frames and
+sam3_build_prompt_and_pos (oracle/mem_prompt_oracle.py).  No GPU: the reference runs this on the
+CPU between the decoder and the memory-attention graphs, and so does this library."""
+import numpy as np
+import pytest
+
+import mem_prompt_oracle as mpo
+
+HP = {"d_model": 256, "mem_dim": 64, "num_maskmem": 7, "max_obj_ptrs": 16}  # SAM2 / SAM3 trackers
+
+
+@pytest.mark.parametrize("max_slots", range(0, 10))
+def test_select_memory_frames_matches_the_restatement(b200, max_slots):
+    for bank in range(0, 41):
+        got = b200.select_memory_frames(bank, max_slots)
+        assert got == mpo.select_memory_frames(bank, max_slots), (bank, max_slots)
+        if bank:
+            assert got == sorted(set(got))
+            if bank > max_slots:
+                assert got[0] == 0 and got[-1] == bank - 1  # the first and the newest slot always take part
+                assert len(got) <= max(max_slots, 2)
+
+
+def test_select_memory_frames_known_cases(b200):
+    """Hand-derived from the reference rule: 7 slots of a 20-slot bank: step 18 / 6 = 3 ->
+    1 + 3, 1 + 6, ... clamped to 18."""
+    assert b200.select_memory_frames(5, 7) == [0, 1, 2, 3, 4]
+    assert b200.select_memory_frames(20, 7) == [0, 4, 7, 10, 13, 16, 19]
+    assert b200.select_memory_frames(9, 7) == [0, 2, 3, 4, 5, 6, 8]  # step 7 / 6: 1 + 1.16.. -> 2, ..., 1 + 5.83 -> 6
+
+
+def _case(rng, n_slots, slot_tokens, n_ptrs, cond=(0,), with_tables=True):
+    MD, D = HP["mem_dim"], HP["d_model"]
+    feats = [rng.normal(0, 1, size=(slot_tokens, MD)).astype(np.float32) for _ in range(n_slots)]
+    pes = [rng.normal(0, 1, size=(slot_tokens, MD)).astype(np.float32) for _ in range(n_slots)]
+    is_cond = [1 if s in cond else 0 for s in range(n_slots)]
+    ptrs = [rng.normal(0, 1, size=D).astype(np.float32) for _ in range(n_ptrs)]
+    frames = list(rng.integers(0, 30, size=n_ptrs))
+    tables = {}
+    if with_tables:
+        tables = {"tpos_enc": rng.normal(0, 0.1, size=(HP["num_maskmem"], MD)).astype(np.float32),
+                  "tpos_proj_w": rng.normal(0, 0.05, size=(MD, D)).astype(np.float32),
+                  "tpos_proj_b": rng.normal(0, 0.1, size=MD).astype(np.float32)}
+    return feats, pes, is_cond, ptrs, frames, tables
+
+
+def _check(b200, case, cur_frame):
+    feats, pes, is_cond, ptrs, frames, tables = case
+    got_p, got_pos, got_n = b200.build_mem_prompt(HP, feats, pes, is_cond, ptrs, frames, cur_frame, **tables)
+    ref_p, ref_pos, ref_n = mpo.build_mem_prompt(HP["d_model"], HP["mem_dim"], HP["num_maskmem"],
+                                                 HP["max_obj_ptrs"], feats, pes, is_cond, ptrs, frames, cur_frame,
+                                                 **tables)
+    assert got_n == ref_n and got_p.shape == ref_p.shape
+    m_spatial = got_p.shape[0] - got_n
+    assert np.array_equal(got_p, ref_p)                           # copies
+    assert np.array_equal(got_pos[:m_spatial], ref_pos[:m_spatial])  # one f32 add per element
+    # pointer codes: libm sin/cos/pow and an f32 dot against numpy's float32 / float64 -- 1e-5
+    np.testing.assert_allclose(got_pos[m_spatial:], ref_pos[m_spatial:], rtol=1e-5, atol=1e-5)
+    return got_p, got_pos, got_n
+
+
+def test_config5_prompt(b200):
+    """7 memory frames of 64 x 64 tokens (frame 0 conditioning) + 20 pointers, 16 of them used:
+    28,736 prompt tokens, the memory attention's M at config 5."""
+    rng = np.random.default_rng(5)
+    case = _case(rng, 7, 64 * 64, 20)
+    case[4][:3] = [10, 9, 11]  # distance 0 -> 1, and 1 on either side
+    p, pos, n = _check(b200, case, cur_frame=10)
+    assert p.shape == (7 * 4096 + 16 * 4, 64) and n == 64
+    assert np.array_equal(pos[:4096], case[1][0] + case[5]["tpos_enc"][6])  # conditioning slot: t = 0
+    assert np.array_equal(pos[4096:8192], case[1][1] + case[5]["tpos_enc"][6 - 6])  # t = 7 - 1 = 6 -> row 0
+    # the four tokens of a pointer share its positional code and carry its 256 values in order
+    assert np.array_equal(pos[-64:-60], np.repeat(pos[-64][None], 4, 0))
+    assert np.array_equal(p[7 * 4096:7 * 4096 + 4].reshape(-1), case[3][0])
+
+
+def test_slots_beyond_the_temporal_table_get_no_temporal_code(b200):
+    """With 8 slots the oldest non-conditioning one has t = 8 >= num_maskmem: spatial code only."""
+    rng = np.random.default_rng(6)
+    case = _case(rng, 8, 16, 3, cond=())
+    _, pos, _ = _check(b200, case, cur_frame=4)
+    assert np.array_equal(pos[:16], case[1][0])
+
+
+@pytest.mark.parametrize("n_slots,n_ptrs,tables", [(0, 5, True), (3, 0, True), (2, 2, False), (0, 0, True)])
+def test_edge_shapes(b200, n_slots, n_ptrs, tables):
+    rng = np.random.default_rng(n_slots * 10 + n_ptrs)
+    _check(b200, _case(rng, n_slots, 32, n_ptrs, with_tables=tables), cur_frame=7)
+
+
+def test_rejects_bad_arguments(b200):
+    L = b200.lib()
+    assert L.sam3b200_build_mem_prompt(None, 0, 0, None, None, None, 0, None, None, 0, None, None, None, None,
+                                       None, 0, None) == -1
+    assert "hyper-parameters" in b200.last_error()
+    assert L.sam3b200_select_memory_frames(20, 7, None, 0) == -1
+    hp = b200.MemPromptHparams(256, 64, 7, 16)
+    import ctypes
+    n = ctypes.c_int32()
+    buf = np.empty((4, 64), np.float32)
+    ptr = np.zeros(256, np.float32)
+    arr = (ctypes.c_void_p * 1)(ptr.ctypes.data)
+    frames = np.zeros(1, np.int32)
+    # one pointer = 4 tokens, room for 3
+    assert L.sam3b200_build_mem_prompt(ctypes.byref(hp), 0, 0, None, None, None, 1, arr, frames.ctypes.data, 0,
+                                       None, None, None, buf.ctypes.data, buf.ctypes.data, 3, ctypes.byref(n)) == -1
+    assert "room for 3" in b200.last_error()
