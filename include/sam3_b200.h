@@ -441,6 +441,15 @@ int64_t sam3b200_build_mem_prompt(const sam3b200_mem_prompt_hparams *hp, int n_s
                                   const float *tpos_proj_w, const float *tpos_proj_b, float *prompt,
                                   float *prompt_pos, int64_t cap_tokens, int32_t *n_ptr_tokens);
 
+/* sam3_extract_obj_ptr_cpu (sam3.cpp:9347-9420): the object pointer of a
+ * decoded frame -- the SAM output token (sam3b200_sam_dec_outputs) through
+ * obj_ptr_proj (three d_model x d_model layers, ReLU after the first two;
+ * w[j] f32 [out][in], b[j] f32 [out]), or no_obj_ptr when the object-score
+ * logit is <= 0.  blend != 0 is the SAM2 / EdgeTAM fixed_no_obj_ptr rule:
+ * l * mlp + (1 - l) * no_obj_ptr with l = [obj_score > 0].  Host code. */
+int sam3b200_extract_obj_ptr(int d_model, int blend, const float *sam_token, float obj_score,
+                             const float *const *w, const float *const *b, const float *no_obj_ptr, float *out);
+
 /* ---- Memory encoder of the video tracker ----------------------------------
  * sam3_encode_memory (sam3.cpp:11510-11615) up to the stored [mem_dim, H, H]
  * memory features: mask logits resized to img (bilinear), sigmoid * scale +

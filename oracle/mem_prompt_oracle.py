@@ -11,6 +11,9 @@ sam3b200_build_mem_prompt.  It restates, in plain Python / numpy:
   - sam3_build_prompt_and_pos (sam3.cpp:9126-9217): spatial tokens with pos + tpos_enc[num_maskmem
     - t - 1] when 0 <= t < num_maskmem; each pointer split into D / MD tokens whose positional
     code is obj_ptr_tpos_proj(sine_1d(distance / 15)) (sam3_get_1d_sine_pe, sam3.cpp:3641-3651).
+  - sam3_extract_obj_ptr_cpu (sam3.cpp:9347-9420): the SAM token through three D x D layers (ReLU
+    after the first two), or no_obj_ptr for a non-positive object score (SAM3), or the SAM2 blend
+    l * mlp + (1 - l) * no_obj_ptr, l = [score > 0].
 Token rows are [tokens][MD] float32.
 """
 from __future__ import annotations
@@ -75,3 +78,21 @@ def build_mem_prompt(d_model: int, mem_dim: int, num_maskmem: int, max_obj_ptrs:
     if not prompt:
         return np.zeros((0, MD), F32), np.zeros((0, MD), F32), 0
     return np.concatenate(prompt).astype(F32), np.concatenate(pos).astype(F32), n_ptr_tokens
+
+
+def extract_obj_ptr(sam_token, obj_score: float, w, b, no_obj_ptr, blend: bool = False) -> np.ndarray:
+    """w[j]: [out][in] float32; accumulation in float64 (the C code sums in f32 order)."""
+    nop = np.asarray(no_obj_ptr, F32).reshape(-1)
+    if not blend and obj_score <= 0.0:
+        return nop.copy()
+    h = np.asarray(sam_token, F32).astype(np.float64)
+    for j in range(3):
+        h = np.asarray(b[j], np.float64) + np.asarray(w[j], np.float64) @ h
+        if j < 2:
+            h = np.maximum(h, 0.0)
+        h = h.astype(F32).astype(np.float64)
+    h = h.astype(F32)
+    if blend:
+        lam = F32(1.0) if obj_score > 0.0 else F32(0.0)
+        return (lam * h + (F32(1.0) - lam) * nop).astype(F32)
+    return h

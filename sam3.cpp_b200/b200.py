@@ -125,6 +125,19 @@ def build_mem_prompt(hp: dict, slot_feats, slot_pes, slot_is_cond, obj_ptrs, ptr
     return prompt[:m], pos[:m], n_ptr_tokens.value
 
 
+def extract_obj_ptr(sam_token, obj_score: float, w, b, no_obj_ptr, blend: bool = False) -> np.ndarray:
+    """sam3b200_extract_obj_ptr: the object pointer of a decoded frame (w: three f32 [D][D] layers
+    [out][in], b: three f32 [D])."""
+    f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    tok, nop = f32(sam_token).reshape(-1), f32(no_obj_ptr).reshape(-1)
+    ws, bs = [f32(x) for x in w], [f32(x) for x in b]
+    arr = lambda arrs: (ctypes.c_void_p * 3)(*[a.ctypes.data for a in arrs])
+    out = np.empty(tok.size, np.float32)
+    _check(lib().sam3b200_extract_obj_ptr(tok.size, 1 if blend else 0, tok.ctypes.data, obj_score, arr(ws),
+                                          arr(bs), nop.ctypes.data, out.ctypes.data), "extract_obj_ptr")
+    return out
+
+
 def graph_compute_status(be_handle, nodes) -> int:
     """sam3b200_graph_compute on a list of GraphTensor nodes; returns the ggml_status."""
     arr = (ctypes.POINTER(GraphTensor) * max(len(nodes), 1))(*[ctypes.pointer(n) for n in nodes])
@@ -192,6 +205,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_get_rows": (i32, [vp, i32, vp, i64, i64, vp, i64, vp]),
         "sam3b200_supports_op": (i32, [ctypes.POINTER(GraphTensor)]),
         "sam3b200_select_memory_frames": (i32, [i32, i32, vp, i32]),
+        "sam3b200_extract_obj_ptr": (i32, [i32, i32, vp, ctypes.c_float, vp, vp, vp, vp]),
         "sam3b200_build_mem_prompt": (i64, [vp, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, i64,
                                             vp]),
         "sam3b200_graph_compute": (i32, [vp, ctypes.POINTER(ctypes.POINTER(GraphTensor)), i32]),

@@ -140,3 +140,39 @@ extern "C" int64_t sam3b200_build_mem_prompt(const sam3b200_mem_prompt_hparams *
     *n_ptr_tokens = P * split;
     return m_total;
 }
+
+// sam3_extract_obj_ptr_cpu (sam3.cpp:9347-9420): the object pointer a propagated (or prompted) frame adds
+// to the pointer bank -- the decoder's SAM output token through obj_ptr_proj (three D x D layers, ReLU
+// after the first two), replaced by no_obj_ptr when the object-score logit says the object is absent
+// (SAM3: score <= 0 -> no_obj_ptr, the MLP skipped; SAM2 / EdgeTAM with fixed_no_obj_ptr: the blend
+// l * mlp + (1 - l) * no_obj_ptr with l = [score > 0]).  Weights f32 row-major [out][in] (ggml [in, out]).
+extern "C" int sam3b200_extract_obj_ptr(int d_model, int blend, const float *sam_token, float obj_score,
+                                        const float *const *w, const float *const *b, const float *no_obj_ptr,
+                                        float *out) {
+    const int D = d_model;
+    if (D <= 0 || !sam_token || !w || !b || !no_obj_ptr || !out || !w[0] || !w[1] || !w[2] || !b[0] || !b[1] ||
+        !b[2]) {
+        set_error("extract_obj_ptr: null argument or bad width");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (!blend && obj_score <= 0.0f) {
+        std::copy(no_obj_ptr, no_obj_ptr + D, out);
+        return SAM3B200_STATUS_SUCCESS;
+    }
+    std::vector<float> h(sam_token, sam_token + D), tmp(D);
+    for (int j = 0; j < 3; ++j) {
+        for (int o = 0; o < D; ++o) {
+            float sum = b[j][o];
+            for (int i = 0; i < D; ++i) sum += w[j][static_cast<int64_t>(o) * D + i] * h[i];
+            tmp[o] = j < 2 ? std::max(0.0f, sum) : sum;
+        }
+        std::swap(h, tmp);
+    }
+    if (blend) {
+        const float l = obj_score > 0.0f ? 1.0f : 0.0f;
+        for (int i = 0; i < D; ++i) out[i] = l * h[i] + (1.0f - l) * no_obj_ptr[i];
+    } else {
+        std::copy(h.begin(), h.end(), out);
+    }
+    return SAM3B200_STATUS_SUCCESS;
+}

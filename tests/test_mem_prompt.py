@@ -1,6 +1,7 @@
 """Host-side memory prompt preparation of the tracker (sam3b200_select_memory_frames,
-sam3b200_build_mem_prompt) against the CPU restatement of sam3_select_memory_frames and
-sam3_build_prompt_and_pos (oracle/mem_prompt_oracle.py).  No GPU: the reference runs this on the
+sam3b200_build_mem_prompt, sam3b200_extract_obj_ptr) against the CPU restatement of
+sam3_select_memory_frames, sam3_build_prompt_and_pos and sam3_extract_obj_ptr_cpu
+(oracle/mem_prompt_oracle.py).  No GPU: the reference runs this on the
 CPU between the decoder and the memory-attention graphs, and so does this library."""
 import numpy as np
 import pytest
@@ -106,3 +107,21 @@ def test_rejects_bad_arguments(b200):
     assert L.sam3b200_build_mem_prompt(ctypes.byref(hp), 0, 0, None, None, None, 1, arr, frames.ctypes.data, 0,
                                        None, None, None, buf.ctypes.data, buf.ctypes.data, 3, ctypes.byref(n)) == -1
     assert "room for 3" in b200.last_error()
+
+
+@pytest.mark.parametrize("score,blend", [(2.5, False), (-0.3, False), (0.0, False), (1.0, True), (-1.0, True)])
+def test_extract_obj_ptr(b200, score, blend):
+    """sam3_extract_obj_ptr_cpu: MLP pointer for a present object, no_obj_ptr (SAM3) or the blend (SAM2)."""
+    rng = np.random.default_rng(int(abs(score) * 10) + blend)
+    D = 256
+    tok = rng.normal(0, 1, size=D).astype(np.float32)
+    w = [rng.normal(0, 1 / 16, size=(D, D)).astype(np.float32) for _ in range(3)]
+    b = [rng.normal(0, 0.1, size=D).astype(np.float32) for _ in range(3)]
+    nop = rng.normal(0, 1, size=D).astype(np.float32)
+    got = b200.extract_obj_ptr(tok, score, w, b, nop, blend)
+    ref = mpo.extract_obj_ptr(tok, score, w, b, nop, blend)
+    if score <= 0:
+        assert np.array_equal(got, nop)  # the absent-object pointer, exactly
+    else:
+        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
+        assert not np.array_equal(got, nop)
