@@ -450,6 +450,32 @@ int64_t sam3b200_build_mem_prompt(const sam3b200_mem_prompt_hparams *hp, int n_s
 int sam3b200_extract_obj_ptr(int d_model, int blend, const float *sam_token, float obj_score,
                              const float *const *w, const float *const *b, const float *no_obj_ptr, float *out);
 
+/* sam3_sinusoidal_pe_2d (sam3.cpp:3601-3637): the 2-D sine code of an H x W
+ * map, out [H][W][d_model] (channels [0, d/2) from y, [d/2, d) from x). */
+int sam3b200_sinusoidal_pe_2d(int H, int W, int d_model, float *out);
+
+/* The memory of one tracked object in one stream (sam3_tracker's mem_banks /
+ * ptr_banks, sam3.cpp:951-990), host side.  add_slot stores the features the
+ * memory encoder produced for a frame ([H*H][MD], sam3b200_mem_enc_output
+ * copied back) with the H x H sine code, keeping at most num_maskmem slots by
+ * dropping the oldest non-conditioning slot (else slot 1) as
+ * sam3_encode_memory does (:11700-11711); add_ptr keeps the newest
+ * max_obj_ptrs object pointers (sam3_store_obj_ptr, :11716-11734); prompt
+ * selects the slots and builds the memory attention's prompt for cur_frame
+ * as sam3_propagate_single does (sam3b200_select_memory_frames +
+ * sam3b200_build_mem_prompt).  state reports the slot frames / flags and the
+ * pointer frames; returns the slot count. */
+typedef struct sam3b200_mem_bank sam3b200_mem_bank;
+sam3b200_mem_bank *sam3b200_mem_bank_create(const sam3b200_mem_prompt_hparams *hp, int feat_size);
+void sam3b200_mem_bank_free(sam3b200_mem_bank *b);
+int sam3b200_mem_bank_add_slot(sam3b200_mem_bank *b, const float *feats, int frame, int is_cond);
+int sam3b200_mem_bank_add_ptr(sam3b200_mem_bank *b, const float *ptr, int frame);
+int sam3b200_mem_bank_state(const sam3b200_mem_bank *b, int32_t *slot_frames, int32_t *slot_cond, int slot_cap,
+                            int32_t *ptr_frames, int ptr_cap, int32_t *n_ptrs);
+int64_t sam3b200_mem_bank_prompt(const sam3b200_mem_bank *b, int cur_frame, const float *tpos_enc,
+                                 const float *tpos_proj_w, const float *tpos_proj_b, float *prompt,
+                                 float *prompt_pos, int64_t cap_tokens, int32_t *n_ptr_tokens);
+
 /* ---- Memory encoder of the video tracker ----------------------------------
  * sam3_encode_memory (sam3.cpp:11510-11615) up to the stored [mem_dim, H, H]
  * memory features: mask logits resized to img (bilinear), sigmoid * scale +

@@ -14,6 +14,9 @@ sam3b200_build_mem_prompt.  It restates, in plain Python / numpy:
   - sam3_extract_obj_ptr_cpu (sam3.cpp:9347-9420): the SAM token through three D x D layers (ReLU
     after the first two), or no_obj_ptr for a non-positive object score (SAM3), or the SAM2 blend
     l * mlp + (1 - l) * no_obj_ptr, l = [score > 0].
+  - sam3_sinusoidal_pe_2d (sam3.cpp:3601-3637) and the memory-bank eviction of sam3_encode_memory
+    (:11700-11711: beyond num_maskmem slots drop the oldest non-conditioning slot, else slot 1) and
+    sam3_store_obj_ptr (:11716-11734: keep the newest max_obj_ptrs pointers).
 Token rows are [tokens][MD] float32.
 """
 from __future__ import annotations
@@ -96,3 +99,44 @@ def extract_obj_ptr(sam_token, obj_score: float, w, b, no_obj_ptr, blend: bool =
         lam = F32(1.0) if obj_score > 0.0 else F32(0.0)
         return (lam * h + (F32(1.0) - lam) * nop).astype(F32)
     return h
+
+
+def sinusoidal_pe_2d(H: int, W: int, d_model: int) -> np.ndarray:
+    """[H][W][d_model] float32; channels [0, d/2) from y, [d/2, d) from x; sin on even, cos on odd."""
+    half = d_model // 2
+    i = np.arange(half)
+    dim_t = np.power(F32(10000.0), (i & ~1).astype(F32) / F32(half)).astype(F32)
+    scale = F32(2.0 * np.pi)
+    py = ((np.arange(H, dtype=F32) + F32(1)) / F32(H) * scale).astype(F32)
+    px = ((np.arange(W, dtype=F32) + F32(1)) / F32(W) * scale).astype(F32)
+    vy = (py[:, None] / dim_t[None, :]).astype(F32)
+    vx = (px[:, None] / dim_t[None, :]).astype(F32)
+    ey = np.where(i % 2 == 0, np.sin(vy), np.cos(vy)).astype(F32)  # [H][half]
+    ex = np.where(i % 2 == 0, np.sin(vx), np.cos(vx)).astype(F32)  # [W][half]
+    out = np.empty((H, W, d_model), F32)
+    out[:, :, :half] = ey[:, None, :]
+    out[:, :, half:] = ex[None, :, :]
+    return out
+
+
+class MemBank:
+    """The bank's bookkeeping: slots [(frame, is_cond, feats)], pointers [(frame, ptr)]."""
+
+    def __init__(self, num_maskmem: int, max_obj_ptrs: int):
+        self.num_maskmem, self.max_obj_ptrs = num_maskmem, max_obj_ptrs
+        self.slots, self.ptrs = [], []
+
+    def add_slot(self, feats, frame: int, is_cond: bool) -> None:
+        self.slots.append((frame, bool(is_cond), np.asarray(feats, F32)))
+        while len(self.slots) > self.num_maskmem:
+            for k, sl in enumerate(self.slots):
+                if not sl[1]:
+                    del self.slots[k]
+                    break
+            else:
+                del self.slots[1]
+
+    def add_ptr(self, ptr, frame: int) -> None:
+        self.ptrs.append((frame, np.asarray(ptr, F32)))
+        while len(self.ptrs) > self.max_obj_ptrs:
+            del self.ptrs[0]

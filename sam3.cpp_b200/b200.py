@@ -138,6 +138,72 @@ def extract_obj_ptr(sam_token, obj_score: float, w, b, no_obj_ptr, blend: bool =
     return out
 
 
+def sinusoidal_pe_2d(H: int, W: int, d_model: int) -> np.ndarray:
+    """sam3b200_sinusoidal_pe_2d: [H][W][d_model] float32."""
+    out = np.empty((H, W, d_model), np.float32)
+    _check(lib().sam3b200_sinusoidal_pe_2d(H, W, d_model, out.ctypes.data), "sinusoidal_pe_2d")
+    return out
+
+
+class MemBank:
+    """sam3b200_mem_bank: the host-side memory of one tracked object (slots + object pointers)."""
+
+    def __init__(self, hp: dict, feat_size: int):
+        self.hp, self.H = hp, feat_size
+        h = MemPromptHparams(hp["d_model"], hp["mem_dim"], hp["num_maskmem"], hp["max_obj_ptrs"])
+        self.h = lib().sam3b200_mem_bank_create(ctypes.byref(h), feat_size)
+        if not self.h:
+            raise B200Error(f"mem_bank_create failed: {last_error()}")
+
+    def add_slot(self, feats: np.ndarray, frame: int, is_cond: bool) -> None:
+        f = np.ascontiguousarray(feats, dtype=np.float32)
+        assert f.size == self.H * self.H * self.hp["mem_dim"]
+        _check(lib().sam3b200_mem_bank_add_slot(self.h, f.ctypes.data, frame, 1 if is_cond else 0), "add_slot")
+
+    def add_ptr(self, ptr: np.ndarray, frame: int) -> None:
+        p = np.ascontiguousarray(ptr, dtype=np.float32)
+        assert p.size == self.hp["d_model"]
+        _check(lib().sam3b200_mem_bank_add_ptr(self.h, p.ctypes.data, frame), "add_ptr")
+
+    def state(self):
+        """([(slot frame, is_cond)], [pointer frame])."""
+        cap = self.hp["num_maskmem"] + self.hp["max_obj_ptrs"] + 2
+        sf, sc, pf = (np.zeros(cap, np.int32) for _ in range(3))
+        n_ptrs = ctypes.c_int32()
+        ns = lib().sam3b200_mem_bank_state(self.h, sf.ctypes.data, sc.ctypes.data, cap, pf.ctypes.data, cap,
+                                           ctypes.byref(n_ptrs))
+        if ns < 0:
+            raise B200Error(f"mem_bank_state failed: {last_error()}")
+        return [(int(sf[i]), bool(sc[i])) for i in range(ns)], [int(x) for x in pf[:n_ptrs.value]]
+
+    def prompt(self, cur_frame: int, tpos_enc=None, tpos_proj_w=None, tpos_proj_b=None):
+        """(prompt [M][MD], prompt_pos [M][MD], n_ptr_tokens) for the frame cur_frame."""
+        f32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+        te, w, b = f32(tpos_enc), f32(tpos_proj_w), f32(tpos_proj_b)
+        cap = self.hp["num_maskmem"] * self.H * self.H + self.hp["max_obj_ptrs"] * (
+            self.hp["d_model"] // self.hp["mem_dim"])
+        prompt = np.empty((max(cap, 1), self.hp["mem_dim"]), np.float32)
+        pos = np.empty_like(prompt)
+        n = ctypes.c_int32()
+        data = lambda a: None if a is None else a.ctypes.data
+        m = lib().sam3b200_mem_bank_prompt(self.h, cur_frame, data(te), data(w), data(b), prompt.ctypes.data,
+                                           pos.ctypes.data, cap, ctypes.byref(n))
+        if m < 0:
+            raise B200Error(f"mem_bank_prompt failed: {last_error()}")
+        return prompt[:m], pos[:m], n.value
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_mem_bank_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 def graph_compute_status(be_handle, nodes) -> int:
     """sam3b200_graph_compute on a list of GraphTensor nodes; returns the ggml_status."""
     arr = (ctypes.POINTER(GraphTensor) * max(len(nodes), 1))(*[ctypes.pointer(n) for n in nodes])
@@ -206,6 +272,13 @@ def lib() -> ctypes.CDLL:
         "sam3b200_supports_op": (i32, [ctypes.POINTER(GraphTensor)]),
         "sam3b200_select_memory_frames": (i32, [i32, i32, vp, i32]),
         "sam3b200_extract_obj_ptr": (i32, [i32, i32, vp, ctypes.c_float, vp, vp, vp, vp]),
+        "sam3b200_sinusoidal_pe_2d": (i32, [i32, i32, i32, vp]),
+        "sam3b200_mem_bank_create": (vp, [vp, i32]),
+        "sam3b200_mem_bank_free": (None, [vp]),
+        "sam3b200_mem_bank_add_slot": (i32, [vp, vp, i32, i32]),
+        "sam3b200_mem_bank_add_ptr": (i32, [vp, vp, i32]),
+        "sam3b200_mem_bank_state": (i32, [vp, vp, vp, i32, vp, i32, vp]),
+        "sam3b200_mem_bank_prompt": (i64, [vp, i32, vp, vp, vp, vp, vp, i64, vp]),
         "sam3b200_build_mem_prompt": (i64, [vp, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, i64,
                                             vp]),
         "sam3b200_graph_compute": (i32, [vp, ctypes.POINTER(ctypes.POINTER(GraphTensor)), i32]),

@@ -176,3 +176,134 @@ extern "C" int sam3b200_extract_obj_ptr(int d_model, int blend, const float *sam
     }
     return SAM3B200_STATUS_SUCCESS;
 }
+
+// sam3_sinusoidal_pe_2d (sam3.cpp:3601-3637): PositionEmbeddingSine with normalised positions
+// (p + 1) / n * 2 pi, temperature 1e4; channels [0, d/2) encode y, [d/2, d) encode x; pairs of
+// channels share a frequency (sin on even, cos on odd).  out [H][W][d_model].
+extern "C" int sam3b200_sinusoidal_pe_2d(int H, int W, int d_model, float *out) {
+    if (H <= 0 || W <= 0 || d_model <= 0 || d_model % 2 != 0 || !out) {
+        set_error("sinusoidal_pe_2d: bad arguments");
+        return SAM3B200_STATUS_FAILED;
+    }
+    const int half = d_model / 2;
+    const float scale = 2.0f * static_cast<float>(M_PI);
+    std::vector<float> dim_t(half);
+    for (int i = 0; i < half; ++i) dim_t[i] = powf(10000.0f, static_cast<float>(i & ~1) / static_cast<float>(half));
+    for (int y = 0; y < H; ++y)
+        for (int x = 0; x < W; ++x) {
+            const float py = (static_cast<float>(y + 1) / static_cast<float>(H)) * scale;
+            const float px = (static_cast<float>(x + 1) / static_cast<float>(W)) * scale;
+            float *o = out + (static_cast<int64_t>(y) * W + x) * d_model;
+            for (int i = 0; i < half; ++i) {
+                o[i] = i % 2 == 0 ? sinf(py / dim_t[i]) : cosf(py / dim_t[i]);
+                o[half + i] = i % 2 == 0 ? sinf(px / dim_t[i]) : cosf(px / dim_t[i]);
+            }
+        }
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+// The memory of one tracked object in one video stream: the slots sam3_encode_memory stores
+// (features [H*H][MD] with the stream's sinusoidal code, frame, conditioning flag; at most num_maskmem,
+// evicting the oldest non-conditioning slot first, else slot 1 -- sam3.cpp:11700-11711) and the object
+// pointers sam3_store_obj_ptr keeps (at most max_obj_ptrs, oldest first out -- :11716-11734).
+struct sam3b200_mem_bank {
+    sam3b200_mem_prompt_hparams hp{};
+    int H = 0;
+    std::vector<float> pe;  // sinusoidal code shared by every slot [H*H][MD]
+    struct Slot {
+        std::vector<float> feats;
+        int frame;
+        int cond;
+    };
+    std::vector<Slot> slots;
+    std::vector<std::pair<int, std::vector<float>>> ptrs;
+};
+
+extern "C" sam3b200_mem_bank *sam3b200_mem_bank_create(const sam3b200_mem_prompt_hparams *hp, int feat_size) {
+    if (!hp || hp->mem_dim <= 0 || hp->d_model <= 0 || hp->d_model % hp->mem_dim != 0 || hp->mem_dim % 2 != 0 ||
+        hp->num_maskmem <= 0 || hp->max_obj_ptrs < 0 || feat_size <= 0 || feat_size > 4096) {
+        set_error("mem_bank_create: bad hyper-parameters");
+        return nullptr;
+    }
+    auto *b = new sam3b200_mem_bank();
+    b->hp = *hp;
+    b->H = feat_size;
+    b->pe.resize(static_cast<size_t>(feat_size) * feat_size * hp->mem_dim);
+    sam3b200_sinusoidal_pe_2d(feat_size, feat_size, hp->mem_dim, b->pe.data());
+    return b;
+}
+
+extern "C" void sam3b200_mem_bank_free(sam3b200_mem_bank *b) { delete b; }
+
+extern "C" int sam3b200_mem_bank_add_slot(sam3b200_mem_bank *b, const float *feats, int frame, int is_cond) {
+    if (!b || !feats) {
+        set_error("mem_bank_add_slot: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    const size_t n = static_cast<size_t>(b->H) * b->H * b->hp.mem_dim;
+    b->slots.push_back({std::vector<float>(feats, feats + n), frame, is_cond ? 1 : 0});
+    while (static_cast<int>(b->slots.size()) > b->hp.num_maskmem) {
+        auto it = std::find_if(b->slots.begin(), b->slots.end(), [](const sam3b200_mem_bank::Slot &s) {
+            return !s.cond;
+        });
+        b->slots.erase(it != b->slots.end() ? it : b->slots.begin() + 1);
+    }
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+extern "C" int sam3b200_mem_bank_add_ptr(sam3b200_mem_bank *b, const float *ptr, int frame) {
+    if (!b || !ptr) {
+        set_error("mem_bank_add_ptr: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    b->ptrs.emplace_back(frame, std::vector<float>(ptr, ptr + b->hp.d_model));
+    while (static_cast<int>(b->ptrs.size()) > b->hp.max_obj_ptrs) b->ptrs.erase(b->ptrs.begin());
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+extern "C" int sam3b200_mem_bank_state(const sam3b200_mem_bank *b, int32_t *slot_frames, int32_t *slot_cond,
+                                       int slot_cap, int32_t *ptr_frames, int ptr_cap, int32_t *n_ptrs) {
+    if (!b || !n_ptrs) {
+        set_error("mem_bank_state: null argument");
+        return -1;
+    }
+    const int ns = static_cast<int>(b->slots.size()), np = static_cast<int>(b->ptrs.size());
+    for (int i = 0; i < ns && i < slot_cap; ++i) {
+        if (slot_frames) slot_frames[i] = b->slots[i].frame;
+        if (slot_cond) slot_cond[i] = b->slots[i].cond;
+    }
+    for (int i = 0; i < np && i < ptr_cap; ++i)
+        if (ptr_frames) ptr_frames[i] = b->ptrs[i].first;
+    *n_ptrs = np;
+    return ns;
+}
+
+extern "C" int64_t sam3b200_mem_bank_prompt(const sam3b200_mem_bank *b, int cur_frame, const float *tpos_enc,
+                                            const float *tpos_proj_w, const float *tpos_proj_b, float *prompt,
+                                            float *prompt_pos, int64_t cap_tokens, int32_t *n_ptr_tokens) {
+    if (!b) {
+        set_error("mem_bank_prompt: null bank");
+        return -1;
+    }
+    const int ns = static_cast<int>(b->slots.size());
+    std::vector<int32_t> sel(std::max(ns, 2));
+    const int n_sel = sam3b200_select_memory_frames(ns, b->hp.num_maskmem, sel.data(), static_cast<int>(sel.size()));
+    if (n_sel < 0) return -1;
+    std::vector<const float *> feats(n_sel), pes(n_sel);
+    std::vector<int32_t> cond(n_sel);
+    for (int s = 0; s < n_sel; ++s) {
+        feats[s] = b->slots[sel[s]].feats.data();
+        pes[s] = b->pe.data();
+        cond[s] = b->slots[sel[s]].cond;
+    }
+    const int np = static_cast<int>(b->ptrs.size());
+    std::vector<const float *> ptrs(np);
+    std::vector<int32_t> frames(np);
+    for (int p = 0; p < np; ++p) {
+        ptrs[p] = b->ptrs[p].second.data();
+        frames[p] = b->ptrs[p].first;
+    }
+    return sam3b200_build_mem_prompt(&b->hp, n_sel, b->H * b->H, feats.data(), pes.data(), cond.data(), np,
+                                     ptrs.data(), frames.data(), cur_frame, tpos_enc, tpos_proj_w, tpos_proj_b,
+                                     prompt, prompt_pos, cap_tokens, n_ptr_tokens);
+}

@@ -1,7 +1,7 @@
-"""Host-side memory prompt preparation of the tracker (sam3b200_select_memory_frames,
-sam3b200_build_mem_prompt, sam3b200_extract_obj_ptr) against the CPU restatement of
-sam3_select_memory_frames, sam3_build_prompt_and_pos and sam3_extract_obj_ptr_cpu
-(oracle/mem_prompt_oracle.py).  No GPU: the reference runs this on the
+"""Host-side memory of the tracker (sam3b200_select_memory_frames, sam3b200_build_mem_prompt,
+sam3b200_extract_obj_ptr, sam3b200_sinusoidal_pe_2d, sam3b200_mem_bank_*) against the CPU
+restatement of sam3_select_memory_frames, sam3_build_prompt_and_pos, sam3_extract_obj_ptr_cpu,
+sam3_sinusoidal_pe_2d and the bank eviction rules (oracle/mem_prompt_oracle.py).  No GPU: the reference runs this on the
 CPU between the decoder and the memory-attention graphs, and so does this library."""
 import numpy as np
 import pytest
@@ -125,3 +125,60 @@ def test_extract_obj_ptr(b200, score, blend):
     else:
         np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
         assert not np.array_equal(got, nop)
+
+
+@pytest.mark.parametrize("H,W,d", [(72, 72, 64), (64, 64, 256), (5, 7, 16)])
+def test_sinusoidal_pe_2d(b200, H, W, d):
+    got = b200.sinusoidal_pe_2d(H, W, d)
+    ref = mpo.sinusoidal_pe_2d(H, W, d)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-6)  # libm vs numpy float32 sin / cos / pow
+    assert np.array_equal(got[0, :, : d // 2], np.repeat(got[0, :1, : d // 2], W, 0))  # y half constant along x
+
+
+def _stream(b200, cond_frames, n_frames, H=8):
+    """Feed a bank and its restatement the slots and pointers of n_frames frames; compare after each."""
+    rng = np.random.default_rng(len(cond_frames) * 100 + n_frames)
+    bank = b200.MemBank(HP, H)
+    ref = mpo.MemBank(HP["num_maskmem"], HP["max_obj_ptrs"])
+    tables = {"tpos_enc": rng.normal(0, 0.1, size=(7, 64)).astype(np.float32),
+              "tpos_proj_w": rng.normal(0, 0.05, size=(64, 256)).astype(np.float32),
+              "tpos_proj_b": rng.normal(0, 0.1, size=64).astype(np.float32)}
+    pe = mpo.sinusoidal_pe_2d(H, H, 64).reshape(-1, 64)
+    for f in range(n_frames):
+        if f:  # the prompt frame f attends to: what the bank held after frame f - 1
+            got = bank.prompt(f, **tables)
+            sel = mpo.select_memory_frames(len(ref.slots), HP["num_maskmem"])
+            want = mpo.build_mem_prompt(256, 64, 7, 16, [ref.slots[s][2] for s in sel], [pe] * len(sel),
+                                        [ref.slots[s][1] for s in sel], [p[1] for p in ref.ptrs],
+                                        [p[0] for p in ref.ptrs], f, **tables)
+            assert got[2] == want[2] and got[0].shape == want[0].shape
+            assert np.array_equal(got[0], want[0])
+            np.testing.assert_allclose(got[1], want[1], rtol=1e-5, atol=1e-5)
+        feats = rng.normal(0, 1, size=(H * H, 64)).astype(np.float32)
+        ptr = rng.normal(0, 1, size=256).astype(np.float32)
+        bank.add_slot(feats, f, f in cond_frames)
+        ref.add_slot(feats, f, f in cond_frames)
+        bank.add_ptr(ptr, f)
+        ref.add_ptr(ptr, f)
+        slots, ptrs = bank.state()
+        assert slots == [(s[0], s[1]) for s in ref.slots]
+        assert ptrs == [p[0] for p in ref.ptrs]
+    return bank
+
+
+def test_mem_bank_video_stream(b200):
+    """16 frames, box prompt on frame 0 (conditioning) and a correction on frame 9: at most 7 slots,
+    conditioning slots kept, the oldest other slot dropped first; 16 newest pointers."""
+    bank = _stream(b200, {0, 9}, 20)
+    slots, ptrs = bank.state()
+    assert len(slots) == 7 and (0, True) in slots and (9, True) in slots and slots[-1] == (19, False)
+    assert ptrs == list(range(4, 20))
+    bank.free()
+
+
+def test_mem_bank_all_conditioning(b200):
+    """Every frame prompted: no non-conditioning slot to drop, so slot 1 goes (frame 0 stays)."""
+    bank = _stream(b200, set(range(12)), 12)
+    slots, _ = bank.state()
+    assert [s[0] for s in slots] == [0] + list(range(6, 12))
+    bank.free()
