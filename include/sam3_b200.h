@@ -210,11 +210,21 @@ int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t n
 #define SAM3B200_OP_NONE              0 /* leaf: data already on the device */
 #define SAM3B200_OP_VIEW              1 /* VIEW / RESHAPE / PERMUTE / TRANSPOSE: data aliases src[0], nothing runs */
 #define SAM3B200_OP_MUL_MAT           2 /* ggml_mul_mat(src0 = weight, src1 = x) */
-#define SAM3B200_OP_ADD               3 /* only as the bias add right after a MUL_MAT (fused into it) */
+#define SAM3B200_OP_ADD               3 /* ggml_add, src1 broadcast (ggml_can_repeat); fused into the MUL_MAT before it when it is that MUL_MAT's bias */
 #define SAM3B200_OP_FLASH_ATTN_EXT    4 /* ggml_flash_attn_ext(q, k, v, mask), op_params[0..2] = scale, max_bias, softcap */
 #define SAM3B200_OP_CONV_TRANSPOSE_2D 5 /* ggml_conv_transpose_2d_p0(kernel, x), op_params[0] = stride */
 #define SAM3B200_OP_CONV_2D           6 /* ggml_conv_2d_direct(kernel, x), op_params = s0, s1, p0, p1, d0, d1 */
 #define SAM3B200_OP_GET_ROWS          7 /* ggml_get_rows(rows, I32 indices) */
+#define SAM3B200_OP_CONT              8 /* ggml_cont / ggml_cpy / ggml_cont_Nd: element i of src0 -> element i of dst, each in its own order */
+#define SAM3B200_OP_MUL               9 /* ggml_mul, src1 broadcast */
+#define SAM3B200_OP_SCALE            10 /* ggml_scale, op_params[0] = s */
+#define SAM3B200_OP_UNARY            11 /* op_params[0] = SAM3B200_UNARY_* */
+#define SAM3B200_OP_NORM             12 /* ggml_norm over ne0 (double sums), op_params[0] = eps */
+
+#define SAM3B200_UNARY_RELU     1
+#define SAM3B200_UNARY_SIGMOID  2
+#define SAM3B200_UNARY_GELU_ERF 3 /* ggml_gelu_erf */
+#define SAM3B200_UNARY_GELU     4 /* ggml_gelu as the CPU backend evaluates it (fp16 table of the tanh form) */
 
 #define SAM3B200_TENSOR_FLAG_OUTPUT 2 /* GGML_TENSOR_FLAG_OUTPUT: the caller reads this node */
 
@@ -239,12 +249,14 @@ int sam3b200_supports_op(const sam3b200_tensor *node);
 /* ggml_backend graph_compute: run nodes[0..n_nodes) in order on the backend
  * stream and wait for them, returning the ggml_status.  Every node is checked
  * first (sam3b200_supports_op, then the graph rules: a MUL_MAT's weight is an
- * uploaded handle of matching shape; an ADD is accepted only as the bias add
- * of the MUL_MAT just before it, whose result nothing else reads and which is
- * not flagged OUTPUT -- the pair runs as one MUL_MAT with the bias fused);
- * if any node is rejected nothing is launched and the message names the
- * node.  The checks come before the backend is touched, so a NULL backend
- * reports a rejected graph's own error first. */
+ * uploaded handle of matching shape; data aligned -- 16 bytes for MUL_MAT,
+ * FLASH_ATTN_EXT, the convolutions and GET_ROWS, one element for the
+ * elementwise ops and NORM); if any node is rejected nothing is launched and
+ * the message names the node.  An ADD of a packed [N] vector right after the
+ * MUL_MAT it reads, when nothing else reads that MUL_MAT and it is not
+ * flagged OUTPUT, runs inside the MUL_MAT as its bias (same result bits as
+ * the unfused pair).  The checks come before the backend is touched, so a
+ * NULL backend reports a rejected graph's own error first. */
 int sam3b200_graph_compute(sam3b200_backend *be, sam3b200_tensor *const *nodes, int n_nodes);
 
 /* ---- SAM2 Hiera image encoder (config 1: Hiera trunk + FPN neck) ----------

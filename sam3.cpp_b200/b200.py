@@ -20,8 +20,9 @@ STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS, STATUS_ABORTED = -2, -1, 0, 
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
 MMQ_AUTO, MMQ_TC, MMQ_SIMT = 0, 1, 2
 TYPE_I32 = 26
-(OP_NONE, OP_VIEW, OP_MUL_MAT, OP_ADD, OP_FLASH_ATTN_EXT, OP_CONV_TRANSPOSE_2D, OP_CONV_2D,
- OP_GET_ROWS) = range(8)
+(OP_NONE, OP_VIEW, OP_MUL_MAT, OP_ADD, OP_FLASH_ATTN_EXT, OP_CONV_TRANSPOSE_2D, OP_CONV_2D, OP_GET_ROWS,
+ OP_CONT, OP_MUL, OP_SCALE, OP_UNARY, OP_NORM) = range(13)
+UNARY_RELU, UNARY_SIGMOID, UNARY_GELU_ERF, UNARY_GELU = 1, 2, 3, 4
 TENSOR_FLAG_OUTPUT = 2
 
 _lib = None

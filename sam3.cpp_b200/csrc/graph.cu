@@ -12,7 +12,10 @@
 // untouched; each node then runs through the same entry point a direct caller
 // uses, so results are those of the op-level entries.
 #include "../../include/sam3_b200.h"
+#include "act.cuh"
 #include "backend_impl.h"
+
+#include <cuda_fp16.h>
 
 #include <cstdarg>
 #include <cstddef>
@@ -21,6 +24,7 @@
 #include <cstring>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 static_assert(sizeof(sam3b200_tensor) == 192, "sam3b200_tensor layout is part of the C ABI");
 static_assert(offsetof(sam3b200_tensor, src) == 144, "sam3b200_tensor layout is part of the C ABI");
@@ -110,6 +114,112 @@ __attribute__((format(printf, 3, 4))) bool reject(char *why, size_t cap, const c
     return false;
 }
 
+// Elementwise ops over ggml strides: one thread per result element (grid-stride), the result's
+// coordinates read back into each source's strides (src1 broadcast by coordinate modulo its ne,
+// ggml_can_repeat).  CONT pairs element i of the source with element i of the result, each in its own
+// ggml order (ggml_cpy / ggml_cont_Nd may reshape).  Memory-bound scalar code; the model-level runners
+// fuse these ops into their neighbours instead.
+struct Shape4 {
+    int64_t ne[4];
+    int64_t nb[4];  // bytes
+};
+
+Shape4 shape_of(const T *t) {
+    Shape4 s;
+    for (int d = 0; d < 4; ++d) {
+        s.ne[d] = t->ne[d];
+        s.nb[d] = static_cast<int64_t>(t->nb[d]);
+    }
+    return s;
+}
+
+__device__ __forceinline__ int64_t offset_of(int64_t i, const Shape4 &s) {
+    int64_t off = 0;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        off += (i % s.ne[d]) * s.nb[d];
+        i /= s.ne[d];
+    }
+    return off;
+}
+
+__global__ void eltwise_kernel(int op, int unary, float scale, int f16, const char *__restrict__ a, Shape4 sa,
+                               const char *__restrict__ b, Shape4 sb, char *__restrict__ d, Shape4 sd,
+                               int64_t total) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        int64_t c[4], t = i, od = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            c[k] = t % sd.ne[k];
+            t /= sd.ne[k];
+            od += c[k] * sd.nb[k];
+        }
+        if (op == SAM3B200_OP_CONT) {
+            const int64_t oa = offset_of(i, sa);
+            if (f16) *reinterpret_cast<__half *>(d + od) = *reinterpret_cast<const __half *>(a + oa);
+            else *reinterpret_cast<float *>(d + od) = *reinterpret_cast<const float *>(a + oa);
+            continue;
+        }
+        const float x = *reinterpret_cast<const float *>(a + c[0] * sa.nb[0] + c[1] * sa.nb[1] + c[2] * sa.nb[2] +
+                                                         c[3] * sa.nb[3]);
+        float y = x;
+        if (op == SAM3B200_OP_ADD || op == SAM3B200_OP_MUL) {
+            int64_t ob = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) ob += (c[k] % sb.ne[k]) * sb.nb[k];
+            const float v = *reinterpret_cast<const float *>(b + ob);
+            y = op == SAM3B200_OP_ADD ? __fadd_rn(x, v) : __fmul_rn(x, v);
+        } else if (op == SAM3B200_OP_SCALE) {
+            y = __fmul_rn(x, scale);
+        } else if (op == SAM3B200_OP_UNARY) {
+            switch (unary) {
+                case SAM3B200_UNARY_RELU: y = x > 0.0f ? x : 0.0f; break;
+                case SAM3B200_UNARY_SIGMOID: y = 1.0f / (1.0f + expf(-x)); break;
+                case SAM3B200_UNARY_GELU_ERF: y = gelu_erf_f(x); break;
+                default: y = gelu_tanh_f16(x); break;
+            }
+        }
+        *reinterpret_cast<float *>(d + od) = y;
+    }
+}
+
+// ggml_norm: per row of ne0 floats, mean and variance as double sums, y = (x - mean) / sqrt(var + eps).
+// One warp per row.
+__global__ void norm_rows_kernel(const char *__restrict__ a, Shape4 sa, char *__restrict__ d, Shape4 sd,
+                                 int64_t rows, float eps) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int64_t r1 = row % sa.ne[1], r2 = (row / sa.ne[1]) % sa.ne[2], r3 = row / (sa.ne[1] * sa.ne[2]);
+    const char *ar = a + r1 * sa.nb[1] + r2 * sa.nb[2] + r3 * sa.nb[3];
+    char *dr = d + r1 * sd.nb[1] + r2 * sd.nb[2] + r3 * sd.nb[3];
+    const int64_t n = sa.ne[0];
+    auto x = [&](int64_t i) { return *reinterpret_cast<const float *>(ar + i * sa.nb[0]); };
+    double s = 0.0;
+    for (int64_t i = lane; i < n; i += 32) s += static_cast<double>(x(i));
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = static_cast<float>(s / static_cast<double>(n));
+    double s2 = 0.0;
+    for (int64_t i = lane; i < n; i += 32) {
+        const float v = __fsub_rn(x(i), mean);
+        s2 += static_cast<double>(__fmul_rn(v, v));
+    }
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float var = static_cast<float>(s2 / static_cast<double>(n));
+    const float sc = 1.0f / sqrtf(__fadd_rn(var, eps));
+    for (int64_t i = lane; i < n; i += 32)
+        *reinterpret_cast<float *>(dr + i * sd.nb[0]) = __fmul_rn(__fsub_rn(x(i), mean), sc);
+}
+
+bool strides_ok(const T *t, size_t elt) {
+    for (int d = 0; d < 4; ++d)
+        if (t->nb[d] % elt != 0 || t->nb[d] == 0) return false;
+    return true;
+}
+
+int64_t nelements(const T *t) { return t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3]; }
+
 // The node-local rules of each op; on failure `why` says which.
 bool check_node(const T *n, char *why, size_t cap) {
     if (!n) return reject(why, cap, "null node");
@@ -137,15 +247,38 @@ bool check_node(const T *n, char *why, size_t cap) {
             if (rows_of(b) > (1 << 24)) return reject(why, cap, "MUL_MAT with more than 2^24 rows");
             return true;
         }
-        case SAM3B200_OP_ADD: {
-            if (!a || !b || a->op != SAM3B200_OP_MUL_MAT)
-                return reject(why, cap, "ADD runs here only as the bias add of a MUL_MAT (src0 = the MUL_MAT)");
-            if (b->type != SAM3B200_TYPE_F32 || b->ne[0] != a->ne[0] || b->ne[1] != 1 || b->ne[2] != 1 ||
-                b->ne[3] != 1 || b->nb[0] != 4)
-                return reject(why, cap, "ADD bias must be a packed f32 vector of the MUL_MAT's %lld outputs",
-                              (long long)a->ne[0]);
-            if (n->type != SAM3B200_TYPE_F32 || std::memcmp(n->ne, a->ne, sizeof n->ne) != 0 || !flat_row_stride(n))
-                return reject(why, cap, "ADD result must be f32 of the MUL_MAT's shape with rows in one strided run");
+        case SAM3B200_OP_ADD:
+        case SAM3B200_OP_MUL: {
+            const char *name = n->op == SAM3B200_OP_ADD ? "ADD" : "MUL";
+            if (!a || !b) return reject(why, cap, "%s needs two sources", name);
+            if (a->type != SAM3B200_TYPE_F32 || b->type != SAM3B200_TYPE_F32 || n->type != SAM3B200_TYPE_F32 ||
+                !shape_ok(a) || !shape_ok(b) || std::memcmp(n->ne, a->ne, sizeof n->ne) != 0)
+                return reject(why, cap, "%s: f32 operands, result of src0's shape", name);
+            for (int d = 0; d < 4; ++d)
+                if (a->ne[d] % b->ne[d] != 0) return reject(why, cap, "%s: src1 does not repeat into src0", name);
+            if (!strides_ok(a, 4) || !strides_ok(b, 4) || !strides_ok(n, 4))
+                return reject(why, cap, "%s: strides must be whole floats", name);
+            return true;
+        }
+        case SAM3B200_OP_SCALE:
+        case SAM3B200_OP_UNARY:
+        case SAM3B200_OP_NORM: {
+            if (!a || a->type != SAM3B200_TYPE_F32 || n->type != SAM3B200_TYPE_F32 || !shape_ok(a) ||
+                std::memcmp(n->ne, a->ne, sizeof n->ne) != 0 || !strides_ok(a, 4) || !strides_ok(n, 4))
+                return reject(why, cap, "SCALE / UNARY / NORM: f32 source and result of the same shape");
+            if (n->op == SAM3B200_OP_UNARY && (n->op_params[0] < SAM3B200_UNARY_RELU ||
+                                               n->op_params[0] > SAM3B200_UNARY_GELU))
+                return reject(why, cap, "UNARY kind %d (RELU 1, SIGMOID 2, GELU_ERF 3, GELU 4)", n->op_params[0]);
+            if (n->op == SAM3B200_OP_NORM && !(param_f32(n, 0) >= 0.0f))
+                return reject(why, cap, "NORM eps must be >= 0");
+            return true;
+        }
+        case SAM3B200_OP_CONT: {
+            if (!a || !shape_ok(a) || !shape_ok(n) || a->type != n->type ||
+                (a->type != SAM3B200_TYPE_F32 && a->type != SAM3B200_TYPE_F16) || nelements(a) != nelements(n))
+                return reject(why, cap, "CONT: F32 or F16 source and result of one type and element count");
+            const size_t elt = a->type == SAM3B200_TYPE_F32 ? 4 : 2;
+            if (!strides_ok(a, elt) || !strides_ok(n, elt)) return reject(why, cap, "CONT: strides must be whole elements");
             return true;
         }
         case SAM3B200_OP_FLASH_ATTN_EXT: {
@@ -233,7 +366,6 @@ bool check_node(const T *n, char *why, size_t cap) {
 
 bool computes(const T *n) { return n->op != SAM3B200_OP_NONE && n->op != SAM3B200_OP_VIEW && !is_empty(n); }
 
-bool aligned16(const void *p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 }  // namespace b200
@@ -246,13 +378,69 @@ extern "C" int sam3b200_supports_op(const sam3b200_tensor *node) {
     return check_node(node, why, sizeof why) ? 1 : 0;
 }
 
+namespace b200 {
+namespace {
+
+// The ADD at nodes[i] is the bias of the MUL_MAT right before it and runs inside it: it reads that
+// MUL_MAT, nothing else reads the MUL_MAT, which is not an output, and the bias is a packed [N] vector.
+bool fuses_into_mul_mat(sam3b200_tensor *const *nodes, int i, std::unordered_map<const T *, int> &uses) {
+    const T *n = nodes[i];
+    if (n->op != SAM3B200_OP_ADD || i == 0) return false;
+    const T *mm = n->src[0], *bias = n->src[1];
+    return nodes[i - 1] == mm && mm->op == SAM3B200_OP_MUL_MAT && !(mm->flags & SAM3B200_TENSOR_FLAG_OUTPUT) &&
+           uses[mm] == 1 && bias->ne[0] == mm->ne[0] && bias->ne[1] == 1 && bias->ne[2] == 1 && bias->ne[3] == 1 &&
+           bias->nb[0] == 4 && flat_row_stride(n) != 0;
+}
+
+// Alignment the op's kernels need of every data pointer: the tensor-core paths stage through 16-byte
+// loads and stores, the elementwise ops read and write single elements.
+uintptr_t data_align(const T *n) {
+    switch (n->op) {
+        case SAM3B200_OP_ADD: case SAM3B200_OP_MUL: case SAM3B200_OP_SCALE: case SAM3B200_OP_UNARY:
+        case SAM3B200_OP_NORM: return 4;
+        case SAM3B200_OP_CONT: return n->type == SAM3B200_TYPE_F16 ? 2 : 4;
+        default: return 16;
+    }
+}
+
+bool aligned_to(const void *p, uintptr_t a) { return p && (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+cudaError_t launch_eltwise(b200::Backend *bk, const T *n) {
+    const T *a = n->src[0], *b = n->src[1];
+    const int64_t total = nelements(n);
+    const int threads = 256;
+    const int64_t want = (total + threads - 1) / threads, cap_blocks = static_cast<int64_t>(bk->num_sms) * 16;
+    const unsigned blocks = static_cast<unsigned>(want < cap_blocks ? want : cap_blocks);
+    const Shape4 sb = b ? shape_of(b) : shape_of(a);
+    eltwise_kernel<<<blocks, threads, 0, bk->stream>>>(
+        n->op, n->op_params[0], param_f32(n, 0), n->type == SAM3B200_TYPE_F16 ? 1 : 0,
+        static_cast<const char *>(a->data), shape_of(a), b ? static_cast<const char *>(b->data) : nullptr, sb,
+        static_cast<char *>(n->data), shape_of(n), total);
+    bk->count(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm(b200::Backend *bk, const T *n) {
+    const T *a = n->src[0];
+    const int64_t rows = a->ne[1] * a->ne[2] * a->ne[3];
+    const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);  // 8 warps, one row each
+    norm_rows_kernel<<<blocks, 256, 0, bk->stream>>>(static_cast<const char *>(a->data), shape_of(a),
+                                                     static_cast<char *>(n->data), shape_of(n), rows,
+                                                     param_f32(n, 0));
+    bk->count(1);
+    return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace b200
+
 extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *const *nodes, int n_nodes) {
     if (n_nodes < 0 || (n_nodes > 0 && !nodes)) {
         set_error("graph_compute: null node list");
         return SAM3B200_STATUS_FAILED;
     }
     char why[256];
-    // pass 1: every node on its own, then the fusion rule of ADD
+    // pass 1: every node on its own
     std::unordered_map<const T *, int> uses;
     for (int i = 0; i < n_nodes; ++i) {
         const T *n = nodes[i];
@@ -270,32 +458,27 @@ extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *cons
             set_error("graph_compute: node %d rejected: %s", i, why);
             return SAM3B200_STATUS_FAILED;
         }
-        if (n->op == SAM3B200_OP_ADD) {
-            const T *mm = n->src[0];
-            if (i == 0 || nodes[i - 1] != mm || (mm->flags & SAM3B200_TENSOR_FLAG_OUTPUT) || uses[mm] != 1) {
-                set_error("graph_compute: node %d rejected: ADD runs only fused into the MUL_MAT just before it, "
-                          "whose result nothing else reads and which is not an output",
-                          i);
-                return SAM3B200_STATUS_FAILED;
-            }
-        }
     }
+    std::vector<char> fused(n_nodes + 1, 0);  // fused[i]: node i is an ADD running inside node i - 1
+    for (int i = 0; i < n_nodes; ++i)
+        if (!is_empty(nodes[i]) && fuses_into_mul_mat(nodes, i, uses)) fused[i] = 1;
     // pass 2: device data of every node that computes, and the uploaded weights
-    // (a MUL_MAT fused with its ADD writes the ADD's result, never its own)
     for (int i = 0; i < n_nodes; ++i) {
         const T *n = nodes[i];
         if (!computes(n)) continue;
-        const bool fused = n->op == SAM3B200_OP_MUL_MAT && i + 1 < n_nodes && nodes[i + 1]->op == SAM3B200_OP_ADD &&
-                           nodes[i + 1]->src[0] == n;
-        if (!fused && !aligned16(n->data)) {
-            set_error("graph_compute: node %d rejected: result data is null or not 16-byte aligned", i);
+        const uintptr_t al = data_align(n);
+        const bool writes_own = !(n->op == SAM3B200_OP_MUL_MAT && fused[i + 1]);
+        if (writes_own && !aligned_to(n->data, al)) {
+            set_error("graph_compute: node %d rejected: result data is null or not %d-byte aligned", i,
+                      static_cast<int>(al));
             return SAM3B200_STATUS_FAILED;
         }
         for (int s = 0; s < 4; ++s) {
             const T *src = n->src[s];
-            if (!src || (n->op == SAM3B200_OP_MUL_MAT && s == 0) || (n->op == SAM3B200_OP_ADD && s == 0)) continue;
-            if (!aligned16(src->data)) {
-                set_error("graph_compute: node %d rejected: src%d data is null or not 16-byte aligned", i, s);
+            if (!src || (n->op == SAM3B200_OP_MUL_MAT && s == 0) || (fused[i] && s == 0)) continue;
+            if (!aligned_to(src->data, fused[i] ? 16 : al)) {
+                set_error("graph_compute: node %d rejected: src%d data is null or not %d-byte aligned", i, s,
+                          static_cast<int>(fused[i] ? 16 : al));
                 return SAM3B200_STATUS_FAILED;
             }
         }
@@ -321,18 +504,18 @@ extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *cons
         set_error("graph_compute: null backend");
         return SAM3B200_STATUS_FAILED;
     }
+    auto *bk = reinterpret_cast<Backend *>(h);
+    cudaSetDevice(bk->device);
     // run the nodes in order
     for (int i = 0; i < n_nodes; ++i) {
         const T *n = nodes[i];
-        if (!computes(n)) continue;
+        if (!computes(n) || fused[i]) continue;
         const T *a = n->src[0], *b = n->src[1];
         int st = SAM3B200_STATUS_SUCCESS;
         switch (n->op) {
             case SAM3B200_OP_MUL_MAT: {
-                // the bias add right after it runs inside it, writing the ADD's result
-                const T *add = i + 1 < n_nodes && nodes[i + 1]->op == SAM3B200_OP_ADD && nodes[i + 1]->src[0] == n
-                                   ? nodes[i + 1]
-                                   : nullptr;
+                // a bias add right after it runs inside it, writing the ADD's result
+                const T *add = fused[i + 1] ? nodes[i + 1] : nullptr;
                 const T *out = add ? add : n;
                 st = sam3b200_mul_mat(be, static_cast<const sam3b200_weight *>(a->extra),
                                       static_cast<const float *>(b->data), static_cast<int64_t>(flat_row_stride(b) / 4),
@@ -340,7 +523,16 @@ extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *cons
                                       static_cast<float *>(out->data), static_cast<int64_t>(flat_row_stride(out) / 4));
                 break;
             }
-            case SAM3B200_OP_ADD: break;  // ran with its MUL_MAT
+            case SAM3B200_OP_ADD:
+            case SAM3B200_OP_MUL:
+            case SAM3B200_OP_SCALE:
+            case SAM3B200_OP_UNARY:
+            case SAM3B200_OP_CONT:
+                if (!cuda_ok(launch_eltwise(bk, n), "graph elementwise")) st = SAM3B200_STATUS_FAILED;
+                break;
+            case SAM3B200_OP_NORM:
+                if (!cuda_ok(launch_norm(bk, n), "graph norm")) st = SAM3B200_STATUS_FAILED;
+                break;
             case SAM3B200_OP_FLASH_ATTN_EXT: {
                 const T *v = n->src[2], *m = n->src[3];
                 const int64_t qn[3] = {static_cast<int64_t>(a->nb[1] / 4), static_cast<int64_t>(a->nb[2] / 4),

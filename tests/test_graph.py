@@ -80,6 +80,21 @@ def test_supports_the_forms_sam3_builds(g):
     assert g.supports_op(g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A))
     assert g.supports_op(g.graph_tensor(F32, [96, 40], op=g.OP_VIEW, src=(mm,), data=A))
     assert g.supports_op(g.graph_tensor(F32, [96, 40]))   # leaf
+    # elementwise ops of the ViT / decoder graphs: residual add, broadcast multiply (LN affine), scale,
+    # activations, ggml_norm, and the CONT that materialises a permuted view (sam3.cpp:3747-3767)
+    x = g.graph_tensor(F32, [64, 24, 24, 9], data=A)
+    row = g.graph_tensor(F32, [64], data=A)
+    assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_ADD, src=(x, x), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_MUL, src=(x, row), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_SCALE, src=(x,), op_params=(g.f32_bits(0.125),),
+                                        data=A))
+    for kind in (g.UNARY_RELU, g.UNARY_SIGMOID, g.UNARY_GELU_ERF, g.UNARY_GELU):
+        assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_UNARY, src=(x,), op_params=(kind,), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_NORM, src=(x,), op_params=(g.f32_bits(1e-6),),
+                                        data=A))
+    perm = g.graph_tensor(F32, [64, 9, 24, 24], nb=[4, 64 * 24 * 24 * 4, 64 * 4, 64 * 24 * 4], data=A)
+    assert g.supports_op(g.graph_tensor(F32, [64, 9, 24, 24], op=g.OP_CONT, src=(perm,), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [64 * 9, 576], op=g.OP_CONT, src=(perm,), data=A))  # ggml_cont_2d
 
 
 def _not_packed_rows(g):
@@ -110,8 +125,20 @@ REJECTED = {
         g.graph_tensor(Q8_0, [256, 96]), g.graph_tensor(F32, [256, 40], data=A)), data=A),
     "3-D weight": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_MUL_MAT, src=(
         g.graph_tensor(Q8_0, [256, 96, 2]), g.graph_tensor(F32, [256, 40], data=A)), data=A),
-    "ADD of two activations": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(
-        g.graph_tensor(F32, [96, 40], data=A), g.graph_tensor(F32, [96], data=A)), data=A),
+    "ADD of a src1 that does not repeat": lambda g: g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(
+        g.graph_tensor(F32, [96, 40], data=A), g.graph_tensor(F32, [96, 3], data=A)), data=A),
+    "MUL f16": lambda g: g.graph_tensor(F32, [8, 4], op=g.OP_MUL, src=(
+        g.graph_tensor(F16, [8, 4], data=A), g.graph_tensor(F32, [8], data=A)), data=A),
+    "SCALE result shape": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_SCALE, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), op_params=(g.f32_bits(0.5),), data=A),
+    "UNARY kind 9": lambda g: g.graph_tensor(F32, [8, 4], op=g.OP_UNARY, src=(g.graph_tensor(F32, [8, 4], data=A),),
+                                             op_params=(9,), data=A),
+    "NORM negative eps": lambda g: g.graph_tensor(F32, [8, 4], op=g.OP_NORM, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), op_params=(g.f32_bits(-1.0),), data=A),
+    "CONT type change": lambda g: g.graph_tensor(F16, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(F32, [8, 4], data=A),),
+                                                 data=A),
+    "CONT element count": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_CONT, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), data=A),
     "ADD bias of the wrong length": _bias_of_wrong_length,
     "attention head dim 80": lambda g: _fa(g, D=80),
     "attention max_bias": lambda g: _fa(g, params=(g.f32_bits(0.125), g.f32_bits(8.0), 0)),
@@ -158,31 +185,42 @@ def test_valid_graph_passes_every_check_before_the_backend(g):
     assert "null backend" in g.last_error()
 
 
-def test_add_must_directly_follow_its_mul_mat(g):
-    mm = _mm(g, data=A)
+def test_unfused_adds_pass_the_checks(g):
+    """An ADD away from its MUL_MAT, over an OUTPUT MUL_MAT or over one read twice runs as a plain ADD:
+    the graph passes every check (it stops at the missing backend).  The MUL_MAT then needs its own
+    aligned result buffer."""
     bias = g.graph_tensor(F32, [96], data=A)
-    add = g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A)
-    assert g.graph_compute_status(None, [mm, _conv(g), add]) == g.STATUS_FAILED
-    assert "node 2 rejected: ADD runs only fused" in g.last_error(), g.last_error()
-
-
-def test_add_is_not_fused_over_an_output_or_shared_mul_mat(g):
     mm = _mm(g, data=A)
+    add = g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A)
+    graphs = [[mm, _conv(g), add], [mm, add, g.graph_tensor(F32, [96, 40], op=g.OP_VIEW, src=(mm,), data=A)]]
+    for nodes in graphs:
+        assert g.graph_compute_status(None, nodes) == g.STATUS_FAILED
+        assert "no handle" in g.last_error(), g.last_error()  # reached pass 2: the MUL_MAT's weight handle
     mm.flags = g.TENSOR_FLAG_OUTPUT
-    bias = g.graph_tensor(F32, [96], data=A)
-    add = g.graph_tensor(F32, [96, 40], op=g.OP_ADD, src=(mm, bias), data=A)
+    mm.data = None
     assert g.graph_compute_status(None, [mm, add]) == g.STATUS_FAILED
-    assert "node 1 rejected" in g.last_error()
+    assert "node 0 rejected: result data is null" in g.last_error(), g.last_error()
     mm.flags = 0
-    view = g.graph_tensor(F32, [96, 40], op=g.OP_VIEW, src=(mm,), data=A)  # a second reader of the MUL_MAT
-    assert g.graph_compute_status(None, [mm, add, view]) == g.STATUS_FAILED
-    assert "node 1 rejected" in g.last_error()
+    assert g.graph_compute_status(None, [mm, add]) == g.STATUS_FAILED  # fused: the MUL_MAT writes the ADD's data
+    assert "no handle" in g.last_error(), g.last_error()
 
 
 def test_mul_mat_needs_an_uploaded_weight_handle(g):
     mm = _mm(g, data=A)
     assert g.graph_compute_status(None, [mm]) == g.STATUS_FAILED
     assert "node 0 rejected: MUL_MAT weight has no handle" in g.last_error(), g.last_error()
+
+
+def test_elementwise_data_needs_element_alignment_only(g):
+    x = g.graph_tensor(F32, [8, 4], data=A + 4)
+    ok = g.graph_tensor(F32, [8, 4], op=g.OP_UNARY, src=(x,), op_params=(g.UNARY_RELU,), data=A + 36)
+    assert g.graph_compute_status(None, [ok]) == g.STATUS_FAILED and "null backend" in g.last_error()
+    h = g.graph_tensor(F16, [8, 4], data=A + 2)
+    assert g.graph_compute_status(None, [g.graph_tensor(F16, [32], op=g.OP_CONT, src=(h,), data=A + 6)]) == \
+        g.STATUS_FAILED and "null backend" in g.last_error()
+    bad = g.graph_tensor(F32, [8, 4], op=g.OP_UNARY, src=(x,), op_params=(g.UNARY_RELU,), data=A + 2)
+    assert g.graph_compute_status(None, [bad]) == g.STATUS_FAILED
+    assert "not 4-byte aligned" in g.last_error()
 
 
 def test_unaligned_or_missing_data_is_rejected(g):

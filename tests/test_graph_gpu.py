@@ -115,27 +115,118 @@ def test_conv_chain_graph(b200, backend):
     assert np.array_equal(_bits(got), _bits(ct2.get((oc2, 2 * ih, 2 * iw), np.float32)))
 
 
-def test_rejected_graph_launches_nothing(b200, backend):
-    """An ADD over a MUL_MAT whose result is also an output cannot be fused: the graph is refused before
-    any launch and the backend stays usable."""
+def test_rejected_graph_launches_nothing_and_unfused_bias_matches_fused(b200, backend):
+    """A graph with one node the backend does not run is refused before any launch; an ADD over a
+    MUL_MAT that is also an output runs unfused (MUL_MAT, then the elementwise ADD) and gives the bits
+    of the fused pair."""
     rng = np.random.default_rng(14)
     K, N, n = 128, 64, 16
     W = backend.weight(Q8_0, oracle_free_q8(rng, N, K), K, N)
-    x, b, y1, y2 = backend.alloc(n * K * 4), backend.alloc(N * 4), backend.alloc(n * N * 4), backend.alloc(n * N * 4)
-    t_mm = b200.graph_tensor(F32, [N, n], op=b200.OP_MUL_MAT, data=y1.ptr, flags=b200.TENSOR_FLAG_OUTPUT, src=(
-        b200.graph_tensor(Q8_0, [K, N], extra=W.h), b200.graph_tensor(F32, [K, n], data=x.ptr)))
-    t_add = b200.graph_tensor(F32, [N, n], op=b200.OP_ADD, src=(t_mm, b200.graph_tensor(F32, [N], data=b.ptr)),
-                              data=y2.ptr)
-    before = backend.launches
-    with pytest.raises(b200.B200Error, match="node 1 rejected"):
-        backend.graph_compute([t_mm, t_add])
-    assert backend.launches == before
-    t_mm.flags = 0  # the same graph without the OUTPUT flag runs
+    x, b = backend.alloc(n * K * 4), backend.alloc(N * 4)
+    y1, y2, y3 = (backend.alloc(n * N * 4) for _ in range(3))
     x.set(rng.normal(0, 1, size=(n, K)).astype(np.float32))
-    b.set(np.zeros(N, np.float32))
-    backend.graph_compute([t_mm, t_add])
-    assert backend.launches > before
+    b.set(rng.normal(0, 1, size=N).astype(np.float32))
+    t_x, t_b = b200.graph_tensor(F32, [K, n], data=x.ptr), b200.graph_tensor(F32, [N], data=b.ptr)
+    t_w = b200.graph_tensor(Q8_0, [K, N], extra=W.h)
+    t_mm = b200.graph_tensor(F32, [N, n], op=b200.OP_MUL_MAT, data=y1.ptr, flags=b200.TENSOR_FLAG_OUTPUT,
+                             src=(t_w, t_x))
+    t_add = b200.graph_tensor(F32, [N, n], op=b200.OP_ADD, src=(t_mm, t_b), data=y2.ptr)
+    odd = b200.graph_tensor(F32, [N, n], op=99, src=(t_add,), data=y3.ptr)
+    before = backend.launches
+    with pytest.raises(b200.B200Error, match="node 2 rejected"):
+        backend.graph_compute([t_mm, t_add, odd])
+    assert backend.launches == before
+    backend.graph_compute([t_mm, t_add])  # unfused: t_mm is an output
+    unfused = y2.get((n, N), np.float32)
+    t_mm.flags = 0
+    t_add.data = y3.ptr
+    backend.graph_compute([t_mm, t_add])  # fused into the MUL_MAT epilogue
+    assert np.array_equal(_bits(unfused), _bits(y3.get((n, N), np.float32)))
     W.free()
+
+
+def _gelu_tanh_f16(x):
+    h = x.astype(np.float16).astype(np.float64)
+    y = (0.5 * h * (1.0 + np.tanh(0.7978845608028654 * h * (1.0 + 0.044715 * h * h)))).astype(np.float16)
+    y = y.astype(np.float32)
+    return np.where(x <= -10, 0.0, np.where(x >= 10, x, y)).astype(np.float32)
+
+
+def _norm_ref(x, eps):
+    mean = (x.astype(np.float64).sum(-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    v = (x - mean).astype(np.float32)
+    var = ((v * v).astype(np.float64).sum(-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    sc = (np.float32(1.0) / np.sqrt(var + np.float32(eps))).astype(np.float32)
+    return (v * sc).astype(np.float32)
+
+
+def test_elementwise_chain_graph(b200, backend):
+    """LayerNorm-style chain in one graph: NORM -> MUL (weight row) -> ADD (bias row) -> GELU_ERF ->
+    SCALE -> ADD (residual); every node checked against numpy applied to the GPU's own input of that node."""
+    rng = np.random.default_rng(15)
+    E, T1, T2 = 96, 10, 3
+    x = rng.normal(0, 2, size=(T2, T1, E)).astype(np.float32)
+    w, bvec = rng.normal(1, 0.2, size=E).astype(np.float32), rng.normal(0, 0.2, size=E).astype(np.float32)
+    dx, dw, db = backend.upload(x), backend.upload(w), backend.upload(bvec)
+    bufs = [backend.alloc(x.nbytes) for _ in range(6)]
+    t_x = b200.graph_tensor(F32, [E, T1, T2], data=dx.ptr)
+    t_w, t_b = b200.graph_tensor(F32, [E], data=dw.ptr), b200.graph_tensor(F32, [E], data=db.ptr)
+    shape = [E, T1, T2]
+    t0 = b200.graph_tensor(F32, shape, op=b200.OP_NORM, src=(t_x,), op_params=(b200.f32_bits(1e-5),),
+                           data=bufs[0].ptr)
+    t1 = b200.graph_tensor(F32, shape, op=b200.OP_MUL, src=(t0, t_w), data=bufs[1].ptr)
+    t2 = b200.graph_tensor(F32, shape, op=b200.OP_ADD, src=(t1, t_b), data=bufs[2].ptr)
+    t3 = b200.graph_tensor(F32, shape, op=b200.OP_UNARY, src=(t2,), op_params=(b200.UNARY_GELU_ERF,),
+                           data=bufs[3].ptr)
+    t4 = b200.graph_tensor(F32, shape, op=b200.OP_SCALE, src=(t3,), op_params=(b200.f32_bits(0.5),),
+                           data=bufs[4].ptr)
+    t5 = b200.graph_tensor(F32, shape, op=b200.OP_ADD, src=(t4, t_x), data=bufs[5].ptr)
+    before = backend.launches
+    backend.graph_compute([t0, t1, t2, t3, t4, t5])
+    assert backend.launches - before == 6
+    o = [bf.get(x.shape, np.float32) for bf in bufs]
+    np.testing.assert_allclose(o[0], _norm_ref(x, 1e-5), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(_bits(o[1]), _bits(o[0] * w))
+    assert np.array_equal(_bits(o[2]), _bits(o[1] + bvec))
+    import math
+    erf = np.vectorize(math.erf)
+    ref3 = 0.5 * o[2].astype(np.float64) * (1.0 + erf(o[2].astype(np.float64) / math.sqrt(2.0)))
+    np.testing.assert_allclose(o[3], ref3, rtol=1e-6, atol=2e-6)
+    assert np.array_equal(_bits(o[4]), _bits(o[3] * np.float32(0.5)))
+    assert np.array_equal(_bits(o[5]), _bits(o[4] + x))
+
+
+def test_unary_and_cont_graph(b200, backend):
+    """RELU, SIGMOID, GELU (the CPU backend's fp16 tanh table); CONT of a permuted view (the head split of
+    sam3.cpp:3747-3767), a CONT that reshapes (ggml_cont_2d), and an F16 CONT."""
+    rng = np.random.default_rng(16)
+    x = np.concatenate([rng.normal(0, 3, size=4000), [-12.0, -10.0, 0.0, 10.0, 12.5]]).astype(np.float32)
+    dx = backend.upload(x)
+    outs = [backend.alloc(x.nbytes) for _ in range(3)]
+    t_x = b200.graph_tensor(F32, [x.size], data=dx.ptr)
+    nodes = [b200.graph_tensor(F32, [x.size], op=b200.OP_UNARY, src=(t_x,), op_params=(k,), data=o.ptr)
+             for k, o in zip((b200.UNARY_RELU, b200.UNARY_SIGMOID, b200.UNARY_GELU), outs)]
+    D, N, H, B = 16, 12, 3, 2
+    qkv = rng.normal(0, 1, size=(B, N, 3, H, D)).astype(np.float32)
+    dq = backend.upload(qkv)
+    # k as a view [D, N, H, B] (token stride 3*H*D), permuted to [D, H, N, B] and made contiguous
+    t_k = b200.graph_tensor(F32, [D, H, N, B], nb=[4, D * 4, 3 * H * D * 4, N * 3 * H * D * 4], data=dq.ptr + H * D * 4)
+    c1, c2 = backend.alloc(B * N * H * D * 4), backend.alloc(B * N * H * D * 4)
+    nodes.append(b200.graph_tensor(F32, [D, H, N, B], op=b200.OP_CONT, src=(t_k,), data=c1.ptr))
+    nodes.append(b200.graph_tensor(F32, [D * H, N * B], op=b200.OP_CONT, src=(t_k,), data=c2.ptr))
+    h = rng.normal(0, 1, size=(7, 33)).astype(np.float16)
+    dh, ch = backend.upload(h), backend.alloc(h.nbytes)
+    t_h = b200.graph_tensor(F16, [7, 33], nb=[33 * 2, 2, 7 * 33 * 2, 7 * 33 * 2], data=dh.ptr)  # transposed view
+    nodes.append(b200.graph_tensor(F16, [7, 33], op=b200.OP_CONT, src=(t_h,), data=ch.ptr))
+    backend.graph_compute(nodes)
+    relu, sig, gelu = (o.get(x.shape, np.float32) for o in outs)
+    assert np.array_equal(relu, np.where(x > 0, x, 0).astype(np.float32))
+    np.testing.assert_allclose(sig, 1.0 / (1.0 + np.exp(-x.astype(np.float64))), rtol=0, atol=1e-6)
+    np.testing.assert_allclose(gelu, _gelu_tanh_f16(x), rtol=2e-3, atol=1e-3)
+    kk = qkv[:, :, 1]  # [B, N, H, D]: memory order of [D, H, N, B]
+    assert np.array_equal(c1.get(kk.shape, np.float32), kk)
+    assert np.array_equal(c2.get(kk.shape, np.float32), kk)
+    assert np.array_equal(ch.get((33, 7), np.float16), h.T)
 
 
 def oracle_free_q8(rng, N, K):
