@@ -212,6 +212,38 @@ __global__ void norm_rows_kernel(const char *__restrict__ a, Shape4 sa, char *__
         *reinterpret_cast<float *>(dr + i * sd.nb[0]) = __fmul_rn(__fsub_rn(x(i), mean), sc);
 }
 
+// ggml_soft_max_ext with max_bias 0: per row of ne0, v = x * scale (+ mask row, F16 or F32, broadcast
+// over dims 2 and 3), y = exp(v - max v) / sum (the sum in double, one reciprocal).  One warp per row.
+__global__ void soft_max_rows_kernel(const char *__restrict__ a, Shape4 sa, const char *__restrict__ m, Shape4 sm,
+                                     int m_f16, char *__restrict__ d, Shape4 sd, int64_t rows, float scale) {
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int64_t r1 = row % sa.ne[1], r2 = (row / sa.ne[1]) % sa.ne[2], r3 = row / (sa.ne[1] * sa.ne[2]);
+    const char *ar = a + r1 * sa.nb[1] + r2 * sa.nb[2] + r3 * sa.nb[3];
+    char *dr = d + r1 * sd.nb[1] + r2 * sd.nb[2] + r3 * sd.nb[3];
+    const char *mr = m ? m + r1 * sm.nb[1] + (r2 % sm.ne[2]) * sm.nb[2] + (r3 % sm.ne[3]) * sm.nb[3] : nullptr;
+    const int64_t n = sa.ne[0];
+    auto v = [&](int64_t i) {
+        float t = __fmul_rn(*reinterpret_cast<const float *>(ar + i * sa.nb[0]), scale);
+        if (mr) {
+            const char *p = mr + i * sm.nb[0];
+            t = __fadd_rn(t, m_f16 ? __half2float(*reinterpret_cast<const __half *>(p))
+                                   : *reinterpret_cast<const float *>(p));
+        }
+        return t;
+    };
+    float mx = -INFINITY;
+    for (int64_t i = lane; i < n; i += 32) mx = fmaxf(mx, v(i));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    double s = 0.0;
+    for (int64_t i = lane; i < n; i += 32) s += static_cast<double>(expf(__fsub_rn(v(i), mx)));
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = static_cast<float>(1.0 / s);
+    for (int64_t i = lane; i < n; i += 32)
+        *reinterpret_cast<float *>(dr + i * sd.nb[0]) = __fmul_rn(expf(__fsub_rn(v(i), mx)), inv);
+}
+
 bool strides_ok(const T *t, size_t elt) {
     for (int d = 0; d < 4; ++d)
         if (t->nb[d] % elt != 0 || t->nb[d] == 0) return false;
@@ -271,6 +303,20 @@ bool check_node(const T *n, char *why, size_t cap) {
                 return reject(why, cap, "UNARY kind %d (RELU 1, SIGMOID 2, GELU_ERF 3, GELU 4)", n->op_params[0]);
             if (n->op == SAM3B200_OP_NORM && !(param_f32(n, 0) >= 0.0f))
                 return reject(why, cap, "NORM eps must be >= 0");
+            return true;
+        }
+        case SAM3B200_OP_SOFT_MAX: {
+            if (!a || a->type != SAM3B200_TYPE_F32 || n->type != SAM3B200_TYPE_F32 || !shape_ok(a) ||
+                std::memcmp(n->ne, a->ne, sizeof n->ne) != 0 || !strides_ok(a, 4) || !strides_ok(n, 4))
+                return reject(why, cap, "SOFT_MAX: f32 source and result of the same shape");
+            if (param_f32(n, 1) != 0.0f) return reject(why, cap, "SOFT_MAX with max_bias (ALiBi) is not run here");
+            if (b) {
+                const size_t elt = b->type == SAM3B200_TYPE_F16 ? 2 : 4;
+                if ((b->type != SAM3B200_TYPE_F16 && b->type != SAM3B200_TYPE_F32) || !shape_ok(b) ||
+                    b->ne[0] != a->ne[0] || b->ne[1] < a->ne[1] || a->ne[2] % b->ne[2] != 0 ||
+                    a->ne[3] % b->ne[3] != 0 || !strides_ok(b, elt))
+                    return reject(why, cap, "SOFT_MAX mask: F16 / F32 [ne0, >= ne1] repeating over dims 2, 3");
+            }
             return true;
         }
         case SAM3B200_OP_CONT: {
@@ -397,7 +443,7 @@ bool fuses_into_mul_mat(sam3b200_tensor *const *nodes, int i, std::unordered_map
 uintptr_t data_align(const T *n) {
     switch (n->op) {
         case SAM3B200_OP_ADD: case SAM3B200_OP_MUL: case SAM3B200_OP_SCALE: case SAM3B200_OP_UNARY:
-        case SAM3B200_OP_NORM: return 4;
+        case SAM3B200_OP_NORM: case SAM3B200_OP_SOFT_MAX: return 4;
         case SAM3B200_OP_CONT: return n->type == SAM3B200_TYPE_F16 ? 2 : 4;
         default: return 16;
     }
@@ -416,6 +462,18 @@ cudaError_t launch_eltwise(b200::Backend *bk, const T *n) {
         n->op, n->op_params[0], param_f32(n, 0), n->type == SAM3B200_TYPE_F16 ? 1 : 0,
         static_cast<const char *>(a->data), shape_of(a), b ? static_cast<const char *>(b->data) : nullptr, sb,
         static_cast<char *>(n->data), shape_of(n), total);
+    bk->count(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_soft_max(b200::Backend *bk, const T *n) {
+    const T *a = n->src[0], *m = n->src[1];
+    const int64_t rows = a->ne[1] * a->ne[2] * a->ne[3];
+    const unsigned blocks = static_cast<unsigned>((rows + 7) / 8);
+    soft_max_rows_kernel<<<blocks, 256, 0, bk->stream>>>(
+        static_cast<const char *>(a->data), shape_of(a), m ? static_cast<const char *>(m->data) : nullptr,
+        m ? shape_of(m) : shape_of(a), m && m->type == SAM3B200_TYPE_F16 ? 1 : 0, static_cast<char *>(n->data),
+        shape_of(n), rows, param_f32(n, 0));
     bk->count(1);
     return cudaGetLastError();
 }
@@ -532,6 +590,9 @@ extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *cons
                 break;
             case SAM3B200_OP_NORM:
                 if (!cuda_ok(launch_norm(bk, n), "graph norm")) st = SAM3B200_STATUS_FAILED;
+                break;
+            case SAM3B200_OP_SOFT_MAX:
+                if (!cuda_ok(launch_soft_max(bk, n), "graph soft_max")) st = SAM3B200_STATUS_FAILED;
                 break;
             case SAM3B200_OP_FLASH_ATTN_EXT: {
                 const T *v = n->src[2], *m = n->src[3];

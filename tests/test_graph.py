@@ -92,6 +92,10 @@ def test_supports_the_forms_sam3_builds(g):
         assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_UNARY, src=(x,), op_params=(kind,), data=A))
     assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_NORM, src=(x,), op_params=(g.f32_bits(1e-6),),
                                         data=A))
+    scores = g.graph_tensor(F32, [70, 20, 4, 2], data=A)
+    for mask in (None, g.graph_tensor(F16, [70, 32], data=A), g.graph_tensor(F32, [70, 20, 4], data=A)):
+        assert g.supports_op(g.graph_tensor(F32, [70, 20, 4, 2], op=g.OP_SOFT_MAX, src=(scores, mask),
+                                            op_params=(g.f32_bits(0.125), 0), data=A))
     perm = g.graph_tensor(F32, [64, 9, 24, 24], nb=[4, 64 * 24 * 24 * 4, 64 * 4, 64 * 24 * 4], data=A)
     assert g.supports_op(g.graph_tensor(F32, [64, 9, 24, 24], op=g.OP_CONT, src=(perm,), data=A))
     assert g.supports_op(g.graph_tensor(F32, [64 * 9, 576], op=g.OP_CONT, src=(perm,), data=A))  # ggml_cont_2d
@@ -135,6 +139,11 @@ REJECTED = {
                                              op_params=(9,), data=A),
     "NORM negative eps": lambda g: g.graph_tensor(F32, [8, 4], op=g.OP_NORM, src=(
         g.graph_tensor(F32, [8, 4], data=A),), op_params=(g.f32_bits(-1.0),), data=A),
+    "SOFT_MAX max_bias": lambda g: g.graph_tensor(F32, [70, 20, 4], op=g.OP_SOFT_MAX, src=(
+        g.graph_tensor(F32, [70, 20, 4], data=A),), op_params=(g.f32_bits(0.125), g.f32_bits(8.0)), data=A),
+    "SOFT_MAX mask rows short": lambda g: g.graph_tensor(F32, [70, 20, 4], op=g.OP_SOFT_MAX, src=(
+        g.graph_tensor(F32, [70, 20, 4], data=A), g.graph_tensor(F16, [70, 16], data=A)),
+        op_params=(g.f32_bits(0.125), 0), data=A),
     "CONT type change": lambda g: g.graph_tensor(F16, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(F32, [8, 4], data=A),),
                                                  data=A),
     "CONT element count": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_CONT, src=(

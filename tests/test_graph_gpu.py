@@ -236,3 +236,35 @@ def oracle_free_q8(rng, N, K):
     blocks[:, :, 0:2] = np.frombuffer(np.float16(1 / 64).tobytes(), np.uint8)
     blocks[:, :, 2:] = rng.integers(-127, 128, size=(N, K // 32, 32)).astype(np.int8).view(np.uint8)
     return blocks.reshape(N, -1)
+
+
+def _softmax_ref(v):
+    v = v.astype(np.float64)
+    e = np.exp(v - v.max(-1, keepdims=True))
+    return e / e.sum(-1, keepdims=True)
+
+
+def test_soft_max_graph(b200, backend):
+    """SOFT_MAX_EXT as the decoder's attention builds it: scaled scores [NKV, NQ, heads, batch] under an F16
+    mask with padded rows (shared by every head), an F32 mask per head, and no mask."""
+    rng = np.random.default_rng(17)
+    NKV, NQ, H, B = 70, 20, 4, 2
+    x = rng.normal(0, 3, size=(B, H, NQ, NKV)).astype(np.float32)
+    m16 = np.zeros((24, NKV), np.float16)
+    m16[np.triu_indices(24, 1, NKV)] = -np.inf
+    m32 = rng.normal(0, 1, size=(H, NQ, NKV)).astype(np.float32)
+    dx, dm16, dm32 = backend.upload(x), backend.upload(m16), backend.upload(m32)
+    outs = [backend.alloc(x.nbytes) for _ in range(3)]
+    t_x = b200.graph_tensor(F32, [NKV, NQ, H, B], data=dx.ptr)
+    masks = [b200.graph_tensor(F16, [NKV, 24], data=dm16.ptr), b200.graph_tensor(F32, [NKV, NQ, H], data=dm32.ptr),
+             None]
+    nodes = [b200.graph_tensor(F32, [NKV, NQ, H, B], op=b200.OP_SOFT_MAX, src=(t_x, m),
+                               op_params=(b200.f32_bits(0.125), 0), data=o.ptr) for m, o in zip(masks, outs)]
+    backend.graph_compute(nodes)
+    v = (x * np.float32(0.125)).astype(np.float32)
+    refs = [_softmax_ref((v + m16[:NQ].astype(np.float32)).astype(np.float32)),
+            _softmax_ref((v + m32[None]).astype(np.float32)), _softmax_ref(v)]
+    for o, ref in zip(outs, refs):
+        got = o.get(x.shape, np.float32)
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7)
+    assert np.all(outs[0].get(x.shape, np.float32)[:, :, 0, 1:] == 0)  # query 0 sees key 0 only
