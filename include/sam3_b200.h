@@ -221,6 +221,8 @@ int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t n
 #define SAM3B200_OP_UNARY            11 /* op_params[0] = SAM3B200_UNARY_* */
 #define SAM3B200_OP_NORM             12 /* ggml_norm over ne0 (double sums), op_params[0] = eps */
 #define SAM3B200_OP_SOFT_MAX         13 /* ggml_soft_max_ext(a, mask, scale, max_bias 0) over ne0; mask F16 / F32 or none */
+#define SAM3B200_OP_WIN_PART         14 /* ggml_win_part(a, w): op_params = npx, npy, w (sam3.cpp:3734) */
+#define SAM3B200_OP_WIN_UNPART       15 /* ggml_win_unpart(a, W, H, w): op_params[0] = w (sam3.cpp:3788) */
 
 #define SAM3B200_UNARY_RELU     1
 #define SAM3B200_UNARY_SIGMOID  2

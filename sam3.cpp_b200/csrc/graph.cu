@@ -244,6 +244,26 @@ __global__ void soft_max_rows_kernel(const char *__restrict__ a, Shape4 sa, cons
         *reinterpret_cast<float *>(dr + i * sd.nb[0]) = __fmul_rn(expf(__fsub_rn(v(i), mx)), inv);
 }
 
+// ggml_win_part / ggml_win_unpart on contiguous f32 maps: windows of w x w tokens, window k = py * npx + px,
+// zero padding right and bottom to whole windows.  part: dst [C, w, w, npx * npy] from src [C, W, H];
+// unpart: dst [C, W, H] from src [C, w, w, nw].  One thread per result element.
+__global__ void win_kernel(int unpart, const float *__restrict__ src, float *__restrict__ dst, int64_t C, int64_t W,
+                           int64_t H, int64_t w, int64_t npx, int64_t total) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = i % C;
+        if (!unpart) {
+            const int64_t i1 = (i / C) % w, i2 = (i / (C * w)) % w, k = i / (C * w * w);
+            const int64_t x = (k % npx) * w + i1, y = (k / npx) * w + i2;
+            dst[i] = (x < W && y < H) ? src[(y * W + x) * C + c] : 0.0f;
+        } else {
+            const int64_t x = (i / C) % W, y = i / (C * W);
+            const int64_t k = (y / w) * npx + x / w;
+            dst[i] = src[((k * w + y % w) * w + x % w) * C + c];
+        }
+    }
+}
+
 bool strides_ok(const T *t, size_t elt) {
     for (int d = 0; d < 4; ++d)
         if (t->nb[d] % elt != 0 || t->nb[d] == 0) return false;
@@ -317,6 +337,22 @@ bool check_node(const T *n, char *why, size_t cap) {
                     a->ne[3] % b->ne[3] != 0 || !strides_ok(b, elt))
                     return reject(why, cap, "SOFT_MAX mask: F16 / F32 [ne0, >= ne1] repeating over dims 2, 3");
             }
+            return true;
+        }
+        case SAM3B200_OP_WIN_PART:
+        case SAM3B200_OP_WIN_UNPART: {
+            const bool part = n->op == SAM3B200_OP_WIN_PART;
+            if (!a || a->type != SAM3B200_TYPE_F32 || n->type != SAM3B200_TYPE_F32 || !shape_ok(a) || !shape_ok(n) ||
+                !contiguous(a) || !contiguous(n))
+                return reject(why, cap, "WIN_PART / WIN_UNPART: contiguous f32 source and result");
+            const T *map = part ? a : n, *win = part ? n : a;
+            const int64_t w = part ? n->op_params[2] : n->op_params[0];
+            if (w <= 0 || map->ne[3] != 1 || win->ne[0] != map->ne[0] || win->ne[1] != w || win->ne[2] != w)
+                return reject(why, cap, "WIN_PART / WIN_UNPART: windows [C, w, w, n] of a map [C, W, H, 1]");
+            const int64_t npx = (map->ne[1] + w - 1) / w, npy = (map->ne[2] + w - 1) / w;
+            if (win->ne[3] != npx * npy || (part && (n->op_params[0] != npx || n->op_params[1] != npy)))
+                return reject(why, cap, "WIN_PART / WIN_UNPART: %lld x %lld windows expected", (long long)npx,
+                              (long long)npy);
             return true;
         }
         case SAM3B200_OP_CONT: {
@@ -443,7 +479,8 @@ bool fuses_into_mul_mat(sam3b200_tensor *const *nodes, int i, std::unordered_map
 uintptr_t data_align(const T *n) {
     switch (n->op) {
         case SAM3B200_OP_ADD: case SAM3B200_OP_MUL: case SAM3B200_OP_SCALE: case SAM3B200_OP_UNARY:
-        case SAM3B200_OP_NORM: case SAM3B200_OP_SOFT_MAX: return 4;
+        case SAM3B200_OP_NORM: case SAM3B200_OP_SOFT_MAX: case SAM3B200_OP_WIN_PART:
+        case SAM3B200_OP_WIN_UNPART: return 4;
         case SAM3B200_OP_CONT: return n->type == SAM3B200_TYPE_F16 ? 2 : 4;
         default: return 16;
     }
@@ -474,6 +511,19 @@ cudaError_t launch_soft_max(b200::Backend *bk, const T *n) {
         static_cast<const char *>(a->data), shape_of(a), m ? static_cast<const char *>(m->data) : nullptr,
         m ? shape_of(m) : shape_of(a), m && m->type == SAM3B200_TYPE_F16 ? 1 : 0, static_cast<char *>(n->data),
         shape_of(n), rows, param_f32(n, 0));
+    bk->count(1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_win(b200::Backend *bk, const T *n) {
+    const bool part = n->op == SAM3B200_OP_WIN_PART;
+    const T *a = n->src[0], *map = part ? a : n;
+    const int64_t w = part ? n->op_params[2] : n->op_params[0];
+    const int64_t total = nelements(n);
+    const int64_t want = (total + 255) / 256, cap_blocks = static_cast<int64_t>(bk->num_sms) * 16;
+    win_kernel<<<static_cast<unsigned>(want < cap_blocks ? want : cap_blocks), 256, 0, bk->stream>>>(
+        part ? 0 : 1, static_cast<const float *>(a->data), static_cast<float *>(n->data), map->ne[0], map->ne[1],
+        map->ne[2], w, (map->ne[1] + w - 1) / w, total);
     bk->count(1);
     return cudaGetLastError();
 }
@@ -593,6 +643,10 @@ extern "C" int sam3b200_graph_compute(sam3b200_backend *h, sam3b200_tensor *cons
                 break;
             case SAM3B200_OP_SOFT_MAX:
                 if (!cuda_ok(launch_soft_max(bk, n), "graph soft_max")) st = SAM3B200_STATUS_FAILED;
+                break;
+            case SAM3B200_OP_WIN_PART:
+            case SAM3B200_OP_WIN_UNPART:
+                if (!cuda_ok(launch_win(bk, n), "graph win_part")) st = SAM3B200_STATUS_FAILED;
                 break;
             case SAM3B200_OP_FLASH_ATTN_EXT: {
                 const T *v = n->src[2], *m = n->src[3];

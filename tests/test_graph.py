@@ -92,6 +92,12 @@ def test_supports_the_forms_sam3_builds(g):
         assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_UNARY, src=(x,), op_params=(kind,), data=A))
     assert g.supports_op(g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_NORM, src=(x,), op_params=(g.f32_bits(1e-6),),
                                         data=A))
+    vmap = g.graph_tensor(F32, [64, 72, 72], data=A)  # ViT windows of 24 (sam3.cpp:3734, 3788); Hiera pads
+    wins = g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_WIN_PART, src=(vmap,), op_params=(3, 3, 24), data=A)
+    assert g.supports_op(wins)
+    assert g.supports_op(g.graph_tensor(F32, [64, 72, 72], op=g.OP_WIN_UNPART, src=(wins,), op_params=(24,), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [96, 8, 8, 4], op=g.OP_WIN_PART, src=(
+        g.graph_tensor(F32, [96, 14, 10], data=A),), op_params=(2, 2, 8), data=A))
     scores = g.graph_tensor(F32, [70, 20, 4, 2], data=A)
     for mask in (None, g.graph_tensor(F16, [70, 32], data=A), g.graph_tensor(F32, [70, 20, 4], data=A)):
         assert g.supports_op(g.graph_tensor(F32, [70, 20, 4, 2], op=g.OP_SOFT_MAX, src=(scores, mask),
@@ -144,6 +150,10 @@ REJECTED = {
     "SOFT_MAX mask rows short": lambda g: g.graph_tensor(F32, [70, 20, 4], op=g.OP_SOFT_MAX, src=(
         g.graph_tensor(F32, [70, 20, 4], data=A), g.graph_tensor(F16, [70, 16], data=A)),
         op_params=(g.f32_bits(0.125), 0), data=A),
+    "WIN_PART window count param": lambda g: g.graph_tensor(F32, [64, 24, 24, 9], op=g.OP_WIN_PART, src=(
+        g.graph_tensor(F32, [64, 72, 72], data=A),), op_params=(3, 2, 24), data=A),
+    "WIN_UNPART window count": lambda g: g.graph_tensor(F32, [64, 72, 72], op=g.OP_WIN_UNPART, src=(
+        g.graph_tensor(F32, [64, 24, 24, 8], data=A),), op_params=(24,), data=A),
     "CONT type change": lambda g: g.graph_tensor(F16, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(F32, [8, 4], data=A),),
                                                  data=A),
     "CONT element count": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_CONT, src=(

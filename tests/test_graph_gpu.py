@@ -268,3 +268,23 @@ def test_soft_max_graph(b200, backend):
         got = o.get(x.shape, np.float32)
         np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7)
     assert np.all(outs[0].get(x.shape, np.float32)[:, :, 0, 1:] == 0)  # query 0 sees key 0 only
+
+
+def test_window_partition_graph(b200, backend):
+    """ggml_win_part / ggml_win_unpart (sam3.cpp:3734, 3788) with zero padding (10 x 9 map, windows of 4):
+    the windows against numpy, and the round trip exact."""
+    rng = np.random.default_rng(18)
+    C, W, H, w = 8, 10, 9, 4
+    npx, npy = 3, 3
+    x = rng.normal(0, 1, size=(H, W, C)).astype(np.float32)
+    dx, dwin, dback = backend.upload(x), backend.alloc(npx * npy * w * w * C * 4), backend.alloc(x.nbytes)
+    t_x = b200.graph_tensor(F32, [C, W, H], data=dx.ptr)
+    t_win = b200.graph_tensor(F32, [C, w, w, npx * npy], op=b200.OP_WIN_PART, src=(t_x,), op_params=(npx, npy, w),
+                              data=dwin.ptr)
+    t_back = b200.graph_tensor(F32, [C, W, H], op=b200.OP_WIN_UNPART, src=(t_win,), op_params=(w,), data=dback.ptr)
+    backend.graph_compute([t_win, t_back])
+    xp = np.zeros((npy * w, npx * w, C), np.float32)
+    xp[:H, :W] = x
+    ref = np.stack([xp[py * w:(py + 1) * w, px * w:(px + 1) * w] for py in range(npy) for px in range(npx)])
+    assert np.array_equal(dwin.get(ref.shape, np.float32), ref)
+    assert np.array_equal(dback.get(x.shape, np.float32), x)
