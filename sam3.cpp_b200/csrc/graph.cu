@@ -3,14 +3,16 @@
 //
 // sam3.cpp reaches every kernel through ggml_backend_graph_compute
 // (sam3.cpp:1019-1030), which hands the backend the nodes of one graph in
-// execution order.  This file is that executor for the ops the B200 backend
-// owns: MUL_MAT (with the bias ADD that follows every linear layer fused into
-// it, sam3.cpp:3742-3743), FLASH_ATTN_EXT (:3778), CONV_TRANSPOSE_2D (:3884),
-// CONV_2D (:3819) and GET_ROWS (the text encoder's token rows).  Views run
-// nothing (their data already aliases their source).  The whole graph is
-// checked before anything is launched, so a rejected graph leaves the device
-// untouched; each node then runs through the same entry point a direct caller
-// uses, so results are those of the op-level entries.
+// execution order.  This file is that executor: MUL_MAT (with the bias ADD
+// that follows every linear layer fused into it when nothing else reads the
+// product, sam3.cpp:3742-3743), FLASH_ATTN_EXT (:3778), CONV_TRANSPOSE_2D
+// (:3884), CONV_2D (:3819) and GET_ROWS (the text encoder's token rows) run
+// through the same entry points a direct caller uses, so their results are
+// those of the op-level entries; the elementwise ops of the graphs (ADD, MUL,
+// SCALE, the activations, ggml_norm, SOFT_MAX_EXT, WIN_PART / WIN_UNPART,
+// CONT) run on the general-stride kernels below.  Views run nothing (their
+// data already aliases their source).  The whole graph is checked before
+// anything is launched, so a rejected graph leaves the device untouched.
 #include "../../include/sam3_b200.h"
 #include "act.cuh"
 #include "backend_impl.h"
