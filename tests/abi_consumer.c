@@ -78,6 +78,33 @@ int main(void) {
     expect(sam3b200_graph_compute(NULL, nodes, 1) == SAM3B200_STATUS_FAILED, "unknown op graph refused");
     expect(strstr(sam3b200_last_error(), "node 0 rejected") != NULL, "names the node");
 
+    /* the tracker's host-side memory of one object: 9 frames (frame 0 prompted), 7 slots kept */
+    {
+        enum { H = 4, MD = 64, D = 256 };
+        static float feats[H * H * MD], ptr[D], prompt[(7 * H * H + 16 * 4) * MD], pos[(7 * H * H + 16 * 4) * MD];
+        sam3b200_mem_prompt_hparams hp = {D, MD, 7, 16};
+        sam3b200_mem_bank *bank = sam3b200_mem_bank_create(&hp, H);
+        int32_t frames[16], cond[16], pframes[16], n_ptrs = 0, n_ptr_tokens = 0;
+        int f, ns;
+        int64_t m;
+        expect(bank != NULL, "mem_bank_create");
+        for (f = 0; bank && f < 9; ++f) {
+            feats[0] = (float)f;
+            ptr[0] = (float)f;
+            expect(sam3b200_mem_bank_add_slot(bank, feats, f, f == 0) == SAM3B200_STATUS_SUCCESS, "add_slot");
+            expect(sam3b200_mem_bank_add_ptr(bank, ptr, f) == SAM3B200_STATUS_SUCCESS, "add_ptr");
+        }
+        ns = bank ? sam3b200_mem_bank_state(bank, frames, cond, 16, pframes, 16, &n_ptrs) : -1;
+        expect(ns == 7 && frames[0] == 0 && cond[0] == 1 && frames[1] == 3 && frames[6] == 8 && n_ptrs == 9,
+               "bank keeps the prompted frame and the newest six");
+        m = bank ? sam3b200_mem_bank_prompt(bank, 9, NULL, NULL, NULL, prompt, pos, 7 * H * H + 16 * 4,
+                                            &n_ptr_tokens)
+                 : -1;
+        expect(m == 7 * H * H + 9 * 4 && n_ptr_tokens == 9 * 4, "prompt of 7 slots and 9 pointers");
+        expect(prompt[0] == 0.0f && prompt[H * H * MD] == 3.0f, "slot features in bank order");
+        sam3b200_mem_bank_free(bank);
+    }
+
     /* backend lifetime: NULL and a message without a GPU; open/close with one */
     be = sam3b200_backend_init(0);
     if (be) {
