@@ -491,6 +491,15 @@ int64_t sam3b200_mem_bank_prompt(const sam3b200_mem_bank *b, int cur_frame, cons
                                  const float *tpos_proj_w, const float *tpos_proj_b, float *prompt,
                                  float *prompt_pos, int64_t cap_tokens, int32_t *n_ptr_tokens);
 
+/* sam3_compute_axial_cis (sam3.cpp:3559-3590): the 2-D RoPE table of an
+ * end_x x end_y map, out [N][dim/2][2] (cos, sin; x frequencies then y). */
+int sam3b200_axial_cis(int dim, int end_x, int end_y, float theta, float scale_pos, float *out);
+/* The memory attention's rope_q ([H*H][d_model/2][2]) and rope_k (rope_q once
+ * per slot the bank's prompt selects, cap_k_tokens rows of room) as
+ * sam3_propagate_single builds them (:11240-11275); returns the rope_k row
+ * count (0 when the bank is empty) or -1. */
+int64_t sam3b200_mem_bank_rope(const sam3b200_mem_bank *b, float *rope_q, float *rope_k, int64_t cap_k_tokens);
+
 /* ---- Memory encoder of the video tracker ----------------------------------
  * sam3_encode_memory (sam3.cpp:11510-11615) up to the stored [mem_dim, H, H]
  * memory features: mask logits resized to img (bilinear), sigmoid * scale +

@@ -139,6 +139,13 @@ def extract_obj_ptr(sam_token, obj_score: float, w, b, no_obj_ptr, blend: bool =
     return out
 
 
+def axial_cis(dim: int, end_x: int, end_y: int, theta: float = 10000.0, scale_pos: float = 1.0) -> np.ndarray:
+    """sam3b200_axial_cis: [end_x*end_y][dim/2][2] float32 (cos, sin)."""
+    out = np.empty((end_x * end_y, dim // 2, 2), np.float32)
+    _check(lib().sam3b200_axial_cis(dim, end_x, end_y, theta, scale_pos, out.ctypes.data), "axial_cis")
+    return out
+
+
 def sinusoidal_pe_2d(H: int, W: int, d_model: int) -> np.ndarray:
     """sam3b200_sinusoidal_pe_2d: [H][W][d_model] float32."""
     out = np.empty((H, W, d_model), np.float32)
@@ -192,6 +199,16 @@ class MemBank:
         if m < 0:
             raise B200Error(f"mem_bank_prompt failed: {last_error()}")
         return prompt[:m], pos[:m], n.value
+
+    def rope(self):
+        """(rope_q [H*H][D/2][2], rope_k [slots*H*H][D/2][2] or None) for the bank's current prompt."""
+        D, HH = self.hp["d_model"], self.H * self.H
+        rq = np.empty((HH, D // 2, 2), np.float32)
+        rk = np.empty((self.hp["num_maskmem"] * HH, D // 2, 2), np.float32)
+        m = lib().sam3b200_mem_bank_rope(self.h, rq.ctypes.data, rk.ctypes.data, rk.shape[0])
+        if m < 0:
+            raise B200Error(f"mem_bank_rope failed: {last_error()}")
+        return rq, (rk[:m] if m else None)
 
     def free(self) -> None:
         if self.h:
@@ -280,6 +297,8 @@ def lib() -> ctypes.CDLL:
         "sam3b200_mem_bank_add_ptr": (i32, [vp, vp, i32]),
         "sam3b200_mem_bank_state": (i32, [vp, vp, vp, i32, vp, i32, vp]),
         "sam3b200_mem_bank_prompt": (i64, [vp, i32, vp, vp, vp, vp, vp, i64, vp]),
+        "sam3b200_axial_cis": (i32, [i32, i32, i32, ctypes.c_float, ctypes.c_float, vp]),
+        "sam3b200_mem_bank_rope": (i64, [vp, vp, vp, i64]),
         "sam3b200_build_mem_prompt": (i64, [vp, i32, i32, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp, vp, vp, i64,
                                             vp]),
         "sam3b200_graph_compute": (i32, [vp, ctypes.POINTER(ctypes.POINTER(GraphTensor)), i32]),

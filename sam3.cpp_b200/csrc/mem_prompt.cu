@@ -307,3 +307,57 @@ extern "C" int64_t sam3b200_mem_bank_prompt(const sam3b200_mem_bank *b, int cur_
                                      ptrs.data(), frames.data(), cur_frame, tpos_enc, tpos_proj_w, tpos_proj_b,
                                      prompt, prompt_pos, cap_tokens, n_ptr_tokens);
 }
+
+// sam3_compute_axial_cis (sam3.cpp:3559-3590): per position idx of an end_x x end_y map, dim/4 x frequencies
+// then dim/4 y frequencies 1 / theta^(4i / dim), stored as (cos, sin) pairs: out [N][dim/2][2].  The
+// tracker's RoPE tables (sam3_ensure_tracker_pe_caches, :11140-11152) are this table unchanged.
+extern "C" int sam3b200_axial_cis(int dim, int end_x, int end_y, float theta, float scale_pos, float *out) {
+    if (dim <= 0 || dim % 4 != 0 || end_x <= 0 || end_y <= 0 || !out) {
+        set_error("axial_cis: bad arguments");
+        return SAM3B200_STATUS_FAILED;
+    }
+    const int q = dim / 4;
+    std::vector<float> freqs(q);
+    for (int i = 0; i < q; ++i) freqs[i] = 1.0f / powf(theta, static_cast<float>(i * 4) / static_cast<float>(dim));
+    const int64_t N = static_cast<int64_t>(end_x) * end_y;
+    for (int64_t idx = 0; idx < N; ++idx) {
+        const float tx = static_cast<float>(idx % end_x) * scale_pos;
+        const float ty = static_cast<float>(idx / end_x) * scale_pos;
+        float *o = out + idx * dim;
+        for (int i = 0; i < q; ++i) {
+            o[2 * i] = cosf(tx * freqs[i]);
+            o[2 * i + 1] = sinf(tx * freqs[i]);
+            o[2 * q + 2 * i] = cosf(ty * freqs[i]);
+            o[2 * q + 2 * i + 1] = sinf(ty * freqs[i]);
+        }
+    }
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+// The memory attention's RoPE inputs for the bank's current prompt: rope_q = the H x H table of d_model
+// (theta 1e4), rope_k = that table once per selected slot (sam3_propagate_single, :11240-11275, standard
+// path).  rope_k needs n_selected * H * H * d_model floats; returns the spatial key count (0: no rope_k).
+extern "C" int64_t sam3b200_mem_bank_rope(const sam3b200_mem_bank *b, float *rope_q, float *rope_k,
+                                          int64_t cap_k_tokens) {
+    if (!b || !rope_q) {
+        set_error("mem_bank_rope: null argument");
+        return -1;
+    }
+    const int D = b->hp.d_model, HH = b->H * b->H;
+    if (sam3b200_axial_cis(D, b->H, b->H, 10000.0f, 1.0f, rope_q) != SAM3B200_STATUS_SUCCESS) return -1;
+    const int ns = static_cast<int>(b->slots.size());
+    std::vector<int32_t> sel(std::max(ns, 2));
+    const int n_sel = sam3b200_select_memory_frames(ns, b->hp.num_maskmem, sel.data(), static_cast<int>(sel.size()));
+    if (n_sel < 0) return -1;
+    const int64_t m_spatial = static_cast<int64_t>(n_sel) * HH;
+    if (m_spatial > 0) {
+        if (!rope_k || m_spatial > cap_k_tokens) {
+            set_error("mem_bank_rope: %lld spatial keys, room for %lld", static_cast<long long>(m_spatial),
+                      static_cast<long long>(rope_k ? cap_k_tokens : 0));
+            return -1;
+        }
+        for (int s = 0; s < n_sel; ++s)
+            std::copy(rope_q, rope_q + static_cast<int64_t>(HH) * D, rope_k + static_cast<int64_t>(s) * HH * D);
+    }
+    return m_spatial;
+}

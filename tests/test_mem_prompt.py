@@ -182,3 +182,29 @@ def test_mem_bank_all_conditioning(b200):
     slots, _ = bank.state()
     assert [s[0] for s in slots] == [0] + list(range(6, 12))
     bank.free()
+
+
+@pytest.mark.parametrize("dim,ex,ey", [(256, 64, 64), (256, 72, 72), (64, 24, 24), (64, 72, 72)])
+def test_axial_cis_matches_the_tables_the_gpu_tests_use(b200, dim, ex, ey):
+    """sam3_compute_axial_cis: the tracker's (d 256) and the ViT's (d 64) RoPE tables, against the oracle table
+    the memory-attention parity tests feed the GPU."""
+    import mem_attn_oracle
+    # libm powf vs numpy's float32 power can differ by an ulp in a frequency, which the position (up to 71)
+    # multiplies: a few 1e-6 in the angle
+    np.testing.assert_allclose(b200.axial_cis(dim, ex, ey), mem_attn_oracle.axial_cis(dim, ex, ey), rtol=0, atol=1e-5)
+
+
+def test_mem_bank_rope(b200):
+    """rope_q = the H x H table; rope_k = that table once per selected slot; none for an empty bank."""
+    import mem_attn_oracle
+    H = 8
+    bank = b200.MemBank(HP, H)
+    rq, rk = bank.rope()
+    assert rk is None
+    np.testing.assert_allclose(rq, mem_attn_oracle.axial_cis(256, H, H), rtol=0, atol=1e-5)
+    for f in range(10):
+        bank.add_slot(np.zeros((H * H, 64), np.float32), f, f == 0)
+    rq, rk = bank.rope()
+    assert rk.shape == (7 * H * H, 128, 2)
+    assert np.array_equal(rk, np.concatenate([rq] * 7))
+    bank.free()
