@@ -122,15 +122,18 @@ int sam3b200_backend_profile_read(sam3b200_backend *be, int cls, double *total_m
  * compute -- a framework that plans all device memory up front (as ggml's
  * graph allocator does for a backend's graph_compute) or a latency-bound
  * loop that cannot take cudaMalloc's implicit synchronisation.  Same
- * arguments and result as sam3b200_mul_mat; the quantised activations go to
- * a fixed 48 MiB array compiled into the library (resident on every GPU
- * that loads it, until the process exits) instead of backend scratch.
- * Shapes whose scratch (M*K bytes of codes + K/32 * roundup(M,128) * 16
- * bytes of scales) exceeds 48 MiB are rejected with an error message.  The
- * first call on a device looks up the array's device address; make that
- * first call before any stream capture.  All calls on a device share the
- * array: calls that overlap on the GPU race and must be serialised by the
- * caller.  Asynchronous on the backend stream. */
+ * arguments and result as sam3b200_mul_mat for Q8_0 and Q4_0 weights only
+ * (Q4_1, F16 and F32 weights are refused with an error); the quantised
+ * activations go to a fixed 48 MiB array compiled into the library
+ * (resident on every GPU that loads it, until the process exits) instead of
+ * backend scratch.  Shapes whose scratch (M*K bytes of codes, rounded up to
+ * 256, + ceil(K/256) * roundup(M,128) * 16 bytes of scale records) exceeds
+ * 48 MiB are rejected with an error message.  The kernel choice
+ * follows sam3b200_set_mmq_impl as for sam3b200_mul_mat.  The first call on
+ * a device looks up the array's device address; make that first call before
+ * any stream capture, and do not cudaDeviceReset the device after it.  All
+ * calls on a device share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller.  Asynchronous on the backend stream. */
 int sam3b200_mul_mat_noalloc(sam3b200_backend *be, const sam3b200_weight *w, const float *x, int64_t ldx, int64_t M,
                              const float *bias, float *dst, int64_t ldd);
 

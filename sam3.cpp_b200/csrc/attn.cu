@@ -32,6 +32,7 @@
 // Tensor memory (512 columns): tile t at 256 t: S (128 columns), P (64: 128
 // bf16 packed in pairs), PV (64).
 #include "attn.cuh"
+#include "mmq.cuh"
 #include "ptx.cuh"
 #include "tmap.h"
 
@@ -343,7 +344,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                             dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                             const int blk = (h * C::HD + hb) >> 5;
-                            qquads[(static_cast<int64_t>(blk >> 3) * qld + r) * 8 + (blk & 7)] = __float2half_rn(dq);
+                            store_act_scale(qquads, blk, static_cast<int>(r), qld, E >> 5, dq);
                         }
                     } else {
                         float *dst = out + r * heads * C::HD + h * C::HD;

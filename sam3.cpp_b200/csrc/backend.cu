@@ -351,7 +351,7 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
         return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
     }
     const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
-    const size_t quad_bytes = static_cast<size_t>(w->K / 32) * lda * 16;
+    const size_t quad_bytes = act_quad_bytes(w->K, lda);
     const bool q41 = w->type == SAM3B200_TYPE_Q4_1;  // Q8_1 activations: the sum fields follow the scales
     if (!be->ensure_scratch(static_cast<size_t>(Mi) * w->K, q41 ? 2 * quad_bytes : quad_bytes))
         return SAM3B200_STATUS_ALLOC_FAILED;

@@ -65,9 +65,9 @@ static bool alloc_activations(Vit *v) {
     bool ok = v->img_f32.alloc(static_cast<size_t>(3) * hp.img * hp.img * 4) &&
               v->a_patch.alloc(static_cast<size_t>(T) * v->KP * 2) && v->conv.alloc(static_cast<size_t>(T) * E * 4) &&
               v->x.alloc(static_cast<size_t>(T) * E * 4) && v->codes_a.alloc(static_cast<size_t>(T) * E) &&
-              v->quads_a.alloc(static_cast<size_t>(E / 32) * v->Tpad * 16) &&
+              v->quads_a.alloc(act_quad_bytes(E, v->Tpad)) &&
               v->codes_b.alloc(static_cast<size_t>(T) * maxk) &&
-              v->quads_b.alloc(maxk / 32 * v->Tpad * 16) &&
+              v->quads_b.alloc(act_quad_bytes(static_cast<int>(maxk), v->Tpad)) &&
               v->q.alloc(static_cast<size_t>(T) * E * 2) && v->k.alloc(static_cast<size_t>(T) * E * 2) &&
               v->v.alloc(static_cast<size_t>(T) * E * 2) &&
               v->rowmap.alloc(static_cast<size_t>(T) * 4) && v->x16.alloc(static_cast<size_t>(T) * E * 2) &&

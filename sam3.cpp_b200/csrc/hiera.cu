@@ -37,7 +37,7 @@ namespace {
 
 // Quantise one 32-wide block (ggml-cpu activation rule) and store codes + scale record.
 __device__ __forceinline__ void q8_block_store(const float (&v)[32], int8_t *codes, __half *quads, int blk, int64_t r,
-                                               int ld) {
+                                               int ld, int nblk) {
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -55,7 +55,7 @@ __device__ __forceinline__ void q8_block_store(const float (&v)[32], int8_t *cod
     uint4 *dst = reinterpret_cast<uint4 *>(codes + blk * 32);
     dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    quads[act_quad_index(blk, static_cast<int>(r), ld)] = __float2half_rn(d);
+    store_act_scale(quads, blk, static_cast<int>(r), ld, nblk, d);
 }
 
 // Window partition (with zero padding) of normed [H][W][C] fused with the Q8
@@ -80,7 +80,7 @@ __global__ void win_gather_q8_kernel(const float *__restrict__ x, int H, int W, 
             v[i + 2] = q.z;
             v[i + 3] = q.w;
         }
-        q8_block_store(v, cr, quads, blk, r, ld);
+        q8_block_store(v, cr, quads, blk, r, ld, C / 32);
     }
 }
 

@@ -86,7 +86,7 @@ __global__ void quantize_rows_q8_kernel(const float *__restrict__ x, int64_t ldx
     *reinterpret_cast<uint2 *>(codes + static_cast<int64_t>(m) * K + e) =
         make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
     if ((e & 31) == 0) {
-        quads[act_quad_index(e >> 5, m, ld)] = __float2half_rn(d);
+        store_act_scale(quads, e >> 5, m, ld, K >> 5, d);
         if (sums) sums[act_quad_index(e >> 5, m, ld)] = __float2half_rn(__fmul_rn(d, static_cast<float>(qsum)));
     }
 }
@@ -369,7 +369,7 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
                 uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
                 dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                ep.qquads[act_quad_index((nb + hb) >> 5, m, ep.qld)] = __float2half_rn(d);
+                store_act_scale(ep.qquads, (nb + hb) >> 5, m, ep.qld, N >> 5, d);
             }
         }
     }

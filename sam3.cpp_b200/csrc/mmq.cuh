@@ -18,6 +18,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace b200 {
@@ -35,11 +36,31 @@ enum MmqOut : int {
 
 constexpr int MMQ_ROW_ALIGN = 128;
 
+// Bytes of an activation operand's scale records: ceil(K/256) groups of ld 16-byte records.
+__host__ __device__ constexpr size_t act_quad_bytes(int K, int ld) {
+    return static_cast<size_t>((K + 255) / 256) * static_cast<size_t>(ld) * 16u;
+}
+
 // element offset (in fp16 units) of block b's scale of row m in an A-side
 // (activation) quad array with `ld` rows per group
 __host__ __device__ constexpr int64_t act_quad_index(int b, int m, int ld) {
     return (static_cast<int64_t>(b >> 3) * ld + m) * 8 + (b & 7);
 }
+
+#ifdef __CUDACC__
+// Store the scale d of block b (of nblk) of row m into an A-side record
+// array.  The writer of a row's last block also zeroes the record slots past
+// it when nblk is not a multiple of 8: the scale MMA reads whole records and
+// multiplies those slots by the weight record's zeros, so left unwritten
+// (holding whatever a previous use of the buffer left, possibly a NaN or an
+// infinity) they would turn the product into a NaN.
+__device__ __forceinline__ void store_act_scale(__half *quads, int b, int m, int ld, int nblk, float d) {
+    const int64_t base = (static_cast<int64_t>(b >> 3) * ld + m) * 8;
+    quads[base + (b & 7)] = __float2half_rn(d);
+    if (b == nblk - 1)
+        for (int s = (b & 7) + 1; s < 8; ++s) quads[base + s] = __ushort_as_half(static_cast<unsigned short>(0));
+}
+#endif
 
 struct QMatrix {
     const void *codes;  // int8 [rows, K]

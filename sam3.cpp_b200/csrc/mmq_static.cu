@@ -13,7 +13,10 @@
 // The array lives in device memory of every GPU that loads the library, for
 // the life of the process, and is shared by all calls on that device: two
 // calls that overlap on the GPU (different streams or backends on the same
-// device) race on it and must be serialised by the caller.
+// device) race on it and must be serialised by the caller.  Its device
+// address is looked up once per device, on the first call there; a
+// cudaDeviceReset after that first call is not supported (the module is
+// reloaded and the cached address would be stale).
 #include "../../include/sam3_b200.h"
 #include "backend_impl.h"
 #include "mmq.cuh"
@@ -23,7 +26,7 @@
 namespace b200 {
 
 // 48 MiB: enough for every MUL_MAT of the SAM3 ViT-32 at 5184 tokens
-// (largest: mlp.lin2, K = 4736: 24.6 MB of codes + 12.4 MB of scale quads).
+// (largest: mlp.lin2, K = 4736: 24.6 MB of codes + 1.6 MB of scale records).
 constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(48) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
@@ -78,7 +81,7 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
     const int Mi = static_cast<int>(M);
     const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
     const size_t codes_bytes = (static_cast<size_t>(Mi) * w->K + 255) / 256 * 256;
-    const size_t quad_bytes = static_cast<size_t>(w->K / 32) * lda * 16;
+    const size_t quad_bytes = act_quad_bytes(w->K, lda);
     if (codes_bytes + quad_bytes > NOALLOC_SCRATCH_BYTES) {
         set_error("mul_mat_noalloc: M=%d x K=%d needs %zu bytes of scratch, more than the fixed %zu-byte array "
                   "(use sam3b200_mul_mat, or split M)",
@@ -91,8 +94,9 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
     void *codes = base;
     void *quads = base + codes_bytes;
     // Nothing in the scratch has to start at zero: every code and scale of
-    // rows [0, M) is rewritten below, and padding rows [M, lda) only feed
-    // output rows that are never stored.
+    // rows [0, M) is rewritten below (the quantiser also zeroes the record
+    // slots past a row's last block, which the scale MMA reads), and padding
+    // rows [M, lda) only feed output rows that are never stored.
     if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, codes, quads, lda, be->stream), "quantize activations"))
         return SAM3B200_STATUS_FAILED;
     MmqArgs a;
@@ -104,8 +108,12 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
     a.dump = nullptr;
     a.err = be->err;
     be->count(2);
-    const cudaError_t e = Mi < 64 ? mmq_simt(a, MMQ_OUT_F32, be->stream)
-                                  : mmq_tc(a, MMQ_OUT_F32, be->num_sms, be->stream, be->mmq_cvt);
+    // the same kernel choice as sam3b200_mul_mat (Q4_1 is refused above)
+    int impl = be->mmq_impl;
+    if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
+    const cudaError_t e = impl == SAM3B200_MMQ_SIMT
+                              ? mmq_simt(a, MMQ_OUT_F32, be->stream)
+                              : mmq_tc(a, MMQ_OUT_F32, be->num_sms, be->stream, be->mmq_cvt, be->mmq_bn);
     if (!cuda_ok(e, "mul_mat_noalloc launch")) return SAM3B200_STATUS_FAILED;
     return SAM3B200_STATUS_SUCCESS;
 }

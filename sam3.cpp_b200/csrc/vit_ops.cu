@@ -3,6 +3,7 @@
 // intrinsics so nvcc cannot contract it into FMAs; LayerNorm sums in double
 // like ggml_norm does.
 #include "vit_ops.cuh"
+#include "mmq.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -233,7 +234,7 @@ __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const
         uint4 *dst = reinterpret_cast<uint4 *>(codes + static_cast<int64_t>(r) * E + blk * 32);
         dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        quads[static_cast<int64_t>((blk >> 3) * ld + r) * 8 + (blk & 7)] = __float2half_rn(d);
+        store_act_scale(quads, blk, r, ld, nblk, d);
     }
 }
 
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
                   __float2int_rn(__fmul_rn(y2, id)), __float2int_rn(__fmul_rn(y3, id)));
         if ((lane & 7) == 0) {
             const int blk = 4 * j + (lane >> 3);
-            quads[static_cast<int64_t>((blk >> 3) * ld + r) * 8 + (blk & 7)] = __float2half_rn(d);
+            store_act_scale(quads, blk, r, ld, E >> 5, d);
         }
     }
 }
