@@ -242,6 +242,8 @@ def _vit_lib():
         L.orc_neck.argtypes = [vp, vp, vp, vp, i32]
         L.orc_layer_norm.argtypes = [vp, vp, ctypes.c_int64, i32, ctypes.c_float, vp, vp, i32]
         L.orc_attention.argtypes = [vp, vp, vp, i32, i32, i32, ctypes.c_float, vp, i32]
+        L.orc_set_attention_f64.argtypes = [i32]
+        L.orc_set_attention_f64.restype = None
         for f in ("orc_preprocess_sam3", "orc_preprocess_sam2", "orc_vit_prefix", "orc_vit_block", "orc_neck", "orc_layer_norm",
                   "orc_attention"):
             getattr(L, f).restype = None
@@ -331,8 +333,15 @@ class OracleVit:
         _vit_lib().orc_neck(ctypes.byref(self.h), ctypes.byref(self.w.neck), x.ctypes.data, ptrs, self.nt)
         return outs
 
-    def encode(self, rgb: np.ndarray, depth: int | None = None) -> tuple:
-        x = self.prefix(self.preprocess(rgb))
-        for i in range(self.hp["depth"] if depth is None else depth):
-            x = self.block(i, x)
-        return x, self.neck(x)
+    def encode(self, rgb: np.ndarray, depth: int | None = None, attn_f64: bool = False) -> tuple:
+        """The whole encode.  attn_f64: attention in float64 instead of float32 -- a
+        second, equally valid evaluation of the same graph (the tests measure the
+        distance between the two)."""
+        _vit_lib().orc_set_attention_f64(1 if attn_f64 else 0)
+        try:
+            x = self.prefix(self.preprocess(rgb))
+            for i in range(self.hp["depth"] if depth is None else depth):
+                x = self.block(i, x)
+            return x, self.neck(x)
+        finally:
+            _vit_lib().orc_set_attention_f64(0)

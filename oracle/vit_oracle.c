@@ -189,9 +189,57 @@ void orc_qkv_split_rope(const float *qkv, const float *freqs, int B, int N, int 
 }
 
 /* ---- attention: softmax(q k^T * scale) v, f32 (ggml_flash_attn_ext, F32 K/V) */
+/* Arithmetic of orc_attention: 0 = float32 (the default, as ggml's CPU backend
+ * computes an F32 FLASH_ATTN_EXT), 1 = float64 throughout.  The float64 form is
+ * a second, equally valid evaluation of the same graph; the tests use the
+ * distance between the two to measure how far a rounding-level change in
+ * attention carries through the quantised blocks. */
+static int g_attn_f64 = 0;
+
+void orc_set_attention_f64(int on) { g_attn_f64 = on ? 1 : 0; }
+
+static void attention_f64(const float *q, const float *k, const float *v, int B, int N, int heads, float scale,
+                          float *out, int n_threads) {
+    const int HD = 64;
+    #pragma omp parallel num_threads(n_threads)
+    {
+        double *s = (double *)malloc(sizeof(double) * N);
+        double acc[64];
+        #pragma omp for collapse(2) schedule(static)
+        for (int bh = 0; bh < B * heads; ++bh)
+            for (int n = 0; n < N; ++n) {
+                const float *qr = q + ((size_t)bh * N + n) * HD;
+                const float *kb = k + (size_t)bh * N * HD;
+                const float *vb = v + (size_t)bh * N * HD;
+                double mx = -INFINITY;
+                for (int m = 0; m < N; ++m) {
+                    double d = 0.0;
+                    for (int i = 0; i < HD; ++i) d += (double)qr[i] * kb[(size_t)m * HD + i];
+                    s[m] = d * scale;
+                    if (s[m] > mx) mx = s[m];
+                }
+                double sum = 0.0;
+                for (int i = 0; i < HD; ++i) acc[i] = 0.0;
+                for (int m = 0; m < N; ++m) {
+                    const double e = exp(s[m] - mx);
+                    sum += e;
+                    for (int i = 0; i < HD; ++i) acc[i] += e * vb[(size_t)m * HD + i];
+                }
+                const int b = bh / heads, h = bh % heads;
+                float *o = out + ((size_t)b * N + n) * heads * HD + h * HD;
+                for (int i = 0; i < HD; ++i) o[i] = (float)(acc[i] / sum);
+            }
+        free(s);
+    }
+}
+
 void orc_attention(const float *q, const float *k, const float *v, int B, int N, int heads, float scale, float *out,
                    int n_threads) {
     const int HD = 64;
+    if (g_attn_f64) {
+        attention_f64(q, k, v, B, N, heads, scale, out, n_threads);
+        return;
+    }
     #pragma omp parallel num_threads(n_threads)
     {
         float *s = (float *)malloc(sizeof(float) * N);

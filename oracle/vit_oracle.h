@@ -79,6 +79,8 @@ void orc_win_unpart(const float *y, float *x, int E, int W, int H, int ws);   /*
 void orc_qkv_split_rope(const float *qkv, const float *freqs, int B, int N, int E, int heads, float *q, float *k,
                         float *v);
 /* ggml_flash_attn_ext without mask: out [B][N][heads*64] (sam3.cpp:3778-3781) */
+/* 1: orc_attention computes in float64 (a second valid evaluation); 0: float32 (default). */
+void orc_set_attention_f64(int on);
 void orc_attention(const float *q, const float *k, const float *v, int B, int N, int heads, float scale, float *out,
                    int n_threads);
 void orc_gelu_erf(float *x, int64_t n);

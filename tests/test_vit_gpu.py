@@ -125,6 +125,76 @@ def test_full_size_block(backend, full8, idx):
     assert err <= TOL, err
 
 
+@pytest.fixture(scope="module")
+def full32(model, oracle, backend):
+    """Config 3 exactly as benchmarked: SAM3 ViT-32 (32 blocks, E = 1024, 16
+    heads, MLP 4736, global blocks 7/15/23/31, Q8_0 weights) + tracker neck."""
+    hp = model.SAM3_VIT
+    tensors = model.random_vit_weights(hp, seed=11)
+    vit = backend.vit(hp)
+    vit.load(tensors)
+    rgb = np.random.default_rng(12).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8)
+    yield hp, vit, oracle.OracleVit(hp, tensors), rgb
+    vit.free()
+
+
+def test_full_size_every_stage_on_the_gpu_trajectory(backend, full32):
+    """sam3_encode_image (sam3.cpp:6028-6216) at config 3, stage by stage along
+    the GPU's own trajectory, at the fixed 1e-2 bound: the prefix on the
+    preprocessed image, then each of the 32 blocks on the residual stream the
+    GPU produced before it, then the neck on the GPU's final stream -- each
+    against the oracle stage on the same input (the per-stage comparison of
+    the reference's own test, tests/test_metal_block_stage_compare.cpp:380-440).
+    The stepwise GPU path is the encode path: its outputs equal encode()'s bit
+    for bit."""
+    hp, vit, ov, rgb = full32
+    img = ov.preprocess(rgb)
+    dimg = backend.upload(img)
+    x_ref = ov.prefix(img)
+    dx = backend.alloc(x_ref.nbytes)
+    vit.run_prefix(dimg, dx)
+    backend.synchronize()
+    x = dx.get(x_ref.shape, np.float32)
+    errs = {"prefix": rel_err(x, x_ref)}
+    for i in range(hp["depth"]):
+        want = ov.block(i, x)
+        vit.run_block(i, dx)
+        backend.synchronize()
+        x = dx.get(x_ref.shape, np.float32)
+        errs[f"block{i}"] = rel_err(x, want)
+    vit.run_neck(dx)
+    refs = ov.neck(x)
+    for i in range(4):
+        errs[f"neck{i}"] = rel_err(vit.output_host(i), refs[i])
+    print("stage errors:", ", ".join(f"{k} {v:.2e}" for k, v in errs.items()))
+    assert max(errs.values()) <= TOL, errs
+    outs = vit.encode(rgb)
+    assert np.array_equal(vit.output_host(-1).reshape(x.shape), x)
+    for i in range(4):
+        assert np.array_equal(outs[i], vit.output_host(i))
+
+
+def test_full_size_free_running_divergence(full32):
+    """The free-running encode against the oracle's, next to the oracle against
+    itself.  Thirty-two re-quantised blocks amplify any rounding-level change:
+    the oracle with its attention in float64 instead of float32 -- an equally
+    valid evaluation -- already lands ~1.4e-2 (max |d| / max |ref|) from its
+    float32 self at the final stream and the neck, so no implementation that is
+    not bit-identical to one particular evaluation can hold 1e-2 here.  The GPU
+    must stay within 1.5x of that self-divergence."""
+    hp, vit, ov, rgb = full32
+    outs = vit.encode(rgb)
+    x = vit.output_host(-1)
+    x32, n32 = ov.encode(rgb)
+    x64, n64 = ov.encode(rgb, attn_f64=True)
+    gpu = [rel_err(x.reshape(x32.shape), x32)] + [rel_err(outs[i], n32[i]) for i in range(4)]
+    own = [rel_err(x64, x32)] + [rel_err(n64[i], n32[i]) for i in range(4)]
+    print("free-running, GPU vs oracle:", ", ".join(f"{e:.3e}" for e in gpu))
+    print("free-running, oracle f64 vs f32:", ", ".join(f"{e:.3e}" for e in own))
+    for g, o in zip(gpu, own):
+        assert g <= 1.5 * o, (gpu, own)
+
+
 def test_missing_weights_fail_loudly(b200, backend, model):
     hp = model.SAM3_VIT_TEST
     vit = backend.vit(hp)
