@@ -1,6 +1,6 @@
-"""Benchmark: SAM3 Q8_0 ViT encode images/s on
-1..8 B200s, with the quantised MUL_MAT's tensor throughput against the int8
-peak as the roofline line.
+"""Benchmark: SAM3 Q8_0 ViT encode images/s (the visual-only ViT-32 + tracker
+neck configuration) on 1..8 B200s, with the quantised MUL_MAT's tensor
+throughput against the int8 peak as the roofline line.
 
 Workload (one step): a batch of 64 seeded uniform-uint8 1008x1008 RGB
 images, data-parallel -- rank r of N encodes images r, r+N, ... (strong
@@ -17,6 +17,7 @@ tracker SimpleFPN neck -- the whole of sam3_encode_image.
 
 python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 python bench.py --workload pcs|video   (secondary lines: config 4 detector / config 5 tracker stages, 1 GPU)
+python bench.py --workload mmq         (config 2: MUL_MAT sweep, Q8_0 / Q4_0 at the four ViT shapes, 1 GPU)
 """
 from __future__ import annotations
 
@@ -27,6 +28,7 @@ import json
 import os
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -178,7 +180,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video"],
+    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video", "mmq"],
                     help="encode (default: the headline, config 3); pcs / video: the config 4 detector or the "
                          "config 5 tracker memory stages, timed per image / frame (sam3.cpp_b200/component_bench.py)")
     ap.add_argument("--images", type=int, default=BATCH,
@@ -189,6 +191,27 @@ def main():
     hp = dict(model_mod.SAM3_VIT)
     if args.impl == "reference":
         return run_reference(args, hp, model_mod)
+    if args.workload == "mmq":
+        import torch
+        b200 = _load("b200")
+        comp = _load("component_bench")
+        torch.cuda.set_device(0)
+        be = b200.Backend(0)
+        peak = measured_int8_peak_tops()
+        res = comp.run_mmq(b200, model_mod, be, max(args.steps, 10), max(args.warmup, 3), peak)
+        sweep = res["sweep"]
+        q8 = [r for r in sweep if r["type"] == "Q8_0" and r["order"] == "tokens"]
+        ops = sum(2.0 * r["M"] * r["K"] * r["N"] for r in q8)
+        kern_s = sum(r["kernel_us"] for r in q8) * 1e-6
+        line = {"metric": "MMQ TOP/s vs int8 peak (config 2 sweep)", "value": ops / kern_s / 1e12,
+                "unit": "TOP/s", "n_gpus": 1, "steps": max(args.steps, 10), "warmup": max(args.warmup, 3),
+                "higher_is_better": True, "dtype": "int8 codes (fp16-held), fp32 fold", "data": "synthetic",
+                "config": {"workload": "cfg2: Q8_0 / Q4_0 MUL_MAT at M = 5184, (K, N) in qkv/proj/fc1/fc2, token "
+                                       "and win_part row orders; value = Q8_0 token-order ops / kernel time"},
+                "peak_int8_tops": peak, "frac": ops / kern_s / 1e12 / peak, "sweep": sweep}
+        print(json.dumps(line), flush=True)
+        be.free()
+        return 0
     if args.workload != "encode":
         b200 = _load("b200")
         comp = _load("component_bench")
@@ -257,8 +280,7 @@ def main():
     for _ in range(args.warmup):
         step_device()
     barrier()
-    clocks = ClockSampler(local, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                                              else "/tmp", f"bench_clocks_{rank}.csv"))
+    clocks = ClockSampler(local, os.path.join(tempfile.gettempdir(), f"sam3b200_bench_clocks_{os.getpid()}_{rank}.csv"))
     launches0 = be.launches
     be.profile(True)
     ms = timed(step_device, args.steps)

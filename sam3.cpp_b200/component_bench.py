@@ -298,3 +298,68 @@ def run_video(b200, model_mod, be, steps: int, warmup: int) -> dict:
             "stages_ms": {"memory_attention": stages[0], "memory_encoder": stages[1]},
             "memory_attention_attn_tflops": attn_flop / (stages[0] / 1e3) / 1e12,
             "memory_attention_attn_flop": attn_flop}
+
+
+# Config 2: the standalone MUL_MAT sweep at the SAM3 ViT-32 shapes
+# (qkv, proj, fc1, fc2 of sam3_vit_block_forward, sam3.cpp:3742,3783,3796,3799).
+MMQ_SHAPES = (("qkv", 1024, 3072), ("proj", 1024, 1024), ("fc1", 1024, 4736), ("fc2", 4736, 1024))
+
+
+def win_part_rows(G: int, win: int) -> np.ndarray:
+    """Source row of each row of ggml_win_part's order for a G x G token map (G % win == 0)."""
+    nw = G // win
+    rows = np.empty(G * G, np.int64)
+    for t in range(G * G):
+        tx, ty = t % G, t // G
+        rows[((ty // win) * nw + tx // win) * win * win + (tx % win) + win * (ty % win)] = t
+    return rows
+
+
+def run_mmq(b200, model_mod, be, steps: int, warmup: int, peak_int8_tops: float | None) -> dict:
+    """Q8_0 and Q4_0 weights at the four ViT shapes, M = 5184 tokens, in token
+    order and in ggml_win_part order (9 windows x 576 tokens).  Per case:
+    the MUL_MAT kernel alone (CUDA events around its launches, via the
+    backend profiler) and the whole op (activation quantisation + kernel),
+    as TOP/s of 2*M*K*N.  Activations N(0, 1), weights N(0, 0.02) quantised
+    with the reference rule."""
+    import torch
+    stream = torch.cuda.ExternalStream(be.stream)
+    G, win, M = 72, 24, 72 * 72
+    rng = np.random.default_rng(2)
+    perm = win_part_rows(G, win)
+    out = []
+    for qtype, qname in ((Q8_0, "Q8_0"), (Q4_0, "Q4_0")):
+        for name, K, N in MMQ_SHAPES:
+            wq = model_mod.quantize_rows(qtype, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+            w = be.weight(qtype, wq, K, N)
+            bias = be.upload(rng.normal(0, 0.02, size=N).astype(np.float32))
+            x = rng.standard_normal((M, K), dtype=np.float32)
+            y = be.alloc(M * N * 4)
+            for order, xs in (("tokens", x), ("win_part", x[perm])):
+                xd = be.upload(np.ascontiguousarray(xs))
+                for _ in range(warmup):
+                    be.mul_mat(w, xd, M, y, bias=bias)
+                be.synchronize()
+                be.profile(True)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(steps):
+                    be.mul_mat(w, xd, M, y, bias=bias)
+                e1.record(stream)
+                be.synchronize()
+                op_ms = e0.elapsed_time(e1) / steps
+                k_ms, k_n = be.profile_read(0)
+                be.profile(False)
+                k_ms /= max(k_n, 1)
+                ops = 2.0 * M * K * N
+                rec = {"type": qname, "layer": name, "M": M, "K": K, "N": N, "order": order,
+                       "kernel_us": k_ms * 1e3, "op_us": op_ms * 1e3,
+                       "kernel_tops": ops / (k_ms * 1e-3) / 1e12, "op_tops": ops / (op_ms * 1e-3) / 1e12}
+                if peak_int8_tops:
+                    rec["kernel_frac_int8"] = rec["kernel_tops"] / peak_int8_tops
+                out.append(rec)
+                xd.free()
+            y.free()
+            bias.free()
+            w.free()
+    return {"sweep": out}
