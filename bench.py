@@ -130,45 +130,62 @@ def measured_int8_peak_tops() -> float:
     return 2 * n ** 3 / best / 1e9
 
 
-def cpu_baseline(model_mod, hp, sample_blocks=(0, 7)):
-    """The CPU restatement (oracle/) of the same encoder on a bounded sample:
-    one windowed and one global ViT block at full size on all host cores;
-    images/s extrapolated to the 28 windowed + 4 global blocks of ViT-32
-    (the neck and prefix, ~5% of the work, are not in the sample)."""
+# Whole images the CPU legs encode per measurement: each is preprocessing,
+# the prefix, all 32 blocks and the neck of one image -- a bounded sample of
+# the 64-image step (~30-40 s of CPU work per image on a 16-core host).
+CPU_IMAGES = 1
+
+
+def oracle_encode_timing(model_mod, hp, tensors, n_images: int):
+    """Time the CPU restatement (oracle/) of sam3_encode_image on whole images,
+    all host cores.  Returns (seconds per image, threads, per-image seconds)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle  # noqa: E402  (CPU baseline leg only)
-    hpo = dict(hp, depth=8, global_idx=(7,))
-    tensors = model_mod.random_vit_weights(hpo, seed=7)
-    ov = oracle.OracleVit(hpo, tensors)
-    x = np.random.default_rng(0).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
-    times = {}
-    for b in sample_blocks:
+    import oracle  # noqa: E402  (CPU baseline legs only)
+    ov = oracle.OracleVit(hp, tensors)
+    imgs = model_mod.random_images(n_images, hp["img"], seed=1234)
+    times = []
+    for im in imgs:
         t0 = time.perf_counter()
-        ov.block(b, x)
-        times[b] = time.perf_counter() - t0
-    n_glob = len(hp["global_idx"])
-    per_image = (hp["depth"] - n_glob) * times[sample_blocks[0]] + n_glob * times[sample_blocks[1]]
-    return {"value": 1.0 / per_image, "unit": "images/s", "cores": ov.nt, "kind": "port",
-            "sample": f"oracle ViT block 0 (windowed, {times[0]:.2f} s) and block 7 (global, {times[7]:.2f} s) at "
-                      f"1008^2 / embed 1024 on {ov.nt} threads; per image = 28 x windowed + 4 x global "
-                      f"(prefix and neck not sampled)"}
+        ov.encode(im)
+        times.append(time.perf_counter() - t0)
+    return sum(times) / len(times), ov.nt, times
+
+
+def cpu_baseline(model_mod, hp, tensors):
+    """The CPU restatement (oracle/) of the same encoder, timed on CPU_IMAGES
+    whole images of the step on all host cores (rank 0, N = 1)."""
+    per_image, nt, times = oracle_encode_timing(model_mod, hp, tensors, CPU_IMAGES)
+    return {"value": 1.0 / per_image, "unit": "images/s", "cores": nt, "kind": "port",
+            "sample": f"{len(times)} whole 1008^2 image(s) of the step (preprocess, prefix, 32 blocks, trk neck) "
+                      f"through the oracle/ C restatement on {nt} threads: "
+                      + ", ".join(f"{t:.1f} s" for t in times)}
 
 
 def run_reference(args, hp, model_mod):
+    """The reference's CPU path for the same metric: its ggml CPU backend cannot
+    be built here (empty ggml submodule), so the oracle/ C restatement of its
+    arithmetic runs instead, on all host cores.  One step = one whole image of
+    the 64-image batch; the line reports the images actually encoded."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    cb = cpu_baseline(model_mod, hp)
-    line = {"impl": "reference", "metric": "SAM3 Q8_0 ViT encode images/s", "value": cb["value"],
-            "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": BATCH / cb["value"] * 1000.0, "higher_is_better": True, "scaling": "strong",
+    tensors = model_mod.random_vit_weights(hp, seed=0)
+    n = max(1, min(args.steps, CPU_IMAGES))
+    per_image, nt, times = oracle_encode_timing(model_mod, hp, tensors, n)
+    value = 1.0 / per_image
+    line = {"impl": "reference", "metric": "SAM3 Q8_0 ViT encode images/s", "value": value,
+            "unit": "images/s", "n_gpus": world, "steps": n, "warmup": 0,
+            "ms_per_step": per_image * 1000.0, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "cfg3: SAM3 visual-only ViT-32 + trk neck, Q8_0, 1008x1008, batch 64",
-                       "global_batch": BATCH, "seq_len": 5184, "parallelism": "cpu"},
-            "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "config": {"workload": "cfg3: SAM3 visual-only ViT-32 + trk neck, Q8_0, 1008x1008; one whole image "
+                                   "of the 64-image batch per step",
+                       "global_batch": 1, "seq_len": 5184, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "images/s", "cores": nt, "kind": "port",
+                             "sample": f"{n} whole image(s): " + ", ".join(f"{t:.1f} s" for t in times)},
+            "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's ggml CPU backend cannot be built (ggml submodule empty); this is the "
-                    "oracle/ C restatement of its arithmetic"}
+                    "oracle/ C restatement of its arithmetic (int8 block dots in AVX2, fp32 attention scalar), "
+                    f"requested steps {args.steps} / warm-up {args.warmup} bounded to {n} image(s)"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -235,7 +252,8 @@ def main():
     tensors = model_mod.random_vit_weights(hp, seed=0)
     vit = be.vit(hp)
     vit.load(tensors)
-    del tensors
+    if not (not args.no_cpu_baseline and world == 1 and rank == 0):
+        del tensors
 
     S = hp["img"]
     batch = args.images
@@ -330,7 +348,7 @@ def main():
             "clocks": clk,
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(model_mod, hp)
+            line["cpu_baseline"] = cpu_baseline(model_mod, hp, tensors)
         print(json.dumps(line), flush=True)
     vit.free()
     be.free()

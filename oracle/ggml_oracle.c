@@ -16,6 +16,9 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#if defined(__AVX2__)
+#include <immintrin.h>
+#endif
 
 #define QK 32
 
@@ -226,20 +229,49 @@ int orc_vec_dot_type(int wtype) {
     }
 }
 
-/* Integer dot of block b, and the fp32 scale pieces of that block. */
+#if defined(__AVX2__)
+/* Exact int32 dot of 32 int8 pairs with |a| <= 127 (ggml's x86 form: |a| times
+ * sign(b, a) by maddubs -- pairwise int16 sums of at most 2 * 127 * 128, no
+ * saturation -- then madd against ones and a horizontal sum). */
+static inline int32_t dot32_i8(__m256i a, __m256i b) {
+    const __m256i ax = _mm256_sign_epi8(a, a);
+    const __m256i sb = _mm256_sign_epi8(b, a);
+    const __m256i d32 = _mm256_madd_epi16(_mm256_maddubs_epi16(ax, sb), _mm256_set1_epi16(1));
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(d32), _mm256_extracti128_si256(d32, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4E));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xB1));
+    return _mm_cvtsi128_si32(s);
+}
+#endif
+
+/* Integer dot of block b (exact; the AVX2 form and the scalar loop give the
+ * same int32). */
 static int32_t block_isum(int wtype, const void *w, const void *xq, int64_t b) {
     int32_t s = 0;
     if (wtype == ORC_Q8_0) {
         const blk_q8_0 *wb = (const blk_q8_0 *)w + b;
         const blk_q8_0 *xb = (const blk_q8_0 *)xq + b;
+#if defined(__AVX2__)
+        return dot32_i8(_mm256_loadu_si256((const __m256i *)xb->qs), _mm256_loadu_si256((const __m256i *)wb->qs));
+#else
         for (int j = 0; j < QK; j++) s += (int32_t)wb->qs[j] * xb->qs[j];
+#endif
     } else if (wtype == ORC_Q4_0) {
         const blk_q4_0 *wb = (const blk_q4_0 *)w + b;
         const blk_q8_0 *xb = (const blk_q8_0 *)xq + b;
+#if defined(__AVX2__)
+        /* nibbles -> int8: low nibbles are elements 0..15, high 16..31, minus 8 */
+        const __m128i raw = _mm_loadu_si128((const __m128i *)wb->qs);
+        const __m256i nib = _mm256_and_si256(
+            _mm256_set_m128i(_mm_srli_epi16(raw, 4), raw), _mm256_set1_epi8(0x0F));
+        const __m256i wv = _mm256_sub_epi8(nib, _mm256_set1_epi8(8));
+        return dot32_i8(_mm256_loadu_si256((const __m256i *)xb->qs), wv);
+#else
         for (int j = 0; j < QK / 2; j++) {
             s += ((wb->qs[j] & 0x0F) - 8) * xb->qs[j];
             s += ((wb->qs[j] >> 4) - 8) * xb->qs[j + QK / 2];
         }
+#endif
     } else if (wtype == ORC_Q4_1) {
         const blk_q4_1 *wb = (const blk_q4_1 *)w + b;
         const blk_q8_1 *xb = (const blk_q8_1 *)xq + b;
