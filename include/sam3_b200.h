@@ -65,6 +65,13 @@ const char *sam3b200_backend_name(const sam3b200_backend *be);
 /* Waits for all work queued on the backend; returns FAILED if a kernel
  * reported an error (including a bounded pipeline wait that timed out). */
 int sam3b200_backend_synchronize(sam3b200_backend *be);
+/* Failure-path diagnostic, no counterpart in the reference (its test hooks
+ * exercise stages, sam3.cpp:6218-6998): queues a one-thread kernel that waits
+ * with the pipelines' bounded mbarrier wait, limited to limit_ns (at most
+ * 1 s), on a barrier that nothing arrives on.  The wait runs out, the kernel
+ * records an error code and returns; the next sam3b200_backend_synchronize
+ * returns FAILED and the backend remains usable. */
+int sam3b200_debug_wait_timeout(sam3b200_backend *be, uint64_t limit_ns);
 /* The backend's CUDA stream (cudaStream_t), for callers that time or order
  * work against it. */
 void *sam3b200_backend_stream(sam3b200_backend *be);

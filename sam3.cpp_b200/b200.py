@@ -258,6 +258,7 @@ def lib() -> ctypes.CDLL:
         "sam3b200_backend_name": (ctypes.c_char_p, [vp]),
         "sam3b200_backend_synchronize": (i32, [vp]),
         "sam3b200_backend_stream": (vp, [vp]),
+        "sam3b200_debug_wait_timeout": (i32, [vp, ctypes.c_uint64]),
         "sam3b200_last_error": (ctypes.c_char_p, []),
         "sam3b200_buffer_alloc": (vp, [vp, sz]),
         "sam3b200_buffer_free": (None, [vp, vp]),
@@ -1084,6 +1085,10 @@ class Backend:
 
     def synchronize(self) -> None:
         _check(lib().sam3b200_backend_synchronize(self.h), "synchronize")
+
+    def debug_wait_timeout(self, limit_ns: int) -> None:
+        """sam3b200_debug_wait_timeout: queue a bounded wait that runs out (failure-path test)."""
+        _check(lib().sam3b200_debug_wait_timeout(self.h, limit_ns), "debug_wait_timeout")
 
     def alloc(self, nbytes: int) -> DeviceBuffer:
         return DeviceBuffer(self, nbytes)

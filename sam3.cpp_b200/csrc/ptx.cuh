@@ -71,19 +71,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.  On timeout
-// the error word gets `code` OR-ed in and false is returned.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+// Bounded wait for the phase with the given parity to complete, giving up
+// after limit_ns nanoseconds.  On timeout the error word gets `code` OR-ed in
+// and false is returned.
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, int *err, int code, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     uint32_t it = 0;
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((++it & 255u) == 0u && globaltimer_ns() - t0 > SAM3B200_WAIT_NS) {
+        if ((++it & 255u) == 0u && globaltimer_ns() - t0 > limit_ns) {
             if (err) atomicOr(err, code);
             return false;
         }
     }
+}
+
+// The pipelines' wait: bounded by SAM3B200_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    return mbar_wait_ns(bar, parity, err, code, SAM3B200_WAIT_NS);
 }
 
 // ---- TMA --------------------------------------------------------------------
