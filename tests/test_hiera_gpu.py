@@ -68,14 +68,15 @@ def test_prefix_matches_oracle(backend, hiera_oracle, tiny256):
 
 @pytest.mark.parametrize("img", [256, 1024])
 def test_encode_matches_oracle(oracle, hiera_oracle, backend, img):
-    """Trunk + FPN neck from a preprocessed image: the four stage outputs and the three FPN levels.
+    """Free-running trunk + FPN neck from a preprocessed image: the four stage outputs and the three
+    FPN levels against the oracle's own encode, next to the oracle against itself.
 
     Twelve chained blocks of activation quantisation amplify rounding-level differences (a code
-    that flips costs a full quantisation step downstream), so the end-to-end bound is calibrated
-    on the oracle itself: the GPU may differ from the oracle by at most 1e-2 or twice the spread
-    between two valid oracle evaluations (attention in float64 and in float32), whichever is
-    larger.  Each block in isolation is held to 1e-2 (test_block_matches_oracle), as the
-    reference's own CPU-vs-Metal stage comparison holds isolated stages on shared inputs."""
+    that flips costs a full quantisation step downstream): two equally valid oracle evaluations
+    (attention in float64 and in float32) already differ by up to ~1.7e-2 at 1024x1024.  So the
+    free-running GPU encode is held to 1e-2 or twice that self-divergence, whichever is larger;
+    parity at the fixed 1e-2 bound is checked stage by stage on the GPU's own trajectory
+    (test_encode_every_stage_on_the_gpu_trajectory)."""
     hp = hiera_tiny(img)
     gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=11)
     model = backend.hiera(hp)
@@ -93,6 +94,54 @@ def test_encode_matches_oracle(oracle, hiera_oracle, backend, img):
             bound = max(1e-2, 2 * rel_err(fpn32[lvl], fpn[lvl]))
             err = rel_err(model.output_host(lvl), fpn[lvl])
             assert err <= bound, ("fpn", lvl, err, bound)
+    finally:
+        model.free()
+
+
+@pytest.mark.parametrize("img", [256, 1024])
+def test_encode_every_stage_on_the_gpu_trajectory(oracle, hiera_oracle, backend, img):
+    """sam2_encode_image_hiera (sam3.cpp:5861-6022) stage by stage along the GPU's own trajectory at the
+    fixed 1e-2 bound: the prefix on the image, each of the 12 blocks on the output the GPU produced
+    before it, and the FPN neck on the GPU's four stage outputs -- each against the oracle stage on the
+    same input.  The stepwise path is the encode path: its stage outputs equal encode_device's bit for
+    bit."""
+    hp = hiera_tiny(img)
+    gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=11)
+    model = backend.hiera(hp)
+    try:
+        model.load(gpu)
+        chw = np.random.default_rng(img).normal(0, 1, size=(3, img, img)).astype(np.float32)
+        blocks, ends = hiera_oracle.metadata(hp)
+        S = (img - 1) // 4 + 1
+        dx = backend.alloc(S * S * blocks[0]["dim_in"] * 4)
+        model.run_prefix(backend.upload(chw), dx)
+        backend.synchronize()
+        x = dx.get((S, S, blocks[0]["dim_in"]), np.float32)
+        pe = hiera_oracle.pos_embed(ref["hiera.pos_embed"], ref["hiera.pos_embed_window"], S)
+        errs = {"prefix": rel_err(x, hiera_oracle.prefix(chw, ref["hiera.patch_embed.weight"],
+                                                          ref["hiera.patch_embed.bias"], pe))}
+        stages = []
+        for i, m in enumerate(blocks):
+            p = f"hiera.blocks.{i}."
+            want = hiera_oracle.block(m, {k[len(p):]: v for k, v in ref.items() if k.startswith(p)}, x)
+            So = S // 2 if m["q_stride"] else S
+            out = backend.alloc(So * So * m["dim_out"] * 4)
+            model.run_block(i, backend.upload(x), S, S, out)
+            backend.synchronize()
+            x = out.get((So, So, m["dim_out"]), np.float32)
+            errs[f"block{i}"] = rel_err(x, want)
+            S = So
+            if i in ends:
+                stages.append(x)
+        model.encode_device(backend.upload(chw))
+        for s in range(4):
+            assert np.array_equal(model.output_host(4 + s).reshape(stages[s].shape), stages[s]), s
+        convs = [(ref[f"fpn.convs.{j}.weight"], ref[f"fpn.convs.{j}.bias"]) for j in range(4)]
+        want_fpn = hiera_oracle.fpn(stages, convs, hp["fpn_top_down_levels"], hp["scalp"])
+        for lvl in range(len(want_fpn)):
+            errs[f"fpn{lvl}"] = rel_err(model.output_host(lvl).reshape(want_fpn[lvl].shape), want_fpn[lvl])
+        print("stage errors:", ", ".join(f"{k} {v:.2e}" for k, v in errs.items()))
+        assert max(errs.values()) <= 1e-2, errs
     finally:
         model.free()
 

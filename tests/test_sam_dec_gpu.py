@@ -69,8 +69,11 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
     """Config 1 end to end (SAM2.1 Hiera-tiny, Q8_0, one positive point): uint8 image -> SAM2 preprocessing
     -> Hiera trunk + FPN -> prompt encoder + mask decoder -> masks at the original size.
 
-    Two checks.  (a) The decoder at this geometry, fed the oracle's own FPN features: every final mask at
-    IoU >= 0.99 against the oracle.  (b) The whole chain against the oracle chain: twelve random-init
+    Three checks.  (a) The decoder at this geometry, fed the oracle's own FPN features: every final mask at
+    IoU >= 0.99 against the oracle.  (c) The decoder fed the GPU's own FPN features (the chain's actual
+    hand-off), against the oracle decoder on those same features: every final mask at IoU >= 0.99; with
+    the Hiera encode held to 1e-2 stage by stage on its own trajectory (test_hiera_gpu), every stage of
+    the chain meets the fixed bounds.  (b) The whole chain free-running against the oracle chain: twelve random-init
     quantised Hiera blocks amplify rounding-level differences (see test_hiera_gpu), so two valid oracle
     evaluations (attention in float64 and float32) agree only to IoU 0.98-0.99 on these masks; the GPU
     must agree with the oracle to within twice that disagreement, 1 - 2 (1 - self IoU), and never
@@ -106,6 +109,14 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
         dec.run(enc.output_ptr(2), enc.output_ptr(0), enc.output_ptr(1), point, label, W, Hh, 1024)
         got = [dec.mask(m, W, Hh) for m in range(4)]
         _, iou, _, _ = dec.outputs()
+        # (c) the oracle decoder on the GPU's own FPN features
+        gf = [enc.output_host(lvl) for lvl in range(3)]
+        gf = [np.ascontiguousarray(f.reshape(fpn[lvl].shape)) for lvl, f in enumerate(gf)]
+        masks_g = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024)[0]
+        for m in range(4):
+            ref_g = dec_oracle.resize_threshold(masks_g[m], W, Hh)
+            assert dec_oracle.mask_iou(got[m], ref_g) >= 0.99, ("decoder on the GPU's features", m,
+                                                               dec_oracle.mask_iou(got[m], ref_g))
     finally:
         enc.free()
         dec.free()
