@@ -219,13 +219,16 @@ int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t n
 
 #define SAM3B200_OP_NONE              0 /* leaf: data already on the device */
 #define SAM3B200_OP_VIEW              1 /* VIEW / RESHAPE / PERMUTE / TRANSPOSE: data aliases src[0], nothing runs */
-#define SAM3B200_OP_MUL_MAT           2 /* ggml_mul_mat(src0 = weight, src1 = x) */
+#define SAM3B200_OP_MUL_MAT           2 /* ggml_mul_mat(src0 = weight, src1 = x); src0 either an uploaded weight
+                                           (extra) or an F32 / F16 tensor of the graph (the IM2COL result of
+                                           ggml_conv_2d), src1 then F32 or F16 */
 #define SAM3B200_OP_ADD               3 /* ggml_add, src1 broadcast (ggml_can_repeat); fused into the MUL_MAT before it when it is that MUL_MAT's bias */
 #define SAM3B200_OP_FLASH_ATTN_EXT    4 /* ggml_flash_attn_ext(q, k, v, mask), op_params[0..2] = scale, max_bias, softcap */
 #define SAM3B200_OP_CONV_TRANSPOSE_2D 5 /* ggml_conv_transpose_2d_p0(kernel, x), op_params[0] = stride */
 #define SAM3B200_OP_CONV_2D           6 /* ggml_conv_2d_direct(kernel, x), op_params = s0, s1, p0, p1, d0, d1 */
 #define SAM3B200_OP_GET_ROWS          7 /* ggml_get_rows(rows, I32 indices) */
-#define SAM3B200_OP_CONT              8 /* ggml_cont / ggml_cpy / ggml_cont_Nd: element i of src0 -> element i of dst, each in its own order */
+#define SAM3B200_OP_CONT              8 /* ggml_cont / ggml_cpy / ggml_cont_Nd / ggml_cast: element i of src0 -> element i of
+                                           dst, each in its own order; F32 <-> F16 converts (round to nearest even) */
 #define SAM3B200_OP_MUL               9 /* ggml_mul, src1 broadcast */
 #define SAM3B200_OP_SCALE            10 /* ggml_scale, op_params[0] = s */
 #define SAM3B200_OP_UNARY            11 /* op_params[0] = SAM3B200_UNARY_* */
@@ -233,6 +236,19 @@ int sam3b200_get_rows(sam3b200_backend *be, int type, const void *src, int64_t n
 #define SAM3B200_OP_SOFT_MAX         13 /* ggml_soft_max_ext(a, mask, scale, max_bias 0) over ne0; mask F16 / F32 or none */
 #define SAM3B200_OP_WIN_PART         14 /* ggml_win_part(a, w): op_params = npx, npy, w (sam3.cpp:3734) */
 #define SAM3B200_OP_WIN_UNPART       15 /* ggml_win_unpart(a, W, H, w): op_params[0] = w (sam3.cpp:3788) */
+#define SAM3B200_OP_SUB              16 /* ggml_sub, src1 broadcast (RoPE, sam3.cpp:3704) */
+#define SAM3B200_OP_REPEAT           17 /* ggml_repeat(src0, shape of the result): element i = src0[i mod src0.ne] (sam3.cpp:3825) */
+#define SAM3B200_OP_CONCAT           18 /* ggml_concat(src0, src1, dim): op_params[0] = dim (sam3.cpp:3708) */
+#define SAM3B200_OP_IM2COL           19 /* ggml_im2col(kernel, x, ...): op_params = s0, s1, p0, p1, d0, d1, is_2D; result
+                                           [IC*KH*KW, OW, OH, N] F32 or F16 (ggml_conv_2d, sam3.cpp:3819) */
+#define SAM3B200_OP_POOL_2D          20 /* ggml_pool_2d: op_params = op (0 max, 1 avg), k0, k1, s0, s1, p0, p1 (sam3.cpp:3918) */
+#define SAM3B200_OP_PAD              21 /* ggml_pad / ggml_pad_ext: op_params = lp0, rp0, lp1, rp1, lp2, rp2, lp3, rp3, zeros
+                                           (sam3.cpp:4210) */
+#define SAM3B200_OP_UPSCALE          22 /* ggml_upscale nearest: op_params[0] = mode 0; factors = result ne / src ne (sam3.cpp:4586) */
+#define SAM3B200_OP_CONV_2D_DW       23 /* ggml_conv_2d_dw_direct(kernel [KW, KH, 1, C], x [W, H, C, N]): op_params = s0, s1,
+                                           p0, p1, d0, d1 (sam3.cpp:9089) */
+#define SAM3B200_OP_GROUP_NORM       24 /* ggml_group_norm over ne0 x ne1 x (ne2 / groups): op_params[0] = groups,
+                                           op_params[1] = eps (sam3.cpp:8923) */
 
 #define SAM3B200_UNARY_RELU     1
 #define SAM3B200_UNARY_SIGMOID  2

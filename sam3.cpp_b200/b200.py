@@ -21,7 +21,8 @@ TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
 MMQ_AUTO, MMQ_TC, MMQ_SIMT = 0, 1, 2
 TYPE_I32 = 26
 (OP_NONE, OP_VIEW, OP_MUL_MAT, OP_ADD, OP_FLASH_ATTN_EXT, OP_CONV_TRANSPOSE_2D, OP_CONV_2D, OP_GET_ROWS,
- OP_CONT, OP_MUL, OP_SCALE, OP_UNARY, OP_NORM, OP_SOFT_MAX, OP_WIN_PART, OP_WIN_UNPART) = range(16)
+ OP_CONT, OP_MUL, OP_SCALE, OP_UNARY, OP_NORM, OP_SOFT_MAX, OP_WIN_PART, OP_WIN_UNPART, OP_SUB, OP_REPEAT,
+ OP_CONCAT, OP_IM2COL, OP_POOL_2D, OP_PAD, OP_UPSCALE, OP_CONV_2D_DW, OP_GROUP_NORM) = range(25)
 UNARY_RELU, UNARY_SIGMOID, UNARY_GELU_ERF, UNARY_GELU = 1, 2, 3, 4
 TENSOR_FLAG_OUTPUT = 2
 

@@ -107,6 +107,79 @@ def test_supports_the_forms_sam3_builds(g):
     assert g.supports_op(g.graph_tensor(F32, [64 * 9, 576], op=g.OP_CONT, src=(perm,), data=A))  # ggml_cont_2d
 
 
+def _im2col(g, iw=56, ih=70, ic=3, k=14, s=14, is_2d=1, otype=F16, out=None):
+    """The patch embedding's IM2COL (sam3.cpp:6726): kernel [14, 14, 3, OC] (shape only), image [W, H, 3, 1]."""
+    w = g.graph_tensor(F16, [k, k, 3, 32])
+    x = g.graph_tensor(F32, [iw, ih, ic, 1], data=A)
+    out = out or [3 * k * k, (iw - k) // s + 1, (ih - k) // s + 1, 1]
+    return g.graph_tensor(otype, out, op=g.OP_IM2COL, src=(w, x), op_params=(s, s, 0, 0, 1, 1, is_2d), data=A)
+
+
+def _pool(g, op=0, out=None):
+    x = g.graph_tensor(F32, [12, 10, 16, 1], data=A)
+    return g.graph_tensor(F32, out or [6, 5, 16, 1], op=g.OP_POOL_2D, src=(x,), op_params=(op, 2, 2, 2, 2, 0, 0),
+                          data=A)
+
+
+def _dw(g, ktype=F32, out=None):
+    k = g.graph_tensor(ktype, [3, 3, 1, 32], data=A)
+    x = g.graph_tensor(F32, [20, 18, 32, 1], data=A)
+    return g.graph_tensor(F32, out or [10, 9, 32, 1], op=g.OP_CONV_2D_DW, src=(k, x), op_params=(2, 2, 1, 1, 1, 1),
+                          data=A)
+
+
+def test_supports_the_shape_and_convolution_ops_sam3_builds(g):
+    """The rest of the op set sam3.cpp's graphs use around the hot path: RoPE's SUB and CONCAT
+    (sam3.cpp:3704-3708), REPEAT of a positional embedding (sam3.cpp:3825), the patch embedding as
+    IM2COL + MUL_MAT of two graph tensors (sam3.cpp:6726-6742), attention scores as a batched MUL_MAT
+    (sam3.cpp:8584), max and average pools (sam3.cpp:3918, 4748), PAD (sam3.cpp:4210), nearest UPSCALE
+    (sam3.cpp:4586), the depthwise convolution (sam3.cpp:9089), GROUP_NORM (sam3.cpp:8923) and casts."""
+    x = g.graph_tensor(F32, [64, 20, 4], data=A)
+    assert g.supports_op(g.graph_tensor(F32, [64, 20, 4], op=g.OP_SUB, src=(x, g.graph_tensor(F32, [64], data=A)),
+                                        data=A))
+    assert g.supports_op(g.graph_tensor(F32, [64, 20, 8], op=g.OP_REPEAT, src=(x,), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [128, 20, 4], op=g.OP_CONCAT, src=(x, x), op_params=(0,), data=A))
+    col = _im2col(g)
+    assert g.supports_op(col)
+    for otype in (F32, F16):
+        assert g.supports_op(_im2col(g, otype=otype))
+    patches = g.graph_tensor(F16, [588, 20], data=A)  # the IM2COL result, reshaped 2-D
+    kern = g.graph_tensor(F16, [588, 32], data=A)     # patch_embed_w reshaped [KW*KH*IC, OC]
+    assert g.supports_op(g.graph_tensor(F32, [20, 32], op=g.OP_MUL_MAT, src=(patches, kern), data=A))
+    k = g.graph_tensor(F32, [64, 70, 4, 1], data=A)
+    q = g.graph_tensor(F32, [64, 20, 8, 2], data=A)   # heads broadcast over src0's 4 heads, batch 2 over 1
+    assert g.supports_op(g.graph_tensor(F32, [70, 20, 8, 2], op=g.OP_MUL_MAT, src=(k, q), data=A))
+    assert g.supports_op(_pool(g)) and g.supports_op(_pool(g, op=1))
+    assert g.supports_op(g.graph_tensor(F32, [10, 7], op=g.OP_PAD, src=(g.graph_tensor(F32, [8, 4], data=A),),
+                                        op_params=(0, 2, 1, 2), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [16, 8, 3], op=g.OP_UPSCALE, src=(
+        g.graph_tensor(F32, [8, 4, 3], data=A),), data=A))
+    assert g.supports_op(_dw(g))
+    assert g.supports_op(g.graph_tensor(F32, [8, 8, 32], op=g.OP_GROUP_NORM, src=(
+        g.graph_tensor(F32, [8, 8, 32], data=A),), op_params=(8, g.f32_bits(1e-5)), data=A))
+    assert g.supports_op(g.graph_tensor(F16, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(F32, [8, 4], data=A),), data=A))
+    assert g.supports_op(g.graph_tensor(F32, [32], op=g.OP_CONT, src=(g.graph_tensor(F16, [8, 4], data=A),), data=A))
+
+
+def test_runtime_mul_mat_reads_its_src0_data(g):
+    """A MUL_MAT whose src0 is an F32 / F16 tensor without a weight handle reads src0 from its data: no
+    handle is asked for, and src0 needs its data like any other source."""
+    a = g.graph_tensor(F32, [64, 70], data=A)
+    mm = g.graph_tensor(F32, [70, 20], op=g.OP_MUL_MAT, src=(a, g.graph_tensor(F32, [64, 20], data=A)), data=A)
+    assert g.graph_compute_status(None, [mm]) == g.STATUS_FAILED and "null backend" in g.last_error()
+    a.data = None
+    assert g.graph_compute_status(None, [mm]) == g.STATUS_FAILED
+    assert "node 0 rejected: src0 data" in g.last_error(), g.last_error()
+    a.data = A + 2  # f32 rows need 4-byte alignment
+    assert g.graph_compute_status(None, [mm]) == g.STATUS_FAILED and "not 4-byte aligned" in g.last_error()
+
+
+def test_im2col_reads_only_its_kernels_shape(g):
+    col = _im2col(g)
+    assert col.src[0].contents.data is None
+    assert g.graph_compute_status(None, [col]) == g.STATUS_FAILED and "null backend" in g.last_error()
+
+
 def _not_packed_rows(g):
     mm = _mm(g)
     mm.src[1].contents.nb[0] = 8
@@ -154,8 +227,8 @@ REJECTED = {
         g.graph_tensor(F32, [64, 72, 72], data=A),), op_params=(3, 2, 24), data=A),
     "WIN_UNPART window count": lambda g: g.graph_tensor(F32, [64, 72, 72], op=g.OP_WIN_UNPART, src=(
         g.graph_tensor(F32, [64, 24, 24, 8], data=A),), op_params=(24,), data=A),
-    "CONT type change": lambda g: g.graph_tensor(F16, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(F32, [8, 4], data=A),),
-                                                 data=A),
+    "CONT from I32": lambda g: g.graph_tensor(F32, [8, 4], op=g.OP_CONT, src=(g.graph_tensor(I32, [8, 4], data=A),),
+                                              data=A),
     "CONT element count": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_CONT, src=(
         g.graph_tensor(F32, [8, 4], data=A),), data=A),
     "ADD bias of the wrong length": _bias_of_wrong_length,
@@ -170,6 +243,37 @@ REJECTED = {
     "conv result shape": lambda g: _conv(g, out=[20, 17, 40, 1]),
     "conv zero stride": lambda g: _conv(g, params=(0, 1, 1, 1, 1, 1), out=[20, 18, 40, 1]),
     "conv transpose result shape": lambda g: _convt(g, out=[20, 17, 16, 1]),
+    "runtime MUL_MAT batches that do not broadcast": lambda g: g.graph_tensor(F32, [70, 20, 6], op=g.OP_MUL_MAT,
+        src=(g.graph_tensor(F32, [64, 70, 4], data=A), g.graph_tensor(F32, [64, 20, 6], data=A)), data=A),
+    "runtime MUL_MAT K mismatch": lambda g: g.graph_tensor(F32, [70, 20], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(F16, [64, 70], data=A), g.graph_tensor(F32, [60, 20], data=A)), data=A),
+    "runtime MUL_MAT f16 result": lambda g: g.graph_tensor(F16, [70, 20], op=g.OP_MUL_MAT, src=(
+        g.graph_tensor(F32, [64, 70], data=A), g.graph_tensor(F32, [64, 20], data=A)), data=A),
+    "SUB shape": lambda g: g.graph_tensor(F32, [8, 5], op=g.OP_SUB, src=(
+        g.graph_tensor(F32, [8, 4], data=A), g.graph_tensor(F32, [8], data=A)), data=A),
+    "REPEAT not a multiple": lambda g: g.graph_tensor(F32, [8, 6], op=g.OP_REPEAT, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), data=A),
+    "CONCAT shapes": lambda g: g.graph_tensor(F32, [8, 7], op=g.OP_CONCAT, src=(
+        g.graph_tensor(F32, [8, 4], data=A), g.graph_tensor(F32, [8, 4], data=A)), op_params=(1,), data=A),
+    "CONCAT dim 4": lambda g: g.graph_tensor(F32, [8, 8], op=g.OP_CONCAT, src=(
+        g.graph_tensor(F32, [8, 4], data=A), g.graph_tensor(F32, [8, 4], data=A)), op_params=(4,), data=A),
+    "IM2COL 1-D form": lambda g: _im2col(g, is_2d=0),
+    "IM2COL result shape": lambda g: _im2col(g, out=[588, 4, 4, 1]),
+    "IM2COL channel mismatch": lambda g: _im2col(g, ic=4),
+    "POOL_2D op 2": lambda g: _pool(g, op=2),
+    "POOL_2D result shape": lambda g: _pool(g, out=[5, 5, 16, 1]),
+    "PAD circular": lambda g: g.graph_tensor(F32, [10, 4], op=g.OP_PAD, src=(g.graph_tensor(F32, [8, 4], data=A),),
+                                             op_params=(1, 1, 0, 0, 0, 0, 0, 0, 1), data=A),
+    "PAD result shape": lambda g: g.graph_tensor(F32, [11, 4], op=g.OP_PAD, src=(g.graph_tensor(F32, [8, 4], data=A),),
+                                                 op_params=(1, 1), data=A),
+    "UPSCALE bilinear": lambda g: g.graph_tensor(F32, [16, 8], op=g.OP_UPSCALE, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), op_params=(1,), data=A),
+    "UPSCALE fractional factor": lambda g: g.graph_tensor(F32, [12, 8], op=g.OP_UPSCALE, src=(
+        g.graph_tensor(F32, [8, 4], data=A),), data=A),
+    "CONV_2D_DW f16 kernel": lambda g: _dw(g, ktype=F16),
+    "CONV_2D_DW result shape": lambda g: _dw(g, out=[20, 20, 32, 1]),
+    "GROUP_NORM zero groups": lambda g: g.graph_tensor(F32, [8, 8, 32], op=g.OP_GROUP_NORM, src=(
+        g.graph_tensor(F32, [8, 8, 32], data=A),), op_params=(0, g.f32_bits(1e-5)), data=A),
     "get_rows f32 indices": lambda g: _rows(g, itype=F32),
     "get_rows Q4_0 with 48 columns": lambda g: _rows(g, Q4_0, ncols=48),
 }

@@ -288,3 +288,183 @@ def test_window_partition_graph(b200, backend):
     ref = np.stack([xp[py * w:(py + 1) * w, px * w:(px + 1) * w] for py in range(npy) for px in range(npx)])
     assert np.array_equal(dwin.get(ref.shape, np.float32), ref)
     assert np.array_equal(dback.get(x.shape, np.float32), x)
+
+
+def test_layout_ops_graph(b200, backend):
+    """SUB with a broadcast row (RoPE, sam3.cpp:3704), REPEAT (sam3.cpp:3825), CONCAT along dims 0 and 1
+    (sam3.cpp:3708, 8278), zero PAD on both sides (sam3.cpp:4210), nearest 2x UPSCALE (sam3.cpp:4586) and
+    the F32 <-> F16 casts, each bit for bit against numpy."""
+    rng = np.random.default_rng(21)
+    x = rng.normal(0, 1, size=(3, 5, 8)).astype(np.float32)   # ggml [8, 5, 3]
+    y = rng.normal(0, 1, size=(3, 5, 8)).astype(np.float32)
+    row = rng.normal(0, 1, size=8).astype(np.float32)
+    dx, dy, drow = backend.upload(x), backend.upload(y), backend.upload(row)
+    t_x, t_y = b200.graph_tensor(F32, [8, 5, 3], data=dx.ptr), b200.graph_tensor(F32, [8, 5, 3], data=dy.ptr)
+    t_row = b200.graph_tensor(F32, [8], data=drow.ptr)
+    out = {}
+
+    def node(name, ttype, ne, op, src, params=(), nbytes=None):
+        count = int(np.prod(ne))
+        buf = backend.alloc(nbytes or count * (2 if ttype == F16 else 4))
+        out[name] = (buf, ne, ttype)
+        return b200.graph_tensor(ttype, ne, op=op, src=src, op_params=params, data=buf.ptr)
+
+    nodes = [
+        node("sub", F32, [8, 5, 3], b200.OP_SUB, (t_x, t_row)),
+        node("repeat", F32, [16, 5, 6], b200.OP_REPEAT, (t_x,)),
+        node("cat0", F32, [16, 5, 3], b200.OP_CONCAT, (t_x, t_y), (0,)),
+        node("cat1", F32, [8, 10, 3], b200.OP_CONCAT, (t_x, t_y), (1,)),
+        node("pad", F32, [11, 9, 3], b200.OP_PAD, (t_x,), (1, 2, 0, 4, 0, 0, 0, 0)),
+        node("up", F32, [16, 10, 3], b200.OP_UPSCALE, (t_x,), (0,)),
+        node("to16", F16, [8, 5, 3], b200.OP_CONT, (t_x,)),
+    ]
+    nodes.append(node("to32", F32, [8, 5, 3], b200.OP_CONT, (nodes[-1],)))
+    backend.graph_compute(nodes)
+
+    def get(name):
+        buf, ne, ttype = out[name]
+        return buf.get(tuple(reversed(ne)), np.float16 if ttype == F16 else np.float32)
+
+    assert np.array_equal(_bits(get("sub")), _bits(x - row))
+    assert np.array_equal(get("repeat"), np.tile(x, (2, 1, 2)))
+    assert np.array_equal(get("cat0"), np.concatenate([x, y], axis=2))
+    assert np.array_equal(get("cat1"), np.concatenate([x, y], axis=1))
+    assert np.array_equal(get("pad"), np.pad(x, ((0, 0), (0, 4), (1, 2))))
+    assert np.array_equal(get("up"), x.repeat(2, axis=1).repeat(2, axis=2))
+    assert np.array_equal(get("to16"), x.astype(np.float16))
+    assert np.array_equal(get("to32"), x.astype(np.float16).astype(np.float32))
+
+
+def _im2col_ref(x, KW, KH, s0, s1, p0, p1, d0, d1):
+    """x [N, C, H, W] -> [N, OH, OW, C*KH*KW] (ggml's IM2COL element order), zero outside the image."""
+    N, C, H, W = x.shape
+    OW = (W + 2 * p0 - d0 * (KW - 1) - 1) // s0 + 1
+    OH = (H + 2 * p1 - d1 * (KH - 1) - 1) // s1 + 1
+    xp = np.zeros((N, C, H + 2 * p1 + s1 * OH + d1 * KH, W + 2 * p0 + s0 * OW + d0 * KW), x.dtype)
+    xp[:, :, p1:p1 + H, p0:p0 + W] = x
+    col = np.zeros((N, OH, OW, C, KH, KW), x.dtype)
+    for ky in range(KH):
+        for kx in range(KW):
+            col[:, :, :, :, ky, kx] = xp[:, :, ky * d1:ky * d1 + s1 * OH:s1, kx * d0:kx * d0 + s0 * OW:s0].transpose(0, 2, 3, 1)
+    return col.reshape(N, OH, OW, C * KH * KW)
+
+
+def test_im2col_and_mul_mat_of_graph_tensors(b200, backend):
+    """The patch embedding as sam3.cpp:6726-6742 builds it: IM2COL of the image into F16 columns, then a
+    MUL_MAT of that graph tensor (src0) with the F16 kernel reshaped to [KW*KH*IC, OC] (src1) -- the
+    fp16 tensor-core path, K = 588 zero-padded to 592.  The columns are bit-exact; the product is
+    checked against float64 of the same fp16 operands at 1e-5 of the largest output."""
+    rng = np.random.default_rng(22)
+    IC, H, W, KH, KW, OC = 3, 140, 126, 14, 14, 160
+    img = rng.normal(0, 1, size=(1, IC, H, W)).astype(np.float32)
+    kern = (rng.normal(0, 0.05, size=(OC, IC, KH, KW))).astype(np.float16)
+    d_img, d_k = backend.upload(img), backend.upload(kern)
+    OH, OW, K = H // KH, W // KW, IC * KH * KW
+    cols = backend.alloc(OH * OW * K * 2)
+    res = backend.alloc(OC * OH * OW * 4)
+    t_k = b200.graph_tensor(F16, [KW, KH, IC, OC], data=d_k.ptr)
+    t_img = b200.graph_tensor(F32, [W, H, IC, 1], data=d_img.ptr)
+    t_col = b200.graph_tensor(F16, [K, OW, OH, 1], op=b200.OP_IM2COL, src=(t_k, t_img),
+                              op_params=(KW, KH, 0, 0, 1, 1, 1), data=cols.ptr)
+    t_col2 = b200.graph_tensor(F16, [K, OW * OH], op=b200.OP_VIEW, src=(t_col,), data=cols.ptr)
+    t_k2 = b200.graph_tensor(F16, [K, OC], op=b200.OP_VIEW, src=(t_k,), data=d_k.ptr)
+    t_mm = b200.graph_tensor(F32, [OW * OH, OC], op=b200.OP_MUL_MAT, src=(t_col2, t_k2), data=res.ptr)
+    before = backend.launches
+    backend.graph_compute([t_col, t_col2, t_k2, t_mm])
+    assert backend.launches - before == 4  # IM2COL, two fp16 operand packs, the tensor-core GEMM
+    col_ref = _im2col_ref(img, KW, KH, KW, KH, 0, 0, 1, 1).astype(np.float16)
+    assert np.array_equal(cols.get((OH * OW, K), np.float16), col_ref.reshape(OH * OW, K))
+    ref = kern.reshape(OC, K).astype(np.float64) @ col_ref.reshape(OH * OW, K).astype(np.float64).T  # [OC, OH*OW]
+    got = res.get((OC, OH * OW), np.float32)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("otype", [F32, F16])
+def test_im2col_padding_stride_dilation(b200, backend, otype):
+    """A 3 x 3 IM2COL with stride 2, padding 1 and dilation 2 over an odd-sized map of 5 channels and 2
+    images: every column element, zero where the window leaves the image."""
+    rng = np.random.default_rng(23)
+    N, C, H, W, s, p, d = 2, 5, 13, 11, 2, 1, 2
+    x = rng.normal(0, 1, size=(N, C, H, W)).astype(np.float32)
+    dx = backend.upload(x)
+    ref = _im2col_ref(x, 3, 3, s, s, p, p, d, d)
+    buf = backend.alloc(ref.size * (2 if otype == F16 else 4))
+    t_k = b200.graph_tensor(F16, [3, 3, C, 7])
+    t_x = b200.graph_tensor(F32, [W, H, C, N], data=dx.ptr)
+    t = b200.graph_tensor(otype, [C * 9, ref.shape[2], ref.shape[1], N], op=b200.OP_IM2COL, src=(t_k, t_x),
+                          op_params=(s, s, p, p, d, d, 1), data=buf.ptr)
+    backend.graph_compute([t])
+    dt = np.float16 if otype == F16 else np.float32
+    assert np.array_equal(buf.get(ref.shape, dt), ref.astype(dt))
+
+
+def test_batched_mul_mat_of_graph_tensors(b200, backend):
+    """Attention scores as the decoder builds them (ggml_mul_mat(K, Q), sam3.cpp:8584, 10218): F32 src0
+    [64, 70, 4 heads, 1] broadcast over src1 [64, 20, 8, 2]; then F16 src0 with a batch (src1 rounded to
+    fp16 first, ggml-cpu's rule) and a 2-D F32 product of odd sizes.  fp32 FMA accumulation against
+    float64: within 1e-5 of the largest output."""
+    rng = np.random.default_rng(24)
+    cases = [((1, 4, 70, 64), np.float32, (2, 8, 20, 64)), ((1, 3, 33, 40), np.float16, (1, 6, 65, 40)),
+             ((1, 1, 129, 77), np.float32, (1, 1, 131, 77))]
+    for sa, dta, sb in cases:
+        a = rng.normal(0, 1, size=sa).astype(dta)
+        b = rng.normal(0, 1, size=sb).astype(np.float32)
+        da, db = backend.upload(a), backend.upload(b)
+        ne_a, ne_b = list(reversed(sa)), list(reversed(sb))
+        ne_o = [ne_a[1], ne_b[1], ne_b[2], ne_b[3]]
+        o = backend.alloc(int(np.prod(ne_o)) * 4)
+        t_a = b200.graph_tensor(F16 if dta == np.float16 else F32, ne_a, data=da.ptr)
+        t_b = b200.graph_tensor(F32, ne_b, data=db.ptr)
+        t = b200.graph_tensor(F32, ne_o, op=b200.OP_MUL_MAT, src=(t_a, t_b), data=o.ptr)
+        backend.graph_compute([t])
+        bb = b.astype(np.float16) if dta == np.float16 else b
+        r2, r3 = sb[1] // sa[1], sb[0] // sa[0]
+        aa = np.repeat(np.repeat(a.astype(np.float64), r2, axis=1), r3, axis=0)
+        ref = np.einsum("xynk,xymk->xymn", aa, bb.astype(np.float64))
+        got = o.get(ref.shape, np.float32)
+        assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max(), sa
+
+
+def test_pool_dw_conv_group_norm_graph(b200, backend):
+    """Max pool 2x2/2 (sam3.cpp:3918) and an average pool with padding (sam3.cpp:4748 pools whole maps),
+    the depthwise 3x3 convolution with stride 2, padding 1 (sam3.cpp:4777), and GROUP_NORM(8) of 32
+    channels (sam3.cpp:8923), against numpy."""
+    rng = np.random.default_rng(25)
+    N, C, H, W = 2, 32, 15, 18
+    x = rng.normal(0, 2, size=(N, C, H, W)).astype(np.float32)
+    kdw = rng.normal(0, 0.3, size=(C, 1, 3, 3)).astype(np.float32)
+    dx, dk = backend.upload(x), backend.upload(kdw)
+    t_x = b200.graph_tensor(F32, [W, H, C, N], data=dx.ptr)
+    t_k = b200.graph_tensor(F32, [3, 3, 1, C], data=dk.ptr)
+    bmax, bavg = backend.alloc(N * C * 7 * 9 * 4), backend.alloc(N * C * 8 * 6 * 4)
+    bdw, bgn = backend.alloc(N * C * 8 * 9 * 4), backend.alloc(x.nbytes)
+    nodes = [
+        b200.graph_tensor(F32, [9, 7, C, N], op=b200.OP_POOL_2D, src=(t_x,), op_params=(0, 2, 2, 2, 2, 0, 0),
+                          data=bmax.ptr),
+        b200.graph_tensor(F32, [6, 8, C, N], op=b200.OP_POOL_2D, src=(t_x,), op_params=(1, 3, 3, 3, 2, 1, 1),
+                          data=bavg.ptr),
+        b200.graph_tensor(F32, [9, 8, C, N], op=b200.OP_CONV_2D_DW, src=(t_k, t_x), op_params=(2, 2, 1, 1, 1, 1),
+                          data=bdw.ptr),
+        b200.graph_tensor(F32, [W, H, C, N], op=b200.OP_GROUP_NORM, src=(t_x,), op_params=(8, b200.f32_bits(1e-5)),
+                          data=bgn.ptr),
+    ]
+    backend.graph_compute(nodes)
+    # max pool 2x2 stride 2: floor((18 - 2) / 2) + 1 = 9, (15 - 2) // 2 + 1 = 7
+    mx = x[:, :, :14, :18].reshape(N, C, 7, 2, 9, 2).max(axis=(3, 5))
+    assert np.array_equal(bmax.get(mx.shape, np.float32), mx)
+    # average 3x3, stride (3, 2), padding 1, divided by 9 whatever the overlap
+    xp = np.zeros((N, C, H + 2, W + 2), np.float64)
+    xp[:, :, 1:-1, 1:-1] = x
+    avg = np.zeros((N, C, 8, 6))
+    for oy in range(8):
+        for ox in range(6):
+            avg[:, :, oy, ox] = xp[:, :, 2 * oy:2 * oy + 3, 3 * ox:3 * ox + 3].sum(axis=(2, 3)) / 9
+    np.testing.assert_allclose(bavg.get(avg.shape, np.float32), avg, rtol=1e-5, atol=1e-6)
+    dw = np.zeros((N, C, 8, 9))
+    for ky in range(3):
+        for kx in range(3):
+            dw += xp[:, :, ky:ky + 16:2, kx:kx + 18:2] * kdw[None, :, 0, ky, kx, None, None]
+    np.testing.assert_allclose(bdw.get(dw.shape, np.float32), dw, rtol=1e-5, atol=1e-5)
+    g = x.reshape(N, 8, -1).astype(np.float64)
+    gn = ((g - g.mean(-1, keepdims=True)) / np.sqrt(g.var(-1, keepdims=True) + 1e-5)).reshape(x.shape)
+    np.testing.assert_allclose(bgn.get(x.shape, np.float32), gn, rtol=1e-5, atol=1e-5)
