@@ -87,11 +87,19 @@ void sam3b200_buffer_free(sam3b200_backend *be, void *ptr);
  * 6119, 10930). */
 int sam3b200_tensor_set(sam3b200_backend *be, void *dev, const void *host, size_t offset, size_t size);
 int sam3b200_tensor_get(sam3b200_backend *be, const void *dev, void *host, size_t offset, size_t size);
+/* ggml_backend_tensor_memset / ggml_backend_buffer_clear: bytes [offset, offset + size) of device
+ * memory at ptr set to `value`, synchronously. */
+int sam3b200_tensor_memset(sam3b200_backend *be, void *dev, int value, size_t offset, size_t size);
+/* ggml_backend_dev_get_memory / ggml_backend_dev_count: free and total bytes of a GPU, GPUs visible. */
+int sam3b200_device_memory(int device, size_t *free_bytes, size_t *total_bytes);
+int sam3b200_device_count(int *count);
 
 /* Upload one 2-D weight tensor in ggml layout: ne0 = K (contiguous, a
  * multiple of 32) by ne1 = N rows of `type` (Q8_0 or Q4_0), as
  * sam3_load_tensors does with ggml_backend_tensor_set (sam3.cpp:3155-3185).
- * The backend keeps the weight in its tensor-core layout.  NULL on error. */
+ * The blocks may be in host memory or in device memory of this backend's GPU
+ * (a weight already in a device buffer).  The backend keeps the weight in its
+ * tensor-core layout.  NULL on error. */
 sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *be, int type, const void *host_blocks, int64_t ne0,
                                         int64_t ne1);
 void sam3b200_weight_free(sam3b200_backend *be, sam3b200_weight *w);

@@ -211,6 +211,43 @@ int sam3b200_tensor_get(sam3b200_backend *h, const void *dev, void *host, size_t
     return SAM3B200_STATUS_SUCCESS;
 }
 
+extern "C" int sam3b200_tensor_memset(sam3b200_backend *h, void *dev, int value, size_t offset, size_t size) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be || (!dev && size)) {
+        set_error("tensor_memset: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (size == 0) return SAM3B200_STATUS_SUCCESS;
+    cudaSetDevice(be->device);
+    if (!cuda_ok(cudaMemsetAsync(static_cast<char *>(dev) + offset, value & 0xff, size, be->stream), "tensor_memset") ||
+        !cuda_ok(cudaStreamSynchronize(be->stream), "tensor_memset sync"))
+        return SAM3B200_STATUS_FAILED;
+    return SAM3B200_STATUS_SUCCESS;
+}
+
+extern "C" int sam3b200_device_memory(int device, size_t *free_bytes, size_t *total_bytes) {
+    if (!free_bytes || !total_bytes) {
+        set_error("device_memory: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    int prev = 0;
+    cudaGetDevice(&prev);
+    const bool ok = cuda_ok(cudaSetDevice(device), "cudaSetDevice") &&
+                    cuda_ok(cudaMemGetInfo(free_bytes, total_bytes), "cudaMemGetInfo");
+    cudaSetDevice(prev);
+    return ok ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+extern "C" int sam3b200_device_count(int *count) {
+    if (!count) {
+        set_error("device_count: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    *count = 0;
+    return cuda_ok(cudaGetDeviceCount(count), "cudaGetDeviceCount") ? SAM3B200_STATUS_SUCCESS
+                                                                     : SAM3B200_STATUS_FAILED;
+}
+
 sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const void *host_blocks, int64_t ne0,
                                         int64_t ne1) {
     auto *be = reinterpret_cast<Backend *>(h);
@@ -244,11 +281,11 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
         const size_t elems = static_cast<size_t>(N) * K;
         ok = cuda_ok(cudaMalloc(&w->dense, elems * 2), "cudaMalloc(dense weight)");
         if (ok && type == SAM3B200_TYPE_F16) {
-            ok = cuda_ok(cudaMemcpyAsync(w->dense, host_blocks, elems * 2, cudaMemcpyHostToDevice, be->stream),
+            ok = cuda_ok(cudaMemcpyAsync(w->dense, host_blocks, elems * 2, cudaMemcpyDefault, be->stream),
                          "weight upload");
         } else if (ok) {
             ok = cuda_ok(cudaMalloc(&raw, elems * 4), "cudaMalloc(weight staging)") &&
-                 cuda_ok(cudaMemcpyAsync(raw, host_blocks, elems * 4, cudaMemcpyHostToDevice, be->stream),
+                 cuda_ok(cudaMemcpyAsync(raw, host_blocks, elems * 4, cudaMemcpyDefault, be->stream),
                          "weight upload") &&
                  cuda_ok(f32_rows_to_f16(static_cast<const float *>(raw), K, N, K, w->dense, be->stream), "to f16");
         }
@@ -264,7 +301,7 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
              cuda_ok(cudaMemsetAsync(w->quads, 0, quad_bytes, be->stream), "memset scale quads") &&
              (type != SAM3B200_TYPE_Q4_1 || (cuda_ok(cudaMalloc(&w->mins, min_bytes), "cudaMalloc(weight minima)") &&
                                              cuda_ok(cudaMemsetAsync(w->mins, 0, min_bytes, be->stream), "memset"))) &&
-             cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyHostToDevice, be->stream),
+             cuda_ok(cudaMemcpyAsync(raw, host_blocks, raw_bytes, cudaMemcpyDefault, be->stream),
                      "weight upload") &&
              cuda_ok(repack_weight_blocks(type, raw, N, K, w->codes, w->quads, w->ld, be->stream, w->mins),
                      "weight repack") &&

@@ -54,3 +54,24 @@ def rel_err(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+@pytest.fixture(scope="session")
+def ggml_caller(b200, tmp_path_factory):
+    """tests/ggml_vit_block.cpp built as C++14 against the ggml-compatible headers and linked with the
+    B200 ggml backend (libggml_b200.so) and the ggml core stand-in (libggml_mini.so)."""
+    import ctypes
+    import shutil
+    import subprocess
+    if shutil.which("g++") is None:
+        pytest.skip("g++ not installed")
+    b200.lib()  # fails loudly if the library was not built
+    pkg = os.path.join(ROOT, "sam3.cpp_b200")
+    for name in ("libggml_b200.so", "libggml_mini.so"):
+        if not os.path.exists(os.path.join(pkg, name)):
+            raise RuntimeError(f"{name} is not built: run make -C sam3.cpp_b200")
+    so = str(tmp_path_factory.mktemp("ggml") / "libggml_vit_block.so")
+    subprocess.run(["g++", "-std=c++14", "-Wall", "-Wextra", "-Werror", "-shared", "-fPIC", "-I",
+                    os.path.join(pkg, "ggml"), os.path.join(ROOT, "tests", "ggml_vit_block.cpp"), "-L", pkg,
+                    "-lggml_b200", "-lggml_mini", "-lsam3_b200", f"-Wl,-rpath,{pkg}", "-o", so], check=True)
+    return ctypes.CDLL(so)
