@@ -16,7 +16,8 @@ tracker SimpleFPN neck -- the whole of sam3_encode_image.
           device, as in sam3.cpp:6138-6149)
 
 python bench.py [--gpus N --steps K --warmup W] [--impl reference]
-python bench.py --workload pcs|video   (secondary lines: config 4 detector / config 5 tracker stages, 1 GPU)
+python bench.py --workload video       (config 5: Hiera-B+ video tracking frames/s, one stream per GPU, 1..8 GPUs)
+python bench.py --workload pcs|memory  (secondary lines: config 4 detector / config 5 memory stages, 1 GPU)
 python bench.py --workload mmq         (config 2: MUL_MAT sweep, Q8_0 / Q4_0 at the four ViT shapes, 1 GPU)
 """
 from __future__ import annotations
@@ -190,6 +191,168 @@ def run_reference(args, hp, model_mod):
     return 0
 
 
+VIDEO_FRAMES = 16
+VIDEO_SIDE = 1024
+VIDEO_BOX = ([[260.0, 300.0], [700.0, 760.0]], [2, 3])
+
+
+def video_attention_flop(N: int, D: int, frame: int, num_maskmem: int = 7, max_ptrs: int = 16,
+                         layers: int = 4) -> int:
+    """q k^T + p v FLOPs of the memory attention on propagated frame `frame` (1-based) of a stream whose
+    frame 0 was prompted: min(frame, 7) memory slots of N tokens and min(frame, 16) pointers of 4 tokens."""
+    M = min(frame, num_maskmem) * N + 4 * min(frame, max_ptrs)
+    return layers * (4 * N * N * D + 4 * N * M * D)
+
+
+def run_video(args, model_mod) -> int:
+    """Config 5: SAM2.1 Hiera-base+ video tracking, one stream of 16 seeded 1024^2 frames per GPU, a seeded
+    box prompt on frame 0, 7 memory slots, 16 object pointers (Q8_0 weights, random-init).  One step =
+    one whole stream on every rank: frame 0 encoded and prompted (sam3_tracker_add_instance), frames
+    1..15 encoded and propagated (sam3_propagate_frame's device work)."""
+    import torch
+    import torch.distributed as dist
+    b200 = _load("b200")
+    comp = _load("component_bench")
+    shard = _load("shard")
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    be = b200.Backend(local)
+    hp_h = model_mod.SAM2_HIERA_BASE_PLUS
+    H, D, MD = hp_h["img"] // 16, 256, 64
+    N = H * H
+    enc = be.hiera(hp_h)
+    enc.load(comp.hiera_weights(model_mod, enc, hp_h))
+    dec = be.sam_decoder(dict(feat_size=H, embed=D, depth=2, heads=8, mlp_dim=2048, n_multimask=3, pred_obj_scores=1,
+                              max_points=16))
+    dec.load(comp.sam_dec_weights(model_mod))
+    attn_t, enc_t = comp.video_weights(model_mod)
+    attn = be.mem_attention(dict(d_model=D, mem_dim=MD, layers=4, ffn_dim=2048, max_tokens=N,
+                                 max_mem_tokens=7 * N + 16 * (D // MD)))
+    attn.load(attn_t)
+    menc = be.mem_encoder(dict(feat=H, img=hp_h["img"], d_model=D, mem_dim=MD, fuser_layers=2, fuser_dim=1024,
+                               sigmoid_scale=20.0, sigmoid_bias=-10.0, max_mask=(4 * H) ** 2))
+    menc.load(enc_t)
+    tr = be.tracker(dict(feat=H, img=hp_h["img"], d_model=D, mem_dim=MD, num_maskmem=7, max_obj_ptrs=16,
+                         multimask_in_sam=1, multimask_token_for_obj_ptr=1, fixed_no_obj_ptr=1, max_instances=4,
+                         max_keep_alive=100), enc, dec, attn, menc)
+    tr.load(comp.tracker_weights())
+    S = VIDEO_SIDE
+    frames = model_mod.random_images(VIDEO_FRAMES, S, seed=5000 + rank)  # this rank's stream
+    dev_frames = [be.upload(f) for f in frames]
+    pinned = torch.from_numpy(frames).pin_memory()
+    chw = be.alloc(3 * hp_h["img"] ** 2 * 4)
+    mask_dev = be.alloc(S * S)
+    mask_host = torch.empty((S, S), dtype=torch.uint8).pin_memory()
+    stream = torch.cuda.ExternalStream(be.stream)
+    lib = b200.lib()
+    box, labels = VIDEO_BOX
+
+    def stream_device():
+        tr.reset()
+        iid = None
+        for f in range(VIDEO_FRAMES):
+            be.preprocess_sam2(dev_frames[f], S, S, hp_h["img"], chw)
+            tr.encode(chw)
+            if f == 0:
+                iid = tr.add_instance(box, labels, S, S)
+            else:
+                tr.propagate()
+        b200._check(lib.sam3b200_tracker_mask(tr.h, iid, S, S, mask_dev.ptr), "tracker_mask")
+
+    def stream_e2e():
+        tr.reset()
+        iid = None
+        for f in range(VIDEO_FRAMES):
+            tr.encode_image(pinned[f].data_ptr(), S, S)
+            if f == 0:
+                iid = tr.add_instance(box, labels, S, S)
+            else:
+                tr.propagate()
+            b200._check(lib.sam3b200_tracker_mask(tr.h, iid, S, S, mask_dev.ptr), "tracker_mask")
+            b200._check(lib.sam3b200_tensor_get(be.h, mask_dev.ptr, mask_host.data_ptr(), 0, S * S), "mask get")
+
+    def barrier():
+        be.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, k):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        be.synchronize()
+        torch.cuda.synchronize()
+        ms = shard.max_over_ranks(e0.elapsed_time(e1), device=torch.device("cuda", local))
+        barrier()
+        return ms
+
+    for _ in range(args.warmup):
+        stream_device()
+    barrier()
+    clocks = ClockSampler(local, os.path.join(tempfile.gettempdir(), f"sam3b200_video_clocks_{os.getpid()}_{rank}.csv"))
+    launches0 = be.launches
+    be.profile(True)
+    ms = timed(stream_device, args.steps)
+    attn_ms, attn_n = be.profile_read(1)
+    be.profile(False)
+    launches = be.launches - launches0
+    clk = clocks.stop()
+    stream_e2e()
+    e2e_ms = timed(stream_e2e, args.steps)
+    total_frames = VIDEO_FRAMES * world * args.steps
+    attn_flop = sum(video_attention_flop(N, D, f) for f in range(1, VIDEO_FRAMES)) * args.steps
+    achieved = attn_flop / (attn_ms / 1e3) / 1e12 if attn_ms else None
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    peak = peaks.get("bf16_tflops") or 1590.0
+    if rank == 0:
+        line = {
+            "metric": "SAM2.1 Hiera-B+ video tracking frames/s",
+            "value": total_frames / (ms / 1e3), "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 linear / fp16 attention", "data": "synthetic",
+            "config": {"workload": "cfg5: SAM2.1 Hiera-base+ tracker, one stream of 16 seeded 1024^2 uint8 frames "
+                                   "per GPU, box prompt on frame 0, 7 memory slots, 16 object pointers; a step is "
+                                   "one whole stream per rank", "frames_per_stream": VIDEO_FRAMES,
+                       "parallelism": f"one stream per GPU x{world}",
+                       "weights": "random-init, Q8_0 linear weights (reference quantiser rule), F32 convolutions",
+                       "l2": "no flush: per-frame working set (Hiera-B+ weights + the 28,736-token memory) exceeds "
+                             "the 126 MB L2"},
+            "e2e": {"value": total_frames / (e2e_ms / 1e3), "unit": "frames/s",
+                    "h2d_bytes_per_step": int(VIDEO_FRAMES * S * S * 3 * world),
+                    "d2h_bytes_per_step": int(VIDEO_FRAMES * S * S * world)},
+            "roofline": {"kernel": "memory attention's attention kernels (fp16 mma.sync, split over keys)",
+                         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if achieved else None, "traffic": None,
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops (dense fp16 runs at the bf16 rate)"
+                         if peaks.get("bf16_tflops") else "fallback 1.59 PFLOP/s",
+                         "flop_per_stream": attn_flop // args.steps, "launches_timed": attn_n,
+                         "kernel_ms_per_step": attn_ms / args.steps},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "cpu_baseline": None,
+            "cpu_baseline_note": "not measured for this secondary line: the oracle chain needs minutes per "
+                                 "full-size frame (the memory attention alone is ~0.55 TFLOP per frame)",
+        }
+        print(json.dumps(line), flush=True)
+    for x in (tr, enc, dec, attn, menc):
+        x.free()
+    be.free()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -197,7 +360,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video", "mmq"],
+    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video", "memory", "mmq"],
                     help="encode (default: the headline, config 3); pcs / video: the config 4 detector or the "
                          "config 5 tracker memory stages, timed per image / frame (sam3.cpp_b200/component_bench.py)")
     ap.add_argument("--images", type=int, default=BATCH,
@@ -229,7 +392,9 @@ def main():
         print(json.dumps(line), flush=True)
         be.free()
         return 0
-    if args.workload != "encode":
+    if args.workload == "video":
+        return run_video(args, model_mod)
+    if args.workload in ("pcs", "memory"):
         b200 = _load("b200")
         comp = _load("component_bench")
         be = b200.Backend(0)

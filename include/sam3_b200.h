@@ -127,8 +127,9 @@ long long sam3b200_backend_launch_count(const sam3b200_backend *be);
 /* Per-kernel-class timing, the analogue of the reference's timed sub-graph
  * profiling helper (sam3.cpp:5041-5094): while enabled, CUDA events are
  * recorded on the backend stream around every launch of class 0 (the
- * quantised MUL_MAT); profile_read syncs and returns their summed time and
- * count.  Enabling resets the record. */
+ * quantised MUL_MAT) and class 1 (the tracker memory attention's attention
+ * kernels); profile_read syncs and returns their summed time and count.
+ * Enabling resets the record. */
 int sam3b200_backend_profile(sam3b200_backend *be, int enable);
 int sam3b200_backend_profile_read(sam3b200_backend *be, int cls, double *total_ms, int *n);
 
@@ -376,6 +377,16 @@ int sam3b200_sam_dec_missing(sam3b200_sam_dec *d, char *buf, int cap);
 int sam3b200_sam_dec_run(sam3b200_sam_dec *d, const float *img_feats_dev, const float *feat_s0_dev,
                          const float *feat_s1_dev, const float *coords, const int32_t *labels, int n_prompts,
                          int orig_w, int orig_h, int img_size);
+/* The decode of a propagated video frame (sam3_propagate_single,
+ * sam3.cpp:11312-11347): the memory-conditioned features [H*H][256] (the
+ * memory attention's output) without no_mem_embed, no user prompt -- the
+ * single not_a_point padding token -- and the same high-resolution maps.
+ * Synchronous like sam3b200_sam_dec_run. */
+int sam3b200_sam_dec_run_tracking(sam3b200_sam_dec *d, const float *cond_feats_dev, const float *feat_s0_dev,
+                                  const float *feat_s1_dev);
+/* Output token of mask m (0 .. n_multimask) of the last run, device [256]:
+ * the decoder's mask_tokens output (token 0 is the SAM output token). */
+int sam3b200_sam_dec_mask_token(sam3b200_sam_dec *d, int m, const float **dev);
 /* Results of the last run: mask logits [n_multimask + 1][(4H)^2] (device),
  * IoU predictions, object-score logit, SAM output token [256] (device). */
 int sam3b200_sam_dec_outputs(sam3b200_sam_dec *d, const float **masks_dev, float iou[4], float *obj_logit,
@@ -575,6 +586,75 @@ int sam3b200_mem_enc_run_device(sam3b200_mem_enc *m, const float *mask_logits, i
                                 const float *pix_feat, float obj_score);
 /* Memory features: device f32 [mem_dim, H, H] (memory [H*H][mem_dim]). */
 int sam3b200_mem_enc_output(sam3b200_mem_enc *m, const float **dev);
+
+/* ---- Video tracker frame loop (visual-only models) ------------------------
+ * sam3_create_visual_tracker / sam3_tracker_add_instance /
+ * sam3_propagate_frame (sam3.cpp:12017-12262) on the device, over the
+ * runners above (all four created on `be`): per frame the Hiera encode, then
+ * per tracked instance the memory prompt from its device-resident bank, the
+ * memory attention, the decoder on the conditioned features, the kept mask,
+ * the memory encoder (-> a new bank slot) and the object pointer (-> the
+ * pointer bank).  Weights by name (sam3.cpp:2046-2060):
+ * "obj_ptr_proj.layers.{0,1,2}.{weight,bias}", "no_obj_ptr",
+ * "obj_ptr_tpos_proj.{weight,bias}" (optional), "mem_enc.tpos_enc"
+ * (optional); F32 or F16.  The host post-processing of sam3_propagate_frame
+ * (hole filling, sprinkle removal, overlap resolution) is not part of it. */
+typedef struct {
+    int32_t feat;             /* H: 64 (SAM2 at 1024) */
+    int32_t img;              /* encoder input side: 1024 */
+    int32_t d_model;          /* 256 */
+    int32_t mem_dim;          /* 64 */
+    int32_t num_maskmem;      /* 7: memory slots per instance */
+    int32_t max_obj_ptrs;     /* 16 */
+    int32_t multimask_in_sam; /* 1 (SAM2): a propagated frame keeps the best of masks 1..3 by IoU */
+    int32_t multimask_token_for_obj_ptr; /* 1: its pointer comes from that mask's token */
+    int32_t fixed_no_obj_ptr; /* 1 (SAM2): pointer = [obj > 0] * mlp + [obj <= 0] * no_obj_ptr */
+    int32_t max_instances;    /* capacity */
+    int32_t max_keep_alive;   /* an instance unseen for more frames is dropped (sam3_update_tracker) */
+} sam3b200_tracker_hparams;
+
+typedef struct sam3b200_tracker sam3b200_tracker;
+
+sam3b200_tracker *sam3b200_tracker_create(sam3b200_backend *be, const sam3b200_tracker_hparams *hp,
+                                          sam3b200_hiera *enc, sam3b200_sam_dec *dec, sam3b200_mem_attn *attn,
+                                          sam3b200_mem_enc *menc);
+void sam3b200_tracker_free(sam3b200_tracker *t);
+int sam3b200_tracker_set_tensor(sam3b200_tracker *t, const char *name, int type, const void *data,
+                                const int64_t ne[4]);
+/* sam3_encode_image of the next frame (a SAM2-preprocessed frame in device memory). */
+int sam3b200_tracker_encode(sam3b200_tracker *t, const float *img_chw_dev);
+/* The same from a host RGB frame (uint8 [h][w][3]): upload, SAM2 preprocessing
+ * (sam2_preprocess_image), encode -- the image half of sam3_propagate_frame. */
+int sam3b200_tracker_encode_image(sam3b200_tracker *t, const uint8_t *rgb, int w, int h);
+/* sam3_tracker_reset (sam3.cpp:12090-12110): no instances, frame index 0. */
+void sam3b200_tracker_reset(sam3b200_tracker *t);
+/* sam3_tracker_add_instance on the encoded frame: PVS decode of the prompts
+ * (sam3b200_sam_dec_run's conventions; mask 0), the mask at orig_w x orig_h
+ * as +-6 logits on the 4H grid -> a conditioning memory slot, and the SAM
+ * token's object pointer.  Returns the instance id (>= 1) or -1. */
+int sam3b200_tracker_add_instance(sam3b200_tracker *t, const float *coords, const int32_t *labels, int n_prompts,
+                                  int orig_w, int orig_h);
+/* sam3_propagate_frame after its encode: every instance propagated and
+ * remembered, then the frame index advances.  Synchronous. */
+int sam3b200_tracker_propagate(sam3b200_tracker *t);
+int sam3b200_tracker_frame_index(const sam3b200_tracker *t);
+/* ids of the tracked instances (count returned) */
+int sam3b200_tracker_instances(const sam3b200_tracker *t, int32_t *ids, int cap);
+/* An instance's last result: kept mask logits [(4H)^2] and its output token
+ * [d_model] (device), predicted IoU, object-score logit, last frame seen. */
+int sam3b200_tracker_instance(sam3b200_tracker *t, int id, const float **mask_logits_dev, const float **token_dev,
+                              float *iou, float *obj_score, int32_t *last_seen);
+/* That mask at out_w x out_h (bilinear, binarised at 0): dst_dev uint8 255 / 0. */
+int sam3b200_tracker_mask(sam3b200_tracker *t, int id, int out_w, int out_h, uint8_t *dst_dev);
+/* An instance's memory: slot frames / conditioning flags / device features
+ * [H*H][mem_dim] (slot count returned), pointer frames / device pointers
+ * [d_model] (*n_ptrs). */
+int sam3b200_tracker_bank(sam3b200_tracker *t, int id, int32_t *slot_frames, int32_t *slot_cond,
+                          const float **slot_feats_dev, int slot_cap, int32_t *ptr_frames, const float **ptrs_dev,
+                          int ptr_cap, int32_t *n_ptrs);
+/* The memory attention inputs the last propagated instance used: prompt and
+ * prompt_pos, device [M_total][mem_dim]. */
+int sam3b200_tracker_prompt(sam3b200_tracker *t, const float **prompt_dev, const float **prompt_pos_dev);
 
 /* ---- Fusion encoder of the SAM3 detector (the PCS path) --------------------
  * The graph sam3_build_fenc_graph builds (sam3.cpp:8146-8165; layer

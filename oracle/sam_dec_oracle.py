@@ -75,15 +75,21 @@ def gelu_erf(x):
     return (F32(0.5) * x * (F32(1.0) + erf(x * F32(0.70710678118654752440)).astype(F32))).astype(F32)
 
 
-def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_w, orig_h, img):
-    """-> (mask logits [nmask][4H][4H], iou [nmask], obj logit, sam token [256])"""
+def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_w, orig_h, img, tracking=False,
+           all_tokens=False):
+    """-> (mask logits [nmask][4H][4H], iou [nmask], obj logit, sam token [256]; with all_tokens the
+    output tokens of every mask [nmask][256] instead).  tracking: the decode of a propagated video frame
+    (sam3_propagate_single, sam3.cpp:11312-11347) -- no prompt but the padding token, and the
+    memory-conditioned features go in without no_mem_embed (the PVS decode adds it, sam3.cpp:10926)."""
     D, H = 256, hp["feat_size"]
     nmask = hp["n_multimask"] + 1
     special = ([t["sam_dec.obj_score_token.weight"]] if hp["pred_obj_scores"] else []) + \
         [t["sam_dec.iou_token.weight"]] + list(t["sam_dec.mask_tokens.weight"].reshape(nmask, D))
-    tok = np.concatenate([np.stack(special), sparse_tokens(t, coords, labels, orig_w, orig_h, img)]).astype(F32)
+    sparse = sparse_tokens(t, [] if tracking else coords, [] if tracking else labels, orig_w, orig_h, img)
+    tok = np.concatenate([np.stack(special), sparse]).astype(F32)
     qpe = tok.copy()
-    keys = ((img_feats.reshape(H * H, D) + t["no_mem_embed"]).astype(F32) + t["sam_pe.no_mask_embed.weight"]).astype(F32)
+    feats = img_feats.reshape(H * H, D) if tracking else (img_feats.reshape(H * H, D) + t["no_mem_embed"]).astype(F32)
+    keys = (feats + t["sam_pe.no_mask_embed.weight"]).astype(F32)
     kpe = dense_pe(t["sam_pe.pe_gaussian"], H).reshape(H * H, D)
     for i in range(hp["depth"]):
         p = f"sam_dec.twoway.{i}."
@@ -133,7 +139,7 @@ def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_
     masks = np.einsum("mc,chw->mhw", hyp.astype(np.float64), up2.astype(np.float64)).astype(F32)
     iou = mlp3("sam_dec.iou_prediction_head", tok[s0][None], sigmoid=True)[0]
     obj = float(mlp3("sam_dec.pred_obj_score_head", tok[0][None])[0][0]) if hp["pred_obj_scores"] else 10.0
-    return masks, iou, obj, tok[s0 + 1]
+    return masks, iou, obj, (tok[s0 + 1:s0 + 1 + nmask].copy() if all_tokens else tok[s0 + 1])
 
 
 def resize_threshold(mask: np.ndarray, dw: int, dh: int) -> np.ndarray:

@@ -312,6 +312,26 @@ def lib() -> ctypes.CDLL:
         "sam3b200_sam_dec_outputs": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), vp, vp,
                                            ctypes.POINTER(ctypes.c_void_p)]),
         "sam3b200_sam_dec_mask": (i32, [vp, i32, i32, i32, vp]),
+        "sam3b200_sam_dec_run_tracking": (i32, [vp, vp, vp, vp]),
+        "sam3b200_sam_dec_mask_token": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_tracker_create": (vp, [vp, vp, vp, vp, vp, vp]),
+        "sam3b200_tracker_free": (None, [vp]),
+        "sam3b200_tracker_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
+        "sam3b200_tracker_encode": (i32, [vp, vp]),
+        "sam3b200_tracker_add_instance": (i32, [vp, vp, vp, i32, i32, i32]),
+        "sam3b200_tracker_propagate": (i32, [vp]),
+        "sam3b200_tracker_encode_image": (i32, [vp, vp, i32, i32]),
+        "sam3b200_tracker_reset": (None, [vp]),
+        "sam3b200_tracker_frame_index": (i32, [vp]),
+        "sam3b200_tracker_instances": (i32, [vp, vp, i32]),
+        "sam3b200_tracker_instance": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                            vp, vp, vp]),
+        "sam3b200_tracker_mask": (i32, [vp, i32, i32, i32, vp]),
+        "sam3b200_tracker_bank": (i32, [vp, i32, vp, vp, vp, i32, vp, vp, i32, vp]),
+        "sam3b200_tracker_prompt": (i32, [vp, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)]),
+        "sam3b200_tensor_memset": (i32, [vp, vp, i32, ctypes.c_size_t, ctypes.c_size_t]),
+        "sam3b200_device_memory": (i32, [i32, vp, vp]),
+        "sam3b200_device_count": (i32, [vp]),
         "sam3b200_text_create": (vp, [vp, vp]),
         "sam3b200_text_free": (None, [vp]),
         "sam3b200_text_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -686,6 +706,17 @@ class SamDecoder:
         _check(lib().sam3b200_tensor_get(self.be.h, tp.value, tok.ctypes.data, 0, tok.nbytes), "tensor_get")
         return masks, np.array(iou[:n], np.float32), obj.value, tok
 
+    def run_tracking(self, cond_feats: int, feat_s0: int, feat_s1: int) -> None:
+        """A propagated frame's decode: memory-conditioned features, no prompt, no no_mem_embed."""
+        _check(lib().sam3b200_sam_dec_run_tracking(self.h, cond_feats, feat_s0, feat_s1), "sam_dec_run_tracking")
+
+    def mask_token(self, m: int) -> np.ndarray:
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_sam_dec_mask_token(self.h, m, ctypes.byref(p)), "sam_dec_mask_token")
+        tok = np.empty(self.hp["embed"], np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, tok.ctypes.data, 0, tok.nbytes), "tensor_get")
+        return tok
+
     def mask(self, m: int, out_w: int, out_h: int) -> np.ndarray:
         buf = DeviceBuffer(self.be, out_w * out_h)
         _check(lib().sam3b200_sam_dec_mask(self.h, m, out_w, out_h, buf.ptr), "sam_dec_mask")
@@ -776,6 +807,15 @@ class MemAttention:
         _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
         return out
 
+    def output_host(self, n_tokens: int) -> np.ndarray:
+        """The last run's conditioned tokens [n_tokens][d_model] (a run through the device entry included)."""
+        p = ctypes.c_void_p()
+        _check(lib().sam3b200_mem_attn_output(self.h, ctypes.byref(p)), "mem_attn_output")
+        self.be.synchronize()
+        out = np.empty((n_tokens, self.hp["d_model"]), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, out.ctypes.data, 0, out.nbytes), "tensor_get")
+        return out
+
     def free(self) -> None:
         if self.h:
             lib().sam3b200_mem_attn_free(self.h)
@@ -826,6 +866,113 @@ class MemEncoder:
     def free(self) -> None:
         if self.h:
             lib().sam3b200_mem_enc_free(self.h)
+            self.h = None
+
+
+class Tracker:
+    """The video tracker's frame loop (sam3b200_tracker) over a Hiera encoder, a SAM decoder, a memory
+    attention and a memory encoder of one backend."""
+
+    FIELDS = ("feat", "img", "d_model", "mem_dim", "num_maskmem", "max_obj_ptrs", "multimask_in_sam",
+              "multimask_token_for_obj_ptr", "fixed_no_obj_ptr", "max_instances", "max_keep_alive")
+
+    def __init__(self, be: "Backend", hp: dict, enc: "Hiera", dec: "SamDecoder", attn: "MemAttention",
+                 menc: "MemEncoder"):
+        self.be, self.hp = be, dict(hp)
+        self._chp = (ctypes.c_int32 * len(self.FIELDS))(*[int(hp[k]) for k in self.FIELDS])
+        self._parts = (enc, dec, attn, menc)
+        self.h = lib().sam3b200_tracker_create(be.h, ctypes.byref(self._chp), enc.h, dec.h, attn.h, menc.h)
+        if not self.h:
+            raise B200Error(f"tracker_create failed: {last_error()}")
+
+    def load(self, tensors: dict) -> None:
+        for name, (t, arr, ne) in tensors.items():
+            arr = np.ascontiguousarray(arr)
+            ne4 = (ctypes.c_int64 * 4)(*(list(ne) + [1] * (4 - len(ne))))
+            _check(lib().sam3b200_tracker_set_tensor(self.h, name.encode(), t, arr.ctypes.data, ne4), f"set {name}")
+
+    def encode(self, img_chw: "DeviceBuffer") -> None:
+        _check(lib().sam3b200_tracker_encode(self.h, img_chw.ptr), "tracker_encode")
+
+    def add_instance(self, coords, labels, orig_w: int, orig_h: int) -> int:
+        c = np.ascontiguousarray(coords, np.float32).reshape(-1)
+        lab = np.ascontiguousarray(labels, np.int32)
+        i = lib().sam3b200_tracker_add_instance(self.h, c.ctypes.data, lab.ctypes.data, lab.size, orig_w, orig_h)
+        if i < 0:
+            raise B200Error(f"tracker_add_instance: {last_error()}")
+        return i
+
+    def propagate(self) -> None:
+        _check(lib().sam3b200_tracker_propagate(self.h), "tracker_propagate")
+
+    def encode_image(self, rgb_ptr: int, w: int, h: int) -> None:
+        """Host uint8 [h][w][3] frame at rgb_ptr: upload, SAM2 preprocessing, encode."""
+        _check(lib().sam3b200_tracker_encode_image(self.h, ctypes.c_void_p(rgb_ptr), w, h), "tracker_encode_image")
+
+    def reset(self) -> None:
+        lib().sam3b200_tracker_reset(self.h)
+
+    @property
+    def frame_index(self) -> int:
+        return lib().sam3b200_tracker_frame_index(self.h)
+
+    def instances(self) -> list:
+        ids = (ctypes.c_int32 * 64)()
+        n = lib().sam3b200_tracker_instances(self.h, ids, 64)
+        return list(ids[:n])
+
+    def instance(self, iid: int) -> dict:
+        """The instance's last kept mask logits [4H][4H], token [d_model], IoU, object score, last frame."""
+        mp, tp = ctypes.c_void_p(), ctypes.c_void_p()
+        iou, obj, seen = ctypes.c_float(), ctypes.c_float(), ctypes.c_int32()
+        _check(lib().sam3b200_tracker_instance(self.h, iid, ctypes.byref(mp), ctypes.byref(tp), ctypes.byref(iou),
+                                               ctypes.byref(obj), ctypes.byref(seen)), "tracker_instance")
+        S, D = 4 * self.hp["feat"], self.hp["d_model"]
+        mask, tok = np.empty((S, S), np.float32), np.empty(D, np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, mp.value, mask.ctypes.data, 0, mask.nbytes), "tensor_get")
+        _check(lib().sam3b200_tensor_get(self.be.h, tp.value, tok.ctypes.data, 0, tok.nbytes), "tensor_get")
+        return dict(mask=mask, token=tok, iou=iou.value, obj=obj.value, last_seen=seen.value)
+
+    def mask(self, iid: int, out_w: int, out_h: int) -> np.ndarray:
+        buf = DeviceBuffer(self.be, out_w * out_h)
+        _check(lib().sam3b200_tracker_mask(self.h, iid, out_w, out_h, buf.ptr), "tracker_mask")
+        self.be.synchronize()
+        return buf.get((out_h, out_w), np.uint8)
+
+    def bank(self, iid: int) -> tuple:
+        """([(frame, is_cond, features [H*H][mem_dim])], [(frame, pointer [d_model])])"""
+        cap = 256
+        sf, sc, pf = (ctypes.c_int32 * cap)(), (ctypes.c_int32 * cap)(), (ctypes.c_int32 * cap)()
+        sp, pp = (ctypes.c_void_p * cap)(), (ctypes.c_void_p * cap)()
+        npt = ctypes.c_int32()
+        ns = lib().sam3b200_tracker_bank(self.h, iid, sf, sc, sp, cap, pf, pp, cap, ctypes.byref(npt))
+        if ns < 0:
+            raise B200Error(f"tracker_bank: {last_error()}")
+        N, MD, D = self.hp["feat"] ** 2, self.hp["mem_dim"], self.hp["d_model"]
+        slots, ptrs = [], []
+        for i in range(ns):
+            a = np.empty((N, MD), np.float32)
+            _check(lib().sam3b200_tensor_get(self.be.h, sp[i], a.ctypes.data, 0, a.nbytes), "tensor_get")
+            slots.append((sf[i], bool(sc[i]), a))
+        for i in range(npt.value):
+            a = np.empty(D, np.float32)
+            _check(lib().sam3b200_tensor_get(self.be.h, pp[i], a.ctypes.data, 0, a.nbytes), "tensor_get")
+            ptrs.append((pf[i], a))
+        return slots, ptrs
+
+    def prompt(self, m_total: int) -> tuple:
+        """The last propagated instance's prompt and prompt_pos, [m_total][mem_dim]."""
+        p, q = ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().sam3b200_tracker_prompt(self.h, ctypes.byref(p), ctypes.byref(q)), "tracker_prompt")
+        MD = self.hp["mem_dim"]
+        a, b = np.empty((m_total, MD), np.float32), np.empty((m_total, MD), np.float32)
+        _check(lib().sam3b200_tensor_get(self.be.h, p.value, a.ctypes.data, 0, a.nbytes), "tensor_get")
+        _check(lib().sam3b200_tensor_get(self.be.h, q.value, b.ctypes.data, 0, b.nbytes), "tensor_get")
+        return a, b
+
+    def free(self) -> None:
+        if self.h:
+            lib().sam3b200_tracker_free(self.h)
             self.h = None
 
 
@@ -1199,6 +1346,10 @@ class Backend:
 
     def mem_encoder(self, hp: dict) -> MemEncoder:
         return MemEncoder(self, hp)
+
+    def tracker(self, hp: dict, enc: "Hiera", dec: "SamDecoder", attn: "MemAttention",
+                menc: "MemEncoder") -> Tracker:
+        return Tracker(self, hp, enc, dec, attn, menc)
 
     def fusion_encoder(self, hp: dict) -> FusionEncoder:
         return FusionEncoder(self, hp)

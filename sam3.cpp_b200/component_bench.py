@@ -171,6 +171,99 @@ def video_weights(model_mod, D=256, MD=64):
     return attn, w.t
 
 
+def hiera_weights(model_mod, enc, hp: dict) -> dict:
+    """Random-init weights of a SAM2 Hiera trunk + FPN, block shapes taken from the created encoder
+    (sam3b200_hiera_block_info); linear weights Q8_0."""
+    w = _Weights(model_mod, Q8_0, seed=11)
+    E, ws0 = hp["embed"], hp["window_spec"][0]
+    w.t["hiera.patch_embed.weight"] = (F32, w.rng.normal(0, 0.02, size=(E, 3, 7, 7)).astype(np.float32), (7, 7, 3, E))
+    w.vec("hiera.patch_embed.bias", E)
+    w.t["hiera.pos_embed"] = (F32, w.rng.normal(0, 0.02, size=(E, hp["bkg_h"], hp["bkg_w"])).astype(np.float32),
+                              (hp["bkg_w"], hp["bkg_h"], E))
+    w.t["hiera.pos_embed_window"] = (F32, w.rng.normal(0, 0.02, size=(E, ws0, ws0)).astype(np.float32),
+                                     (ws0, ws0, E))
+    for i in range(sum(hp["stages"])):
+        di, do = enc.block_info(i)[:2]
+        p = f"hiera.blocks.{i}."
+        w.norm(p + "norm1", di)
+        w.norm(p + "norm2", do)
+        w.lin(p + "attn.qkv", di, 3 * do)
+        w.lin(p + "attn.proj", do, do)
+        w.lin(p + "mlp.fc1", do, 4 * do)
+        w.lin(p + "mlp.fc2", 4 * do, do)
+        if di != do:
+            w.lin(p + "proj", di, do)
+    D = hp["neck_dim"]
+    for j in range(4):
+        C = E * 2 ** (3 - j)
+        w.t[f"fpn.convs.{j}.weight"] = (F32, w.rng.normal(0, 0.02, size=(D, C)).astype(np.float32), (1, 1, C, D))
+        w.vec(f"fpn.convs.{j}.bias", D)
+    return w.t
+
+
+def sam_dec_weights(model_mod, D=256) -> dict:
+    """Random-init prompt encoder + mask decoder weights (sam3.cpp:1854-1968 names), Q8_0 linear weights."""
+    w = _Weights(model_mod, Q8_0, seed=12)
+
+    def f32(name, shape, std=1.0):
+        arr = w.rng.normal(0, std, size=shape).astype(np.float32)
+        w.t[name] = (F32, arr, arr.shape[::-1] if len(shape) > 1 else (shape[0], 1))
+
+    def attn(pfx, idim):
+        for n in ("q", "k", "v"):
+            w.lin(f"{pfx}.{n}_proj", D, idim)
+        w.lin(f"{pfx}.out_proj", idim, D)
+
+    w.t["sam_pe.pe_gaussian"] = (F32, w.rng.normal(0, 1, size=(2, 128)).astype(np.float32), (128, 2))
+    for i in range(4):
+        f32(f"sam_pe.point_embeddings.{i}.weight", (D,))
+    for n in ("sam_pe.not_a_point_embed.weight", "sam_pe.no_mask_embed.weight", "sam_dec.iou_token.weight",
+              "sam_dec.obj_score_token.weight"):
+        f32(n, (D,))
+    w.t["no_mem_embed"] = (F32, w.rng.normal(0, 0.02, size=D).astype(np.float32), (D, 1, 1))
+    w.t["sam_dec.mask_tokens.weight"] = (F32, w.rng.normal(0, 1, size=(4, D)).astype(np.float32), (D, 4))
+    for i in range(2):
+        p = f"sam_dec.twoway.{i}"
+        attn(p + ".sa", D)
+        attn(p + ".cross_attn_token_to_image", 128)
+        attn(p + ".cross_attn_image_to_token", 128)
+        for j in range(1, 5):
+            w.norm(f"{p}.norm{j}", D)
+        w.lin(p + ".mlp.lin1", D, 2048)
+        w.lin(p + ".mlp.lin2", 2048, D)
+    attn("sam_dec.final_attn", 128)
+    w.norm("sam_dec.final_norm", D)
+    w.t["sam_dec.upscale.0.weight"] = (F32, w.rng.normal(0, 0.05, size=(D, 64, 2, 2)).astype(np.float32), (2, 2, 64, D))
+    w.vec("sam_dec.upscale.0.bias", 64)
+    w.norm("sam_dec.upscale.1", 64)
+    w.t["sam_dec.upscale.3.weight"] = (F32, w.rng.normal(0, 0.1, size=(64, 32, 2, 2)).astype(np.float32), (2, 2, 32, 64))
+    w.vec("sam_dec.upscale.3.bias", 32)
+    for name, oc in (("sam_dec.conv_s0", 32), ("sam_dec.conv_s1", 64)):
+        w.t[name + ".weight"] = (F32, w.rng.normal(0, 0.05, size=(oc, D)).astype(np.float32), (1, 1, D, oc))
+        w.vec(name + ".bias", oc)
+    for m in range(4):
+        for j in range(3):
+            w.lin(f"sam_dec.hyper.{m}.layers.{j}", D, 32 if j == 2 else D)
+    for head, nout in (("iou_prediction_head", 4), ("pred_obj_score_head", 1)):
+        for j in range(3):
+            w.lin(f"sam_dec.{head}.layers.{j}", D, nout if j == 2 else D)
+    return w.t
+
+
+def tracker_weights(D=256, MD=64, num_maskmem=7) -> dict:
+    """Random-init object-pointer and temporal-code weights of the video tracker."""
+    rng = np.random.default_rng(13)
+    t = {}
+    for j in range(3):
+        t[f"obj_ptr_proj.layers.{j}.weight"] = rng.normal(0, 1 / 16, size=(D, D)).astype(np.float32)
+        t[f"obj_ptr_proj.layers.{j}.bias"] = rng.normal(0, 0.1, size=D).astype(np.float32)
+    t["no_obj_ptr"] = rng.normal(0, 1, size=D).astype(np.float32)
+    t["obj_ptr_tpos_proj.weight"] = rng.normal(0, 1 / 16, size=(MD, D)).astype(np.float32)
+    t["obj_ptr_tpos_proj.bias"] = rng.normal(0, 0.1, size=MD).astype(np.float32)
+    t["mem_enc.tpos_enc"] = rng.normal(0, 0.1, size=(num_maskmem, MD)).astype(np.float32)
+    return {k: (F32, v, v.shape[::-1]) for k, v in t.items()}
+
+
 def _events(torch, stream):
     e = torch.cuda.Event(enable_timing=True)
     e.record(stream)

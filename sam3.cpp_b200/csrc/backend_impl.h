@@ -53,4 +53,9 @@ bool cuda_ok(cudaError_t e, const char *what);
 int run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx, int64_t M, const float *bias, float *dst,
                 int64_t ldd, int32_t *dump);
 
+// sam_dec.cu: a decoder mask's logits [S][S] resized to out_w x out_h (bilinear) and binarised at 0 -> 255 / 0
+cudaError_t launch_mask_resize(const float *src, int S, int out_w, int out_h, uint8_t *dst, cudaStream_t s);
+// mem_prompt.cu: the positional row (MD floats) shared by an object pointer's prompt tokens
+void obj_ptr_pos_row(int D, int MD, int rel, const float *w, const float *b, float *out);
+
 }  // namespace b200

@@ -130,11 +130,14 @@ bool attend(MemAttn *m, const float *q, const float *k, const float *v, int N, i
     ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(k, n, m->k16.as<__half>());
     ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(v, n, m->v16.as<__half>());
     const AttnStrides rs{0, 0, D};
-    return mok(m, cudaGetLastError(), "mem_attn fp16 k, v") &&
-           mok(m, attention_mma_f16kv_split(D, q, rs, N, m->k16.as<__half>(), rs, m->v16.as<__half>(), rs, NK, 1, 1,
-                                            scale, out, rs, m->splits, m->part_o.as<float>(), m->part_ml.as<float2>(),
-                                            s),
-               "mem_attn attention");
+    if (!mok(m, cudaGetLastError(), "mem_attn fp16 k, v")) return false;
+    m->be->prof_mark(1);  // profile class 1: the memory attention's attention kernels
+    const bool ok = mok(m, attention_mma_f16kv_split(D, q, rs, N, m->k16.as<__half>(), rs, m->v16.as<__half>(), rs, NK,
+                                                     1, 1, scale, out, rs, m->splits, m->part_o.as<float>(),
+                                                     m->part_ml.as<float2>(), s),
+                        "mem_attn attention");
+    m->be->prof_mark(1);
+    return ok;
 }
 
 bool forward(MemAttn *m, const float *curr, const float *spos, const float *prompt, const float *ppos,

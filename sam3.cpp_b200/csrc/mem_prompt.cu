@@ -33,6 +33,18 @@ void sine_pe_1d(float *out, float pos, int dim) {
 
 }  // namespace
 
+// The positional row of an object pointer's tokens: the 1-D sine code of max(1, |frame distance|) / 15
+// (d_model wide) through obj_ptr_tpos_proj (weight ggml [D, MD]: w[j * D + i]; bias [MD]; NULL = zeros).
+void b200::obj_ptr_pos_row(int D, int MD, int rel, const float *w, const float *b, float *out) {
+    std::vector<float> sine(static_cast<size_t>(D));
+    sine_pe_1d(sine.data(), static_cast<float>(rel) / 15.0f, D);
+    for (int j = 0; j < MD; ++j) {
+        float sum = b ? b[j] : 0.0f;
+        for (int i = 0; i < D; ++i) sum += (w ? w[i + static_cast<int64_t>(j) * D] : 0.0f) * sine[i];
+        out[j] = sum;
+    }
+}
+
 using b200::set_error;
 
 extern "C" int sam3b200_select_memory_frames(int bank_size, int max_slots, int32_t *out, int cap) {
@@ -120,17 +132,11 @@ extern "C" int64_t sam3b200_build_mem_prompt(const sam3b200_mem_prompt_hparams *
 
     // 2. object pointers: each D-wide pointer as D / MD tokens; their positional code is the 1-D sine
     //    code of the frame distance / 15 projected D -> MD (obj_ptr_tpos_proj), shared by the pointer's tokens
-    std::vector<float> sine(D), proj(MD);
+    std::vector<float> proj(MD);
     int64_t tok = m_spatial;
     for (int p = 0; p < P; ++p) {
         const int rel = std::max(1, std::abs(cur_frame - ptr_frames[p]));
-        sine_pe_1d(sine.data(), static_cast<float>(rel) / 15.0f, D);
-        for (int j = 0; j < MD; ++j) {
-            float sum = tpos_proj_b ? tpos_proj_b[j] : 0.0f;
-            for (int i = 0; i < D; ++i)
-                sum += (tpos_proj_w ? tpos_proj_w[i + static_cast<int64_t>(j) * D] : 0.0f) * sine[i];
-            proj[j] = sum;
-        }
+        b200::obj_ptr_pos_row(D, MD, rel, tpos_proj_w, tpos_proj_b, proj.data());
         for (int t = 0; t < split; ++t, ++tok)
             for (int d = 0; d < MD; ++d) {
                 prompt[tok * MD + d] = obj_ptrs[p][t * MD + d];

@@ -142,6 +142,17 @@ __global__ void mask_resize_kernel(const float *__restrict__ src, int sw, int sh
     dst[i] = v > 0.0f ? 255 : 0;
 }
 
+}  // namespace
+
+// The same resize + binarisation for another owner of a decoder mask (the video tracker's kept masks).
+cudaError_t launch_mask_resize(const float *src, int S, int out_w, int out_h, uint8_t *dst, cudaStream_t s) {
+    const int64_t n = static_cast<int64_t>(out_w) * out_h;
+    mask_resize_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(src, S, S, out_w, out_h, dst);
+    return cudaGetLastError();
+}
+
+namespace {
+
 struct DecAttn {
     sam3b200_weight *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     DevBuf qb, kb, vb, ob;
@@ -282,13 +293,16 @@ bool to_channels(SamDec *d, const float *x, int64_t P, int C, float *y) {
     return dlaunched(d, cudaGetLastError(), "sam_dec transpose");
 }
 
-bool decode(SamDec *d, const float *img, const float *fs0, const float *fs1) {
+// add_no_mem: the PVS decode adds no_mem_embed to the image features (sam3.cpp:10926-10936); a
+// propagated frame's memory-conditioned features go in without it (sam3.cpp:11296-11335).
+bool decode(SamDec *d, const float *img, const float *fs0, const float *fs1, bool add_no_mem = true) {
     const int D = d->D, H = d->H, HH = H * H;
     const int64_t P1 = static_cast<int64_t>(2 * H) * 2 * H, P0 = static_cast<int64_t>(4 * H) * 4 * H;
     cudaStream_t s = d->be->stream;
     auto *hb = reinterpret_cast<sam3b200_backend *>(d->be);
-    // keys = image features + no_mem_embed + no-mask dense embedding; key PE = dense grid
-    if (!add(d, img, nullptr, HH, d->keys.as<float>(), d->no_mem.as<float>(), d->no_mask_dev.as<float>()) ||
+    // keys = image features (+ no_mem_embed) + no-mask dense embedding; key PE = dense grid
+    if (!add(d, img, nullptr, HH, d->keys.as<float>(), add_no_mem ? d->no_mem.as<float>() : nullptr,
+             d->no_mask_dev.as<float>()) ||
         !cuda_ok(cudaMemcpyAsync(d->kpe.p, d->dense_pe.p, static_cast<size_t>(HH) * D * 4, cudaMemcpyDeviceToDevice, s),
                  "kpe"))
         return false;
@@ -649,6 +663,44 @@ int sam3b200_sam_dec_run(sam3b200_sam_dec *hd, const float *img_feats_dev, const
         !cuda_ok(cudaStreamSynchronize(d->be->stream), "tokens sync"))
         return SAM3B200_STATUS_FAILED;
     return decode(d, img_feats_dev, feat_s0_dev, feat_s1_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_sam_dec_run_tracking(sam3b200_sam_dec *hd, const float *cond_feats_dev, const float *feat_s0_dev,
+                                  const float *feat_s1_dev) {
+    auto *d = reinterpret_cast<SamDec *>(hd);
+    if (!d || !cond_feats_dev || !feat_s0_dev || !feat_s1_dev) {
+        set_error("sam_dec_run_tracking: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(d->be->device);
+    if (!check_ready(d)) return SAM3B200_STATUS_FAILED;
+    // tokens: [obj_score?, iou, masks x n, not_a_point] -- the single padding token of sam3_propagate_single
+    const int D = d->D;
+    d->ntok = d->nspecial + 1;
+    std::vector<float> tok(static_cast<size_t>(d->ntok) * D);
+    size_t o = 0;
+    if (d->hp.pred_obj_scores) std::copy(d->tok_obj.begin(), d->tok_obj.end(), tok.begin() + (o++) * D);
+    std::copy(d->tok_iou.begin(), d->tok_iou.end(), tok.begin() + (o++) * D);
+    std::copy(d->tok_masks.begin(), d->tok_masks.end(), tok.begin() + o * D);
+    o += d->nmask;
+    std::copy(d->not_a_point.begin(), d->not_a_point.end(), tok.begin() + o * D);
+    const size_t bytes = tok.size() * 4;
+    if (!cuda_ok(cudaMemcpyAsync(d->tok.p, tok.data(), bytes, cudaMemcpyHostToDevice, d->be->stream), "tokens") ||
+        !cuda_ok(cudaMemcpyAsync(d->qpe.p, tok.data(), bytes, cudaMemcpyHostToDevice, d->be->stream), "tokens") ||
+        !cuda_ok(cudaStreamSynchronize(d->be->stream), "tokens sync"))
+        return SAM3B200_STATUS_FAILED;
+    return decode(d, cond_feats_dev, feat_s0_dev, feat_s1_dev, false) ? SAM3B200_STATUS_SUCCESS
+                                                                       : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_sam_dec_mask_token(sam3b200_sam_dec *hd, int m, const float **dev) {
+    auto *d = reinterpret_cast<SamDec *>(hd);
+    if (!d || d->ntok == 0 || m < 0 || m >= d->nmask || !dev) {
+        set_error("sam_dec_mask_token: no decode yet or token %d out of range", m);
+        return SAM3B200_STATUS_FAILED;
+    }
+    *dev = d->tok.as<float>() + (d->hp.pred_obj_scores ? 2 + m : 1 + m) * d->D;
+    return SAM3B200_STATUS_SUCCESS;
 }
 
 int sam3b200_sam_dec_outputs(sam3b200_sam_dec *hd, const float **masks_dev, float iou[4], float *obj_logit,
