@@ -173,7 +173,7 @@ def video_weights(model_mod, D=256, MD=64):
 
 def hiera_weights(model_mod, enc, hp: dict) -> dict:
     """Random-init weights of a SAM2 Hiera trunk + FPN, block shapes taken from the created encoder
-    (sam3b200_hiera_block_info); linear weights Q8_0."""
+    (sam3b200_hiera_block_info); linear weights Q8_0 where the row length allows it, else F16."""
     w = _Weights(model_mod, Q8_0, seed=11)
     E, ws0 = hp["embed"], hp["window_spec"][0]
     w.t["hiera.patch_embed.weight"] = (F32, w.rng.normal(0, 0.02, size=(E, 3, 7, 7)).astype(np.float32), (7, 7, 3, E))
@@ -182,17 +182,26 @@ def hiera_weights(model_mod, enc, hp: dict) -> dict:
                               (hp["bkg_w"], hp["bkg_h"], E))
     w.t["hiera.pos_embed_window"] = (F32, w.rng.normal(0, 0.02, size=(E, ws0, ws0)).astype(np.float32),
                                      (ws0, ws0, E))
+    def lin(name, K, N):
+        # ggml's quantiser keeps a tensor whose row length is no multiple of 32 in F16
+        if K % 32 == 0:
+            w.lin(name, K, N)
+            return
+        arr = w.rng.normal(0, 1.0 / math.sqrt(K), size=(N, K)).astype(np.float16)
+        w.t[name + ".weight"] = (F16, arr, (K, N))
+        w.vec(name + ".bias", N)
+
     for i in range(sum(hp["stages"])):
         di, do = enc.block_info(i)[:2]
         p = f"hiera.blocks.{i}."
         w.norm(p + "norm1", di)
         w.norm(p + "norm2", do)
-        w.lin(p + "attn.qkv", di, 3 * do)
-        w.lin(p + "attn.proj", do, do)
-        w.lin(p + "mlp.fc1", do, 4 * do)
-        w.lin(p + "mlp.fc2", 4 * do, do)
+        lin(p + "attn.qkv", di, 3 * do)
+        lin(p + "attn.proj", do, do)
+        lin(p + "mlp.fc1", do, 4 * do)
+        lin(p + "mlp.fc2", 4 * do, do)
         if di != do:
-            w.lin(p + "proj", di, do)
+            lin(p + "proj", di, do)
     D = hp["neck_dim"]
     for j in range(4):
         C = E * 2 ** (3 - j)

@@ -19,6 +19,7 @@
 // counts of Q-pooled blocks, padded windows), global attention two fp16
 // tensor-core GEMMs around a row softmax.
 #include "../../include/sam3_b200.h"
+#include "act.cuh"
 #include "attn_simt.cuh"
 #include "gemm_f16.cuh"
 #include "model_util.h"
@@ -82,6 +83,29 @@ __global__ void win_gather_q8_kernel(const float *__restrict__ x, int H, int W, 
         }
         q8_block_store(v, cr, quads, blk, r, ld, C / 32);
     }
+}
+
+// The same window partition into f32 rows (the input of an F16 / F32 qkv weight).
+__global__ void win_gather_f32_kernel(const float *__restrict__ x, int H, int W, int C, int ws, int nWh, int64_t rows,
+                                      float *__restrict__ y) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= rows * C) return;
+    const int64_t r = i / C;
+    const int c = static_cast<int>(i % C);
+    const int N = ws * ws, w = static_cast<int>(r / N), n = static_cast<int>(r % N);
+    const int gx = n % ws + ws * (w / nWh), gy = n / ws + ws * (w % nWh);
+    y[i] = (gx < W && gy < H) ? x[(static_cast<int64_t>(gy) * W + gx) * C + c] : 0.0f;
+}
+
+// ggml_gelu (the CPU backend's fp16-table tanh form) in place
+__global__ void gelu_tanh_inplace_kernel(float *__restrict__ x, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = gelu_tanh_f16(x[i]);
+}
+
+__global__ void add_inplace_kernel(float *__restrict__ y, const float *__restrict__ x, int64_t n) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = __fadd_rn(y[i], x[i]);
 }
 
 // 2x2 max pool of the q part (columns [0, C)) of qkv rows [Bw][wh][ww] (row stride
@@ -265,11 +289,21 @@ void bicubic_chw(const std::vector<float> &src, int C, int hi, int wi, std::vect
         }
 }
 
+// A linear layer of a block: Q8_0 / Q4_0 weights on the int8 tensor-core MUL_MAT, or F16 / F32 ones
+// (a file whose row length is no multiple of 32 keeps those tensors F16, as ggml's quantiser does;
+// F16 files throughout) on the fp16 tensor-core GEMM with the activations rounded to fp16 -- ggml-cpu's
+// vec_dot_f16 arithmetic.
+struct HLinear {
+    QWeight q;
+    sam3b200_weight *dense = nullptr;
+    bool set() const { return q.set || dense != nullptr; }
+};
+
 struct HBlock {
     int dim_in = 0, dim_out = 0, heads = 0, ws = 0, stage = 0;
     bool q_stride = false;
     DevBuf n1w, n1b, n2w, n2b, qkv_b, proj_b, fc1_b, fc2_b, dproj_b;
-    QWeight qkv, proj, fc1, fc2, dproj;
+    HLinear qkv, proj, fc1, fc2, dproj;
 };
 
 struct FpnLevel {
@@ -293,6 +327,12 @@ struct Hiera {
     DevBuf xa, xb, normed, shortf, shortp, qkv, qp, attn, proj, codes_a, quads_a, codes_b, quads_b;
     DevBuf stage_out[4], fpn_out[4], x16;
     DevBuf gq, gk, gvt, gs, gp;  // global attention on the tensor cores: fp16 q, k, v^T, f32 scores, fp16 probs
+    DevBuf xwin, hid;            // blocks with F16 / F32 linear layers: f32 windowed rows, MLP hidden rows
+    ~Hiera() {
+        for (auto &b : blk)
+            for (HLinear *l : {&b.qkv, &b.proj, &b.fc1, &b.fc2, &b.dproj})
+                if (l->dense) sam3b200_weight_free(reinterpret_cast<sam3b200_backend *>(be), l->dense);
+    }
     int stage_side[4] = {0, 0, 0, 0}, stage_dim[4] = {0, 0, 0, 0};
     int n_fpn = 0;
     bool ready = false;
@@ -327,6 +367,33 @@ bool h_mmq(Hiera *h, const void *codes, const void *quads, int M, const QWeight 
     return ok;
 }
 
+// y = x W^T + bias for an F16 / F32 weight: x f32 rows (ld = K), y rows of N
+bool h_dense(Hiera *h, const float *x, int M, const HLinear &w, const float *bias, float *y) {
+    const auto *wt = reinterpret_cast<const Weight *>(w.dense);
+    return run_mul_mat(h->be, wt, x, wt->K, M, bias, y, wt->N, nullptr) == SAM3B200_STATUS_SUCCESS;
+}
+
+// a linear layer on f32 input rows, either kind of weight (f32 out, optionally added to y); a quantised
+// weight takes its activation codes in the `wide` (MLP hidden, codes_b / quads_b: To x 4 Co) or the
+// narrow (codes_a / quads_a) scratch
+bool h_linear(Hiera *h, const float *x, int M, int K, const HLinear &w, const float *bias, float *y, int add,
+              float *tmp, bool wide = false) {
+    cudaStream_t s = h->be->stream;
+    if (w.dense) {
+        if (!add) return h_dense(h, x, M, w, bias, y);
+        const auto *wt = reinterpret_cast<const Weight *>(w.dense);
+        const int64_t n = static_cast<int64_t>(M) * wt->N;
+        if (!h_dense(h, x, M, w, bias, tmp)) return false;
+        add_inplace_kernel<<<blocks_for(n, 256), 256, 0, s>>>(y, tmp, n);
+        return hlaunched(h, cudaGetLastError(), "hiera residual");
+    }
+    void *codes = wide ? h->codes_b.p : h->codes_a.p, *quads = wide ? h->quads_b.p : h->quads_a.p;
+    return hlaunched(h, quantize_rows_q8(x, K, M, K, codes, quads, round128(M), s), "hiera quantize") &&
+           h_mmq(h, codes, quads, M, w.q, MMQ_OUT_F32, bias, y, add, nullptr, nullptr, 0);
+}
+
+bool ensure_buf(DevBuf &b, size_t bytes) { return b.n >= bytes || b.alloc(bytes); }
+
 // Derive the per-block metadata exactly as sam2_precompute_hiera_metadata (sam3.cpp:1680-1740).
 bool hiera_metadata(Hiera *h) {
     const auto &hp = h->hp;
@@ -360,7 +427,9 @@ bool hiera_metadata(Hiera *h) {
         for (int qb : qpool)
             if (qb == i) b.q_stride = true;
         embed = dout;
-        if (b.dim_in % 32 != 0 || b.dim_out % 32 != 0 || b.dim_out % b.heads != 0) return false;
+        // fp16 GEMM rows need 8 | dim (a Q8_0 / Q4_0 weight further needs 32 | its row length, checked
+        // when it is set)
+        if (b.dim_in % 8 != 0 || b.dim_out % 8 != 0 || b.dim_out % b.heads != 0) return false;
     }
     return true;
 }
@@ -508,10 +577,8 @@ bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
     // 2. shortcut
     const float *sc = x;
     if (Ci != Co) {
-        if (!hlaunched(h, quantize_rows_q8(h->normed.as<float>(), Ci, T, Ci, h->codes_a.p, h->quads_a.p, round128(T), s),
-                       "hiera quantize") ||
-            !h_mmq(h, h->codes_a.p, h->quads_a.p, T, b.dproj, MMQ_OUT_F32, b.dproj_b.as<float>(),
-                   h->shortf.as<float>(), 0, nullptr, nullptr, 0))
+        if (!h_linear(h, h->normed.as<float>(), T, Ci, b.dproj, b.dproj_b.as<float>(), h->shortf.as<float>(), 0,
+                      nullptr))
             return false;
         sc = h->shortf.as<float>();
     }
@@ -522,19 +589,31 @@ bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
         sc = h->shortp.as<float>();
     }
     // 3. qkv over the window-partitioned normed input
-    cudaError_t e;
-    if (b.ws > 0) {
-        win_gather_q8_kernel<<<blocks_for(rw, 8), 256, 0, s>>>(h->normed.as<float>(), H, W, Ci, b.ws, g.nWh, rw,
-                                                               h->codes_a.as<int8_t>(), h->quads_a.as<__half>(),
-                                                               round128(rw));
-        e = cudaGetLastError();
+    if (b.qkv.dense) {
+        const float *xin = h->normed.as<float>();
+        if (b.ws > 0) {
+            if (!ensure_buf(h->xwin, static_cast<size_t>(rw) * Ci * 4)) return false;
+            win_gather_f32_kernel<<<blocks_for(static_cast<int64_t>(rw) * Ci, 256), 256, 0, s>>>(
+                h->normed.as<float>(), H, W, Ci, b.ws, g.nWh, rw, h->xwin.as<float>());
+            if (!hlaunched(h, cudaGetLastError(), "hiera qkv windows")) return false;
+            xin = h->xwin.as<float>();
+        }
+        if (!h_dense(h, xin, rw, b.qkv, b.qkv_b.as<float>(), h->qkv.as<float>())) return false;
     } else {
-        e = quantize_rows_q8(h->normed.as<float>(), Ci, T, Ci, h->codes_a.p, h->quads_a.p, round128(T), s);
+        cudaError_t e;
+        if (b.ws > 0) {
+            win_gather_q8_kernel<<<blocks_for(rw, 8), 256, 0, s>>>(h->normed.as<float>(), H, W, Ci, b.ws, g.nWh, rw,
+                                                                   h->codes_a.as<int8_t>(), h->quads_a.as<__half>(),
+                                                                   round128(rw));
+            e = cudaGetLastError();
+        } else {
+            e = quantize_rows_q8(h->normed.as<float>(), Ci, T, Ci, h->codes_a.p, h->quads_a.p, round128(T), s);
+        }
+        if (!hlaunched(h, e, "hiera qkv input") ||
+            !h_mmq(h, h->codes_a.p, h->quads_a.p, rw, b.qkv.q, MMQ_OUT_F32, b.qkv_b.as<float>(), h->qkv.as<float>(), 0,
+                   nullptr, nullptr, 0))
+            return false;
     }
-    if (!hlaunched(h, e, "hiera qkv input") ||
-        !h_mmq(h, h->codes_a.p, h->quads_a.p, rw, b.qkv, MMQ_OUT_F32, b.qkv_b.as<float>(), h->qkv.as<float>(), 0,
-               nullptr, nullptr, 0))
-        return false;
     // 4. Q pooling inside the windows
     const float *qptr = h->qkv.as<float>();
     int64_t q_ld = 3 * Co;
@@ -595,24 +674,34 @@ bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
             return false;
     }
     // 6. output projection
-    if (!hlaunched(h, quantize_rows_q8(h->attn.as<float>(), Co, rq, Co, h->codes_a.p, h->quads_a.p, round128(rq), s),
-                   "hiera quantize attn") ||
-        !h_mmq(h, h->codes_a.p, h->quads_a.p, rq, b.proj, MMQ_OUT_F32, b.proj_b.as<float>(), h->proj.as<float>(), 0,
-               nullptr, nullptr, 0))
+    if (!h_linear(h, h->attn.as<float>(), rq, Co, b.proj, b.proj_b.as<float>(), h->proj.as<float>(), 0, nullptr))
         return false;
     // 7. unpartition + crop + residual
     unpart_add_kernel<<<blocks_for(static_cast<int64_t>(To) * Co, 256), 256, 0, s>>>(sc, h->proj.as<float>(), g.Ho, g.Wo,
                                                                                      Co, g.ws_o, g.nWh_o, out);
     if (!hlaunched(h, cudaGetLastError(), "hiera unpartition")) return false;
     // 8. MLP: LN2 -> fc1 + GELU (tanh, fp16 table) -> Q8 -> fc2 + bias, residual
-    return hlaunched(h,
-                     layernorm_q8(out, To, Co, b.n2w.as<float>(), b.n2b.as<float>(), 1e-6f, g.Wo, 0, h->codes_a.p,
-                                  h->quads_a.p, round128(To), s),
-                     "hiera ln2") &&
-           h_mmq(h, h->codes_a.p, h->quads_a.p, To, b.fc1, MMQ_OUT_Q8, b.fc1_b.as<float>(), nullptr, 0, h->codes_b.p,
-                 h->quads_b.p, 2) &&
-           h_mmq(h, h->codes_b.p, h->quads_b.p, To, b.fc2, MMQ_OUT_F32, b.fc2_b.as<float>(), out, 1, nullptr, nullptr,
-                 0);
+    if (!b.fc1.dense && !b.fc2.dense)
+        return hlaunched(h,
+                         layernorm_q8(out, To, Co, b.n2w.as<float>(), b.n2b.as<float>(), 1e-6f, g.Wo, 0, h->codes_a.p,
+                                      h->quads_a.p, round128(To), s),
+                         "hiera ln2") &&
+               h_mmq(h, h->codes_a.p, h->quads_a.p, To, b.fc1.q, MMQ_OUT_Q8, b.fc1_b.as<float>(), nullptr, 0,
+                     h->codes_b.p, h->quads_b.p, 2) &&
+               h_mmq(h, h->codes_b.p, h->quads_b.p, To, b.fc2.q, MMQ_OUT_F32, b.fc2_b.as<float>(), out, 1, nullptr,
+                     nullptr, 0);
+    // a block with an F16 / F32 MLP weight: the same steps on f32 rows
+    const int64_t nh = static_cast<int64_t>(To) * 4 * Co;
+    if (!ensure_buf(h->hid, static_cast<size_t>(nh) * 4)) return false;
+    ln_rows_kernel<<<blocks_for(To, 8), 256, 0, s>>>(out, To, Co, b.n2w.as<float>(), b.n2b.as<float>(), 1e-6f,
+                                                     h->normed.as<float>());
+    if (!hlaunched(h, cudaGetLastError(), "hiera ln2") ||
+        !h_linear(h, h->normed.as<float>(), To, Co, b.fc1, b.fc1_b.as<float>(), h->hid.as<float>(), 0, nullptr))
+        return false;
+    gelu_tanh_inplace_kernel<<<blocks_for(nh, 256), 256, 0, s>>>(h->hid.as<float>(), nh);
+    return hlaunched(h, cudaGetLastError(), "hiera gelu") &&
+           h_linear(h, h->hid.as<float>(), To, 4 * Co, b.fc2, b.fc2_b.as<float>(), out, 1, h->shortf.as<float>(),
+                    true);
 }
 
 bool run_fpn(Hiera *h) {
@@ -699,10 +788,10 @@ bool check_ready(Hiera *h) {
         const HBlock &b = h->blk[i];
         const std::string p = "hiera.blocks." + std::to_string(i);
         if (!b.n1w.p || !b.n1b.p || !b.n2w.p || !b.n2b.p) h->missing.push_back(p + ".norm1/norm2");
-        if (!b.qkv.set || !b.qkv_b.p) h->missing.push_back(p + ".attn.qkv");
-        if (!b.proj.set || !b.proj_b.p) h->missing.push_back(p + ".attn.proj");
-        if (!b.fc1.set || !b.fc1_b.p || !b.fc2.set || !b.fc2_b.p) h->missing.push_back(p + ".mlp");
-        if (b.dim_in != b.dim_out && (!b.dproj.set || !b.dproj_b.p)) h->missing.push_back(p + ".proj");
+        if (!b.qkv.set() || !b.qkv_b.p) h->missing.push_back(p + ".attn.qkv");
+        if (!b.proj.set() || !b.proj_b.p) h->missing.push_back(p + ".attn.proj");
+        if (!b.fc1.set() || !b.fc1_b.p || !b.fc2.set() || !b.fc2_b.p) h->missing.push_back(p + ".mlp");
+        if (b.dim_in != b.dim_out && (!b.dproj.set() || !b.dproj_b.p)) h->missing.push_back(p + ".proj");
     }
     for (int j = 0; j < 4; ++j)
         if (!h->fpn[j].w16.p || !h->fpn[j].b.p) h->missing.push_back("fpn.convs." + std::to_string(j));
@@ -722,7 +811,7 @@ using namespace b200;
 sam3b200_hiera *sam3b200_hiera_create(sam3b200_backend *hb, const sam3b200_hiera_hparams *hp) {
     auto *be = reinterpret_cast<Backend *>(hb);
     if (!be || !hp) return nullptr;
-    if (hp->img <= 0 || hp->img % 32 != 0 || hp->embed <= 0 || hp->embed % 32 != 0 || hp->heads <= 0 ||
+    if (hp->img <= 0 || hp->img % 32 != 0 || hp->embed <= 0 || hp->embed % 8 != 0 || hp->heads <= 0 ||
         hp->neck_dim <= 0 || hp->neck_dim % 8 != 0 || hp->window_spec[0] <= 0 || hp->bkg_h <= 0 || hp->bkg_w <= 0 ||
         hp->scalp < 0 || hp->scalp > 3) {
         set_error("hiera_create: unsupported hyperparameters");
@@ -734,7 +823,7 @@ sam3b200_hiera *sam3b200_hiera_create(sam3b200_backend *hb, const sam3b200_hiera
     h->hp = *hp;
     h->S = (hp->img + 2 * 3 - 7) / 4 + 1;
     if (!hiera_metadata(h)) {
-        set_error("hiera_create: block dimensions must be multiples of 32 and divisible by the head count");
+        set_error("hiera_create: block dimensions must be multiples of 8 and divisible by the head count");
         delete h;
         return nullptr;
     }
@@ -834,7 +923,7 @@ int sam3b200_hiera_set_tensor(sam3b200_hiera *hh, const char *name_c, int type, 
         if (r == "mlp.fc1.bias") return vec(b.fc1_b, 4 * b.dim_out);
         if (r == "mlp.fc2.bias") return vec(b.fc2_b, b.dim_out);
         if (r == "proj.bias") return vec(b.dproj_b, b.dim_out);
-        QWeight *w = nullptr;
+        HLinear *w = nullptr;
         int64_t K = 0, N = 0;
         if (r == "attn.qkv.weight") w = &b.qkv, K = b.dim_in, N = 3 * b.dim_out;
         else if (r == "attn.proj.weight") w = &b.proj, K = b.dim_out, N = b.dim_out;
@@ -847,7 +936,17 @@ int sam3b200_hiera_set_tensor(sam3b200_hiera *hh, const char *name_c, int type, 
                           (long long)K, (long long)N);
                 return SAM3B200_STATUS_FAILED;
             }
-            return upload_qweight(h->be, *w, type, data, K, N) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+            if (type == SAM3B200_TYPE_F16 || type == SAM3B200_TYPE_F32) {
+                if (w->dense) sam3b200_weight_free(reinterpret_cast<sam3b200_backend *>(h->be), w->dense);
+                w->dense = sam3b200_weight_upload(reinterpret_cast<sam3b200_backend *>(h->be), type, data, K, N);
+                w->q.set = false;
+                return w->dense ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+            }
+            if (w->dense) {
+                sam3b200_weight_free(reinterpret_cast<sam3b200_backend *>(h->be), w->dense);
+                w->dense = nullptr;
+            }
+            return upload_qweight(h->be, w->q, type, data, K, N) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
         }
     }
     set_error("hiera: unknown tensor %s", name_c);

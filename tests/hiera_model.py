@@ -9,12 +9,23 @@ HIERA_TINY = dict(embed=96, heads=1, stages=[1, 2, 7, 2], q_pool=3, window_spec=
                   global_idx=[5, 7, 9], bkg_h=7, bkg_w=7, neck_dim=256, fpn_top_down_levels=[2, 3], scalp=1)
 
 
+HIERA_BASE_PLUS = dict(embed=112, heads=2, stages=[2, 3, 16, 3], q_pool=3, window_spec=[8, 4, 14, 7],
+                       global_idx=[12, 16, 20], bkg_h=14, bkg_w=14, neck_dim=256, fpn_top_down_levels=[2, 3], scalp=1)
+F16T = 1
+
+
 def hiera_tiny(img: int) -> dict:
     return dict(HIERA_TINY, img=img)
 
 
-def make_tensors(oracle, hiera_oracle, hp: dict, seed: int = 0):
-    """-> (gpu: name -> (type, array, ne), ref: name -> array | (qtype, blocks, K, N))"""
+def hiera_base_plus(img: int) -> dict:
+    return dict(HIERA_BASE_PLUS, img=img)
+
+
+def make_tensors(oracle, hiera_oracle, hp: dict, seed: int = 0, wtype: str = "q8"):
+    """-> (gpu: name -> (type, array, ne), ref: name -> array | (qtype, blocks, K, N)).
+    wtype: "q8" -- every linear weight Q8_0; "mixed" -- Q8_0 where the row length is a multiple of 32,
+    F16 otherwise (what ggml's quantiser leaves in a Q8_0 Hiera-B+ file); "f16" -- every one F16."""
     rng = np.random.default_rng(seed)
     blocks, ends = hiera_oracle.metadata(hp)
     gpu, ref = {}, {}
@@ -26,6 +37,11 @@ def make_tensors(oracle, hiera_oracle, hp: dict, seed: int = 0):
 
     def lin(name, K, N):
         w = rng.normal(0, 0.02, size=(N, K)).astype(np.float32)
+        if wtype == "f16" or (wtype == "mixed" and K % 32 != 0):
+            w16 = w.astype(np.float16)
+            gpu[name] = (F16T, w16, (K, N))
+            ref[name] = (F16T, w16, K, N)
+            return
         q = oracle.quantize_weights(Q8_0, w)
         gpu[name] = (Q8_0, q, (K, N))
         ref[name] = (Q8_0, q, K, N)

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 from conftest import rel_err
-from hiera_model import hiera_tiny, make_tensors
+from hiera_model import hiera_base_plus, hiera_tiny, make_tensors
 
 pytestmark = pytest.mark.gpu
 
@@ -180,3 +180,63 @@ def test_block_matches_oracle_1024(oracle, hiera_oracle, backend, i):
         assert err <= 1e-2, (i, err)
     finally:
         model.free()
+
+
+@pytest.fixture(scope="module", params=["mixed", "f16"])
+def base_plus256(request, oracle, hiera_oracle, backend):
+    """Hiera-base+ (config 5's backbone: embed 112, stages 2/3/16/3, global blocks 12/16/20, 14x14
+    background embedding) at a 256x256 input; "mixed": Q8_0 weights except the ones whose row length
+    112 is no multiple of 32 (F16, as ggml's quantiser leaves them); "f16": an F16 file."""
+    hp = hiera_base_plus(256)
+    gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=9, wtype=request.param)
+    model = backend.hiera(hp)
+    model.load(gpu)
+    yield hp, model, ref
+    model.free()
+
+
+@pytest.mark.parametrize("i", [0, 1, 2, 4, 5, 12, 21, 22])
+def test_base_plus_block_matches_oracle(backend, hiera_oracle, base_plus256, i):
+    """Hiera-B+ blocks: stage 1 (dims 112, F16 linear weights in both files), the stage transitions with
+    their dimension projection (112 -> 224, 448 -> 896), a global block (12), the last stage."""
+    hp, model, ref = base_plus256
+    blocks, _ = hiera_oracle.metadata(hp)
+    m = blocks[i]
+    assert model.block_info(i) == (m["dim_in"], m["dim_out"], m["heads"], m["ws"], int(m["q_stride"]))
+    S = 64
+    for b in blocks[:i]:
+        if b["q_stride"]:
+            S //= 2
+    x = np.random.default_rng(200 + i).normal(0, 1, size=(S, S, m["dim_in"])).astype(np.float32)
+    So = S // 2 if m["q_stride"] else S
+    out = backend.alloc(So * So * m["dim_out"] * 4)
+    model.run_block(i, backend.upload(x), S, S, out)
+    backend.synchronize()
+    got = out.get((So, So, m["dim_out"]), np.float32)
+    p = f"hiera.blocks.{i}."
+    want = hiera_oracle.block(m, {k[len(p):]: v for k, v in ref.items() if k.startswith(p)}, x)
+    assert rel_err(got, want) <= 1e-2, (i, rel_err(got, want))
+
+
+def test_base_plus_encode_every_stage_on_the_gpu_trajectory(backend, hiera_oracle, base_plus256):
+    """The whole Hiera-B+ trunk + FPN at 256x256 stage by stage along the GPU's trajectory (each block
+    against the oracle block on the GPU's own input) at the fixed 1e-2 bound."""
+    hp, model, ref = base_plus256
+    blocks, ends = hiera_oracle.metadata(hp)
+    img = np.random.default_rng(8).normal(0, 1, size=(3, 256, 256)).astype(np.float32)
+    x = backend.alloc(64 * 64 * hp["embed"] * 4)
+    model.run_prefix(backend.upload(img), x)
+    backend.synchronize()
+    S, errs = 64, {}
+    cur = x.get((S, S, hp["embed"]), np.float32)
+    for i, m in enumerate(blocks):
+        So = S // 2 if m["q_stride"] else S
+        out = backend.alloc(So * So * m["dim_out"] * 4)
+        model.run_block(i, backend.upload(cur), S, S, out)
+        backend.synchronize()
+        got = out.get((So, So, m["dim_out"]), np.float32)
+        p = f"hiera.blocks.{i}."
+        errs[i] = rel_err(got, hiera_oracle.block(m, {k[len(p):]: v for k, v in ref.items() if k.startswith(p)}, cur))
+        cur, S = got, So
+    print("Hiera-B+ block errors:", ", ".join(f"{k}: {v:.2e}" for k, v in errs.items()))
+    assert max(errs.values()) <= 1e-2, errs
