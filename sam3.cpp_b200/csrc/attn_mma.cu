@@ -288,6 +288,20 @@ cudaError_t attention_mma_f32mask(int D, const float *q, AttnStrides qs, int NQ,
     }
 }
 
+cudaError_t attention_combine(int D, const float *part_o, const float2 *part_ml, int splits, int NQ, int batch,
+                              int heads, float *o, AttnStrides os, cudaStream_t s) {
+    if (NQ <= 0 || splits < 1 || batch < 1 || heads < 1) return cudaErrorInvalidValue;
+    const dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(NQ) * D + 255) / 256),
+                     static_cast<unsigned>(batch * heads));
+    switch (D) {
+    case 64: attn_combine_kernel<64><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
+    case 128: attn_combine_kernel<128><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
+    case 256: attn_combine_kernel<256><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int NQ, const __half *k, AttnStrides ks,
                                       const __half *v, AttnStrides vs, int NKV, int batch, int heads, float scale,
                                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml,

@@ -35,4 +35,9 @@ cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int
                                       float *o, AttnStrides os, int splits, float *part_o, float2 *part_ml,
                                       cudaStream_t s);
 
+// The combine pass of a split-KV attention: o = sum_z 2^(m_z - M) part_o_z / sum_z 2^(m_z - M) l_z per
+// row (part_ml = (m in log2 units, l) per split and row, part_o unnormalised).  D in {64, 128, 256}.
+cudaError_t attention_combine(int D, const float *part_o, const float2 *part_ml, int splits, int NQ, int batch,
+                              int heads, float *o, AttnStrides os, cudaStream_t s);
+
 }  // namespace b200

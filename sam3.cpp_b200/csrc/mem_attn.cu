@@ -16,6 +16,7 @@
 // 256, fp16 k and v, the keys split across CTAs).
 #include "../../include/sam3_b200.h"
 #include "attn_mma.cuh"
+#include "attn_tc256.cuh"
 #include "model_util.h"
 #include "eltwise.cuh"
 #include "row_norm.cuh"
@@ -83,8 +84,9 @@ struct MemAttn {
     // activations
     DevBuf x, xn, q, k, v, att, tmp, ffn, kvpos, out;
     // attention operands in fp16 and the split-KV partial results
-    DevBuf k16, v16, part_o, part_ml;
+    DevBuf k16, v16, q16, part_o, part_ml;
     int splits = 1;
+    bool tc = true;  // d_model 256: tcgen05 flash attention (env SAM3B200_MEM_ATTN_TC=0: the mma.sync kernel)
     // host-run staging of the inputs
     DevBuf in_curr, in_spos, in_prompt, in_ppos, in_rq, in_rk;
     std::vector<std::string> missing;
@@ -92,8 +94,8 @@ struct MemAttn {
 
 namespace {
 
-bool mok(MemAttn *m, cudaError_t e, const char *what) {
-    m->be->count(1);
+bool mok(MemAttn *m, cudaError_t e, const char *what, int n = 1) {
+    m->be->count(n);
     return cuda_ok(e, what);
 }
 
@@ -127,6 +129,27 @@ bool attend(MemAttn *m, const float *q, const float *k, const float *v, int N, i
     const int D = m->hp.d_model;
     const int64_t n = static_cast<int64_t>(NK) * D;
     cudaStream_t s = m->be->stream;
+    if (D == 256 && m->tc) {
+        // tcgen05 flash attention: q, k fp16 row-major, v transposed to fp16 [256][keys]
+        const int ldt = (NK + 63) / 64 * 64;
+        const int64_t nq = static_cast<int64_t>(N) * D;
+        ew_to_half_kernel<<<ew_blocks(nq), 256, 0, s>>>(q, nq, m->q16.as<__half>());
+        ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(k, n, m->k16.as<__half>());
+        if (!mok(m, cudaGetLastError(), "mem_attn fp16 q, k", 2) ||
+            !mok(m, v_to_half_transposed(v, NK, D, m->v16.as<__half>(), ldt, s), "mem_attn fp16 v^T"))
+            return false;
+        // no more key ranges than part_o / part_ml hold rows of N queries for
+        const int room = static_cast<int>(std::min(m->part_o.n / (static_cast<size_t>(N) * D * 4),
+                                                   m->part_ml.n / (static_cast<size_t>(N) * 8)));
+        const int splits = std::max(1, std::min(attention_tc256_splits(N, NK, m->be->num_sms), room));
+        m->be->prof_mark(1);  // profile class 1: the memory attention's attention kernels
+        const bool ok = mok(m, attention_tc256(m->q16.as<__half>(), N, m->k16.as<__half>(), NK, m->v16.as<__half>(), ldt,
+                                               scale, splits, m->part_o.as<float>(), m->part_ml.as<float2>(), out,
+                                               m->be->err, s),
+                            "mem_attn attention", 2);
+        m->be->prof_mark(1);
+        return ok;
+    }
     ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(k, n, m->k16.as<__half>());
     ew_to_half_kernel<<<ew_blocks(n), 256, 0, s>>>(v, n, m->v16.as<__half>());
     const AttnStrides rs{0, 0, D};
@@ -239,8 +262,14 @@ sam3b200_mem_attn *sam3b200_mem_attn_create(sam3b200_backend *hb, const sam3b200
     // split-KV: about two CTAs per SM for the 64-query tiles of max_tokens
     const int qtiles = static_cast<int>((N + 63) / 64);
     m->splits = std::min(8, std::max(1, (2 * be->num_sms + qtiles - 1) / qtiles));
-    const size_t sp = static_cast<size_t>(m->splits);
-    const bool ok = m->k16.alloc(NM * d * 2) && m->v16.alloc(NM * d * 2) && m->part_o.alloc(sp * N * d * 4) &&
+    const char *tc_env = std::getenv("SAM3B200_MEM_ATTN_TC");
+    m->tc = D == 256 && !(tc_env && tc_env[0] == '0');
+    // the tcgen05 path splits keys into up to num_sms / (query tiles of 128) ranges
+    const int tc_splits = std::max(1, be->num_sms / static_cast<int>((N + 127) / 128));
+    const size_t sp = static_cast<size_t>(std::max(m->splits, m->tc ? tc_splits : 1));
+    const size_t NMp = (NM + 63) / 64 * 64;  // v^T rows padded to whole 64-key tiles
+    const bool ok = m->k16.alloc(NM * d * 2) && m->v16.alloc(NMp * d * 2) && m->q16.alloc(N * d * 2) &&
+                    m->part_o.alloc(sp * N * d * 4) &&
                     m->part_ml.alloc(sp * N * 8) && m->x.alloc(N * d * 4) && m->xn.alloc(N * d * 4) &&
                     m->q.alloc(N * d * 4) &&
                     m->k.alloc(NM * d * 4) && m->v.alloc(NM * d * 4) && m->att.alloc(N * d * 4) &&

@@ -184,7 +184,7 @@ struct SamDec {
     Mlp3 hyper[4], iou_head, obj_head;
     // prompt encoder (host copies: the sparse embeddings are formed on the host per call)
     std::vector<float> pe_gauss, point_emb[4], not_a_point, no_mask;
-    DevBuf dense_pe, no_mask_dev;
+    DevBuf dense_pe, no_mask_dev, track_tok;  // track_tok: the token rows of a propagated frame's decode
     std::vector<std::string> missing;
     // activations
     DevBuf tok, qpe, q2, keys, kpe, k2, tq, tk, tv, to, tmp_tok, tmp_keys, mlp, cm, up1, up1b, hs1, fs, up2, hs0,
@@ -674,20 +674,23 @@ int sam3b200_sam_dec_run_tracking(sam3b200_sam_dec *hd, const float *cond_feats_
     }
     cudaSetDevice(d->be->device);
     if (!check_ready(d)) return SAM3B200_STATUS_FAILED;
-    // tokens: [obj_score?, iou, masks x n, not_a_point] -- the single padding token of sam3_propagate_single
+    // tokens: [obj_score?, iou, masks x n, not_a_point] -- the single padding token of sam3_propagate_single;
+    // the same every frame, so they are formed once and kept on the device
     const int D = d->D;
     d->ntok = d->nspecial + 1;
-    std::vector<float> tok(static_cast<size_t>(d->ntok) * D);
-    size_t o = 0;
-    if (d->hp.pred_obj_scores) std::copy(d->tok_obj.begin(), d->tok_obj.end(), tok.begin() + (o++) * D);
-    std::copy(d->tok_iou.begin(), d->tok_iou.end(), tok.begin() + (o++) * D);
-    std::copy(d->tok_masks.begin(), d->tok_masks.end(), tok.begin() + o * D);
-    o += d->nmask;
-    std::copy(d->not_a_point.begin(), d->not_a_point.end(), tok.begin() + o * D);
-    const size_t bytes = tok.size() * 4;
-    if (!cuda_ok(cudaMemcpyAsync(d->tok.p, tok.data(), bytes, cudaMemcpyHostToDevice, d->be->stream), "tokens") ||
-        !cuda_ok(cudaMemcpyAsync(d->qpe.p, tok.data(), bytes, cudaMemcpyHostToDevice, d->be->stream), "tokens") ||
-        !cuda_ok(cudaStreamSynchronize(d->be->stream), "tokens sync"))
+    const size_t bytes = static_cast<size_t>(d->ntok) * D * 4;
+    if (!d->track_tok.p) {
+        std::vector<float> tok(static_cast<size_t>(d->ntok) * D);
+        size_t o = 0;
+        if (d->hp.pred_obj_scores) std::copy(d->tok_obj.begin(), d->tok_obj.end(), tok.begin() + (o++) * D);
+        std::copy(d->tok_iou.begin(), d->tok_iou.end(), tok.begin() + (o++) * D);
+        std::copy(d->tok_masks.begin(), d->tok_masks.end(), tok.begin() + o * D);
+        o += d->nmask;
+        std::copy(d->not_a_point.begin(), d->not_a_point.end(), tok.begin() + o * D);
+        if (!upload(d->track_tok, tok.data(), bytes, d->be->stream)) return SAM3B200_STATUS_FAILED;
+    }
+    if (!cuda_ok(cudaMemcpyAsync(d->tok.p, d->track_tok.p, bytes, cudaMemcpyDeviceToDevice, d->be->stream), "tokens") ||
+        !cuda_ok(cudaMemcpyAsync(d->qpe.p, d->track_tok.p, bytes, cudaMemcpyDeviceToDevice, d->be->stream), "tokens"))
         return SAM3B200_STATUS_FAILED;
     return decode(d, cond_feats_dev, feat_s0_dev, feat_s1_dev, false) ? SAM3B200_STATUS_SUCCESS
                                                                        : SAM3B200_STATUS_FAILED;

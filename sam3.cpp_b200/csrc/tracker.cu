@@ -141,7 +141,12 @@ struct Tracker {
     DevBuf src_pos, pe64, rope_q, rope_k;
     // per frame
     DevBuf prompt, prompt_pos, mask_u8, synth, rgb, chw;
-    std::vector<float> ptr_pos_host;
+    // pinned: the pointer positional rows reach the device without a sync; rewritten by the next
+    // instance only after the decoder's readback has synchronised the stream
+    float *ptr_pos_host = nullptr;
+    ~Tracker() {
+        if (ptr_pos_host) cudaFreeHost(ptr_pos_host);
+    }
     std::vector<std::unique_ptr<Instance>> inst;
     int next_id = 1;
     int frame_index = 0;
@@ -260,11 +265,10 @@ int64_t build_prompt(Tracker *t, Instance *in, int cur_frame, int *n_ptr_tok, in
     *m_spatial = n_sel * static_cast<int64_t>(t->N);
     const int P = std::min(static_cast<int>(in->ptrs.size()), t->hp.max_obj_ptrs);
     int64_t tok = *m_spatial;
-    t->ptr_pos_host.assign(static_cast<size_t>(P) * t->split * t->MD, 0.0f);
     for (int p = 0; p < P; ++p) {
         const Ptr &pp = in->ptrs[static_cast<size_t>(p)];
         const int rel = std::max(1, std::abs(cur_frame - pp.frame));
-        float *row = t->ptr_pos_host.data() + static_cast<size_t>(p) * t->split * t->MD;
+        float *row = t->ptr_pos_host + static_cast<size_t>(p) * t->split * t->MD;
         obj_ptr_pos_row(t->D, t->MD, rel, t->tpos_w.empty() ? nullptr : t->tpos_w.data(),
                         t->tpos_b.empty() ? nullptr : t->tpos_b.data(), row);
         for (int k = 1; k < t->split; ++k) std::copy(row, row + t->MD, row + static_cast<size_t>(k) * t->MD);
@@ -274,12 +278,10 @@ int64_t build_prompt(Tracker *t, Instance *in, int cur_frame, int *n_ptr_tok, in
                 "tracker pointer tokens", 0))
             return -1;
     }
-    if (P > 0 && !tl(t, cudaMemcpyAsync(pos + tok * t->MD, t->ptr_pos_host.data(), t->ptr_pos_host.size() * 4,
-                                        cudaMemcpyHostToDevice, s),
+    if (P > 0 && !tl(t, cudaMemcpyAsync(pos + tok * t->MD, t->ptr_pos_host,
+                                        static_cast<size_t>(P) * t->split * t->MD * 4, cudaMemcpyHostToDevice, s),
                      "tracker pointer positions", 0))
         return -1;
-    // the pageable source must stay valid until the copy has read it
-    if (P > 0 && !cuda_ok(cudaStreamSynchronize(s), "tracker prompt sync")) return -1;
     *n_ptr_tok = P * t->split;
     return tok + static_cast<int64_t>(P) * t->split;
 }
@@ -363,7 +365,9 @@ sam3b200_tracker *sam3b200_tracker_create(sam3b200_backend *h, const sam3b200_tr
          upload(t->pe64, pe.data(), pe.size() * 4, be->stream) && upload(t->rope_q, rq.data(), rq.size() * 4, be->stream) &&
          upload(t->rope_k, rk.data(), rk.size() * 4, be->stream) &&
          t->prompt.alloc(static_cast<size_t>(t->m_max) * t->MD * 4) &&
-         t->prompt_pos.alloc(static_cast<size_t>(t->m_max) * t->MD * 4);
+         t->prompt_pos.alloc(static_cast<size_t>(t->m_max) * t->MD * 4) &&
+         cuda_ok(cudaMallocHost(&t->ptr_pos_host, static_cast<size_t>(hp->max_obj_ptrs + 1) * t->D * 4),
+                 "cudaMallocHost(pointer positions)");
     if (!ok) {
         delete t;
         return nullptr;
