@@ -333,7 +333,8 @@ def run_video(args, model_mod) -> int:
             "e2e": {"value": total_frames / (e2e_ms / 1e3), "unit": "frames/s",
                     "h2d_bytes_per_step": int(VIDEO_FRAMES * S * S * 3 * world),
                     "d2h_bytes_per_step": int(VIDEO_FRAMES * S * S * world)},
-            "roofline": {"kernel": "memory attention's attention kernels (fp16 mma.sync, split over keys)",
+            "roofline": {"kernel": "attn_tc256_kernel: the memory attention's attention (tcgen05, fp16, split over "
+                                   "keys) + its combine pass",
                          "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if achieved else None, "traffic": None,
                          "peak_source": "MEASURED_PEAKS.json bf16_tflops (dense fp16 runs at the bf16 rate)"
