@@ -20,6 +20,7 @@
 // tensor-core GEMMs around a row softmax.
 #include "../../include/sam3_b200.h"
 #include "act.cuh"
+#include "sgemm.cuh"
 #include "attn_simt.cuh"
 #include "gemm_f16.cuh"
 #include "model_util.h"
@@ -209,36 +210,6 @@ __global__ void __launch_bounds__(256) softmax_rows_f16_kernel(const float *__re
     for (int i = threadIdx.x; i < n; i += blockDim.x) pr[i] = __float2half_rn(expf(sr[i] - m) * inv);
 }
 
-// Patch embedding in f32, as the reference's F32 kernel computes it
-// (ggml_conv_2d with an F32 kernel: f32 im2col + f32 MUL_MAT, sam3.cpp:4474):
-// Conv2d(3 -> E, k 7, s 4, p 3) + bias, then + pe; x [P][E] token-major.  One
-// thread per (pixel, channel); the kernel [E][147] sits in shared memory.
-__global__ void patch_conv_f32_kernel(const float *__restrict__ img, int img_side, int S, int E,
-                                      const float *__restrict__ w, const float *__restrict__ bias,
-                                      const float *__restrict__ pe, float *__restrict__ x) {
-    extern __shared__ float wsm[];
-    for (int i = threadIdx.x; i < E * 147; i += blockDim.x) wsm[i] = w[i];
-    __syncthreads();
-    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= static_cast<int64_t>(S) * S * E) return;
-    const int e = static_cast<int>(idx % E);
-    const int p = static_cast<int>(idx / E);
-    const int ox = p % S, oy = p / S;
-    const float *wr = wsm + e * 147;
-    float acc = 0.f;
-    for (int ic = 0; ic < 3; ++ic)
-        for (int ky = 0; ky < 7; ++ky) {
-            const int iy = oy * 4 + ky - 3;
-            if (iy < 0 || iy >= img_side) continue;
-            const float *row = img + (static_cast<int64_t>(ic) * img_side + iy) * img_side;
-            for (int kx = 0; kx < 7; ++kx) {
-                const int ix = ox * 4 + kx - 3;
-                if (ix >= 0 && ix < img_side) acc = fmaf(row[ix], wr[(ic * 7 + ky) * 7 + kx], acc);
-            }
-        }
-    x[idx] = __fadd_rn(__fadd_rn(acc, bias[e]), pe[idx]);
-}
-
 // FPN top-down fusion: y[t] = lat[t] + prev[nearest 2x source of t] (sam3.cpp:4568-4573)
 __global__ void upsample2_add_kernel(const float *lat, const float *__restrict__ prev, int H, int W, int D,
                                      float *y) {  // y may alias lat
@@ -328,6 +299,7 @@ struct Hiera {
     DevBuf stage_out[4], fpn_out[4], x16;
     DevBuf gq, gk, gvt, gs, gp;  // global attention on the tensor cores: fp16 q, k, v^T, f32 scores, fp16 probs
     DevBuf xwin, hid;            // blocks with F16 / F32 linear layers: f32 windowed rows, MLP hidden rows
+    DevBuf col;                  // the patch embedding's f32 im2col rows
     ~Hiera() {
         for (auto &b : blk)
             for (HLinear *l : {&b.qkv, &b.proj, &b.fc1, &b.fc2, &b.dproj})
@@ -551,12 +523,17 @@ bool make_pe(Hiera *h) {
 bool run_prefix(Hiera *h, const float *img_chw, float *x) {
     const auto &hp = h->hp;
     const int S = h->S, E = hp.embed;
-    const int smem = E * 147 * 4;
-    if (!hlaunched(h, cudaFuncSetAttribute(patch_conv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                   "hiera patch smem", 0))
+    cudaStream_t s = h->be->stream;
+    // f32 im2col [S*S][3*7*7] and an f32 GEMM with the kernel [E][147] (ggml_conv_2d with an F32
+    // kernel), then + bias and + the positional embedding in that order
+    const int64_t P = static_cast<int64_t>(S) * S, n = P * E;
+    if (!ensure_buf(h->col, static_cast<size_t>(P) * 147 * 4)) return false;
+    if (!hlaunched(h, im2col_chw(img_chw, 3, hp.img, hp.img, 7, 4, 3, S, S, h->col.as<float>(), s), "hiera patch im2col") ||
+        !hlaunched(h, sgemm_nt(h->col.as<float>(), 147, 1, h->patch_w32.as<float>(), 147, 1, static_cast<int>(P), E, 147,
+                               h->patch_b.as<float>(), x, E, false, s),
+                   "hiera patch gemm"))
         return false;
-    patch_conv_f32_kernel<<<blocks_for(static_cast<int64_t>(S) * S * E, 256), 256, smem, h->be->stream>>>(
-        img_chw, hp.img, S, E, h->patch_w32.as<float>(), h->patch_b.as<float>(), h->pe.as<float>(), x);
+    add_inplace_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, h->pe.as<float>(), n);
     return hlaunched(h, cudaGetLastError(), "hiera patch embedding");
 }
 

@@ -20,6 +20,7 @@
 #include "../../include/sam3_b200.h"
 #include "act.cuh"
 #include "model_util.h"
+#include "sgemm.cuh"
 #include "row_norm.cuh"
 
 #include <cmath>
@@ -58,54 +59,6 @@ __global__ void bilinear_kernel(const float *__restrict__ src, int sw, int sh, f
         v = __fadd_rn(__fmul_rn(s, scale), bias);
     }
     dst[i] = v;
-}
-
-// Direct convolution, channel-major in and out: out[o][oy][ox] = bias[o] +
-// sum over (c, ky, kx) of in(c, oy*s - p + ky, ox*s - p + kx) * w[o][c][ky][kx]
-// (zero outside the map); in_f16 rounds the input to fp16 first.
-__global__ void conv_direct_kernel(const float *__restrict__ x, int C, int IH, int IW, const float *__restrict__ w,
-                                   const float *__restrict__ bias, int O, int K, int S, int P, int OH, int OW,
-                                   int in_f16, float *__restrict__ y) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<int64_t>(O) * OH * OW) return;
-    const int ox = static_cast<int>(i % OW), oy = static_cast<int>((i / OW) % OH), o = static_cast<int>(i / OW / OH);
-    float acc = 0.0f;
-    for (int c = 0; c < C; ++c) {
-        const float *xc = x + static_cast<int64_t>(c) * IH * IW;
-        const float *wc = w + (static_cast<int64_t>(o) * C + c) * K * K;
-        for (int ky = 0; ky < K; ++ky) {
-            const int iy = oy * S - P + ky;
-            if (iy < 0 || iy >= IH) continue;
-            for (int kx = 0; kx < K; ++kx) {
-                const int ix = ox * S - P + kx;
-                if (ix < 0 || ix >= IW) continue;
-                float v = xc[static_cast<int64_t>(iy) * IW + ix];
-                if (in_f16) v = __half2float(__float2half_rn(v));
-                acc = fmaf(v, wc[ky * K + kx], acc);
-            }
-        }
-    }
-    y[i] = __fadd_rn(acc, bias[o]);
-}
-
-// 1x1 convolution to token-major out[p][o] = bias[o] + sum_c x(p, c) w[o][c],
-// the input element (p, c) at x[p * sp + c * sc] (either layout).
-__global__ void pointwise_kernel(const float *__restrict__ x, int64_t sp, int64_t sc, int64_t P, int C,
-                                 const float *__restrict__ w, const float *__restrict__ bias, int O, int in_f16,
-                                 float *__restrict__ y) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= P * O) return;
-    const int o = static_cast<int>(i % O);
-    const int64_t p = i / O;
-    const float *wr = w + static_cast<int64_t>(o) * C;
-    const float *xr = x + p * sp;
-    float acc = 0.0f;
-    for (int c = 0; c < C; ++c) {
-        float v = xr[c * sc];
-        if (in_f16) v = __half2float(__float2half_rn(v));
-        acc = fmaf(v, wr[c], acc);
-    }
-    y[i] = __fadd_rn(acc, bias[o]);
 }
 
 // Depthwise KxK convolution, padding K/2, token-major [H][W][C] in and out
@@ -180,6 +133,7 @@ struct MemEnc {
     DevBuf dsnw[4], dsnb[4], noobj;
     std::vector<FuserW> fu;
     DevBuf logits, hires, a, b, pixin, x, h, xn, mlp, out;
+    DevBuf col;  // im2col rows of the downsampler's convolutions
     std::vector<std::string> missing;
 };
 
@@ -208,9 +162,14 @@ bool forward(MemEnc *m, const float *logits, int mw, int mh, const float *pixf, 
         const ConvW &c = m->ds[st];
         const int os = (side + 2 - 3) / 2 + 1;
         const int64_t n = static_cast<int64_t>(c.oc) * os * os;
-        conv_direct_kernel<<<eblocks(n), 256, 0, s>>>(a, c.ic, side, side, c.w.as<float>(), c.b.as<float>(), c.oc, 3, 2,
-                                                      1, os, os, c.f16 ? 1 : 0, b);
-        if (!eok(m, cudaGetLastError(), "mem_enc downsample conv")) return false;
+        // 3x3 s2 p1: f32 im2col + f32 GEMM, channel-major out [oc][os * os] (bias per output channel)
+        const int64_t pix = static_cast<int64_t>(os) * os, kk = static_cast<int64_t>(c.ic) * 9;
+        if (m->col.n < static_cast<size_t>(pix * kk) * 4 && !m->col.alloc(static_cast<size_t>(pix * kk) * 4)) return false;
+        if (!eok(m, im2col_chw(a, c.ic, side, side, 3, 2, 1, os, os, m->col.as<float>(), s), "mem_enc im2col") ||
+            !eok(m, sgemm_nt(c.w.as<float>(), kk, 1, m->col.as<float>(), kk, 1, c.oc, static_cast<int>(pix),
+                             static_cast<int>(kk), c.b.as<float>(), b, pix, false, s, c.f16, true),
+                 "mem_enc downsample conv"))
+            return false;
         ln_channels_kernel<<<eblocks(static_cast<int64_t>(os) * os), 256, 0, s>>>(
             b, c.oc, static_cast<int64_t>(os) * os, m->dsnw[st].as<float>(), m->dsnb[st].as<float>(), 1e-6f, a);
         if (!eok(m, cudaGetLastError(), "mem_enc downsample norm")) return false;
@@ -220,11 +179,16 @@ bool forward(MemEnc *m, const float *logits, int mw, int mh, const float *pixf, 
     }
     // final 1x1 of the downsampler (channel-major a [D][P] -> token-major b [P][D])
     float *x = m->x.as<float>(), *h = m->h.as<float>(), *xn = m->xn.as<float>();
-    pointwise_kernel<<<eblocks(PD), 256, 0, s>>>(a, 1, P, P, D, m->ds[4].w.as<float>(), m->ds[4].b.as<float>(), D,
-                                                 m->ds[4].f16 ? 1 : 0, b);
+    // (1x1 convolutions as f32 GEMMs: ggml_conv_2d of an F32 kernel is an f32 MUL_MAT)
+    if (!eok(m, sgemm_nt(a, 1, P, m->ds[4].w.as<float>(), D, 1, static_cast<int>(P), D, D, m->ds[4].b.as<float>(), b, D,
+                         m->ds[4].f16, s),
+             "mem_enc downsample 1x1"))
+        return false;
     // pixel projection (token-major in and out), then x = pix + mask features
-    pointwise_kernel<<<eblocks(PD), 256, 0, s>>>(pixf, D, 1, P, D, m->pix.w.as<float>(), m->pix.b.as<float>(), D,
-                                                 m->pix.f16 ? 1 : 0, x);
+    if (!eok(m, sgemm_nt(pixf, D, 1, m->pix.w.as<float>(), D, 1, static_cast<int>(P), D, D, m->pix.b.as<float>(), x, D,
+                         m->pix.f16, s),
+             "mem_enc pixel projection"))
+        return false;
     me_add_kernel<<<eblocks(PD), 256, 0, s>>>(x, b, PD, x);
     if (!eok(m, cudaGetLastError(), "mem_enc fuse")) return false;
     for (const FuserW &f : m->fu) {
@@ -245,9 +209,10 @@ bool forward(MemEnc *m, const float *logits, int mw, int mh, const float *pixf, 
         if (!eok(m, cudaGetLastError(), "mem_enc fuser residual")) return false;
     }
     float *out = m->out.as<float>();
-    pointwise_kernel<<<eblocks(P * MD), 256, 0, s>>>(x, D, 1, P, D, m->outp.w.as<float>(), m->outp.b.as<float>(), MD,
-                                                     m->outp.f16 ? 1 : 0, out);
-    if (!eok(m, cudaGetLastError(), "mem_enc out proj")) return false;
+    if (!eok(m, sgemm_nt(x, D, 1, m->outp.w.as<float>(), D, 1, static_cast<int>(P), MD, D, m->outp.b.as<float>(), out,
+                         MD, m->outp.f16, s),
+             "mem_enc out proj"))
+        return false;
     if (obj_score <= 0.0f && m->noobj.p) {  // occluded: + no_obj_embed_spatial (sam3.cpp:11602-11615)
         add_channel_kernel<<<eblocks(P * MD), 256, 0, s>>>(out, m->noobj.as<float>(), MD, P * MD);
         if (!eok(m, cudaGetLastError(), "mem_enc no-object embedding")) return false;
