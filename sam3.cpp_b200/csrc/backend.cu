@@ -296,7 +296,7 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
         const size_t quad_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
         const size_t min_bytes = static_cast<size_t>(K / 32) * w->ld * 2;
         ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
-             cuda_ok(cudaMalloc(&w->codes, static_cast<size_t>(N) * K), "cudaMalloc(weight codes)") &&
+             cuda_ok(cudaMalloc(&w->codes, weight_code_bytes(type, N, K)), "cudaMalloc(weight codes)") &&
              cuda_ok(cudaMalloc(&w->quads, quad_bytes), "cudaMalloc(weight scale quads)") &&
              cuda_ok(cudaMemsetAsync(w->quads, 0, quad_bytes, be->stream), "memset scale quads") &&
              (type != SAM3B200_TYPE_Q4_1 || (cuda_ok(cudaMalloc(&w->mins, min_bytes), "cudaMalloc(weight minima)") &&
@@ -398,7 +398,7 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
         return SAM3B200_STATUS_FAILED;
     MmqArgs a;
     a.a = QMatrix{be->act_codes, be->act_quads, Mi, w->K, lda};
-    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld};
+    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld, weight_nib(w->type)};
     a.bias = bias;
     a.y = dst;
     a.ldy = ldd;

@@ -100,7 +100,7 @@ static bool mmq(Vit *v, const void *codes, const void *quads, const QWeight &w, 
                 float *y, int add, const int *rowmap, void *out_codes, void *out_quads, int gelu) {
     MmqArgs a;
     a.a = QMatrix{codes, quads, v->T, w.K, v->Tpad};
-    a.b = QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld};
+    a.b = QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld, w.nib};
     a.bias = bias;
     a.y = y;
     a.ldy = w.N;
@@ -122,7 +122,7 @@ static bool mmq(Vit *v, const void *codes, const void *quads, const QWeight &w, 
 static bool mmq_qkv(Vit *v, const BlockW &w, int win_tokens) {
     MmqArgs a;
     a.a = QMatrix{v->codes_a.p, v->quads_a.p, v->T, w.qkv.K, v->Tpad};
-    a.b = QMatrix{w.qkv.codes.p, w.qkv.quads.p, w.qkv.N, w.qkv.K, w.qkv.ld};
+    a.b = QMatrix{w.qkv.codes.p, w.qkv.quads.p, w.qkv.N, w.qkv.K, w.qkv.ld, w.qkv.nib};
     a.bias = w.qkv_b.as<float>();
     a.y = nullptr;
     a.ldy = 0;

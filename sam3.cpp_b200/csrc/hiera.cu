@@ -322,7 +322,7 @@ bool h_mmq(Hiera *h, const void *codes, const void *quads, int M, const QWeight 
     MmqArgs a;
     const int ld = round128(M);
     a.a = QMatrix{codes, quads, M, w.K, ld};
-    a.b = QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld};
+    a.b = QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld, w.nib};
     a.bias = bias;
     a.y = y;
     a.ldy = w.N;

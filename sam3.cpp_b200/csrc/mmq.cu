@@ -111,7 +111,8 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 }
 
 // ---------------------------------------------------------------------------
-// Weight repack: ggml blocks -> int8 codes + scale quads.
+// Weight repack: ggml blocks -> codes (int8 for Q8_0, the blocks' own nibble
+// bytes for Q4_0 / Q4_1) + scale quads.
 // ---------------------------------------------------------------------------
 __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ blocks, int N, int K,
                                      int8_t *__restrict__ codes, uint4 *__restrict__ quads, __half *__restrict__ mins,
@@ -122,22 +123,19 @@ __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ block
     if (w >= static_cast<int64_t>(N) * nblk) return;
     const int n = static_cast<int>(w / nblk);
     const int b = static_cast<int>(w % nblk);
-    int code;
     const uint8_t *blk;
     if (type == 8) {  // Q8_0 {fp16 d; int8 qs[32]}
         blk = blocks + w * 34;
-        code = static_cast<int8_t>(blk[2 + lane]);
-    } else if (type == 2) {  // Q4_0 {fp16 d; uint8 qs[16]}: low nibbles 0..15, high 16..31
-        blk = blocks + w * 18;
-        const uint8_t byte = blk[2 + (lane & 15)];
-        code = (lane < 16 ? (byte & 0x0F) : (byte >> 4)) - 8;
-    } else {                 // Q4_1 {fp16 d; fp16 m; uint8 qs[16]}: code = nibble, value = d * code + m
-        blk = blocks + w * 20;
-        const uint8_t byte = blk[4 + (lane & 15)];
-        code = lane < 16 ? (byte & 0x0F) : (byte >> 4);
-        if (lane == 0) mins[static_cast<int64_t>(b) * ld + n] = __half(__half_raw{static_cast<unsigned short>(blk[2] | (blk[3] << 8))});
+        codes[static_cast<int64_t>(n) * K + b * 32 + lane] = static_cast<int8_t>(blk[2 + lane]);
+    } else {
+        // Q4_0 {fp16 d; uint8 qs[16]} (code = nibble - 8), Q4_1 {fp16 d; fp16 m; uint8 qs[16]}
+        // (code = nibble, value = d * code + m): the 16 nibble bytes are kept as they are
+        blk = blocks + w * (type == 2 ? 18 : 20);
+        if (lane < 16)
+            codes[static_cast<int64_t>(n) * (K / 2) + b * 16 + lane] = static_cast<int8_t>(blk[(type == 2 ? 2 : 4) + lane]);
+        if (type == 3 && lane == 0)
+            mins[static_cast<int64_t>(b) * ld + n] = __half(__half_raw{static_cast<unsigned short>(blk[2] | (blk[3] << 8))});
     }
-    codes[static_cast<int64_t>(n) * K + b * 32 + lane] = static_cast<int8_t>(code);
     if (lane == 0) {
         const uint32_t dbits = static_cast<uint32_t>(blk[0] | (blk[1] << 8));
         uint32_t rec[4] = {0u, 0u, 0u, 0u};  // d in fp16 slot b % 8
@@ -188,7 +186,7 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
 // zero), a 2 KB zero region (the unused second K-chunk of every scale
 // operand), barriers.
 // ---------------------------------------------------------------------------
-template <int BN_, int EPQ_ = 2>
+template <int BN_, int EPQ_ = 2, int NIB_ = 0>
 struct TcCfg {
     static constexpr int BM = 128;                  // MMA rows
     static constexpr int ROWS = 96;                 // tokens per tile
@@ -212,7 +210,13 @@ struct TcCfg {
     static constexpr int SLOT_COLS = 2 * BN;        // one K-block: I (BN columns) then S (BN columns)
     static constexpr int SLOTS = 512 / SLOT_COLS;   // K-blocks in flight between MMA and epilogue
     static constexpr int TMEM_COLS = 512;
-    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+    // 4-bit B codes (NIB = 1, Q4_0): each stage's nibble bytes land here (BN rows x 64 bytes, as
+    // stored) and warps 9 and 13 unpack them into the stage's swizzled int8 B operand
+    static constexpr int NIB = NIB_;
+    static constexpr int RAW_STAGE = BN * BK / 2;
+    static constexpr int RAW_OFF = BAR_OFF + 256;
+    static constexpr int SMEM_BYTES = RAW_OFF + (NIB ? STAGES * RAW_STAGE : 0) + 1024;
+    static_assert(!NIB || (BN == 128 && EPQ == 4), "4-bit B codes are unpacked by the idle warps 9 and 13");
     static_assert(STAGE_BYTES % 1024 == 0, "stage alignment");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -222,6 +226,7 @@ enum : int {
     ERR_WAIT_FULL_MMA = 2,
     ERR_WAIT_TEMPTY = 4,
     ERR_WAIT_TFULL = 16,
+    ERR_WAIT_RAW = 32,
 };
 
 // No-swizzle K-major operand descriptor for the K=16 scale MMA: core
@@ -375,20 +380,21 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
     }
 }
 
-template <int MODE, int CVT, int BN, int EPQ>
+template <int MODE, int CVT, int BN, int EPQ, int NIB>
 __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
                   int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err) {
     int32_t *__restrict__ dump = ep.dump;
-    using C = TcCfg<BN, EPQ>;
+    using C = TcCfg<BN, EPQ, NIB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *empty = full + C::STAGES;
     uint64_t *tfull = empty + C::STAGES;
     uint64_t *tempty = tfull + C::SLOTS;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + C::SLOTS);
+    uint64_t *rfull = tempty + C::SLOTS;  // NIB: a stage's nibble bytes have landed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(rfull + C::STAGES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -411,8 +417,9 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], NIB ? 3 : 1);  // NIB: + one arrival per unpacking warp
             mbar_init(&empty[s], 1);
+            mbar_init(&rfull[s], 1);
         }
         for (int i = 0; i < C::SLOTS; ++i) {
             mbar_init(&tfull[i], 1);
@@ -454,12 +461,17 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     // scale records are contiguous per (group or block, tile): one bulk copy each
                     const int b0 = ks * C::BLK;
                     const int nb = nblk - b0 < C::BLK ? nblk - b0 : C::BLK;
-                    mbar_arrive_expect_tx(&full[stage],
-                                          3 * 32 * C::BK + C::B_BYTES + (r1 + r2) * 16 + nb * C::QB_BYTES);
+                    mbar_arrive_expect_tx(&full[stage], 3 * 32 * C::BK + (NIB ? 0 : C::B_BYTES) + (r1 + r2) * 16 +
+                                                            nb * C::QB_BYTES);
                     tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);                         // MMA rows 0..31
                     tma_load_2d(sb + 64 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 32);       // 64..95
                     tma_load_2d(sb + 96 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 64);       // 96..127
-                    tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
+                    if constexpr (NIB) {
+                        mbar_arrive_expect_tx(&rfull[stage], C::RAW_STAGE);
+                        tma_load_2d(smem + C::RAW_OFF + stage * C::RAW_STAGE, &tm_b, &rfull[stage], ks * (C::BK / 2), n0);
+                    } else {
+                        tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
+                    }
                     const uint8_t *qa = quads_a + (static_cast<int64_t>(b0 >> 3) * lda_q + m0) * 16;
                     if (r1 > 0) bulk_load(q, qa, r1 * 16, &full[stage]);
                     if (r2 > 0) bulk_load(q + 64 * 16, qa + 32 * 16, r2 * 16, &full[stage]);
@@ -520,6 +532,50 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                 if (!ok) break;
                 if (elect_one()) mma_commit(&empty[stage]);
                 __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    } else if (NIB != 0 && (warp == 9 || warp == 13)) {
+        // ---- nibble unpack (Q4_0 weights): the stage's BN x 64 nibble bytes -> the
+        // int8 B operand in the layout a 128-byte-swizzled TMA load would have
+        // left (row r at r * 128, its 16-byte chunk c at chunk c ^ (r % 8)).  One
+        // 16-byte source chunk is one block's nibbles: low nibbles are elements
+        // 0..15 (chunk 2j of the row), high nibbles 16..31 (chunk 2j + 1); the
+        // code nibble - 8 of each byte is (nibble + 0x78) ^ 0x80, no carries. ----
+        const int ct = (warp == 9 ? 0 : 32) + lane;
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&rfull[stage], phase, err, ERR_WAIT_RAW))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *raw = smem + C::RAW_OFF + stage * C::RAW_STAGE;
+                uint8_t *dst = smem + stage * C::STAGE_BYTES + C::A_BYTES;
+#pragma unroll
+                for (int i = 0; i < C::BN * 4 / 64; ++i) {
+                    const int c = ct + 64 * i, r = c >> 2, j = c & 3;
+                    const uint4 x = *reinterpret_cast<const uint4 *>(raw + r * 64 + j * 16);
+                    uint4 lo, hi;
+                    lo.x = ((x.x & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    lo.y = ((x.y & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    lo.z = ((x.z & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    lo.w = ((x.w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    hi.x = (((x.x >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    hi.y = (((x.y >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    hi.z = (((x.z >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    hi.w = (((x.w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * j) ^ (r & 7)) << 4)) = lo;
+                    *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * j + 1) ^ (r & 7)) << 4)) = hi;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMA's reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[stage]);
                 if (++stage == C::STAGES) {
                     stage = 0;
                     phase ^= 1u;
@@ -601,17 +657,21 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
 // ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
-template <int MODE, int CVT, int BN, int EPQ = 2>
+template <int MODE, int CVT, int BN, int EPQ = 2, int NIB = 0>
 static cudaError_t launch_tc_epq(const MmqArgs &a, int num_sms, cudaStream_t s) {
-    using C = TcCfg<BN, EPQ>;
+    using C = TcCfg<BN, EPQ, NIB>;
     const int M = a.a.rows, N = a.b.rows, K = a.a.K, nblk = K / 32;
     CUtensorMap tma, tmb;
-    const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, db[2] = {uint64_t(K), uint64_t(N)}, sk[1] = {uint64_t(K)};
-    const uint32_t bxa[2] = {C::BK, 32}, bxb[2] = {C::BK, C::BN};
+    const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, sk[1] = {uint64_t(K)};
+    const uint32_t bxa[2] = {C::BK, 32};
+    // B: int8 codes [N][K] in 128-byte-swizzled boxes, or (NIB) nibble bytes [N][K/2] in plain 64-byte rows
+    const uint64_t db[2] = {uint64_t(NIB ? K / 2 : K), uint64_t(N)}, skb[1] = {uint64_t(NIB ? K / 2 : K)};
+    const uint32_t bxb[2] = {NIB ? C::BK / 2 : C::BK, C::BN};
     if (!make_tmap(&tma, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.a.codes, 2, da, sk, bxa, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, sk, bxb, CU_TENSOR_MAP_SWIZZLE_128B))
+        !make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.b.codes, 2, db, skb, bxb,
+                   NIB ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    auto kern = mmq_tc_kernel<MODE, CVT, BN, EPQ>;
+    auto kern = mmq_tc_kernel<MODE, CVT, BN, EPQ, NIB>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     const int tiles = ((M + C::ROWS - 1) / C::ROWS) * ((N + C::BN - 1) / C::BN);
@@ -651,6 +711,8 @@ static int mmq_epq() {
 
 template <int MODE, int CVT, int BN>
 static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
+    // Q4_0 nibble codes: BN 128 with 4 epilogue warps per quarter, whose idle warps 9 and 13 unpack
+    if (a.b.nib == 1) return launch_tc_epq<MODE, CVT, 128, 4, 1>(a, num_sms, s);
     if constexpr (BN == 128)  // 4 warps per quarter need BN / 4 >= 32 columns each
         if (mmq_epq() == 4) return launch_tc_epq<MODE, CVT, BN, 4>(a, num_sms, s);
     return launch_tc_epq<MODE, CVT, BN, 2>(a, num_sms, s);
@@ -685,7 +747,8 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
 }
 
 cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt, int bn) {
-    if (!valid_args(a) || num_sms <= 0 || a.b_mins) return cudaErrorInvalidValue;  // Q4_1: SIMT path only
+    if (!valid_args(a) || num_sms <= 0 || a.b_mins || a.b.nib == 2 || a.a.nib != 0)  // Q4_1: SIMT path only
+        return cudaErrorInvalidValue;
     if (bn == 64) return dispatch_tc<64>(a, mode, num_sms, s, cvt);
     if (bn == 128) return dispatch_tc<128>(a, mode, num_sms, s, cvt);
     return cudaErrorInvalidValue;
@@ -698,17 +761,26 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
                                 const int8_t *__restrict__ cb, const uint4 *__restrict__ qb, int ldb_q, int M, int N,
                                 int K, const float *__restrict__ bias, float *__restrict__ y, int64_t ldy,
                                 int32_t *__restrict__ dump, int mode, const __half *__restrict__ mins_b,
-                                const __half *__restrict__ sums_a) {
+                                const __half *__restrict__ sums_a, int nib) {
     const int n = blockIdx.x * blockDim.x + threadIdx.x;
     const int m = blockIdx.y;
     if (n >= N || m >= M) return;
     const int nblk = K >> 5;
     const int8_t *ar = ca + static_cast<int64_t>(m) * K;
-    const int8_t *br = cb + static_cast<int64_t>(n) * K;
+    const int8_t *br = cb + static_cast<int64_t>(n) * (nib ? K / 2 : K);
     float acc = 0.f;
     for (int b = 0; b < nblk; ++b) {
         int isum = 0;
-        for (int j = 0; j < 32; ++j) isum += static_cast<int>(ar[b * 32 + j]) * static_cast<int>(br[b * 32 + j]);
+        for (int j = 0; j < 32; ++j) {
+            int w;
+            if (nib == 0) {
+                w = br[b * 32 + j];
+            } else {  // the block's nibble bytes: byte j % 16, low nibble for j < 16
+                const int byte = static_cast<uint8_t>(br[b * 16 + (j & 15)]);
+                w = (j < 16 ? (byte & 15) : (byte >> 4)) - (nib == 1 ? 8 : 0);
+            }
+            isum += static_cast<int>(ar[b * 32 + j]) * w;
+        }
         if (mode == MMQ_OUT_BLOCKDOTS) {
             dump[(static_cast<int64_t>(m) * N + n) * nblk + b] = isum;
         } else {
@@ -731,6 +803,14 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
 // flight.  CTA: 32 weight rows x 8 activation rows, one output per thread.
 constexpr int SKINNY_MAX_M = 64;
 
+// Q4_0 nibble codes of 4 bytes -> the int8 codes (nibble - 8) of their low
+// (elements j..j+3) or high (j+16..j+19) nibbles; (n + 0x78) ^ 0x80 per byte.
+__device__ __forceinline__ int q4_lo(int v) { return static_cast<int>(((static_cast<uint32_t>(v) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u); }
+__device__ __forceinline__ int q4_hi(int v) {
+    return static_cast<int>((((static_cast<uint32_t>(v) >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u);
+}
+
+template <int NIB>
 __global__ void __launch_bounds__(256) mmq_skinny_kernel(const int8_t *__restrict__ ca, const __half *__restrict__ qa,
                                                          int lda_q, const int8_t *__restrict__ cb,
                                                          const __half *__restrict__ qb, int ldb_q, int M, int N, int K,
@@ -740,12 +820,20 @@ __global__ void __launch_bounds__(256) mmq_skinny_kernel(const int8_t *__restric
     const int m = blockIdx.y * 8 + (threadIdx.x >> 5);
     if (n >= N || m >= M) return;
     const int nblk = K >> 5;
-    const int4 *br = reinterpret_cast<const int4 *>(cb + static_cast<int64_t>(n) * K);
+    const int4 *br = reinterpret_cast<const int4 *>(cb + static_cast<int64_t>(n) * (NIB ? K / 2 : K));
     const int4 *ar = reinterpret_cast<const int4 *>(ca + static_cast<int64_t>(m) * K);
     float acc = 0.f;
 #pragma unroll 4
     for (int b = 0; b < nblk; ++b) {
-        const int4 w0 = __ldg(br + 2 * b), w1 = __ldg(br + 2 * b + 1);
+        int4 w0, w1;
+        if constexpr (NIB) {  // one 16-byte load holds the block's 32 codes
+            const int4 p = __ldg(br + b);
+            w0 = make_int4(q4_lo(p.x), q4_lo(p.y), q4_lo(p.z), q4_lo(p.w));
+            w1 = make_int4(q4_hi(p.x), q4_hi(p.y), q4_hi(p.z), q4_hi(p.w));
+        } else {
+            w0 = __ldg(br + 2 * b);
+            w1 = __ldg(br + 2 * b + 1);
+        }
         const int4 a0 = __ldg(ar + 2 * b), a1 = __ldg(ar + 2 * b + 1);
         const float dw = __half2float(qb[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]);
         const float dx = __half2float(qa[act_quad_index(b, m, lda_q)]);
@@ -768,8 +856,9 @@ cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
     const int M = a.a.rows, N = a.b.rows, K = a.a.K;
     const bool aligned = (reinterpret_cast<uintptr_t>(a.a.codes) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(a.b.codes) & 15) == 0;
-    if (mode == MMQ_OUT_F32 && !a.b_mins && M <= SKINNY_MAX_M && aligned) {
-        mmq_skinny_kernel<<<dim3((N + 31) / 32, (M + 7) / 8), 256, 0, s>>>(
+    if (mode == MMQ_OUT_F32 && !a.b_mins && a.b.nib != 2 && M <= SKINNY_MAX_M && aligned) {
+        auto kern = a.b.nib == 1 ? mmq_skinny_kernel<1> : mmq_skinny_kernel<0>;
+        kern<<<dim3((N + 31) / 32, (M + 7) / 8), 256, 0, s>>>(
             static_cast<const int8_t *>(a.a.codes), static_cast<const __half *>(a.a.quads), a.a.ld,
             static_cast<const int8_t *>(a.b.codes), static_cast<const __half *>(a.b.quads), a.b.ld, M, N, K, a.bias,
             a.y, a.ldy);
@@ -780,7 +869,7 @@ cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
                                          a.a.ld, static_cast<const int8_t *>(a.b.codes),
                                          static_cast<const uint4 *>(a.b.quads), a.b.ld, M, N, K, a.bias, a.y, a.ldy,
                                          a.dump, mode, static_cast<const __half *>(a.b_mins),
-                                         static_cast<const __half *>(a.a_sums));
+                                         static_cast<const __half *>(a.a_sums), a.b.nib);
     return cudaGetLastError();
 }
 

@@ -63,9 +63,13 @@ __device__ __forceinline__ void store_act_scale(__half *quads, int b, int m, int
 #endif
 
 struct QMatrix {
-    const void *codes;  // int8 [rows, K]
+    const void *codes;  // int8 [rows, K], or (nib != 0) 4-bit codes [rows, K/2]
     const void *quads;  // A side: fp16 [ceil(K/256)][ld][8]; B side: fp16 [K/32][ld][8]
     int rows, K, ld;
+    // 0: one int8 code per element.  1 (Q4_0) / 2 (Q4_1): the blocks' own nibble
+    // bytes, 16 per 32-element block, byte j = element j (low nibble) and element
+    // j + 16 (high nibble); the code is nibble - 8 (Q4_0) or the nibble (Q4_1).
+    int nib = 0;
 };
 
 struct MmqArgs {
@@ -102,6 +106,12 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 // Repack ggml weight blocks (N rows of K) into the device layout.
 // type: 8 = Q8_0, 2 = Q4_0, 3 = Q4_1 (codes = nibbles 0..15, block minima to
 // `mins`, fp16 [K/32][ld]).  Returns cudaErrorInvalidValue otherwise.
+// Codes: int8 [N][K] for Q8_0; the nibble bytes [N][K/2] for Q4_0 / Q4_1
+// (weight_code_bytes).
+inline size_t weight_code_bytes(int type, int N, int K) {
+    return static_cast<size_t>(N) * static_cast<size_t>(type == 8 ? K : K / 2);
+}
+inline int weight_nib(int type) { return type == 2 ? 1 : type == 3 ? 2 : 0; }
 cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, void *codes, void *quads, int ld,
                                  cudaStream_t s, void *mins = nullptr);
 

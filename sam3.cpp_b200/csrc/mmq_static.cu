@@ -101,7 +101,7 @@ extern "C" int sam3b200_mul_mat_noalloc(sam3b200_backend *h, const sam3b200_weig
         return SAM3B200_STATUS_FAILED;
     MmqArgs a;
     a.a = QMatrix{codes, quads, Mi, w->K, lda};
-    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld};
+    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld, weight_nib(w->type)};
     a.bias = bias;
     a.y = dst;
     a.ldy = ldd;

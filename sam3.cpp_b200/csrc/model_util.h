@@ -45,6 +45,7 @@ struct DevBuf {
 struct QWeight {  // a repacked linear weight (see mmq.cuh)
     DevBuf codes, quads;
     int K = 0, N = 0, ld = 0;
+    int nib = 0;  // QMatrix::nib of the codes (0 Q8_0, 1 Q4_0)
     bool set = false;
 };
 
@@ -95,10 +96,11 @@ inline bool upload_qweight(Backend *be, QWeight &w, int type, const void *data, 
     w.K = static_cast<int>(K);
     w.N = static_cast<int>(N);
     w.ld = (w.N + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
+    w.nib = weight_nib(type);
     DevBuf raw;
     const size_t raw_bytes = static_cast<size_t>(type_row_bytes(type, K)) * N;
     const size_t qb = static_cast<size_t>(K / 32) * w.ld * 16;
-    bool ok = raw.alloc(raw_bytes) && w.codes.alloc(static_cast<size_t>(K) * N) && w.quads.alloc(qb) &&
+    bool ok = raw.alloc(raw_bytes) && w.codes.alloc(weight_code_bytes(type, w.N, w.K)) && w.quads.alloc(qb) &&
               cuda_ok(cudaMemsetAsync(w.quads.p, 0, qb, be->stream), "memset quads") &&
               cuda_ok(cudaMemcpyAsync(raw.p, data, raw_bytes, cudaMemcpyHostToDevice, be->stream), "upload") &&
               cuda_ok(repack_weight_blocks(type, raw.p, w.N, w.K, w.codes.p, w.quads.p, w.ld, be->stream),

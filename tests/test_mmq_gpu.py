@@ -90,13 +90,16 @@ def test_mul_mat_row_strides_and_zero_rows(oracle, b200, backend):
     w.free()
 
 
+@pytest.mark.parametrize("qt", [8, 2])
 @pytest.mark.parametrize("K,N", [(1024, 3072), (1024, 1024), (1024, 4736), (4736, 1024)])
-def test_vit_shapes_sampled_rows(oracle, b200, backend, K, N):
+def test_vit_shapes_sampled_rows(oracle, b200, backend, qt, K, N):
     """Full ViT-32 GEMM shapes (M = 5184 tokens); the oracle checks a
-    sample of rows spread over every M tile including the ragged last one."""
+    sample of rows spread over every M tile including the ragged last one.
+    Q4_0 weights stay 4-bit in device memory; the tensor-core kernel unpacks
+    each stage's nibbles in shared memory."""
     M = 5184
-    wq, x, bias = _case(oracle, 8, M, K, N, seed=K + N)
-    w = backend.weight(8, wq, K, N)
+    wq, x, bias = _case(oracle, qt, M, K, N, seed=K + N)
+    w = backend.weight(qt, wq, K, N)
     xd, bd = backend.upload(x), backend.upload(bias)
     yd = backend.alloc(M * N * 4)
     backend.set_mmq_impl(b200.MMQ_AUTO)
@@ -104,7 +107,7 @@ def test_vit_shapes_sampled_rows(oracle, b200, backend, K, N):
     backend.synchronize()
     got = yd.get((M, N), np.float32)
     rows = np.unique(np.concatenate([np.arange(0, M, 97), [M - 1, M - 64, 5120, 127, 128]]))
-    ref = oracle.mul_mat(8, wq, K, N, x[rows]) + bias[None, :]
+    ref = oracle.mul_mat(qt, wq, K, N, x[rows]) + bias[None, :]
     assert np.array_equal(got[rows], ref)
     w.free()
 

@@ -59,6 +59,30 @@ def test_prefix(backend, small):
     assert rel_err(dx.get(ref.shape, np.float32), ref) <= TOL
 
 
+@pytest.fixture(scope="module")
+def small_q4(model, oracle, backend):
+    """The test geometry with Q4_0 linear weights: every MUL_MAT epilogue
+    (RoPE'd Q/K/V^T, GELU + Q8_0 re-quantisation, residual) on nibble codes."""
+    hp = dict(model.SAM3_VIT_TEST, wtype=model.Q4_0)
+    tensors = model.random_vit_weights(hp, seed=3)
+    vit = backend.vit(hp)
+    vit.load(tensors)
+    yield hp, tensors, vit, oracle.OracleVit(hp, tensors)
+    vit.free()
+
+
+@pytest.mark.parametrize("idx", [0, 1])
+def test_block_q4_0(backend, small_q4, idx):
+    hp, _, vit, ov = small_q4
+    x = np.random.default_rng(20 + idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
+    ref = ov.block(idx, x)
+    dx = backend.upload(x)
+    vit.run_block(idx, dx)
+    backend.synchronize()
+    err = rel_err(dx.get(ref.shape, np.float32), ref)
+    assert err <= TOL, err
+
+
 @pytest.mark.parametrize("idx", [0, 1])  # block 0 windowed, block 1 global
 def test_block(backend, small, idx):
     hp, _, vit, ov = small
