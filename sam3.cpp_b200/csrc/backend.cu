@@ -294,7 +294,7 @@ sam3b200_weight *sam3b200_weight_upload(sam3b200_backend *h, int type, const voi
         const size_t block_bytes = type == SAM3B200_TYPE_Q8_0 ? 34 : type == SAM3B200_TYPE_Q4_0 ? 18 : 20;
         const size_t raw_bytes = static_cast<size_t>(N) * (K / 32) * block_bytes;
         const size_t quad_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
-        const size_t min_bytes = static_cast<size_t>(K / 32) * w->ld * 2;
+        const size_t min_bytes = static_cast<size_t>(K / 32) * w->ld * 16;
         ok = cuda_ok(cudaMalloc(&raw, raw_bytes), "cudaMalloc(weight staging)") &&
              cuda_ok(cudaMalloc(&w->codes, weight_code_bytes(type, N, K)), "cudaMalloc(weight codes)") &&
              cuda_ok(cudaMalloc(&w->quads, quad_bytes), "cudaMalloc(weight scale quads)") &&
@@ -409,7 +409,6 @@ int b200::run_mul_mat(Backend *be, const Weight *w, const float *x, int64_t ldx,
     const int mode = dump ? MMQ_OUT_BLOCKDOTS : MMQ_OUT_F32;
     int impl = be->mmq_impl;
     if (impl == SAM3B200_MMQ_AUTO) impl = Mi < 64 ? SAM3B200_MMQ_SIMT : SAM3B200_MMQ_TC;
-    if (q41) impl = SAM3B200_MMQ_SIMT;  // the m_w * s_x term exists only in the SIMT kernel
     cudaError_t e;
     be->count(2);
     be->prof_mark(0);

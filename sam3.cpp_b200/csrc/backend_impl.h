@@ -43,7 +43,7 @@ struct Weight {
     int ld = 0;    // scale-quad rows per block (N rounded up to 128)
     void *codes = nullptr;
     void *quads = nullptr;
-    void *mins = nullptr;   // Q4_1: fp16 block minima [K/32][ld]
+    void *mins = nullptr;   // Q4_1: block minima as fp16 records [K/32][ld][8] (slot b % 8)
     void *dense = nullptr;  // F16 / F32 weights: fp16 [N][K] for the fp16 tensor-core GEMM
 };
 

@@ -115,7 +115,7 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 // bytes for Q4_0 / Q4_1) + scale quads.
 // ---------------------------------------------------------------------------
 __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ blocks, int N, int K,
-                                     int8_t *__restrict__ codes, uint4 *__restrict__ quads, __half *__restrict__ mins,
+                                     int8_t *__restrict__ codes, uint4 *__restrict__ quads, uint4 *__restrict__ mins,
                                      int ld) {
     const int nblk = K >> 5;
     const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -133,14 +133,19 @@ __global__ void repack_weight_kernel(int type, const uint8_t *__restrict__ block
         blk = blocks + w * (type == 2 ? 18 : 20);
         if (lane < 16)
             codes[static_cast<int64_t>(n) * (K / 2) + b * 16 + lane] = static_cast<int8_t>(blk[(type == 2 ? 2 : 4) + lane]);
-        if (type == 3 && lane == 0)
-            mins[static_cast<int64_t>(b) * ld + n] = __half(__half_raw{static_cast<unsigned short>(blk[2] | (blk[3] << 8))});
     }
-    if (lane == 0) {
+    if (lane == 0) {  // fp16 records (d, and m for Q4_1) in slot b % 8, the rest zero: the scale MMA's B operand
+        const int slot = b & 7;
         const uint32_t dbits = static_cast<uint32_t>(blk[0] | (blk[1] << 8));
-        uint32_t rec[4] = {0u, 0u, 0u, 0u};  // d in fp16 slot b % 8
-        rec[(b & 7) >> 1] = (b & 1) ? (dbits << 16) : dbits;
+        uint32_t rec[4] = {0u, 0u, 0u, 0u};
+        rec[slot >> 1] = (slot & 1) ? (dbits << 16) : dbits;
         quads[static_cast<int64_t>(b) * ld + n] = make_uint4(rec[0], rec[1], rec[2], rec[3]);
+        if (type == 3) {
+            const uint32_t mbits = static_cast<uint32_t>(blk[2] | (blk[3] << 8));
+            uint32_t mr[4] = {0u, 0u, 0u, 0u};
+            mr[slot >> 1] = (slot & 1) ? (mbits << 16) : mbits;
+            mins[static_cast<int64_t>(b) * ld + n] = make_uint4(mr[0], mr[1], mr[2], mr[3]);
+        }
     }
 }
 
@@ -153,7 +158,7 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
     const unsigned grid = static_cast<unsigned>((warps * 32 + threads - 1) / threads);
     repack_weight_kernel<<<grid, threads, 0, s>>>(type, static_cast<const uint8_t *>(blocks), N, K,
                                                   static_cast<int8_t *>(codes), static_cast<uint4 *>(quads),
-                                                  static_cast<__half *>(mins), ld);
+                                                  static_cast<uint4 *>(mins), ld);
     return cudaGetLastError();
 }
 
@@ -188,6 +193,12 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
 // ---------------------------------------------------------------------------
 template <int BN_, int EPQ_ = 2, int NIB_ = 0>
 struct TcCfg {
+    // NIB: B codes as stored.  0 = int8 (Q8_0); 1 = Q4_0 nibbles, 2 = Q4_1 nibbles (each
+    // stage's nibble bytes land in the RAW region, BN rows x 64 bytes, and warps 9 and 13
+    // unpack them into the stage's swizzled int8 B operand).  Q4_1 adds the term m_w s_x
+    // per block: its records (A: Q8_1 sum fields, B: minima) ride in the stage like the
+    // scale records and a third MMA puts the product next to I and S.
+    static constexpr int NIB = NIB_;
     static constexpr int BM = 128;                  // MMA rows
     static constexpr int ROWS = 96;                 // tokens per tile
     static constexpr int BN = BN_;
@@ -197,8 +208,10 @@ struct TcCfg {
     static constexpr int B_BYTES = BN * BK;
     static constexpr int Q_BYTES = BM * 16;         // the stage's A scale operand (one record group): 2 KB
     static constexpr int QB_BYTES = BN * 16;        // one block's B scale operand
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + Q_BYTES + BLK * QB_BYTES;
-    static constexpr int STAGES = BN == 128 ? 4 : 6;
+    static constexpr int Q_OFF = A_BYTES + B_BYTES;                    // A scale group, then BLK B scale records
+    static constexpr int MIN_OFF = Q_OFF + Q_BYTES + BLK * QB_BYTES;   // Q4_1: A sum group, then BLK B minima
+    static constexpr int STAGE_BYTES = MIN_OFF + (NIB == 2 ? Q_BYTES + BLK * QB_BYTES : 0);
+    static constexpr int STAGES = NIB == 2 ? 3 : BN == 128 ? 4 : 6;
     static constexpr int ZERO_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = ZERO_OFF + Q_BYTES;
     static constexpr int EPQ = EPQ_;                // epilogue warps per used lane quarter (2 or 4)
@@ -207,12 +220,10 @@ struct TcCfg {
     static constexpr int COLS = BN / EPQ;           // output columns per epilogue thread
     static constexpr int CHUNK = 32;
     static_assert(COLS % CHUNK == 0, "whole 32-column TMEM loads (and whole Q8_0 blocks) per thread");
-    static constexpr int SLOT_COLS = 2 * BN;        // one K-block: I (BN columns) then S (BN columns)
+    static constexpr int TERMS = NIB == 2 ? 3 : 2;  // TMEM per K-block: I, S (, M = m_w s_x), BN columns each
+    static constexpr int SLOT_COLS = TERMS * BN;
     static constexpr int SLOTS = 512 / SLOT_COLS;   // K-blocks in flight between MMA and epilogue
     static constexpr int TMEM_COLS = 512;
-    // 4-bit B codes (NIB = 1, Q4_0): each stage's nibble bytes land here (BN rows x 64 bytes, as
-    // stored) and warps 9 and 13 unpack them into the stage's swizzled int8 B operand
-    static constexpr int NIB = NIB_;
     static constexpr int RAW_STAGE = BN * BK / 2;
     static constexpr int RAW_OFF = BAR_OFF + 256;
     static constexpr int SMEM_BYTES = RAW_OFF + (NIB ? STAGES * RAW_STAGE : 0) + 1024;
@@ -384,7 +395,8 @@ template <int MODE, int CVT, int BN, int EPQ, int NIB>
 __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
-                  int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err) {
+                  int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err, const uint8_t *__restrict__ sums_a,
+                  const uint8_t *__restrict__ mins_b) {
     int32_t *__restrict__ dump = ep.dump;
     using C = TcCfg<BN, EPQ, NIB>;
     extern __shared__ uint8_t smem_raw[];
@@ -414,6 +426,10 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                                            : sb + C::A_BYTES + C::B_BYTES + 32 * 16 + (j - 32 * C::BK / 16) * 16;
         *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
     }
+    if constexpr (NIB == 2)  // and of the Q4_1 sum-field records
+        for (int i = threadIdx.x; i < C::STAGES * 32; i += blockDim.x)
+            *reinterpret_cast<uint4 *>(smem + (i >> 5) * C::STAGE_BYTES + C::MIN_OFF + (32 + (i & 31)) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -461,8 +477,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     // scale records are contiguous per (group or block, tile): one bulk copy each
                     const int b0 = ks * C::BLK;
                     const int nb = nblk - b0 < C::BLK ? nblk - b0 : C::BLK;
-                    mbar_arrive_expect_tx(&full[stage], 3 * 32 * C::BK + (NIB ? 0 : C::B_BYTES) + (r1 + r2) * 16 +
-                                                            nb * C::QB_BYTES);
+                    mbar_arrive_expect_tx(&full[stage], 3 * 32 * C::BK + (NIB ? 0 : C::B_BYTES) +
+                                                            (NIB == 2 ? 2 : 1) * ((r1 + r2) * 16 + nb * C::QB_BYTES));
                     tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);                         // MMA rows 0..31
                     tma_load_2d(sb + 64 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 32);       // 64..95
                     tma_load_2d(sb + 96 * C::BK, &tm_a, &full[stage], ks * C::BK, m0 + 64);       // 96..127
@@ -478,6 +494,16 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     for (int j = 0; j < nb; ++j)
                         bulk_load(q + C::Q_BYTES + j * C::QB_BYTES,
                                   quads_b + (static_cast<int64_t>(b0 + j) * ldb_q + n0) * 16, C::QB_BYTES, &full[stage]);
+                    if constexpr (NIB == 2) {  // the same records for m_w s_x: A sum fields, B minima
+                        uint8_t *mq = sb + C::MIN_OFF;
+                        const uint8_t *sa = sums_a + (static_cast<int64_t>(b0 >> 3) * lda_q + m0) * 16;
+                        if (r1 > 0) bulk_load(mq, sa, r1 * 16, &full[stage]);
+                        if (r2 > 0) bulk_load(mq + 64 * 16, sa + 32 * 16, r2 * 16, &full[stage]);
+                        for (int j = 0; j < nb; ++j)
+                            bulk_load(mq + C::Q_BYTES + j * C::QB_BYTES,
+                                      mins_b + (static_cast<int64_t>(b0 + j) * ldb_q + n0) * 16, C::QB_BYTES,
+                                      &full[stage]);
+                    }
                 }
                 __syncwarp();
                 if (++stage == C::STAGES) {
@@ -488,7 +514,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
         }
     } else if (warp == 1) {
         // ---- MMA issuer: warp-uniform loop, one elected lane issues ----
-        constexpr uint32_t idesc_i = idesc_s8_s32(C::BM, C::BN);
+        constexpr uint32_t idesc_i = NIB == 2 ? idesc_s8u8_s32(C::BM, C::BN) : idesc_s8_s32(C::BM, C::BN);
         constexpr uint32_t idesc_s = idesc_f16_f32(C::BM, C::BN);
         const uint32_t zero_addr = smem_u32(smem + C::ZERO_OFF);
         int stage = 0;
@@ -524,6 +550,12 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     if (elect_one()) {
                         mma_i8(d_tmem, a_desc, b_desc, idesc_i, 0);
                         if constexpr (MODE != MMQ_OUT_BLOCKDOTS) mma_f16(d_tmem + C::BN, qa_desc, qb_desc, idesc_s, 0);
+                        if constexpr (NIB == 2 && MODE != MMQ_OUT_BLOCKDOTS) {
+                            const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES + C::MIN_OFF);
+                            const uint32_t mb = sa + C::Q_BYTES + j * C::QB_BYTES;
+                            mma_f16(d_tmem + 2 * C::BN, noswz_kmajor_desc(sa, zero_addr - sa),
+                                    noswz_kmajor_desc(mb, zero_addr - mb), idesc_s, 0);
+                        }
                         mma_commit(&tfull[buf]);
                     }
                     __syncwarp();
@@ -546,6 +578,7 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
         // 0..15 (chunk 2j of the row), high nibbles 16..31 (chunk 2j + 1); the
         // code nibble - 8 of each byte is (nibble + 0x78) ^ 0x80, no carries. ----
         const int ct = (warp == 9 ? 0 : 32) + lane;
+        const uint32_t off = NIB == 1 ? 0x78787878u : 0u, flip = NIB == 1 ? 0x80808080u : 0u;  // Q4_1: the nibble
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
@@ -562,14 +595,14 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     const int c = ct + 64 * i, r = c >> 2, j = c & 3;
                     const uint4 x = *reinterpret_cast<const uint4 *>(raw + r * 64 + j * 16);
                     uint4 lo, hi;
-                    lo.x = ((x.x & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    lo.y = ((x.y & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    lo.z = ((x.z & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    lo.w = ((x.w & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    hi.x = (((x.x >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    hi.y = (((x.y >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    hi.z = (((x.z >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
-                    hi.w = (((x.w >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+                    lo.x = ((x.x & 0x0F0F0F0Fu) + off) ^ flip;
+                    lo.y = ((x.y & 0x0F0F0F0Fu) + off) ^ flip;
+                    lo.z = ((x.z & 0x0F0F0F0Fu) + off) ^ flip;
+                    lo.w = ((x.w & 0x0F0F0F0Fu) + off) ^ flip;
+                    hi.x = (((x.x >> 4) & 0x0F0F0F0Fu) + off) ^ flip;
+                    hi.y = (((x.y >> 4) & 0x0F0F0F0Fu) + off) ^ flip;
+                    hi.z = (((x.z >> 4) & 0x0F0F0F0Fu) + off) ^ flip;
+                    hi.w = (((x.w >> 4) & 0x0F0F0F0Fu) + off) ^ flip;
                     *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * j) ^ (r & 7)) << 4)) = lo;
                     *reinterpret_cast<uint4 *>(dst + r * 128 + (((2 * j + 1) ^ (r & 7)) << 4)) = hi;
                 }
@@ -612,7 +645,8 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                     tmem_ld_32x32b_x32(ta + c0, vi);
                     if constexpr (MODE != MMQ_OUT_BLOCKDOTS) tmem_ld_32x32b_x32(ta + C::BN + c0, vs);
                     tmem_wait_ld();
-                    if (c0 + CHUNK == C::COLS) {
+                    constexpr bool MINS = NIB == 2 && MODE != MMQ_OUT_BLOCKDOTS;  // Q4_1: + m_w s_x after the fma
+                    if (!MINS && c0 + CHUNK == C::COLS) {
                         // the whole buffer is in registers: hand it back to the MMA warp
                         // (all 32 lanes arrive: no divergent branch on the per-block path, 2% faster)
                         tc_fence_before();
@@ -631,6 +665,19 @@ __global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
                             }
                             ffma2(acc[c0 + i], acc[c0 + i + 1], f0, f1, __uint_as_float(vs[i]),
                                   __uint_as_float(vs[i + 1]));
+                        }
+                        if constexpr (MINS) {
+                            // M = m_w s_x is exact in fp32, so acc + M is ggml's fma(m_w, s_x, acc)
+                            tmem_ld_32x32b_x32(ta + 2 * C::BN + c0, vs);
+                            tmem_wait_ld();
+                            if (c0 + CHUNK == C::COLS) {
+                                tc_fence_before();
+                                mbar_arrive(&tempty[buf]);
+                            }
+#pragma unroll
+                            for (int i = 0; i < CHUNK; i += 2)
+                                fadd2(acc[c0 + i], acc[c0 + i + 1], acc[c0 + i], acc[c0 + i + 1], __uint_as_float(vs[i]),
+                                      __uint_as_float(vs[i + 1]));
                         }
                     } else {
                         if (m < M) {
@@ -695,7 +742,8 @@ static cudaError_t launch_tc_epq(const MmqArgs &a, int num_sms, cudaStream_t s) 
     ep.heads = a.heads;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(tma, tmb, static_cast<const uint8_t *>(a.a.quads),
                                                   static_cast<const uint8_t *>(a.b.quads), M, N, nblk, a.a.ld, a.b.ld,
-                                                  ep, a.err);
+                                                  ep, a.err, static_cast<const uint8_t *>(a.a_sums),
+                                                  static_cast<const uint8_t *>(a.b_mins));
     return cudaGetLastError();
 }
 
@@ -711,8 +759,11 @@ static int mmq_epq() {
 
 template <int MODE, int CVT, int BN>
 static cudaError_t launch_tc(const MmqArgs &a, int num_sms, cudaStream_t s) {
-    // Q4_0 nibble codes: BN 128 with 4 epilogue warps per quarter, whose idle warps 9 and 13 unpack
+    // Q4_0 / Q4_1 nibble codes: BN 128 with 4 epilogue warps per quarter, whose idle warps 9 and 13 unpack
     if (a.b.nib == 1) return launch_tc_epq<MODE, CVT, 128, 4, 1>(a, num_sms, s);
+    if constexpr (MODE == MMQ_OUT_F32 || MODE == MMQ_OUT_BLOCKDOTS)
+        if (a.b.nib == 2) return launch_tc_epq<MODE, CVT, 128, 4, 2>(a, num_sms, s);
+    if (a.b.nib == 2) return cudaErrorInvalidValue;  // Q4_1: f32 output only
     if constexpr (BN == 128)  // 4 warps per quarter need BN / 4 >= 32 columns each
         if (mmq_epq() == 4) return launch_tc_epq<MODE, CVT, BN, 4>(a, num_sms, s);
     return launch_tc_epq<MODE, CVT, BN, 2>(a, num_sms, s);
@@ -747,7 +798,8 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
 }
 
 cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt, int bn) {
-    if (!valid_args(a) || num_sms <= 0 || a.b_mins || a.b.nib == 2 || a.a.nib != 0)  // Q4_1: SIMT path only
+    if (!valid_args(a) || num_sms <= 0 || a.a.nib != 0 ||
+        (a.b.nib == 2) != (a.b_mins != nullptr) || (a.b.nib == 2 && !a.a_sums))  // Q4_1: minima and sum fields
         return cudaErrorInvalidValue;
     if (bn == 64) return dispatch_tc<64>(a, mode, num_sms, s, cvt);
     if (bn == 128) return dispatch_tc<128>(a, mode, num_sms, s, cvt);
@@ -788,7 +840,7 @@ __global__ void mmq_simt_kernel(const int8_t *__restrict__ ca, const uint4 *__re
             const float dw = __half2float(reinterpret_cast<const __half *>(qb)[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]);
             acc = fmaf(static_cast<float>(isum), dx * dw, acc);
             if (mins_b)  // Q4_1 x Q8_1: + m_w * s_x per block (ggml vec_dot_q4_1_q8_1)
-                acc = fmaf(__half2float(mins_b[static_cast<int64_t>(b) * ldb_q + n]),
+                acc = fmaf(__half2float(mins_b[(static_cast<int64_t>(b) * ldb_q + n) * 8 + (b & 7)]),
                            __half2float(sums_a[act_quad_index(b, m, lda_q)]), acc);
         }
     }

@@ -92,7 +92,7 @@ struct MmqArgs {
     const float *freqs = nullptr;   // MMQ_OUT_QKV: RoPE table [win_tokens][32][2] (cos, sin), or null
     int win_tokens = 0;             // MMQ_OUT_QKV: tokens per window
     int heads = 0;                  // MMQ_OUT_QKV: heads (N = 3 * 64 * heads)
-    const void *b_mins = nullptr;   // Q4_1 weights: fp16 m_w [K/32][ld] (SIMT path)
+    const void *b_mins = nullptr;   // Q4_1 weights: m_w records, fp16 [K/32][ld][8] (m_w in slot b % 8)
     const void *a_sums = nullptr;   // Q4_1 weights: Q8_1 sum fields of the activations (act_quad_index layout)
 };
 
@@ -105,7 +105,8 @@ cudaError_t quantize_rows_q8(const float *x, int64_t ldx, int M, int K, void *co
 
 // Repack ggml weight blocks (N rows of K) into the device layout.
 // type: 8 = Q8_0, 2 = Q4_0, 3 = Q4_1 (codes = nibbles 0..15, block minima to
-// `mins`, fp16 [K/32][ld]).  Returns cudaErrorInvalidValue otherwise.
+// `mins` as records fp16 [K/32][ld][8], m_w in slot b % 8 like the scale
+// records).  Returns cudaErrorInvalidValue otherwise.
 // Codes: int8 [N][K] for Q8_0; the nibble bytes [N][K/2] for Q4_0 / Q4_1
 // (weight_code_bytes).
 inline size_t weight_code_bytes(int type, int N, int K) {

@@ -323,4 +323,9 @@ __host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N) {
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// kind::i8 with signed A and unsigned B (u8 codes, e.g. Q4_1 nibbles 0..15), s32 D.
+__host__ __device__ constexpr uint32_t idesc_s8u8_s32(int M, int N) {
+    return (2u << 4) | (1u << 7) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 }  // namespace b200

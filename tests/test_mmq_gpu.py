@@ -122,17 +122,24 @@ def test_bad_weight_type_is_rejected(b200, backend):
         backend.weight(1, blocks, 12, 1)   # F16 rows must be a multiple of 8 (16-byte TMA pitch)
 
 
-@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (37, 96, 136), (1, 32, 8)])
-def test_q4_1_bit_exact(oracle, b200, backend, M, K, N):
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("M,K,N", [(200, 256, 384), (37, 96, 136), (1, 32, 8), (300, 1024, 520)])
+def test_q4_1_bit_exact(oracle, b200, backend, impl, M, K, N):
     """Q4_1 weights x Q8_1 activations (ggml vec_dot_q4_1_q8_1): block dots of the nibble codes and the
-    f32 output, whose per-block sum is fma(I, d_w d_x, acc) then fma(m_w, s_x, acc), bit-exact."""
+    f32 output, whose per-block sum is fma(I, d_w d_x, acc) then fma(m_w, s_x, acc), bit-exact.  On the
+    tensor cores the nibbles are unpacked in shared memory as unsigned codes and m_w s_x comes from a
+    third MMA next to the block dot and the scale product."""
     wq, x, bias = _case(oracle, 3, M, K, N, seed=M + 11 * K + N)
     w = backend.weight(3, wq, K, N)
     dx, db = backend.upload(x), backend.upload(bias)
-    dots = backend.mul_mat_block_dots(w, dx, M)
-    y = backend.alloc(M * N * 4)
-    backend.mul_mat(w, dx, M, y, bias=db)
-    backend.synchronize()
+    prev = backend.set_mmq_impl(_impl(b200, impl))
+    try:
+        dots = backend.mul_mat_block_dots(w, dx, M)
+        y = backend.alloc(M * N * 4)
+        backend.mul_mat(w, dx, M, y, bias=db)
+        backend.synchronize()
+    finally:
+        backend.set_mmq_impl(prev)
     assert np.array_equal(dots, oracle.block_dots(3, wq, K, N, x))
     assert np.array_equal(y.get((M, N), np.float32), oracle.mul_mat(3, wq, K, N, x) + bias[None, :])
     w.free()
