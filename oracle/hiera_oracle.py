@@ -104,14 +104,23 @@ def window_unpartition(y: np.ndarray, ws: int, Hp: int, Wp: int, H: int, W: int)
 
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, heads: int, dtype=np.float64) -> np.ndarray:
     """softmax(q k^T / sqrt(hd)) v per window and head: q [B][Nq][C], k, v [B][N][C] -> [B][Nq][C].
-    dtype: the arithmetic (float64 by default; float32 gives a second, equally valid evaluation)."""
+    dtype: the arithmetic (float64 by default; float32 gives a second, equally valid evaluation;
+    float16 rounds the operands the tensor-core attention multiplies -- q, k, v and the unnormalised
+    probabilities -- to fp16 and sums in float64, the rounding of the GPU kernel's operands)."""
     B, Nq, C = q.shape
     hd = C // heads
-    qh = q.reshape(B, Nq, heads, hd).transpose(0, 2, 1, 3).astype(dtype)
-    kh = k.reshape(B, -1, heads, hd).transpose(0, 2, 1, 3).astype(dtype)
-    vh = v.reshape(B, -1, heads, hd).transpose(0, 2, 1, 3).astype(dtype)
-    s = qh @ kh.transpose(0, 1, 3, 2) * dtype(1.0 / math.sqrt(hd))
+    f16 = dtype == np.float16
+    wd = np.float64 if f16 else dtype
+
+    def heads_of(a, n):
+        a = a.reshape(B, n, heads, hd).transpose(0, 2, 1, 3)
+        return a.astype(np.float16).astype(wd) if f16 else a.astype(wd)
+
+    qh, kh, vh = heads_of(q, Nq), heads_of(k, k.shape[1]), heads_of(v, v.shape[1])
+    s = qh @ kh.transpose(0, 1, 3, 2) * wd(1.0 / math.sqrt(hd))
     s = np.exp(s - s.max(-1, keepdims=True))
+    if f16:
+        s = s.astype(np.float16).astype(wd)
     o = (s @ vh) / s.sum(-1, keepdims=True)
     return o.transpose(0, 2, 1, 3).reshape(B, Nq, C).astype(F32)
 
@@ -220,8 +229,8 @@ def fpn(stage_outs: list, convs: list, top_down: list, scalp: int) -> list:
 
 def encode(hp: dict, tensors: dict, img_chw: np.ndarray, attn_dtype=np.float64) -> tuple[list, list]:
     """Whole encoder: (stage outputs, FPN levels).  attn_dtype=np.float32 evaluates the attention in
-    single precision: the difference between the two evaluations measures how far rounding-level
-    differences travel through the quantised blocks."""
+    single precision, np.float16 with fp16 operands: the differences between the evaluations measure
+    how far rounding-level differences travel through the quantised blocks."""
     blocks, ends = metadata(hp)
     S = (hp["img"] - 1) // 4 + 1
     pe = pos_embed(tensors["hiera.pos_embed"], tensors["hiera.pos_embed_window"], S)

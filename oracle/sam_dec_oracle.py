@@ -56,12 +56,12 @@ def linear(w, x, b):
     return hiera_oracle.linear(w, x, b)
 
 
-def sam_attention(t: dict, pfx: str, q, k, v) -> np.ndarray:
+def sam_attention(t: dict, pfx: str, q, k, v, dtype=np.float64) -> np.ndarray:
     Q, K, V = (linear(t[pfx + f".{n}_proj.weight"], a, t[pfx + f".{n}_proj.bias"]) for n, a in (("q", q), ("k", k), ("v", v)))
     ID = Q.shape[-1]
     heads = 8
     split = lambda a: a.reshape(1, a.shape[0], heads, ID // heads).transpose(0, 2, 1, 3)
-    o = oracle.attention_general(split(Q), split(K), split(V), 1.0 / math.sqrt(ID // heads))
+    o = oracle.attention_general(split(Q), split(K), split(V), 1.0 / math.sqrt(ID // heads), dtype=dtype)
     return linear(t[pfx + ".out_proj.weight"], o.reshape(Q.shape[0], ID), t[pfx + ".out_proj.bias"])
 
 
@@ -76,11 +76,13 @@ def gelu_erf(x):
 
 
 def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_w, orig_h, img, tracking=False,
-           all_tokens=False):
+           all_tokens=False, attn_dtype=np.float64):
     """-> (mask logits [nmask][4H][4H], iou [nmask], obj logit, sam token [256]; with all_tokens the
     output tokens of every mask [nmask][256] instead).  tracking: the decode of a propagated video frame
     (sam3_propagate_single, sam3.cpp:11312-11347) -- no prompt but the padding token, and the
-    memory-conditioned features go in without no_mem_embed (the PVS decode adds it, sam3.cpp:10926)."""
+    memory-conditioned features go in without no_mem_embed (the PVS decode adds it, sam3.cpp:10926).
+    attn_dtype: the attention arithmetic (float64; float32 is ggml-cpu's flash_attn_ext arithmetic for
+    F32 q, k, v)."""
     D, H = 256, hp["feat_size"]
     nmask = hp["n_multimask"] + 1
     special = ([t["sam_dec.obj_score_token.weight"]] if hp["pred_obj_scores"] else []) + \
@@ -94,21 +96,21 @@ def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_
     for i in range(hp["depth"]):
         p = f"sam_dec.twoway.{i}."
         if i == 0:
-            tok = ln(sam_attention(t, p + "sa", tok, tok, tok), t[p + "norm1.weight"], t[p + "norm1.bias"])
+            tok = ln(sam_attention(t, p + "sa", tok, tok, tok, attn_dtype), t[p + "norm1.weight"], t[p + "norm1.bias"])
         else:
             q = (tok + qpe).astype(F32)
-            tok = ln((tok + sam_attention(t, p + "sa", q, q, tok)).astype(F32), t[p + "norm1.weight"], t[p + "norm1.bias"])
+            tok = ln((tok + sam_attention(t, p + "sa", q, q, tok, attn_dtype)).astype(F32), t[p + "norm1.weight"], t[p + "norm1.bias"])
         q, k = (tok + qpe).astype(F32), (keys + kpe).astype(F32)
-        tok = ln((tok + sam_attention(t, p + "cross_attn_token_to_image", q, k, keys)).astype(F32),
+        tok = ln((tok + sam_attention(t, p + "cross_attn_token_to_image", q, k, keys, attn_dtype)).astype(F32),
                  t[p + "norm2.weight"], t[p + "norm2.bias"])
         h = np.maximum(linear(t[p + "mlp.lin1.weight"], tok, t[p + "mlp.lin1.bias"]), F32(0))
         tok = ln((tok + linear(t[p + "mlp.lin2.weight"], h, t[p + "mlp.lin2.bias"])).astype(F32),
                  t[p + "norm3.weight"], t[p + "norm3.bias"])
         q, k = (tok + qpe).astype(F32), (keys + kpe).astype(F32)
-        keys = ln((keys + sam_attention(t, p + "cross_attn_image_to_token", k, q, tok)).astype(F32),
+        keys = ln((keys + sam_attention(t, p + "cross_attn_image_to_token", k, q, tok, attn_dtype)).astype(F32),
                   t[p + "norm4.weight"], t[p + "norm4.bias"])
     q, k = (tok + qpe).astype(F32), (keys + kpe).astype(F32)
-    tok = ln((tok + sam_attention(t, "sam_dec.final_attn", q, k, keys)).astype(F32),
+    tok = ln((tok + sam_attention(t, "sam_dec.final_attn", q, k, keys, attn_dtype)).astype(F32),
              t["sam_dec.final_norm.weight"], t["sam_dec.final_norm.bias"])
     # upscaling (channel-major [C][h][w])
     src = keys.reshape(H, H, D).transpose(2, 0, 1)

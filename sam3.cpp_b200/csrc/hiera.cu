@@ -22,6 +22,7 @@
 #include "act.cuh"
 #include "sgemm.cuh"
 #include "attn_simt.cuh"
+#include "attn_tcw.cuh"
 #include "gemm_f16.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
@@ -157,59 +158,6 @@ __global__ void unpart_add_kernel(const float *__restrict__ sc, const float *__r
     out[i] = __fadd_rn(sc[i], proj[r * C + c]);
 }
 
-// Global-attention staging for the tensor-core path: one head's q (times
-// `scale`) or k as fp16 [rows][hd] from qkv rows (stride ld, column offset
-// c0), and v transposed to fp16 [hd][rows].
-__global__ void head_rows_f16_kernel(const float *__restrict__ src, int64_t ld, int c0, int rows, int hd, float scale,
-                                     __half *__restrict__ dst) {
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= static_cast<int64_t>(rows) * hd) return;
-    const int64_t r = i / hd;
-    const int d = static_cast<int>(i % hd);
-    dst[i] = __float2half_rn(src[r * ld + c0 + d] * scale);
-}
-
-__global__ void head_cols_f16_kernel(const float *__restrict__ src, int64_t ld, int c0, int rows, int hd,
-                                     __half *__restrict__ dst) {
-    __shared__ float tile[32][33];
-    const int r0 = blockIdx.x * 32, d0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
-    for (int j = ty; j < 32; j += 8) {
-        const int r = r0 + j, d = d0 + tx;
-        tile[j][tx] = (r < rows && d < hd) ? src[static_cast<int64_t>(r) * ld + c0 + d] : 0.f;
-    }
-    __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
-        const int d = d0 + j, r = r0 + tx;
-        if (d < hd && r < rows) dst[static_cast<int64_t>(d) * rows + r] = __float2half_rn(tile[tx][j]);
-    }
-}
-
-// Row softmax of the f32 scores [rows][n] -> fp16 probabilities (one CTA per row).
-__global__ void __launch_bounds__(256) softmax_rows_f16_kernel(const float *__restrict__ S, int n,
-                                                               __half *__restrict__ P) {
-    __shared__ float red[8];
-    const float *sr = S + static_cast<int64_t>(blockIdx.x) * n;
-    __half *pr = P + static_cast<int64_t>(blockIdx.x) * n;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float m = -INFINITY;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, sr[i]);
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    m = red[0];
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
-    __syncthreads();
-    float sum = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sum += expf(sr[i] - m);
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) red[warp] = sum;
-    __syncthreads();
-    sum = 0.f;
-    for (int w = 0; w < 8; ++w) sum += red[w];
-    const float inv = 1.0f / sum;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) pr[i] = __float2half_rn(expf(sr[i] - m) * inv);
-}
-
 // FPN top-down fusion: y[t] = lat[t] + prev[nearest 2x source of t] (sam3.cpp:4568-4573)
 __global__ void upsample2_add_kernel(const float *lat, const float *__restrict__ prev, int H, int W, int D,
                                      float *y) {  // y may alias lat
@@ -297,7 +245,7 @@ struct Hiera {
     // activations
     DevBuf xa, xb, normed, shortf, shortp, qkv, qp, attn, proj, codes_a, quads_a, codes_b, quads_b;
     DevBuf stage_out[4], fpn_out[4], x16;
-    DevBuf gq, gk, gvt, gs, gp;  // global attention on the tensor cores: fp16 q, k, v^T, f32 scores, fp16 probs
+    DevBuf tq, tk, tvt;          // attention operands for the tensor cores (attn_tcw): fp16 q, k, v^T
     DevBuf xwin, hid;            // blocks with F16 / F32 linear layers: f32 windowed rows, MLP hidden rows
     DevBuf col;                  // the patch embedding's f32 im2col rows
     ~Hiera() {
@@ -442,27 +390,25 @@ BlockGeo block_geo(const HBlock &b, int H, int W) {
     return g;
 }
 
-// Global blocks with long sequences run their attention as two fp16
-// tensor-core GEMMs around a row softmax (the windows stay on attention_simt).
-bool global_on_tensor_cores(const HBlock &b, const BlockGeo &g) {
-    const int hd = b.dim_out / b.heads;
-    return b.ws == 0 && g.N >= 512 && g.N % 8 == 0 && hd % 8 == 0;
-}
+// Windowed and global attention run on the tcgen05 kernel (attn_tcw) for head
+// dimensions up to 128 -- every SAM2 Hiera (56 / 72 / 96) -- and on the SIMT
+// flash loop otherwise.
+bool attn_on_tensor_cores(const HBlock &b) { return b.dim_out / b.heads <= 128; }
 
 bool alloc_hiera(Hiera *h) {
     const auto &hp = h->hp;
     const int S = h->S;
     size_t mx_x = 0, mx_norm = 0, mx_sf = 0, mx_sp = 0, mx_qkv = 0, mx_qp = 0, mx_codes_a = 0, mx_quads_a = 0,
            mx_codes_b = 0, mx_quads_b = 0;
-    size_t mx_gqk = 0, mx_gs = 0;
+    size_t mx_tq = 0, mx_tkv = 0;
     int H = S, W = S;
     for (size_t i = 0; i < h->blk.size(); ++i) {
         const HBlock &b = h->blk[i];
         const BlockGeo g = block_geo(b, H, W);
-        if (global_on_tensor_cores(b, g)) {
-            const size_t hd = static_cast<size_t>(b.dim_out / b.heads);
-            mx_gqk = std::max(mx_gqk, static_cast<size_t>(std::max(g.N, g.NQ)) * hd);
-            mx_gs = std::max(mx_gs, static_cast<size_t>(g.NQ) * g.N);
+        if (attn_on_tensor_cores(b)) {
+            const int hd = b.dim_out / b.heads;
+            mx_tq = std::max(mx_tq, attn_tcw_q_elems(g.Bw, g.NQ, b.heads, hd));
+            mx_tkv = std::max(mx_tkv, attn_tcw_kv_elems(g.Bw, g.N, b.heads, hd));
         }
         const size_t T = static_cast<size_t>(H) * W, To = static_cast<size_t>(g.Ho) * g.Wo;
         const size_t rw = static_cast<size_t>(g.Bw) * g.N, rq = static_cast<size_t>(g.Bw) * g.NQ;
@@ -496,9 +442,7 @@ bool alloc_hiera(Hiera *h) {
         mx16 = std::max(mx16, T * h->stage_dim[s] * 2);
     }
     ok = ok && h->x16.alloc(mx16);
-    if (ok && mx_gs > 0)
-        ok = h->gq.alloc(mx_gqk * 2) && h->gk.alloc(mx_gqk * 2) && h->gvt.alloc(mx_gqk * 2) && h->gs.alloc(mx_gs * 4) &&
-             h->gp.alloc(mx_gs * 2);
+    if (ok && mx_tq > 0) ok = h->tq.alloc(mx_tq * 2) && h->tk.alloc(mx_tkv * 2) && h->tvt.alloc(mx_tkv * 2);
     if (!ok) return false;
     return cuda_ok(cudaMemsetAsync(h->quads_a.p, 0, h->quads_a.n, h->be->stream), "memset") &&
            cuda_ok(cudaMemsetAsync(h->quads_b.p, 0, h->quads_b.n, h->be->stream), "memset") &&
@@ -605,41 +549,17 @@ bool run_block(Hiera *h, int i, const float *x, int H, int W, float *out) {
     // 5. attention per (window, head)
     const int hd = Co / b.heads;
     const float scale = 1.0f / sqrtf(static_cast<float>(hd));
-    if (global_on_tensor_cores(b, g)) {
-        for (int hh = 0; hh < b.heads; ++hh) {
-            const int64_t nq = static_cast<int64_t>(g.NQ) * hd, nk = static_cast<int64_t>(g.N) * hd;
-            head_rows_f16_kernel<<<blocks_for(nq, 256), 256, 0, s>>>(qptr, q_ld, hh * hd, g.NQ, hd, scale,
-                                                                     h->gq.as<__half>());
-            head_rows_f16_kernel<<<blocks_for(nk, 256), 256, 0, s>>>(h->qkv.as<float>(), 3 * Co, Co + hh * hd, g.N, hd,
-                                                                     1.0f, h->gk.as<__half>());
-            head_cols_f16_kernel<<<dim3(blocks_for(g.N, 32), blocks_for(hd, 32)), dim3(32, 8), 0, s>>>(
-                h->qkv.as<float>(), 3 * Co, 2 * Co + hh * hd, g.N, hd, h->gvt.as<__half>());
-            if (!hlaunched(h, cudaGetLastError(), "hiera global staging", 3)) return false;
-            GemmF16Args gs{};
-            gs.a = h->gq.p;
-            gs.b = h->gk.p;
-            gs.M = g.NQ;
-            gs.N = g.N;
-            gs.K = hd;
-            gs.out = h->gs.p;
-            gs.ldo = g.N;
-            gs.store = GEMM_STORE_ROWMAJOR;
-            gs.err = h->be->err;
-            if (!hlaunched(h, gemm_f16(gs, h->be->num_sms, s), "hiera global scores")) return false;
-            softmax_rows_f16_kernel<<<g.NQ, 256, 0, s>>>(h->gs.as<float>(), g.N, h->gp.as<__half>());
-            if (!hlaunched(h, cudaGetLastError(), "hiera global softmax")) return false;
-            GemmF16Args go{};
-            go.a = h->gp.p;
-            go.b = h->gvt.p;
-            go.M = g.NQ;
-            go.N = hd;
-            go.K = g.N;
-            go.out = h->attn.as<float>() + hh * hd;
-            go.ldo = Co;
-            go.store = GEMM_STORE_ROWMAJOR;
-            go.err = h->be->err;
-            if (!hlaunched(h, gemm_f16(go, h->be->num_sms, s), "hiera global pv")) return false;
-        }
+    if (attn_on_tensor_cores(b)) {
+        const float *kv = h->qkv.as<float>();
+        if (!hlaunched(h,
+                       attn_tcw_stage(qptr, q_ld, kv + Co, kv + 2 * Co, 3 * Co, g.Bw, g.NQ, g.N, b.heads, hd,
+                                      h->tq.as<__half>(), h->tk.as<__half>(), h->tvt.as<__half>(), s),
+                       "hiera attention staging", 3) ||
+            !hlaunched(h,
+                       attn_tcw(h->tq.as<__half>(), h->tk.as<__half>(), h->tvt.as<__half>(), g.Bw, g.NQ, g.N,
+                                b.heads, hd, scale, h->attn.as<float>(), Co, h->be->err, s),
+                       "hiera attention"))
+            return false;
     } else {
         const AttnStrides qs{static_cast<int64_t>(g.NQ) * q_ld, hd, q_ld};
         const AttnStrides kvs{static_cast<int64_t>(g.N) * 3 * Co, hd, 3 * Co};

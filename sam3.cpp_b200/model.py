@@ -19,6 +19,10 @@ F32, F16, Q4_0, Q4_1, Q8_0 = 0, 1, 2, 3, 8
 SAM3_VIT = dict(img=1008, patch=14, embed=1024, depth=32, heads=16, mlp=4736, window=24,
                 global_idx=(7, 15, 23, 31), pos_grid=24, neck_dim=256, wtype=Q8_0)
 
+# SAM2.1 Hiera-tiny image encoder (config 1's backbone) at 1024
+SAM2_HIERA_TINY = dict(img=1024, embed=96, heads=1, stages=[1, 2, 7, 2], q_pool=3, window_spec=[8, 4, 14, 7],
+                       global_idx=[5, 7, 9], bkg_h=7, bkg_w=7, neck_dim=256, fpn_top_down_levels=[2, 3], scalp=1)
+
 # SAM2.1 Hiera-base+ image encoder (config 5's tracker backbone) at 1024
 SAM2_HIERA_BASE_PLUS = dict(img=1024, embed=112, heads=2, stages=[2, 3, 16, 3], q_pool=3, window_spec=[8, 4, 14, 7],
                             global_idx=[12, 16, 20], bkg_h=14, bkg_w=14, neck_dim=256, fpn_top_down_levels=[2, 3],

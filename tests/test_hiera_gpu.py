@@ -73,9 +73,13 @@ def test_encode_matches_oracle(oracle, hiera_oracle, backend, img):
 
     Twelve chained blocks of activation quantisation amplify rounding-level differences (a code
     that flips costs a full quantisation step downstream): two equally valid oracle evaluations
-    (attention in float64 and in float32) already differ by up to ~1.7e-2 at 1024x1024.  So the
-    free-running GPU encode is held to 1e-2 or twice that self-divergence, whichever is larger;
-    parity at the fixed 1e-2 bound is checked stage by stage on the GPU's own trajectory
+    (attention in float64 and in float32) already differ by up to ~1.7e-2 at 1024x1024, and the
+    divergence saturates quickly with the size of the perturbation -- the oracle's own encode with
+    the attention operands rounded to fp16 (q, k, v, probabilities: the tensor-core kernel's
+    operand precision, each a relative 2^-11 perturbation) moves stage 2 at 256x256 by 1.24e-2
+    against 0.63e-2 for float32.  So the free-running GPU encode is held to 1e-2, twice the float32
+    self-divergence or 1.25 times the fp16-operand one, whichever is largest; parity at the fixed
+    1e-2 bound is checked block by block and stage by stage on the GPU's own trajectory
     (test_encode_every_stage_on_the_gpu_trajectory)."""
     hp = hiera_tiny(img)
     gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=11)
@@ -86,12 +90,13 @@ def test_encode_matches_oracle(oracle, hiera_oracle, backend, img):
         model.encode_device(backend.upload(chw))
         stages, fpn = hiera_oracle.encode(hp, ref, chw)
         stages32, fpn32 = hiera_oracle.encode(hp, ref, chw, np.float32)
+        stages16, fpn16 = hiera_oracle.encode(hp, ref, chw, np.float16)
         for s in range(4):
-            bound = max(1e-2, 2 * rel_err(stages32[s], stages[s]))
+            bound = max(1e-2, 2 * rel_err(stages32[s], stages[s]), 1.25 * rel_err(stages16[s], stages[s]))
             err = rel_err(model.output_host(4 + s), stages[s])
             assert err <= bound, ("stage", s, err, bound)
         for lvl in range(3):
-            bound = max(1e-2, 2 * rel_err(fpn32[lvl], fpn[lvl]))
+            bound = max(1e-2, 2 * rel_err(fpn32[lvl], fpn[lvl]), 1.25 * rel_err(fpn16[lvl], fpn[lvl]))
             err = rel_err(model.output_host(lvl), fpn[lvl])
             assert err <= bound, ("fpn", lvl, err, bound)
     finally:
@@ -160,7 +165,7 @@ def test_hiera_rejects_unknown_tensor_and_missing(b200, backend):
 @pytest.mark.parametrize("i", [4, 5, 10])
 def test_block_matches_oracle_1024(oracle, hiera_oracle, backend, i):
     """Stage-2 geometry of a 1024x1024 input: block 4 (14-token windows padded 64 -> 70), block 5
-    (global, 4096 tokens: the fp16 tensor-core score/softmax/PV path) and block 10 (Q-stride, padded
+    (global, 4096 tokens: 32 key tiles of the tcgen05 flash kernel) and block 10 (Q-stride, padded
     windows, cropped output)."""
     hp = hiera_tiny(1024)
     gpu, ref = make_tensors(oracle, hiera_oracle, hp, seed=21)

@@ -71,7 +71,8 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
 
     Three checks.  (a) The decoder at this geometry, fed the oracle's own FPN features: every final mask at
     IoU >= 0.99 against the oracle.  (c) The decoder fed the GPU's own FPN features (the chain's actual
-    hand-off), against the oracle decoder on those same features: every final mask at IoU >= 0.99; with
+    hand-off), against the oracle decoder on those same features with its attention in float32 (the
+    reference CPU backend's arithmetic): every final mask at IoU >= 0.99; with
     the Hiera encode held to 1e-2 stage by stage on its own trajectory (test_hiera_gpu), every stage of
     the chain meets the fixed bounds.  (b) The whole chain free-running against the oracle chain: twelve random-init
     quantised Hiera blocks amplify rounding-level differences (see test_hiera_gpu), so two valid oracle
@@ -112,7 +113,10 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
         # (c) the oracle decoder on the GPU's own FPN features
         gf = [enc.output_host(lvl) for lvl in range(3)]
         gf = [np.ascontiguousarray(f.reshape(fpn[lvl].shape)) for lvl, f in enumerate(gf)]
-        masks_g = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024)[0]
+        # attention in float32, ggml-cpu's flash_attn_ext arithmetic for F32 q, k, v (the float64
+        # evaluation differs from it by as much as from the GPU here: mask 0 IoU 0.9887 both ways)
+        masks_g = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024,
+                                    attn_dtype=np.float32)[0]
         for m in range(4):
             ref_g = dec_oracle.resize_threshold(masks_g[m], W, Hh)
             assert dec_oracle.mask_iou(got[m], ref_g) >= 0.99, ("decoder on the GPU's features", m,
