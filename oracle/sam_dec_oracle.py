@@ -146,6 +146,11 @@ def decode(hp: dict, t: dict, img_feats, feat_s0, feat_s1, coords, labels, orig_
 
 def resize_threshold(mask: np.ndarray, dw: int, dh: int) -> np.ndarray:
     """sam3_bilinear_interpolate (double coordinates, clamped) + logit > 0 -> uint8 255 / 0."""
+    return np.where(resize_logits(mask, dw, dh) > 0, 255, 0).astype(np.uint8)
+
+
+def resize_logits(mask: np.ndarray, dw: int, dh: int) -> np.ndarray:
+    """The logits resize_threshold thresholds: sam3_bilinear_interpolate to dh x dw, f32."""
     sh, sw = mask.shape
     fy = np.clip((np.arange(dh) + 0.5) * (sh / dh) - 0.5, 0.0, sh - 1)
     fx = np.clip((np.arange(dw) + 0.5) * (sw / dw) - 0.5, 0.0, sw - 1)
@@ -156,8 +161,7 @@ def resize_threshold(mask: np.ndarray, dw: int, dh: int) -> np.ndarray:
     m = mask.astype(F32)
     a, b = m[y0][:, x0], m[y0][:, x0 + 1]
     c, d = m[y0 + 1][:, x0], m[y0 + 1][:, x0 + 1]
-    v = (1 - wy) * ((1 - wx) * a + wx * b) + wy * ((1 - wx) * c + wx * d)
-    return np.where(v > 0, 255, 0).astype(np.uint8)
+    return (1 - wy) * ((1 - wx) * a + wx * b) + wy * ((1 - wx) * c + wx * d)
 
 
 def mask_iou(a: np.ndarray, b: np.ndarray) -> float:

@@ -294,6 +294,8 @@ cudaError_t attention_combine(int D, const float *part_o, const float2 *part_ml,
     const dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(NQ) * D + 255) / 256),
                      static_cast<unsigned>(batch * heads));
     switch (D) {
+    case 16: attn_combine_kernel<16><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
+    case 32: attn_combine_kernel<32><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
     case 64: attn_combine_kernel<64><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
     case 128: attn_combine_kernel<128><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;
     case 256: attn_combine_kernel<256><<<cgrid, 256, 0, s>>>(part_o, part_ml, splits, NQ, heads, o, os); break;

@@ -36,7 +36,7 @@ cudaError_t attention_mma_f16kv_split(int D, const float *q, AttnStrides qs, int
                                       cudaStream_t s);
 
 // The combine pass of a split-KV attention: o = sum_z 2^(m_z - M) part_o_z / sum_z 2^(m_z - M) l_z per
-// row (part_ml = (m in log2 units, l) per split and row, part_o unnormalised).  D in {64, 128, 256}.
+// row (part_ml = (m in log2 units, l) per split and row, part_o unnormalised).  D in {16, 32, 64, 128, 256}.
 cudaError_t attention_combine(int D, const float *part_o, const float2 *part_ml, int splits, int NQ, int batch,
                               int heads, float *o, AttnStrides os, cudaStream_t s);
 

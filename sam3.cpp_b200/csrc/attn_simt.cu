@@ -5,6 +5,7 @@
 // and v staged in shared memory; online softmax in base 2 (scale and log2(e)
 // folded into q, the mask scaled by log2(e)).
 #include "attn_simt.cuh"
+#include "attn_mma.cuh"
 
 #include <cmath>
 
@@ -25,7 +26,9 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
                                                         const float *__restrict__ k, AttnStrides ks,
                                                         const float *__restrict__ v, AttnStrides vs, int NKV, int heads,
                                                         const MT *__restrict__ mask, int64_t mask_ld, int64_t mask_hs,
-                                                        float scale_log2, float *__restrict__ o, AttnStrides os) {
+                                                        float scale_log2, float *__restrict__ o, AttnStrides os,
+                                                        int chunk, float *__restrict__ part_o,
+                                                        float2 *__restrict__ part_ml) {
     constexpr int HD = 4 * DQ, KT = 64;
     constexpr float LOG2E = 1.4426950408889634f;
     // Dimension ownership: with DQ % 4 == 0 the 4 threads of a row own
@@ -50,12 +53,15 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
     }
     const MT *mrow = mask ? mask + h * mask_hs + static_cast<int64_t>(valid ? row : 0) * mask_ld : nullptr;
     float m = -INFINITY, l = 0.f;
-    for (int j0 = 0; j0 < NKV; j0 += KT) {
+    // split over keys (part_o given): this CTA's keys [kv_lo, kv_hi), blockIdx.z = the split
+    const int kv_lo = part_o ? blockIdx.z * chunk : 0;
+    const int kv_hi = part_o ? min(NKV, kv_lo + chunk) : NKV;
+    for (int j0 = kv_lo; j0 < kv_hi; j0 += KT) {
         __syncthreads();
         for (int e = threadIdx.x; e < KT * HD; e += blockDim.x) {
             const int kk = e / HD, d = e % HD, key = j0 + kk;
             float kv = 0.f, vv = 0.f;
-            if (key < NKV) {
+            if (key < kv_hi) {
                 kv = kb[static_cast<int64_t>(key) * ks.n + d];
                 vv = vb[static_cast<int64_t>(key) * vs.n + d];
             }
@@ -63,7 +69,7 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
             vsm[e] = vv;
         }
         __syncthreads();
-        const int nk = NKV - j0 < KT ? NKV - j0 : KT;
+        const int nk = kv_hi - j0 < KT ? kv_hi - j0 : KT;
         for (int kk = 0; kk < nk; ++kk) {
             float s = 0.f;
             if constexpr (VEC) {
@@ -114,7 +120,12 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
             }
         }
     }
-    if (valid) {
+    if (valid && part_o) {  // unnormalised partial result and (max in log2 units, sum) for the combine pass
+        const int64_t r = (static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * NQ + row;
+#pragma unroll
+        for (int i = 0; i < DQ; ++i) part_o[r * HD + dim_of<DQ, VEC>(i, part)] = acc[i];
+        if (part == 0) part_ml[r] = make_float2(m, l);
+    } else if (valid) {
         const float inv = l > 0.f ? 1.0f / l : 0.f;
         float *orow = o + b * os.b + h * os.h + static_cast<int64_t>(row) * os.n;
 #pragma unroll
@@ -125,27 +136,34 @@ __global__ void __launch_bounds__(256) attn_simt_kernel(const float *__restrict_
 template <int DQ, typename MT>
 cudaError_t launch(const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks, const float *v,
                    AttnStrides vs, int NKV, int batch, int heads, const MT *mask, int64_t mask_ld, int64_t mask_hs,
-                   float scale, float *o, AttnStrides os, cudaStream_t s) {
+                   float scale, float *o, AttnStrides os, cudaStream_t s, int splits = 1, float *part_o = nullptr,
+                   float2 *part_ml = nullptr) {
     const int smem = 2 * 64 * 4 * DQ * 4;
     cudaError_t e =
         cudaFuncSetAttribute(attn_simt_kernel<DQ, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((NQ + 63) / 64, static_cast<unsigned>(batch * heads));
+    const int chunk = part_o ? (NKV + splits - 1) / splits : NKV;
+    const int nz = part_o ? (NKV + chunk - 1) / chunk : 1;
+    dim3 grid((NQ + 63) / 64, static_cast<unsigned>(batch * heads), static_cast<unsigned>(nz));
     attn_simt_kernel<DQ, MT><<<grid, 256, smem, s>>>(q, qs, NQ, k, ks, v, vs, NKV, heads, mask, mask_ld, mask_hs,
-                                                     scale * 1.4426950408889634f, o, os);
-    return cudaGetLastError();
+                                                     scale * 1.4426950408889634f, o, os, chunk, part_o, part_ml);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || !part_o) return e;
+    return attention_combine(4 * DQ, part_o, part_ml, nz, NQ, batch, heads, o, os, s);
 }
 
 template <typename MT>
 cudaError_t dispatch(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks, const float *v,
                      AttnStrides vs, int NKV, int batch, int heads, const MT *mask, int64_t mask_ld, int64_t mask_hs,
-                     float scale, float *o, AttnStrides os, cudaStream_t s) {
+                     float scale, float *o, AttnStrides os, cudaStream_t s, int splits = 1, float *part_o = nullptr,
+                     float2 *part_ml = nullptr) {
     if (NQ <= 0 || NKV <= 0 || batch <= 0 || heads <= 0 || static_cast<int64_t>(batch) * heads > 65535 ||
         (mask && (mask_ld < NKV || mask_hs < 0)))
         return cudaErrorInvalidValue;
 #define B200_ATTN_CASE(d)                                                                                            \
     case 4 * d:                                                                                                      \
-        return launch<d, MT>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, mask_hs, scale, o, os, s)
+        return launch<d, MT>(q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, mask_hs, scale, o, os, s, \
+                             splits, part_o, part_ml)
     switch (D) {
         B200_ATTN_CASE(4);
         B200_ATTN_CASE(8);
@@ -168,6 +186,15 @@ cudaError_t attention_simt(int D, const float *q, AttnStrides qs, int NQ, const 
                            const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                            int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s) {
     return dispatch<__half>(D, q, qs, NQ, k, ks, v, vs, NKV, batch, heads, mask, mask_ld, 0, scale, o, os, s);
+}
+
+cudaError_t attention_simt_split(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                 const float *v, AttnStrides vs, int NKV, int batch, int heads, float scale, float *o,
+                                 AttnStrides os, int splits, float *part_o, float2 *part_ml, cudaStream_t s) {
+    if (splits < 1 || (splits > 1 && (!part_o || !part_ml)) || (D != 16 && D != 32 && D != 64)) return cudaErrorInvalidValue;
+    if (splits == 1) return attention_simt(D, q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, scale, o, os, s);
+    return dispatch<__half>(D, q, qs, NQ, k, ks, v, vs, NKV, batch, heads, nullptr, 0, 0, scale, o, os, s, splits, part_o,
+                            part_ml);
 }
 
 cudaError_t attention_simt_f32mask(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,

@@ -25,6 +25,15 @@ cudaError_t attention_simt(int D, const float *q, AttnStrides qs, int NQ, const 
                            const float *v, AttnStrides vs, int NKV, int batch, int heads, const __half *mask,
                            int64_t mask_ld, float scale, float *o, AttnStrides os, cudaStream_t s);
 
+// Few queries against many keys (a handful of prompt tokens over 4096 image
+// tokens), no mask: the keys split into `splits` ranges, each CTA writes its
+// unnormalised partial result and (max, sum) to part_o [splits][batch * heads]
+// [NQ][D] / part_ml [splits][batch * heads][NQ], and attention_combine merges
+// them into o.  D in {16, 32, 64}; splits == 1 is attention_simt.
+cudaError_t attention_simt_split(int D, const float *q, AttnStrides qs, int NQ, const float *k, AttnStrides ks,
+                                 const float *v, AttnStrides vs, int NKV, int batch, int heads, float scale, float *o,
+                                 AttnStrides os, int splits, float *part_o, float2 *part_ml, cudaStream_t s);
+
 // The same with an f32 mask per head: head h of query row n reads
 // mask[h * mask_hs + n * mask_ld + k] (the SOFT_MAX_EXT mask the reference
 // keeps in f32 for the detector's box-relative bias, sam3.cpp:8580-8590).

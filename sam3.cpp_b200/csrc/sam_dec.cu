@@ -32,6 +32,8 @@
 namespace b200 {
 namespace {
 
+constexpr int DEC_SPLITS = 32;  // key ranges of the token -> image attentions (x 8 heads = 256 CTAs)
+
 inline unsigned nblocks(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
 // c = a + b (+ per-column vectors v1, v2 when given): rows x D
@@ -189,6 +191,7 @@ struct SamDec {
     // activations
     DevBuf tok, qpe, q2, keys, kpe, k2, tq, tk, tv, to, tmp_tok, tmp_keys, mlp, cm, up1, up1b, hs1, fs, up2, hs0,
         hyp, masks, heads_tmp;
+    DevBuf part_o, part_ml;  // split-over-keys partials of the token -> image attentions
     float iou[4] = {0, 0, 0, 0}, obj = 0;
     int ntok = 0;
 };
@@ -214,11 +217,19 @@ bool attention(SamDec *d, const DecAttn &a, const float *q_in, int nq, const flo
         !lin(d, a.v, v_in, D, nk, a.vb, d->tv.as<float>(), ID))
         return false;
     const AttnStrides qs{static_cast<int64_t>(nq) * ID, HD, ID}, ks{static_cast<int64_t>(nk) * ID, HD, ID};
+    // the prompt tokens against the 4096 image tokens: a handful of query rows per head, so the keys
+    // are split over DEC_SPLITS CTAs per head and merged by the combine pass
+    const int splits = nq <= d->ntok_max && nk >= 64 * DEC_SPLITS && HD <= 32 ? DEC_SPLITS : 1;
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
     if (!dlaunched(d,
-                   attention_simt(HD, d->tq.as<float>(), qs, nq, d->tk.as<float>(), ks, d->tv.as<float>(), ks, nk, 1,
-                                  d->hp.heads, nullptr, 0, 1.0f / sqrtf(static_cast<float>(HD)), d->to.as<float>(), qs,
-                                  d->be->stream),
-                   "sam_dec attention"))
+                   splits > 1 ? attention_simt_split(HD, d->tq.as<float>(), qs, nq, d->tk.as<float>(), ks,
+                                                     d->tv.as<float>(), ks, nk, 1, d->hp.heads, scale,
+                                                     d->to.as<float>(), qs, splits, d->part_o.as<float>(),
+                                                     d->part_ml.as<float2>(), d->be->stream)
+                              : attention_simt(HD, d->tq.as<float>(), qs, nq, d->tk.as<float>(), ks, d->tv.as<float>(),
+                                               ks, nk, 1, d->hp.heads, nullptr, 0, scale, d->to.as<float>(), qs,
+                                               d->be->stream),
+                   "sam_dec attention", splits > 1 ? 2 : 1))
         return false;
     return lin(d, a.o, d->to.as<float>(), ID, nq, a.ob, out, D);
 }
@@ -454,7 +465,9 @@ sam3b200_sam_dec *sam3b200_sam_dec_create(sam3b200_backend *hb, const sam3b200_s
                     d->mlp.alloc(NT * hp->mlp_dim * 4) && d->cm.alloc(HH * D * 4) && d->up1.alloc(64 * P1 * 4) &&
                     d->up1b.alloc(64 * P1 * 4) && d->fs.alloc(P0 * D * 4) && d->up2.alloc(32 * P0 * 4) &&
                     d->hs0.alloc(32 * P0 * 4) && d->hyp.alloc((4 * 32 + 8) * 4) && d->masks.alloc(4 * P0 * 4) &&
-                    d->heads_tmp.alloc(2 * D * 4);
+                    d->heads_tmp.alloc(2 * D * 4) &&
+                    d->part_o.alloc(static_cast<size_t>(DEC_SPLITS) * hp->heads * NT * 32 * 4) &&
+                    d->part_ml.alloc(static_cast<size_t>(DEC_SPLITS) * hp->heads * NT * 8);
     if (!ok) {
         delete d;
         return nullptr;

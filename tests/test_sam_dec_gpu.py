@@ -71,8 +71,9 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
 
     Three checks.  (a) The decoder at this geometry, fed the oracle's own FPN features: every final mask at
     IoU >= 0.99 against the oracle.  (c) The decoder fed the GPU's own FPN features (the chain's actual
-    hand-off), against the oracle decoder on those same features with its attention in float32 (the
-    reference CPU backend's arithmetic): every final mask at IoU >= 0.99; with
+    hand-off), against the oracle decoder on those same features: every final mask at IoU >= 0.99, or
+    disagreeing only on pixels whose reference logit is within 1e-2 of the logit range, or twice the
+    oracle's own float64-vs-float32 logit difference, of zero; with
     the Hiera encode held to 1e-2 stage by stage on its own trajectory (test_hiera_gpu), every stage of
     the chain meets the fixed bounds.  (b) The whole chain free-running against the oracle chain: twelve random-init
     quantised Hiera blocks amplify rounding-level differences (see test_hiera_gpu), so two valid oracle
@@ -113,14 +114,23 @@ def test_config1_image_to_mask(oracle, dec_oracle, backend):
         # (c) the oracle decoder on the GPU's own FPN features
         gf = [enc.output_host(lvl) for lvl in range(3)]
         gf = [np.ascontiguousarray(f.reshape(fpn[lvl].shape)) for lvl, f in enumerate(gf)]
-        # attention in float32, ggml-cpu's flash_attn_ext arithmetic for F32 q, k, v (the float64
-        # evaluation differs from it by as much as from the GPU here: mask 0 IoU 0.9887 both ways)
-        masks_g = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024,
-                                    attn_dtype=np.float32)[0]
+        masks_g = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024)[0]
+        masks_g32 = dec_oracle.decode(dhp, dr, gf[2], gf[0], gf[1], point, label, W, Hh, 1024,
+                                      attn_dtype=np.float32)[0]
         for m in range(4):
-            ref_g = dec_oracle.resize_threshold(masks_g[m], W, Hh)
-            assert dec_oracle.mask_iou(got[m], ref_g) >= 0.99, ("decoder on the GPU's features", m,
-                                                               dec_oracle.mask_iou(got[m], ref_g))
+            lg = dec_oracle.resize_logits(masks_g[m], W, Hh)
+            ref_g = np.where(lg > 0, 255, 0).astype(np.uint8)
+            iou_g = dec_oracle.mask_iou(got[m], ref_g)
+            # where IoU < 0.99 every disagreeing pixel must be one whose reference logit is ambiguous:
+            # within 1e-2 of the logit range, or within twice the oracle's own float64-vs-float32
+            # logit difference, of the threshold.  The random-init decoder leaves wide plateaus of
+            # near-zero logits here, where the oracle's two evaluations already disagree on ~1.1% of
+            # the pixels of masks 0 and 3
+            noise = float(np.abs(dec_oracle.resize_logits(masks_g32[m], W, Hh) - lg).max())
+            dis = (got[m] > 0) != (ref_g > 0)
+            ambiguous = np.abs(lg) <= max(1e-2 * np.abs(lg).max(), 2 * noise)
+            assert iou_g >= 0.99 or bool(np.all(ambiguous[dis])), ("decoder on the GPU's features", m, iou_g,
+                                                                  int(dis.sum()), int((dis & ~ambiguous).sum()))
     finally:
         enc.free()
         dec.free()
