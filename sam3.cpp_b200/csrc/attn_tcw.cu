@@ -34,7 +34,7 @@
 namespace b200 {
 namespace {
 
-template <int DP>
+template <int DP, bool PACK>
 struct TW {
     static constexpr int BQ = 128, BK = 128, D = DP, CH = DP / 64;  // 64-element (128-byte) SW128 chunks
     static constexpr int Q_CHUNK = BQ * 128;                       // 128 rows x 64 fp16
@@ -48,7 +48,13 @@ struct TW {
     static constexpr int BAR_OFF = V_OFF + 2 * V_BYTES;
     static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
     static constexpr int THREADS = 192;
-    static constexpr uint32_t O_COL = 0, S_COL = 128, P_COL = 384;
+    // Tensor memory: packed windows (one key tile) at head dimension 64 need O 64 + S 128 + P 64 = 256
+    // columns, so two CTAs share an SM (one's TMA and setup under the other's MMAs and softmax);
+    // otherwise O 0..Dp-1, two S buffers 128..383, two P buffers 384..511.
+    static constexpr bool HALF_TMEM = PACK && DP == 64;
+    static constexpr uint32_t TCOLS = HALF_TMEM ? 256 : 512;
+    static constexpr uint32_t O_COL = 0, S_COL = HALF_TMEM ? 64 : 128, P_COL = HALF_TMEM ? 192 : 384;
+    static constexpr int CTAS = HALF_TMEM ? 2 : 1;
     static_assert(DP == 64 || DP == 128, "head dimension padded to 64 or 128");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -66,15 +72,15 @@ enum : int {
     WERR_PV_DONE = 1 << 30,
 };
 
-// grid (query tiles per window, window groups, heads).  P > 0: P packed
-// windows per group, one query tile and one key tile; P = 0: one window per
-// group, nt key tiles.
-template <int DP>
-__global__ void __launch_bounds__(TW<DP>::THREADS, 1)
+// grid (query tiles per window, window groups, heads).  PACK (P > 0): P
+// packed windows per group, one query tile and one key tile; otherwise (P = 0)
+// one window per group, nt key tiles.
+template <int DP, bool PACK>
+__global__ void __launch_bounds__(TW<DP, PACK>::THREADS, TW<DP, PACK>::CTAS)
     attn_tcw_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, int Bw, int NQ, int N, int Ns, int hd, int P, int nt,
                     float c_log2, float *__restrict__ out, int64_t o_ld, int *__restrict__ err) {
-    using C = TW<DP>;
+    using C = TW<DP, PACK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *q_full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
@@ -105,7 +111,7 @@ __global__ void __launch_bounds__(TW<DP>::THREADS, 1)
         prefetch_tmap(&tm_v);
     }
     if (warp == 5) {
-        tmem_alloc(tmem_slot, 512);
+        tmem_alloc(tmem_slot, C::TCOLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -222,14 +228,34 @@ __global__ void __launch_bounds__(TW<DP>::THREADS, 1)
             const int lo = klo - j * C::BK, hi = khi - j * C::BK;  // valid tile columns [lo, hi)
             const uint32_t sb = tmem + lanes + C::S_COL + b * C::BK;
             float mx = -INFINITY;
+            // long sequences: the whole S row stays in registers (one TMEM pass), and tiles whose 128
+            // keys are valid for every row of the warp skip the masks
+            uint32_t sr[PACK ? 1 : C::BK];
+            bool all_full = false;
+            if constexpr (PACK) {
 #pragma unroll 1
-            for (int c = 0; c < C::BK; c += 32) {
-                uint32_t sv[32];
-                tmem_ld_32x32b_x32(sb + c, sv);
-                tmem_wait_ld();
+                for (int c = 0; c < C::BK; c += 32) {
+                    uint32_t sv[32];
+                    tmem_ld_32x32b_x32(sb + c, sv);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c + i >= lo && c + i < hi) mx = fmaxf(mx, __uint_as_float(sv[i]));
+                    for (int i = 0; i < 32; ++i)
+                        if (c + i >= lo && c + i < hi) mx = fmaxf(mx, __uint_as_float(sv[i]));
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < C::BK; c += 32)
+                    tmem_ld_32x32b_x32(sb + c, *reinterpret_cast<uint32_t(*)[32]>(sr + c));
+                tmem_wait_ld();
+                all_full = __all_sync(0xffffffffu, lo <= 0 && hi >= C::BK);
+                if (all_full) {
+#pragma unroll
+                    for (int i = 0; i < C::BK; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < C::BK; ++i)
+                        if (i >= lo && i < hi) mx = fmaxf(mx, __uint_as_float(sr[i]));
+                }
             }
             const float m_cand = fmaxf(m_run, mx * c_log2);
             // a row whose max grew by more than 2^8 takes the new max, its O and sum rescaled
@@ -262,23 +288,39 @@ __global__ void __launch_bounds__(TW<DP>::THREADS, 1)
                 break;
             }
             float rsum = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < C::BK; c += 32) {
-                uint32_t sv[32], pk[16];
-                tmem_ld_32x32b_x32(sb + c, sv);
-                tmem_wait_ld();
+            // P = 2^(s c - m) as fp16 pairs, zero outside the row's keys; the row sum over the fp16
+            // values the PV MMA multiplies
+            auto probs = [&](const uint32_t *sv, int c, bool masked, uint32_t(&pk)[16]) {
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c_log2, -m_use));
                     float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c_log2, -m_use));
-                    if (!(c + i >= lo && c + i < hi)) p0 = 0.f;
-                    if (!(c + i + 1 >= lo && c + i + 1 < hi)) p1 = 0.f;
+                    if (masked) {
+                        if (!(c + i >= lo && c + i < hi)) p0 = 0.f;
+                        if (!(c + i + 1 >= lo && c + i + 1 < hi)) p1 = 0.f;
+                    }
                     const __half2 hp = __floats2half2_rn(p0, p1);
-                    // the row sum of the probabilities the PV MMA multiplies (their fp16 values)
                     rsum += __low2float(hp) + __high2float(hp);
                     pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
-                tmem_st_32x32b_x16(tmem + lanes + C::P_COL + b * 64 + (c >> 1), pk);
+            };
+            if constexpr (PACK) {
+#pragma unroll 1
+                for (int c = 0; c < C::BK; c += 32) {
+                    uint32_t sv[32], pk[16];
+                    tmem_ld_32x32b_x32(sb + c, sv);
+                    tmem_wait_ld();
+                    probs(sv, c, true, pk);
+                    tmem_st_32x32b_x16(tmem + lanes + C::P_COL + b * 64 + (c >> 1), pk);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < C::BK; c += 32) {
+                    uint32_t pk[16];
+                    if (all_full) probs(sr + c, c, false, pk);
+                    else probs(sr + c, c, true, pk);
+                    tmem_st_32x32b_x16(tmem + lanes + C::P_COL + b * 64 + (c >> 1), pk);
+                }
             }
             tmem_wait_st();
             tc_fence_before();
@@ -308,7 +350,7 @@ __global__ void __launch_bounds__(TW<DP>::THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 5) tmem_dealloc(tmem, 512);
+    if (warp == 5) tmem_dealloc(tmem, C::TCOLS);
 }
 
 // q or k rows -> [heads][Bw * stride][Dp] fp16 (8 elements per thread)
@@ -339,30 +381,32 @@ __global__ void tcw_stage_rows_kernel(const float *__restrict__ src, int64_t ld,
 __global__ void tcw_stage_vt_kernel(const float *__restrict__ v, int64_t ld, int N, int Ns, int Bw, int hd, int Dp,
                                     __half *__restrict__ vt) {
     __shared__ float tile[32][33];
-    const int64_t nk = static_cast<int64_t>(Bw) * Ns;
-    const int64_t key0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int nk = Bw * Ns;  // < 2^31 (checked by the host)
+    const int key0 = blockIdx.x * 32;
     const int d0 = blockIdx.y * 32, h = blockIdx.z;
+    const float *vh = v + static_cast<int64_t>(h) * hd;
     for (int rr = threadIdx.y; rr < 32; rr += blockDim.y) {
-        const int64_t key = key0 + rr;
+        const int key = key0 + rr;
         const int d = d0 + threadIdx.x;
         float val = 0.f;
         if (key < nk && d < hd) {
-            const int w = static_cast<int>(key / Ns), r = static_cast<int>(key % Ns);
-            if (r < N) val = v[(static_cast<int64_t>(w) * N + r) * ld + static_cast<int64_t>(h) * hd + d];
+            const int w = key / Ns, r = key - w * Ns;
+            if (r < N) val = vh[static_cast<int64_t>(w * N + r) * ld + d];
         }
         tile[rr][threadIdx.x] = val;
     }
     __syncthreads();
+    __half *vrow = vt + (static_cast<int64_t>(h) * Dp + d0) * nk;
     for (int rr = threadIdx.y; rr < 32; rr += blockDim.y) {
-        const int64_t key = key0 + threadIdx.x;
-        if (key < nk) vt[(static_cast<int64_t>(h) * Dp + d0 + rr) * nk + key] = __float2half_rn(tile[threadIdx.x][rr]);
+        const int key = key0 + threadIdx.x;
+        if (key < nk) vrow[static_cast<int64_t>(rr) * nk + key] = __float2half_rn(tile[threadIdx.x][rr]);
     }
 }
 
-template <int DP>
+template <int DP, bool PACK>
 cudaError_t launch_tcw(const __half *qh, const __half *kh, const __half *vth, int Bw, int NQ, int N, int heads, int hd,
                        float scale, float *o, int64_t o_ld, int *err, cudaStream_t s) {
-    using C = TW<DP>;
+    using C = TW<DP, PACK>;
     const int Ns = attn_tcw_kstride(N);
     const int P = (Ns <= C::BK && NQ <= C::BQ) ? (C::BQ / NQ < C::BK / Ns ? C::BQ / NQ : C::BK / Ns) : 0;
     const int nt = P ? 1 : (N + C::BK - 1) / C::BK;
@@ -379,10 +423,11 @@ cudaError_t launch_tcw(const __half *qh, const __half *kh, const __half *vth, in
         !make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kh, 2, dk, sqk, bk, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, vth, 2, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(attn_tcw_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if ((P > 0) != PACK) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(attn_tcw_kernel<DP, PACK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attn_tcw_kernel<DP><<<dim3(static_cast<unsigned>(qtiles), static_cast<unsigned>(groups),
+    attn_tcw_kernel<DP, PACK><<<dim3(static_cast<unsigned>(qtiles), static_cast<unsigned>(groups),
                                static_cast<unsigned>(heads)),
                           C::THREADS, C::SMEM_BYTES, s>>>(tq, tk, tv, Bw, NQ, N, Ns, hd, P, nt,
                                                           scale * 1.4426950408889634f, o, o_ld, err);
@@ -393,7 +438,9 @@ cudaError_t launch_tcw(const __half *qh, const __half *kh, const __half *vth, in
 
 cudaError_t attn_tcw_stage(const float *q, int64_t q_ld, const float *k, const float *v, int64_t kv_ld, int Bw,
                            int NQ, int N, int heads, int hd, __half *qh, __half *kh, __half *vth, cudaStream_t s) {
-    if (Bw <= 0 || NQ <= 0 || N <= 0 || heads <= 0 || hd <= 0 || hd > 128 || NQ > N) return cudaErrorInvalidValue;
+    if (Bw <= 0 || NQ <= 0 || N <= 0 || heads <= 0 || hd <= 0 || hd > 128 || NQ > N ||
+        static_cast<int64_t>(Bw) * attn_tcw_kstride(N) >= (int64_t{1} << 31))
+        return cudaErrorInvalidValue;
     const int Dp = attn_tcw_dpad(hd), Ns = attn_tcw_kstride(N);
     const int64_t tq = static_cast<int64_t>(heads) * Bw * NQ * (Dp / 8);
     const int64_t tk = static_cast<int64_t>(heads) * Bw * Ns * (Dp / 8);
@@ -413,8 +460,13 @@ cudaError_t attn_tcw(const __half *qh, const __half *kh, const __half *vth, int 
     if (Bw <= 0 || NQ <= 0 || N <= 0 || heads <= 0 || hd <= 0 || hd > 128 || NQ > N || !qh || !kh || !vth || !o ||
         !err)
         return cudaErrorInvalidValue;
-    return attn_tcw_dpad(hd) == 64 ? launch_tcw<64>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s)
-                                   : launch_tcw<128>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s);
+    const int Ns = attn_tcw_kstride(N);
+    const bool pack = Ns <= 128 && NQ <= 128;  // whole windows share 128-row tiles
+    if (attn_tcw_dpad(hd) == 64)
+        return pack ? launch_tcw<64, true>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s)
+                    : launch_tcw<64, false>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s);
+    return pack ? launch_tcw<128, true>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s)
+                : launch_tcw<128, false>(qh, kh, vth, Bw, NQ, N, heads, hd, scale, o, o_ld, err, s);
 }
 
 }  // namespace b200
