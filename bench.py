@@ -18,6 +18,7 @@ tracker SimpleFPN neck -- the whole of sam3_encode_image.
 python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 python bench.py --workload video       (config 5: Hiera-B+ video tracking frames/s, one stream per GPU, 1..8 GPUs)
 python bench.py --workload pcs|memory  (secondary lines: config 4 detector / config 5 memory stages, 1 GPU)
+python bench.py --workload pvs         (config 1: SAM2.1 Hiera-tiny PVS images/s, device and end to end, 1 GPU)
 python bench.py --workload mmq         (config 2: MUL_MAT sweep, Q8_0 / Q4_0 at the four ViT shapes, 1 GPU)
 """
 from __future__ import annotations
@@ -363,7 +364,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "video", "memory", "mmq"],
+    ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "pvs", "video", "memory", "mmq"],
                     help="encode (default: the headline, config 3); pcs / video: the config 4 detector or the "
                          "config 5 tracker memory stages, timed per image / frame (sam3.cpp_b200/component_bench.py)")
     ap.add_argument("--images", type=int, default=BATCH,
@@ -397,11 +398,11 @@ def main():
         return 0
     if args.workload == "video":
         return run_video(args, model_mod)
-    if args.workload in ("pcs", "memory"):
+    if args.workload in ("pcs", "pvs", "memory"):
         b200 = _load("b200")
         comp = _load("component_bench")
         be = b200.Backend(0)
-        fn = comp.run_pcs if args.workload == "pcs" else comp.run_video
+        fn = {"pcs": comp.run_pcs, "pvs": comp.run_pvs, "memory": comp.run_video}[args.workload]
         print(json.dumps(fn(b200, model_mod, be, args.steps, args.warmup)), flush=True)
         be.free()
         return 0

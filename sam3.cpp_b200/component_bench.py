@@ -344,6 +344,81 @@ def run_pcs(b200, model_mod, be, steps: int, warmup: int) -> dict:
                           "seg_head": stages[3]}}
 
 
+def run_pvs(b200, model_mod, be, steps: int, warmup: int) -> dict:
+    """Config 1 (SAM2.1 Hiera-tiny, PVS): a seeded uint8 1024^2 image -> SAM2 preprocessing -> Hiera-tiny
+    trunk + FPN -> prompt encoder + mask decoder for one positive point -> the four masks at the image's
+    size.  value: device-timed images/s with the image already on the device; e2e: the same step from a
+    pinned host image with the masks read back (sam3b200_tensor_set / _get around it)."""
+    import torch
+    lib = b200.lib()
+    hp = model_mod.SAM2_HIERA_TINY
+    S = hp["img"]
+    enc = be.hiera(hp)
+    enc.load(hiera_weights(model_mod, enc, hp))
+    dec = be.sam_decoder(dict(feat_size=S // 16, embed=256, depth=2, heads=8, mlp_dim=2048, n_multimask=3,
+                              pred_obj_scores=1, max_points=16))
+    dec.load(sam_dec_weights(model_mod))
+    img = model_mod.random_images(1, S, seed=77)[0]
+    src = be.upload(img)
+    pinned = torch.from_numpy(img).pin_memory()
+    chw = be.alloc(3 * S * S * 4)
+    masks = be.alloc(4 * S * S)
+    masks_host = torch.empty(4 * S * S, dtype=torch.uint8).pin_memory()
+    point, label = [[0.41 * S, 0.43 * S]], [1]
+    stream = torch.cuda.ExternalStream(be.stream)
+
+    def step(marks=None):
+        def mark():
+            if marks is not None:
+                marks.append(_events(torch, stream))
+        mark()
+        be.preprocess_sam2(src, S, S, S, chw)
+        enc.encode_device(chw)
+        mark()
+        dec.run(enc.output_ptr(2), enc.output_ptr(0), enc.output_ptr(1), point, label, S, S, S)
+        for m in range(4):
+            b200._check(lib.sam3b200_sam_dec_mask(dec.h, m, S, S, masks.ptr + m * S * S), "sam_dec_mask")
+        mark()
+
+    def step_e2e():
+        b200._check(lib.sam3b200_tensor_set(be.h, src.ptr, pinned.data_ptr(), 0, S * S * 3), "image set")
+        step()
+        b200._check(lib.sam3b200_tensor_get(be.h, masks.ptr, masks_host.data_ptr(), 0, 4 * S * S), "masks get")
+
+    def timed(fn):
+        be.synchronize()
+        e0, e1 = _events(torch, stream), None
+        for _ in range(steps):
+            fn()
+        e1 = _events(torch, stream)
+        be.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    for _ in range(warmup):
+        step()
+        step_e2e()
+    be.synchronize()
+    stages = np.zeros(2)
+    for _ in range(steps):
+        marks = []
+        step(marks)
+        be.synchronize()
+        stages += [marks[i].elapsed_time(marks[i + 1]) for i in range(2)]
+    stages /= steps
+    ms = timed(step)
+    e2e_ms = timed(step_e2e)
+    enc.free()
+    dec.free()
+    return {"metric": "SAM2.1 Hiera-tiny PVS images/s (preprocess + encode + one-point decode + 4 masks)",
+            "value": 1000.0 / ms, "unit": "images/s", "higher_is_better": True, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms, "dtype": "int8 linear / fp16 attention", "data": "synthetic", "n_gpus": 1,
+            "config": {"workload": "cfg1: SAM2.1 Hiera-tiny 1024^2, Q8_0 linear weights where the row length allows "
+                                   "(random-init), one positive point, 4 masks at 1024^2"},
+            "e2e": {"value": 1000.0 / e2e_ms, "unit": "images/s", "h2d_bytes_per_step": S * S * 3,
+                    "d2h_bytes_per_step": 4 * S * S},
+            "stages_ms": {"preprocess_and_encode": stages[0], "decode_and_masks": stages[1]}}
+
+
 def run_video(b200, model_mod, be, steps: int, warmup: int) -> dict:
     import torch
     lib = b200.lib()

@@ -22,6 +22,7 @@
 #include "attn_simt.cuh"
 #include "model_util.h"
 #include "row_norm.cuh"
+#include "sgemm.cuh"
 
 #include <cmath>
 #include <cstdio>
@@ -77,33 +78,6 @@ __global__ void to_channels_kernel(const float *__restrict__ x, int64_t P, int C
         const int c = c0 + j;
         const int64_t p = p0 + tx;
         if (c < C && p < P) y[static_cast<int64_t>(c) * P + p] = tile[tx][j];
-    }
-}
-
-// 1x1 convolution with an F32 kernel (ggml_conv_2d_sk_p0 on the high-resolution
-// features, sam3.cpp:10658, 10678), fp32: out[oc][p] = acc[oc] + bias[oc] +
-// add[oc][p]; x channel-major [C][P]; one thread per pixel, kernel in shared memory.
-template <int OC>
-__global__ void conv1x1_f32_kernel(const float *__restrict__ x, int C, int64_t P, const float *__restrict__ w,
-                                   const float *__restrict__ bias, const float *__restrict__ add,
-                                   float *__restrict__ out) {
-    extern __shared__ float wsm[];
-    for (int i = threadIdx.x; i < OC * C; i += blockDim.x) wsm[i] = w[i];
-    __syncthreads();
-    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (p >= P) return;
-    float acc[OC];
-#pragma unroll
-    for (int o = 0; o < OC; ++o) acc[o] = 0.f;
-    for (int c = 0; c < C; ++c) {
-        const float v = x[static_cast<int64_t>(c) * P + p];
-#pragma unroll
-        for (int o = 0; o < OC; ++o) acc[o] = fmaf(v, wsm[o * C + c], acc[o]);
-    }
-#pragma unroll
-    for (int o = 0; o < OC; ++o) {
-        const int64_t i = static_cast<int64_t>(o) * P + p;
-        out[i] = __fadd_rn(add[i], __fadd_rn(acc[o], bias[o]));
     }
 }
 
@@ -189,7 +163,7 @@ struct SamDec {
     DevBuf dense_pe, no_mask_dev, track_tok;  // track_tok: the token rows of a propagated frame's decode
     std::vector<std::string> missing;
     // activations
-    DevBuf tok, qpe, q2, keys, kpe, k2, tq, tk, tv, to, tmp_tok, tmp_keys, mlp, cm, up1, up1b, hs1, fs, up2, hs0,
+    DevBuf tok, qpe, q2, keys, kpe, k2, tq, tk, tv, to, tmp_tok, tmp_keys, mlp, cm, up1, up1b, hs1, up2, hs0,
         hyp, masks, heads_tmp;
     DevBuf part_o, part_ml;  // split-over-keys partials of the token -> image attentions
     float iou[4] = {0, 0, 0, 0}, obj = 0;
@@ -287,15 +261,20 @@ bool twoway(SamDec *d, const DecBlock &b, bool skip_pe) {
            ln(d, tk, HH, b.n4w, b.n4b, keys);
 }
 
-template <int OC>
-bool conv1x1(SamDec *d, const float *xc, int64_t P, const DevBuf &w, const DevBuf &b, const float *add_cm, float *out) {
-    const int smem = OC * d->D * 4;
-    if (!dlaunched(d, cudaFuncSetAttribute(conv1x1_f32_kernel<OC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                   "conv1x1 smem", 0))
+// 1x1 convolution with an F32 kernel (ggml_conv_2d_sk_p0 on the high-resolution
+// features, sam3.cpp:10658, 10678) in fp32: out[oc][p] = add[oc][p] + (sum_c w[oc][c]
+// x[p][c] + bias[oc]), x token-major [P][D] as the encoder hands it over, out
+// channel-major.  An f32 GEMM (one fma per channel in channel order, then the bias,
+// then the upscaled map).
+bool conv1x1(SamDec *d, const float *x_tok, int64_t P, int OC, const DevBuf &w, const DevBuf &b, const float *add_cm,
+             float *out) {
+    if (!dlaunched(d, sgemm_nt(w.as<float>(), d->D, 1, x_tok, d->D, 1, OC, static_cast<int>(P), d->D, b.as<float>(),
+                               out, P, false, d->be->stream, false, true),
+                   "sam_dec conv1x1"))
         return false;
-    conv1x1_f32_kernel<OC><<<nblocks(P, 128), 128, smem, d->be->stream>>>(xc, d->D, P, w.as<float>(), b.as<float>(),
-                                                                           add_cm, out);
-    return dlaunched(d, cudaGetLastError(), "sam_dec conv1x1");
+    const int64_t n = static_cast<int64_t>(OC) * P;
+    if (n % d->D != 0) return dlaunched(d, cudaErrorInvalidValue, "sam_dec conv1x1 add");
+    return add(d, add_cm, out, n / d->D, out);
 }
 
 bool to_channels(SamDec *d, const float *x, int64_t P, int C, float *y) {
@@ -328,11 +307,11 @@ bool decode(SamDec *d, const float *img, const float *fs0, const float *fs1, boo
         !add(d, tok, tt, nt, tt) || !ln(d, tt, nt, d->final_nw, d->final_nb, tok))
         return false;
     // upscaling: keys (token-major) -> channel-major; ConvT (D -> 64) + bias + conv_s1(feat_s1); LN2d; GELU
-    float *cm = d->cm.as<float>(), *up1 = d->up1.as<float>(), *fsb = d->fs.as<float>();
+    float *cm = d->cm.as<float>(), *up1 = d->up1.as<float>();
     if (!to_channels(d, d->keys.as<float>(), HH, D, cm) ||
         sam3b200_conv_transpose_2d(hb, d->up1_w16.p, cm, H, H, D, 64, 2, 2, 2, up1) != SAM3B200_STATUS_SUCCESS ||
-        !act(d, up1, 64 * P1, 0, d->up1_b.as<float>(), P1) || !to_channels(d, fs1, P1, D, fsb) ||
-        !conv1x1<64>(d, fsb, P1, d->cs1_w, d->cs1_b, up1, d->up1b.as<float>()))
+        !act(d, up1, 64 * P1, 0, d->up1_b.as<float>(), P1) ||
+        !conv1x1(d, fs1, P1, 64, d->cs1_w, d->cs1_b, up1, d->up1b.as<float>()))
         return false;
     ln_channels_kernel<<<nblocks(P1, 256), 256, 0, s>>>(d->up1b.as<float>(), 64, P1, d->up1_nw.as<float>(),
                                                         d->up1_nb.as<float>(), 1e-6f, up1);
@@ -341,8 +320,8 @@ bool decode(SamDec *d, const float *img, const float *fs0, const float *fs1, boo
     float *up2 = d->up2.as<float>();
     if (sam3b200_conv_transpose_2d(hb, d->up2_w16.p, up1, 2 * H, 2 * H, 64, 32, 2, 2, 2, d->hs0.as<float>()) !=
             SAM3B200_STATUS_SUCCESS ||
-        !act(d, d->hs0.as<float>(), 32 * P0, 0, d->up2_b.as<float>(), P0) || !to_channels(d, fs0, P0, D, fsb) ||
-        !conv1x1<32>(d, fsb, P0, d->cs0_w, d->cs0_b, d->hs0.as<float>(), up2) || !act(d, up2, 32 * P0, 2))
+        !act(d, d->hs0.as<float>(), 32 * P0, 0, d->up2_b.as<float>(), P0) ||
+        !conv1x1(d, fs0, P0, 32, d->cs0_w, d->cs0_b, d->hs0.as<float>(), up2) || !act(d, up2, 32 * P0, 2))
         return false;
     // hypernetworks on the mask tokens, masks, IoU and object heads
     const int s0 = d->hp.pred_obj_scores ? 1 : 0;
@@ -463,7 +442,7 @@ sam3b200_sam_dec *sam3b200_sam_dec_create(sam3b200_backend *hb, const sam3b200_s
                     d->tq.alloc(HH * D * 4) && d->tk.alloc(HH * D * 4) && d->tv.alloc(HH * D * 4) &&
                     d->to.alloc(HH * D * 4) && d->tmp_tok.alloc(NT * D * 4) && d->tmp_keys.alloc(HH * D * 4) &&
                     d->mlp.alloc(NT * hp->mlp_dim * 4) && d->cm.alloc(HH * D * 4) && d->up1.alloc(64 * P1 * 4) &&
-                    d->up1b.alloc(64 * P1 * 4) && d->fs.alloc(P0 * D * 4) && d->up2.alloc(32 * P0 * 4) &&
+                    d->up1b.alloc(64 * P1 * 4) && d->up2.alloc(32 * P0 * 4) &&
                     d->hs0.alloc(32 * P0 * 4) && d->hyp.alloc((4 * 32 + 8) * 4) && d->masks.alloc(4 * P0 * 4) &&
                     d->heads_tmp.alloc(2 * D * 4) &&
                     d->part_o.alloc(static_cast<size_t>(DEC_SPLITS) * hp->heads * NT * 32 * 4) &&
