@@ -117,7 +117,7 @@ sam3b200_backend *sam3b200_backend_init(int device) {
     be->device = device;
     be->num_sms = prop.multiProcessorCount;
     if (const char *ev = getenv("SAM3B200_MMQ_CVT")) be->mmq_cvt = atoi(ev) == 0 ? 0 : 1;
-    if (const char *ev = getenv("SAM3B200_MMQ_BN")) be->mmq_bn = atoi(ev) == 64 ? 64 : 128;
+    if (const char *ev = getenv("SAM3B200_MMQ_BN")) be->mmq_bn = atoi(ev) == 64 ? 64 : atoi(ev) == 128 ? 128 : 0;
     snprintf(be->name, sizeof(be->name), "B200[%d] %s", device, prop.name);
     if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
         !cuda_ok(cudaMalloc(&be->err, sizeof(int)), "cudaMalloc(err)") ||

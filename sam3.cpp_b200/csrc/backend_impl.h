@@ -15,7 +15,7 @@ struct Backend {
     int *err = nullptr;  // device error word written by bounded pipeline waits
     int mmq_impl = 0;    // SAM3B200_MMQ_*
     int mmq_cvt = 0;     // MMQ epilogue int->float conversion (tuning: env SAM3B200_MMQ_CVT=0|1)
-    int mmq_bn = 128;    // MMQ tile width (tuning: env SAM3B200_MMQ_BN=64|128)
+    int mmq_bn = 0;      // MMQ tile width: 0 = by K (tuning: env SAM3B200_MMQ_BN=64|128)
     char name[320] = {0};
     // scratch for the quantised activations of the current MUL_MAT
     void *act_codes = nullptr;

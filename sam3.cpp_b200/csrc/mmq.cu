@@ -211,7 +211,10 @@ struct TcCfg {
     static constexpr int Q_OFF = A_BYTES + B_BYTES;                    // A scale group, then BLK B scale records
     static constexpr int MIN_OFF = Q_OFF + Q_BYTES + BLK * QB_BYTES;   // Q4_1: A sum group, then BLK B minima
     static constexpr int STAGE_BYTES = MIN_OFF + (NIB == 2 ? Q_BYTES + BLK * QB_BYTES : 0);
-    static constexpr int STAGES = NIB == 2 ? 3 : BN == 128 ? 4 : 6;
+    // BN = 64 runs two CTAs per SM (3 stages and 256 TMEM columns each): one CTA's tile
+    // stores and handshakes overlap the other's MMAs
+    static constexpr int CTAS = BN == 64 ? 2 : 1;
+    static constexpr int STAGES = NIB == 2 ? 3 : BN == 128 ? 4 : 3;
     static constexpr int ZERO_OFF = STAGES * STAGE_BYTES;
     static constexpr int BAR_OFF = ZERO_OFF + Q_BYTES;
     static constexpr int EPQ = EPQ_;                // epilogue warps per used lane quarter (2 or 4)
@@ -222,8 +225,8 @@ struct TcCfg {
     static_assert(COLS % CHUNK == 0, "whole 32-column TMEM loads (and whole Q8_0 blocks) per thread");
     static constexpr int TERMS = NIB == 2 ? 3 : 2;  // TMEM per K-block: I, S (, M = m_w s_x), BN columns each
     static constexpr int SLOT_COLS = TERMS * BN;
-    static constexpr int SLOTS = 512 / SLOT_COLS;   // K-blocks in flight between MMA and epilogue
-    static constexpr int TMEM_COLS = 512;
+    static constexpr int TMEM_COLS = 512 / CTAS;
+    static constexpr int SLOTS = TMEM_COLS / SLOT_COLS;  // K-blocks in flight between MMA and epilogue
     static constexpr int RAW_STAGE = BN * BK / 2;
     static constexpr int RAW_OFF = BAR_OFF + 256;
     static constexpr int SMEM_BYTES = RAW_OFF + (NIB ? STAGES * RAW_STAGE : 0) + 1024;
@@ -392,7 +395,7 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
 }
 
 template <int MODE, int CVT, int BN, int EPQ, int NIB>
-__global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, 1)
+__global__ void __launch_bounds__(TcCfg<BN, EPQ>::THREADS, TcCfg<BN, EPQ>::CTAS)
     mmq_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const uint8_t *__restrict__ quads_a, const uint8_t *__restrict__ quads_b, int M, int N, int nblk,
                   int lda_q, int ldb_q, const MmqEpi ep, int *__restrict__ err, const uint8_t *__restrict__ sums_a,
@@ -722,7 +725,7 @@ static cudaError_t launch_tc_epq(const MmqArgs &a, int num_sms, cudaStream_t s) 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     const int tiles = ((M + C::ROWS - 1) / C::ROWS) * ((N + C::BN - 1) / C::BN);
-    const int grid = tiles < num_sms ? tiles : num_sms;
+    const int grid = tiles < C::CTAS * num_sms ? tiles : C::CTAS * num_sms;
     MmqEpi ep;
     ep.bias = a.bias;
     ep.y = a.y;
@@ -798,6 +801,10 @@ static cudaError_t dispatch_tc(const MmqArgs &a, int mode, int num_sms, cudaStre
 }
 
 cudaError_t mmq_tc(const MmqArgs &a, int mode, int num_sms, cudaStream_t s, int cvt, int bn) {
+    // auto: short K (many tiles per CTA, the tile stores a large share) on the two-CTA BN = 64
+    // configuration, long K (few tiles, long K loops) on BN = 128 (measured at the ViT shapes:
+    // qkv -6%, fc1 -11%, proj -2% with BN = 64 x 2 CTAs; fc2, K = 4736, +4%)
+    if (bn == 0) bn = a.a.K <= 2048 ? 64 : 128;
     if (!valid_args(a) || num_sms <= 0 || a.a.nib != 0 ||
         (a.b.nib == 2) != (a.b_mins != nullptr) || (a.b.nib == 2 && !a.a_sums))  // Q4_1: minima and sum fields
         return cudaErrorInvalidValue;

@@ -119,7 +119,8 @@ cudaError_t repack_weight_blocks(int type, const void *blocks, int N, int K, voi
 // tcgen05 tensor-core MMQ, tile 128 x bn (bn = 64 or 128).  cvt selects the
 // epilogue's exact int32 -> fp32 conversion: 0 = cvt instruction, 1 =
 // magic-number add.
-cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, int cvt = 0, int bn = 128);
+// bn = 0 picks the tile width from K.
+cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, int cvt = 0, int bn = 0);
 
 // Straight SIMT version of the same arithmetic (small M, cross-checks).
 cudaError_t mmq_simt(const MmqArgs &args, int mode, cudaStream_t s);
