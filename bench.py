@@ -367,6 +367,10 @@ def main():
     ap.add_argument("--workload", default="encode", choices=["encode", "pcs", "pvs", "video", "memory", "mmq"],
                     help="encode (default: the headline, config 3); pcs / video: the config 4 detector or the "
                          "config 5 tracker memory stages, timed per image / frame (sam3.cpp_b200/component_bench.py)")
+    ap.add_argument("--arith", default="dq16", choices=["dq16", "exact"],
+                    help="linear-layer arithmetic of the encoder (sam3b200_set_arith): dq16 (default) = Q8_0 "
+                         "codes and weight blocks dequantised to fp16 on the fp16 tensor cores; exact = int8 block "
+                         "dots with the block-ordered fp32 fold")
     ap.add_argument("--images", type=int, default=BATCH,
                     help="images per step (default 64, the config's batch; smaller only for profiling runs)")
     args = ap.parse_args()
@@ -384,15 +388,20 @@ def main():
         peak = measured_int8_peak_tops()
         res = comp.run_mmq(b200, model_mod, be, max(args.steps, 10), max(args.warmup, 3), peak)
         sweep = res["sweep"]
-        q8 = [r for r in sweep if r["type"] == "Q8_0" and r["order"] == "tokens"]
-        ops = sum(2.0 * r["M"] * r["K"] * r["N"] for r in q8)
-        kern_s = sum(r["kernel_us"] for r in q8) * 1e-6
-        line = {"metric": "MMQ TOP/s vs int8 peak (config 2 sweep)", "value": ops / kern_s / 1e12,
+        def total(arith):
+            rs = [r for r in sweep if r["type"] == "Q8_0" and r["order"] == "tokens" and r["arith"] == arith]
+            return sum(2.0 * r["M"] * r["K"] * r["N"] for r in rs) / (sum(r["kernel_us"] for r in rs) * 1e-6) / 1e12
+        tops, tops_exact = total(args.arith), total("exact" if args.arith == "dq16" else "dq16")
+        line = {"metric": "MMQ TOP/s vs int8 peak (config 2 sweep)", "value": tops,
                 "unit": "TOP/s", "n_gpus": 1, "steps": max(args.steps, 10), "warmup": max(args.warmup, 3),
-                "higher_is_better": True, "dtype": "int8 codes (fp16-held), fp32 fold", "data": "synthetic",
+                "higher_is_better": True,
+                "dtype": "Q8_0 codes as fp16 x fp16, fp32 accumulate" if args.arith == "dq16"
+                         else "int8 block dots, fp32 fold", "data": "synthetic",
                 "config": {"workload": "cfg2: Q8_0 / Q4_0 MUL_MAT at M = 5184, (K, N) in qkv/proj/fc1/fc2, token "
-                                       "and win_part row orders; value = Q8_0 token-order ops / kernel time"},
-                "peak_int8_tops": peak, "frac": ops / kern_s / 1e12 / peak, "sweep": sweep}
+                                       "and win_part row orders; value = Q8_0 token-order ops / kernel time",
+                           "arith": args.arith},
+                "peak_int8_tops": peak, "frac": tops / peak,
+                "other_arith_tops": tops_exact, "sweep": sweep}
         print(json.dumps(line), flush=True)
         be.free()
         return 0
@@ -418,6 +427,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     be = b200.Backend(local)
+    arith = b200.ARITH_DQ16 if args.arith == "dq16" else b200.ARITH_EXACT
+    be.set_arith(arith)
     tensors = model_mod.random_vit_weights(hp, seed=0)
     vit = be.vit(hp)
     vit.load(tensors)
@@ -480,39 +491,74 @@ def main():
         step_e2e()
     e2e_ms = timed(step_e2e, args.steps)
 
+    # the other arithmetic, same weights and images, for comparison (device-resident, 1 warm-up + 2 steps)
+    other = b200.ARITH_EXACT if arith == b200.ARITH_DQ16 else b200.ARITH_DQ16
+    be.set_arith(other)
+    step_device()
+    be.profile(True)
+    other_ms = timed(step_device, 2)
+    other_mmq_ms, _ = be.profile_read(0)
+    be.profile(False)
+    be.set_arith(arith)
+
     images = batch * args.steps
     value = images / (ms / 1000.0)
     e2e = images / (e2e_ms / 1000.0)
     ops = vit_ops_per_image(hp)
     mmq_per_launch_ms = mmq_ms / max(mmq_n, 1)
     achieved = ops * len(mine) * args.steps / (mmq_ms / 1000.0) / 1e12  # TOP/s of the MUL_MAT launches
+    other_achieved = ops * len(mine) * 2 / (other_mmq_ms / 1000.0) / 1e12
     peak_int8 = measured_int8_peak_tops() if rank == 0 else 0.0
+    peaks = {}
+    if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")):
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    peak_f16 = peaks.get("bf16_tflops") or 1590.0
+    dq16 = arith == b200.ARITH_DQ16
+    if dq16:
+        kernel = ("mmq_dq16_kernel (quantised MUL_MAT, 4 per ViT block: Q8_0 activation codes and weight blocks "
+                  "dequantised to fp16, fp16 tcgen05 MMA, fp32 accumulation)")
+        peak = peak_f16
+        peak_source = ("MEASURED_PEAKS.json bf16_tflops (burst; dense fp16 runs at the bf16 rate)"
+                       if peaks.get("bf16_tflops") else "fallback 1.59 PFLOP/s")
+    else:
+        kernel = "mmq_tc_kernel (quantised MUL_MAT, 4 per ViT block: int8 block dots, fp32 block fold)"
+        peak = peak_int8
+        peak_source = ("dense int8 measured in this run (cuBLASLt torch._int_mm 8192^3); "
+                       "MEASURED_PEAKS.json holds no int8 figure")
 
     if rank == 0:
         line = {
             "metric": "SAM3 Q8_0 ViT encode images/s",
             "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "vs_baseline": None,
+            "dtype": "Q8_0 codes as fp16 x fp16, fp32 accumulate" if dq16 else "int8 block dots, fp32 fold",
+            "data": "synthetic",
             "config": {"workload": "cfg3: SAM3 visual-only ViT-32 (Q8_0) + trk SimpleFPN neck, 1008x1008, "
                                    "64 seeded uint8 images per step split across ranks",
+                       "arith": args.arith,
                        "global_batch": batch, "seq_len": (S // hp["patch"]) ** 2, "parallelism": f"dp{world}",
                        "weights": "random-init N(0,0.02), Q8_0 reference quantiser rule",
                        "l2": "no flush: per-image working set (~0.5 GB of weights) exceeds the 126 MB L2"},
             "e2e": {"value": e2e, "unit": "images/s",
                     "h2d_bytes_per_step": int(batch * S * S * 3),
                     "d2h_bytes_per_step": int(small.nbytes * batch)},
-            "roofline": {"kernel": "mmq_tc_kernel (quantised MUL_MAT, 4 per ViT block)", "bound": "tensor",
-                         "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
-                         "frac": achieved / peak_int8 if peak_int8 else None,
-                         "traffic": MMQ_DRAM_BYTES_PER_LAUNCH, "traffic_unit": "bytes per launch",
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
+            "roofline": {"kernel": kernel, "bound": "tensor",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None,
+                         "frac_of_int8_peak": achieved / peak_int8 if peak_int8 else None,
+                         "peak_int8_measured": peak_int8,
+                         "traffic": None if dq16 else MMQ_DRAM_BYTES_PER_LAUNCH, "traffic_unit": "bytes per launch",
+                         "traffic_source": "not captured for this kernel" if dq16 else
+                                           "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
                                            "MUL_MAT launches of one ViT block (qkv 10.6, proj 28.9, fc1 13.1, "
                                            "fc2 57.1 MB); operands stream L2 -> SM, not from DRAM",
-                         "peak_source": "dense int8 measured in this run (cuBLASLt torch._int_mm 8192^3); "
-                                        "MEASURED_PEAKS.json holds no int8 figure",
+                         "peak_source": peak_source,
                          "ops_per_image": ops, "launches_timed": mmq_n,
                          "avg_launch_ms": mmq_per_launch_ms},
+            "other_arith": {"arith": "exact" if dq16 else "dq16", "value": batch * 2 / (other_ms / 1000.0),
+                            "unit": "images/s", "steps": 2, "mmq_achieved_tops": other_achieved,
+                            "note": "same weights and images, device-resident, timed after the main run"},
             "gpu_launches": int(launches),
             "clocks": clk,
         }

@@ -156,6 +156,34 @@ int sam3b200_mul_mat_noalloc(sam3b200_backend *be, const sam3b200_weight *w, con
 /* Select the MUL_MAT kernel (SAM3B200_MMQ_*); returns the previous one. */
 int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
 
+/* Arithmetic of the quantised linear layers inside the model-level encoder
+ * runners (sam3b200_vit_*: the ViT blocks of sam3_vit_block_forward,
+ * sam3.cpp:3742,3783,3796,3799).  Both quantise the activations to Q8_0 with
+ * ggml-cpu's rule (the same codes and scales):
+ *   SAM3B200_ARITH_EXACT: int8 tcgen05 block dots (bit-exact with ggml's
+ *     int32 block dots) folded block by block in fp32 on the CUDA cores;
+ *   SAM3B200_ARITH_DQ16 (default): activation codes and weight blocks
+ *     dequantised to fp16 (fp16(q * d), one rounding of the exact product)
+ *     and multiplied on the fp16 tensor cores with fp32 accumulation over
+ *     all of K -- the same sum up to rounding (~1e-4 normwise), without the
+ *     per-block fold; the weights are held a second time as fp16.
+ * Op-level sam3b200_mul_mat is always EXACT.  Returns the previous value;
+ * other values are ignored.  Environment: SAM3B200_ARITH=0|1 at init. */
+#define SAM3B200_ARITH_EXACT 0
+#define SAM3B200_ARITH_DQ16  1
+int sam3b200_set_arith(sam3b200_backend *be, int arith);
+
+/* GGML_OP_MUL_MAT (sam3.cpp:3742,3783,3796,3799) in the DQ16 arithmetic of
+ * sam3b200_set_arith: x quantised to Q8_0 (ggml-cpu's rule), codes and
+ * weight blocks dequantised to fp16, fp16 tensor-core GEMM with fp32
+ * accumulation, + bias.  Same arguments as sam3b200_mul_mat; Q8_0 and Q4_0
+ * weights only (others are refused with an error).  The first call with a
+ * weight makes its fp16 copy (N*K*2 bytes, freed with the weight); scratch
+ * is the backend's, as for sam3b200_mul_mat.  Asynchronous on the backend
+ * stream. */
+int sam3b200_mul_mat_dq16(sam3b200_backend *be, const sam3b200_weight *w, const float *x, int64_t ldx, int64_t M,
+                          const float *bias, float *dst, int64_t ldd);
+
 /* GGML_OP_FLASH_ATTN_EXT as the ViT blocks use it (sam3.cpp:3778: no mask,
  * max_bias 0, logit softcap 0): dst = softmax(q k^T * scale) v per (head,
  * batch).  q, k, v: device f32 ggml tensors [D, N, heads, batch], contiguous

@@ -19,6 +19,7 @@ HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "sam3_b200.h")
 STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS, STATUS_ABORTED = -2, -1, 0, 1
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 0, 1, 2, 3, 8
 MMQ_AUTO, MMQ_TC, MMQ_SIMT = 0, 1, 2
+ARITH_EXACT, ARITH_DQ16 = 0, 1
 TYPE_I32 = 26
 (OP_NONE, OP_VIEW, OP_MUL_MAT, OP_ADD, OP_FLASH_ATTN_EXT, OP_CONV_TRANSPOSE_2D, OP_CONV_2D, OP_GET_ROWS,
  OP_CONT, OP_MUL, OP_SCALE, OP_UNARY, OP_NORM, OP_SOFT_MAX, OP_WIN_PART, OP_WIN_UNPART, OP_SUB, OP_REPEAT,
@@ -271,6 +272,8 @@ def lib() -> ctypes.CDLL:
         "sam3b200_mul_mat_block_dots": (i32, [vp, vp, vp, i64, vp]),
         "sam3b200_mul_mat_noalloc": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
         "sam3b200_set_mmq_impl": (i32, [vp, i32]),
+        "sam3b200_set_arith": (i32, [vp, i32]),
+        "sam3b200_mul_mat_dq16": (i32, [vp, vp, vp, i64, i64, vp, vp, i64]),
         "sam3b200_vit_create": (vp, [vp, vp]),
         "sam3b200_vit_free": (None, [vp]),
         "sam3b200_vit_set_tensor": (i32, [vp, ctypes.c_char_p, i32, vp, vp]),
@@ -1253,11 +1256,22 @@ class Backend:
     def set_mmq_impl(self, impl: int) -> int:
         return lib().sam3b200_set_mmq_impl(self.h, impl)
 
+    def set_arith(self, arith: int) -> int:
+        """sam3b200_set_arith: ARITH_EXACT or ARITH_DQ16 for the encoder runners; returns the previous one."""
+        return lib().sam3b200_set_arith(self.h, arith)
+
     def mul_mat(self, w: Weight, x: DeviceBuffer, M: int, y: DeviceBuffer, bias: DeviceBuffer | None = None,
                 ldx: int | None = None, ldy: int | None = None) -> None:
         st = lib().sam3b200_mul_mat(self.h, w.h, x.ptr, ldx or w.K, M, bias.ptr if bias else None, y.ptr,
                                     ldy or w.N)
         _check(st, "mul_mat")
+
+    def mul_mat_dq16(self, w: Weight, x: DeviceBuffer, M: int, y: DeviceBuffer, bias: DeviceBuffer | None = None,
+                     ldx: int | None = None, ldy: int | None = None) -> None:
+        """sam3b200_mul_mat_dq16: the MUL_MAT in the DQ16 arithmetic (fp16 tensor cores on dequantised Q8_0)."""
+        st = lib().sam3b200_mul_mat_dq16(self.h, w.h, x.ptr, ldx or w.K, M, bias.ptr if bias else None, y.ptr,
+                                         ldy or w.N)
+        _check(st, "mul_mat_dq16")
 
     def mul_mat_noalloc(self, w: Weight, x: DeviceBuffer, M: int, y: DeviceBuffer,
                         bias: DeviceBuffer | None = None) -> None:

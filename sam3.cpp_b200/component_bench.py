@@ -498,14 +498,18 @@ def run_mmq(b200, model_mod, be, steps: int, warmup: int, peak_int8_tops: float 
     the MUL_MAT kernel alone (CUDA events around its launches, via the
     backend profiler) and the whole op (activation quantisation + kernel),
     as TOP/s of 2*M*K*N.  Activations N(0, 1), weights N(0, 0.02) quantised
-    with the reference rule."""
+    with the reference rule.  Both arithmetics: exact (int8 block dots, the
+    fp32 block fold) and dq16 (the dequantised fp16 operands on the fp16
+    tensor cores; its op time includes the quantise + dequantise passes)."""
     import torch
     stream = torch.cuda.ExternalStream(be.stream)
     G, win, M = 72, 24, 72 * 72
     rng = np.random.default_rng(2)
     perm = win_part_rows(G, win)
     out = []
-    for qtype, qname in ((Q8_0, "Q8_0"), (Q4_0, "Q4_0")):
+    for (qtype, qname), arith in [((Q8_0, "Q8_0"), "exact"), ((Q4_0, "Q4_0"), "exact"),
+                                  ((Q8_0, "Q8_0"), "dq16"), ((Q4_0, "Q4_0"), "dq16")]:
+        op = be.mul_mat if arith == "exact" else be.mul_mat_dq16
         for name, K, N in MMQ_SHAPES:
             wq = model_mod.quantize_rows(qtype, rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
             w = be.weight(qtype, wq, K, N)
@@ -515,13 +519,13 @@ def run_mmq(b200, model_mod, be, steps: int, warmup: int, peak_int8_tops: float 
             for order, xs in (("tokens", x), ("win_part", x[perm])):
                 xd = be.upload(np.ascontiguousarray(xs))
                 for _ in range(warmup):
-                    be.mul_mat(w, xd, M, y, bias=bias)
+                    op(w, xd, M, y, bias=bias)
                 be.synchronize()
                 be.profile(True)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
                 for _ in range(steps):
-                    be.mul_mat(w, xd, M, y, bias=bias)
+                    op(w, xd, M, y, bias=bias)
                 e1.record(stream)
                 be.synchronize()
                 op_ms = e0.elapsed_time(e1) / steps
@@ -529,7 +533,7 @@ def run_mmq(b200, model_mod, be, steps: int, warmup: int, peak_int8_tops: float 
                 be.profile(False)
                 k_ms /= max(k_n, 1)
                 ops = 2.0 * M * K * N
-                rec = {"type": qname, "layer": name, "M": M, "K": K, "N": N, "order": order,
+                rec = {"type": qname, "arith": arith, "layer": name, "M": M, "K": K, "N": N, "order": order,
                        "kernel_us": k_ms * 1e3, "op_us": op_ms * 1e3,
                        "kernel_tops": ops / (k_ms * 1e-3) / 1e12, "op_tops": ops / (op_ms * 1e-3) / 1e12}
                 if peak_int8_tops:

@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
     flash_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, int N, int heads, float c_log2,
                          float *__restrict__ out, int8_t *__restrict__ qcodes, __half *__restrict__ qquads, int qld,
+                         __half *__restrict__ o16,
                          int *__restrict__ err) {
     using C = AttnCfg;
     extern __shared__ uint8_t smem_raw[];
@@ -321,7 +322,31 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                     const int64_t r = static_cast<int64_t>(bb) * N + n;  // output row
 #pragma unroll
                     for (int d = 0; d < C::HD; ++d) o[d] = o[d] * inv;
-                    if (qcodes) {
+                    if (o16) {  // Q8_0 of the row's 32-blocks, written dequantised as fp16
+                        const int E = heads * C::HD;
+#pragma unroll
+                        for (int hb = 0; hb < C::HD; hb += 32) {
+                            float amax = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[hb + i]));
+                            const float dq = __fdiv_rn(amax, 127.f);
+                            const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                            const float dh = __half2float(__float2half_rn(dq));
+                            uint4 *dst = reinterpret_cast<uint4 *>(o16 + r * E + h * C::HD + hb);
+#pragma unroll
+                            for (int i = 0; i < 32; i += 8) {
+                                uint32_t hw[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float a0 = static_cast<float>(__float2int_rn(__fmul_rn(o[hb + i + 2 * e], id)));
+                                    const float a1 = static_cast<float>(__float2int_rn(__fmul_rn(o[hb + i + 2 * e + 1], id)));
+                                    const __half2 h2 = __floats2half2_rn(__fmul_rn(a0, dh), __fmul_rn(a1, dh));
+                                    hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                                }
+                                dst[i >> 3] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                            }
+                        }
+                    } else if (qcodes) {
                         const int E = heads * C::HD;
 #pragma unroll
                         for (int hb = 0; hb < C::HD; hb += 32) {
@@ -365,8 +390,8 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
 cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B, int N, int heads, float scale,
                             const AttnOut &o, int *err, cudaStream_t s) {
     using C = AttnCfg;
-    if (B <= 0 || N <= 0 || heads <= 0 || N % 8 != 0 || !err || (!o.f32 && !o.codes) ||
-        (o.codes && (!o.quads || o.ld < B * N)))
+    if (B <= 0 || N <= 0 || heads <= 0 || N % 8 != 0 || !err || (!o.f32 && !o.codes && !o.dq16) ||
+        (o.codes && (!o.quads || o.ld < B * N)) || (reinterpret_cast<uintptr_t>(o.dq16) & 15))
         return cudaErrorInvalidValue;
     const uint64_t bhn = static_cast<uint64_t>(B) * heads;
     CUtensorMap tq, tk, tv;
@@ -387,7 +412,7 @@ cudaError_t flash_attention(const void *q, const void *k, const void *vt, int B,
     dim3 grid((N + C::QT * C::ROWS - 1) / (C::QT * C::ROWS), static_cast<unsigned>(bhn));
     flash_attn_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(
         tq, tk, tv, N, heads, scale * 1.4426950408889634f, o.f32, static_cast<int8_t *>(o.codes),
-        static_cast<__half *>(o.quads), o.ld, err);
+        static_cast<__half *>(o.quads), o.ld, static_cast<__half *>(o.dq16), err);
     return cudaGetLastError();
 }
 

@@ -13,6 +13,9 @@ struct AttnOut {
     void *codes = nullptr;
     void *quads = nullptr;
     int ld = 0;
+    // or (dq16 set) the same Q8_0 quantisation written dequantised,
+    // fp16(q * fp16(d)) [B*N][heads*64] -- the A operand of mmq_dq16
+    void *dq16 = nullptr;
 };
 
 // q, k: bf16 [B*heads][N][64]; vt: bf16 [B*heads][64][N] (V transposed).

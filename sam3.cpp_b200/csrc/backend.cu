@@ -118,6 +118,8 @@ sam3b200_backend *sam3b200_backend_init(int device) {
     be->num_sms = prop.multiProcessorCount;
     if (const char *ev = getenv("SAM3B200_MMQ_CVT")) be->mmq_cvt = atoi(ev) == 0 ? 0 : 1;
     if (const char *ev = getenv("SAM3B200_MMQ_BN")) be->mmq_bn = atoi(ev) == 64 ? 64 : atoi(ev) == 128 ? 128 : 0;
+    if (const char *ev = getenv("SAM3B200_ARITH"))
+        be->mmq_arith = atoi(ev) == SAM3B200_ARITH_EXACT ? SAM3B200_ARITH_EXACT : SAM3B200_ARITH_DQ16;
     snprintf(be->name, sizeof(be->name), "B200[%d] %s", device, prop.name);
     if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "cudaStreamCreate") ||
         !cuda_ok(cudaMalloc(&be->err, sizeof(int)), "cudaMalloc(err)") ||
@@ -331,6 +333,7 @@ void sam3b200_weight_free(sam3b200_backend *h, sam3b200_weight *wh) {
     cudaFree(w->quads);
     cudaFree(w->mins);
     cudaFree(w->dense);
+    cudaFree(w->w16);
     delete w;
 }
 
@@ -339,6 +342,14 @@ int sam3b200_set_mmq_impl(sam3b200_backend *h, int impl) {
     if (!be) return -1;
     const int prev = be->mmq_impl;
     if (impl >= SAM3B200_MMQ_AUTO && impl <= SAM3B200_MMQ_SIMT) be->mmq_impl = impl;
+    return prev;
+}
+
+int sam3b200_set_arith(sam3b200_backend *h, int arith) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    if (!be) return -1;
+    const int prev = be->mmq_arith;
+    if (arith == SAM3B200_ARITH_EXACT || arith == SAM3B200_ARITH_DQ16) be->mmq_arith = arith;
     return prev;
 }
 
@@ -440,4 +451,63 @@ extern "C" int sam3b200_mul_mat_block_dots(sam3b200_backend *h, const sam3b200_w
     const int st = run_mul_mat(be, w, x, w->K, M, nullptr, nullptr, 0, dst_dev);
     if (st != SAM3B200_STATUS_SUCCESS) return st;
     return sam3b200_backend_synchronize(h);
+}
+
+extern "C" int sam3b200_mul_mat_dq16(sam3b200_backend *h, const sam3b200_weight *wh, const float *x, int64_t ldx,
+                                     int64_t M, const float *bias, float *dst, int64_t ldd) {
+    auto *be = reinterpret_cast<Backend *>(h);
+    auto *w = const_cast<Weight *>(reinterpret_cast<const Weight *>(wh));
+    if (!be || !w || !x || !dst) {
+        set_error("mul_mat_dq16: null argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (reinterpret_cast<uintptr_t>(bias) & 15) {
+        set_error("mul_mat_dq16: bias must be 16-byte aligned");
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (w->type != SAM3B200_TYPE_Q8_0 && w->type != SAM3B200_TYPE_Q4_0) {
+        set_error("mul_mat_dq16: weight type %d is not supported (Q8_0 and Q4_0 only)", w->type);
+        return SAM3B200_STATUS_FAILED;
+    }
+    if (M <= 0 || M > (1 << 24) || ldx < w->K || ldd < w->N || w->K % 32 != 0) {
+        set_error("mul_mat_dq16: bad shape M=%lld ldx=%lld ldd=%lld for K=%d N=%d", (long long)M, (long long)ldx,
+                  (long long)ldd, w->K, w->N);
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(be->device);
+    if (!w->w16) {  // first use: the fp16 copy of the weight, kept with it until sam3b200_weight_free
+        void *p = nullptr;
+        if (!cuda_ok(cudaMalloc(&p, static_cast<size_t>(w->N) * w->K * 2), "cudaMalloc(fp16 weight)"))
+            return SAM3B200_STATUS_ALLOC_FAILED;
+        if (!cuda_ok(dequant_weight_f16(QMatrix{w->codes, w->quads, w->N, w->K, w->ld, weight_nib(w->type)}, p,
+                                        be->stream),
+                     "dequant weight")) {
+            cudaFree(p);
+            return SAM3B200_STATUS_FAILED;
+        }
+        w->w16 = p;
+    }
+    const int Mi = static_cast<int>(M);
+    const int lda = (Mi + MMQ_ROW_ALIGN - 1) / MMQ_ROW_ALIGN * MMQ_ROW_ALIGN;
+    const size_t code_bytes = (static_cast<size_t>(Mi) * w->K + 255) / 256 * 256;
+    if (!be->ensure_scratch(code_bytes + static_cast<size_t>(Mi) * w->K * 2, act_quad_bytes(w->K, lda)))
+        return SAM3B200_STATUS_ALLOC_FAILED;
+    void *a16 = static_cast<char *>(be->act_codes) + code_bytes;
+    MmqArgs a;
+    a.a = QMatrix{be->act_codes, be->act_quads, Mi, w->K, lda};
+    a.b = QMatrix{w->codes, w->quads, w->N, w->K, w->ld, weight_nib(w->type)};
+    a.bias = bias;
+    a.y = dst;
+    a.ldy = ldd;
+    a.dump = nullptr;
+    a.err = be->err;
+    be->count(3);
+    if (!cuda_ok(quantize_rows_q8(x, ldx, Mi, w->K, be->act_codes, be->act_quads, lda, be->stream),
+                 "quantize activations") ||
+        !cuda_ok(dequant_act_f16(be->act_codes, be->act_quads, Mi, w->K, lda, a16, be->stream), "dequant activations"))
+        return SAM3B200_STATUS_FAILED;
+    be->prof_mark(0);
+    const cudaError_t e = mmq_dq16(a, a16, w->w16, MMQ_OUT_F32, be->num_sms, be->stream);
+    be->prof_mark(0);
+    return cuda_ok(e, "mul_mat_dq16 launch") ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
 }

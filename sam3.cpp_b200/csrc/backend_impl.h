@@ -16,6 +16,7 @@ struct Backend {
     int mmq_impl = 0;    // SAM3B200_MMQ_*
     int mmq_cvt = 0;     // MMQ epilogue int->float conversion (tuning: env SAM3B200_MMQ_CVT=0|1)
     int mmq_bn = 0;      // MMQ tile width: 0 = by K (tuning: env SAM3B200_MMQ_BN=64|128)
+    int mmq_arith = 1;   // SAM3B200_ARITH_*: the encoder runners' linear-layer arithmetic (env SAM3B200_ARITH)
     char name[320] = {0};
     // scratch for the quantised activations of the current MUL_MAT
     void *act_codes = nullptr;
@@ -45,6 +46,7 @@ struct Weight {
     void *quads = nullptr;
     void *mins = nullptr;   // Q4_1: block minima as fp16 records [K/32][ld][8] (slot b % 8)
     void *dense = nullptr;  // F16 / F32 weights: fp16 [N][K] for the fp16 tensor-core GEMM
+    void *w16 = nullptr;    // Q8_0 / Q4_0: the blocks dequantised to fp16 [N][K], made by the first mul_mat_dq16
 };
 
 void set_error(const char *fmt, ...);

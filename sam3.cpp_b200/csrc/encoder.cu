@@ -47,6 +47,7 @@ struct Vit {
     std::vector<std::string> missing;
     // activations
     DevBuf img_u8, img_rs, img_f32, a_patch, conv, x, codes_a, quads_a, codes_b, quads_b, q, k, v, rowmap;
+    DevBuf a16, b16;  // DQ16 arithmetic: dequantised A operands, fp16 [T][E] and [T][mlp]
     DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4], out_det[4];
     int out_side[4] = {0, 0, 0, 0};
     int img_cap = 0;  // pixels of img_u8
@@ -68,6 +69,7 @@ static bool alloc_activations(Vit *v) {
               v->quads_a.alloc(act_quad_bytes(E, v->Tpad)) &&
               v->codes_b.alloc(static_cast<size_t>(T) * maxk) &&
               v->quads_b.alloc(act_quad_bytes(static_cast<int>(maxk), v->Tpad)) &&
+              v->a16.alloc(static_cast<size_t>(T) * E * 2) && v->b16.alloc(static_cast<size_t>(T) * hp.mlp * 2) &&
               v->q.alloc(static_cast<size_t>(T) * E * 2) && v->k.alloc(static_cast<size_t>(T) * E * 2) &&
               v->v.alloc(static_cast<size_t>(T) * E * 2) &&
               v->rowmap.alloc(static_cast<size_t>(T) * 4) && v->x16.alloc(static_cast<size_t>(T) * E * 2) &&
@@ -141,6 +143,64 @@ static bool mmq_qkv(Vit *v, const BlockW &w, int win_tokens) {
     return ok;
 }
 
+// DQ16 arithmetic (mmq.cuh): the dequantised A operand a16 [T][K] against the
+// weight's fp16 copy, with the same epilogue modes
+static bool mmq16(Vit *v, const void *a16, const QWeight &w, int mode, const float *bias, float *y, int add,
+                  const int *rowmap, void *out16, int gelu) {
+    MmqArgs a;
+    a.a = QMatrix{nullptr, nullptr, v->T, w.K, v->Tpad};
+    a.b = QMatrix{nullptr, nullptr, w.N, w.K, w.ld, w.nib};
+    a.bias = bias;
+    a.y = y;
+    a.ldy = w.N;
+    a.dump = nullptr;
+    a.err = v->be->err;
+    a.add = add;
+    a.rowmap = rowmap;
+    a.gelu = gelu;
+    a.out16 = out16;
+    v->be->prof_mark(0);
+    const bool ok = launched(v, mmq_dq16(a, a16, w.w16.p, mode, v->be->num_sms, v->be->stream), "mmq dq16");
+    v->be->prof_mark(0);
+    return ok;
+}
+
+static bool mmq16_qkv(Vit *v, const BlockW &w, int win_tokens) {
+    MmqArgs a;
+    a.a = QMatrix{nullptr, nullptr, v->T, w.qkv.K, v->Tpad};
+    a.b = QMatrix{nullptr, nullptr, w.qkv.N, w.qkv.K, w.qkv.ld, w.qkv.nib};
+    a.bias = w.qkv_b.as<float>();
+    a.y = nullptr;
+    a.ldy = 0;
+    a.dump = nullptr;
+    a.err = v->be->err;
+    a.q_out = v->q.p;
+    a.k_out = v->k.p;
+    a.vt_out = v->v.p;
+    a.freqs = w.freqs.p ? w.freqs.as<float>() : nullptr;
+    a.win_tokens = win_tokens;
+    a.heads = v->hp.heads;
+    v->be->prof_mark(0);
+    const bool ok =
+        launched(v, mmq_dq16(a, v->a16.p, w.qkv.w16.p, MMQ_OUT_QKV, v->be->num_sms, v->be->stream), "mmq dq16 qkv");
+    v->be->prof_mark(0);
+    return ok;
+}
+
+// LayerNorm + Q8_0 of the residual stream, written dequantised into a16 (one
+// kernel for the supported widths, else layernorm_q8 and a dequantising pass)
+static bool ln_dq16(Vit *v, const float *x, const DevBuf &w, const DevBuf &b, int win) {
+    const int E = v->hp.embed;
+    cudaStream_t s = v->be->stream;
+    if (E % 256 == 0 && E <= 1536)
+        return launched(v, layernorm_dq16(x, v->T, E, w.as<float>(), b.as<float>(), 1e-5f, v->G, win, v->a16.p, s),
+                        "ln dq16");
+    return launched(v, layernorm_q8(x, v->T, E, w.as<float>(), b.as<float>(), 1e-5f, v->G, win, v->codes_a.p,
+                                    v->quads_a.p, v->Tpad, s),
+                    "ln") &&
+           launched(v, dequant_act_f16(v->codes_a.p, v->quads_a.p, v->T, E, v->Tpad, v->a16.p, s), "dequant_act_f16");
+}
+
 static bool gemm(Vit *v, const void *a, const DevBuf &b, int M, int N, int K, const DevBuf *bias, int gelu,
                  int out_f16, void *out, int store, int win, int cout) {
     GemmF16Args g;
@@ -172,7 +232,32 @@ static bool run_prefix(Vit *v, const float *img_chw, float *x) {
                    "add_pos_layernorm");
 }
 
+// run_block with DQ16 linear layers: the same Q8_0 activations as the exact
+// path (LayerNorm, attention and fc1's GELU epilogue quantise with ggml's
+// rule), each written dequantised as the next fp16 MUL_MAT's operand.
+static bool run_block_dq16(Vit *v, int i, float *x) {
+    const auto &hp = v->hp;
+    const BlockW &w = v->blk[i];
+    cudaStream_t s = v->be->stream;
+    const int E = hp.embed, G = v->G, T = v->T, ws = hp.window;
+    const bool glob = is_global(hp, i);
+    const int B = glob ? 1 : (G / ws) * (G / ws);
+    const int N = glob ? T : ws * ws;
+    AttnOut attn_dq;  // the proj MUL_MAT's operand (window order), written by the attention
+    attn_dq.dq16 = v->a16.p;
+    return ln_dq16(v, x, w.n1w, w.n1b, glob ? 0 : ws) && mmq16_qkv(v, w, N) &&
+           launched(v, flash_attention(v->q.p, v->k.p, v->v.p, B, N, hp.heads,
+                                       1.0f / sqrtf(static_cast<float>(E / hp.heads)), attn_dq, v->be->err, s),
+                    "attention") &&
+           mmq16(v, v->a16.p, w.proj, MMQ_OUT_F32, w.proj_b.as<float>(), x, 1, glob ? nullptr : v->rowmap.as<int>(),
+                 nullptr, 0) &&
+           ln_dq16(v, x, w.n2w, w.n2b, 0) &&
+           mmq16(v, v->a16.p, w.fc1, MMQ_OUT_DQ16, w.fc1_b.as<float>(), nullptr, 0, nullptr, v->b16.p, 1) &&
+           mmq16(v, v->b16.p, w.fc2, MMQ_OUT_F32, w.fc2_b.as<float>(), x, 1, nullptr, nullptr, 0);
+}
+
 static bool run_block(Vit *v, int i, float *x) {
+    if (v->be->mmq_arith == SAM3B200_ARITH_DQ16) return run_block_dq16(v, i, x);
     const auto &hp = v->hp;
     const BlockW &w = v->blk[i];
     cudaStream_t s = v->be->stream;
@@ -421,7 +506,8 @@ int sam3b200_vit_set_tensor(sam3b200_vit *hv, const char *name_c, int type, cons
                           (long long)eK, (long long)eN);
                 return SAM3B200_STATUS_FAILED;
             }
-            return upload_qweight(v->be, *qw, type, data, K, NN) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+            return upload_qweight(v->be, *qw, type, data, K, NN) && make_w16(v->be, *qw) ? SAM3B200_STATUS_SUCCESS
+                                                                                         : SAM3B200_STATUS_FAILED;
         }
         set_error("%s: unknown block tensor", name_c);
         return SAM3B200_STATUS_FAILED;

@@ -244,6 +244,7 @@ struct Hiera {
     std::vector<std::string> missing;
     // activations
     DevBuf xa, xb, normed, shortf, shortp, qkv, qp, attn, proj, codes_a, quads_a, codes_b, quads_b;
+    DevBuf a16, b16;  // DQ16 arithmetic: codes_a / codes_b dequantised to fp16
     DevBuf stage_out[4], fpn_out[4], x16;
     DevBuf tq, tk, tvt;          // attention operands for the tensor cores (attn_tcw): fp16 q, k, v^T
     DevBuf xwin, hid;            // blocks with F16 / F32 linear layers: f32 windowed rows, MLP hidden rows
@@ -281,6 +282,15 @@ bool h_mmq(Hiera *h, const void *codes, const void *quads, int M, const QWeight 
     a.out_codes = oc;
     a.out_quads = oq;
     a.out_ld = ld;
+    if (h->be->mmq_arith == SAM3B200_ARITH_DQ16 && w.w16.p) {
+        // DQ16 arithmetic (mmq.cuh): the same Q8_0 codes, dequantised, on the fp16 tensor cores
+        void *a16 = codes == h->codes_b.p ? h->b16.p : h->a16.p;
+        if (!hlaunched(h, dequant_act_f16(codes, quads, M, w.K, ld, a16, h->be->stream), "hiera dequant")) return false;
+        h->be->prof_mark(0);
+        const bool ok = hlaunched(h, mmq_dq16(a, a16, w.w16.p, mode, h->be->num_sms, h->be->stream), "hiera mmq dq16");
+        h->be->prof_mark(0);
+        return ok;
+    }
     h->be->prof_mark(0);
     const bool ok = hlaunched(h, mmq_tc(a, mode, h->be->num_sms, h->be->stream, h->be->mmq_cvt, h->be->mmq_bn), "hiera mmq");
     h->be->prof_mark(0);
@@ -434,7 +444,8 @@ bool alloc_hiera(Hiera *h) {
               h->xb.alloc(mx_x * 4) && h->normed.alloc(mx_norm * 4) && h->shortf.alloc(mx_sf * 4) &&
               h->shortp.alloc(mx_sp * 4) && h->qkv.alloc(mx_qkv * 4) && h->qp.alloc(mx_qp * 4) &&
               h->attn.alloc(mx_qp * 4) && h->proj.alloc(mx_qp * 4) && h->codes_a.alloc(mx_codes_a) &&
-              h->quads_a.alloc(mx_quads_a) && h->codes_b.alloc(mx_codes_b) && h->quads_b.alloc(mx_quads_b);
+              h->quads_a.alloc(mx_quads_a) && h->codes_b.alloc(mx_codes_b) && h->quads_b.alloc(mx_quads_b) &&
+              h->a16.alloc(mx_codes_a * 2) && h->b16.alloc(mx_codes_b * 2);
     size_t mx16 = 0;
     for (int s = 0; s < 4 && ok; ++s) {
         const size_t T = static_cast<size_t>(h->stage_side[s]) * h->stage_side[s];
@@ -843,7 +854,8 @@ int sam3b200_hiera_set_tensor(sam3b200_hiera *hh, const char *name_c, int type, 
                 sam3b200_weight_free(reinterpret_cast<sam3b200_backend *>(h->be), w->dense);
                 w->dense = nullptr;
             }
-            return upload_qweight(h->be, w->q, type, data, K, N) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+            return upload_qweight(h->be, w->q, type, data, K, N) && make_w16(h->be, w->q) ? SAM3B200_STATUS_SUCCESS
+                                                                                          : SAM3B200_STATUS_FAILED;
         }
     }
     set_error("hiera: unknown tensor %s", name_c);

@@ -274,6 +274,7 @@ struct MmqEpi {
     __nv_bfloat16 *q, *k, *vt;
     const float *freqs;
     int win_tokens, heads;
+    __half *o16;  // MMQ_OUT_DQ16
 };
 
 __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
@@ -361,8 +362,8 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
                 for (int i = 0; i < COLS; ++i) dst[static_cast<int64_t>(i) * ep.win_tokens] = __float2bfloat16_rn(acc[i]);
             }
         }
-    } else if constexpr (MODE == MMQ_OUT_Q8) {
-        // this thread's 64 columns are two whole 32-wide Q8_0 blocks of the output row
+    } else if constexpr (MODE == MMQ_OUT_Q8 || MODE == MMQ_OUT_DQ16) {
+        // this thread's COLS columns are whole 32-wide Q8_0 blocks of the output row
         if (m < M) {
 #pragma unroll
             for (int hb = 0; hb < COLS; hb += 32) {
@@ -378,17 +379,35 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
                 }
                 const float d = __fdiv_rn(amax, 127.f);
                 const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-                uint32_t pk[8];
+                if constexpr (MODE == MMQ_OUT_DQ16) {
+                    // the block's codes times its stored (fp16) scale, rounded once to fp16
+                    const float dh = __half2float(__float2half_rn(d));
+                    uint4 *dst = reinterpret_cast<uint4 *>(ep.o16 + static_cast<int64_t>(m) * N + nb + hb);
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    pk[i] = pack4_i8(__float2int_rn(__fmul_rn(acc[hb + 4 * i], id)),
-                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 1], id)),
-                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 2], id)),
-                                     __float2int_rn(__fmul_rn(acc[hb + 4 * i + 3], id)));
-                uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
-                dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                store_act_scale(ep.qquads, (nb + hb) >> 5, m, ep.qld, N >> 5, d);
+                    for (int i = 0; i < 32; i += 8) {
+                        uint32_t hw[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float q0 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + i + 2 * e], id)));
+                            const float q1 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + i + 2 * e + 1], id)));
+                            const __half2 h2 = __floats2half2_rn(__fmul_rn(q0, dh), __fmul_rn(q1, dh));
+                            hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                        dst[i >> 3] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    }
+                } else {
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        pk[i] = pack4_i8(__float2int_rn(__fmul_rn(acc[hb + 4 * i], id)),
+                                         __float2int_rn(__fmul_rn(acc[hb + 4 * i + 1], id)),
+                                         __float2int_rn(__fmul_rn(acc[hb + 4 * i + 2], id)),
+                                         __float2int_rn(__fmul_rn(acc[hb + 4 * i + 3], id)));
+                    uint4 *dst = reinterpret_cast<uint4 *>(ep.qcodes + static_cast<int64_t>(m) * N + nb + hb);
+                    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    store_act_scale(ep.qquads, (nb + hb) >> 5, m, ep.qld, N >> 5, d);
+                }
             }
         }
     }
@@ -930,6 +949,331 @@ cudaError_t mmq_simt(const MmqArgs &a, int mode, cudaStream_t s) {
                                          a.dump, mode, static_cast<const __half *>(a.b_mins),
                                          static_cast<const __half *>(a.a_sums), a.b.nib);
     return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// DQ16 arithmetic (mmq.cuh): Q8_0 / Q4_0 operands dequantised to fp16 and one
+// kind::f16 MMA pass over the whole of K per tile.
+// ---------------------------------------------------------------------------
+__global__ void dequant_act_f16_kernel(const int8_t *__restrict__ codes, const __half *__restrict__ quads, int M, int K,
+                                       int ld, __half *__restrict__ out) {
+    const int kg = K >> 3;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 8-element group
+    if (i >= static_cast<int64_t>(M) * kg) return;
+    const int m = static_cast<int>(i / kg), k = static_cast<int>(i % kg) * 8;
+    const uint2 c = *reinterpret_cast<const uint2 *>(codes + static_cast<int64_t>(m) * K + k);
+    const float d = __half2float(quads[act_quad_index(k >> 5, m, ld)]);
+    uint32_t hw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint32_t word = e < 2 ? c.x : c.y;
+        const int sh = (e & 1) * 16;
+        const float q0 = static_cast<float>(static_cast<int8_t>((word >> sh) & 0xFFu));
+        const float q1 = static_cast<float>(static_cast<int8_t>((word >> (sh + 8)) & 0xFFu));
+        const __half2 h2 = __floats2half2_rn(__fmul_rn(q0, d), __fmul_rn(q1, d));
+        hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+    }
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(m) * K + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+cudaError_t dequant_act_f16(const void *codes, const void *quads, int M, int K, int ld, void *out, cudaStream_t s) {
+    if (M <= 0 || K <= 0 || K % 32 != 0 || ld < M) return cudaErrorInvalidValue;
+    const int64_t groups = static_cast<int64_t>(M) * (K >> 3);
+    dequant_act_f16_kernel<<<static_cast<unsigned>((groups + 255) / 256), 256, 0, s>>>(
+        static_cast<const int8_t *>(codes), static_cast<const __half *>(quads), M, K, ld, static_cast<__half *>(out));
+    return cudaGetLastError();
+}
+
+template <int NIB>
+__global__ void dequant_weight_f16_kernel(const uint8_t *__restrict__ codes, const __half *__restrict__ quads, int N,
+                                          int K, int ld, __half *__restrict__ out) {
+    const int kg = K >> 3;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(N) * kg) return;
+    const int n = static_cast<int>(i / kg), k = static_cast<int>(i % kg) * 8, b = k >> 5;
+    const float d = __half2float(quads[(static_cast<int64_t>(b) * ld + n) * 8 + (b & 7)]);
+    int q[8];
+    if constexpr (NIB == 0) {
+        const uint2 c = *reinterpret_cast<const uint2 *>(codes + static_cast<int64_t>(n) * K + k);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = static_cast<int8_t>(((e < 4 ? c.x : c.y) >> (8 * (e & 3))) & 0xFFu);
+    } else {
+        // Q4_0 block bytes: byte j holds element j (low nibble) and j + 16 (high nibble); code = nibble - 8
+        const int j0 = k & 31;
+        const uint2 c = *reinterpret_cast<const uint2 *>(codes + static_cast<int64_t>(n) * (K / 2) + b * 16 + (j0 & 15));
+        const int sh = j0 < 16 ? 0 : 4;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            q[e] = static_cast<int>((((e < 4 ? c.x : c.y) >> (8 * (e & 3) + sh)) & 0xFu)) - 8;
+    }
+    uint32_t hw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __half2 h2 = __floats2half2_rn(__fmul_rn(static_cast<float>(q[2 * e]), d),
+                                             __fmul_rn(static_cast<float>(q[2 * e + 1]), d));
+        hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+    }
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(n) * K + k) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+}
+
+cudaError_t dequant_weight_f16(const QMatrix &w, void *out, cudaStream_t s) {
+    if (w.rows <= 0 || w.K <= 0 || w.K % 32 != 0 || w.ld < w.rows || (w.nib != 0 && w.nib != 1))
+        return cudaErrorInvalidValue;
+    const int64_t groups = static_cast<int64_t>(w.rows) * (w.K >> 3);
+    const unsigned grid = static_cast<unsigned>((groups + 255) / 256);
+    auto kern = w.nib == 1 ? dequant_weight_f16_kernel<1> : dequant_weight_f16_kernel<0>;
+    kern<<<grid, 256, 0, s>>>(static_cast<const uint8_t *>(w.codes), static_cast<const __half *>(w.quads), w.rows, w.K,
+                              w.ld, static_cast<__half *>(out));
+    return cudaGetLastError();
+}
+
+// CTA tile 128 tokens x BN features, persistent over tiles, 576 threads:
+//   warp 0      : TMA producer (one elected lane): 64-wide K stages of A
+//                 (128 rows) and B (BN rows), 128-byte swizzle;
+//   warp 1      : TMEM allocator + MMA issuer (one elected lane): four K = 16
+//                 MMAs per stage into accumulator buffer (tile & 1), BN
+//                 columns each, so a tile's epilogue overlaps the next
+//                 tile's MMAs;
+//   warps 2..17 : epilogue, four per TMEM lane quarter (warp w reads lane
+//                 quarter w % 4, column slice (w - 2) / 4 of BN / 4 columns),
+//                 then the mode's tile_store (bias, residual through the row
+//                 map, RoPE + head split, GELU + Q8_0 re-quantisation).
+template <int BN_>
+struct DqCfg {
+    static constexpr int BM = 128, BN = BN_, BK = 64;
+    static constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    static constexpr int EPI_WARPS = 16;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int COLS = BN / 4;  // output columns per epilogue thread
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+    static_assert(COLS % 32 == 0 && COLS <= 64, "whole 32-column TMEM loads, inside one 64-wide head");
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <int MODE, int BN>
+__global__ void __launch_bounds__(DqCfg<BN>::THREADS, 1)
+    mmq_dq16_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, int M, int N,
+                    int K, const MmqEpi ep, int *__restrict__ err) {
+    using C = DqCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + C::STAGES;
+    uint64_t *tfull = empty + C::STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_m = (M + C::BM - 1) / C::BM, num_n = (N + C::BN - 1) / C::BN;
+    const int num_tiles = num_m * num_n;
+    const int kstages = (K + C::BK - 1) / C::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], C::EPI_WARPS);
+        }
+        fence_mbar_init();
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, err, ERR_WAIT_EMPTY))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *sb = smem + stage * C::STAGE_BYTES;
+                if (elect_one()) {
+                    mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+                    tma_load_2d(sb, &tm_a, &full[stage], ks * C::BK, m0);
+                    tma_load_2d(sb + C::A_BYTES, &tm_b, &full[stage], ks * C::BK, n0);
+                }
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        constexpr uint32_t idesc = idesc_f16_f32(C::BM, C::BN);
+        int stage = 0;
+        uint32_t phase = 0, it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+            const uint32_t buf = it & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tempty[buf], ((it >> 1) & 1u) ^ 1u, err, ERR_WAIT_TEMPTY))) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + buf * C::BN;
+            for (int ks = 0; ks < kstages; ++ks) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, err, ERR_WAIT_FULL_MMA))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+                const uint32_t b_addr = a_addr + C::A_BYTES;
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16(d_tmem, sw128_kmajor_desc(a_addr + kk * 32), sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                                (ks | kk) != 0);
+                    mma_commit(&empty[stage]);
+                }
+                __syncwarp();
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&tfull[buf]);
+            __syncwarp();
+        }
+    } else {
+        const int q = warp & 3;
+        const int cs = ((warp - 2) >> 2) * C::COLS;
+        const int row = q * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+            const uint32_t buf = it & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (it >> 1) & 1u, err, ERR_WAIT_TFULL))) break;
+            tc_fence_after();
+            const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
+            uint32_t v[C::COLS];
+#pragma unroll
+            for (int c = 0; c < C::COLS; c += 32)
+                tmem_ld_32x32b_x32(tmem_base + lane_addr + buf * C::BN + cs + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            float acc[C::COLS];
+#pragma unroll
+            for (int i = 0; i < C::COLS; ++i) acc[i] = __uint_as_float(v[i]);
+            tile_store<MODE, C::COLS>(ep, acc, m0 + row, M, N, n0 + cs);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+static MmqEpi dq16_epi(const MmqArgs &a) {
+    MmqEpi ep;
+    ep.bias = a.bias;
+    ep.y = a.y;
+    ep.ldy = a.ldy;
+    ep.dump = nullptr;
+    ep.add = a.add;
+    ep.rowmap = a.rowmap;
+    ep.gelu = a.gelu;
+    ep.qcodes = static_cast<int8_t *>(a.out_codes);
+    ep.qquads = static_cast<__half *>(a.out_quads);
+    ep.qld = a.out_ld;
+    ep.q = static_cast<__nv_bfloat16 *>(a.q_out);
+    ep.k = static_cast<__nv_bfloat16 *>(a.k_out);
+    ep.vt = static_cast<__nv_bfloat16 *>(a.vt_out);
+    ep.freqs = a.freqs;
+    ep.win_tokens = a.win_tokens;
+    ep.heads = a.heads;
+    ep.o16 = static_cast<__half *>(a.out16);
+    return ep;
+}
+
+template <int MODE, int BN>
+static cudaError_t launch_dq16(const MmqArgs &a, const void *a16, const void *b16, int num_sms, cudaStream_t s) {
+    using C = DqCfg<BN>;
+    const int M = a.a.rows, N = a.b.rows, K = a.a.K;
+    CUtensorMap ta, tb;
+    const uint64_t da[2] = {uint64_t(K), uint64_t(M)}, db[2] = {uint64_t(K), uint64_t(N)};
+    const uint64_t st[1] = {uint64_t(K) * 2};
+    const uint32_t bxa[2] = {C::BK, C::BM}, bxb[2] = {C::BK, C::BN};
+    if (!make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a16, 2, da, st, bxa, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, 2, db, st, bxb, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    auto kern = mmq_dq16_kernel<MODE, BN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ta, tb, M, N, K, dq16_epi(a), a.err);
+    return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t dispatch_dq16(const MmqArgs &a, const void *a16, const void *b16, int mode, int num_sms,
+                                 cudaStream_t s) {
+    if (mode == MMQ_OUT_F32) return launch_dq16<MMQ_OUT_F32, BN>(a, a16, b16, num_sms, s);
+    if (mode == MMQ_OUT_DQ16) {
+        if (a.b.rows % 32 != 0 || !a.out16) return cudaErrorInvalidValue;
+        return launch_dq16<MMQ_OUT_DQ16, BN>(a, a16, b16, num_sms, s);
+    }
+    if (mode == MMQ_OUT_Q8) {
+        if (a.b.rows % 32 != 0 || !a.out_codes || !a.out_quads || a.out_ld < a.a.rows) return cudaErrorInvalidValue;
+        return launch_dq16<MMQ_OUT_Q8, BN>(a, a16, b16, num_sms, s);
+    }
+    if (mode == MMQ_OUT_QKV) {
+        if (!a.q_out || !a.k_out || !a.vt_out || a.heads <= 0 || a.b.rows != 3 * 64 * a.heads ||
+            a.win_tokens <= 0 || a.a.rows % a.win_tokens != 0)
+            return cudaErrorInvalidValue;
+        return launch_dq16<MMQ_OUT_QKV, BN>(a, a16, b16, num_sms, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+// Tile width from the tile count: persistent CTAs take ceil(tiles / SMs)
+// tiles each, and a BN-wide tile costs about BN + 64 columns' worth of time
+// (the fixed part: its epilogue handshake and pipeline fill).
+static int dq16_pick_bn(int M, int N, int num_sms) {
+    static const int forced = [] {
+        const char *ev = getenv("SAM3B200_DQ16_BN");
+        return ev ? atoi(ev) : 0;
+    }();
+    if (forced == 128 || forced == 256) return forced;
+    auto cost = [&](int bn) {
+        const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + bn - 1) / bn);
+        return ((tiles + num_sms - 1) / num_sms) * (bn + 64);
+    };
+    return cost(256) <= cost(128) ? 256 : 128;
+}
+
+cudaError_t mmq_dq16(const MmqArgs &a, const void *a16, const void *b16, int mode, int num_sms, cudaStream_t s,
+                     int bn) {
+    const int M = a.a.rows, N = a.b.rows, K = a.a.K;
+    if (!a16 || !b16 || M <= 0 || N <= 0 || K <= 0 || K % 8 != 0 || K != a.b.K || num_sms <= 0 ||
+        (reinterpret_cast<uintptr_t>(a16) & 15) || (reinterpret_cast<uintptr_t>(b16) & 15))
+        return cudaErrorInvalidValue;
+    if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return cudaErrorInvalidValue;
+    if (bn == 0) bn = dq16_pick_bn(M, N, num_sms);
+    if (bn == 128) return dispatch_dq16<128>(a, a16, b16, mode, num_sms, s);
+    if (bn == 256) return dispatch_dq16<256>(a, a16, b16, mode, num_sms, s);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace b200

@@ -32,6 +32,9 @@ enum MmqOut : int {
                            // N = 3E columns (q | k | v thirds, 64-wide heads), RoPE on the q and k
                            // thirds (sam3.cpp:3671-3710), written as bf16 Q, K [win*heads][tokens][64]
                            // and V^T [win*heads][64][tokens]; row m = window * win_tokens + token
+    MMQ_OUT_DQ16 = 4,      // v = acc + bias (GELU if gelu), quantised to Q8_0 exactly as MMQ_OUT_Q8 and
+                           // written dequantised, fp16(q * fp16(d)), into out16 [M, N] (the A operand of
+                           // the next mmq_dq16)
 };
 
 constexpr int MMQ_ROW_ALIGN = 128;
@@ -94,6 +97,7 @@ struct MmqArgs {
     int heads = 0;                  // MMQ_OUT_QKV: heads (N = 3 * 64 * heads)
     const void *b_mins = nullptr;   // Q4_1 weights: m_w records, fp16 [K/32][ld][8] (m_w in slot b % 8)
     const void *a_sums = nullptr;   // Q4_1 weights: Q8_1 sum fields of the activations (act_quad_index layout)
+    void *out16 = nullptr;          // MMQ_OUT_DQ16: fp16 [M, N]
 };
 
 // Quantise f32 rows (ggml-cpu x86 activation rule) into the device layout.
@@ -124,5 +128,26 @@ cudaError_t mmq_tc(const MmqArgs &args, int mode, int num_sms, cudaStream_t s, i
 
 // Straight SIMT version of the same arithmetic (small M, cross-checks).
 cudaError_t mmq_simt(const MmqArgs &args, int mode, cudaStream_t s);
+
+// ---- DQ16 arithmetic ------------------------------------------------------
+// The same Q8_0 activation codes and scales (ggml's quantiser) and the same
+// weight blocks, each element dequantised to fp16 -- fp16(q * d), one
+// rounding of an exact product, relative error <= 2^-11 -- and multiplied on
+// the fp16 tensor cores with fp32 accumulation over the whole of K.  The sum
+// differs from the exact block-ordered fold by rounding only (about 1e-4
+// normwise), and one MMA pass over K replaces the per-block int32 -> fp32
+// fold on the CUDA cores.
+
+// Dequantise an activation QMatrix (codes + A-side records, `ld` rows per
+// record group) into fp16 [M][K].
+cudaError_t dequant_act_f16(const void *codes, const void *quads, int M, int K, int ld, void *out, cudaStream_t s);
+// Dequantise a Q8_0 (nib 0) or Q4_0 (nib 1) weight QMatrix into fp16 [N][K].
+cudaError_t dequant_weight_f16(const QMatrix &w, void *out, cudaStream_t s);
+// y = a16 . b16^T with the epilogues of mmq_tc (MMQ_OUT_F32, MMQ_OUT_QKV,
+// MMQ_OUT_Q8, MMQ_OUT_DQ16): a16 fp16 [M][K], b16 fp16 [N][K], M = args.a.rows,
+// N = args.b.rows, K = args.a.K (a multiple of 64).  bn: 128 or 256 (tile
+// width), 0 = chosen from the tile count.
+cudaError_t mmq_dq16(const MmqArgs &args, const void *a16, const void *b16, int mode, int num_sms, cudaStream_t s,
+                     int bn = 0);
 
 }  // namespace b200

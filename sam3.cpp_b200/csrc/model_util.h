@@ -44,6 +44,7 @@ struct DevBuf {
 
 struct QWeight {  // a repacked linear weight (see mmq.cuh)
     DevBuf codes, quads;
+    DevBuf w16;  // the same blocks dequantised to fp16 [N][K] (DQ16 arithmetic), when the runner uses it
     int K = 0, N = 0, ld = 0;
     int nib = 0;  // QMatrix::nib of the codes (0 Q8_0, 1 Q4_0)
     bool set = false;
@@ -109,6 +110,14 @@ inline bool upload_qweight(Backend *be, QWeight &w, int type, const void *data, 
     raw.release();
     w.set = ok;
     return ok;
+}
+
+// The fp16 dequantised copy of an uploaded weight (mmq.cuh, DQ16 arithmetic).
+inline bool make_w16(Backend *be, QWeight &w) {
+    return w.set && w.w16.alloc(static_cast<size_t>(w.N) * w.K * 2) &&
+           cuda_ok(dequant_weight_f16(QMatrix{w.codes.p, w.quads.p, w.N, w.K, w.ld, w.nib}, w.w16.p, be->stream),
+                   "dequant weight") &&
+           cuda_ok(cudaStreamSynchronize(be->stream), "dequant sync");
 }
 
 // Upload rows [r0, r0 + rows) of a ggml [K, N] weight as a weight of its own

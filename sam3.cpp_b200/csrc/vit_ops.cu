@@ -253,11 +253,13 @@ struct LnMinBlocks {
     static constexpr int value = NJ <= 4 || NJ == 8 ? 9 : NJ <= 6 ? 8 : 4;
 };
 
-template <int NJ>
+// DQ: write the row's Q8_0 blocks dequantised, fp16(q * fp16(d)), into o16
+// [rows][E] (the A operand of mmq_dq16) instead of codes + scale records.
+template <int NJ, bool DQ = false>
 __global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
     ln_q8_coal_kernel(const float *__restrict__ x, int rows, const float *__restrict__ w,
                                   const float *__restrict__ b, float eps, int G, int win, int8_t *__restrict__ codes,
-                                  __half *__restrict__ quads, int ld) {
+                                  __half *__restrict__ quads, int ld, __half *__restrict__ o16 = nullptr) {
     constexpr int E = NJ * 128;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -304,14 +306,47 @@ __global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
         const float d = __fdiv_rn(amax, 127.f);
         const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-        *reinterpret_cast<uint32_t *>(cr + 128 * j) =
-            pack4(__float2int_rn(__fmul_rn(y0, id)), __float2int_rn(__fmul_rn(y1, id)),
-                  __float2int_rn(__fmul_rn(y2, id)), __float2int_rn(__fmul_rn(y3, id)));
-        if ((lane & 7) == 0) {
-            const int blk = 4 * j + (lane >> 3);
-            store_act_scale(quads, blk, r, ld, E >> 5, d);
+        if constexpr (DQ) {
+            const float dh = __half2float(__float2half_rn(d));
+            const __half2 h01 = __floats2half2_rn(__fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y0, id))), dh),
+                                                  __fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y1, id))), dh));
+            const __half2 h23 = __floats2half2_rn(__fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y2, id))), dh),
+                                                  __fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y3, id))), dh));
+            *reinterpret_cast<uint2 *>(o16 + static_cast<int64_t>(r) * E + 128 * j + 4 * lane) =
+                make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
+        } else {
+            *reinterpret_cast<uint32_t *>(cr + 128 * j) =
+                pack4(__float2int_rn(__fmul_rn(y0, id)), __float2int_rn(__fmul_rn(y1, id)),
+                      __float2int_rn(__fmul_rn(y2, id)), __float2int_rn(__fmul_rn(y3, id)));
+            if ((lane & 7) == 0) {
+                const int blk = 4 * j + (lane >> 3);
+                store_act_scale(quads, blk, r, ld, E >> 5, d);
+            }
         }
     }
+}
+
+template <int NJ>
+static void launch_ln_dq16(const float *x, int rows, const float *w, const float *b, float eps, int G, int win,
+                           void *out16, cudaStream_t s) {
+    ln_q8_coal_kernel<NJ, true><<<grid_for(rows, 4), 128, 0, s>>>(x, rows, w, b, eps, G, win, nullptr, nullptr, 0,
+                                                                   static_cast<__half *>(out16));
+}
+
+cudaError_t layernorm_dq16(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
+                           void *out16, cudaStream_t s) {
+    if (rows <= 0 || (reinterpret_cast<uintptr_t>(out16) & 15) || (win > 0 && (G % win != 0 || rows != G * G)))
+        return cudaErrorInvalidValue;
+    switch (E) {
+    case 256: launch_ln_dq16<2>(x, rows, w, b, eps, G, win, out16, s); break;
+    case 512: launch_ln_dq16<4>(x, rows, w, b, eps, G, win, out16, s); break;
+    case 768: launch_ln_dq16<6>(x, rows, w, b, eps, G, win, out16, s); break;
+    case 1024: launch_ln_dq16<8>(x, rows, w, b, eps, G, win, out16, s); break;
+    case 1280: launch_ln_dq16<10>(x, rows, w, b, eps, G, win, out16, s); break;
+    case 1536: launch_ln_dq16<12>(x, rows, w, b, eps, G, win, out16, s); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
 }
 
 template <int NJ>

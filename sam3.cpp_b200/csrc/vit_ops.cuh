@@ -32,6 +32,12 @@ cudaError_t add_pos_layernorm(const float *conv, const float *pos, int g, int G,
 // ggml_win_part position (window-major, sam3.cpp:3734).
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s);
+// layernorm_q8's LayerNorm and Q8_0 quantisation (same codes and scales),
+// written dequantised -- fp16(q * fp16(d)) [rows][E] in the same row order --
+// as the A operand of mmq_dq16.  E in {256, 512, 768, 1024, 1280, 1536};
+// cudaErrorInvalidValue otherwise.
+cudaError_t layernorm_dq16(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
+                           void *out16, cudaStream_t s);
 
 // Attention inputs from ggml f32 tensors Q, K, V [64, N, H, B] (contiguous:
 // [BH][N][64]) -> bf16 Q, K (same layout) and V^T [BH][64][N].  N % 8 == 0.

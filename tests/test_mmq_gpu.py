@@ -165,3 +165,35 @@ def test_dense_weights_within_bound(oracle, b200, backend, qt, M, K, N):
     err = np.abs(got[rows] - ref).max() / np.abs(ref).max()
     assert err <= 1e-2, err
     wt.free()
+
+
+@pytest.mark.parametrize("qt", [8, 2])
+@pytest.mark.parametrize("M,K,N", [(5184, 1024, 3072), (5184, 1024, 1024), (5184, 1024, 4736), (5184, 4736, 1024),
+                                   (300, 96, 288), (77, 1024, 520), (1, 64, 32)])
+def test_mul_mat_dq16_against_oracle(oracle, b200, backend, qt, M, K, N):
+    """sam3b200_mul_mat_dq16: the same Q8_0 activation codes and weight blocks, each element dequantised to
+    fp16 and multiplied on the fp16 tensor cores with fp32 accumulation over K.  Against the oracle's exact
+    block-ordered sum it differs by rounding only: held to 1e-3 (max|d| / max|ref|, ten times inside the
+    north-star 1e-2), on a sample of rows spread over every 128-row tile including the ragged last one."""
+    wq, x, bias = _case(oracle, qt, M, K, N, seed=M + 5 * K + N)
+    w = backend.weight(qt, wq, K, N)
+    xd, bd = backend.upload(x), backend.upload(bias)
+    yd = backend.alloc(M * N * 4)
+    for _ in range(2):  # the second call reuses the weight's fp16 copy made by the first
+        backend.mul_mat_dq16(w, xd, M, yd, bias=bd)
+        backend.synchronize()
+    got = yd.get((M, N), np.float32)
+    rows = np.unique(np.clip(np.concatenate([np.arange(0, M, 97), [M - 1, M - 64, 5120, 127, 128]]), 0, M - 1))
+    ref = oracle.mul_mat(qt, wq, K, N, x[rows]) + bias[None, :]
+    err = np.max(np.abs(got[rows] - ref)) / np.max(np.abs(ref))
+    assert err <= 1e-3, err
+    w.free()
+
+
+def test_mul_mat_dq16_refuses_other_weight_types(b200, backend):
+    K, N, M = 64, 32, 8
+    w = backend.weight(b200.TYPE_F16, np.zeros((N, K), np.float16).view(np.uint8), K, N)
+    x, y = backend.alloc(M * K * 4), backend.alloc(M * N * 4)
+    with pytest.raises(b200.B200Error, match="not supported"):
+        backend.mul_mat_dq16(w, x, M, y)
+    w.free()

@@ -13,6 +13,16 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 
+@pytest.fixture(params=["dq16", "exact"])
+def arith(request, b200, backend):
+    """The encoder's linear-layer arithmetic (sam3b200_set_arith): DQ16 (the
+    default: Q8_0 codes dequantised to fp16, fp16 tensor cores) and EXACT
+    (int8 block dots, block-ordered fp32 fold); both at the same bound."""
+    prev = backend.set_arith(b200.ARITH_DQ16 if request.param == "dq16" else b200.ARITH_EXACT)
+    yield request.param
+    backend.set_arith(prev)
+
+
 @pytest.fixture(scope="module")
 def small(model, oracle, backend):
     hp = model.SAM3_VIT_TEST
@@ -72,7 +82,7 @@ def small_q4(model, oracle, backend):
 
 
 @pytest.mark.parametrize("idx", [0, 1])
-def test_block_q4_0(backend, small_q4, idx):
+def test_block_q4_0(backend, small_q4, idx, arith):
     hp, _, vit, ov = small_q4
     x = np.random.default_rng(20 + idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
     ref = ov.block(idx, x)
@@ -84,7 +94,7 @@ def test_block_q4_0(backend, small_q4, idx):
 
 
 @pytest.mark.parametrize("idx", [0, 1])  # block 0 windowed, block 1 global
-def test_block(backend, small, idx):
+def test_block(backend, small, idx, arith):
     hp, _, vit, ov = small
     x = np.random.default_rng(idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
     ref = ov.block(idx, x)
@@ -105,7 +115,7 @@ def test_neck(backend, small):
         assert err <= TOL, (i, err)
 
 
-def test_encode_end_to_end(small):
+def test_encode_end_to_end(small, arith):
     hp, _, vit, ov = small
     rgb = np.random.default_rng(5).integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8)
     x_ref, outs_ref = ov.encode(rgb)
@@ -138,7 +148,7 @@ def full8(model, oracle, backend):
 
 
 @pytest.mark.parametrize("idx", [0, 7])
-def test_full_size_block(backend, full8, idx):
+def test_full_size_block(backend, full8, idx, arith):
     hp, vit, ov = full8
     x = np.random.default_rng(idx).standard_normal((ov.G ** 2, hp["embed"]), dtype=np.float32)
     ref = ov.block(idx, x)
@@ -162,7 +172,7 @@ def full32(model, oracle, backend):
     vit.free()
 
 
-def test_full_size_every_stage_on_the_gpu_trajectory(backend, full32):
+def test_full_size_every_stage_on_the_gpu_trajectory(backend, full32, arith):
     """sam3_encode_image (sam3.cpp:6028-6216) at config 3, stage by stage along
     the GPU's own trajectory, at the fixed 1e-2 bound: the prefix on the
     preprocessed image, then each of the 32 blocks on the residual stream the
