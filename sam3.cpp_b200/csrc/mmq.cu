@@ -1027,6 +1027,186 @@ cudaError_t dequant_weight_f16(const QMatrix &w, void *out, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---- warp-staged row segments (the DQ16 epilogue's stores) -----------------
+// Every epilogue lane owns one output row (its TMEM lane), so a per-lane
+// store touches 32 cache lines per instruction, and the L1 replays it 32
+// times.  Instead each lane puts a 64-byte segment of its row into a per-warp
+// 2 KB staging buffer -- 16-byte chunks XOR-swizzled by (row >> 1) & 3, which
+// keeps both the row-per-lane writes and the 8-rows-per-instruction reads
+// free of bank conflicts -- and the warp writes 8 rows x 64 bytes per
+// instruction.  Row mappings (window order, head split) are per row, so any
+// destination layout with 16-byte-aligned row segments works.
+__device__ __forceinline__ int stage_idx(int row, int chunk) { return row * 4 + (chunk ^ ((row >> 1) & 3)); }
+
+__device__ __forceinline__ void stage_put(uint4 *st, int lane, const uint4 (&seg)[4]) {
+    __syncwarp();  // the previous round's reads are done
+#pragma unroll
+    for (int c = 0; c < 4; ++c) st[stage_idx(lane, c)] = seg[c];
+    __syncwarp();
+}
+
+__device__ __forceinline__ uint32_t f2_bits(float a) { return __float_as_uint(a); }
+__device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&p);
+}
+
+// tile_store of the DQ16 kernel for MODE F32 / DQ16 / QKV, warp-collective
+// (every lane of the warp calls it, rows m >= M included); m = this lane's tile
+// row, the warp's rows are m - lane .. m - lane + 31.  Same arithmetic as
+// tile_store, only the memory access pattern differs.
+template <int MODE, int COLS>
+__device__ __forceinline__ void tile_store_staged(const MmqEpi &ep, float (&acc)[COLS], int m, int M, int N, int nb,
+                                                  uint4 *st, int lane) {
+    constexpr unsigned FULL = 0xffffffffu;
+    const float *__restrict__ bias = ep.bias;
+    const int m_warp = m - lane;
+    if constexpr (MODE == MMQ_OUT_F32) {
+        const bool vec = ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0) && ((N & 3) == 0);
+        if (!vec) {  // warp-uniform: the per-lane path handles any stride / width
+            tile_store<MODE, COLS>(ep, acc, m, M, N, nb);
+            return;
+        }
+        if (bias) {
+#pragma unroll
+            for (int i = 0; i < COLS; ++i)
+                if (nb + i < N) acc[i] = __fadd_rn(acc[i], bias[nb + i]);
+        }
+        const int myrow = m < M ? (ep.rowmap ? ep.rowmap[m] : m) : -1;
+#pragma unroll
+        for (int c0 = 0; c0 < COLS; c0 += 16) {
+            uint4 seg[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                seg[k] = make_uint4(f2_bits(acc[c0 + 4 * k]), f2_bits(acc[c0 + 4 * k + 1]), f2_bits(acc[c0 + 4 * k + 2]),
+                                    f2_bits(acc[c0 + 4 * k + 3]));
+            stage_put(st, lane, seg);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                const int orow = __shfl_sync(FULL, myrow, r);
+                const int n = nb + c0 + ch * 4;
+                if (orow >= 0 && n < N) {
+                    const uint4 v = st[stage_idx(r, ch)];
+                    float4 f = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z),
+                                           __uint_as_float(v.w));
+                    float *p = ep.y + static_cast<int64_t>(orow) * ep.ldy + n;
+                    if (ep.add) {
+                        const float4 prev = *reinterpret_cast<const float4 *>(p);
+                        f.x = __fadd_rn(prev.x, f.x);
+                        f.y = __fadd_rn(prev.y, f.y);
+                        f.z = __fadd_rn(prev.z, f.z);
+                        f.w = __fadd_rn(prev.w, f.w);
+                    }
+                    *reinterpret_cast<float4 *>(p) = f;
+                }
+            }
+        }
+    } else if constexpr (MODE == MMQ_OUT_DQ16) {
+        const int rowok = m < M;
+#pragma unroll
+        for (int hb = 0; hb < COLS; hb += 32) {
+            if (nb + hb >= N) break;  // warp-uniform
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float val = bias ? __fadd_rn(acc[hb + i], bias[nb + hb + i]) : acc[hb + i];
+                if (ep.gelu == 1) val = gelu_erf_f(val);
+                else if (ep.gelu == 2) val = gelu_tanh_f16(val);
+                acc[hb + i] = val;
+                amax = fmaxf(amax, fabsf(val));
+            }
+            const float d = __fdiv_rn(amax, 127.f);
+            const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+            const float dh = __half2float(__float2half_rn(d));  // the block's stored (fp16) scale
+            uint32_t hw[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float q0 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + 2 * e], id)));
+                const float q1 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + 2 * e + 1], id)));
+                const __half2 h2 = __floats2half2_rn(__fmul_rn(q0, dh), __fmul_rn(q1, dh));
+                hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+            }
+            const uint4 seg[4] = {make_uint4(hw[0], hw[1], hw[2], hw[3]), make_uint4(hw[4], hw[5], hw[6], hw[7]),
+                                  make_uint4(hw[8], hw[9], hw[10], hw[11]), make_uint4(hw[12], hw[13], hw[14], hw[15])};
+            stage_put(st, lane, seg);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                if (__shfl_sync(FULL, rowok, r))
+                    *reinterpret_cast<uint4 *>(ep.o16 + static_cast<int64_t>(m_warp + r) * N + nb + hb + ch * 8) =
+                        st[stage_idx(r, ch)];
+            }
+        }
+    } else if constexpr (MODE == MMQ_OUT_QKV) {
+        // this thread's COLS columns lie inside one 64-wide head of the q, k or v third;
+        // M is a multiple of win_tokens and a warp's 32 rows never straddle a window
+        const int E = N / 3;
+        const int part = nb / E, c0h = nb - part * E, hd = c0h >> 6, d0 = c0h & 63;
+        const int win = m / ep.win_tokens, pos = m - win * ep.win_tokens;
+        const int64_t bh = static_cast<int64_t>(win) * ep.heads + hd;
+        if (bias) {
+#pragma unroll
+            for (int i = 0; i < COLS; ++i) acc[i] = __fadd_rn(acc[i], bias[nb + i]);
+        }
+        if (part < 2) {
+            if (ep.freqs) {
+                // the row's RoPE (cos, sin) pairs, gathered 8 rows x 64 bytes per instruction
+#pragma unroll
+                for (int c0 = 0; c0 < COLS; c0 += 16) {
+                    __syncwarp();
+#pragma unroll
+                    for (int it = 0; it < 4; ++it) {
+                        const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                        const int pr = __shfl_sync(FULL, pos, r);
+                        st[stage_idx(r, ch)] = *reinterpret_cast<const uint4 *>(
+                            ep.freqs + (static_cast<int64_t>(pr) * 32 + (d0 >> 1)) * 2 + c0 + ch * 4);
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint4 cs = st[stage_idx(lane, k)];  // cos, sin of pairs c0/2 + 2k, + 1
+                        const int i = c0 + 4 * k;
+                        float x0 = acc[i], x1 = acc[i + 1];
+                        acc[i] = __fsub_rn(__fmul_rn(x0, __uint_as_float(cs.x)), __fmul_rn(x1, __uint_as_float(cs.y)));
+                        acc[i + 1] = __fadd_rn(__fmul_rn(x0, __uint_as_float(cs.y)), __fmul_rn(x1, __uint_as_float(cs.x)));
+                        x0 = acc[i + 2];
+                        x1 = acc[i + 3];
+                        acc[i + 2] = __fsub_rn(__fmul_rn(x0, __uint_as_float(cs.z)), __fmul_rn(x1, __uint_as_float(cs.w)));
+                        acc[i + 3] = __fadd_rn(__fmul_rn(x0, __uint_as_float(cs.w)), __fmul_rn(x1, __uint_as_float(cs.z)));
+                    }
+                }
+            }
+            const int64_t base = m < M ? (bh * ep.win_tokens + pos) * 64 + d0 : -1;
+            __nv_bfloat16 *dst = part == 0 ? ep.q : ep.k;
+#pragma unroll
+            for (int c0 = 0; c0 < COLS; c0 += 32) {
+                uint4 seg[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    seg[k] = make_uint4(bf2_bits(acc[c0 + 8 * k], acc[c0 + 8 * k + 1]),
+                                        bf2_bits(acc[c0 + 8 * k + 2], acc[c0 + 8 * k + 3]),
+                                        bf2_bits(acc[c0 + 8 * k + 4], acc[c0 + 8 * k + 5]),
+                                        bf2_bits(acc[c0 + 8 * k + 6], acc[c0 + 8 * k + 7]));
+                stage_put(st, lane, seg);
+#pragma unroll
+                for (int it = 0; it < 4; ++it) {
+                    const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                    const long long b = __shfl_sync(FULL, static_cast<long long>(base), r);
+                    if (b >= 0) *reinterpret_cast<uint4 *>(dst + b + c0 + ch * 8) = st[stage_idx(r, ch)];
+                }
+            }
+        } else if (m < M) {
+            // V^T: consecutive lanes hold consecutive tokens, so each store is 64 contiguous bytes
+            __nv_bfloat16 *dst = ep.vt + (bh * 64 + d0) * ep.win_tokens + pos;
+#pragma unroll
+            for (int i = 0; i < COLS; ++i) dst[static_cast<int64_t>(i) * ep.win_tokens] = __float2bfloat16_rn(acc[i]);
+        }
+    } else {
+        tile_store<MODE, COLS>(ep, acc, m, M, N, nb);
+    }
+}
+
 // CTA tile 128 tokens x BN features, persistent over tiles, 576 threads:
 //   warp 0      : TMA producer (one elected lane): 64-wide K stages of A
 //                 (128 rows) and B (BN rows), 128-byte swizzle;
@@ -1036,8 +1216,9 @@ cudaError_t dequant_weight_f16(const QMatrix &w, void *out, cudaStream_t s) {
 //                 tile's MMAs;
 //   warps 2..17 : epilogue, four per TMEM lane quarter (warp w reads lane
 //                 quarter w % 4, column slice (w - 2) / 4 of BN / 4 columns),
-//                 then the mode's tile_store (bias, residual through the row
-//                 map, RoPE + head split, GELU + Q8_0 re-quantisation).
+//                 then the mode's epilogue (bias, residual through the row
+//                 map, RoPE + head split, GELU + Q8_0 re-quantisation) with
+//                 its stores staged through shared memory (tile_store_staged).
 template <int BN_>
 struct DqCfg {
     static constexpr int BM = 128, BN = BN_, BK = 64;
@@ -1049,7 +1230,8 @@ struct DqCfg {
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int COLS = BN / 4;  // output columns per epilogue thread
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+    static constexpr int STAGE_OFF = BAR_OFF + 256;  // per-warp 2 KB row-segment staging (tile_store_staged)
+    static constexpr int SMEM_BYTES = STAGE_OFF + EPI_WARPS * 2048 + 1024;
     static_assert(COLS % 32 == 0 && COLS <= 64, "whole 32-column TMEM loads, inside one 64-wide head");
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -1175,7 +1357,8 @@ __global__ void __launch_bounds__(DqCfg<BN>::THREADS, 1)
             float acc[C::COLS];
 #pragma unroll
             for (int i = 0; i < C::COLS; ++i) acc[i] = __uint_as_float(v[i]);
-            tile_store<MODE, C::COLS>(ep, acc, m0 + row, M, N, n0 + cs);
+            tile_store_staged<MODE, C::COLS>(ep, acc, m0 + row, M, N, n0 + cs,
+                                             reinterpret_cast<uint4 *>(smem + C::STAGE_OFF) + (warp - 2) * 128, lane);
         }
     }
     tc_fence_before();
