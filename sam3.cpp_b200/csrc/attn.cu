@@ -338,8 +338,8 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                                 uint32_t hw[4];
 #pragma unroll
                                 for (int e = 0; e < 4; ++e) {
-                                    const float a0 = static_cast<float>(__float2int_rn(__fmul_rn(o[hb + i + 2 * e], id)));
-                                    const float a1 = static_cast<float>(__float2int_rn(__fmul_rn(o[hb + i + 2 * e + 1], id)));
+                                    const float a0 = q8_code_f(__fmul_rn(o[hb + i + 2 * e], id));
+                                    const float a1 = q8_code_f(__fmul_rn(o[hb + i + 2 * e + 1], id));
                                     const __half2 h2 = __floats2half2_rn(__fmul_rn(a0, dh), __fmul_rn(a1, dh));
                                     hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
                                 }

@@ -388,8 +388,8 @@ __device__ __forceinline__ void tile_store(const MmqEpi &ep, float (&acc)[COLS],
                         uint32_t hw[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const float q0 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + i + 2 * e], id)));
-                            const float q1 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + i + 2 * e + 1], id)));
+                            const float q0 = q8_code_f(__fmul_rn(acc[hb + i + 2 * e], id));
+                            const float q1 = q8_code_f(__fmul_rn(acc[hb + i + 2 * e + 1], id));
                             const __half2 h2 = __floats2half2_rn(__fmul_rn(q0, dh), __fmul_rn(q1, dh));
                             hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
                         }
@@ -1055,14 +1055,39 @@ __device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
 // (every lane of the warp calls it, rows m >= M included); m = this lane's tile
 // row, the warp's rows are m - lane .. m - lane + 31.  Same arithmetic as
 // tile_store, only the memory access pattern differs.
+__device__ __forceinline__ bool f32_rows_vec(const MmqEpi &ep, int N) {
+    return ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0) && ((N & 3) == 0);
+}
+
+// The residual values tile_store_staged's MMQ_OUT_F32 path adds for COLS
+// columns from nb (rounds of 16 columns, 8 rows x 64 bytes per load), read
+// before the tile's accumulator is ready so their latency overlaps its MMAs.
+template <int COLS>
+__device__ __forceinline__ void prefetch_residual(const MmqEpi &ep, float4 (&pre)[COLS / 16][4], int m, int M, int N,
+                                                  int nb, int lane) {
+    const int myrow = m < M ? (ep.rowmap ? ep.rowmap[m] : m) : -1;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + (lane >> 2), ch = lane & 3;
+        const int orow = __shfl_sync(0xffffffffu, myrow, r);
+#pragma unroll
+        for (int c = 0; c < COLS / 16; ++c) {
+            const int n = nb + c * 16 + ch * 4;
+            pre[c][it] = orow >= 0 && n < N
+                             ? *reinterpret_cast<const float4 *>(ep.y + static_cast<int64_t>(orow) * ep.ldy + n)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+
 template <int MODE, int COLS>
 __device__ __forceinline__ void tile_store_staged(const MmqEpi &ep, float (&acc)[COLS], int m, int M, int N, int nb,
-                                                  uint4 *st, int lane) {
+                                                  uint4 *st, int lane, const float4 (*pre)[4] = nullptr) {
     constexpr unsigned FULL = 0xffffffffu;
     const float *__restrict__ bias = ep.bias;
     const int m_warp = m - lane;
     if constexpr (MODE == MMQ_OUT_F32) {
-        const bool vec = ((ep.ldy & 3) == 0) && ((reinterpret_cast<uintptr_t>(ep.y) & 15) == 0) && ((N & 3) == 0);
+        const bool vec = f32_rows_vec(ep, N);
         if (!vec) {  // warp-uniform: the per-lane path handles any stride / width
             tile_store<MODE, COLS>(ep, acc, m, M, N, nb);
             return;
@@ -1092,7 +1117,7 @@ __device__ __forceinline__ void tile_store_staged(const MmqEpi &ep, float (&acc)
                                            __uint_as_float(v.w));
                     float *p = ep.y + static_cast<int64_t>(orow) * ep.ldy + n;
                     if (ep.add) {
-                        const float4 prev = *reinterpret_cast<const float4 *>(p);
+                        const float4 prev = pre ? pre[c0 / 16][it] : *reinterpret_cast<const float4 *>(p);
                         f.x = __fadd_rn(prev.x, f.x);
                         f.y = __fadd_rn(prev.y, f.y);
                         f.z = __fadd_rn(prev.z, f.z);
@@ -1122,8 +1147,8 @@ __device__ __forceinline__ void tile_store_staged(const MmqEpi &ep, float (&acc)
             uint32_t hw[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-                const float q0 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + 2 * e], id)));
-                const float q1 = static_cast<float>(__float2int_rn(__fmul_rn(acc[hb + 2 * e + 1], id)));
+                const float q0 = q8_code_f(__fmul_rn(acc[hb + 2 * e], id));
+                const float q1 = q8_code_f(__fmul_rn(acc[hb + 2 * e + 1], id));
                 const __half2 h2 = __floats2half2_rn(__fmul_rn(q0, dh), __fmul_rn(q1, dh));
                 hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
             }
@@ -1341,11 +1366,17 @@ __global__ void __launch_bounds__(DqCfg<BN>::THREADS, 1)
         const int row = q * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         uint32_t it = 0;
+        // F32 with a residual add at 32 columns per thread (proj, fc2): the residual is read early
+        constexpr bool PREF = MODE == MMQ_OUT_F32 && C::COLS == 32;
+        const bool pref = PREF && ep.add && f32_rows_vec(ep, N);
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
             const uint32_t buf = it & 1u;
+            const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
+            float4 pre[PREF ? C::COLS / 16 : 1][4];
+            if constexpr (PREF)
+                if (pref) prefetch_residual<C::COLS>(ep, pre, m0 + row, M, N, n0 + cs, lane);
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[buf], (it >> 1) & 1u, err, ERR_WAIT_TFULL))) break;
             tc_fence_after();
-            const int m0 = (t % num_m) * C::BM, n0 = (t / num_m) * C::BN;
             uint32_t v[C::COLS];
 #pragma unroll
             for (int c = 0; c < C::COLS; c += 32)
@@ -1358,7 +1389,8 @@ __global__ void __launch_bounds__(DqCfg<BN>::THREADS, 1)
 #pragma unroll
             for (int i = 0; i < C::COLS; ++i) acc[i] = __uint_as_float(v[i]);
             tile_store_staged<MODE, C::COLS>(ep, acc, m0 + row, M, N, n0 + cs,
-                                             reinterpret_cast<uint4 *>(smem + C::STAGE_OFF) + (warp - 2) * 128, lane);
+                                             reinterpret_cast<uint4 *>(smem + C::STAGE_OFF) + (warp - 2) * 128, lane,
+                                             PREF && pref ? pre : nullptr);
         }
     }
     tc_fence_before();

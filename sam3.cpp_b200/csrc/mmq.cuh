@@ -51,6 +51,14 @@ __host__ __device__ constexpr int64_t act_quad_index(int b, int m, int ld) {
 }
 
 #ifdef __CUDACC__
+// The Q8_0 code of v = x * id (|v| <= 127) as a float: round half to even,
+// like (float)__float2int_rn(v), but on the FMA pipe -- adding 1.5 * 2^23
+// leaves no fraction bits and the IEEE add rounds to nearest even -- instead
+// of a float -> int -> float conversion pair.  Bit-identical for |v| < 2^22.
+__device__ __forceinline__ float q8_code_f(float v) {
+    return __fsub_rn(__fadd_rn(v, 12582912.0f), 12582912.0f);
+}
+
 // Store the scale d of block b (of nblk) of row m into an A-side record
 // array.  The writer of a row's last block also zeroes the record slots past
 // it when nblk is not a multiple of 8: the scale MMA reads whole records and

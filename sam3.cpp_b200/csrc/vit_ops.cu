@@ -308,10 +308,10 @@ __global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
         const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
         if constexpr (DQ) {
             const float dh = __half2float(__float2half_rn(d));
-            const __half2 h01 = __floats2half2_rn(__fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y0, id))), dh),
-                                                  __fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y1, id))), dh));
-            const __half2 h23 = __floats2half2_rn(__fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y2, id))), dh),
-                                                  __fmul_rn(static_cast<float>(__float2int_rn(__fmul_rn(y3, id))), dh));
+            const __half2 h01 = __floats2half2_rn(__fmul_rn(q8_code_f(__fmul_rn(y0, id)), dh),
+                                                  __fmul_rn(q8_code_f(__fmul_rn(y1, id)), dh));
+            const __half2 h23 = __floats2half2_rn(__fmul_rn(q8_code_f(__fmul_rn(y2, id)), dh),
+                                                  __fmul_rn(q8_code_f(__fmul_rn(y3, id)), dh));
             *reinterpret_cast<uint2 *>(o16 + static_cast<int64_t>(r) * E + 128 * j + 4 * lane) =
                 make_uint2(*reinterpret_cast<const uint32_t *>(&h01), *reinterpret_cast<const uint32_t *>(&h23));
         } else {
