@@ -371,6 +371,9 @@ def main():
                     help="linear-layer arithmetic of the encoder (sam3b200_set_arith): dq16 (default) = Q8_0 "
                          "codes and weight blocks dequantised to fp16 on the fp16 tensor cores; exact = int8 block "
                          "dots with the block-ordered fp32 fold")
+    ap.add_argument("--batch", type=int, default=4,
+                    help="images per encoder call (sam3b200_encode_images): the ViT blocks run once over that "
+                         "many images' tokens; 1 = one sam3b200_encode_image per image")
     ap.add_argument("--images", type=int, default=BATCH,
                     help="images per step (default 64, the config's batch; smaller only for profiling runs)")
     args = ap.parse_args()
@@ -443,16 +446,26 @@ def main():
     pinned = torch.from_numpy(imgs).pin_memory()
     stream = torch.cuda.ExternalStream(be.stream)
     small = np.empty((hp["img"] // hp["patch"] // 2, hp["img"] // hp["patch"] // 2, hp["neck_dim"]), np.float32)
-    small_ptrs = (ctypes.c_void_p * 4)(None, None, None, small.ctypes.data)
+
+    nb = max(1, args.batch)
+    chunks = [list(range(i, min(i + nb, len(mine)))) for i in range(0, len(mine), nb)]
+    # per call: the host images of the chunk, and the smallest neck map of each image as its read-back
+    e2e_args = []
+    for c in chunks:
+        srcs = (ctypes.c_void_p * len(c))(*[pinned[i].data_ptr() for i in c])
+        outs = (ctypes.c_void_p * (4 * len(c)))(*([None, None, None, small.ctypes.data] * len(c)))
+        e2e_args.append((len(c), srcs, outs))
 
     def step_device():
-        for d in dev_imgs:
-            vit.encode_device(d, S, S)
+        for c in chunks:
+            if len(c) == 1:
+                vit.encode_device(dev_imgs[c[0]], S, S)
+            else:
+                vit.encode_batch_device([dev_imgs[i] for i in c], S, S)
 
     def step_e2e():
-        for i in range(len(mine)):
-            ptr = pinned[i].data_ptr()
-            st = b200.lib().sam3b200_encode_image(vit.h, ctypes.c_void_p(ptr), S, S, small_ptrs)
+        for n, srcs, outs in e2e_args:
+            st = b200.lib().sam3b200_encode_images(vit.h, n, srcs, S, S, outs)
             if st != 0:
                 raise b200.B200Error(b200.last_error())
 
@@ -536,7 +549,7 @@ def main():
             "data": "synthetic",
             "config": {"workload": "cfg3: SAM3 visual-only ViT-32 (Q8_0) + trk SimpleFPN neck, 1008x1008, "
                                    "64 seeded uint8 images per step split across ranks",
-                       "arith": args.arith,
+                       "arith": args.arith, "images_per_call": nb,
                        "global_batch": batch, "seq_len": (S // hp["patch"]) ** 2, "parallelism": f"dp{world}",
                        "weights": "random-init N(0,0.02), Q8_0 reference quantiser rule",
                        "l2": "no flush: per-image working set (~0.5 GB of weights) exceeds the 126 MB L2"},

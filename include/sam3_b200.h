@@ -870,6 +870,26 @@ int sam3b200_encode_image(sam3b200_vit *vit, const uint8_t *rgb, int w, int h, f
  * (sam3b200_vit_output). */
 int sam3b200_encode_image_device(sam3b200_vit *vit, const uint8_t *rgb_dev, int w, int h);
 
+/* sam3_encode_image for n images at once (a batch of sam3.cpp:6028-6149
+ * calls; the reference has no batched form): each image is preprocessed and
+ * embedded, then the ViT blocks run once over the n images' tokens stacked
+ * image-major -- every MUL_MAT, attention and LayerNorm launch covers all n,
+ * which fills the 148 SMs in whole waves -- and each image gets its neck.
+ * Results per image are bit-identical to n single encodes.  DQ16 arithmetic
+ * (sam3b200_set_arith); under EXACT the images are encoded one by one.  The
+ * first call with a larger n than before grows the block-loop buffers (~0.11
+ * GB per extra 1008^2 image) and synchronises.  rgb[i]: n uint8 RGB HWC host
+ * images of w x h; out_host[4 i + j]: image i's neck map j (as for
+ * sam3b200_encode_image; NULL entries skipped).  Synchronous. */
+int sam3b200_encode_images(sam3b200_vit *vit, int n, const uint8_t *const *rgb, int w, int h,
+                           float *const *out_host);
+
+/* Same with the images in device memory; asynchronous on the backend
+ * stream.  Afterwards sam3b200_vit_output(0..3) holds the last image's neck
+ * maps and sam3b200_vit_output(-1) the first image's ViT output (the n
+ * outputs follow it, image-major). */
+int sam3b200_encode_images_device(sam3b200_vit *vit, int n, const uint8_t *const *rgb_dev, int w, int h);
+
 /* Device pointer and ggml shape of output i (0..3 = neck_trk_i, -1 = the
  * ViT output [embed, G, G]) of the last encode. */
 int sam3b200_vit_output(sam3b200_vit *vit, int i, const float **dev, int64_t ne[4]);

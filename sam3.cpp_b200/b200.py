@@ -280,6 +280,8 @@ def lib() -> ctypes.CDLL:
         "sam3b200_vit_missing": (i32, [vp, ctypes.c_char_p, i32]),
         "sam3b200_encode_image": (i32, [vp, vp, i32, i32, vp]),
         "sam3b200_encode_image_device": (i32, [vp, vp, i32, i32]),
+        "sam3b200_encode_images": (i32, [vp, i32, vp, i32, i32, vp]),
+        "sam3b200_encode_images_device": (i32, [vp, i32, vp, i32, i32]),
         "sam3b200_vit_output": (i32, [vp, i32, ctypes.POINTER(ctypes.c_void_p), vp]),
         "sam3b200_vit_run_prefix": (i32, [vp, vp, vp]),
         "sam3b200_vit_run_block": (i32, [vp, i32, vp]),
@@ -533,6 +535,23 @@ class Vit:
 
     def encode_device(self, rgb_dev: "DeviceBuffer", w: int, h: int) -> None:
         _check(lib().sam3b200_encode_image_device(self.h, rgb_dev.ptr, w, h), "encode_image_device")
+
+    def encode_batch(self, rgbs) -> list:
+        """sam3b200_encode_images: n host uint8 HxWx3 images (same size) -> per image four neck maps."""
+        rgbs = [np.ascontiguousarray(r, dtype=np.uint8) for r in rgbs]
+        h, w = rgbs[0].shape[:2]
+        D = self.hp["neck_dim"]
+        outs = [[np.empty((s, s, D), np.float32) for s in (4 * self.G, 2 * self.G, self.G, self.G // 2)]
+                for _ in rgbs]
+        srcs = (ctypes.c_void_p * len(rgbs))(*[r.ctypes.data for r in rgbs])
+        ptrs = (ctypes.c_void_p * (4 * len(rgbs)))(*[o.ctypes.data for os_ in outs for o in os_])
+        _check(lib().sam3b200_encode_images(self.h, len(rgbs), srcs, w, h, ptrs), "encode_images")
+        return outs
+
+    def encode_batch_device(self, rgb_devs, w: int, h: int) -> None:
+        """sam3b200_encode_images_device: n device images, one batched pass through the blocks."""
+        srcs = (ctypes.c_void_p * len(rgb_devs))(*[d.ptr for d in rgb_devs])
+        _check(lib().sam3b200_encode_images_device(self.h, len(rgb_devs), srcs, w, h), "encode_images_device")
 
     def output(self, i: int):
         p = ctypes.c_void_p()

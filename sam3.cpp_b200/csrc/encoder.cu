@@ -51,6 +51,7 @@ struct Vit {
     DevBuf x16, mp16, n_a, n_c, n_d, n_col, out[4], out_det[4];
     int out_side[4] = {0, 0, 0, 0};
     int img_cap = 0;  // pixels of img_u8
+    int bcap = 1;     // images the block-loop buffers (x, a16, b16, q, k, v, rowmap) hold, image-major
 };
 
 static bool is_global(const sam3b200_vit_hparams &hp, int i) {
@@ -145,10 +146,10 @@ static bool mmq_qkv(Vit *v, const BlockW &w, int win_tokens) {
 
 // DQ16 arithmetic (mmq.cuh): the dequantised A operand a16 [T][K] against the
 // weight's fp16 copy, with the same epilogue modes
-static bool mmq16(Vit *v, const void *a16, const QWeight &w, int mode, const float *bias, float *y, int add,
+static bool mmq16(Vit *v, int rows, const void *a16, const QWeight &w, int mode, const float *bias, float *y, int add,
                   const int *rowmap, void *out16, int gelu) {
     MmqArgs a;
-    a.a = QMatrix{nullptr, nullptr, v->T, w.K, v->Tpad};
+    a.a = QMatrix{nullptr, nullptr, rows, w.K, rows};
     a.b = QMatrix{nullptr, nullptr, w.N, w.K, w.ld, w.nib};
     a.bias = bias;
     a.y = y;
@@ -165,9 +166,9 @@ static bool mmq16(Vit *v, const void *a16, const QWeight &w, int mode, const flo
     return ok;
 }
 
-static bool mmq16_qkv(Vit *v, const BlockW &w, int win_tokens) {
+static bool mmq16_qkv(Vit *v, int rows, const BlockW &w, int win_tokens) {
     MmqArgs a;
-    a.a = QMatrix{nullptr, nullptr, v->T, w.qkv.K, v->Tpad};
+    a.a = QMatrix{nullptr, nullptr, rows, w.qkv.K, rows};
     a.b = QMatrix{nullptr, nullptr, w.qkv.N, w.qkv.K, w.qkv.ld, w.qkv.nib};
     a.bias = w.qkv_b.as<float>();
     a.y = nullptr;
@@ -189,12 +190,16 @@ static bool mmq16_qkv(Vit *v, const BlockW &w, int win_tokens) {
 
 // LayerNorm + Q8_0 of the residual stream, written dequantised into a16 (one
 // kernel for the supported widths, else layernorm_q8 and a dequantising pass)
-static bool ln_dq16(Vit *v, const float *x, const DevBuf &w, const DevBuf &b, int win) {
+static bool ln_dq16(Vit *v, int rows, const float *x, const DevBuf &w, const DevBuf &b, int win) {
     const int E = v->hp.embed;
     cudaStream_t s = v->be->stream;
     if (E % 256 == 0 && E <= 1536)
-        return launched(v, layernorm_dq16(x, v->T, E, w.as<float>(), b.as<float>(), 1e-5f, v->G, win, v->a16.p, s),
+        return launched(v, layernorm_dq16(x, rows, E, w.as<float>(), b.as<float>(), 1e-5f, v->G, win, v->a16.p, s),
                         "ln dq16");
+    if (rows != v->T) {
+        set_error("vit: batched encode needs an embedding width in {256, 512, ..., 1536}");
+        return false;
+    }
     return launched(v, layernorm_q8(x, v->T, E, w.as<float>(), b.as<float>(), 1e-5f, v->G, win, v->codes_a.p,
                                     v->quads_a.p, v->Tpad, s),
                     "ln") &&
@@ -235,29 +240,36 @@ static bool run_prefix(Vit *v, const float *img_chw, float *x) {
 // run_block with DQ16 linear layers: the same Q8_0 activations as the exact
 // path (LayerNorm, attention and fc1's GELU epilogue quantise with ggml's
 // rule), each written dequantised as the next fp16 MUL_MAT's operand.
-static bool run_block_dq16(Vit *v, int i, float *x) {
+// nimg images stacked image-major in x (nimg * T rows): every kernel of the
+// block runs once over all of them (the windows and global blocks of image j
+// follow those of image j - 1), so results per image are those of nimg = 1.
+static bool run_block_dq16(Vit *v, int i, float *x, int nimg) {
     const auto &hp = v->hp;
     const BlockW &w = v->blk[i];
     cudaStream_t s = v->be->stream;
-    const int E = hp.embed, G = v->G, T = v->T, ws = hp.window;
+    const int E = hp.embed, G = v->G, T = v->T, ws = hp.window, rows = nimg * T;
     const bool glob = is_global(hp, i);
-    const int B = glob ? 1 : (G / ws) * (G / ws);
+    const int B = nimg * (glob ? 1 : (G / ws) * (G / ws));
     const int N = glob ? T : ws * ws;
     AttnOut attn_dq;  // the proj MUL_MAT's operand (window order), written by the attention
     attn_dq.dq16 = v->a16.p;
-    return ln_dq16(v, x, w.n1w, w.n1b, glob ? 0 : ws) && mmq16_qkv(v, w, N) &&
+    return ln_dq16(v, rows, x, w.n1w, w.n1b, glob ? 0 : ws) && mmq16_qkv(v, rows, w, N) &&
            launched(v, flash_attention(v->q.p, v->k.p, v->v.p, B, N, hp.heads,
                                        1.0f / sqrtf(static_cast<float>(E / hp.heads)), attn_dq, v->be->err, s),
                     "attention") &&
-           mmq16(v, v->a16.p, w.proj, MMQ_OUT_F32, w.proj_b.as<float>(), x, 1, glob ? nullptr : v->rowmap.as<int>(),
-                 nullptr, 0) &&
-           ln_dq16(v, x, w.n2w, w.n2b, 0) &&
-           mmq16(v, v->a16.p, w.fc1, MMQ_OUT_DQ16, w.fc1_b.as<float>(), nullptr, 0, nullptr, v->b16.p, 1) &&
-           mmq16(v, v->b16.p, w.fc2, MMQ_OUT_F32, w.fc2_b.as<float>(), x, 1, nullptr, nullptr, 0);
+           mmq16(v, rows, v->a16.p, w.proj, MMQ_OUT_F32, w.proj_b.as<float>(), x, 1,
+                 glob ? nullptr : v->rowmap.as<int>(), nullptr, 0) &&
+           ln_dq16(v, rows, x, w.n2w, w.n2b, 0) &&
+           mmq16(v, rows, v->a16.p, w.fc1, MMQ_OUT_DQ16, w.fc1_b.as<float>(), nullptr, 0, nullptr, v->b16.p, 1) &&
+           mmq16(v, rows, v->b16.p, w.fc2, MMQ_OUT_F32, w.fc2_b.as<float>(), x, 1, nullptr, nullptr, 0);
 }
 
-static bool run_block(Vit *v, int i, float *x) {
-    if (v->be->mmq_arith == SAM3B200_ARITH_DQ16) return run_block_dq16(v, i, x);
+static bool run_block(Vit *v, int i, float *x, int nimg = 1) {
+    if (v->be->mmq_arith == SAM3B200_ARITH_DQ16) return run_block_dq16(v, i, x, nimg);
+    if (nimg != 1) {
+        set_error("vit: batched blocks need the DQ16 arithmetic");
+        return false;
+    }
     const auto &hp = v->hp;
     const BlockW &w = v->blk[i];
     cudaStream_t s = v->be->stream;
@@ -375,7 +387,8 @@ static bool check_ready(Vit *v) {
     return true;
 }
 
-static bool encode(Vit *v, const uint8_t *rgb_dev, int w, int h) {
+// preprocessing + prefix of one image into rows [0, T) of x
+static bool prefix_image(Vit *v, const uint8_t *rgb_dev, int w, int h, float *x) {
     const auto &hp = v->hp;
     cudaStream_t s = v->be->stream;
     const uint8_t *src = rgb_dev;
@@ -385,11 +398,67 @@ static bool encode(Vit *v, const uint8_t *rgb_dev, int w, int h) {
             return false;
         src = v->img_rs.as<uint8_t>();
     }
-    if (!launched(v, preprocess_sam3(src, hp.img, v->img_f32.as<float>(), s), "preprocess")) return false;
-    if (!run_prefix(v, v->img_f32.as<float>(), v->x.as<float>())) return false;
-    for (int i = 0; i < hp.depth; ++i)
+    return launched(v, preprocess_sam3(src, hp.img, v->img_f32.as<float>(), s), "preprocess") &&
+           run_prefix(v, v->img_f32.as<float>(), x);
+}
+
+static bool encode(Vit *v, const uint8_t *rgb_dev, int w, int h) {
+    if (!prefix_image(v, rgb_dev, w, h, v->x.as<float>())) return false;
+    for (int i = 0; i < v->hp.depth; ++i)
         if (!run_block(v, i, v->x.as<float>())) return false;
     return run_necks(v, v->x.as<float>());
+}
+
+// Block-loop buffers for n images stacked image-major (the batched encode);
+// single-image encodes use the first image's part.  Grows only; contents are
+// not kept across a growth.
+static bool ensure_batch(Vit *v, int n) {
+    if (n <= v->bcap) return true;
+    const auto &hp = v->hp;
+    const size_t T = static_cast<size_t>(v->T), E = static_cast<size_t>(hp.embed), nn = static_cast<size_t>(n);
+    if (!cuda_ok(cudaStreamSynchronize(v->be->stream), "batch sync")) return false;
+    v->bcap = 0;
+    const bool ok = v->x.alloc(nn * T * E * 4) && v->a16.alloc(nn * T * E * 2) &&
+                    v->b16.alloc(nn * T * static_cast<size_t>(hp.mlp) * 2) && v->q.alloc(nn * T * E * 2) &&
+                    v->k.alloc(nn * T * E * 2) && v->v.alloc(nn * T * E * 2) && v->rowmap.alloc(nn * T * 4) &&
+                    cuda_ok(window_rowmap(v->G, hp.window, v->rowmap.as<int>(), v->be->stream, n), "rowmap") &&
+                    cuda_ok(cudaStreamSynchronize(v->be->stream), "rowmap sync");
+    if (ok) v->bcap = n;
+    return ok;
+}
+
+static bool copy_outputs(Vit *v, float *const *out_host) {
+    for (int i = 0; i < 4; ++i) {
+        if (!out_host || !out_host[i]) continue;
+        const size_t ob = static_cast<size_t>(v->out_side[i]) * v->out_side[i] * v->hp.neck_dim * 4;
+        if (!cuda_ok(cudaMemcpyAsync(out_host[i], v->out[i].p, ob, cudaMemcpyDeviceToHost, v->be->stream),
+                     "output download"))
+            return false;
+    }
+    return true;
+}
+
+// n images through the encoder: the prefix per image, the blocks once over
+// all n images' tokens (DQ16; the exact arithmetic runs image by image), then
+// each image's neck, whose outputs go to out_host[4 i .. 4 i + 3] (if given)
+// before the next image's neck overwrites them.
+static bool encode_batch(Vit *v, int n, const uint8_t *const *rgb_dev, int w, int h, float *const *out_host) {
+    if (v->be->mmq_arith != SAM3B200_ARITH_DQ16 || n == 1) {
+        for (int i = 0; i < n; ++i)
+            if (!encode(v, rgb_dev[i], w, h) || !copy_outputs(v, out_host ? out_host + 4 * i : nullptr)) return false;
+        return true;
+    }
+    if (!ensure_batch(v, n)) return false;
+    const size_t img_elems = static_cast<size_t>(v->T) * v->hp.embed;
+    for (int i = 0; i < n; ++i)
+        if (!prefix_image(v, rgb_dev[i], w, h, v->x.as<float>() + i * img_elems)) return false;
+    for (int b = 0; b < v->hp.depth; ++b)
+        if (!run_block(v, b, v->x.as<float>(), n)) return false;
+    for (int i = 0; i < n; ++i)
+        if (!run_necks(v, v->x.as<float>() + i * img_elems) ||
+            !copy_outputs(v, out_host ? out_host + 4 * i : nullptr))
+            return false;
+    return true;
 }
 
 }  // namespace b200
@@ -615,14 +684,51 @@ int sam3b200_encode_image(sam3b200_vit *hv, const uint8_t *rgb, int w, int h, fl
     if (v->img_u8.n < bytes && !v->img_u8.alloc(bytes)) return SAM3B200_STATUS_ALLOC_FAILED;
     cudaStream_t s = v->be->stream;
     if (!cuda_ok(cudaMemcpyAsync(v->img_u8.p, rgb, bytes, cudaMemcpyHostToDevice, s), "image upload") ||
-        !encode(v, v->img_u8.as<uint8_t>(), w, h))
+        !encode(v, v->img_u8.as<uint8_t>(), w, h) || !copy_outputs(v, out_host))
         return SAM3B200_STATUS_FAILED;
-    for (int i = 0; i < 4; ++i) {
-        if (!out_host || !out_host[i]) continue;
-        const size_t ob = static_cast<size_t>(v->out_side[i]) * v->out_side[i] * v->hp.neck_dim * 4;
-        if (!cuda_ok(cudaMemcpyAsync(out_host[i], v->out[i].p, ob, cudaMemcpyDeviceToHost, s), "output download"))
+    return sam3b200_backend_synchronize(reinterpret_cast<sam3b200_backend *>(v->be));
+}
+
+int sam3b200_encode_images_device(sam3b200_vit *hv, int n, const uint8_t *const *rgb_dev, int w, int h) {
+    auto *v = reinterpret_cast<Vit *>(hv);
+    if (!v || n <= 0 || !rgb_dev || w <= 0 || h <= 0) {
+        set_error("encode_images_device: bad argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    for (int i = 0; i < n; ++i)
+        if (!rgb_dev[i]) {
+            set_error("encode_images_device: image %d is null", i);
+            return SAM3B200_STATUS_FAILED;
+        }
+    cudaSetDevice(v->be->device);
+    if (!check_ready(v)) return SAM3B200_STATUS_FAILED;
+    return encode_batch(v, n, rgb_dev, w, h, nullptr) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+}
+
+int sam3b200_encode_images(sam3b200_vit *hv, int n, const uint8_t *const *rgb, int w, int h,
+                           float *const *out_host) {
+    auto *v = reinterpret_cast<Vit *>(hv);
+    if (!v || n <= 0 || !rgb || w <= 0 || h <= 0) {
+        set_error("encode_images: bad argument");
+        return SAM3B200_STATUS_FAILED;
+    }
+    cudaSetDevice(v->be->device);
+    if (!check_ready(v)) return SAM3B200_STATUS_FAILED;
+    const size_t bytes = static_cast<size_t>(w) * h * 3;
+    if (v->img_u8.n < bytes * n && !v->img_u8.alloc(bytes * n)) return SAM3B200_STATUS_ALLOC_FAILED;
+    cudaStream_t s = v->be->stream;
+    std::vector<const uint8_t *> dev(static_cast<size_t>(n));
+    for (int i = 0; i < n; ++i) {
+        if (!rgb[i]) {
+            set_error("encode_images: image %d is null", i);
+            return SAM3B200_STATUS_FAILED;
+        }
+        dev[i] = v->img_u8.as<uint8_t>() + bytes * i;
+        if (!cuda_ok(cudaMemcpyAsync(const_cast<uint8_t *>(dev[i]), rgb[i], bytes, cudaMemcpyHostToDevice, s),
+                     "image upload"))
             return SAM3B200_STATUS_FAILED;
     }
+    if (!encode_batch(v, n, dev.data(), w, h, out_host)) return SAM3B200_STATUS_FAILED;
     return sam3b200_backend_synchronize(reinterpret_cast<sam3b200_backend *>(v->be));
 }
 

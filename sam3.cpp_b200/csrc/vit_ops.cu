@@ -203,9 +203,10 @@ __global__ void ln_q8_kernel(const float *__restrict__ x, int rows, int E, const
     const float variance = static_cast<float>(sum2 / E);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
     int r = t;
-    if (win > 0) {  // ggml_win_part position
-        const int tx = t % G, ty = t / G, nw = G / win;
-        r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
+    if (win > 0) {  // ggml_win_part position (image-major: rows of image i are [i G^2, (i + 1) G^2))
+        const int img = t / (G * G), tl = t - img * (G * G);
+        const int tx = tl % G, ty = tl / G, nw = G / win;
+        r = img * (G * G) + ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
     }
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
@@ -288,9 +289,10 @@ __global__ void __launch_bounds__(128, LnMinBlocks<NJ>::value)
     const float variance = static_cast<float>(sum2 / E);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
     int r = t;
-    if (win > 0) {  // ggml_win_part position
-        const int tx = t % G, ty = t / G, nw = G / win;
-        r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
+    if (win > 0) {  // ggml_win_part position (image-major: rows of image i are [i G^2, (i + 1) G^2))
+        const int img = t / (G * G), tl = t - img * (G * G);
+        const int tx = tl % G, ty = tl / G, nw = G / win;
+        r = img * (G * G) + ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
     }
     int8_t *cr = codes + static_cast<int64_t>(r) * E + 4 * lane;
 #pragma unroll
@@ -335,7 +337,7 @@ static void launch_ln_dq16(const float *x, int rows, const float *w, const float
 
 cudaError_t layernorm_dq16(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                            void *out16, cudaStream_t s) {
-    if (rows <= 0 || (reinterpret_cast<uintptr_t>(out16) & 15) || (win > 0 && (G % win != 0 || rows != G * G)))
+    if (rows <= 0 || (reinterpret_cast<uintptr_t>(out16) & 15) || (win > 0 && (G % win != 0 || rows % (G * G) != 0)))
         return cudaErrorInvalidValue;
     switch (E) {
     case 256: launch_ln_dq16<2>(x, rows, w, b, eps, G, win, out16, s); break;
@@ -358,7 +360,7 @@ static void launch_ln_coal(const float *x, int rows, const float *w, const float
 
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s) {
-    if (E % 32 != 0 || E > 2048 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows != G * G)))
+    if (E % 32 != 0 || E > 2048 || rows <= 0 || ld < rows || (win > 0 && (G % win != 0 || rows % (G * G) != 0)))
         return cudaErrorInvalidValue;
     switch (E) {
     case 128: launch_ln_coal<1>(x, rows, w, b, eps, G, win, codes, quads, ld, s); break;
@@ -431,17 +433,18 @@ cudaError_t attn_inputs_from_f32(const float *q, const float *k, const float *v,
     return cudaGetLastError();
 }
 
-__global__ void rowmap_kernel(int G, int win, int *__restrict__ rowmap) {
+__global__ void rowmap_kernel(int G, int win, int nimg, int *__restrict__ rowmap) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= G * G) return;
-    const int tx = t % G, ty = t / G, nw = G / win;
+    if (t >= nimg * G * G) return;
+    const int img = t / (G * G), tl = t - img * (G * G);
+    const int tx = tl % G, ty = tl / G, nw = G / win;
     const int r = ((ty / win) * nw + tx / win) * win * win + (tx % win) + win * (ty % win);
-    rowmap[r] = t;
+    rowmap[img * (G * G) + r] = t;
 }
 
-cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s) {
-    if (win <= 0 || G % win != 0) return cudaErrorInvalidValue;
-    rowmap_kernel<<<grid_for(static_cast<int64_t>(G) * G, 256), 256, 0, s>>>(G, win, rowmap);
+cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s, int nimg) {
+    if (win <= 0 || G % win != 0 || nimg <= 0) return cudaErrorInvalidValue;
+    rowmap_kernel<<<grid_for(static_cast<int64_t>(nimg) * G * G, 256), 256, 0, s>>>(G, win, nimg, rowmap);
     return cudaGetLastError();
 }
 

@@ -29,7 +29,8 @@ cudaError_t add_pos_layernorm(const float *conv, const float *pos, int g, int G,
 
 // LayerNorm of rows of x (eps, w, b) quantised to Q8_0 into codes/quads
 // (mmq.cuh layout).  win > 0: row t of the G x G grid is written at its
-// ggml_win_part position (window-major, sam3.cpp:3734).
+// ggml_win_part position (window-major, sam3.cpp:3734); rows may hold several
+// G x G images stacked image-major, each partitioned on its own.
 cudaError_t layernorm_q8(const float *x, int rows, int E, const float *w, const float *b, float eps, int G, int win,
                          void *codes, void *quads, int ld, cudaStream_t s);
 // layernorm_q8's LayerNorm and Q8_0 quantisation (same codes and scales),
@@ -44,8 +45,9 @@ cudaError_t layernorm_dq16(const float *x, int rows, int E, const float *w, cons
 cudaError_t attn_inputs_from_f32(const float *q, const float *k, const float *v, int BH, int N, void *qb, void *kb,
                                  void *vt, cudaStream_t s);
 
-// Row map of ggml_win_unpart: windowed row -> token row (G x G grid).
-cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s);
+// Row map of ggml_win_unpart: windowed row -> token row (G x G grid), for
+// nimg images stacked image-major (rows of image i at [i G^2, (i + 1) G^2)).
+cudaError_t window_rowmap(int G, int win, int *rowmap, cudaStream_t s, int nimg = 1);
 
 cudaError_t f32_to_f16(const float *x, int64_t n, void *y, cudaStream_t s);
 

@@ -259,3 +259,44 @@ def test_detector_neck(model, oracle, backend, small):
             assert rel_err(got.reshape(want[i].shape), want[i]) <= TOL, i
     finally:
         vit.free()
+
+
+def test_batch_encode_matches_single_encodes(b200, backend, small):
+    """sam3b200_encode_images: n images through the blocks as one token batch (image-major rows, every
+    launch over all of them) give each image exactly its single-image encode -- bit for bit, since no
+    per-row arithmetic depends on the other rows -- also after a larger batch grew the buffers."""
+    hp, _, vit, _ = small
+    prev = backend.set_arith(b200.ARITH_DQ16)
+    try:
+        rng = np.random.default_rng(31)
+        rgbs = [rng.integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8) for _ in range(3)]
+        singles = [vit.encode(r) for r in rgbs]
+        for group in (rgbs, rgbs[1:]):
+            got = vit.encode_batch(group)
+            for g, want in zip(got, singles[len(rgbs) - len(group):]):
+                for a, b in zip(g, want):
+                    assert np.array_equal(a, b)
+    finally:
+        backend.set_arith(prev)
+
+
+def test_batch_encode_full_size(b200, backend, full8):
+    """Two 1008^2 images as one batch through windowed and global (N = 5184) ViT-32 blocks at full size:
+    both images' ViT outputs equal their single encodes bit for bit."""
+    hp, vit, _ = full8
+    prev = backend.set_arith(b200.ARITH_DQ16)
+    try:
+        rng = np.random.default_rng(32)
+        rgbs = [rng.integers(0, 256, (hp["img"], hp["img"], 3), dtype=np.uint8) for _ in range(2)]
+        singles = []
+        for r in rgbs:
+            outs = vit.encode(r)
+            singles.append((vit.output_host(-1).copy(), outs))
+        outs = vit.encode_batch(rgbs)
+        x_all = vit.output_host(-1)  # the first image's rows; the second image's follow in device memory
+        assert np.array_equal(x_all, singles[0][0])
+        for i in range(2):
+            for a, b in zip(outs[i], singles[i][1]):
+                assert np.array_equal(a, b)
+    finally:
+        backend.set_arith(prev)
