@@ -28,7 +28,8 @@ struct GCfg {
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int COLS = BN / (EPI_WARPS / 4);  // columns per epilogue thread
     static constexpr int TMEM_COLS = 256;
-    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+    static constexpr int STAGE_OFF = BAR_OFF + 256;  // per-warp 2 KB row-segment staging (ptx.cuh stage_put)
+    static constexpr int SMEM_BYTES = STAGE_OFF + EPI_WARPS * 2048 + 1024;
     static_assert(SMEM_BYTES <= 232448, "smem");
 };
 
@@ -157,6 +158,69 @@ __global__ void __launch_bounds__(GCfg::THREADS, 1)
                     if (lane == 0) mbar_arrive(&tempty[buf]);
                 }
                 const int nc = n0 + c;
+                // whole 32-column chunks with 16-byte-aligned row segments: the warp stores 8 rows x 64
+                // bytes per instruction through its staging buffer (warp-uniform condition)
+                const bool staged = nc + 32 <= N && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                                    (store == GEMM_STORE_CONVT2X2 || (ldo & (out_f16 ? 7 : 3)) == 0);
+                if (staged) {
+                    float f[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        float y = __uint_as_float(v[i]);
+                        const int n = nc + i;
+                        if (bias) y = y + bias[store == GEMM_STORE_CONVT2X2 ? n % cout : n];
+                        if (gelu) y = gelu_erf(y);
+                        f[i] = y;
+                    }
+                    long long base = -1;  // element offset of this lane's row segment; -1: row past M
+                    if (m < M) {
+                        if (store == GEMM_STORE_CONVT2X2) {
+                            const int g = nc / cout, co = nc % cout;
+                            const int iy = m / win, ix = m % win, ky = g >> 1, kx = g & 1;
+                            base = (static_cast<long long>(2 * iy + ky) * (2 * win) + 2 * ix + kx) * cout + co;
+                        } else {
+                            base = static_cast<long long>(m) * ldo + nc;
+                        }
+                    }
+                    uint4 *st = reinterpret_cast<uint4 *>(smem + C::STAGE_OFF) + (warp - 2) * 128;
+                    if (out_f16) {
+                        uint32_t hw[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const __half2 h2 = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+                            hw[i] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                        const uint4 seg[4] = {make_uint4(hw[0], hw[1], hw[2], hw[3]), make_uint4(hw[4], hw[5], hw[6], hw[7]),
+                                              make_uint4(hw[8], hw[9], hw[10], hw[11]),
+                                              make_uint4(hw[12], hw[13], hw[14], hw[15])};
+                        stage_put(st, lane, seg);
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                            const long long b = __shfl_sync(0xffffffffu, base, r);
+                            if (b >= 0) *reinterpret_cast<uint4 *>(static_cast<__half *>(out) + b + ch * 8) = st[stage_idx(r, ch)];
+                        }
+                    } else {
+#pragma unroll
+                        for (int c0 = 0; c0 < 32; c0 += 16) {
+                            uint4 seg[4];
+#pragma unroll
+                            for (int k = 0; k < 4; ++k)
+                                seg[k] = make_uint4(__float_as_uint(f[c0 + 4 * k]), __float_as_uint(f[c0 + 4 * k + 1]),
+                                                    __float_as_uint(f[c0 + 4 * k + 2]), __float_as_uint(f[c0 + 4 * k + 3]));
+                            stage_put(st, lane, seg);
+#pragma unroll
+                            for (int it = 0; it < 4; ++it) {
+                                const int r = it * 8 + (lane >> 2), ch = lane & 3;
+                                const long long b = __shfl_sync(0xffffffffu, base, r);
+                                if (b >= 0)
+                                    *reinterpret_cast<uint4 *>(static_cast<float *>(out) + b + c0 + ch * 4) =
+                                        st[stage_idx(r, ch)];
+                            }
+                        }
+                    }
+                    continue;
+                }
                 if (m >= M || nc >= N) continue;
                 float f[32];
 #pragma unroll

@@ -21,6 +21,7 @@
 #include "ptx.cuh"
 #include "tmap.h"
 
+#include <atomic>
 #include <cstdlib>
 
 #include <cuda_bf16.h>
@@ -1036,14 +1037,7 @@ cudaError_t dequant_weight_f16(const QMatrix &w, void *out, cudaStream_t s) {
 // free of bank conflicts -- and the warp writes 8 rows x 64 bytes per
 // instruction.  Row mappings (window order, head split) are per row, so any
 // destination layout with 16-byte-aligned row segments works.
-__device__ __forceinline__ int stage_idx(int row, int chunk) { return row * 4 + (chunk ^ ((row >> 1) & 3)); }
-
-__device__ __forceinline__ void stage_put(uint4 *st, int lane, const uint4 (&seg)[4]) {
-    __syncwarp();  // the previous round's reads are done
-#pragma unroll
-    for (int c = 0; c < 4; ++c) st[stage_idx(lane, c)] = seg[c];
-    __syncwarp();
-}
+// (stage_idx / stage_put: ptx.cuh)
 
 __device__ __forceinline__ uint32_t f2_bits(float a) { return __float_as_uint(a); }
 __device__ __forceinline__ uint32_t bf2_bits(float a, float b) {
@@ -1433,8 +1427,17 @@ static cudaError_t launch_dq16(const MmqArgs &a, const void *a16, const void *b1
         !make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, b16, 2, db, st, bxb, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     auto kern = mmq_dq16_kernel<MODE, BN>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    // the shared-memory opt-in, once per device and instantiation (a host call per launch otherwise)
+    static std::atomic<uint64_t> attr_done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+    if (!bit || !(attr_done.load(std::memory_order_relaxed) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_done.fetch_or(bit, std::memory_order_relaxed);
+    }
     const int tiles = ((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     kern<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ta, tb, M, N, K, dq16_epi(a), a.err);

@@ -328,4 +328,22 @@ __host__ __device__ constexpr uint32_t idesc_s8u8_s32(int M, int N) {
     return (2u << 4) | (1u << 7) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+
+// ---- warp-staged row segments -------------------------------------------------
+// Epilogues where each lane owns one output row (its TMEM lane) stage 64-byte
+// row segments in a per-warp 2 KB shared buffer and write them 8 rows x 64
+// bytes per instruction instead of one row per lane (32 cache lines per
+// instruction).  16-byte chunks are XOR-swizzled by (row >> 1) & 3, which keeps
+// both the row-per-lane writes and the 8-rows-per-instruction reads free of
+// bank conflicts.  Reader of round `it` (0..3): row it * 8 + (lane >> 2),
+// chunk lane & 3.
+__device__ __forceinline__ int stage_idx(int row, int chunk) { return row * 4 + (chunk ^ ((row >> 1) & 3)); }
+
+__device__ __forceinline__ void stage_put(uint4 *st, int lane, const uint4 (&seg)[4]) {
+    __syncwarp();  // the previous round's reads are done
+#pragma unroll
+    for (int c = 0; c < 4; ++c) st[stage_idx(lane, c)] = seg[c];
+    __syncwarp();
+}
+
 }  // namespace b200
