@@ -1,6 +1,7 @@
 """Benchmark: SAM3 Q8_0 ViT encode images/s (the visual-only ViT-32 + tracker
 neck configuration) on 1..8 B200s, with the quantised MUL_MAT's tensor
-throughput against the int8 peak as the roofline line.
+throughput as the roofline line (against the bf16 peak for the default DQ16
+arithmetic, against the int8 peak for the exact one; both fractions given).
 
 Workload (one step): a batch of 64 seeded uniform-uint8 1008x1008 RGB
 images, data-parallel -- rank r of N encodes images r, r+N, ... (strong
@@ -10,10 +11,15 @@ random-init N(0, 0.02), quantised with the reference quantiser rule) and the
 tracker SimpleFPN neck -- the whole of sam3_encode_image.
 
   value : images/s with the images already in device memory (encode only)
-  e2e   : images/s through the host API sam3b200_encode_image from pinned
+  e2e   : images/s through the host API (sam3b200_encode_images, --batch
+          images per call; sam3b200_encode_image at --batch 1) from pinned
           host memory, including the image upload and a device->host read
           of the smallest neck map (the encode result otherwise stays on the
           device, as in sam3.cpp:6138-6149)
+  --batch N (default 4): images per encoder call; the ViT blocks run once
+          over those images' tokens (bit-identical per image to one call each)
+  --arith dq16|exact: the MUL_MAT arithmetic (sam3b200_set_arith); the line
+          also carries the other one's images/s from the same run
 
 python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 python bench.py --workload video       (config 5: Hiera-B+ video tracking frames/s, one stream per GPU, 1..8 GPUs)
