@@ -402,8 +402,11 @@ static bool prefix_image(Vit *v, const uint8_t *rgb_dev, int w, int h, float *x)
            run_prefix(v, v->img_f32.as<float>(), x);
 }
 
+static bool ensure_batch(Vit *v, int n);
+
 static bool encode(Vit *v, const uint8_t *rgb_dev, int w, int h) {
-    if (!prefix_image(v, rgb_dev, w, h, v->x.as<float>())) return false;
+    // (a failed batch growth leaves no block-loop buffers: re-establish one image's)
+    if (!ensure_batch(v, 1) || !prefix_image(v, rgb_dev, w, h, v->x.as<float>())) return false;
     for (int i = 0; i < v->hp.depth; ++i)
         if (!run_block(v, i, v->x.as<float>())) return false;
     return run_necks(v, v->x.as<float>());
@@ -812,7 +815,7 @@ int sam3b200_vit_run_block(sam3b200_vit *hv, int idx, float *x_dev) {
     auto *v = reinterpret_cast<Vit *>(hv);
     if (!v || !x_dev || idx < 0 || idx >= v->hp.depth) return SAM3B200_STATUS_FAILED;
     cudaSetDevice(v->be->device);
-    return run_block(v, idx, x_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
+    return ensure_batch(v, 1) && run_block(v, idx, x_dev) ? SAM3B200_STATUS_SUCCESS : SAM3B200_STATUS_FAILED;
 }
 
 int sam3b200_vit_run_neck(sam3b200_vit *hv, const float *x_dev) {
