@@ -54,8 +54,11 @@ struct AttnCfg {
     static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
     static constexpr int KV_OFF = QT * Q_BYTES;
     static constexpr int BAR_OFF = KV_OFF + STAGES * STAGE_BYTES;  // 128 KB: one CTA per SM
-    static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-    static constexpr int THREADS = 256;
+    // softmax halves' exchange: values, then ok flags, each [2 parities][QT][4 quarters][2 halves][32 lanes]
+    static constexpr int XCH_OFF = BAR_OFF + 256;
+    static constexpr int XCH_BYTES = 2 * QT * 4 * 2 * 32 * 4;
+    static constexpr int SMEM_BYTES = XCH_OFF + 2 * XCH_BYTES + 1024;
+    static constexpr int THREADS = 512;
     static constexpr uint32_t S_COL = 0, P_COL = 128, PV_COL = 192, TILE_COLS = 256;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -141,7 +144,7 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
         }
         for (int t = 0; t < C::QT; ++t) {
             mbar_init(&ready[t], 1);
-            mbar_init(&pdone[t], 3);
+            mbar_init(&pdone[t], 6);  // both halves of the three lane quarters
         }
         fence_mbar_init();
         prefetch_tmap(&tm_q);
@@ -245,65 +248,86 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
             __syncwarp();
         }
     } else if ((warp & 3) != 1) {
-        // ---- softmax: one query row per thread ----
-        const int t = warp >> 2;
+        // ---- softmax: each query row split over two threads (halves h = 0, 1 take keys 64 h .. 64 h + 63
+        // of every key tile and output dimensions 32 h .. 32 h + 31), in two warps of one sub-partition
+        // that exchange the row max per tile (and the row sum at the end) through shared memory ----
+        const int t = (warp >> 2) & 1;
+        const int half = warp >> 3;
         const int quarter = warp & 3;                             // 0, 2 or 3
         const int row = (quarter == 0 ? 0 : (quarter - 1) * 32) + lane;  // query q0 + 96 t + row
         const uint32_t base = tmem + t * C::TILE_COLS + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t bar_id = 1 + t * 4 + quarter;  // named barrier of the two halves (64 threads)
+        float *xf = reinterpret_cast<float *>(smem + C::XCH_OFF);
+        int *xok = reinterpret_cast<int *>(smem + C::XCH_OFF + C::XCH_BYTES);
+        // exchange slot: [parity][t][quarter][half][lane]; parity alternates so a slot is rewritten only
+        // after the partner passed the next barrier (and so finished reading it)
+        auto slot = [&](int parity, int h) { return (((parity * 2 + t) * 4 + quarter) * 2 + h) * 32 + lane; };
+        // both halves reach every exchange, failed waits included, and take the same decision after it
+        auto exchange = [&](int parity, float v, bool ok_in, float &partner, bool &ok_both) {
+            xf[slot(parity, half)] = v;
+            xok[slot(parity, half)] = ok_in ? 1 : 0;
+            asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(64) : "memory");
+            partner = xf[slot(parity, half ^ 1)];
+            ok_both = ok_in && xok[slot(parity, half ^ 1)] != 0;
+        };
         if (t < nq) {
-            float o[C::HD];
+            float o[C::HD / 2];
 #pragma unroll
-            for (int i = 0; i < C::HD; ++i) o[i] = 0.f;
+            for (int i = 0; i < C::HD / 2; ++i) o[i] = 0.f;
             float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
             bool ok = true;
-            // O = O alpha + PV (PV_t(j-1) was formed against the running max of step j-1);
-            // the caller has waited for ready[t] phase j
+            // O = O alpha + PV (this half's 32 output dimensions; PV_t(j-1) was formed against the running
+            // max of step j-1); the caller has waited for ready[t] phase j
             auto fold_pv = [&](float alpha) {
-                uint32_t pv[C::HD];
-                tmem_ld_32x32b_x32(base + C::PV_COL, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
-                tmem_ld_32x32b_x32(base + C::PV_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
+                uint32_t pv[32];
+                tmem_ld_32x32b_x32(base + C::PV_COL + 32 * half, pv);
                 tmem_wait_ld();
 #pragma unroll
-                for (int d = 0; d < C::HD; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(pv[d]));
+                for (int d = 0; d < C::HD / 2; ++d) o[d] = fmaf(o[d], alpha, __uint_as_float(pv[d]));
             };
             for (int j = 0; j < ntiles; ++j) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&ready[t], j & 1, err, AERR_S_FULL))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const int nvalid = N - j * C::BKV;  // keys of this tile below N
-                // pass 1: row max of the raw scores (c > 0, so the max commutes with the scaling)
+                const bool wok = __all_sync(0xffffffffu, mbar_wait(&ready[t], j & 1, err, AERR_S_FULL));
+                const int nvalid = N - j * C::BKV - 64 * half;  // keys of this half-tile below N
+                uint32_t s0[32];
                 float mx = -INFINITY;
-#pragma unroll
-                for (int cc = 0; cc < C::BKV; cc += 64) {
-                    uint32_t s0[32], s1[32];
-                    tmem_ld_32x32b_x32(base + C::S_COL + cc, s0);
-                    tmem_ld_32x32b_x32(base + C::S_COL + cc + 32, s1);
+                if (wok) {
+                    tc_fence_after();
+                    uint32_t s1[32];
+                    tmem_ld_32x32b_x32(base + C::S_COL + 64 * half, s0);
+                    tmem_ld_32x32b_x32(base + C::S_COL + 64 * half + 32, s1);
                     tmem_wait_ld();
-                    if (nvalid >= C::BKV) {
+                    // row max of the raw scores (c > 0, so the max commutes with the scaling); the second
+                    // 32 scores are read again for the exponentials (registers: the output row stays in them)
+                    if (nvalid >= 64) {
                         mx = chunk_max<false>(s0, mx, 32);
                         mx = chunk_max<false>(s1, mx, 32);
                     } else {
-                        mx = chunk_max<true>(s0, mx, nvalid - cc);
-                        mx = chunk_max<true>(s1, mx, nvalid - cc - 32);
+                        mx = chunk_max<true>(s0, mx, nvalid);
+                        mx = chunk_max<true>(s1, mx, nvalid - 32);
                     }
                 }
-                const float m_new = fmaxf(m_run, mx * c_log2);
-                const float alpha = ex2_approx(m_run - m_new);
-                // PV_t(j-1) (complete with S_t(j)) has read P_t(j-1): fold it, then overwrite P_t
-                if (j > 0) fold_pv(alpha_prev);
-                // pass 2: P = 2^(s c - m) into tensor memory, row sum
-                float rsum = 0.f;
-#pragma unroll
-                for (int cc = 0; cc < C::BKV; cc += 32) {
-                    uint32_t s0[32], pk[16];
-                    tmem_ld_32x32b_x32(base + C::S_COL + cc, s0);
-                    tmem_wait_ld();
-                    rsum += nvalid >= C::BKV ? chunk_exp<false>(s0, c_log2, -m_new, pk, 32)
-                                             : chunk_exp<true>(s0, c_log2, -m_new, pk, nvalid - cc);
-                    tmem_st_32x32b_x16(base + C::P_COL + cc / 2, pk);
+                float mx_other;
+                bool both;
+                exchange(j & 1, mx, wok, mx_other, both);
+                if (!both) {
+                    ok = false;
+                    break;
                 }
+                const float m_new = fmaxf(m_run, fmaxf(mx, mx_other) * c_log2);
+                const float alpha = ex2_approx(m_run - m_new);
+                // P = 2^(s c - m) of this half's 64 keys into tensor memory (PV_t(j-1), complete with
+                // S_t(j), has read P_t(j-1)), row sum
+                uint32_t pk[16];
+                float rsum = nvalid >= 64 ? chunk_exp<false>(s0, c_log2, -m_new, pk, 32)
+                                          : chunk_exp<true>(s0, c_log2, -m_new, pk, nvalid);
+                tmem_st_32x32b_x16(base + C::P_COL + 32 * half, pk);
+                tmem_ld_32x32b_x32(base + C::S_COL + 64 * half + 32, s0);
+                tmem_wait_ld();
+                rsum += nvalid >= 64 ? chunk_exp<false>(s0, c_log2, -m_new, pk, 32)
+                                     : chunk_exp<true>(s0, c_log2, -m_new, pk, nvalid - 32);
+                tmem_st_32x32b_x16(base + C::P_COL + 32 * half + 16, pk);
+                // fold PV_t(j-1) before pdone lets PV_t(j) overwrite it (after the scores: fewer live registers)
+                if (j > 0) fold_pv(alpha_prev);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -312,25 +336,31 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                 m_run = m_new;
                 alpha_prev = alpha;
             }
-            if (ok && __all_sync(0xffffffffu, mbar_wait(&ready[t], ntiles & 1, err, AERR_PV_FULL))) {
-                tc_fence_after();
-                fold_pv(alpha_prev);
+            if (ok) {
+                const bool wok = __all_sync(0xffffffffu, mbar_wait(&ready[t], ntiles & 1, err, AERR_PV_FULL));
+                if (wok) {
+                    tc_fence_after();
+                    fold_pv(alpha_prev);
+                }
+                float l_other;
+                bool both;
+                exchange(ntiles & 1, l_run, wok, l_other, both);
                 const int n = q0 + t * C::ROWS + row;
-                if (n < N) {
+                if (both && n < N) {
                     const int bb = bh / heads, h = bh % heads;
-                    const float inv = 1.0f / l_run;
+                    const float inv = 1.0f / (half == 0 ? l_run + l_other : l_other + l_run);
                     const int64_t r = static_cast<int64_t>(bb) * N + n;  // output row
+                    const int hb = 32 * half;                             // this half's 32-wide Q8_0 block
 #pragma unroll
-                    for (int d = 0; d < C::HD; ++d) o[d] = o[d] * inv;
-                    if (o16) {  // Q8_0 of the row's 32-blocks, written dequantised as fp16
-                        const int E = heads * C::HD;
+                    for (int d = 0; d < C::HD / 2; ++d) o[d] = o[d] * inv;
+                    const int E = heads * C::HD;
+                    if (o16 || qcodes) {
+                        float amax = 0.f;
 #pragma unroll
-                        for (int hb = 0; hb < C::HD; hb += 32) {
-                            float amax = 0.f;
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[hb + i]));
-                            const float dq = __fdiv_rn(amax, 127.f);
-                            const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[i]));
+                        const float dq = __fdiv_rn(amax, 127.f);
+                        const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+                        if (o16) {  // Q8_0 of the block, written dequantised as fp16
                             const float dh = __half2float(__float2half_rn(dq));
                             uint4 *dst = reinterpret_cast<uint4 *>(o16 + r * E + h * C::HD + hb);
 #pragma unroll
@@ -338,43 +368,33 @@ __global__ void __launch_bounds__(AttnCfg::THREADS, 1)
                                 uint32_t hw[4];
 #pragma unroll
                                 for (int e = 0; e < 4; ++e) {
-                                    const float a0 = q8_code_f(__fmul_rn(o[hb + i + 2 * e], id));
-                                    const float a1 = q8_code_f(__fmul_rn(o[hb + i + 2 * e + 1], id));
+                                    const float a0 = q8_code_f(__fmul_rn(o[i + 2 * e], id));
+                                    const float a1 = q8_code_f(__fmul_rn(o[i + 2 * e + 1], id));
                                     const __half2 h2 = __floats2half2_rn(__fmul_rn(a0, dh), __fmul_rn(a1, dh));
                                     hw[e] = *reinterpret_cast<const uint32_t *>(&h2);
                                 }
                                 dst[i >> 3] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                             }
-                        }
-                    } else if (qcodes) {
-                        const int E = heads * C::HD;
-#pragma unroll
-                        for (int hb = 0; hb < C::HD; hb += 32) {
-                            float amax = 0.f;
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(o[hb + i]));
-                            const float dq = __fdiv_rn(amax, 127.f);
-                            const float id = amax != 0.f ? __fdiv_rn(127.f, amax) : 0.f;
-                            uint32_t pk[8];
+                        } else {
+                            uint32_t pk8[8];
 #pragma unroll
                             for (int i = 0; i < 8; ++i) {
-                                const int a0 = __float2int_rn(__fmul_rn(o[hb + 4 * i], id));
-                                const int a1 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 1], id));
-                                const int a2 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 2], id));
-                                const int a3 = __float2int_rn(__fmul_rn(o[hb + 4 * i + 3], id));
-                                pk[i] = (static_cast<uint32_t>(a0) & 0xFFu) | ((static_cast<uint32_t>(a1) & 0xFFu) << 8) |
-                                        ((static_cast<uint32_t>(a2) & 0xFFu) << 16) | ((static_cast<uint32_t>(a3) & 0xFFu) << 24);
+                                const int a0 = __float2int_rn(__fmul_rn(o[4 * i], id));
+                                const int a1 = __float2int_rn(__fmul_rn(o[4 * i + 1], id));
+                                const int a2 = __float2int_rn(__fmul_rn(o[4 * i + 2], id));
+                                const int a3 = __float2int_rn(__fmul_rn(o[4 * i + 3], id));
+                                pk8[i] = (static_cast<uint32_t>(a0) & 0xFFu) | ((static_cast<uint32_t>(a1) & 0xFFu) << 8) |
+                                         ((static_cast<uint32_t>(a2) & 0xFFu) << 16) | ((static_cast<uint32_t>(a3) & 0xFFu) << 24);
                             }
                             uint4 *dst = reinterpret_cast<uint4 *>(qcodes + r * E + h * C::HD + hb);
-                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-                            const int blk = (h * C::HD + hb) >> 5;
-                            store_act_scale(qquads, blk, static_cast<int>(r), qld, E >> 5, dq);
+                            dst[0] = make_uint4(pk8[0], pk8[1], pk8[2], pk8[3]);
+                            dst[1] = make_uint4(pk8[4], pk8[5], pk8[6], pk8[7]);
+                            store_act_scale(qquads, (h * C::HD + hb) >> 5, static_cast<int>(r), qld, E >> 5, dq);
                         }
                     } else {
-                        float *dst = out + r * heads * C::HD + h * C::HD;
+                        float *dst = out + r * E + h * C::HD + hb;
 #pragma unroll
-                        for (int d = 0; d < C::HD; d += 4)
+                        for (int d = 0; d < 32; d += 4)
                             *reinterpret_cast<float4 *>(dst + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
                     }
                 }
