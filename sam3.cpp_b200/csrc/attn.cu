@@ -23,12 +23,18 @@
 //                (ready[t]) for the pair: commits hold the issuing thread far
 //                longer than MMAs.  The tiles alternate, so the tensor core
 //                works on one tile while the other tile's softmax runs;
-//   warps 0, 2, 3 (tile 0) and 4, 6, 7 (tile 1): softmax, one query row per
-//                thread (the TMEM lane quarter of warp w is w % 4).  Per key
-//                tile: pass 1 takes the row max of S, pass 2 writes
-//                P = 2^(s c - m) as bf16 into tensor memory and sums it; the
-//                output row stays in registers and PV_t(j-1) is folded in as
-//                O = O 2^(m(j-2) - m(j-1)) + PV_t(j-1), one step behind.
+//   warps w with w % 4 != 1 (12 of the 16): softmax.  Warp w serves tile
+//                (w >> 2) & 1, TMEM lane quarter w % 4 (the only quarter its
+//                sub-partition can read) and half w >> 3 of every query row:
+//                keys 64 h .. 64 h + 63 of each key tile and output
+//                dimensions 32 h .. 32 h + 31.  Per key tile each half reads
+//                its 64 scores, takes their max, exchanges it with the other
+//                half through shared memory (a named barrier of the two
+//                warps), writes P = 2^(s c - m) as bf16 into tensor memory and
+//                sums it; its 32 output dimensions stay in registers and
+//                PV_t(j-1) is folded in as O = O 2^(m(j-2) - m(j-1)) + PV_t(j-1),
+//                one step behind.  The two halves' row sums are added at the
+//                end, and each half quantises its own 32-wide Q8_0 block.
 // Tensor memory (512 columns): tile t at 256 t: S (128 columns), P (64: 128
 // bf16 packed in pairs), PV (64).
 #include "attn.cuh"
