@@ -57,6 +57,9 @@ def _load(name):
 # DRAM traffic of one MUL_MAT launch at the cfg3 shapes (mean of qkv, proj, fc1,
 # fc2), from an ncu capture of ViT block 0's four launches.
 MMQ_DRAM_BYTES_PER_LAUNCH = 27.44e6
+# The same for the DQ16 kernel: mean dram read + write of ViT block 0's four launches at M = 5184 (qkv 20.7,
+# proj 34.0, fc1 24.1, fc2 99.6 MB), captured one image per launch.
+DQ16_DRAM_BYTES_PER_LAUNCH_1IMG = 44.6e6
 
 
 def vit_ops_per_image(hp):
@@ -567,8 +570,14 @@ def main():
                          "frac": achieved / peak if peak else None,
                          "frac_of_int8_peak": achieved / peak_int8 if peak_int8 else None,
                          "peak_int8_measured": peak_int8,
-                         "traffic": None if dq16 else MMQ_DRAM_BYTES_PER_LAUNCH, "traffic_unit": "bytes per launch",
-                         "traffic_source": "not captured for this kernel" if dq16 else
+                         "traffic": DQ16_DRAM_BYTES_PER_LAUNCH_1IMG * nb if dq16 else MMQ_DRAM_BYTES_PER_LAUNCH,
+                         "traffic_unit": "bytes per launch",
+                         "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over ViT block 0's "
+                                            "four MUL_MAT launches captured at one image per launch (44.6 MB), scaled "
+                                            "by the images per launch; the algorithmic bytes (fp16 A and B read once, "
+                                            "outputs and the residual read / written once) are ~69 MB per image-launch, "
+                                            "so DRAM moves less than the operands: they are reused from L2")
+                                           if dq16 else
                                            "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the four "
                                            "MUL_MAT launches of one ViT block (qkv 10.6, proj 28.9, fc1 13.1, "
                                            "fc2 57.1 MB); operands stream L2 -> SM, not from DRAM",
