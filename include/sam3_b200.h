@@ -165,7 +165,7 @@ int sam3b200_set_mmq_impl(sam3b200_backend *be, int impl);
  *   SAM3B200_ARITH_DQ16 (default): activation codes and weight blocks
  *     dequantised to fp16 (fp16(q * d), one rounding of the exact product)
  *     and multiplied on the fp16 tensor cores with fp32 accumulation over
- *     all of K -- the same sum up to rounding (~1e-4 normwise), without the
+ *     all of K -- the same sum up to rounding (~3e-4 normwise), without the
  *     per-block fold; the weights are held a second time as fp16.
  * Op-level sam3b200_mul_mat is always EXACT.  Returns the previous value;
  * other values are ignored.  Environment: SAM3B200_ARITH=0|1 at init. */

@@ -110,6 +110,17 @@ def mul_mat(qtype: int, wq: np.ndarray, K: int, N: int, x: np.ndarray, n_threads
     return y
 
 
+def mul_mat_dq16(qtype: int, wq: np.ndarray, K: int, N: int, x: np.ndarray) -> np.ndarray:
+    """The library's DQ16 MUL_MAT arithmetic restated (checker only): x quantised to Q8_0 with the ggml-cpu
+    rule, every activation code and every weight element dequantised (q * d, exact in float32) and rounded
+    once to fp16, the products summed in float64 -- the tensor cores sum in fp32 in an unspecified order, so
+    float64 is the reference that bounds them.  Returns float32 [M, N]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    a16 = dequantize(Q8_0, quantize_activations(Q8_0, x), K).astype(np.float16)
+    w16 = dequantize(qtype, np.ascontiguousarray(wq), K).astype(np.float16)
+    return (a16.astype(np.float64) @ w16.astype(np.float64).T).astype(np.float32)
+
+
 def block_dots(qtype: int, wq: np.ndarray, K: int, N: int, x: np.ndarray, n_threads: int = 0) -> np.ndarray:
     """Per-(m, n, block) int32 dots of the integer codes: int32 [M, N, K/32]."""
     x = np.ascontiguousarray(x, dtype=np.float32)

@@ -142,7 +142,7 @@ cudaError_t mmq_simt(const MmqArgs &args, int mode, cudaStream_t s);
 // weight blocks, each element dequantised to fp16 -- fp16(q * d), one
 // rounding of an exact product, relative error <= 2^-11 -- and multiplied on
 // the fp16 tensor cores with fp32 accumulation over the whole of K.  The sum
-// differs from the exact block-ordered fold by rounding only (about 1e-4
+// differs from the exact block-ordered fold by rounding only (about 3e-4
 // normwise), and one MMA pass over K replaces the per-block int32 -> fp32
 // fold on the CUDA cores.
 

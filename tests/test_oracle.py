@@ -93,3 +93,20 @@ def test_block_dots_consistent_with_mul_mat(oracle):
     qx = xq[..., 2:].view(np.int8).astype(np.int64)
     qw = wqq[..., 2:].view(np.int8).astype(np.int64)
     assert np.array_equal(bd, np.einsum("mbk,nbk->mnb", qx, qw).astype(np.int32))
+
+
+@pytest.mark.parametrize("qt", [8, 2])  # Q8_0, Q4_0
+@pytest.mark.parametrize("M,K,N", [(192, 1024, 384), (96, 4736, 256), (130, 96, 288)])
+def test_dq16_arithmetic_within_rounding_of_the_exact_fold(oracle, qt, M, K, N):
+    """The DQ16 arithmetic (Q8_0 activation codes and weight blocks dequantised to fp16, one fp16 product
+    per element, wide accumulation) against the exact block-ordered fold of the same codes: they differ by
+    the two fp16 roundings only, far inside the north-star 1e-2 (max|d| / max|ref|; observed ~3e-4)."""
+    rng = np.random.default_rng(M + K + N + qt)
+    w = rng.normal(0, 0.02, size=(N, K)).astype(np.float32)
+    x = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+    wq = oracle.quantize_weights(qt, w)
+    exact = oracle.mul_mat(qt, wq, K, N, x)
+    dq = oracle.mul_mat_dq16(qt, wq, K, N, x)
+    err = float(np.max(np.abs(dq - exact)) / np.max(np.abs(exact)))
+    assert err <= 1e-3, err
+    assert err > 0.0  # the roundings are real: the two arithmetics are not the same function
